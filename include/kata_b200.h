@@ -1,0 +1,151 @@
+/*
+ * kata_b200.h -- C ABI of the B200 (sm_100a) KATA-SPD attention hot path.
+ *
+ * This is the drop-in boundary below the reference's Python operator API.  Each entry point
+ * takes plain device pointers, sizes and a CUDA stream; no PyTorch (or other framework) type
+ * appears in any signature.  The library never allocates or frees device memory: outputs and
+ * workspace are owned by the caller, and no pointer is retained after a call returns.  Every
+ * call is stream-ordered on the given stream and performs no host synchronisation.
+ *
+ * Layout: all token tensors are time-major and contiguous, i.e. (B, T, heads, dim) with dim
+ * fastest, exactly as the reference launchers require after their .contiguous() calls
+ * (kata/parallel_kata_attn.py:229-231).  Per-token scalars (den, c, beta, gates) are (B, T, heads).
+ *
+ * Return value: KATA_OK (0) or a negative KATA_ERR_* code; kata_strerror() names it.
+ * Device-side bounded waits never trap: when one times out the kernel stores a nonzero code
+ * into *status (if status != NULL) and returns early.  Callers check the word after the stream
+ * drains (KATA_STATUS_* values).
+ */
+#ifndef KATA_B200_H
+#define KATA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define KATA_API __attribute__((visibility("default")))
+#else
+#define KATA_API
+#endif
+
+/* Same object as cudaStream_t / CUstream; declared opaquely so this header needs no CUDA. */
+typedef struct CUstream_st* kata_stream_t;
+
+enum {
+  KATA_OK = 0,
+  KATA_ERR_INVALID = -1,     /* null pointer or inconsistent argument */
+  KATA_ERR_DTYPE = -2,       /* unsupported dtype */
+  KATA_ERR_SHAPE = -3,       /* unsupported or inconsistent shape */
+  KATA_ERR_ALIGN = -4,       /* pointer not 16-byte aligned (TMA requirement) */
+  KATA_ERR_WORKSPACE = -5,   /* workspace missing or too small */
+  KATA_ERR_CUDA = -6,        /* a CUDA runtime call failed (e.g. launch error) */
+  KATA_ERR_DRIVER = -7,      /* driver entry point (tensor-map encoder) unavailable */
+  KATA_ERR_UNSUPPORTED = -8  /* algorithm not available for this configuration */
+};
+
+/* Values a kernel may store into the optional device status word. */
+enum { KATA_STATUS_OK = 0, KATA_STATUS_WAIT_TIMEOUT = 1 };
+
+enum { KATA_DTYPE_F32 = 0, KATA_DTYPE_BF16 = 1, KATA_DTYPE_F16 = 2 };
+
+/* Kernel family.  AUTO picks the tcgen05 tensor-core kernels for bf16/f16 inputs whose shape
+ * they cover and the fp32-exact SIMT kernels otherwise (fp32 inputs always take SIMT, which is
+ * the fp32-accurate mode).  TC / SIMT force one family (TC returns KATA_ERR_UNSUPPORTED when the
+ * shape or dtype is outside its envelope). */
+enum { KATA_ALGO_AUTO = 0, KATA_ALGO_TC = 1, KATA_ALGO_SIMT = 2 };
+
+/* Score form.  CONCAT: A[t,s] = sum_g (scale * q_g[t].k_g[s])^2  (kata_quadratic)
+ *              SUM:    A[t,s] = sum_{i,j} (scale * q_i[t].k_j[s])^2 (kata_quadratic_sum) */
+enum { KATA_SCORE_CONCAT = 0, KATA_SCORE_SUM = 1 };
+
+/* ---------------------------------------------------------------------------------------------
+ * Causal normalised KATA-SPD attention, forward.
+ *   o_t = sum_{s<=t} A[t,s] v_s / den_t,  den_t = sum_{s<=t} A[t,s]  (den_t <= 0 -> divide by 1)
+ *   with A optionally multiplied by exp(min(c_t - c_s, 0)) when c != NULL.
+ * Replaces the Triton launchers parallel_kata_attn_fwd_impl (kata/parallel_kata_attn.py:211-288)
+ * and parallel_kata_attn_sum_fwd_impl (kata/parallel_kata_attn.py:539-576), i.e. kernels
+ * parallel_kata_attn_fwd_kernel (kata/kernels/parallel_kata.py:10-197) and
+ * parallel_kata_attn_sum_fwd_kernel (kata/kernels/parallel_kata.py:202-345).
+ * GQA: HQ must be a multiple of H; query head hq reads key/value head hq / (HQ/H).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;   /* (B,T,HQ,D)  dtype                                  */
+  const void* k;   /* (B,T,H,D)   dtype                                  */
+  const void* v;   /* (B,T,H,Dv)  dtype                                  */
+  const float* c;  /* (B,T,HQ) fp32 cumulative log-decay, or NULL         */
+  void* o;         /* (B,T,HQ,Dv) dtype   [out]                          */
+  float* den;      /* (B,T,HQ) fp32       [out]                          */
+  int* status;     /* optional device status word (int32), may be NULL   */
+  int dtype;       /* KATA_DTYPE_*                                       */
+  int B, T, H, HQ, D, Dv;
+  int M;           /* num_groups; D % M == 0                             */
+  int score;       /* KATA_SCORE_*                                       */
+  int algo;        /* KATA_ALGO_*                                        */
+  float scale;     /* per-group dot scale (reference default 1/sqrt(D/M)) */
+} kata_attn_fwd_args;
+
+KATA_API int kata_attn_fwd(const kata_attn_fwd_args* args, kata_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Causal normalised KATA-SPD attention, backward.
+ *   delta_t = <o_t, dO_t>;  dA[t,s] = (dO_t.v_s - delta_t) / den_t  (causal);
+ *   dq, dk from d(qk_p) = 2 qk_p dA (times the decay factor); dv = (A/den)^T dO;
+ *   dc_t = sum_s G[t,s] - sum_t' G[t',t], G = dA * A over pairs with c_t - c_s <= 0.
+ * Replaces parallel_kata_attn_bwd_triton (kata/parallel_kata_attn.py:364-529) with kernels
+ * K3-K9 (kata/kernels/parallel_kata.py:349-1342), the sum-form Triton backward
+ * (kata/parallel_kata_attn.py:755-901, kata/kernels/parallel_kata_sum.py), the PyTorch
+ * fallbacks parallel_kata_attn_bwd (:49-146) / parallel_kata_attn_bwd_sum_torch (:579-653),
+ * and the autograd recompute of the decayed form (_KataDecayFunction.backward, :329-347).
+ * workspace: kata_attn_bwd_workspace_bytes(args) bytes of device memory (may be 0 -> NULL ok).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;     /* (B,T,HQ,D)  dtype */
+  const void* k;     /* (B,T,H,D)   dtype */
+  const void* v;     /* (B,T,H,Dv)  dtype */
+  const void* o;     /* (B,T,HQ,Dv) dtype (forward output) */
+  const float* den;  /* (B,T,HQ) fp32 (forward denominator) */
+  const void* dout;  /* (B,T,HQ,Dv) dtype, upstream gradient */
+  const float* c;    /* (B,T,HQ) fp32 or NULL */
+  void* dq;          /* (B,T,HQ,D)  dtype [out] */
+  void* dk;          /* (B,T,H,D)   dtype [out] */
+  void* dv;          /* (B,T,H,Dv)  dtype [out] */
+  float* dc;         /* (B,T,HQ) fp32 [out], required iff c != NULL */
+  void* workspace;
+  size_t workspace_bytes;
+  int* status;
+  int dtype;
+  int B, T, H, HQ, D, Dv;
+  int M;
+  int score;
+  int algo;
+  float scale;
+} kata_attn_bwd_args;
+
+KATA_API size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* args);
+KATA_API int kata_attn_bwd(const kata_attn_bwd_args* args, kata_stream_t stream);
+
+/* Human-readable name of a KATA_ERR_* code (static storage). */
+KATA_API const char* kata_strerror(int code);
+
+/* ABI revision of this header; bumped on any incompatible change. */
+KATA_API int kata_abi_version(void);
+#define KATA_ABI_VERSION 1
+
+/* Diagnostic: D(M x N, fp32, row-major) = A * B^T through one CTA of TMA loads and tcgen05 MMAs.
+ * A is (M x K) bf16, stored K-contiguous when a_mn == 0 or as (K x M) M-contiguous when a_mn == 1;
+ * B is (N x K) K-contiguous when b_mn == 0 or (K x N) N-contiguous when b_mn == 1.  *_sw is the
+ * shared-memory swizzle span in bytes (32, 64 or 128).  a_tmem == 1 stages A in tensor memory
+ * (tcgen05.st) instead of shared memory.  M == 128; N, K multiples of 16, <= 256.
+ * No counterpart in the reference: it checks this library's descriptor encodings on the device. */
+KATA_API int kata_selftest_umma(const void* A, const void* B, float* D, int M, int N, int K, int a_mn, int b_mn,
+                       int a_sw, int b_sw, int a_tmem, kata_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KATA_B200_H */

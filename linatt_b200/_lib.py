@@ -1,0 +1,138 @@
+"""ctypes binding of the C ABI in ``include/kata_b200.h`` (``libkata_b200.so``).
+
+This module is the only place that touches the shared library.  It mirrors the argument
+structs field for field, converts torch tensors to raw device pointers and sizes, and turns
+nonzero return codes into ``RuntimeError`` with the library's own message.  There is no CPU
+or framework fallback: if the library is missing, or a tensor is not on a CUDA device, every
+call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "libkata_b200.so"
+
+KATA_OK = 0
+DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+ALGO = {"auto": 0, "tc": 1, "simt": 2}
+SCORE = {"concat": 0, "sum": 1}
+ABI_VERSION = 1
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+c_size_t = ctypes.c_size_t
+
+
+class AttnFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("c", c_void_p),
+        ("o", c_void_p), ("den", c_void_p), ("status", c_void_p),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HQ", c_int), ("D", c_int), ("Dv", c_int),
+        ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float),
+    ]
+
+
+class AttnBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("o", c_void_p), ("den", c_void_p),
+        ("dout", c_void_p), ("c", c_void_p), ("dq", c_void_p), ("dk", c_void_p), ("dv", c_void_p),
+        ("dc", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("status", c_void_p),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HQ", c_int), ("D", c_int), ("Dv", c_int),
+        ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not _LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{_LIB_PATH.name} is not built; run `python -m linatt_b200.build` "
+                    "(nvcc with sm_100a support is required)")
+            L = ctypes.CDLL(str(_LIB_PATH))
+            L.kata_strerror.restype = ctypes.c_char_p
+            L.kata_strerror.argtypes = [c_int]
+            L.kata_abi_version.restype = c_int
+            L.kata_attn_fwd.restype = c_int
+            L.kata_attn_fwd.argtypes = [ctypes.POINTER(AttnFwdArgs), c_void_p]
+            L.kata_attn_bwd.restype = c_int
+            L.kata_attn_bwd.argtypes = [ctypes.POINTER(AttnBwdArgs), c_void_p]
+            L.kata_attn_bwd_workspace_bytes.restype = c_size_t
+            L.kata_attn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnBwdArgs)]
+            L.kata_selftest_umma.restype = c_int
+            L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 9 + [c_void_p]
+            if L.kata_abi_version() != ABI_VERSION:
+                raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
+            _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != KATA_OK:
+        msg = lib().kata_strerror(rc).decode()
+        raise RuntimeError(f"{what} failed: {msg} (code {rc})")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("linatt_b200 kernels run on CUDA tensors only (got a tensor on "
+                               f"{t.device}); there is no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def stream_handle(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+# Per-device status word that bounded device-side waits write on timeout.
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(dev: torch.device) -> torch.Tensor:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        _status[idx] = t
+    return t
+
+
+def check_device_status(dev: torch.device | None = None) -> None:
+    """Synchronise and raise if any kernel on ``dev`` reported a bounded-wait timeout."""
+    devs = [dev] if dev is not None else [torch.device("cuda", i) for i in _status]
+    for d in devs:
+        t = status_word(d)
+        v = int(t.item())
+        if v != 0:
+            t.zero_()
+            raise RuntimeError(f"linatt_b200 device status {v}: a kernel wait timed out on {d}")
+
+
+SYNC_CHECK = os.environ.get("KATA_SYNC_CHECK", "0") == "1"

@@ -1,0 +1,444 @@
+// attn_tc_fwd.cu -- tcgen05 tensor-core forward of causal KATA-SPD attention (bf16 / fp16).
+//
+// Math (kata/kernels/parallel_kata.py:10-197 concat, :202-345 sum):
+//   S_p[t,s] = <q_a[t], k_b[s]>      for score parts p = (a,b): concat (g,g), sum all (a,b)
+//   A[t,s]   = scale^2 * sum_p S_p^2 (* exp(min(c_t - c_s, 0)))   causal
+//   O[t]     = sum_s half(A[t,s]) v_s,  den_t = sum_s A[t,s],  o_t = O[t] / (den_t > 0 ? den_t : 1)
+//
+// One CTA per (128-query tile, batch*head).  Warp roles (320 threads):
+//   warp 0      TMA producer: Q once, K and V tiles through 2-stage rings (4-D tensor maps over
+//               the time-major (B,T,H,D) tensors, so rows past T are zero-filled per batch).
+//   warp 1      TMEM owner + single-thread MMA issuer: for each key tile, one tcgen05.mma chain
+//               per score part into a 3-slot TMEM ring (128 fp32 columns per slot), then the
+//               P*V chain into the O accumulator (columns 384..384+Dv).
+//   warps 2..9  two compute warpgroups.  Thread (warp%4, lane) owns TMEM lane = query row;
+//               warpgroup 0 owns key columns 0..63, warpgroup 1 owns 64..127.  They square and
+//               accumulate the parts (packed fp32x2 FMAs), apply mask/decay, accumulate the row
+//               sum, and write P = half(A) into a 128B-swizzled K-major smem tile for the P*V MMA.
+//               Finally they read O from TMEM, divide by den and store o and den.
+// Every mbarrier wait is bounded (see sm100.cuh); a timeout records a status code and drains.
+#include "attn_common.cuh"
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace kata {
+namespace {
+
+constexpr int kBT = 128;  // query rows per tile (= UMMA M)
+constexpr int kBK = 128;  // keys per tile (= UMMA N of the score MMAs, K of the P*V MMA)
+constexpr int kSlots = 3;
+constexpr int kThreads = 320;
+constexpr int kComputeWarp0 = 2;
+constexpr uint32_t kOCol = 384;
+
+template <int D, int DV>
+struct FwdSmem {
+  static constexpr int Q_BYTES = kBT * D * 2;
+  static constexpr int K_BYTES = kBK * D * 2;
+  static constexpr int V_BYTES = kBK * DV * 2;
+  static constexpr int P_BYTES = kBT * kBK * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+  static constexpr int TOTAL = OFF_P + 2 * P_BYTES;
+};
+
+struct FwdBarriers {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full[2], v_empty[2];
+  uint64_t s_full[kSlots], s_empty[kSlots];
+  uint64_t p_full[2], p_empty[2];
+  uint64_t o_full;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float den_x[2][kBT];  // partial row sums of the two column halves
+};
+
+template <typename T>
+struct FwdTma {
+  CUtensorMap q, k, v;
+};
+
+// UMMA descriptor of K-step `kk` (16 elements) of group `g` for a [rows=128][D] operand stored as
+// boxes of CW columns (CW*2 = swizzle span).
+template <int CW>
+__device__ __forceinline__ uint64_t grp_kmajor_desc(uint32_t base, int g, int E, int kk) {
+  const int col = g * E + kk * 16;
+  const uint32_t box = static_cast<uint32_t>(col / CW);
+  const uint32_t within = static_cast<uint32_t>(col % CW) * 2u;
+  return umma_smem_desc(base + box * (128u * CW * 2u) + within, 16u, 8u * CW * 2u, CW * 2);
+}
+
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
+  constexpr int E = D / M;
+  constexpr int CW = E < 64 ? E : 64;  // group box width (elements); swizzle = 2*CW bytes
+  constexpr int NBOX = D / CW;
+  constexpr int VCW = DV < 64 ? DV : 64;
+  constexpr int NVBOX = DV / VCW;
+  constexpr int NP = SUM ? M * M : M;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  using L = FwdSmem<D, DV>;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ FwdBarriers bars;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T_ = p.T;
+  const int nqt = (T_ + kBT - 1) / kBT;
+  const int qt = nqt - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
+  const int bh = blockIdx.y, b = bh / p.HQ, hq = bh % p.HQ, h = hq / p.G;
+  const int t0 = qt * kBT;
+  const int nk = qt + 1;  // causal: key tiles 0..qt
+  WaitCtx wc{p.status, &bars.abort_flag};
+
+  if (threadIdx.x == 0) {
+    bars.abort_flag = 0;
+    mbar_init(&bars.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.k_full[i], 1);
+      mbar_init(&bars.k_empty[i], 1);
+      mbar_init(&bars.v_full[i], 1);
+      mbar_init(&bars.v_empty[i], 1);
+      mbar_init(&bars.p_full[i], 8);
+      mbar_init(&bars.p_empty[i], 1);
+    }
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&bars.s_full[i], 1);
+      mbar_init(&bars.s_empty[i], 8);
+    }
+    mbar_init(&bars.o_full, 1);
+    mbar_init(&bars.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(&bars.q_full, L::Q_BYTES);
+      for (int bx = 0; bx < NBOX; ++bx)
+        tma_load_4d(smem + L::OFF_Q + bx * (kBT * CW * 2), &tmQ, &bars.q_full, bx * CW, hq, t0, b);
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&bars.k_empty[st], ph ^ 1, wc)) break;
+        mbar_arrive_expect_tx(&bars.k_full[st], L::K_BYTES);
+        uint8_t* sk = smem + L::OFF_K + st * L::K_BYTES;
+        for (int bx = 0; bx < NBOX; ++bx)
+          tma_load_4d(sk + bx * (kBK * CW * 2), &tmK, &bars.k_full[st], bx * CW, h, j * kBK, b);
+        issued_k = j + 1;
+        if (!mbar_wait(&bars.v_empty[st], ph ^ 1, wc)) break;
+        mbar_arrive_expect_tx(&bars.v_full[st], L::V_BYTES);
+        uint8_t* sv = smem + L::OFF_V + st * L::V_BYTES;
+        for (int bx = 0; bx < NVBOX; ++bx)
+          tma_load_4d(sv + bx * (kBK * VCW * 2), &tmV, &bars.v_full[st], bx * VCW, h, j * kBK, b);
+        issued_v = j + 1;
+      }
+      if (*wc.abort) {
+        // drain: wait (bounded) for the most recent copies of each stage so no TMA write lands
+        // in shared memory after the CTA retires.
+        for (int j = (issued_k > 2 ? issued_k - 2 : 0); j < issued_k; ++j)
+          mbar_drain(&bars.k_full[j & 1], (j >> 1) & 1);
+        for (int j = (issued_v > 2 ? issued_v - 2 : 0); j < issued_v; ++j)
+          mbar_drain(&bars.v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = umma_idesc_f16(128, kBK, kBF16, false, false);
+      const uint32_t idesc_pv = umma_idesc_f16(128, DV, kBF16, false, true);
+      const uint32_t sQ = smem_u32(smem + L::OFF_Q);
+      bool ok = mbar_wait(&bars.q_full, 0, wc);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&bars.p_full[st], ph, wc)) return false;
+        if (!mbar_wait(&bars.v_full[st], ph, wc)) return false;
+        tc_fence_after();
+        const uint32_t sP = smem_u32(smem + L::OFF_P + st * L::P_BYTES);
+        const uint32_t sV = smem_u32(smem + L::OFF_V + st * L::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // P: K-major 128x128, two 64-column boxes of 16 KB, SW128
+          const uint64_t ad = umma_smem_desc(sP + (kk >> 2) * 16384u + (kk & 3) * 32u, 16u, 1024u, 128);
+          // V: MN-major, rows = keys (K), boxes of VCW columns (N); LBO = box stride
+          const uint64_t bd = umma_smem_desc(sV + kk * 16u * (VCW * 2u), kBK * VCW * 2u, 8u * VCW * 2u, VCW * 2);
+          umma_ss(tbase + kOCol, ad, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars.p_empty[st]);
+        umma_commit(&bars.v_empty[st]);
+        return true;
+      };
+      int u = 0;
+      for (int j = 0; ok && j < nk; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bars.k_full[st], (j >> 1) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sK = smem_u32(smem + L::OFF_K + st * L::K_BYTES);
+        for (int pp = 0; pp < NP; ++pp, ++u) {
+          const int slot = u % kSlots;
+          if (!mbar_wait(&bars.s_empty[slot], ((u / kSlots) & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+#pragma unroll
+          for (int kk = 0; kk < E / 16; ++kk) {
+            umma_ss(tbase + slot * 128u, grp_kmajor_desc<CW>(sQ, ga, E, kk), grp_kmajor_desc<CW>(sK, gb, E, kk),
+                    idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars.s_full[slot]);
+        }
+        if (!ok) break;
+        umma_commit(&bars.k_empty[st]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) ok = issue_pv(nk - 1);
+      if (ok) umma_commit(&bars.o_full);
+      // drain outstanding MMAs before the CTA can retire
+      umma_commit(&bars.drain);
+      mbar_drain(&bars.drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ compute warpgroups
+    const int cw = warp - kComputeWarp0;  // 0..7
+    const int hc = cw >> 2;               // column half
+    const int quarter = warp & 3;         // TMEM lane quarter
+    const int row = quarter * 32 + lane;  // query row within the tile
+    const int t = t0 + row;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float scale2 = p.scale * p.scale;
+    float c_t = 0.f;
+    const float* cbase = nullptr;
+    if (DECAY) {
+      cbase = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
+      c_t = (t < T_) ? cbase[static_cast<size_t>(t) * p.HQ] : 0.f;
+    }
+    float den = 0.f;
+    bool ok = true;
+    int u = 0;
+    for (int j = 0; j < nk && ok; ++j) {
+      float2 acc[32];
+      for (int pp = 0; pp < NP; ++pp, ++u) {
+        const int slot = u % kSlots;
+        if (!mbar_wait(&bars.s_full[slot], (u / kSlots) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        const uint32_t a = lane_addr + slot * 128u + hc * 64u;
+        tmem_ld32(a, r0);
+        tmem_ld32(a + 32u, r1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.s_empty[slot]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+          const float2 x1 = make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+          if (pp == 0) {
+            acc[i] = fmul2(x0, x0);
+            acc[16 + i] = fmul2(x1, x1);
+          } else {
+            acc[i] = ffma2(x0, x0, acc[i]);
+            acc[16 + i] = ffma2(x1, x1, acc[16 + i]);
+          }
+        }
+      }
+      if (!ok) break;
+      // A = scale^2 * acc, causal mask on the diagonal tile, optional decay; row sum; P -> smem
+      const float2 sc2 = make_float2(scale2, scale2);
+      const int s_base = j * kBK + hc * 64;
+      const bool diag = (j == qt);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float2 x = fmul2(acc[i], sc2);
+        const int s0 = s_base + 2 * i;
+        if (diag) {
+          if (s0 > t) x.x = 0.f;
+          if (s0 + 1 > t) x.y = 0.f;
+        }
+        if (DECAY) {
+          const float cs0 = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
+          const float cs1 = (s0 + 1 < T_) ? __ldg(cbase + static_cast<size_t>(s0 + 1) * p.HQ) : 0.f;
+          x.x *= __expf(fminf(c_t - cs0, 0.f));
+          x.y *= __expf(fminf(c_t - cs1, 0.f));
+        }
+        acc[i] = x;
+      }
+      float2 rs = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) rs = fadd2(rs, acc[i]);
+      den += rs.x + rs.y;
+      const int pst = j & 1;
+      if (!mbar_wait(&bars.p_empty[pst], ((j >> 1) & 1) ^ 1, wc)) {
+        ok = false;
+        break;
+      }
+      const uint32_t pbase = smem_u32(smem + L::OFF_P + pst * L::P_BYTES) + hc * 16384u;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint32_t w0 = pack2<T>(acc[4 * ch + 0].x, acc[4 * ch + 0].y);
+        const uint32_t w1 = pack2<T>(acc[4 * ch + 1].x, acc[4 * ch + 1].y);
+        const uint32_t w2 = pack2<T>(acc[4 * ch + 2].x, acc[4 * ch + 2].y);
+        const uint32_t w3 = pack2<T>(acc[4 * ch + 3].x, acc[4 * ch + 3].y);
+        st_shared_v4(pbase + swz_offset(row, ch * 16, 128), w0, w1, w2, w3);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.p_full[pst]);
+    }
+    // ------------------------------------------------------------------ epilogue
+    bars.den_x[hc][row] = den;
+    named_bar_sync(1, 256);
+    const float den_all = bars.den_x[0][row] + bars.den_x[1][row];
+    if (ok && mbar_wait(&bars.o_full, 0, wc)) {
+      tc_fence_after();
+      const float inv = 1.f / (den_all > 0.f ? den_all : 1.f);
+      constexpr int HALF = DV / 2;
+      T* orow = static_cast<T*>(p.o) + ((static_cast<size_t>(b) * T_ + t) * p.HQ + hq) * DV + hc * HALF;
+#pragma unroll
+      for (int c0 = 0; c0 < HALF; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(lane_addr + kOCol + hc * HALF + c0, r);
+        tmem_wait_ld();
+        if (t < T_) {
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v4 + 0]) * inv, __uint_as_float(r[8 * v4 + 1]) * inv);
+            w.y = pack2<T>(__uint_as_float(r[8 * v4 + 2]) * inv, __uint_as_float(r[8 * v4 + 3]) * inv);
+            w.z = pack2<T>(__uint_as_float(r[8 * v4 + 4]) * inv, __uint_as_float(r[8 * v4 + 5]) * inv);
+            w.w = pack2<T>(__uint_as_float(r[8 * v4 + 6]) * inv, __uint_as_float(r[8 * v4 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c0 + 8 * v4) = w;
+          }
+        }
+      }
+      if (hc == 0 && t < T_) p.den[(static_cast<size_t>(b) * T_ + t) * p.HQ + hq] = den_all;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
+  constexpr int E = D / M;
+  constexpr int CW = E < 64 ? E : 64;
+  constexpr int VCW = DV < 64 ? DV : 64;
+  CUtensorMap tq, tk, tv;
+  const uint64_t es = 2;
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(p.HQ), static_cast<uint64_t>(p.T),
+                              static_cast<uint64_t>(p.B)};
+    const uint64_t str[3] = {D * es, D * es * p.HQ, D * es * p.HQ * p.T};
+    const uint32_t box[4] = {CW, 1, kBT, 1};
+    int e = encode_tmap_16bit(&tq, p.q, 4, dims, str, box, CW * 2);
+    if (e) return e;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(p.H), static_cast<uint64_t>(p.T),
+                              static_cast<uint64_t>(p.B)};
+    const uint64_t str[3] = {D * es, D * es * p.H, D * es * p.H * p.T};
+    const uint32_t box[4] = {CW, 1, kBK, 1};
+    int e = encode_tmap_16bit(&tk, p.k, 4, dims, str, box, CW * 2);
+    if (e) return e;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(DV), static_cast<uint64_t>(p.H), static_cast<uint64_t>(p.T),
+                              static_cast<uint64_t>(p.B)};
+    const uint64_t str[3] = {DV * es, DV * es * p.H, DV * es * p.H * p.T};
+    const uint32_t box[4] = {VCW, 1, kBK, 1};
+    int e = encode_tmap_16bit(&tv, p.v, 4, dims, str, box, VCW * 2);
+    if (e) return e;
+  }
+  const size_t smem = FwdSmem<D, DV>::TOTAL + 1024;
+  auto kern = attn_fwd_tc<T, D, DV, M, SUM, DECAY>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return KATA_ERR_CUDA;
+  const dim3 grid((p.T + kBT - 1) / kBT, p.B * p.HQ);
+  kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  return from_cuda(cudaGetLastError());
+}
+
+template <typename T, int D, int DV, int M>
+int dispatch_variant(const AttnFwdParams& p, bool sum, cudaStream_t st) {
+  const bool dec = p.c != nullptr;
+  if (sum) {
+    // the reference pairs decay with the concat score only (kata/layer.py:187-193)
+    if constexpr (M * M <= 16) {
+      if (!dec) return launch_fwd<T, D, DV, M, true, false>(p, st);
+    }
+    return KATA_ERR_UNSUPPORTED;
+  }
+  return dec ? launch_fwd<T, D, DV, M, false, true>(p, st) : launch_fwd<T, D, DV, M, false, false>(p, st);
+}
+
+template <typename T, int D, int DV>
+int dispatch_m(const AttnFwdParams& p, bool sum, cudaStream_t st) {
+  switch (p.M) {
+    case 1: return dispatch_variant<T, D, DV, 1>(p, sum, st);
+    case 2: return dispatch_variant<T, D, DV, 2>(p, sum, st);
+    case 4: return dispatch_variant<T, D, DV, 4>(p, sum, st);
+    default: break;
+  }
+  if constexpr (D / 8 >= 16) {
+    if (p.M == 8) return dispatch_variant<T, D, DV, 8>(p, sum, st);
+  }
+  return KATA_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+int dispatch_dims(const AttnFwdParams& p, bool sum, cudaStream_t st) {
+  if (p.D == 128 && p.Dv == 128) return dispatch_m<T, 128, 128>(p, sum, st);
+  if (p.D == 64 && p.Dv == 64) return dispatch_m<T, 64, 64>(p, sum, st);
+  return KATA_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+bool tc_fwd_supported(int dtype, int D, int Dv, int M, bool sum) {
+  if (dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return false;
+  if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128))) return false;
+  if (!(M == 1 || M == 2 || M == 4 || M == 8) || D % M) return false;
+  if ((D / M) % 16) return false;
+  if (sum && M * M > 16) return false;
+  return true;
+}
+
+bool tc_fwd_supports_decay(bool sum) { return !sum; }
+
+int tc_attn_fwd(const AttnFwdParams& p, int dtype, bool sum, cudaStream_t st) {
+  if (!tc_fwd_supported(dtype, p.D, p.Dv, p.M, sum)) return KATA_ERR_UNSUPPORTED;
+  return dtype == KATA_DTYPE_BF16 ? dispatch_dims<__nv_bfloat16>(p, sum, st) : dispatch_dims<__half>(p, sum, st);
+}
+
+}  // namespace kata

@@ -1,0 +1,84 @@
+// capi_attn.cu -- C-ABI entry points for causal KATA-SPD attention: argument validation and
+// dispatch between the tcgen05 tensor-core kernels and the fp32-exact SIMT kernels.
+#include "attn_common.cuh"
+#include "host_util.h"
+
+namespace kata {
+bool simt_supported(int D, int Dv, int M, bool sum);
+int simt_attn_fwd(const AttnFwdParams& p, int dtype, bool sum, cudaStream_t st);
+int simt_attn_bwd(const AttnBwdParams& p, int dtype, bool sum, cudaStream_t st);
+bool tc_fwd_supported(int dtype, int D, int Dv, int M, bool sum);
+bool tc_bwd_supported(int dtype, int D, int Dv, int M, bool sum);
+int tc_attn_fwd(const AttnFwdParams& p, int dtype, bool sum, cudaStream_t st);
+int tc_attn_bwd(const AttnBwdParams& p, int dtype, bool sum, cudaStream_t st);
+}  // namespace kata
+
+using namespace kata;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int dtype, int B, int T, int H, int HQ, int D, int Dv, int M, int score) {
+  if (dtype != KATA_DTYPE_F32 && dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (B < 1 || T < 1 || H < 1 || HQ < 1 || D < 1 || Dv < 1 || M < 1) return KATA_ERR_SHAPE;
+  if (HQ % H != 0 || D % M != 0) return KATA_ERR_SHAPE;
+  if (score != KATA_SCORE_CONCAT && score != KATA_SCORE_SUM) return KATA_ERR_INVALID;
+  if (static_cast<long long>(B) * T * HQ * (D > Dv ? D : Dv) >= (1ll << 40)) return KATA_ERR_SHAPE;
+  return KATA_OK;
+}
+
+// Chooses the kernel family: 1 = tensor cores, 2 = SIMT, or a negative error.
+int choose_algo(int algo, bool tc_ok, bool simt_ok, int dtype) {
+  if (algo == KATA_ALGO_TC) return tc_ok ? 1 : KATA_ERR_UNSUPPORTED;
+  if (algo == KATA_ALGO_SIMT) return simt_ok ? 2 : KATA_ERR_UNSUPPORTED;
+  if (algo != KATA_ALGO_AUTO) return KATA_ERR_INVALID;
+  if (dtype != KATA_DTYPE_F32 && tc_ok) return 1;
+  return simt_ok ? 2 : KATA_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" int kata_attn_fwd(const kata_attn_fwd_args* a, kata_stream_t stream) {
+  if (!a) return KATA_ERR_INVALID;
+  int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
+  if (e) return e;
+  if (!a->q || !a->k || !a->v || !a->o || !a->den) return KATA_ERR_INVALID;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return KATA_ERR_ALIGN;
+  const bool sum = a->score == KATA_SCORE_SUM;
+  const bool tc_ok = tc_fwd_supported(a->dtype, a->D, a->Dv, a->M, sum) && !(a->c && sum);
+  const int alg = choose_algo(a->algo, tc_ok, simt_supported(a->D, a->Dv, a->M, sum), a->dtype);
+  if (alg < 0) return alg;
+  AttnFwdParams p{a->q, a->k, a->v, a->c, a->o, a->den, a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
+                  a->HQ / a->H, a->scale};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return alg == 1 ? tc_attn_fwd(p, a->dtype, sum, st) : simt_attn_fwd(p, a->dtype, sum, st);
+}
+
+extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
+  if (!a) return 0;
+  // delta = <o, dO> per (b, t, hq), fp32
+  return sizeof(float) * static_cast<size_t>(a->B) * a->T * a->HQ;
+}
+
+extern "C" int kata_attn_bwd(const kata_attn_bwd_args* a, kata_stream_t stream) {
+  if (!a) return KATA_ERR_INVALID;
+  int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
+  if (e) return e;
+  if (!a->q || !a->k || !a->v || !a->o || !a->den || !a->dout || !a->dq || !a->dk || !a->dv) return KATA_ERR_INVALID;
+  if (a->c && !a->dc) return KATA_ERR_INVALID;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) || !aligned16(a->dout) ||
+      !aligned16(a->dq) || !aligned16(a->dk) || !aligned16(a->dv))
+    return KATA_ERR_ALIGN;
+  const size_t need = kata_attn_bwd_workspace_bytes(a);
+  if (need && (!a->workspace || a->workspace_bytes < need)) return KATA_ERR_WORKSPACE;
+  const bool sum = a->score == KATA_SCORE_SUM;
+  const bool tc_ok = tc_bwd_supported(a->dtype, a->D, a->Dv, a->M, sum) && !(a->c && sum);
+  const int alg = choose_algo(a->algo, tc_ok, simt_supported(a->D, a->Dv, a->M, sum), a->dtype);
+  if (alg < 0) return alg;
+  AttnBwdParams p{a->q,  a->k,  a->v,  a->o,  a->den, a->dout, a->c,  a->dq, a->dk,           a->dv,
+                  a->dc, static_cast<float*>(a->workspace), a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
+                  a->HQ / a->H, a->scale};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return alg == 1 ? tc_attn_bwd(p, a->dtype, sum, st) : simt_attn_bwd(p, a->dtype, sum, st);
+}

@@ -1,0 +1,82 @@
+"""The C-ABI library builds, loads, exports every symbol declared in include/*.h, and rejects bad
+arguments on the host (these paths never touch a GPU)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    syms = set()
+    for h in (ROOT / "include").glob("*.h"):
+        for m in re.finditer(r"KATA_API\s+[\w\s\*]+?\b(kata_\w+)\s*\(", h.read_text()):
+            syms.add(m.group(1))
+    return sorted(syms)
+
+
+@pytest.fixture(scope="module")
+def L():
+    from linatt_b200 import build, _lib
+
+    build.build()
+    return _lib.lib()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for s in ("kata_attn_fwd", "kata_attn_bwd", "kata_attn_bwd_workspace_bytes", "kata_strerror",
+              "kata_abi_version"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(L):
+    for s in declared_symbols():
+        assert hasattr(L, s), f"{s} not exported"
+
+
+def test_abi_version_and_strerror(L):
+    from linatt_b200 import _lib
+
+    assert L.kata_abi_version() == _lib.ABI_VERSION
+    assert L.kata_strerror(0) == b"ok"
+    assert b"workspace" in L.kata_strerror(-5)
+    assert L.kata_strerror(12345) == b"unknown error"
+
+
+def test_host_side_validation(L):
+    from linatt_b200 import _lib
+
+    assert L.kata_attn_fwd(None, None) == -1
+    a = _lib.AttnFwdArgs(dtype=7, B=1, T=8, H=1, HQ=1, D=64, Dv=64, M=4, score=0, algo=0, scale=1.0)
+    assert L.kata_attn_fwd(a, None) == -2  # dtype
+    a = _lib.AttnFwdArgs(dtype=1, B=1, T=8, H=2, HQ=3, D=64, Dv=64, M=4, score=0, algo=0, scale=1.0)
+    assert L.kata_attn_fwd(a, None) == -3  # HQ % H
+    a = _lib.AttnFwdArgs(dtype=1, B=1, T=8, H=1, HQ=1, D=64, Dv=64, M=3, score=0, algo=0, scale=1.0)
+    assert L.kata_attn_fwd(a, None) == -3  # D % M
+    a = _lib.AttnFwdArgs(dtype=1, B=1, T=8, H=1, HQ=1, D=64, Dv=64, M=4, score=0, algo=0, scale=1.0)
+    assert L.kata_attn_fwd(a, None) == -1  # null pointers
+    a = _lib.AttnFwdArgs(q=16, k=16, v=16, o=24, den=16, dtype=1, B=1, T=8, H=1, HQ=1, D=64, Dv=64, M=4, score=0,
+                         algo=0, scale=1.0)
+    assert L.kata_attn_fwd(a, None) == -4  # misaligned o
+    b = _lib.AttnBwdArgs(q=16, k=16, v=16, o=16, den=16, dout=16, dq=16, dk=16, dv=16, dtype=1, B=2, T=8, H=1, HQ=2,
+                         D=64, Dv=64, M=4, score=0, algo=0, scale=1.0)
+    assert L.kata_attn_bwd_workspace_bytes(b) == 4 * 2 * 8 * 2
+    assert L.kata_attn_bwd(b, None) == -5  # workspace missing
+    b.c = 16
+    assert L.kata_attn_bwd(b, None) == -1  # decay without dc
+
+
+def test_product_path_refuses_cpu_tensors():
+    import torch
+
+    from linatt_b200.parallel_kata_attn import parallel_kata_attn
+
+    q = torch.randn(1, 8, 1, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        parallel_kata_attn(q, q, q, num_groups=4)

@@ -1,0 +1,49 @@
+"""Device check of the tcgen05 / TMA encodings (shared-memory descriptors for every swizzle and
+major-ness, TMEM-sourced A operand) used by the attention kernels, against a plain GEMM."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+# (N, K, a_mn, b_mn, a_sw, b_sw, a_tmem)
+CASES = [
+    (128, 128, 0, 0, 128, 128, 0),
+    (128, 64, 0, 0, 64, 64, 0),
+    (128, 32, 0, 0, 32, 32, 0),
+    (64, 128, 0, 0, 128, 64, 0),
+    (128, 128, 0, 1, 128, 128, 0),
+    (64, 128, 0, 1, 128, 128, 0),
+    (32, 128, 0, 1, 128, 64, 0),
+    (16, 64, 0, 1, 64, 32, 0),
+    (128, 128, 1, 0, 128, 128, 0),
+    (128, 64, 1, 1, 128, 128, 0),
+    (256, 64, 0, 0, 128, 128, 0),
+    (128, 128, 0, 0, 128, 128, 1),
+    (128, 64, 0, 1, 128, 128, 1),
+    (32, 128, 0, 1, 128, 64, 1),
+]
+
+
+@pytest.mark.parametrize("N,K,a_mn,b_mn,a_sw,b_sw,a_tmem", CASES)
+def test_umma_selftest(N, K, a_mn, b_mn, a_sw, b_sw, a_tmem):
+    from linatt_b200 import _lib
+
+    L = _lib.lib()
+    M = 128
+    g = torch.Generator(device="cuda").manual_seed(N * 1000 + K)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    As = A.t().contiguous() if a_mn else A.contiguous()
+    Bs = B.t().contiguous() if b_mn else B.contiguous()
+    D = torch.full((M, N), float("nan"), device="cuda")
+    rc = L.kata_selftest_umma(As.data_ptr(), Bs.data_ptr(), D.data_ptr(), M, N, K, a_mn, b_mn, a_sw, b_sw, a_tmem,
+                              torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "kata_selftest_umma")
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().t()
+    err = (D - ref).norm() / ref.norm()
+    assert torch.isfinite(D).all()
+    assert err < 1e-5, f"rel err {err.item():.3e}"

@@ -1,0 +1,78 @@
+"""The CPU oracle against the golden fixtures produced by the reference's own code."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import kata_oracle as ko
+from tests.conftest import attn_case_meta
+
+ATTN_CASES = ["concat_m1", "concat_m2", "concat_m4", "concat_m4_d128", "sum_m2", "sum_m4", "decay_m2",
+              "decay_m4", "gqa_m2"]
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_oracle_forward_matches_reference(golden, case):
+    rec = golden[case]
+    m = attn_case_meta(rec)
+    scale = 1.0 / math.sqrt(m["D"] // m["M"])
+    o, den = ko.attn_fwd(rec["q"], rec["k"], rec["v"], m["M"], scale, m["score"], rec.get("c"))
+    # Triton K1/K2 (interpreter, fp32) and the float64 torch reference
+    assert ko.rel_l2(o, rec["o"]) < 2e-6
+    assert ko.rel_l2(den, rec["den"]) < 2e-6
+    if "o_ref64" in rec:
+        assert ko.rel_l2(o, rec["o_ref64"]) < 1e-6
+
+
+@pytest.mark.parametrize("case", ATTN_CASES)
+def test_oracle_backward_matches_reference(golden, case):
+    rec = golden[case]
+    m = attn_case_meta(rec)
+    scale = 1.0 / math.sqrt(m["D"] // m["M"])
+    dq, dk, dv, dc = ko.attn_bwd(rec["q"], rec["k"], rec["v"], rec["do"], m["M"], scale, m["score"], rec.get("c"))
+    for name, x in (("dq", dq), ("dk", dk), ("dv", dv)):
+        assert ko.rel_l2(x, rec[name]) < 2e-6, name
+    if m["decay"]:
+        assert ko.rel_l2(dc, rec["dc"]) < 2e-6
+
+
+def test_oracle_offset_gate_matches_reference(golden):
+    rec = golden["offset_m2"]
+    M, E = (int(x) for x in rec["meta"])
+    qi, ki = ko.augment_offset(rec["q"], rec["k"], rec["off"], M)
+    np.testing.assert_array_equal(qi.astype(np.float32), rec["q_in"])
+    np.testing.assert_array_equal(ki.astype(np.float32), rec["k_in"])
+
+
+def test_oracle_backward_is_gradient_of_forward():
+    """Finite-difference check of the closed-form backward (independent of the fixtures)."""
+    rng = np.random.default_rng(3)
+    B, T, H, D, M = 1, 9, 1, 8, 2
+    q, k, v, do = (rng.standard_normal((B, T, H, D)) for _ in range(4))
+    c = np.cumsum(-np.log1p(np.exp(rng.standard_normal((B, T, H)))), axis=1)
+    for score, cc in (("concat", None), ("sum", None), ("concat", c)):
+        dq, dk, dv, dc = ko.attn_bwd(q, k, v, do, M, 0.7, score, cc)
+
+        def f(qq, kk, vv, c2):
+            return float((ko.attn_fwd(qq, kk, vv, M, 0.7, score, c2)[0] * do).sum())
+
+        eps = 1e-6
+        for arr, grad, idx in ((q, dq, (0, 5, 0, 3)), (k, dk, (0, 2, 0, 6)), (v, dv, (0, 1, 0, 0))):
+            xp = arr.copy()
+            xp[idx] += eps
+            xm = arr.copy()
+            xm[idx] -= eps
+            args_p = [xp if a is arr else a for a in (q, k, v)]
+            args_m = [xm if a is arr else a for a in (q, k, v)]
+            num = (f(*args_p, cc) - f(*args_m, cc)) / (2 * eps)
+            assert abs(num - grad[idx]) < 1e-6 * max(1.0, abs(num))
+        if cc is not None:
+            cp = cc.copy()
+            cp[0, 4, 0] += eps
+            cm = cc.copy()
+            cm[0, 4, 0] -= eps
+            num = (f(q, k, v, cp) - f(q, k, v, cm)) / (2 * eps)
+            assert abs(num - dc[0, 4, 0]) < 1e-6 * max(1.0, abs(num))
