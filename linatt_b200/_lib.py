@@ -75,7 +75,7 @@ def lib() -> ctypes.CDLL:
             L.kata_attn_bwd_workspace_bytes.restype = c_size_t
             L.kata_attn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnBwdArgs)]
             L.kata_selftest_umma.restype = c_int
-            L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 9 + [c_void_p]
+            L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:
                 raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
             _lib = L

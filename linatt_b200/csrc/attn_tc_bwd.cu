@@ -1,17 +1,895 @@
 // attn_tc_bwd.cu -- tcgen05 tensor-core backward of causal KATA-SPD attention (bf16 / fp16).
-#include "attn_common.cuh"
-#include "host_util.h"
+//
+// Math (kata/parallel_kata_attn.py:49-146 concat, :579-653 sum; decay as autograd of :291-310):
+//   S_p = <q_a, k_b>,  A = scale^2 sum_p S_p^2 * dec,  P = A / den,  delta_t = <o_t, dO_t>
+//   dA[t,s]  = (dO_t . v_s - delta_t) / den_t                       (causal)
+//   W_p[t,s] = 2 scale^2 S_p[t,s] dec[t,s] dA[t,s]   (= d(loss)/d(q_a.k_b))
+//   dq_a = sum_b W_(a,b) k_b,  dk_b = sum_a W_(a,b)^T q_a,  dv = P^T dO
+//   dc_t = sum_s G[t,s] - sum_t' G[t',t],  G = dA * A on pairs with c_t - c_s <= 0
+//
+// Two kernels, each warp-specialised like the forward (warp 0 TMA, warp 1 TMEM owner and single
+// MMA issuer, warps 2..9 two compute warpgroups splitting the 128 columns of every score tile):
+//   dq kernel   one CTA per (query tile, batch*query head).  TMEM: S ring 2x128, dN = dO V^T (128),
+//               dQ (D).  Prologue computes delta and writes delta, 1/den and delta/den to the
+//               workspace for the second kernel; with decay it also writes dc_t = sum_s G[t,s].
+//   dkdv kernel one CTA per (key tile, batch*kv head) looping over the query tiles of every query
+//               head of its GQA group.  TMEM: S^T (128), dN^T = V dO^T (128), dK (D), dV (Dv).
+//               W^T and P^T are written as 128B-swizzled K-major smem tiles that feed
+//               dK += W^T Q (Q read MN-major) and dV += P^T dO (dO read MN-major); with decay it
+//               atomically subtracts sum_t G[t,s] from dc.
+// Every mbarrier wait is bounded; named barriers are only used outside the main loops so that an
+// aborting warp never strands the others.
+#include "attn_tc_common.cuh"
 
 namespace kata {
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int kComputeWarp0 = 2;
+constexpr int kRing = 3;
+
+struct BwdWs {
+  // workspace views (fp32), each 16-byte aligned:
+  //   delta (B,T,HQ) | rden (B,HQ,Tp) | delta*rden (B,HQ,Tp)   with Tp = T rounded up to 4,
+  // so that head-major rows start on 16-byte boundaries and even-index float2 loads are aligned.
+  float* delta;
+  float* rden;
+  float* dr;
+  int Tp;
+};
+__host__ __device__ inline BwdWs ws_views(float* base, int B, int T, int HQ) {
+  const int Tp = (T + 3) & ~3;
+  const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
+  const size_t n1 = static_cast<size_t>(B) * HQ * Tp;
+  return BwdWs{base, base + n0, base + n0 + n1, Tp};
+}
+
+template <int D, int DV>
+struct BwdSmem {
+  static constexpr int Q_BYTES = kTile * D * 2;
+  static constexpr int O_BYTES = kTile * DV * 2;
+  static constexpr int ITEM = Q_BYTES > O_BYTES ? Q_BYTES : O_BYTES;
+  static constexpr int T_BYTES = kTile * kTile * 2;  // P / W tiles
+  // dq kernel: Q, dO resident; ring of K/V tiles; W tile
+  static constexpr int DQ_OFF_Q = 0;
+  static constexpr int DQ_OFF_O = DQ_OFF_Q + Q_BYTES;
+  static constexpr int DQ_OFF_RING = DQ_OFF_O + O_BYTES;
+  static constexpr int DQ_OFF_W = DQ_OFF_RING + kRing * ITEM;
+  static constexpr int DQ_TOTAL = DQ_OFF_W + T_BYTES;
+  // dkdv kernel: K, V resident; ring of Q/dO tiles; P^T and W^T tiles
+  static constexpr int KV_OFF_K = 0;
+  static constexpr int KV_OFF_V = KV_OFF_K + Q_BYTES;
+  static constexpr int KV_OFF_RING = KV_OFF_V + O_BYTES;
+  static constexpr int KV_OFF_P = KV_OFF_RING + kRing * ITEM;
+  static constexpr int KV_OFF_W = KV_OFF_P + T_BYTES;
+  static constexpr int KV_TOTAL = KV_OFF_W + T_BYTES;
+};
+
+struct DqBars {
+  uint64_t qo_full;
+  uint64_t ring_full[kRing], ring_empty[kRing];
+  uint64_t dn_full, dn_empty;
+  uint64_t s_full[2], s_empty[2];
+  uint64_t w_full, w_empty;
+  uint64_t acc_done, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float xch_delta[2][kTile];
+  float xch_r[2][kTile];
+};
+
+struct DkvBars {
+  uint64_t kv_full;
+  uint64_t ring_full[kRing], ring_empty[kRing];
+  uint64_t dn_full, dn_empty;
+  uint64_t s_full, s_empty;
+  uint64_t w_full, w_empty;
+  uint64_t p_full, p_empty;
+  uint64_t acc_done, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ float2 u2f2(uint32_t a, uint32_t b) { return make_float2(__uint_as_float(a), __uint_as_float(b)); }
+
+// ================================================================================================
+// dq kernel
+// ================================================================================================
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                   AttnBwdParams p) {
+  constexpr int E = D / M;
+  constexpr int CW = BoxW<E>::value;
+  constexpr int NBOX = D / CW;
+  constexpr int VCW = BoxW<DV>::value;
+  constexpr int NVBOX = DV / VCW;
+  constexpr int NP = SUM ? M * M : M;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kColDN = 256, kColDQ = 384;
+  using L = BwdSmem<D, DV>;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ DqBars bars;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T_ = p.T;
+  const int nqt = (T_ + kTile - 1) / kTile;
+  const int qi = nqt - 1 - static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y, b = bh / p.HQ, hq = bh % p.HQ, h = hq / p.G;
+  const int t0 = qi * kTile;
+  const int nk = qi + 1;
+  WaitCtx wc{p.status, &bars.abort_flag};
+
+  if (threadIdx.x == 0) {
+    bars.abort_flag = 0;
+    mbar_init(&bars.qo_full, 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&bars.ring_full[i], 1);
+      mbar_init(&bars.ring_empty[i], 1);
+    }
+    mbar_init(&bars.dn_full, 1);
+    mbar_init(&bars.dn_empty, 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.s_full[i], 1);
+      mbar_init(&bars.s_empty[i], 8);
+    }
+    mbar_init(&bars.w_full, 8);
+    mbar_init(&bars.w_empty, 1);
+    mbar_init(&bars.acc_done, 1);
+    mbar_init(&bars.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmO);
+      mbar_arrive_expect_tx(&bars.qo_full, L::Q_BYTES + L::O_BYTES);
+      for (int bx = 0; bx < NBOX; ++bx)
+        tma_load_4d(smem + L::DQ_OFF_Q + bx * (kTile * CW * 2), &tmQ, &bars.qo_full, bx * CW, hq, t0, b);
+      for (int bx = 0; bx < NVBOX; ++bx)
+        tma_load_4d(smem + L::DQ_OFF_O + bx * (kTile * VCW * 2), &tmO, &bars.qo_full, bx * VCW, hq, t0, b);
+      int r = 0;
+      bool ok = true;
+      for (int j = 0; j < nk && ok; ++j) {
+        for (int item = 0; item < 2; ++item, ++r) {  // V_j then K_j
+          const int slot = r % kRing;
+          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + L::DQ_OFF_RING + slot * L::ITEM;
+          if (item == 0) {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
+            for (int bx = 0; bx < NVBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmV, &bars.ring_full[slot], bx * VCW, h, j * kTile, b);
+          } else {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
+            for (int bx = 0; bx < NBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, j * kTile, b);
+          }
+        }
+      }
+      if (!ok) {
+        for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
+          mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
+      const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
+      const uint32_t sQ = smem_u32(smem + L::DQ_OFF_Q);
+      const uint32_t sO = smem_u32(smem + L::DQ_OFF_O);
+      const uint32_t sW = smem_u32(smem + L::DQ_OFF_W);
+      bool ok = mbar_wait(&bars.qo_full, 0, wc);
+      int r = 0, u = 0;
+      for (int j = 0; ok && j < nk; ++j) {
+        // dN = dO V^T
+        const int slotV = r % kRing;
+        if (!mbar_wait(&bars.ring_full[slotV], (r / kRing) & 1, wc) || !mbar_wait(&bars.dn_empty, (j & 1) ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + L::DQ_OFF_RING + slotV * L::ITEM);
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk)
+          umma_ss(tbase + kColDN, kmajor_desc<VCW>(sO, 0, DV, kk), kmajor_desc<VCW>(sV, 0, DV, kk), id_nn,
+                  kk > 0 ? 1u : 0u);
+        umma_commit(&bars.dn_full);
+        umma_commit(&bars.ring_empty[slotV]);
+        ++r;
+        const int slotK = r % kRing;
+        if (!mbar_wait(&bars.ring_full[slotK], (r / kRing) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sK = smem_u32(smem + L::DQ_OFF_RING + slotK * L::ITEM);
+        auto issue_dq = [&](int pp, int uu) -> bool {
+          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+          if (!mbar_wait(&bars.w_full, uu & 1, wc)) return false;
+          tc_fence_after();
+          const bool first = (j == 0) && (!SUM || gb == 0);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_ss(tbase + kColDQ + ga * E, kmajor128_desc(sW, kk), mnmajor_desc<CW>(sK, gb * E / CW, kk), id_dq,
+                    (!first || kk > 0) ? 1u : 0u);
+          umma_commit(&bars.w_empty);
+          return true;
+        };
+        for (int pp = 0; pp < NP; ++pp, ++u) {
+          const int slot = u & 1;
+          if (!mbar_wait(&bars.s_empty[slot], ((u >> 1) & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+#pragma unroll
+          for (int kk = 0; kk < E / 16; ++kk)
+            umma_ss(tbase + slot * 128u, kmajor_desc<CW>(sQ, ga, E, kk), kmajor_desc<CW>(sK, gb, E, kk), id_nn,
+                    kk > 0 ? 1u : 0u);
+          umma_commit(&bars.s_full[slot]);
+          if (pp > 0 && !issue_dq(pp - 1, u - 1)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok || !issue_dq(NP - 1, u - 1)) {
+          ok = false;
+          break;
+        }
+        umma_commit(&bars.ring_empty[slotK]);
+        ++r;
+      }
+      if (ok) umma_commit(&bars.acc_done);
+      umma_commit(&bars.drain);
+      mbar_drain(&bars.drain, 0);
+    }
+  } else {
+    const int cw = warp - kComputeWarp0;
+    const int hc = cw >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int tg = t0 + row;
+    const bool live = tg < T_;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    const size_t rowidx = (static_cast<size_t>(b) * T_ + tg) * p.HQ + hq;  // (b, tg, hq)
+    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
+    // ---- delta_t = <o_t, dO_t> over this thread's half of Dv, then exchanged
+    float dpart = 0.f;
+    if (live) {
+      constexpr int HV = DV / 2;
+      const T* orow = static_cast<const T*>(p.o) + rowidx * DV + hc * HV;
+      const T* grow = static_cast<const T*>(p.dout) + rowidx * DV + hc * HV;
+#pragma unroll
+      for (int c8 = 0; c8 < HV; c8 += 8) {
+        const uint4 a = *reinterpret_cast<const uint4*>(orow + c8);
+        const uint4 g = *reinterpret_cast<const uint4*>(grow + c8);
+        const T* ah = reinterpret_cast<const T*>(&a);
+        const T* gh = reinterpret_cast<const T*>(&g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dpart = fmaf(to_f32<T>(ah[e]), to_f32<T>(gh[e]), dpart);
+      }
+    }
+    bars.xch_delta[hc][row] = dpart;
+    named_bar_sync(1, 256);
+    const float delta = bars.xch_delta[0][row] + bars.xch_delta[1][row];
+    float rden = 1.f;
+    if (live) {
+      const float dn = p.den[rowidx];
+      rden = 1.f / (dn > 0.f ? dn : 1.f);
+      if (hc == 0) {
+        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
+        ws.delta[rowidx] = delta;
+        ws.rden[hm] = rden;
+        ws.dr[hm] = delta * rden;
+      }
+    }
+    const float w_scale = 2.f * p.scale * p.scale;
+    const float scale2 = p.scale * p.scale;
+    float c_t = 0.f;
+    const float* cb = nullptr;
+    if (DECAY) {
+      cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
+      c_t = live ? cb[static_cast<size_t>(tg) * p.HQ] : 0.f;
+    }
+    float rsum = 0.f;
+    bool ok = true;
+    int u = 0;
+    const uint32_t sW = smem_u32(smem + L::DQ_OFF_W);
+    for (int j = 0; j < nk && ok; ++j) {
+      const bool diag = (j == qi);
+      if (!mbar_wait(&bars.dn_full, j & 1, wc)) {
+        ok = false;
+        break;
+      }
+      float2 acc[32];  // DECAY only: sum_p S_p^2 for this thread's 64 columns
+      for (int pp = 0; pp < NP; ++pp, ++u) {
+        const int slot = u & 1;
+        if (!mbar_wait(&bars.s_full[slot], (u >> 1) & 1, wc) || !mbar_wait(&bars.w_empty, (u & 1) ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t rs[32], rn[32];
+          tmem_ld32(lane_addr + slot * 128u + hc * 64u + c * 32u, rs);
+          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+          tmem_wait_ld();
+          if (c == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.s_empty[slot]);
+          }
+          const int cbase = hc * 64 + c * 32;  // key column within the tile
+          uint32_t wv[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const int s0 = cbase + 2 * x;
+            const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
+            const float2 nv = u2f2(rn[2 * x], rn[2 * x + 1]);
+            float da0 = (nv.x - delta) * rden, da1 = (nv.y - delta) * rden;
+            if (diag) {
+              if (s0 > row) da0 = 0.f;
+              if (s0 + 1 > row) da1 = 0.f;
+            }
+            float dec0 = 1.f, dec1 = 1.f;
+            if (DECAY) {
+              const int sg = j * kTile + s0;
+              const float cs0 = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
+              const float cs1 = sg + 1 < T_ ? __ldg(cb + static_cast<size_t>(sg + 1) * p.HQ) : 0.f;
+              dec0 = __expf(fminf(c_t - cs0, 0.f));
+              dec1 = __expf(fminf(c_t - cs1, 0.f));
+              const float2 sq = fmul2(sv, sv);
+              acc[16 * c + x] = pp == 0 ? sq : fadd2(acc[16 * c + x], sq);
+            }
+            wv[x] = pack2<T>(w_scale * sv.x * dec0 * da0, w_scale * sv.y * dec1 * da1);
+          }
+#pragma unroll
+          for (int m4 = 0; m4 < 4; ++m4)
+            st_tile128(sW, row, cbase + 8 * m4, wv[4 * m4], wv[4 * m4 + 1], wv[4 * m4 + 2], wv[4 * m4 + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.w_full);
+      }
+      if (!ok) break;
+      if (DECAY) {
+        // R_t += sum_s dA * A  over pairs with c_t - c_s <= 0 (A includes the decay factor)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t rn[32];
+          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+          tmem_wait_ld();
+          const int cbase = hc * 64 + c * 32;
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const int s0 = cbase + x;
+            const int sg = j * kTile + s0;
+            if (diag && s0 > row) continue;
+            const float cs = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
+            const float xd = c_t - cs;
+            if (xd > 0.f) continue;
+            const float2 a2 = acc[16 * c + (x >> 1)];
+            const float av = scale2 * ((x & 1) ? a2.y : a2.x) * __expf(xd);
+            rsum += (__uint_as_float(rn[x]) - delta) * rden * av;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.dn_empty);
+    }
+    // ---- epilogue: dQ -> global; dc_t = row sum of G
+    if (DECAY) bars.xch_r[hc][row] = rsum;
+    named_bar_sync(1, 256);
+    if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
+      tc_fence_after();
+      constexpr int HD = D / 2;
+      T* dqrow = static_cast<T*>(p.dq) + rowidx * D + hc * HD;
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + kColDQ + hc * HD + c0, r);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            *reinterpret_cast<uint4*>(dqrow + c0 + 8 * v2) = w;
+          }
+        }
+      }
+      if (DECAY && live && hc == 0) p.dc[rowidx] = bars.xch_r[0][row] + bars.xch_r[1][row];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ================================================================================================
+// dk / dv kernel
+// ================================================================================================
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                     AttnBwdParams p) {
+  constexpr int E = D / M;
+  constexpr int CW = BoxW<E>::value;
+  constexpr int NBOX = D / CW;
+  constexpr int VCW = BoxW<DV>::value;
+  constexpr int NVBOX = DV / VCW;
+  constexpr int NP = SUM ? M * M : M;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kColDN = 128, kColDK = 256, kColDV = 384;
+  using L = BwdSmem<D, DV>;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ DkvBars bars;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T_ = p.T;
+  const int nqt = (T_ + kTile - 1) / kTile;
+  const int kj = static_cast<int>(blockIdx.x);  // small j = most work, launched first
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int s0 = kj * kTile;
+  const int nq = nqt - kj;          // query tiles kj..nqt-1 per query head
+  const int nwork = p.G * nq;       // (query head, query tile) items
+  WaitCtx wc{p.status, &bars.abort_flag};
+
+  if (threadIdx.x == 0) {
+    bars.abort_flag = 0;
+    mbar_init(&bars.kv_full, 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&bars.ring_full[i], 1);
+      mbar_init(&bars.ring_empty[i], 1);
+    }
+    mbar_init(&bars.dn_full, 1);
+    mbar_init(&bars.dn_empty, 8);
+    mbar_init(&bars.s_full, 1);
+    mbar_init(&bars.s_empty, 8);
+    mbar_init(&bars.w_full, 8);
+    mbar_init(&bars.w_empty, 1);
+    mbar_init(&bars.p_full, 8);
+    mbar_init(&bars.p_empty, 1);
+    mbar_init(&bars.acc_done, 1);
+    mbar_init(&bars.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmO);
+      mbar_arrive_expect_tx(&bars.kv_full, L::Q_BYTES + L::O_BYTES);
+      for (int bx = 0; bx < NBOX; ++bx)
+        tma_load_4d(smem + L::KV_OFF_K + bx * (kTile * CW * 2), &tmK, &bars.kv_full, bx * CW, h, s0, b);
+      for (int bx = 0; bx < NVBOX; ++bx)
+        tma_load_4d(smem + L::KV_OFF_V + bx * (kTile * VCW * 2), &tmV, &bars.kv_full, bx * VCW, h, s0, b);
+      int r = 0;
+      bool ok = true;
+      for (int n = 0; n < nwork && ok; ++n) {
+        const int hq = h * p.G + n / nq;
+        const int ti = (kj + n % nq) * kTile;
+        for (int item = 0; item < 2; ++item, ++r) {  // Q_i then dO_i
+          const int slot = r % kRing;
+          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + L::KV_OFF_RING + slot * L::ITEM;
+          if (item == 0) {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
+            for (int bx = 0; bx < NBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * CW * 2), &tmQ, &bars.ring_full[slot], bx * CW, hq, ti, b);
+          } else {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
+            for (int bx = 0; bx < NVBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmO, &bars.ring_full[slot], bx * VCW, hq, ti, b);
+          }
+        }
+      }
+      if (!ok) {
+        for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
+          mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
+      const uint32_t id_dk = umma_idesc_f16(128, E, kBF16, false, true);
+      const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
+      const uint32_t sK = smem_u32(smem + L::KV_OFF_K);
+      const uint32_t sV = smem_u32(smem + L::KV_OFF_V);
+      const uint32_t sP = smem_u32(smem + L::KV_OFF_P);
+      const uint32_t sW = smem_u32(smem + L::KV_OFF_W);
+      bool ok = mbar_wait(&bars.kv_full, 0, wc);
+      int r = 0, u = 0;
+      for (int n = 0; ok && n < nwork; ++n, r += 2) {
+        const int slotQ = r % kRing, slotO = (r + 1) % kRing;
+        if (!mbar_wait(&bars.ring_full[slotO], ((r + 1) / kRing) & 1, wc) ||
+            !mbar_wait(&bars.dn_empty, (n & 1) ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sO = smem_u32(smem + L::KV_OFF_RING + slotO * L::ITEM);
+        // dN^T = V dO^T  (rows: keys, cols: queries)
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk)
+          umma_ss(tbase + kColDN, kmajor_desc<VCW>(sV, 0, DV, kk), kmajor_desc<VCW>(sO, 0, DV, kk), id_nn,
+                  kk > 0 ? 1u : 0u);
+        umma_commit(&bars.dn_full);
+        if (!mbar_wait(&bars.ring_full[slotQ], (r / kRing) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sQ = smem_u32(smem + L::KV_OFF_RING + slotQ * L::ITEM);
+        auto issue_dk = [&](int pp, int uu) -> bool {
+          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+          if (!mbar_wait(&bars.w_full, uu & 1, wc)) return false;
+          tc_fence_after();
+          const bool first = (n == 0) && (!SUM || ga == 0);
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_ss(tbase + kColDK + gb * E, kmajor128_desc(sW, kk), mnmajor_desc<CW>(sQ, ga * E / CW, kk), id_dk,
+                    (!first || kk > 0) ? 1u : 0u);
+          umma_commit(&bars.w_empty);
+          return true;
+        };
+        for (int pp = 0; pp < NP; ++pp, ++u) {
+          if (!mbar_wait(&bars.s_empty, (u & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+#pragma unroll
+          for (int kk = 0; kk < E / 16; ++kk)
+            umma_ss(tbase, kmajor_desc<CW>(sK, gb, E, kk), kmajor_desc<CW>(sQ, ga, E, kk), id_nn, kk > 0 ? 1u : 0u);
+          umma_commit(&bars.s_full);
+          if (pp > 0 && !issue_dk(pp - 1, u - 1)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok || !issue_dk(NP - 1, u - 1)) {
+          ok = false;
+          break;
+        }
+        umma_commit(&bars.ring_empty[slotQ]);
+        // dV += P^T dO
+        if (!mbar_wait(&bars.p_full, n & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_ss(tbase + kColDV, kmajor128_desc(sP, kk), mnmajor_desc<VCW>(sO, 0, kk), id_dv,
+                  (n > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&bars.p_empty);
+        umma_commit(&bars.ring_empty[slotO]);
+      }
+      if (ok) umma_commit(&bars.acc_done);
+      umma_commit(&bars.drain);
+      mbar_drain(&bars.drain, 0);
+    }
+  } else {
+    const int cw = warp - kComputeWarp0;
+    const int hc = cw >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // key row within the tile
+    const int sg = s0 + row;
+    const bool live = sg < T_;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
+    const float w_scale = 2.f * p.scale * p.scale;
+    const float scale2 = p.scale * p.scale;
+    const uint32_t sP = smem_u32(smem + L::KV_OFF_P);
+    const uint32_t sW = smem_u32(smem + L::KV_OFF_W);
+    bool ok = true;
+    int u = 0;
+    float csum = 0.f;
+    for (int n = 0; n < nwork && ok; ++n) {
+      const int hq = h * p.G + n / nq;
+      const int qi = kj + n % nq;
+      const bool diag = (qi == kj);
+      const size_t hm0 = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp;  // head-major row base
+      float c_s = 0.f;
+      const float* cb = nullptr;
+      if (DECAY) {
+        cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
+        c_s = live ? cb[static_cast<size_t>(sg) * p.HQ] : 0.f;
+      }
+      if (!mbar_wait(&bars.dn_full, n & 1, wc)) {
+        ok = false;
+        break;
+      }
+      float2 acc[32];
+      for (int pp = 0; pp < NP; ++pp, ++u) {
+        if (!mbar_wait(&bars.s_full, u & 1, wc) || !mbar_wait(&bars.w_empty, (u & 1) ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t rs[32], rn[32];
+          tmem_ld32(lane_addr + hc * 64u + c * 32u, rs);
+          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+          tmem_wait_ld();
+          if (c == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.s_empty);
+          }
+          const int cbase = hc * 64 + c * 32;  // query column within the tile
+          uint32_t wv[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const int tl = cbase + 2 * x;
+            const int tq = qi * kTile + tl;
+            const float2 rd = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.rden + hm0 + tq))
+                                          : make_float2(tq < T_ ? ws.rden[hm0 + tq] : 1.f, 1.f);
+            const float2 dr = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.dr + hm0 + tq))
+                                          : make_float2(tq < T_ ? ws.dr[hm0 + tq] : 0.f, 0.f);
+            const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
+            const float2 nv = u2f2(rn[2 * x], rn[2 * x + 1]);
+            float da0 = fmaf(nv.x, rd.x, -dr.x), da1 = fmaf(nv.y, rd.y, -dr.y);
+            if (diag) {
+              if (tl < row) da0 = 0.f;
+              if (tl + 1 < row) da1 = 0.f;
+            }
+            float dec0 = 1.f, dec1 = 1.f;
+            if (DECAY) {
+              const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
+              const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
+              dec0 = __expf(fminf(ct0 - c_s, 0.f));
+              dec1 = __expf(fminf(ct1 - c_s, 0.f));
+            }
+            const float2 sq = fmul2(sv, sv);
+            acc[16 * c + x] = pp == 0 ? sq : fadd2(acc[16 * c + x], sq);
+            wv[x] = pack2<T>(w_scale * sv.x * dec0 * da0, w_scale * sv.y * dec1 * da1);
+          }
+#pragma unroll
+          for (int m4 = 0; m4 < 4; ++m4)
+            st_tile128(sW, row, cbase + 8 * m4, wv[4 * m4], wv[4 * m4 + 1], wv[4 * m4 + 2], wv[4 * m4 + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.w_full);
+      }
+      if (!ok) break;
+      // P^T = A / den  (and, with decay, the column part of dc)
+      if (!mbar_wait(&bars.p_empty, (n & 1) ^ 1, wc)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int cbase = hc * 64 + c * 32;
+        uint32_t rn[32];
+        if (DECAY) {
+          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+          tmem_wait_ld();
+        }
+        uint32_t pv[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          const int tl = cbase + 2 * x;
+          const int tq = qi * kTile + tl;
+          const float2 rd = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.rden + hm0 + tq))
+                                        : make_float2(tq < T_ ? ws.rden[hm0 + tq] : 1.f, 1.f);
+          float a0 = scale2 * acc[16 * c + x].x, a1 = scale2 * acc[16 * c + x].y;
+          if (diag) {
+            if (tl < row) a0 = 0.f;
+            if (tl + 1 < row) a1 = 0.f;
+          }
+          if (DECAY) {
+            const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
+            const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
+            const float x0 = ct0 - c_s, x1 = ct1 - c_s;
+            a0 *= __expf(fminf(x0, 0.f));
+            a1 *= __expf(fminf(x1, 0.f));
+            const float2 dr = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.dr + hm0 + tq))
+                                          : make_float2(tq < T_ ? ws.dr[hm0 + tq] : 0.f, 0.f);
+            const float da0 = fmaf(__uint_as_float(rn[2 * x]), rd.x, -dr.x);
+            const float da1 = fmaf(__uint_as_float(rn[2 * x + 1]), rd.y, -dr.y);
+            if (x0 <= 0.f) csum += da0 * a0;
+            if (x1 <= 0.f) csum += da1 * a1;
+          }
+          pv[x] = pack2<T>(a0 * rd.x, a1 * rd.y);
+        }
+#pragma unroll
+        for (int m4 = 0; m4 < 4; ++m4)
+          st_tile128(sP, row, cbase + 8 * m4, pv[4 * m4], pv[4 * m4 + 1], pv[4 * m4 + 2], pv[4 * m4 + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars.p_full);
+        mbar_arrive(&bars.dn_empty);
+      }
+      if (DECAY && (n % nq == nq - 1)) {
+        // last query tile of this query head: dc_s -= sum_t G[t, s]
+        if (live) atomicAdd(p.dc + (static_cast<size_t>(b) * T_ + sg) * p.HQ + hq, -csum);
+        csum = 0.f;
+      }
+    }
+    // ---- epilogue: dK, dV -> global
+    named_bar_sync(1, 256);
+    if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
+      tc_fence_after();
+      constexpr int HD = D / 2, HV = DV / 2;
+      const size_t rowkv = (static_cast<size_t>(b) * T_ + sg) * p.H + h;
+      T* dkrow = static_cast<T*>(p.dk) + rowkv * D + hc * HD;
+      T* dvrow = static_cast<T*>(p.dv) + rowkv * DV + hc * HV;
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + kColDK + hc * HD + c0, r);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
+          }
+        }
+      }
+#pragma unroll
+      for (int c0 = 0; c0 < HV; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + kColDV + hc * HV + c0, r);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            *reinterpret_cast<uint4*>(dvrow + c0 + 8 * v2) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ================================================================================================
+// host side
+// ================================================================================================
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
+  constexpr int E = D / M;
+  constexpr int CW = BoxW<E>::value;
+  constexpr int VCW = BoxW<DV>::value;
+  using L = BwdSmem<D, DV>;
+  CUtensorMap tq, tk, tv, to;
+  int e = make_tm_tokens(&tq, p.q, p.B, p.T, p.HQ, D, CW);
+  if (!e) e = make_tm_tokens(&tk, p.k, p.B, p.T, p.H, D, CW);
+  if (!e) e = make_tm_tokens(&tv, p.v, p.B, p.T, p.H, DV, VCW);
+  if (!e) e = make_tm_tokens(&to, p.dout, p.B, p.T, p.HQ, DV, VCW);
+  if (e) return e;
+  const int nt = (p.T + kTile - 1) / kTile;
+  {
+    auto kern = attn_bwd_dq_tc<T, D, DV, M, SUM, DECAY>;
+    const size_t smem = L::DQ_TOTAL + 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return KATA_ERR_CUDA;
+    kern<<<dim3(nt, p.B * p.HQ), kThreads, smem, st>>>(tq, tk, tv, to, p);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
+  {
+    auto kern = attn_bwd_dkdv_tc<T, D, DV, M, SUM, DECAY>;
+    const size_t smem = L::KV_TOTAL + 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return KATA_ERR_CUDA;
+    kern<<<dim3(nt, p.B * p.H), kThreads, smem, st>>>(tq, tk, tv, to, p);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
+  return KATA_OK;
+}
+
+template <typename T, int D, int DV, int M>
+int bwd_variant(const AttnBwdParams& p, bool sum, cudaStream_t st) {
+  const bool dec = p.c != nullptr;
+  if (sum) {
+    if constexpr (M * M <= 16) {
+      if (!dec) return launch_bwd<T, D, DV, M, true, false>(p, st);
+    }
+    return KATA_ERR_UNSUPPORTED;
+  }
+  return dec ? launch_bwd<T, D, DV, M, false, true>(p, st) : launch_bwd<T, D, DV, M, false, false>(p, st);
+}
+
+template <typename T, int D, int DV>
+int bwd_m(const AttnBwdParams& p, bool sum, cudaStream_t st) {
+  switch (p.M) {
+    case 1: return bwd_variant<T, D, DV, 1>(p, sum, st);
+    case 2: return bwd_variant<T, D, DV, 2>(p, sum, st);
+    case 4: return bwd_variant<T, D, DV, 4>(p, sum, st);
+    default: break;
+  }
+  if constexpr (D / 8 >= 16) {
+    if (p.M == 8) return bwd_variant<T, D, DV, 8>(p, sum, st);
+  }
+  return KATA_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+int bwd_dims(const AttnBwdParams& p, bool sum, cudaStream_t st) {
+  if (p.D == 128 && p.Dv == 128) return bwd_m<T, 128, 128>(p, sum, st);
+  if (p.D == 64 && p.Dv == 64) return bwd_m<T, 64, 64>(p, sum, st);
+  return KATA_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+size_t tc_bwd_workspace_bytes(int B, int T, int HQ) {
+  const size_t Tp = (static_cast<size_t>(T) + 3) & ~static_cast<size_t>(3);
+  const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
+  return sizeof(float) * (n0 + 2 * static_cast<size_t>(B) * HQ * Tp);
+}
 
 bool tc_bwd_supported(int dtype, int D, int Dv, int M, bool sum) {
-  (void)dtype; (void)D; (void)Dv; (void)M; (void)sum;
-  return false;
+  if (dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return false;
+  if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128))) return false;
+  if (!(M == 1 || M == 2 || M == 4 || M == 8) || D % M) return false;
+  if ((D / M) % 16) return false;
+  if (sum && M * M > 16) return false;
+  return true;
 }
 
 int tc_attn_bwd(const AttnBwdParams& p, int dtype, bool sum, cudaStream_t st) {
-  (void)p; (void)dtype; (void)sum; (void)st;
-  return KATA_ERR_UNSUPPORTED;
+  if (!tc_bwd_supported(dtype, p.D, p.Dv, p.M, sum)) return KATA_ERR_UNSUPPORTED;
+  return dtype == KATA_DTYPE_BF16 ? bwd_dims<__nv_bfloat16>(p, sum, st) : bwd_dims<__half>(p, sum, st);
 }
 
 }  // namespace kata

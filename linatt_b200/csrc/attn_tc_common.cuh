@@ -1,0 +1,68 @@
+// attn_tc_common.cuh -- tile geometry, UMMA descriptor helpers and tensor-map construction
+// shared by the tcgen05 forward and backward attention kernels.
+//
+// Shared-memory tile layout.  A [128 rows][W cols] 16-bit tile is stored as W/CW TMA boxes of
+// [128 rows][CW cols], each box dense with CW*2-byte rows and the matching 32/64/128-byte swizzle
+// (CW = min(group width, 64)).  For the score operands the box width equals the group width E
+// (or 64 when E >= 64), so every group g of q/k is a whole number of boxes: its K-major slices
+// (score MMAs) and its MN-major slices (gradient MMAs) are both canonical UMMA layouts.
+#pragma once
+#include "attn_common.cuh"
+#include "host_util.h"
+#include "sm100.cuh"
+
+namespace kata {
+
+constexpr int kTile = 128;  // rows of every q/k/v/dO tile (= UMMA M)
+
+// K-major descriptor of K-step kk (16 elements) inside columns [g*E, (g+1)*E) of a tile stored as
+// boxes of CW columns, 128 rows each.
+template <int CW>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int g, int E, int kk) {
+  const int col = g * E + kk * 16;
+  const uint32_t box = static_cast<uint32_t>(col / CW);
+  const uint32_t within = static_cast<uint32_t>(col % CW) * 2u;
+  return umma_smem_desc(base + box * (kTile * CW * 2u) + within, 16u, 8u * CW * 2u, CW * 2);
+}
+
+// MN-major descriptor of K-step kk (16 rows of the tile) for the N extent starting at box
+// `box0` of a tile stored as boxes of CW columns (the N extent may span several boxes, LBO apart).
+template <int CW>
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int box0, int kk) {
+  const uint32_t box_bytes = kTile * CW * 2u;
+  return umma_smem_desc(base + static_cast<uint32_t>(box0) * box_bytes + static_cast<uint32_t>(kk) * 16u * (CW * 2u),
+                        box_bytes, 8u * CW * 2u, CW * 2);
+}
+
+// K-major descriptor of K-step kk of a [128][128] 16-bit tile written by threads as two
+// 128B-swizzled boxes of 64 columns (P / dA tiles).
+__device__ __forceinline__ uint64_t kmajor128_desc(uint32_t base, int kk) {
+  return umma_smem_desc(base + static_cast<uint32_t>(kk >> 2) * 16384u + static_cast<uint32_t>(kk & 3) * 32u, 16u,
+                        1024u, 128);
+}
+
+// Thread-side store of 8 consecutive 16-bit values (one 16-byte chunk) of row `row`, columns
+// [col0, col0+8) of a [128][128] tile stored as two 128B-swizzled boxes of 64 columns.
+__device__ __forceinline__ void st_tile128(uint32_t base, int row, int col0, uint32_t w0, uint32_t w1, uint32_t w2,
+                                           uint32_t w3) {
+  const uint32_t box = static_cast<uint32_t>(col0 >> 6);
+  const uint32_t byte = static_cast<uint32_t>(col0 & 63) * 2u;
+  st_shared_v4(base + box * 16384u + swz_offset(static_cast<uint32_t>(row), byte, 128), w0, w1, w2, w3);
+}
+
+// Tensor map over a time-major (B, T, heads, W) 16-bit tensor with boxes [cw cols][1][128 rows][1].
+inline int make_tm_tokens(CUtensorMap* tm, const void* base, int B, int T, int heads, int W, int cw) {
+  const uint64_t es = 2;
+  const uint64_t dims[4] = {static_cast<uint64_t>(W), static_cast<uint64_t>(heads), static_cast<uint64_t>(T),
+                            static_cast<uint64_t>(B)};
+  const uint64_t str[3] = {W * es, W * es * heads, W * es * heads * T};
+  const uint32_t box[4] = {static_cast<uint32_t>(cw), 1, kTile, 1};
+  return encode_tmap_16bit(tm, base, 4, dims, str, box, cw * 2);
+}
+
+template <int W>
+struct BoxW {
+  static constexpr int value = W < 64 ? W : 64;
+};
+
+}  // namespace kata

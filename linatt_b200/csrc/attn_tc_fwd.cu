@@ -17,9 +17,7 @@
 //               sum, and write P = half(A) into a 128B-swizzled K-major smem tile for the P*V MMA.
 //               Finally they read O from TMEM, divide by den and store o and den.
 // Every mbarrier wait is bounded (see sm100.cuh); a timeout records a status code and drains.
-#include "attn_common.cuh"
-#include "host_util.h"
-#include "sm100.cuh"
+#include "attn_tc_common.cuh"
 
 namespace kata {
 namespace {
@@ -56,21 +54,6 @@ struct FwdBarriers {
   int abort_flag;
   float den_x[2][kBT];  // partial row sums of the two column halves
 };
-
-template <typename T>
-struct FwdTma {
-  CUtensorMap q, k, v;
-};
-
-// UMMA descriptor of K-step `kk` (16 elements) of group `g` for a [rows=128][D] operand stored as
-// boxes of CW columns (CW*2 = swizzle span).
-template <int CW>
-__device__ __forceinline__ uint64_t grp_kmajor_desc(uint32_t base, int g, int E, int kk) {
-  const int col = g * E + kk * 16;
-  const uint32_t box = static_cast<uint32_t>(col / CW);
-  const uint32_t within = static_cast<uint32_t>(col % CW) * 2u;
-  return umma_smem_desc(base + box * (128u * CW * 2u) + within, 16u, 8u * CW * 2u, CW * 2);
-}
 
 template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -206,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk) {
-            umma_ss(tbase + slot * 128u, grp_kmajor_desc<CW>(sQ, ga, E, kk), grp_kmajor_desc<CW>(sK, gb, E, kk),
+            umma_ss(tbase + slot * 128u, kmajor_desc<CW>(sQ, ga, E, kk), kmajor_desc<CW>(sK, gb, E, kk),
                     idesc_qk, kk > 0 ? 1u : 0u);
           }
           umma_commit(&bars.s_full[slot]);
@@ -355,31 +338,10 @@ int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
   constexpr int CW = E < 64 ? E : 64;
   constexpr int VCW = DV < 64 ? DV : 64;
   CUtensorMap tq, tk, tv;
-  const uint64_t es = 2;
-  {
-    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(p.HQ), static_cast<uint64_t>(p.T),
-                              static_cast<uint64_t>(p.B)};
-    const uint64_t str[3] = {D * es, D * es * p.HQ, D * es * p.HQ * p.T};
-    const uint32_t box[4] = {CW, 1, kBT, 1};
-    int e = encode_tmap_16bit(&tq, p.q, 4, dims, str, box, CW * 2);
-    if (e) return e;
-  }
-  {
-    const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(p.H), static_cast<uint64_t>(p.T),
-                              static_cast<uint64_t>(p.B)};
-    const uint64_t str[3] = {D * es, D * es * p.H, D * es * p.H * p.T};
-    const uint32_t box[4] = {CW, 1, kBK, 1};
-    int e = encode_tmap_16bit(&tk, p.k, 4, dims, str, box, CW * 2);
-    if (e) return e;
-  }
-  {
-    const uint64_t dims[4] = {static_cast<uint64_t>(DV), static_cast<uint64_t>(p.H), static_cast<uint64_t>(p.T),
-                              static_cast<uint64_t>(p.B)};
-    const uint64_t str[3] = {DV * es, DV * es * p.H, DV * es * p.H * p.T};
-    const uint32_t box[4] = {VCW, 1, kBK, 1};
-    int e = encode_tmap_16bit(&tv, p.v, 4, dims, str, box, VCW * 2);
-    if (e) return e;
-  }
+  int e = make_tm_tokens(&tq, p.q, p.B, p.T, p.HQ, D, CW);
+  if (!e) e = make_tm_tokens(&tk, p.k, p.B, p.T, p.H, D, CW);
+  if (!e) e = make_tm_tokens(&tv, p.v, p.B, p.T, p.H, DV, VCW);
+  if (e) return e;
   const size_t smem = FwdSmem<D, DV>::TOTAL + 1024;
   auto kern = attn_fwd_tc<T, D, DV, M, SUM, DECAY>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)

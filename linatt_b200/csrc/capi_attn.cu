@@ -11,6 +11,7 @@ bool tc_fwd_supported(int dtype, int D, int Dv, int M, bool sum);
 bool tc_bwd_supported(int dtype, int D, int Dv, int M, bool sum);
 int tc_attn_fwd(const AttnFwdParams& p, int dtype, bool sum, cudaStream_t st);
 int tc_attn_bwd(const AttnBwdParams& p, int dtype, bool sum, cudaStream_t st);
+size_t tc_bwd_workspace_bytes(int B, int T, int HQ);
 }  // namespace kata
 
 using namespace kata;
@@ -56,9 +57,10 @@ extern "C" int kata_attn_fwd(const kata_attn_fwd_args* a, kata_stream_t stream) 
 }
 
 extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
-  if (!a) return 0;
-  // delta = <o, dO> per (b, t, hq), fp32
-  return sizeof(float) * static_cast<size_t>(a->B) * a->T * a->HQ;
+  if (!a || a->B < 1 || a->T < 1 || a->HQ < 1) return 0;
+  // fp32 delta = <o, dO> per (b, t, hq), plus 1/den and delta/den in a padded head-major layout
+  // for the tensor-core key-tile kernel (the SIMT kernels use the first part only)
+  return tc_bwd_workspace_bytes(a->B, a->T, a->HQ);
 }
 
 extern "C" int kata_attn_bwd(const kata_attn_bwd_args* a, kata_stream_t stream) {

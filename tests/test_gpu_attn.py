@@ -155,6 +155,13 @@ def test_half_precision_vs_oracle(dtype, B, T, HQ, H, D, M, score, decay):
     cc = c if decay else None
     got = run(pka, q, k, v, do, M, score, cc)
     ref = oracle(q.float(), k.float(), v.float(), do.float(), M, score, cc)
+    if T == 1:
+        # one token attends only to itself: o = v, and dq = dk = 0 exactly (dA = dO.v - <o,dO> = 0),
+        # so only o and dv carry a relative error; dq, dk must be tiny in absolute terms
+        assert_close(got, ref, TOL[dtype], names=("o", "dv"))
+        for n in ("dq", "dk"):
+            assert np.abs(got[n]).max() < 1e-2
+        return
     assert_close(got, ref, TOL[dtype])
 
 
