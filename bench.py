@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the KATA-SPD attention hot path (config 3 of the measurement plan).
+
+One *step* = forward + backward of causal concat-score KATA-SPD attention (num_groups M=4,
+bf16, fp32 accumulation) over one synthetic batch of B=16, T=4096, H=8, D=Dv=128 per GPU:
+three kernels (tcgen05 forward, backward dq pass, backward dk/dv pass).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun); every rank processes its own B*H shard of the same
+shape with no data-path collective ("scaling": "weak"); the step time is the max over ranks.
+
+Printed JSON line (rank 0):
+  value     whole-job tokens/s with inputs resident in HBM (device-timed with CUDA events)
+  e2e       the same metric through the public autograd API with pinned host buffers, including
+            the host->device copy of q, k, v, dO and the device->host copy of o, dq, dk, dv
+  roofline  the dominant kernel: algorithmic TFLOP per launch / its mean CUDA-event duration,
+            against the measured bf16 peak (MEASURED_PEAKS.json); traffic from the committed ncu
+            summary when available
+  cpu_baseline  the reference's CPU path (its PyTorch fp32 functions, restated in
+            oracle/kata_cpu_ref.py) on this host's cores, on a bounded sample of (b,h) slices
+  clocks    SM clock median / max and throttle reasons sampled through NVML during the timing
+
+L2: three rotating input sets (3 x 67 MB of bf16 q/k/v/dO) plus 84 MB of outputs are touched per
+cycle, more than the 126 MB L2, so no step reads inputs left in L2 by the previous step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, T, H, D, DV, M = 16, 4096, 8, 128, 128, 4
+METRIC = "KATA attn fwd+bwd tokens/s/GPU at B16·T4096·H8·D128; % of bf16 TC peak"
+UNIT = "tokens/s"
+
+
+def pairs(t: int) -> float:
+    return t * (t + 1) / 2.0
+
+
+# algorithmic FLOPs per launch (one B*H batch): GEMM-equivalent = 2 * P * 128 per head
+GEMM_EQ = B * H * 2.0 * pairs(T) * D
+ALG_FLOPS = {"fwd": 2 * GEMM_EQ, "bwd_dq": 1 * GEMM_EQ, "bwd_dkdv": 4 * GEMM_EQ}
+STEP_FLOPS = sum(ALG_FLOPS.values())  # 3.5 x forward
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "KATA-SPD flash attention fwd+bwd, concat score M=4, causal, bf16 (config 3)",
+        "batch_per_gpu": B, "global_batch": B * n_gpus, "seq_len": T, "heads": H, "head_dim": D,
+        "value_dim": DV, "num_groups": M, "score": "concat",
+        "parallelism": f"batch*head shard x{n_gpus}, no collective",
+        "l2": "3 rotating input sets (201 MB) + 84 MB outputs per cycle > 126 MB L2",
+    }
+
+
+def load_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def load_traffic(kernel: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(kernel, {}).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU reference path
+# ------------------------------------------------------------------------------------------------
+def cpu_reference(slices: int, warmup: int):
+    """Time the reference CPU path on `slices` (b,h) slices at full T; returns (tokens/s, cores, s/slice)."""
+    import torch
+
+    from oracle.kata_cpu_ref import fwd_bwd_slice
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = (torch.randn(1, T, 1, D, generator=g) / math.sqrt(D) for _ in range(4))
+    scale = 1.0 / math.sqrt(D // M)
+    for _ in range(warmup):
+        fwd_bwd_slice(q, k, v, do, M, scale)
+    t0 = time.perf_counter()
+    for _ in range(slices):
+        fwd_bwd_slice(q, k, v, do, M, scale)
+    per = (time.perf_counter() - t0) / slices
+    tok_s = (B * T) / (per * B * H)  # tokens of the full workload / time for its B*H slices
+    return tok_s, torch.get_num_threads(), per
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    steps, warmup = args.steps, args.warmup
+    tok_s, cores, per = cpu_reference(steps, warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": workload_config(world),
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{steps} (b,h) slices of fwd+bwd at T={T}, D={D}, M={M} "
+                                   f"(each step = 1 of the {B * H} slices of the workload)"},
+        "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a background thread (read-only)."""
+
+    NAMES = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+             0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+             0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period: float = 0.02):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                try:
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except Exception:
+                    rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._nv is not None:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        loaded = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        reasons = 0
+        for _, r in loaded:
+            reasons |= r
+        names = [n for bit, n in self.NAMES.items() if reasons & bit and bit != 0x1]
+        return {"sm_mhz": statistics.median(m for m, _ in loaded), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(loaded)}
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------------
+class AbiStep:
+    """One step through the C ABI with preallocated outputs: fwd, bwd dq pass, bwd dk/dv pass."""
+
+    def __init__(self, torch, dev, q, k, v, do):
+        from linatt_b200 import _lib
+
+        self.L = _lib.lib()
+        self._lib = _lib
+        self.dev = dev
+        self.o = torch.empty(B, T, H, DV, device=dev, dtype=torch.bfloat16)
+        self.den = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        self.dq = torch.empty(B, T, H, D, device=dev, dtype=torch.bfloat16)
+        self.dk = torch.empty_like(self.dq)
+        self.dv = torch.empty(B, T, H, DV, device=dev, dtype=torch.bfloat16)
+        self.status = _lib.status_word(dev)
+        scale = 1.0 / math.sqrt(D // M)
+        self.fa = _lib.AttnFwdArgs(o=self.o.data_ptr(), den=self.den.data_ptr(), status=self.status.data_ptr(),
+                                   dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=0, algo=1, scale=scale)
+        self.ba = _lib.AttnBwdArgs(o=self.o.data_ptr(), den=self.den.data_ptr(), dq=self.dq.data_ptr(),
+                                   dk=self.dk.data_ptr(), dv=self.dv.data_ptr(), status=self.status.data_ptr(),
+                                   dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=0, algo=1, scale=scale)
+        nbytes = self.L.kata_attn_bwd_workspace_bytes(self.ba)
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.ba.workspace = self.ws.data_ptr()
+        self.ba.workspace_bytes = nbytes
+        self.sets = []
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def bind(self, q, k, v, do):
+        self.fa.q, self.fa.k, self.fa.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+        self.ba.q, self.ba.k, self.ba.v, self.ba.dout = q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr()
+
+    def fwd(self):
+        self._lib.check(self.L.kata_attn_fwd(self.fa, self.stream), "kata_attn_fwd")
+
+    def bwd(self, phases):
+        self.ba.phases = phases
+        self._lib.check(self.L.kata_attn_bwd(self.ba, self.stream), "kata_attn_bwd")
+
+
+def run_gpu(args, rank: int, world: int, local: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    import linatt_b200.parallel_kata_attn as pka
+    from linatt_b200 import _lib
+
+    # ---------------- inputs: 3 rotating sets, seeded per rank
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = []
+    for _ in range(3):
+        q, k, v = ((torch.randn(B, T, H, D, device=dev, generator=g) / math.sqrt(D)).bfloat16() for _ in range(3))
+        do = torch.randn(B, T, H, DV, device=dev, generator=g).bfloat16()
+        sets.append((q, k, v, do))
+    step = AbiStep(torch, dev, *sets[0])
+
+    def run_step(i, ev=None):
+        step.bind(*sets[i % 3])
+        if ev is not None:
+            ev[0].record()
+        step.fwd()
+        if ev is not None:
+            ev[1].record()
+        step.bwd(1)
+        if ev is not None:
+            ev[2].record()
+        step.bwd(2)
+        if ev is not None:
+            ev[3].record()
+
+    for i in range(args.warmup):
+        run_step(i)
+    torch.cuda.synchronize()
+    _lib.check_device_status(dev)
+
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(K):
+            run_step(i, evs[i])
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    _lib.check_device_status(dev)
+    total_ms = start.elapsed_time(end)
+    kern_ms = {"fwd": 0.0, "bwd_dq": 0.0, "bwd_dkdv": 0.0}
+    for e in evs:
+        kern_ms["fwd"] += e[0].elapsed_time(e[1])
+        kern_ms["bwd_dq"] += e[1].elapsed_time(e[2])
+        kern_ms["bwd_dkdv"] += e[2].elapsed_time(e[3])
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_step = total_ms / K
+    value = world * B * T * K / (total_ms / 1e3)
+
+    # ---------------- e2e through the public autograd API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = [tuple(x.cpu().pin_memory() for x in s) for s in sets[:2]]
+        outs = [torch.empty(B, T, H, DV, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+
+        def e2e_step(i):
+            qh, kh, vh, doh = host[i % 2]
+            q = qh.to(dev, non_blocking=True).requires_grad_(True)
+            k = kh.to(dev, non_blocking=True).requires_grad_(True)
+            v = vh.to(dev, non_blocking=True).requires_grad_(True)
+            do = doh.to(dev, non_blocking=True)
+            o = pka.parallel_kata_attn(q, k, v, num_groups=M)
+            o.backward(do)
+            for dst, src in zip(outs, (o.detach(), q.grad, k.grad, v.grad)):
+                dst.copy_(src, non_blocking=True)
+
+        for i in range(max(2, args.warmup)):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        Ke = max(5, min(K, 20))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(Ke):
+            e2e_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        elem = B * T * H * D * 2
+        e2e = {"value": world * B * T * Ke / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": 4 * elem,
+               "d2h_bytes_per_step": 4 * elem, "steps": Ke, "ms_per_step": e_ms / Ke}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peak, peak_src = load_peaks()
+    kernels = {}
+    for name, ms in kern_ms.items():
+        avg = ms / K
+        kernels[name] = {"ms": avg, "tflops": ALG_FLOPS[name] / (avg / 1e3) / 1e12}
+    dom = max(kern_ms, key=kern_ms.get)
+    ach = kernels[dom]["tflops"]
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                "frac": ach / peak, "traffic": load_traffic(dom), "peak_source": peak_src,
+                "step_tflops": STEP_FLOPS / (ms_step / 1e3) / 1e12,
+                "step_frac": STEP_FLOPS / (ms_step / 1e3) / 1e12 / peak, "kernels": kernels}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        tok_s, cores, per = cpu_reference(args.cpu_slices, 1)
+        cpu = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{args.cpu_slices} of the {B * H} (b,h) slices, fwd+bwd at T={T} "
+                         f"({per:.2f} s per slice), scaled to the full workload"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(world), "roofline": roofline, "cpu_baseline": cpu,
+        "e2e": e2e, "clocks": clk.summary(), "gpu_launches": 3 * K,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-slices", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world == 1 and args.gpus > 1:
+        ap.error("--gpus N > 1 must be launched with torchrun (one process per GPU)")
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_gpu(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -123,6 +123,9 @@ typedef struct {
   int score;
   int algo;
   float scale;
+  int phases;        /* 0 = full backward; 1 = dq pass only (also fills the workspace: delta,
+                        1/den, delta/den, dc row part); 2 = dk/dv pass only (needs a prior dq
+                        pass on the same workspace).  Splitting lets a caller time each pass. */
 } kata_attn_bwd_args;
 
 KATA_API size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* args);

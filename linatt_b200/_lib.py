@@ -45,7 +45,7 @@ class AttnBwdArgs(ctypes.Structure):
         ("dout", c_void_p), ("c", c_void_p), ("dq", c_void_p), ("dk", c_void_p), ("dv", c_void_p),
         ("dc", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("status", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HQ", c_int), ("D", c_int), ("Dv", c_int),
-        ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float),
+        ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float), ("phases", c_int),
     ]
 
 

@@ -55,6 +55,7 @@ struct AttnBwdParams {
   int B, T, H, HQ, D, Dv, M;
   int G;
   float scale;
+  int phases;  // 0 both passes, 1 dq pass, 2 dk/dv pass
 };
 
 }  // namespace kata

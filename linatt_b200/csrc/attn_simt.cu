@@ -435,8 +435,12 @@ int fwd_typed(const AttnFwdParams& p, bool sum, cudaStream_t st) {
 template <typename T, bool SUM, bool DEC>
 int bwd_typed2(const AttnBwdParams& p, cudaStream_t st) {
   const int NP = SUM ? p.M * p.M : p.M;
-  int e = launch(attn_bwd_dq_simt<T, SUM, DEC>, dim3((p.T + BQ - 1) / BQ, p.B * p.HQ), dq_smem(p.D, p.Dv, NP), st, p);
-  if (e) return e;
+  if (p.phases != 2) {
+    int e = launch(attn_bwd_dq_simt<T, SUM, DEC>, dim3((p.T + BQ - 1) / BQ, p.B * p.HQ), dq_smem(p.D, p.Dv, NP), st,
+                   p);
+    if (e) return e;
+  }
+  if (p.phases == 1) return KATA_OK;
   return launch(attn_bwd_dkdv_simt<T, SUM, DEC>, dim3((p.T + BS - 1) / BS, p.B * p.H), dkdv_smem(p.D, p.Dv, NP), st,
                 p);
 }

@@ -816,7 +816,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (!e) e = make_tm_tokens(&to, p.dout, p.B, p.T, p.HQ, DV, VCW);
   if (e) return e;
   const int nt = (p.T + kTile - 1) / kTile;
-  {
+  if (p.phases != 2) {
     auto kern = attn_bwd_dq_tc<T, D, DV, M, SUM, DECAY>;
     const size_t smem = L::DQ_TOTAL + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
@@ -825,7 +825,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
     kern<<<dim3(nt, p.B * p.HQ), kThreads, smem, st>>>(tq, tk, tv, to, p);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
-  {
+  if (p.phases != 1) {
     auto kern = attn_bwd_dkdv_tc<T, D, DV, M, SUM, DECAY>;
     const size_t smem = L::KV_TOTAL + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=

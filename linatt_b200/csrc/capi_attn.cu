@@ -80,7 +80,8 @@ extern "C" int kata_attn_bwd(const kata_attn_bwd_args* a, kata_stream_t stream) 
   if (alg < 0) return alg;
   AttnBwdParams p{a->q,  a->k,  a->v,  a->o,  a->den, a->dout, a->c,  a->dq, a->dk,           a->dv,
                   a->dc, static_cast<float*>(a->workspace), a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
-                  a->HQ / a->H, a->scale};
+                  a->HQ / a->H, a->scale, a->phases};
+  if (a->phases < 0 || a->phases > 2) return KATA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return alg == 1 ? tc_attn_bwd(p, a->dtype, sum, st) : simt_attn_bwd(p, a->dtype, sum, st);
 }
