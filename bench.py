@@ -21,8 +21,8 @@ Printed JSON line (rank 0):
             oracle/kata_cpu_ref.py) on this host's cores, on a bounded sample of (b,h) slices
   clocks    SM clock median / max and throttle reasons sampled through NVML during the timing
 
-L2: three rotating input sets (3 x 67 MB of bf16 q/k/v/dO) plus 84 MB of outputs are touched per
-cycle, more than the 126 MB L2, so no step reads inputs left in L2 by the previous step.
+L2: three rotating input sets of 537 MB each (bf16 q, k, v, dO of 134 MB apiece) are cycled, each
+larger than the 126 MB L2, so no step reads inputs left in L2 by the previous step.
 """
 
 from __future__ import annotations
@@ -61,7 +61,7 @@ def workload_config(n_gpus: int) -> dict:
         "batch_per_gpu": B, "global_batch": B * n_gpus, "seq_len": T, "heads": H, "head_dim": D,
         "value_dim": DV, "num_groups": M, "score": "concat",
         "parallelism": f"batch*head shard x{n_gpus}, no collective",
-        "l2": "3 rotating input sets (201 MB) + 84 MB outputs per cycle > 126 MB L2",
+        "l2": "3 rotating input sets of 537 MB (bf16 q, k, v, dO) per cycle, each larger than the 126 MB L2",
     }
 
 

@@ -30,15 +30,16 @@ constexpr int kRing = 3;
 
 struct BwdWs {
   // workspace views (fp32), each 16-byte aligned:
-  //   delta (B,T,HQ) | rden (B,HQ,Tp) | delta*rden (B,HQ,Tp)   with Tp = T rounded up to 4,
-  // so that head-major rows start on 16-byte boundaries and even-index float2 loads are aligned.
+  //   delta (B,T,HQ) | rden (B,HQ,Tp) | delta*rden (B,HQ,Tp)   with Tp = T rounded up to 128,
+  // so that the 128 values of every query tile are one contiguous, in-bounds, 512-byte run that a
+  // bulk copy can move into shared memory (rows past T hold rden = 1, delta*rden = 0).
   float* delta;
   float* rden;
   float* dr;
   int Tp;
 };
 __host__ __device__ inline BwdWs ws_views(float* base, int B, int T, int HQ) {
-  const int Tp = (T + 3) & ~3;
+  const int Tp = (T + 127) & ~127;
   const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
   const size_t n1 = static_cast<size_t>(B) * HQ * Tp;
   return BwdWs{base, base + n0, base + n0 + n1, Tp};
@@ -62,7 +63,9 @@ struct BwdSmem {
   static constexpr int KV_OFF_RING = KV_OFF_V + O_BYTES;
   static constexpr int KV_OFF_P = KV_OFF_RING + kRing * ITEM;
   static constexpr int KV_OFF_W = KV_OFF_P + T_BYTES;
-  static constexpr int KV_TOTAL = KV_OFF_W + T_BYTES;
+  static constexpr int KV_OFF_VEC = KV_OFF_W + T_BYTES;      // 2 stages x {rden, delta*rden} x 128 fp32
+  static constexpr int KV_OFF_BARS = KV_OFF_VEC + 2 * 2 * kTile * 4;
+  static constexpr int KV_TOTAL = KV_OFF_BARS + 256;          // DkvBars lives here (no static smem)
 };
 
 struct DqBars {
@@ -80,6 +83,7 @@ struct DqBars {
 
 struct DkvBars {
   uint64_t kv_full;
+  uint64_t vec_full[2], vec_empty[2];
   uint64_t ring_full[kRing], ring_empty[kRing];
   uint64_t dn_full, dn_empty;
   uint64_t s_full, s_empty;
@@ -293,12 +297,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (live) {
       const float dn = p.den[rowidx];
       rden = 1.f / (dn > 0.f ? dn : 1.f);
-      if (hc == 0) {
-        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
-        ws.delta[rowidx] = delta;
-        ws.rden[hm] = rden;
-        ws.dr[hm] = delta * rden;
-      }
+      if (hc == 0) ws.delta[rowidx] = delta;
+    }
+    if (hc == 0) {  // every row of the tile, including rows past T (rden 1, delta 0)
+      const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
+      ws.rden[hm] = rden;
+      ws.dr[hm] = live ? delta * rden : 0.f;
     }
     const float w_scale = 2.f * p.scale * p.scale;
     const float scale2 = p.scale * p.scale;
@@ -445,10 +449,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kColDN = 128, kColDK = 256, kColDV = 384;
   using L = BwdSmem<D, DV>;
+  static_assert(sizeof(DkvBars) <= 256, "barrier block");
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ DkvBars bars;
+  // The whole shared footprint is dynamic (no static __shared__), so the dynamic window starts at
+  // the CTA's shared base, which is 1024-byte aligned; checked below rather than assumed.
+  extern __shared__ __align__(1024) uint8_t smem[];
+  DkvBars& bars = *reinterpret_cast<DkvBars*>(smem + L::KV_OFF_BARS);
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kStatusWaitTimeout + 1);
+    return;
+  }
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T_ = p.T;
@@ -456,13 +466,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kj = static_cast<int>(blockIdx.x);  // small j = most work, launched first
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int s0 = kj * kTile;
-  const int nq = nqt - kj;          // query tiles kj..nqt-1 per query head
-  const int nwork = p.G * nq;       // (query head, query tile) items
+  const int nq = nqt - kj;     // query tiles kj..nqt-1 per query head
+  const int nwork = p.G * nq;  // (query head, query tile) items
+  const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
   WaitCtx wc{p.status, &bars.abort_flag};
 
   if (threadIdx.x == 0) {
     bars.abort_flag = 0;
     mbar_init(&bars.kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.vec_full[i], 1);
+      mbar_init(&bars.vec_empty[i], 8);
+    }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&bars.ring_full[i], 1);
       mbar_init(&bars.ring_empty[i], 1);
@@ -487,6 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars.tmem_base;
+  float* vec = reinterpret_cast<float*>(smem + L::KV_OFF_VEC);  // [stage][0: rden, 1: delta*rden][128]
 
   if (warp == 0) {
     if (lane == 0) {
@@ -499,11 +515,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(smem + L::KV_OFF_K + bx * (kTile * CW * 2), &tmK, &bars.kv_full, bx * CW, h, s0, b);
       for (int bx = 0; bx < NVBOX; ++bx)
         tma_load_4d(smem + L::KV_OFF_V + bx * (kTile * VCW * 2), &tmV, &bars.kv_full, bx * VCW, h, s0, b);
-      int r = 0;
+      int r = 0, nv = 0;
       bool ok = true;
       for (int n = 0; n < nwork && ok; ++n) {
         const int hq = h * p.G + n / nq;
         const int ti = (kj + n % nq) * kTile;
+        // per-query vectors of this tile: rden and delta*rden (512 B each, contiguous)
+        const int vs = n & 1;
+        if (!mbar_wait(&bars.vec_empty[vs], ((n >> 1) & 1) ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + ti;
+        mbar_arrive_expect_tx(&bars.vec_full[vs], 2 * kTile * 4);
+        bulk_load(vec + (vs * 2 + 0) * kTile, ws.rden + hm, kTile * 4, &bars.vec_full[vs]);
+        bulk_load(vec + (vs * 2 + 1) * kTile, ws.dr + hm, kTile * 4, &bars.vec_full[vs]);
+        nv = n + 1;
         for (int item = 0; item < 2; ++item, ++r) {  // Q_i then dO_i
           const int slot = r % kRing;
           if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
@@ -525,6 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
           mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
+        for (int n = (nv > 2 ? nv - 2 : 0); n < nv; ++n) mbar_drain(&bars.vec_full[n & 1], (n >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -616,7 +644,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sg = s0 + row;
     const bool live = sg < T_;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
     const float w_scale = 2.f * p.scale * p.scale;
     const float scale2 = p.scale * p.scale;
     const uint32_t sP = smem_u32(smem + L::KV_OFF_P);
@@ -628,14 +655,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int hq = h * p.G + n / nq;
       const int qi = kj + n % nq;
       const bool diag = (qi == kj);
-      const size_t hm0 = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp;  // head-major row base
+      const int vs = n & 1;
+      const float* v_rd = vec + (vs * 2 + 0) * kTile;
+      const float* v_dr = vec + (vs * 2 + 1) * kTile;
       float c_s = 0.f;
       const float* cb = nullptr;
       if (DECAY) {
         cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
         c_s = live ? cb[static_cast<size_t>(sg) * p.HQ] : 0.f;
       }
-      if (!mbar_wait(&bars.dn_full, n & 1, wc)) {
+      if (!mbar_wait(&bars.vec_full[vs], (n >> 1) & 1, wc) || !mbar_wait(&bars.dn_full, n & 1, wc)) {
         ok = false;
         break;
       }
@@ -647,47 +676,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t rs[32], rn[32];
-          tmem_ld32(lane_addr + hc * 64u + c * 32u, rs);
-          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rs[16], rn[16];
+          tmem_ld16(lane_addr + hc * 64u + c * 16u, rs);
+          tmem_ld16(lane_addr + kColDN + hc * 64u + c * 16u, rn);
           tmem_wait_ld();
-          if (c == 1) {
+          if (c == 3) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.s_empty);
           }
-          const int cbase = hc * 64 + c * 32;  // query column within the tile
-          uint32_t wv[16];
+          const int cbase = hc * 64 + c * 16;  // query column within the tile
+          uint32_t wv[8];
 #pragma unroll
-          for (int x = 0; x < 16; ++x) {
-            const int tl = cbase + 2 * x;
-            const int tq = qi * kTile + tl;
-            const float2 rd = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.rden + hm0 + tq))
-                                          : make_float2(tq < T_ ? ws.rden[hm0 + tq] : 1.f, 1.f);
-            const float2 dr = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.dr + hm0 + tq))
-                                          : make_float2(tq < T_ ? ws.dr[hm0 + tq] : 0.f, 0.f);
-            const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
-            const float2 nv = u2f2(rn[2 * x], rn[2 * x + 1]);
-            float da0 = fmaf(nv.x, rd.x, -dr.x), da1 = fmaf(nv.y, rd.y, -dr.y);
-            if (diag) {
-              if (tl < row) da0 = 0.f;
-              if (tl + 1 < row) da1 = 0.f;
+          for (int x4 = 0; x4 < 4; ++x4) {
+            const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
+            const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
+            const float rdv[4] = {rd.x, rd.y, rd.z, rd.w};
+            const float drv[4] = {dr.x, dr.y, dr.z, dr.w};
+#pragma unroll
+            for (int y = 0; y < 2; ++y) {
+              const int x = 2 * x4 + y;  // pair index within the chunk
+              const int tl = cbase + 2 * x;
+              const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
+              const float2 nv = u2f2(rn[2 * x], rn[2 * x + 1]);
+              float da0 = fmaf(nv.x, rdv[2 * y], -drv[2 * y]);
+              float da1 = fmaf(nv.y, rdv[2 * y + 1], -drv[2 * y + 1]);
+              if (diag) {
+                if (tl < row) da0 = 0.f;
+                if (tl + 1 < row) da1 = 0.f;
+              }
+              float dec0 = 1.f, dec1 = 1.f;
+              if (DECAY) {
+                const int tq = qi * kTile + tl;
+                const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
+                const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
+                dec0 = __expf(fminf(ct0 - c_s, 0.f));
+                dec1 = __expf(fminf(ct1 - c_s, 0.f));
+              }
+              const float2 sq = fmul2(sv, sv);
+              acc[8 * c + x] = pp == 0 ? sq : fadd2(acc[8 * c + x], sq);
+              wv[x] = pack2<T>(w_scale * sv.x * dec0 * da0, w_scale * sv.y * dec1 * da1);
             }
-            float dec0 = 1.f, dec1 = 1.f;
-            if (DECAY) {
-              const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
-              const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
-              dec0 = __expf(fminf(ct0 - c_s, 0.f));
-              dec1 = __expf(fminf(ct1 - c_s, 0.f));
-            }
-            const float2 sq = fmul2(sv, sv);
-            acc[16 * c + x] = pp == 0 ? sq : fadd2(acc[16 * c + x], sq);
-            wv[x] = pack2<T>(w_scale * sv.x * dec0 * da0, w_scale * sv.y * dec1 * da1);
           }
-#pragma unroll
-          for (int m4 = 0; m4 < 4; ++m4)
-            st_tile128(sW, row, cbase + 8 * m4, wv[4 * m4], wv[4 * m4 + 1], wv[4 * m4 + 2], wv[4 * m4 + 3]);
+          st_tile128(sW, row, cbase, wv[0], wv[1], wv[2], wv[3]);
+          st_tile128(sW, row, cbase + 8, wv[4], wv[5], wv[6], wv[7]);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -700,33 +733,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int cbase = hc * 64 + c * 32;
-        uint32_t rn[32];
+      for (int c = 0; c < 4; ++c) {
+        const int cbase = hc * 64 + c * 16;
+        uint32_t rn[16];
         if (DECAY) {
-          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+          tmem_ld16(lane_addr + kColDN + hc * 64u + c * 16u, rn);
           tmem_wait_ld();
         }
-        uint32_t pv[16];
+        uint32_t pv[8];
 #pragma unroll
-        for (int x = 0; x < 16; ++x) {
+        for (int x = 0; x < 8; ++x) {
           const int tl = cbase + 2 * x;
-          const int tq = qi * kTile + tl;
-          const float2 rd = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.rden + hm0 + tq))
-                                        : make_float2(tq < T_ ? ws.rden[hm0 + tq] : 1.f, 1.f);
-          float a0 = scale2 * acc[16 * c + x].x, a1 = scale2 * acc[16 * c + x].y;
+          const float2 rd = *reinterpret_cast<const float2*>(v_rd + tl);
+          float a0 = scale2 * acc[8 * c + x].x, a1 = scale2 * acc[8 * c + x].y;
           if (diag) {
             if (tl < row) a0 = 0.f;
             if (tl + 1 < row) a1 = 0.f;
           }
           if (DECAY) {
+            const int tq = qi * kTile + tl;
             const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
             const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
             const float x0 = ct0 - c_s, x1 = ct1 - c_s;
             a0 *= __expf(fminf(x0, 0.f));
             a1 *= __expf(fminf(x1, 0.f));
-            const float2 dr = tq + 1 < T_ ? __ldg(reinterpret_cast<const float2*>(ws.dr + hm0 + tq))
-                                          : make_float2(tq < T_ ? ws.dr[hm0 + tq] : 0.f, 0.f);
+            const float2 dr = *reinterpret_cast<const float2*>(v_dr + tl);
             const float da0 = fmaf(__uint_as_float(rn[2 * x]), rd.x, -dr.x);
             const float da1 = fmaf(__uint_as_float(rn[2 * x + 1]), rd.y, -dr.y);
             if (x0 <= 0.f) csum += da0 * a0;
@@ -734,9 +765,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           pv[x] = pack2<T>(a0 * rd.x, a1 * rd.y);
         }
-#pragma unroll
-        for (int m4 = 0; m4 < 4; ++m4)
-          st_tile128(sP, row, cbase + 8 * m4, pv[4 * m4], pv[4 * m4 + 1], pv[4 * m4 + 2], pv[4 * m4 + 3]);
+        st_tile128(sP, row, cbase, pv[0], pv[1], pv[2], pv[3]);
+        st_tile128(sP, row, cbase + 8, pv[4], pv[5], pv[6], pv[7]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -744,6 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         mbar_arrive(&bars.p_full);
         mbar_arrive(&bars.dn_empty);
+        mbar_arrive(&bars.vec_empty[vs]);
       }
       if (DECAY && (n % nq == nq - 1)) {
         // last query tile of this query head: dc_s -= sum_t G[t, s]
@@ -827,7 +858,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   }
   if (p.phases != 1) {
     auto kern = attn_bwd_dkdv_tc<T, D, DV, M, SUM, DECAY>;
-    const size_t smem = L::KV_TOTAL + 1024;
+    const size_t smem = L::KV_TOTAL;  // no alignment slack: the kernel has no static shared memory
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
@@ -873,7 +904,7 @@ int bwd_dims(const AttnBwdParams& p, bool sum, cudaStream_t st) {
 }  // namespace
 
 size_t tc_bwd_workspace_bytes(int B, int T, int HQ) {
-  const size_t Tp = (static_cast<size_t>(T) + 3) & ~static_cast<size_t>(3);
+  const size_t Tp = (static_cast<size_t>(T) + 127) & ~static_cast<size_t>(127);
   const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
   return sizeof(float) * (n0 + 2 * static_cast<size_t>(B) * HQ * Tp);
 }

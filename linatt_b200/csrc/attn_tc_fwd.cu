@@ -256,13 +256,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      // A = scale^2 * acc, causal mask on the diagonal tile, optional decay; row sum; P -> smem
+      // A = scale^2 * acc, causal mask on the diagonal tile, optional decay; row sum; P -> smem.
+      // For bf16 the scale^2 factor is left out of P and of the row sum: o = (P v) / den is
+      // invariant under a common scale of P and den (bf16 has the fp32 exponent range, so the
+      // unscaled P cannot overflow where the scaled one would not) and den is rescaled once in the
+      // epilogue.  fp16 keeps the per-element scale so its overflow behaviour matches the
+      // reference's cast of the scaled score to the value dtype.
       const float2 sc2 = make_float2(scale2, scale2);
       const int s_base = j * kBK + hc * 64;
       const bool diag = (j == qt);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        float2 x = fmul2(acc[i], sc2);
+        float2 x = kBF16 ? acc[i] : fmul2(acc[i], sc2);
         const int s0 = s_base + 2 * i;
         if (diag) {
           if (s0 > t) x.x = 0.f;
@@ -301,10 +306,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue
     bars.den_x[hc][row] = den;
     named_bar_sync(1, 256);
-    const float den_all = bars.den_x[0][row] + bars.den_x[1][row];
+    const float den_all = (bars.den_x[0][row] + bars.den_x[1][row]) * (kBF16 ? scale2 : 1.f);
     if (ok && mbar_wait(&bars.o_full, 0, wc)) {
       tc_fence_after();
-      const float inv = 1.f / (den_all > 0.f ? den_all : 1.f);
+      // O holds sum_s P v with P unscaled for bf16, so divide by the unscaled row sum there
+      const float den_o = kBF16 ? den_all / scale2 : den_all;
+      const float inv = 1.f / (den_o > 0.f ? den_o : 1.f);
       constexpr int HALF = DV / 2;
       T* orow = static_cast<T*>(p.o) + ((static_cast<size_t>(b) * T_ + t) * p.HQ + hq) * DV + hc * HALF;
 #pragma unroll

@@ -76,16 +76,20 @@ struct WaitCtx {
 };
 
 // Bounded wait on an mbarrier phase.  Returns false on timeout or when the CTA is aborting.
+// The clock and the abort flag are only consulted every 256 polls so the spin costs almost no
+// issue slots of the (shared) pipes that read them.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*w.abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      *w.abort = 1;
-      if (w.status) atomicCAS(w.status, 0, kStatusWaitTimeout);
-      return false;
+    if ((it & 255u) == 0) {
+      if (*w.abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *w.abort = 1;
+        if (w.status) atomicCAS(w.status, 0, kStatusWaitTimeout);
+        return false;
+      }
     }
   }
 }
@@ -94,7 +98,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
 // retires (100 ms limit, ignores the abort flag).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity) && globaltimer_ns() - t0 < 100000000ull) {
+  for (uint32_t it = 1; !mbar_try_wait(bar, parity); ++it) {
+    if ((it & 255u) == 0 && globaltimer_ns() - t0 > 100000000ull) break;
   }
 }
 
@@ -128,6 +133,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// Plain bulk copy global -> this CTA's shared memory (no tensor map, no multicast).  Both
+// addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 

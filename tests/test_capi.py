@@ -66,8 +66,8 @@ def test_host_side_validation(L):
     assert L.kata_attn_fwd(a, None) == -4  # misaligned o
     b = _lib.AttnBwdArgs(q=16, k=16, v=16, o=16, den=16, dout=16, dq=16, dk=16, dv=16, dtype=1, B=2, T=8, H=1, HQ=2,
                          D=64, Dv=64, M=4, score=0, algo=0, scale=1.0)
-    # delta (B*T*HQ) + two padded head-major rows (B*HQ*roundup(T,4)), fp32
-    assert L.kata_attn_bwd_workspace_bytes(b) == 4 * (2 * 8 * 2 + 2 * 2 * 2 * 8)
+    # delta (B*T*HQ) + two head-major arrays with rows padded to 128 (B*HQ*roundup(T,128)), fp32
+    assert L.kata_attn_bwd_workspace_bytes(b) == 4 * (2 * 8 * 2 + 2 * 2 * 2 * 128)
     assert L.kata_attn_bwd(b, None) == -5  # workspace missing
     b.c = 16
     assert L.kata_attn_bwd(b, None) == -1  # decay without dc
