@@ -44,7 +44,8 @@ enum {
   KATA_ERR_WORKSPACE = -5,   /* workspace missing or too small */
   KATA_ERR_CUDA = -6,        /* a CUDA runtime call failed (e.g. launch error) */
   KATA_ERR_DRIVER = -7,      /* driver entry point (tensor-map encoder) unavailable */
-  KATA_ERR_UNSUPPORTED = -8  /* algorithm not available for this configuration */
+  KATA_ERR_UNSUPPORTED = -8, /* algorithm not available for this configuration */
+  KATA_ERR_SCRATCH_LIMIT = -9 /* problem needs more scratch than the library's fixed array */
 };
 
 /* Values a kernel may store into the optional device status word. */
@@ -130,6 +131,19 @@ typedef struct {
 
 KATA_API size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* args);
 KATA_API int kata_attn_bwd(const kata_attn_bwd_args* args, kata_stream_t stream);
+
+/* Backward for callers that cannot allocate device memory.  No counterpart in the reference.
+ * Some callers cannot call cudaMalloc: host code that runs under a fixed, pre-reserved device
+ * memory budget that forbids further allocation once loaded, or a plugin host whose operator
+ * interface passes the kernel only its inputs and outputs and offers no workspace.  This entry
+ * point runs exactly the computation of kata_attn_bwd but ignores args->workspace and uses a
+ * 16 MiB file-scope device array of the library instead (held on every GPU that loads the
+ * library until the process exits).  Problems whose kata_attn_bwd_workspace_bytes() exceeds
+ * 16 MiB are rejected with KATA_ERR_SCRATCH_LIMIT.  The first call on a device resolves the
+ * array's address for that device, so make it outside any stream capture.  All calls on a device
+ * share the array: calls whose kernels overlap on the GPU race on it.  The caller still passes
+ * every input and output buffer; this path calls no allocating routine. */
+KATA_API int kata_attn_bwd_noalloc(const kata_attn_bwd_args* args, kata_stream_t stream);
 
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);

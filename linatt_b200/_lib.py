@@ -72,6 +72,8 @@ def lib() -> ctypes.CDLL:
             L.kata_attn_fwd.argtypes = [ctypes.POINTER(AttnFwdArgs), c_void_p]
             L.kata_attn_bwd.restype = c_int
             L.kata_attn_bwd.argtypes = [ctypes.POINTER(AttnBwdArgs), c_void_p]
+            L.kata_attn_bwd_noalloc.restype = c_int
+            L.kata_attn_bwd_noalloc.argtypes = [ctypes.POINTER(AttnBwdArgs), c_void_p]
             L.kata_attn_bwd_workspace_bytes.restype = c_size_t
             L.kata_attn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnBwdArgs)]
             L.kata_selftest_umma.restype = c_int

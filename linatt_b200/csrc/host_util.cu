@@ -56,6 +56,7 @@ extern "C" const char* kata_strerror(int code) {
     case KATA_ERR_CUDA: return "CUDA runtime error";
     case KATA_ERR_DRIVER: return "driver entry point cuTensorMapEncodeTiled unavailable";
     case KATA_ERR_UNSUPPORTED: return "algorithm not available for this configuration";
+    case KATA_ERR_SCRATCH_LIMIT: return "problem needs more scratch than the library's fixed 16 MiB array";
     default: return "unknown error";
   }
 }
