@@ -71,9 +71,8 @@ struct BwdSmem {
 struct DqBars {
   uint64_t qo_full;
   uint64_t ring_full[kRing], ring_empty[kRing];
-  uint64_t dn_full, dn_empty;
-  uint64_t s_full[2], s_empty[2];
-  uint64_t w_full, w_empty;
+  uint64_t dn_full, dn_free;
+  uint64_t s_full[2], w_full[2];
   uint64_t acc_done, drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -99,6 +98,12 @@ __device__ __forceinline__ float2 u2f2(uint32_t a, uint32_t b) { return make_flo
 // ================================================================================================
 // dq kernel
 // ================================================================================================
+// TMEM: score slots at columns 0 and 128, dN at 256, dQ at 384.  W_p (bf16 pairs) is written over
+// the first 32 columns of each half of its own score slot and read from there as the A operand of
+// dQ_a += W_p K_b.  A score MMA reuses a slot only after the dQ chain that reads the W in it was
+// issued (same-CTA MMAs execute in order), and that chain waited for the W to be complete.
+// Without decay and with several parts, part 0 replaces dN by dA' = 2 scale^2 (dN - delta)/den
+// (masked) in tensor memory so the other parts skip that arithmetic.
 template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -111,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NVBOX = DV / VCW;
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool kHoist = (NP > 1) && !DECAY;
   constexpr uint32_t kColDN = 256, kColDQ = 384;
   using L = BwdSmem<D, DV>;
 
@@ -135,13 +141,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.ring_empty[i], 1);
     }
     mbar_init(&bars.dn_full, 1);
-    mbar_init(&bars.dn_empty, 8);
+    mbar_init(&bars.dn_free, 8);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.s_full[i], 1);
-      mbar_init(&bars.s_empty[i], 8);
+      mbar_init(&bars.w_full[i], 8);
     }
-    mbar_init(&bars.w_full, 8);
-    mbar_init(&bars.w_empty, 1);
     mbar_init(&bars.acc_done, 1);
     mbar_init(&bars.drain, 1);
     fence_mbar_init();
@@ -198,13 +202,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
       const uint32_t sQ = smem_u32(smem + L::DQ_OFF_Q);
       const uint32_t sO = smem_u32(smem + L::DQ_OFF_O);
-      const uint32_t sW = smem_u32(smem + L::DQ_OFF_W);
       bool ok = mbar_wait(&bars.qo_full, 0, wc);
       int r = 0, u = 0;
       for (int j = 0; ok && j < nk; ++j) {
-        // dN = dO V^T
+        // dN = dO V^T  (the compute warps released the previous tile's dN / dA')
         const int slotV = r % kRing;
-        if (!mbar_wait(&bars.ring_full[slotV], (r / kRing) & 1, wc) || !mbar_wait(&bars.dn_empty, (j & 1) ^ 1, wc)) {
+        if (!mbar_wait(&bars.ring_full[slotV], (r / kRing) & 1, wc) || !mbar_wait(&bars.dn_free, (j & 1) ^ 1, wc)) {
           ok = false;
           break;
         }
@@ -223,25 +226,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const uint32_t sK = smem_u32(smem + L::DQ_OFF_RING + slotK * L::ITEM);
+        // dQ_a += W_p K_b with W_p read from TMEM (slot of part uu)
         auto issue_dq = [&](int pp, int uu) -> bool {
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          if (!mbar_wait(&bars.w_full, uu & 1, wc)) return false;
+          const int slot = uu & 1;
+          if (!mbar_wait(&bars.w_full[slot], (uu >> 1) & 1, wc)) return false;
           tc_fence_after();
           const bool first = (j == 0) && (!SUM || gb == 0);
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ss(tbase + kColDQ + ga * E, kmajor128_desc(sW, kk), mnmajor_desc<CW>(sK, gb * E / CW, kk), id_dq,
-                    (!first || kk > 0) ? 1u : 0u);
-          umma_commit(&bars.w_empty);
+            umma_ts(tbase + kColDQ + ga * E, tbase + slot * 128u + packed_col(kk),
+                    mnmajor_desc<CW>(sK, gb * E / CW, kk), id_dq, (!first || kk > 0) ? 1u : 0u);
           return true;
         };
         for (int pp = 0; pp < NP; ++pp, ++u) {
           const int slot = u & 1;
-          if (!mbar_wait(&bars.s_empty[slot], ((u >> 1) & 1) ^ 1, wc)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
@@ -306,6 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const float w_scale = 2.f * p.scale * p.scale;
     const float scale2 = p.scale * p.scale;
+    // dA' = dN * rden_w - dr_w = 2 scale^2 (dN - delta) / den
+    const float2 rden_w = make_float2(rden * w_scale, rden * w_scale);
+    const float2 ndr_w = make_float2(-delta * rden * w_scale, -delta * rden * w_scale);
     float c_t = 0.f;
     const float* cb = nullptr;
     if (DECAY) {
@@ -315,7 +317,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     float rsum = 0.f;
     bool ok = true;
     int u = 0;
-    const uint32_t sW = smem_u32(smem + L::DQ_OFF_W);
     for (int j = 0; j < nk && ok; ++j) {
       const bool diag = (j == qi);
       if (!mbar_wait(&bars.dn_full, j & 1, wc)) {
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float2 acc[32];  // DECAY only: sum_p S_p^2 for this thread's 64 columns
       for (int pp = 0; pp < NP; ++pp, ++u) {
         const int slot = u & 1;
-        if (!mbar_wait(&bars.s_full[slot], (u >> 1) & 1, wc) || !mbar_wait(&bars.w_empty, (u & 1) ^ 1, wc)) {
+        if (!mbar_wait(&bars.s_full[slot], (u >> 1) & 1, wc)) {
           ok = false;
           break;
         }
@@ -333,45 +334,61 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t rs[32], rn[32];
+          const uint32_t dcol = kColDN + hc * 64u + c * 32u;
           tmem_ld32(lane_addr + slot * 128u + hc * 64u + c * 32u, rs);
-          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
+          tmem_ld32(lane_addr + dcol, rn);
           tmem_wait_ld();
-          if (c == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.s_empty[slot]);
-          }
           const int cbase = hc * 64 + c * 32;  // key column within the tile
+          float2 da[16];
+          if (!kHoist || pp == 0) {
+#pragma unroll
+            for (int x = 0; x < 16; ++x) da[x] = ffma2(u2f2(rn[2 * x], rn[2 * x + 1]), rden_w, ndr_w);
+            if (diag) {
+#pragma unroll
+              for (int x = 0; x < 16; ++x) {
+                const int s0 = cbase + 2 * x;
+                if (s0 > row) da[x].x = 0.f;
+                if (s0 + 1 > row) da[x].y = 0.f;
+              }
+            }
+            if (DECAY) {
+#pragma unroll
+              for (int x = 0; x < 16; ++x) {
+                const int sg = j * kTile + cbase + 2 * x;
+                const float cs0 = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
+                const float cs1 = sg + 1 < T_ ? __ldg(cb + static_cast<size_t>(sg + 1) * p.HQ) : 0.f;
+                da[x].x *= __expf(fminf(c_t - cs0, 0.f));
+                da[x].y *= __expf(fminf(c_t - cs1, 0.f));
+                const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
+                const float2 sq = fmul2(sv, sv);
+                acc[16 * c + x] = pp == 0 ? sq : fadd2(acc[16 * c + x], sq);
+              }
+            }
+            if (kHoist) {  // keep dA' for the remaining parts of this tile
+              uint32_t dw[32];
+#pragma unroll
+              for (int x = 0; x < 16; ++x) {
+                dw[2 * x] = __float_as_uint(da[x].x);
+                dw[2 * x + 1] = __float_as_uint(da[x].y);
+              }
+              tmem_st32(lane_addr + dcol, dw);
+            }
+          } else {
+#pragma unroll
+            for (int x = 0; x < 16; ++x) da[x] = u2f2(rn[2 * x], rn[2 * x + 1]);
+          }
           uint32_t wv[16];
 #pragma unroll
           for (int x = 0; x < 16; ++x) {
-            const int s0 = cbase + 2 * x;
-            const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
-            const float2 nv = u2f2(rn[2 * x], rn[2 * x + 1]);
-            float da0 = (nv.x - delta) * rden, da1 = (nv.y - delta) * rden;
-            if (diag) {
-              if (s0 > row) da0 = 0.f;
-              if (s0 + 1 > row) da1 = 0.f;
-            }
-            float dec0 = 1.f, dec1 = 1.f;
-            if (DECAY) {
-              const int sg = j * kTile + s0;
-              const float cs0 = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
-              const float cs1 = sg + 1 < T_ ? __ldg(cb + static_cast<size_t>(sg + 1) * p.HQ) : 0.f;
-              dec0 = __expf(fminf(c_t - cs0, 0.f));
-              dec1 = __expf(fminf(c_t - cs1, 0.f));
-              const float2 sq = fmul2(sv, sv);
-              acc[16 * c + x] = pp == 0 ? sq : fadd2(acc[16 * c + x], sq);
-            }
-            wv[x] = pack2<T>(w_scale * sv.x * dec0 * da0, w_scale * sv.y * dec1 * da1);
+            const float2 w = fmul2(u2f2(rs[2 * x], rs[2 * x + 1]), da[x]);
+            wv[x] = pack2<T>(w.x, w.y);
           }
-#pragma unroll
-          for (int m4 = 0; m4 < 4; ++m4)
-            st_tile128(sW, row, cbase + 8 * m4, wv[4 * m4], wv[4 * m4 + 1], wv[4 * m4 + 2], wv[4 * m4 + 3]);
+          tmem_st16(lane_addr + slot * 128u + hc * 64u + c * 16u, wv);
         }
-        fence_proxy_async_smem();
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.w_full);
+        if (lane == 0) mbar_arrive(&bars.w_full[slot]);
       }
       if (!ok) break;
       if (DECAY) {
@@ -398,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars.dn_empty);
+      if (lane == 0) mbar_arrive(&bars.dn_free);
     }
     // ---- epilogue: dQ -> global; dc_t = row sum of G
     if (DECAY) bars.xch_r[hc][row] = rsum;
@@ -448,6 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kColDN = 128, kColDK = 256, kColDV = 384;
+  constexpr bool kHoist = (NP > 1) && !DECAY;
   using L = BwdSmem<D, DV>;
   static_assert(sizeof(DkvBars) <= 256, "barrier block");
 
@@ -645,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool live = sg < T_;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     const float w_scale = 2.f * p.scale * p.scale;
+    const float2 wsc2 = make_float2(w_scale, w_scale);
     const float scale2 = p.scale * p.scale;
     const uint32_t sP = smem_u32(smem + L::KV_OFF_P);
     const uint32_t sW = smem_u32(smem + L::KV_OFF_W);
@@ -678,8 +697,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t rs[16], rn[16];
+          const uint32_t dcol = kColDN + hc * 64u + c * 16u;
           tmem_ld16(lane_addr + hc * 64u + c * 16u, rs);
-          tmem_ld16(lane_addr + kColDN + hc * 64u + c * 16u, rn);
+          tmem_ld16(lane_addr + dcol, rn);
           tmem_wait_ld();
           if (c == 3) {
             tc_fence_before();
@@ -687,41 +707,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&bars.s_empty);
           }
           const int cbase = hc * 64 + c * 16;  // query column within the tile
-          uint32_t wv[8];
+          float2 da[8];
+          if (!kHoist || pp == 0) {
+            // dA' = 2 scale^2 (dN rden - delta rden) (* decay), masked: t >= s on the diagonal
 #pragma unroll
-          for (int x4 = 0; x4 < 4; ++x4) {
-            const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
-            const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
-            const float rdv[4] = {rd.x, rd.y, rd.z, rd.w};
-            const float drv[4] = {dr.x, dr.y, dr.z, dr.w};
+            for (int x4 = 0; x4 < 4; ++x4) {
+              const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
+              const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
+              const float2 nv0 = u2f2(rn[4 * x4], rn[4 * x4 + 1]), nv1 = u2f2(rn[4 * x4 + 2], rn[4 * x4 + 3]);
+              da[2 * x4] = fmul2(ffma2(nv0, make_float2(rd.x, rd.y), make_float2(-dr.x, -dr.y)), wsc2);
+              da[2 * x4 + 1] = fmul2(ffma2(nv1, make_float2(rd.z, rd.w), make_float2(-dr.z, -dr.w)), wsc2);
+            }
+            if (diag) {
 #pragma unroll
-            for (int y = 0; y < 2; ++y) {
-              const int x = 2 * x4 + y;  // pair index within the chunk
-              const int tl = cbase + 2 * x;
-              const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
-              const float2 nv = u2f2(rn[2 * x], rn[2 * x + 1]);
-              float da0 = fmaf(nv.x, rdv[2 * y], -drv[2 * y]);
-              float da1 = fmaf(nv.y, rdv[2 * y + 1], -drv[2 * y + 1]);
-              if (diag) {
-                if (tl < row) da0 = 0.f;
-                if (tl + 1 < row) da1 = 0.f;
+              for (int x = 0; x < 8; ++x) {
+                const int tl = cbase + 2 * x;
+                if (tl < row) da[x].x = 0.f;
+                if (tl + 1 < row) da[x].y = 0.f;
               }
-              float dec0 = 1.f, dec1 = 1.f;
-              if (DECAY) {
-                const int tq = qi * kTile + tl;
+            }
+            if (DECAY) {
+#pragma unroll
+              for (int x = 0; x < 8; ++x) {
+                const int tq = qi * kTile + cbase + 2 * x;
                 const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
                 const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
-                dec0 = __expf(fminf(ct0 - c_s, 0.f));
-                dec1 = __expf(fminf(ct1 - c_s, 0.f));
+                da[x].x *= __expf(fminf(ct0 - c_s, 0.f));
+                da[x].y *= __expf(fminf(ct1 - c_s, 0.f));
               }
-              const float2 sq = fmul2(sv, sv);
-              acc[8 * c + x] = pp == 0 ? sq : fadd2(acc[8 * c + x], sq);
-              wv[x] = pack2<T>(w_scale * sv.x * dec0 * da0, w_scale * sv.y * dec1 * da1);
             }
+            if (kHoist) {  // keep dA' for the remaining parts of this query tile
+              uint32_t dw[16];
+#pragma unroll
+              for (int x = 0; x < 8; ++x) {
+                dw[2 * x] = __float_as_uint(da[x].x);
+                dw[2 * x + 1] = __float_as_uint(da[x].y);
+              }
+              tmem_st16(lane_addr + dcol, dw);
+            }
+          } else {
+#pragma unroll
+            for (int x = 0; x < 8; ++x) da[x] = u2f2(rn[2 * x], rn[2 * x + 1]);
+          }
+          uint32_t wv[8];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
+            const float2 sq = fmul2(sv, sv);
+            acc[8 * c + x] = pp == 0 ? sq : fadd2(acc[8 * c + x], sq);
+            const float2 w = fmul2(sv, da[x]);
+            wv[x] = pack2<T>(w.x, w.y);
           }
           st_tile128(sW, row, cbase, wv[0], wv[1], wv[2], wv[3]);
           st_tile128(sW, row, cbase + 8, wv[4], wv[5], wv[6], wv[7]);
         }
+        if (kHoist && pp == 0) tmem_wait_st();
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars.w_full);

@@ -50,6 +50,13 @@ __device__ __forceinline__ void st_tile128(uint32_t base, int row, int col0, uin
   st_shared_v4(base + box * 16384u + swz_offset(static_cast<uint32_t>(row), byte, 128), w0, w1, w2, w3);
 }
 
+// TMEM column (relative to a 128-column slot) of K-step kk of a packed 16-bit A operand written
+// by the two column halves of the compute warpgroups: each half stores its 64 values as 32
+// packed words at the start of its own 64-column half, i.e. slot columns [0,32) and [64,96).
+__device__ __forceinline__ uint32_t packed_col(int kk) {
+  return static_cast<uint32_t>(8 * kk + (kk >= 4 ? 32 : 0));
+}
+
 // Tensor map over a time-major (B, T, heads, W) 16-bit tensor with boxes [cw cols][1][128 rows][1].
 inline int make_tm_tokens(CUtensorMap* tm, const void* base, int B, int T, int heads, int W, int cw) {
   const uint64_t es = 2;

@@ -6,16 +6,20 @@
 //   O[t]     = sum_s half(A[t,s]) v_s,  den_t = sum_s A[t,s],  o_t = O[t] / (den_t > 0 ? den_t : 1)
 //
 // One CTA per (128-query tile, batch*head).  Warp roles (320 threads):
-//   warp 0      TMA producer: Q once, K and V tiles through 2-stage rings (4-D tensor maps over
+//   warp 0      TMA producer: Q once, K and V tiles through 3-stage rings (4-D tensor maps over
 //               the time-major (B,T,H,D) tensors, so rows past T are zero-filled per batch).
 //   warp 1      TMEM owner + single-thread MMA issuer: for each key tile, one tcgen05.mma chain
 //               per score part into a 3-slot TMEM ring (128 fp32 columns per slot), then the
-//               P*V chain into the O accumulator (columns 384..384+Dv).
+//               P*V chain into the O accumulator (columns 384..384+Dv).  P is read straight from
+//               tensor memory (A operand in TMEM), so P never touches shared memory.
 //   warps 2..9  two compute warpgroups.  Thread (warp%4, lane) owns TMEM lane = query row;
 //               warpgroup 0 owns key columns 0..63, warpgroup 1 owns 64..127.  They square and
 //               accumulate the parts (packed fp32x2 FMAs), apply mask/decay, accumulate the row
-//               sum, and write P = half(A) into a 128B-swizzled K-major smem tile for the P*V MMA.
+//               sum, and store P = half(A) as packed pairs into the first 32 columns of their half
+//               of the tile's last score slot (already read), where the P*V MMA reads it.
 //               Finally they read O from TMEM, divide by den and store o and den.
+// Slot reuse: the issuer never issues a score MMA into the slot that holds a P before it has
+// issued the P*V chain reading it (tcgen05 MMAs of one CTA execute in issue order).
 // Every mbarrier wait is bounded (see sm100.cuh); a timeout records a status code and drains.
 #include "attn_tc_common.cuh"
 
@@ -25,6 +29,7 @@ namespace {
 constexpr int kBT = 128;  // query rows per tile (= UMMA M)
 constexpr int kBK = 128;  // keys per tile (= UMMA N of the score MMAs, K of the P*V MMA)
 constexpr int kSlots = 3;
+constexpr int kStages = 3;
 constexpr int kThreads = 320;
 constexpr int kComputeWarp0 = 2;
 constexpr uint32_t kOCol = 384;
@@ -34,20 +39,18 @@ struct FwdSmem {
   static constexpr int Q_BYTES = kBT * D * 2;
   static constexpr int K_BYTES = kBK * D * 2;
   static constexpr int V_BYTES = kBK * DV * 2;
-  static constexpr int P_BYTES = kBT * kBK * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-  static constexpr int TOTAL = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_V = OFF_K + kStages * K_BYTES;
+  static constexpr int TOTAL = OFF_V + kStages * V_BYTES;
 };
 
 struct FwdBarriers {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[kSlots], s_empty[kSlots];
-  uint64_t p_full[2], p_empty[2];
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[kSlots], s_free[kSlots];
+  uint64_t p_full[2];
   uint64_t o_full;
   uint64_t drain;
   uint32_t tmem_base;
@@ -84,18 +87,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     bars.abort_flag = 0;
     mbar_init(&bars.q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&bars.k_full[i], 1);
       mbar_init(&bars.k_empty[i], 1);
       mbar_init(&bars.v_full[i], 1);
       mbar_init(&bars.v_empty[i], 1);
-      mbar_init(&bars.p_full[i], 8);
-      mbar_init(&bars.p_empty[i], 1);
     }
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&bars.s_full[i], 1);
-      mbar_init(&bars.s_empty[i], 8);
+      mbar_init(&bars.s_free[i], 8);
     }
+    mbar_init(&bars.p_full[0], 8);
+    mbar_init(&bars.p_full[1], 8);
     mbar_init(&bars.o_full, 1);
     mbar_init(&bars.drain, 1);
     fence_mbar_init();
@@ -120,8 +123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(smem + L::OFF_Q + bx * (kBT * CW * 2), &tmQ, &bars.q_full, bx * CW, hq, t0, b);
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < nk; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
         if (!mbar_wait(&bars.k_empty[st], ph ^ 1, wc)) break;
         mbar_arrive_expect_tx(&bars.k_full[st], L::K_BYTES);
         uint8_t* sk = smem + L::OFF_K + st * L::K_BYTES;
@@ -138,10 +141,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*wc.abort) {
         // drain: wait (bounded) for the most recent copies of each stage so no TMA write lands
         // in shared memory after the CTA retires.
-        for (int j = (issued_k > 2 ? issued_k - 2 : 0); j < issued_k; ++j)
-          mbar_drain(&bars.k_full[j & 1], (j >> 1) & 1);
-        for (int j = (issued_v > 2 ? issued_v - 2 : 0); j < issued_v; ++j)
-          mbar_drain(&bars.v_full[j & 1], (j >> 1) & 1);
+        for (int j = (issued_k > kStages ? issued_k - kStages : 0); j < issued_k; ++j)
+          mbar_drain(&bars.k_full[j % kStages], (j / kStages) & 1);
+        for (int j = (issued_v > kStages ? issued_v - kStages : 0); j < issued_v; ++j)
+          mbar_drain(&bars.v_full[j % kStages], (j / kStages) & 1);
       }
     }
   } else if (warp == 1) {
@@ -151,37 +154,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_pv = umma_idesc_f16(128, DV, kBF16, false, true);
       const uint32_t sQ = smem_u32(smem + L::OFF_Q);
       bool ok = mbar_wait(&bars.q_full, 0, wc);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&bars.p_full[st], ph, wc)) return false;
-        if (!mbar_wait(&bars.v_full[st], ph, wc)) return false;
+      // O += P_i V_i with P_i read from TMEM slot `sl`
+      auto issue_pv = [&](int i, int sl) -> bool {
+        const int st = i % kStages;
+        if (!mbar_wait(&bars.p_full[i & 1], (i >> 1) & 1, wc)) return false;
+        if (!mbar_wait(&bars.v_full[st], (i / kStages) & 1, wc)) return false;
         tc_fence_after();
-        const uint32_t sP = smem_u32(smem + L::OFF_P + st * L::P_BYTES);
         const uint32_t sV = smem_u32(smem + L::OFF_V + st * L::V_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          // P: K-major 128x128, two 64-column boxes of 16 KB, SW128
-          const uint64_t ad = umma_smem_desc(sP + (kk >> 2) * 16384u + (kk & 3) * 32u, 16u, 1024u, 128);
-          // V: MN-major, rows = keys (K), boxes of VCW columns (N); LBO = box stride
-          const uint64_t bd = umma_smem_desc(sV + kk * 16u * (VCW * 2u), kBK * VCW * 2u, 8u * VCW * 2u, VCW * 2);
-          umma_ss(tbase + kOCol, ad, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&bars.p_empty[st]);
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_ts(tbase + kOCol, tbase + sl * 128u + packed_col(kk), mnmajor_desc<VCW>(sV, 0, kk), idesc_pv,
+                  (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&bars.v_empty[st]);
         return true;
       };
       int u = 0;
+      int pend = -1, pend_slot = 0;  // key tile whose P*V chain is not issued yet, and its slot
       for (int j = 0; ok && j < nk; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&bars.k_full[st], (j >> 1) & 1, wc)) {
+        const int st = j % kStages;
+        if (!mbar_wait(&bars.k_full[st], (j / kStages) & 1, wc)) {
           ok = false;
           break;
         }
         const uint32_t sK = smem_u32(smem + L::OFF_K + st * L::K_BYTES);
         for (int pp = 0; pp < NP; ++pp, ++u) {
           const int slot = u % kSlots;
-          if (!mbar_wait(&bars.s_empty[slot], ((u / kSlots) & 1) ^ 1, wc)) {
+          if (pend >= 0 && slot == pend_slot) {
+            if (!issue_pv(pend, pend_slot)) {
+              ok = false;
+              break;
+            }
+            pend = -1;
+          }
+          if (!mbar_wait(&bars.s_free[slot], ((u / kSlots) & 1) ^ 1, wc)) {
             ok = false;
             break;
           }
@@ -196,12 +201,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         umma_commit(&bars.k_empty[st]);
-        if (j > 0 && !issue_pv(j - 1)) {
+        if (pend >= 0 && !issue_pv(pend, pend_slot)) {
           ok = false;
           break;
         }
+        pend = j;
+        pend_slot = (u - 1) % kSlots;
       }
-      if (ok) ok = issue_pv(nk - 1);
+      if (ok && pend >= 0) ok = issue_pv(pend, pend_slot);
       if (ok) umma_commit(&bars.o_full);
       // drain outstanding MMAs before the CTA can retire
       umma_commit(&bars.drain);
@@ -222,13 +229,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       cbase = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
       c_t = (t < T_) ? cbase[static_cast<size_t>(t) * p.HQ] : 0.f;
     }
-    float den = 0.f;
+    float2 den2 = make_float2(0.f, 0.f);
     bool ok = true;
     int u = 0;
     for (int j = 0; j < nk && ok; ++j) {
       float2 acc[32];
+      int slot = 0;
       for (int pp = 0; pp < NP; ++pp, ++u) {
-        const int slot = u % kSlots;
+        slot = u % kSlots;
         if (!mbar_wait(&bars.s_full[slot], (u / kSlots) & 1, wc)) {
           ok = false;
           break;
@@ -239,9 +247,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(a, r0);
         tmem_ld32(a + 32u, r1);
         tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.s_empty[slot]);
+        if (pp < NP - 1) {  // the last part's slot receives P and is released after it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.s_free[slot]);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
@@ -256,54 +266,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      // A = scale^2 * acc, causal mask on the diagonal tile, optional decay; row sum; P -> smem.
+      // A = scale^2 * acc, causal mask on the diagonal tile, optional decay; row sum; P -> TMEM.
       // For bf16 the scale^2 factor is left out of P and of the row sum: o = (P v) / den is
       // invariant under a common scale of P and den (bf16 has the fp32 exponent range, so the
       // unscaled P cannot overflow where the scaled one would not) and den is rescaled once in the
       // epilogue.  fp16 keeps the per-element scale so its overflow behaviour matches the
       // reference's cast of the scaled score to the value dtype.
-      const float2 sc2 = make_float2(scale2, scale2);
-      const int s_base = j * kBK + hc * 64;
-      const bool diag = (j == qt);
+      if (!kBF16) {
+        const float2 sc2 = make_float2(scale2, scale2);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float2 x = kBF16 ? acc[i] : fmul2(acc[i], sc2);
-        const int s0 = s_base + 2 * i;
-        if (diag) {
-          if (s0 > t) x.x = 0.f;
-          if (s0 + 1 > t) x.y = 0.f;
+        for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], sc2);
+      }
+      const int s_base = j * kBK + hc * 64;
+      if (j == qt) {  // diagonal tile: causal mask
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s0 = s_base + 2 * i;
+          if (s0 > t) acc[i].x = 0.f;
+          if (s0 + 1 > t) acc[i].y = 0.f;
         }
-        if (DECAY) {
+      }
+      if (DECAY) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s0 = s_base + 2 * i;
           const float cs0 = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
           const float cs1 = (s0 + 1 < T_) ? __ldg(cbase + static_cast<size_t>(s0 + 1) * p.HQ) : 0.f;
-          x.x *= __expf(fminf(c_t - cs0, 0.f));
-          x.y *= __expf(fminf(c_t - cs1, 0.f));
+          acc[i].x *= __expf(fminf(c_t - cs0, 0.f));
+          acc[i].y *= __expf(fminf(c_t - cs1, 0.f));
         }
-        acc[i] = x;
       }
-      float2 rs = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) rs = fadd2(rs, acc[i]);
-      den += rs.x + rs.y;
-      const int pst = j & 1;
-      if (!mbar_wait(&bars.p_empty[pst], ((j >> 1) & 1) ^ 1, wc)) {
-        ok = false;
-        break;
-      }
-      const uint32_t pbase = smem_u32(smem + L::OFF_P + pst * L::P_BYTES) + hc * 16384u;
+      for (int i = 0; i < 32; ++i) den2 = fadd2(den2, acc[i]);
+      uint32_t w0[16], w1[16];
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t w0 = pack2<T>(acc[4 * ch + 0].x, acc[4 * ch + 0].y);
-        const uint32_t w1 = pack2<T>(acc[4 * ch + 1].x, acc[4 * ch + 1].y);
-        const uint32_t w2 = pack2<T>(acc[4 * ch + 2].x, acc[4 * ch + 2].y);
-        const uint32_t w3 = pack2<T>(acc[4 * ch + 3].x, acc[4 * ch + 3].y);
-        st_shared_v4(pbase + swz_offset(row, ch * 16, 128), w0, w1, w2, w3);
+      for (int i = 0; i < 16; ++i) {
+        w0[i] = pack2<T>(acc[i].x, acc[i].y);
+        w1[i] = pack2<T>(acc[16 + i].x, acc[16 + i].y);
       }
-      fence_proxy_async_smem();
+      const uint32_t pa = lane_addr + slot * 128u + hc * 64u;
+      tmem_st16(pa, w0);
+      tmem_st16(pa + 16u, w1);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars.p_full[pst]);
+      if (lane == 0) {
+        mbar_arrive(&bars.p_full[j & 1]);
+        mbar_arrive(&bars.s_free[slot]);
+      }
     }
     // ------------------------------------------------------------------ epilogue
+    const float den = den2.x + den2.y;
     bars.den_x[hc][row] = den;
     named_bar_sync(1, 256);
     const float den_all = (bars.den_x[0][row] + bars.den_x[1][row]) * (kBF16 ? scale2 : 1.f);
