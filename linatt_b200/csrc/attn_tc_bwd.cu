@@ -57,13 +57,13 @@ struct BwdSmem {
   static constexpr int DQ_OFF_RING = DQ_OFF_O + O_BYTES;
   static constexpr int DQ_OFF_W = DQ_OFF_RING + kRing * ITEM;
   static constexpr int DQ_TOTAL = DQ_OFF_W + T_BYTES;
-  // dkdv kernel: K, V resident; ring of Q/dO tiles; P^T and W^T tiles
+  // dkdv kernel: K, V resident; ring of Q/dO tiles; two tiles that alternately receive W^T_p
+  // (for dK) and P^T (for dV), in the order W_0..W_{NP-1}, P, W_0, ... of the query tiles
   static constexpr int KV_OFF_K = 0;
   static constexpr int KV_OFF_V = KV_OFF_K + Q_BYTES;
   static constexpr int KV_OFF_RING = KV_OFF_V + O_BYTES;
-  static constexpr int KV_OFF_P = KV_OFF_RING + kRing * ITEM;
-  static constexpr int KV_OFF_W = KV_OFF_P + T_BYTES;
-  static constexpr int KV_OFF_VEC = KV_OFF_W + T_BYTES;      // 2 stages x {rden, delta*rden} x 128 fp32
+  static constexpr int KV_OFF_T = KV_OFF_RING + kRing * ITEM;  // 2 x T_BYTES
+  static constexpr int KV_OFF_VEC = KV_OFF_T + 2 * T_BYTES;   // 2 stages x {rden, delta*rden} x 128 fp32
   static constexpr int KV_OFF_BARS = KV_OFF_VEC + 2 * 2 * kTile * 4;
   static constexpr int KV_TOTAL = KV_OFF_BARS + 256;          // DkvBars lives here (no static smem)
 };
@@ -86,8 +86,7 @@ struct DkvBars {
   uint64_t ring_full[kRing], ring_empty[kRing];
   uint64_t dn_full, dn_empty;
   uint64_t s_full, s_empty;
-  uint64_t w_full, w_empty;
-  uint64_t p_full, p_empty;
+  uint64_t t_full[2], t_empty[2];  // the two smem tiles that alternately hold W^T_p and P^T
   uint64_t acc_done, drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -213,10 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t sV = smem_u32(smem + L::DQ_OFF_RING + slotV * L::ITEM);
+        {
+          const uint64_t od = kmajor_desc<VCW>(sO, 0, DV, 0), vd = kmajor_desc<VCW>(sV, 0, DV, 0);
 #pragma unroll
-        for (int kk = 0; kk < DV / 16; ++kk)
-          umma_ss(tbase + kColDN, kmajor_desc<VCW>(sO, 0, DV, kk), kmajor_desc<VCW>(sV, 0, DV, kk), id_nn,
-                  kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < DV / 16; ++kk)
+            umma_ss(tbase + kColDN, od + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+        }
         umma_commit(&bars.dn_full);
         umma_commit(&bars.ring_empty[slotV]);
         ++r;
@@ -233,19 +234,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&bars.w_full[slot], (uu >> 1) & 1, wc)) return false;
           tc_fence_after();
           const bool first = (j == 0) && (!SUM || gb == 0);
+          const uint64_t kd = mnmajor_desc<CW>(sK, gb * E / CW, 0);
+          const uint32_t wa = tbase + slot * 128u;
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ts(tbase + kColDQ + ga * E, tbase + slot * 128u + packed_col(kk),
-                    mnmajor_desc<CW>(sK, gb * E / CW, kk), id_dq, (!first || kk > 0) ? 1u : 0u);
+            umma_ts(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
+                    (!first || kk > 0) ? 1u : 0u);
           return true;
         };
         for (int pp = 0; pp < NP; ++pp, ++u) {
           const int slot = u & 1;
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+          const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0), kd = kmajor_desc<CW>(sK, gb, E, 0);
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss(tbase + slot * 128u, kmajor_desc<CW>(sQ, ga, E, kk), kmajor_desc<CW>(sK, gb, E, kk), id_nn,
-                    kk > 0 ? 1u : 0u);
+            umma_ss(tbase + slot * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
           umma_commit(&bars.s_full[slot]);
           if (pp > 0 && !issue_dq(pp - 1, u - 1)) {
             ok = false;
@@ -331,21 +334,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        // Software-pipelined over four 16-column chunks (loads of chunk c+1 in flight while chunk c
+        // is processed).  W chunk c goes to packed slot columns [8c, 8c+8) of this half, which hold
+        // S values already in registers; dA' (hoisted) overwrites dN chunk c in place.
+        uint32_t rs[2][16], rn[2][16];
+        const uint32_t sbase = lane_addr + slot * 128u + hc * 64u;
+        const uint32_t nbase = lane_addr + kColDN + hc * 64u;
+        tmem_ld16(sbase, rs[0]);
+        tmem_ld16(nbase, rn[0]);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t rs[32], rn[32];
-          const uint32_t dcol = kColDN + hc * 64u + c * 32u;
-          tmem_ld32(lane_addr + slot * 128u + hc * 64u + c * 32u, rs);
-          tmem_ld32(lane_addr + dcol, rn);
-          tmem_wait_ld();
-          const int cbase = hc * 64 + c * 32;  // key column within the tile
-          float2 da[16];
+        for (int c = 0; c < 4; ++c) {
+          const int cur = c & 1;
+          if (c < 3) {
+            tmem_ld16(sbase + (c + 1) * 16u, rs[cur ^ 1]);
+            tmem_ld16(nbase + (c + 1) * 16u, rn[cur ^ 1]);
+          }
+          const int cbase = hc * 64 + c * 16;  // key column within the tile
+          float2 da[8];
           if (!kHoist || pp == 0) {
 #pragma unroll
-            for (int x = 0; x < 16; ++x) da[x] = ffma2(u2f2(rn[2 * x], rn[2 * x + 1]), rden_w, ndr_w);
+            for (int x = 0; x < 8; ++x) da[x] = ffma2(u2f2(rn[cur][2 * x], rn[cur][2 * x + 1]), rden_w, ndr_w);
             if (diag) {
 #pragma unroll
-              for (int x = 0; x < 16; ++x) {
+              for (int x = 0; x < 8; ++x) {
                 const int s0 = cbase + 2 * x;
                 if (s0 > row) da[x].x = 0.f;
                 if (s0 + 1 > row) da[x].y = 0.f;
@@ -353,37 +365,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (DECAY) {
 #pragma unroll
-              for (int x = 0; x < 16; ++x) {
+              for (int x = 0; x < 8; ++x) {
                 const int sg = j * kTile + cbase + 2 * x;
                 const float cs0 = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
                 const float cs1 = sg + 1 < T_ ? __ldg(cb + static_cast<size_t>(sg + 1) * p.HQ) : 0.f;
                 da[x].x *= __expf(fminf(c_t - cs0, 0.f));
                 da[x].y *= __expf(fminf(c_t - cs1, 0.f));
-                const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
+                const float2 sv = u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]);
                 const float2 sq = fmul2(sv, sv);
-                acc[16 * c + x] = pp == 0 ? sq : fadd2(acc[16 * c + x], sq);
+                acc[8 * c + x] = pp == 0 ? sq : fadd2(acc[8 * c + x], sq);
               }
             }
             if (kHoist) {  // keep dA' for the remaining parts of this tile
-              uint32_t dw[32];
+              uint32_t dw[16];
 #pragma unroll
-              for (int x = 0; x < 16; ++x) {
+              for (int x = 0; x < 8; ++x) {
                 dw[2 * x] = __float_as_uint(da[x].x);
                 dw[2 * x + 1] = __float_as_uint(da[x].y);
               }
-              tmem_st32(lane_addr + dcol, dw);
+              tmem_st16(nbase + c * 16u, dw);
             }
           } else {
 #pragma unroll
-            for (int x = 0; x < 16; ++x) da[x] = u2f2(rn[2 * x], rn[2 * x + 1]);
+            for (int x = 0; x < 8; ++x) da[x] = u2f2(rn[cur][2 * x], rn[cur][2 * x + 1]);
           }
-          uint32_t wv[16];
+          uint32_t wv[8];
 #pragma unroll
-          for (int x = 0; x < 16; ++x) {
-            const float2 w = fmul2(u2f2(rs[2 * x], rs[2 * x + 1]), da[x]);
+          for (int x = 0; x < 8; ++x) {
+            const float2 w = fmul2(u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]), da[x]);
             wv[x] = pack2<T>(w.x, w.y);
           }
-          tmem_st16(lane_addr + slot * 128u + hc * 64u + c * 16u, wv);
+          tmem_st8(sbase + c * 8u, wv);
+          if (c < 3) tmem_wait_ld();
         }
         tmem_wait_st();
         tc_fence_before();
@@ -407,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float cs = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
             const float xd = c_t - cs;
             if (xd > 0.f) continue;
-            const float2 a2 = acc[16 * c + (x >> 1)];
+            const float2 a2 = acc[(s0 - hc * 64) >> 1];
             const float av = scale2 * ((x & 1) ? a2.y : a2.x) * __expf(xd);
             rsum += (__uint_as_float(rn[x]) - delta) * rden * av;
           }
@@ -442,6 +455,344 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (DECAY && live && hc == 0) p.dc[rowidx] = bars.xch_r[0][row] + bars.xch_r[1][row];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ================================================================================================
+// dq kernel, ring form (no decay)
+// ================================================================================================
+// TMEM: a ring of three 128-column slots that the items of every key tile pass through in order
+// -- dN = dO V^T, then the score parts S_0..S_{NP-1} -- and dQ at columns 384..511.  The compute
+// warps read dN once per tile and keep dA' = 2 scale^2 (dN - delta)/den (masked) in registers, so
+// the dN slot is handed back at once; each S_p slot is overwritten in place by W_p = S_p dA' (bf16
+// pairs), which the dQ chain reads as its A operand.  Before the issuer reuses a slot it waits for
+// the compute warps to release it and, if it held a W, issues that W's dQ chain first (MMAs of one
+// CTA execute in issue order).  So score MMAs run up to two items ahead of the compute warps.
+struct DqRingBars {
+  uint64_t qo_full;
+  uint64_t ring_full[kRing], ring_empty[kRing];
+  uint64_t i_full[3], i_free[3];
+  uint64_t acc_done, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float xch_delta[2][kTile];
+};
+
+template <typename T, int D, int DV, int M, bool SUM>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dq_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                        AttnBwdParams p) {
+  constexpr int E = D / M;
+  constexpr int CW = BoxW<E>::value;
+  constexpr int NBOX = D / CW;
+  constexpr int VCW = BoxW<DV>::value;
+  constexpr int NVBOX = DV / VCW;
+  constexpr int NP = SUM ? M * M : M;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kColDQ = 384;
+  using L = BwdSmem<D, DV>;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ DqRingBars bars;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T_ = p.T;
+  const int nqt = (T_ + kTile - 1) / kTile;
+  const int qi = nqt - 1 - static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y, b = bh / p.HQ, hq = bh % p.HQ, h = hq / p.G;
+  const int t0 = qi * kTile;
+  const int nk = qi + 1;
+  WaitCtx wc{p.status, &bars.abort_flag};
+
+  if (threadIdx.x == 0) {
+    bars.abort_flag = 0;
+    mbar_init(&bars.qo_full, 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&bars.ring_full[i], 1);
+      mbar_init(&bars.ring_empty[i], 1);
+    }
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars.i_full[i], 1);
+      mbar_init(&bars.i_free[i], 8);
+    }
+    mbar_init(&bars.acc_done, 1);
+    mbar_init(&bars.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmO);
+      mbar_arrive_expect_tx(&bars.qo_full, L::Q_BYTES + L::O_BYTES);
+      for (int bx = 0; bx < NBOX; ++bx)
+        tma_load_4d(smem + L::DQ_OFF_Q + bx * (kTile * CW * 2), &tmQ, &bars.qo_full, bx * CW, hq, t0, b);
+      for (int bx = 0; bx < NVBOX; ++bx)
+        tma_load_4d(smem + L::DQ_OFF_O + bx * (kTile * VCW * 2), &tmO, &bars.qo_full, bx * VCW, hq, t0, b);
+      int r = 0;
+      bool ok = true;
+      for (int j = 0; j < nk && ok; ++j) {
+        for (int item = 0; item < 2; ++item, ++r) {  // V_j then K_j
+          const int slot = r % kRing;
+          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + L::DQ_OFF_RING + slot * L::ITEM;
+          if (item == 0) {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
+            for (int bx = 0; bx < NVBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmV, &bars.ring_full[slot], bx * VCW, h, j * kTile, b);
+          } else {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
+            for (int bx = 0; bx < NBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, j * kTile, b);
+          }
+        }
+      }
+      if (!ok) {
+        for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
+          mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr int kItems = 1 + NP;  // items per key tile: dN, then S_0..S_{NP-1}
+      const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
+      const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
+      const uint32_t sQ = smem_u32(smem + L::DQ_OFF_Q);
+      const uint32_t sO = smem_u32(smem + L::DQ_OFF_O);
+      const uint32_t sRing = smem_u32(smem + L::DQ_OFF_RING);
+      bool ok = mbar_wait(&bars.qo_full, 0, wc);
+      // Item `it` lives in slot it % 3.  The previous occupant of that slot is item it - 3; if it was
+      // a score part, its W is in the slot and its dQ chain is issued before the slot is reused.
+      int it = 0, x = 0;       // x = it % 3
+      uint32_t use_par = 0;    // parity of (it / 3), i.e. of the current use of slot x
+      int r = 0;
+      for (int j = 0; ok && j <= nk; ++j) {
+        const int n_items = (j < nk) ? kItems : 3;  // after the last tile: three drain claims
+        for (int q = 0; q < n_items; ++q) {
+          // ---- claim slot x for item it
+          if (it >= 3) {
+            if (!mbar_wait(&bars.i_free[x], use_par ^ 1, wc)) {
+              ok = false;
+              break;
+            }
+            const int prev = it - 3;
+            const int pq = prev % kItems;
+            if (pq > 0) {  // issue the pending dQ chain of score part pq - 1 of tile prev / kItems
+              const int pj = prev / kItems, pp = pq - 1;
+              const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+              const bool first = (pj == 0) && (!SUM || gb == 0);
+              const int kslot = (2 * pj + 1) % kRing;
+              const uint64_t kd = mnmajor_desc<CW>(sRing + kslot * L::ITEM, gb * E / CW, 0);
+              const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
+              tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < kTile / 16; ++kk)
+                umma_ts(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
+                        (!first || kk > 0) ? 1u : 0u);
+              if (pp == NP - 1) umma_commit(&bars.ring_empty[kslot]);  // K tile no longer needed
+            }
+          }
+          if (j == nk) {  // drain claim only
+            ++it;
+            if (++x == 3) { x = 0; use_par ^= 1; }
+            continue;
+          }
+          // ---- issue item (j, q) into slot x
+          if (q == 0) {  // dN = dO V_j^T
+            const int slotV = r % kRing;
+            if (!mbar_wait(&bars.ring_full[slotV], (r / kRing) & 1, wc)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t od = kmajor_desc<VCW>(sO, 0, DV, 0);
+            const uint64_t vd = kmajor_desc<VCW>(sRing + slotV * L::ITEM, 0, DV, 0);
+#pragma unroll
+            for (int kk = 0; kk < DV / 16; ++kk)
+              umma_ss(tbase + x * 128u, od + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit(&bars.i_full[x]);
+            umma_commit(&bars.ring_empty[slotV]);
+            r += 1;
+            if (!mbar_wait(&bars.ring_full[r % kRing], (r / kRing) & 1, wc)) {  // K_j
+              ok = false;
+              break;
+            }
+            r += 1;
+          } else {  // S_p = Q_a K_b^T
+            const int pp = q - 1;
+            const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+            const int slotK = (2 * j + 1) % kRing;
+            tc_fence_after();
+            const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0);
+            const uint64_t kd = kmajor_desc<CW>(sRing + slotK * L::ITEM, gb, E, 0);
+#pragma unroll
+            for (int kk = 0; kk < E / 16; ++kk)
+              umma_ss(tbase + x * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit(&bars.i_full[x]);
+          }
+          ++it;
+          if (++x == 3) {
+            x = 0;
+            use_par ^= 1;
+          }
+        }
+      }
+      if (ok) umma_commit(&bars.acc_done);
+      umma_commit(&bars.drain);
+      mbar_drain(&bars.drain, 0);
+    }
+  } else {
+    const int cw = warp - kComputeWarp0;
+    const int hc = cw >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int tg = t0 + row;
+    const bool live = tg < T_;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    const size_t rowidx = (static_cast<size_t>(b) * T_ + tg) * p.HQ + hq;  // (b, tg, hq)
+    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
+    // ---- delta_t = <o_t, dO_t> over this thread's half of Dv, then exchanged
+    float dpart = 0.f;
+    if (live) {
+      constexpr int HV = DV / 2;
+      const T* orow = static_cast<const T*>(p.o) + rowidx * DV + hc * HV;
+      const T* grow = static_cast<const T*>(p.dout) + rowidx * DV + hc * HV;
+#pragma unroll
+      for (int c8 = 0; c8 < HV; c8 += 8) {
+        const uint4 a = *reinterpret_cast<const uint4*>(orow + c8);
+        const uint4 g = *reinterpret_cast<const uint4*>(grow + c8);
+        const T* ah = reinterpret_cast<const T*>(&a);
+        const T* gh = reinterpret_cast<const T*>(&g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dpart = fmaf(to_f32<T>(ah[e]), to_f32<T>(gh[e]), dpart);
+      }
+    }
+    bars.xch_delta[hc][row] = dpart;
+    named_bar_sync(1, 256);
+    const float delta = bars.xch_delta[0][row] + bars.xch_delta[1][row];
+    float rden = 1.f;
+    if (live) {
+      const float dn = p.den[rowidx];
+      rden = 1.f / (dn > 0.f ? dn : 1.f);
+      if (hc == 0) ws.delta[rowidx] = delta;
+    }
+    if (hc == 0) {  // every row of the tile, including rows past T (rden 1, delta 0)
+      const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
+      ws.rden[hm] = rden;
+      ws.dr[hm] = live ? delta * rden : 0.f;
+    }
+    const float w_scale = 2.f * p.scale * p.scale;
+    const float2 rden_w = make_float2(rden * w_scale, rden * w_scale);
+    const float2 ndr_w = make_float2(-delta * rden * w_scale, -delta * rden * w_scale);
+    bool ok = true;
+    int it = 0;
+    for (int j = 0; j < nk && ok; ++j) {
+      const bool diag = (j == qi);
+      float2 da[32];  // dA' of this thread's 64 key columns
+      {
+        const int x = it % 3;
+        if (!mbar_wait(&bars.i_full[x], (it / 3) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t nbase = lane_addr + x * 128u + hc * 64u;
+        uint32_t rn[2][16];
+        tmem_ld16(nbase, rn[0]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cur = c & 1;
+          if (c < 3) tmem_ld16(nbase + (c + 1) * 16u, rn[cur ^ 1]);
+#pragma unroll
+          for (int x2 = 0; x2 < 8; ++x2) da[8 * c + x2] = ffma2(u2f2(rn[cur][2 * x2], rn[cur][2 * x2 + 1]), rden_w, ndr_w);
+          if (c < 3) tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.i_free[x]);
+        ++it;
+        if (diag) {
+#pragma unroll
+          for (int x2 = 0; x2 < 32; ++x2) {
+            const int s0 = hc * 64 + 2 * x2;
+            if (s0 > row) da[x2].x = 0.f;
+            if (s0 + 1 > row) da[x2].y = 0.f;
+          }
+        }
+      }
+      for (int pp = 0; pp < NP; ++pp, ++it) {
+        const int x = it % 3;
+        if (!mbar_wait(&bars.i_full[x], (it / 3) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sbase = lane_addr + x * 128u + hc * 64u;
+        uint32_t rs[2][16];
+        tmem_ld16(sbase, rs[0]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cur = c & 1;
+          if (c < 3) tmem_ld16(sbase + (c + 1) * 16u, rs[cur ^ 1]);
+          uint32_t wv[8];
+#pragma unroll
+          for (int x2 = 0; x2 < 8; ++x2) {
+            const float2 w = fmul2(u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]), da[8 * c + x2]);
+            wv[x2] = pack2<T>(w.x, w.y);
+          }
+          tmem_st8(sbase + c * 8u, wv);  // columns of S already in registers
+          if (c < 3) tmem_wait_ld();
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.i_free[x]);
+      }
+    }
+    // ---- epilogue: dQ -> global
+    named_bar_sync(1, 256);
+    if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
+      tc_fence_after();
+      constexpr int HD = D / 2;
+      T* dqrow = static_cast<T*>(p.dq) + rowidx * D + hc * HD;
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + kColDQ + hc * HD + c0, r);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            *reinterpret_cast<uint4*>(dqrow + c0 + 8 * v2) = w;
+          }
+        }
+      }
     }
   }
   tc_fence_before();
@@ -504,10 +855,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars.dn_empty, 8);
     mbar_init(&bars.s_full, 1);
     mbar_init(&bars.s_empty, 8);
-    mbar_init(&bars.w_full, 8);
-    mbar_init(&bars.w_empty, 1);
-    mbar_init(&bars.p_full, 8);
-    mbar_init(&bars.p_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.t_full[i], 8);
+      mbar_init(&bars.t_empty[i], 1);
+    }
     mbar_init(&bars.acc_done, 1);
     mbar_init(&bars.drain, 1);
     fence_mbar_init();
@@ -580,10 +931,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
       const uint32_t sK = smem_u32(smem + L::KV_OFF_K);
       const uint32_t sV = smem_u32(smem + L::KV_OFF_V);
-      const uint32_t sP = smem_u32(smem + L::KV_OFF_P);
-      const uint32_t sW = smem_u32(smem + L::KV_OFF_W);
+      const uint32_t sT = smem_u32(smem + L::KV_OFF_T);
       bool ok = mbar_wait(&bars.kv_full, 0, wc);
-      int r = 0, u = 0;
+      int r = 0, u = 0, g = 0;  // g counts uses of the two W/P tiles (tile g & 1, use g >> 1)
       for (int n = 0; ok && n < nwork; ++n, r += 2) {
         const int slotQ = r % kRing, slotO = (r + 1) % kRing;
         if (!mbar_wait(&bars.ring_full[slotO], ((r + 1) / kRing) & 1, wc) ||
@@ -594,10 +944,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t sO = smem_u32(smem + L::KV_OFF_RING + slotO * L::ITEM);
         // dN^T = V dO^T  (rows: keys, cols: queries)
+        {
+          const uint64_t vd = kmajor_desc<VCW>(sV, 0, DV, 0), od = kmajor_desc<VCW>(sO, 0, DV, 0);
 #pragma unroll
-        for (int kk = 0; kk < DV / 16; ++kk)
-          umma_ss(tbase + kColDN, kmajor_desc<VCW>(sV, 0, DV, kk), kmajor_desc<VCW>(sO, 0, DV, kk), id_nn,
-                  kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < DV / 16; ++kk)
+            umma_ss(tbase + kColDN, vd + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+        }
         umma_commit(&bars.dn_full);
         if (!mbar_wait(&bars.ring_full[slotQ], (r / kRing) & 1, wc)) {
           ok = false;
@@ -606,14 +958,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sQ = smem_u32(smem + L::KV_OFF_RING + slotQ * L::ITEM);
         auto issue_dk = [&](int pp, int uu) -> bool {
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          if (!mbar_wait(&bars.w_full, uu & 1, wc)) return false;
+          const int tb = g & 1;
+          if (!mbar_wait(&bars.t_full[tb], (g >> 1) & 1, wc)) return false;
           tc_fence_after();
           const bool first = (n == 0) && (!SUM || ga == 0);
+          const uint64_t wd = kmajor128_desc(sT + tb * L::T_BYTES, 0), qd = mnmajor_desc<CW>(sQ, ga * E / CW, 0);
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ss(tbase + kColDK + gb * E, kmajor128_desc(sW, kk), mnmajor_desc<CW>(sQ, ga * E / CW, kk), id_dk,
+            umma_ss(tbase + kColDK + gb * E, wd + kstep<64>(kk), qd + mnstep<CW>(kk), id_dk,
                     (!first || kk > 0) ? 1u : 0u);
-          umma_commit(&bars.w_empty);
+          umma_commit(&bars.t_empty[tb]);
+          ++g;
+          (void)uu;
           return true;
         };
         for (int pp = 0; pp < NP; ++pp, ++u) {
@@ -623,9 +979,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+          const uint64_t kd = kmajor_desc<CW>(sK, gb, E, 0), qd = kmajor_desc<CW>(sQ, ga, E, 0);
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss(tbase, kmajor_desc<CW>(sK, gb, E, kk), kmajor_desc<CW>(sQ, ga, E, kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_ss(tbase, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
           umma_commit(&bars.s_full);
           if (pp > 0 && !issue_dk(pp - 1, u - 1)) {
             ok = false;
@@ -638,16 +995,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&bars.ring_empty[slotQ]);
         // dV += P^T dO
-        if (!mbar_wait(&bars.p_full, n & 1, wc)) {
+        const int tbp = g & 1;
+        if (!mbar_wait(&bars.t_full[tbp], (g >> 1) & 1, wc)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        {
+          const uint64_t pd = kmajor128_desc(sT + tbp * L::T_BYTES, 0), od = mnmajor_desc<VCW>(sO, 0, 0);
+          const uint32_t acc0 = n > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_ss(tbase + kColDV, kmajor128_desc(sP, kk), mnmajor_desc<VCW>(sO, 0, kk), id_dv,
-                  (n > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&bars.p_empty);
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_ss(tbase + kColDV, pd + kstep<64>(kk), od + mnstep<VCW>(kk), id_dv, kk > 0 ? 1u : acc0);
+        }
+        umma_commit(&bars.t_empty[tbp]);
+        ++g;
         umma_commit(&bars.ring_empty[slotO]);
       }
       if (ok) umma_commit(&bars.acc_done);
@@ -665,10 +1027,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float w_scale = 2.f * p.scale * p.scale;
     const float2 wsc2 = make_float2(w_scale, w_scale);
     const float scale2 = p.scale * p.scale;
-    const uint32_t sP = smem_u32(smem + L::KV_OFF_P);
-    const uint32_t sW = smem_u32(smem + L::KV_OFF_W);
+    const uint32_t sT = smem_u32(smem + L::KV_OFF_T);
     bool ok = true;
-    int u = 0;
+    int u = 0, g = 0;  // g: uses of the two W/P tiles, in the issuer's order
     float csum = 0.f;
     for (int n = 0; n < nwork && ok; ++n) {
       const int hq = h * p.G + n / nq;
@@ -689,22 +1050,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float2 acc[32];
       for (int pp = 0; pp < NP; ++pp, ++u) {
-        if (!mbar_wait(&bars.s_full, u & 1, wc) || !mbar_wait(&bars.w_empty, (u & 1) ^ 1, wc)) {
+        const int tb = g & 1;
+        const uint32_t sW = sT + tb * L::T_BYTES;
+        if (!mbar_wait(&bars.s_full, u & 1, wc) || !mbar_wait(&bars.t_empty[tb], ((g >> 1) & 1) ^ 1, wc)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        // Software-pipelined over four 16-column chunks: the TMEM loads of chunk c+1 are in
+        // flight while chunk c is processed; the score slot is released as soon as the last
+        // chunk of S has landed in registers.
+        uint32_t rs[2][16], rn[2][16];
+        tmem_ld16(lane_addr + hc * 64u, rs[0]);
+        tmem_ld16(lane_addr + kColDN + hc * 64u, rn[0]);
+        tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t rs[16], rn[16];
+          const int cur = c & 1;
           const uint32_t dcol = kColDN + hc * 64u + c * 16u;
-          tmem_ld16(lane_addr + hc * 64u + c * 16u, rs);
-          tmem_ld16(lane_addr + dcol, rn);
-          tmem_wait_ld();
-          if (c == 3) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.s_empty);
+          if (c < 3) {
+            tmem_ld16(lane_addr + hc * 64u + (c + 1) * 16u, rs[cur ^ 1]);
+            tmem_ld16(lane_addr + dcol + 16u, rn[cur ^ 1]);
           }
           const int cbase = hc * 64 + c * 16;  // query column within the tile
           float2 da[8];
@@ -714,7 +1080,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int x4 = 0; x4 < 4; ++x4) {
               const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
               const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
-              const float2 nv0 = u2f2(rn[4 * x4], rn[4 * x4 + 1]), nv1 = u2f2(rn[4 * x4 + 2], rn[4 * x4 + 3]);
+              const float2 nv0 = u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]);
+              const float2 nv1 = u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]);
               da[2 * x4] = fmul2(ffma2(nv0, make_float2(rd.x, rd.y), make_float2(-dr.x, -dr.y)), wsc2);
               da[2 * x4 + 1] = fmul2(ffma2(nv1, make_float2(rd.z, rd.w), make_float2(-dr.z, -dr.w)), wsc2);
             }
@@ -747,28 +1114,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
 #pragma unroll
-            for (int x = 0; x < 8; ++x) da[x] = u2f2(rn[2 * x], rn[2 * x + 1]);
+            for (int x = 0; x < 8; ++x) da[x] = u2f2(rn[cur][2 * x], rn[cur][2 * x + 1]);
           }
           uint32_t wv[8];
 #pragma unroll
           for (int x = 0; x < 8; ++x) {
-            const float2 sv = u2f2(rs[2 * x], rs[2 * x + 1]);
-            const float2 sq = fmul2(sv, sv);
-            acc[8 * c + x] = pp == 0 ? sq : fadd2(acc[8 * c + x], sq);
+            const float2 sv = u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]);
+            acc[8 * c + x] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x]);
             const float2 w = fmul2(sv, da[x]);
             wv[x] = pack2<T>(w.x, w.y);
           }
           st_tile128(sW, row, cbase, wv[0], wv[1], wv[2], wv[3]);
           st_tile128(sW, row, cbase + 8, wv[4], wv[5], wv[6], wv[7]);
+          if (c < 3) {
+            tmem_wait_ld();
+            if (c == 2) {  // all of S is in registers: hand the slot back to the issuer
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars.s_empty);
+            }
+          }
         }
         if (kHoist && pp == 0) tmem_wait_st();
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.w_full);
+        if (lane == 0) mbar_arrive(&bars.t_full[tb]);
+        ++g;
       }
       if (!ok) break;
       // P^T = A / den  (and, with decay, the column part of dc)
-      if (!mbar_wait(&bars.p_empty, (n & 1) ^ 1, wc)) {
+      const int tbp = g & 1;
+      const uint32_t sP = sT + tbp * L::T_BYTES;
+      if (!mbar_wait(&bars.t_empty[tbp], ((g >> 1) & 1) ^ 1, wc)) {
         ok = false;
         break;
       }
@@ -812,10 +1189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bars.p_full);
+        mbar_arrive(&bars.t_full[tbp]);
         mbar_arrive(&bars.dn_empty);
         mbar_arrive(&bars.vec_empty[vs]);
       }
+      ++g;
       if (DECAY && (n % nq == nq - 1)) {
         // last query tile of this query head: dc_s -= sum_t G[t, s]
         if (live) atomicAdd(p.dc + (static_cast<size_t>(b) * T_ + sg) * p.HQ + hq, -csum);
@@ -888,7 +1266,8 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (e) return e;
   const int nt = (p.T + kTile - 1) / kTile;
   if (p.phases != 2) {
-    auto kern = attn_bwd_dq_tc<T, D, DV, M, SUM, DECAY>;
+    // decay needs sum_p S_p^2 for its dc row sums and keeps the two-slot kernel; otherwise the ring
+    auto kern = DECAY ? attn_bwd_dq_tc<T, D, DV, M, SUM, DECAY> : attn_bwd_dq_ring_tc<T, D, DV, M, SUM>;
     const size_t smem = L::DQ_TOTAL + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)

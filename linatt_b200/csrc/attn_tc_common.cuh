@@ -25,6 +25,20 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int g, int E, int
   return umma_smem_desc(base + box * (kTile * CW * 2u) + within, 16u, 8u * CW * 2u, CW * 2);
 }
 
+// Descriptor increment (in 16-byte units, added to the start-address field) from K-step 0 to K-step
+// kk of a K-major operand stored as boxes of CW columns: 16 elements = 32 bytes per step, and a new
+// box every 64 elements.  Compile-time after unrolling; the start address never carries out of
+// its 14-bit field because shared-memory addresses are below 256 KB.
+template <int CW>
+__device__ __forceinline__ constexpr uint64_t kstep(int kk) {
+  return static_cast<uint64_t>(((kk >> 2) * (kTile * CW * 2) + (kk & 3) * 32) >> 4);
+}
+// Same for an MN-major operand: each K-step is 16 rows of CW*2 bytes.
+template <int CW>
+__device__ __forceinline__ constexpr uint64_t mnstep(int kk) {
+  return static_cast<uint64_t>((kk * 16 * CW * 2) >> 4);
+}
+
 // MN-major descriptor of K-step kk (16 rows of the tile) for the N extent starting at box
 // `box0` of a tile stored as boxes of CW columns (the N extent may span several boxes, LBO apart).
 template <int CW>

@@ -161,10 +161,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&bars.v_full[st], (i / kStages) & 1, wc)) return false;
         tc_fence_after();
         const uint32_t sV = smem_u32(smem + L::OFF_V + st * L::V_BYTES);
+        const uint64_t vd = mnmajor_desc<VCW>(sV, 0, 0);
+        const uint32_t pa = tbase + sl * 128u;
+        const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_ts(tbase + kOCol, tbase + sl * 128u + packed_col(kk), mnmajor_desc<VCW>(sV, 0, kk), idesc_pv,
-                  (i > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(tbase + kOCol, pa + packed_col(kk), vd + mnstep<VCW>(kk), idesc_pv, kk > 0 ? 1u : acc0);
         umma_commit(&bars.v_empty[st]);
         return true;
       };
@@ -192,11 +194,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+          const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0), kd = kmajor_desc<CW>(sK, gb, E, 0);
 #pragma unroll
-          for (int kk = 0; kk < E / 16; ++kk) {
-            umma_ss(tbase + slot * 128u, kmajor_desc<CW>(sQ, ga, E, kk), kmajor_desc<CW>(sK, gb, E, kk),
-                    idesc_qk, kk > 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < E / 16; ++kk)
+            umma_ss(tbase + slot * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), idesc_qk, kk > 0 ? 1u : 0u);
           umma_commit(&bars.s_full[slot]);
         }
         if (!ok) break;
@@ -242,10 +243,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        // two 32-column chunks; the second chunk's load is in flight while the first is squared
         uint32_t r0[32], r1[32];
         const uint32_t a = lane_addr + slot * 128u + hc * 64u;
         tmem_ld32(a, r0);
+        tmem_wait_ld();
         tmem_ld32(a + 32u, r1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+          acc[i] = pp == 0 ? fmul2(x0, x0) : ffma2(x0, x0, acc[i]);
+        }
         tmem_wait_ld();
         if (pp < NP - 1) {  // the last part's slot receives P and is released after it
           tc_fence_before();
@@ -254,15 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
           const float2 x1 = make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
-          if (pp == 0) {
-            acc[i] = fmul2(x0, x0);
-            acc[16 + i] = fmul2(x1, x1);
-          } else {
-            acc[i] = ffma2(x0, x0, acc[i]);
-            acc[16 + i] = ffma2(x1, x1, acc[16 + i]);
-          }
+          acc[16 + i] = pp == 0 ? fmul2(x1, x1) : ffma2(x1, x1, acc[16 + i]);
         }
       }
       if (!ok) break;

@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/kata_b200.h"
+#include "kata_b200.h"
 
 namespace kata {
 
