@@ -40,7 +40,9 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-B, T, H, D, DV, M = 16, 4096, 8, 128, 128, 4
+B, T, H, D, DV = 16, 4096, 8, 128, 128
+M = 4          # num_groups of the headline configuration (overridable with --num-groups)
+SCORE = "concat"
 METRIC = "KATA attn fwd+bwd tokens/s/GPU at B16·T4096·H8·D128; % of bf16 TC peak"
 UNIT = "tokens/s"
 
@@ -49,17 +51,22 @@ def pairs(t: int) -> float:
     return t * (t + 1) / 2.0
 
 
-# algorithmic FLOPs per launch (one B*H batch): GEMM-equivalent = 2 * P * 128 per head
+# algorithmic FLOPs per launch (one B*H batch): GEMM-equivalent = 2 * P * 128 per head.  The
+# sum score does M*M part products instead of M, i.e. its score GEMM costs M GEMM-eq.
 GEMM_EQ = B * H * 2.0 * pairs(T) * D
-ALG_FLOPS = {"fwd": 2 * GEMM_EQ, "bwd_dq": 1 * GEMM_EQ, "bwd_dkdv": 4 * GEMM_EQ}
-STEP_FLOPS = sum(ALG_FLOPS.values())  # 3.5 x forward
+
+
+def alg_flops():
+    s_eq = M if SCORE == "sum" else 1  # score-product GEMM-eq (S in fwd, S in dk/dv, dQ/dK parts)
+    fl = {"fwd": (s_eq + 1) * GEMM_EQ, "bwd_dq": s_eq * GEMM_EQ, "bwd_dkdv": (2 * s_eq + 2) * GEMM_EQ}
+    return fl, sum(fl.values())
 
 
 def workload_config(n_gpus: int) -> dict:
     return {
-        "workload": "KATA-SPD flash attention fwd+bwd, concat score M=4, causal, bf16 (config 3)",
+        "workload": f"KATA-SPD flash attention fwd+bwd, {SCORE} score M={M}, causal, bf16 (config 3)",
         "batch_per_gpu": B, "global_batch": B * n_gpus, "seq_len": T, "heads": H, "head_dim": D,
-        "value_dim": DV, "num_groups": M, "score": "concat",
+        "value_dim": DV, "num_groups": M, "score": SCORE,
         "parallelism": f"batch*head shard x{n_gpus}, no collective",
         "l2": "3 rotating input sets of 537 MB (bf16 q, k, v, dO) per cycle, each larger than the 126 MB L2",
     }
@@ -207,11 +214,12 @@ class AbiStep:
         self.dv = torch.empty(B, T, H, DV, device=dev, dtype=torch.bfloat16)
         self.status = _lib.status_word(dev)
         scale = 1.0 / math.sqrt(D // M)
+        sc = _lib.SCORE[SCORE]
         self.fa = _lib.AttnFwdArgs(o=self.o.data_ptr(), den=self.den.data_ptr(), status=self.status.data_ptr(),
-                                   dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=0, algo=1, scale=scale)
+                                   dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=sc, algo=1, scale=scale)
         self.ba = _lib.AttnBwdArgs(o=self.o.data_ptr(), den=self.den.data_ptr(), dq=self.dq.data_ptr(),
                                    dk=self.dk.data_ptr(), dv=self.dv.data_ptr(), status=self.status.data_ptr(),
-                                   dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=0, algo=1, scale=scale)
+                                   dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=sc, algo=1, scale=scale)
         nbytes = self.L.kata_attn_bwd_workspace_bytes(self.ba)
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.ba.workspace = self.ws.data_ptr()
@@ -313,7 +321,8 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
             k = kh.to(dev, non_blocking=True).requires_grad_(True)
             v = vh.to(dev, non_blocking=True).requires_grad_(True)
             do = doh.to(dev, non_blocking=True)
-            o = pka.parallel_kata_attn(q, k, v, num_groups=M)
+            fn = pka.parallel_kata_attn_sum if SCORE == "sum" else pka.parallel_kata_attn
+            o = fn(q, k, v, num_groups=M)
             o.backward(do)
             for dst, src in zip(outs, (o.detach(), q.grad, k.grad, v.grad)):
                 dst.copy_(src, non_blocking=True)
@@ -347,6 +356,7 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
         return
 
     peak, peak_src = load_peaks()
+    ALG_FLOPS, STEP_FLOPS = alg_flops()
     kernels = {}
     for name, ms in kern_ms.items():
         avg = ms / K
@@ -383,7 +393,11 @@ def main() -> None:
     ap.add_argument("--cpu-slices", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--num-groups", type=int, default=4, help="M (the benchmark metric is quoted at M=4)")
+    ap.add_argument("--score", choices=["concat", "sum"], default="concat")
     args = ap.parse_args()
+    global M, SCORE
+    M, SCORE = args.num_groups, args.score
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -76,3 +76,56 @@ def test_oracle_backward_is_gradient_of_forward():
             cm[0, 4, 0] -= eps
             num = (f(q, k, v, cp) - f(q, k, v, cm)) / (2 * eps)
             assert abs(num - dc[0, 4, 0]) < 1e-6 * max(1.0, abs(num))
+
+
+# ------------------------------------------------------------------------------------------------
+# SPD delta rule
+# ------------------------------------------------------------------------------------------------
+def _delta_golden():
+    from tests.conftest import GOLDEN
+
+    z = np.load(GOLDEN / "delta_golden.npz")
+    out = {}
+    for key in z.files:
+        case, name = key.split("/")
+        out.setdefault(case, {})[name] = z[key]
+    return out
+
+
+@pytest.mark.parametrize("case", ["m1", "m2", "m4_default_scale"])
+def test_delta_oracle_matches_reference_U(case):
+    from oracle import delta_oracle as do
+
+    rec = _delta_golden()[case]
+    B, T, H, D, Dv, M, scale = rec["meta"]
+    scale = None if scale < 0 else float(scale)
+    res = do.flash_delta(rec["q"], rec["k"], rec["v"], rec["beta"], int(M), scale)
+    assert ko.rel_l2(res["U"], rec["U"]) < 1e-5
+    # erase term identity: beta * (V - E) = U
+    assert ko.rel_l2(rec["beta"][..., None] * (rec["v"] - res["E"]), res["U"]) < 1e-10
+
+
+def test_delta_oracle_gradients_finite_difference():
+    from oracle import delta_oracle as do
+
+    rng = np.random.default_rng(5)
+    B, T, H, D, M = 1, 11, 1, 8, 2
+    q, k, v = (rng.standard_normal((B, T, H, D)) for _ in range(3))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((B, T, H))))
+    go = rng.standard_normal((B, T, H, D))
+    for normalize in (False, True):
+        res = do.flash_delta(q, k, v, beta, M, 0.5, normalize, grad_out=go)
+
+        def f(qq, kk, vv, bb):
+            return float((do.flash_delta(qq, kk, vv, bb, M, 0.5, normalize)["o"] * go).sum())
+
+        eps = 1e-6
+        for arr, gname, idx in ((q, "dq", (0, 6, 0, 3)), (k, "dk", (0, 2, 0, 5)), (v, "dv", (0, 4, 0, 1)),
+                                (beta, "dbeta", (0, 3, 0))):
+            xp, xm = arr.copy(), arr.copy()
+            xp[idx] += eps
+            xm[idx] -= eps
+            args_p = [xp if a is arr else a for a in (q, k, v, beta)]
+            args_m = [xm if a is arr else a for a in (q, k, v, beta)]
+            num = (f(*args_p) - f(*args_m)) / (2 * eps)
+            assert abs(num - res[gname][idx]) < 1e-6 * max(1.0, abs(num)), gname
