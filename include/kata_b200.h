@@ -145,6 +145,75 @@ KATA_API int kata_attn_bwd(const kata_attn_bwd_args* args, kata_stream_t stream)
  * every input and output buffer; this path calls no allocating routine. */
 KATA_API int kata_attn_bwd_noalloc(const kata_attn_bwd_args* args, kata_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * SPD delta rule (DeltaKATA), forward.
+ *   kappa(x,y) = sum_{g,h} (scale * x_g . y_h)^2   over all M*M group pairs (E = D/M)
+ *   U = (I + diag(beta) tril(kappa(k,k), -1))^{-1} diag(beta) v
+ *   num = tril(kappa(q,k)) U (diagonal included),  den_t = sum_{s<=t} kappa(q_t,k_s)
+ *   o = num / (den + eps) if normalize else num
+ * Replaces flash_delta_U (kata/spd/flash_delta.py:186-212, kernel K14 :27-183),
+ * flash_delta_readout (:975-983, K15 :900-972) and flash_delta_den (:1049-1057, K16 :988-1046),
+ * i.e. _FlashDelta.forward (:1062-1081).  The reference requires T % 64 == 0; any T >= 1 works here.
+ * Outputs are fp32 like the reference's.  E = tril(kappa(k,k),-1) U (the erase term) is written
+ * when E != NULL.  phases: 0 = U (+E) then o and den; 1 = U (+E) only (flash_delta_U);
+ * 2 = readout from a given U: o when o != NULL (flash_delta_readout), den when den != NULL
+ * (flash_delta_den; U may then be NULL); v, beta, E unused.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;     /* (B,T,H,D)  dtype */
+  const void* k;     /* (B,T,H,D)  dtype */
+  const void* v;     /* (B,T,H,Dv) dtype */
+  const float* beta; /* (B,T,H) fp32 */
+  float* U;          /* (B,T,H,Dv) fp32 [out; in for phases == 2] */
+  float* E;          /* (B,T,H,Dv) fp32 [out] or NULL */
+  float* o;          /* (B,T,H,Dv) fp32 [out] */
+  float* den;        /* (B,T,H) fp32 [out] (written for both normalize settings) */
+  int dtype;         /* of q, k, v */
+  int B, T, H, D, Dv;
+  int M;             /* groups; D % M == 0, M*M <= 16 */
+  int normalize;
+  float scale;       /* reference default 1/E */
+  float eps;
+  int phases;
+} kata_delta_fwd_args;
+
+KATA_API int kata_delta_fwd(const kata_delta_fwd_args* args, kata_stream_t stream);
+
+/* SPD delta rule, backward: dq, dk, dv, dbeta (fp32) from the forward's U (and o, den) and dO.
+ * normalize: dO' = dO/(den+eps) and z_t = <dO_t,o_t>/(den_t+eps) enter dA_qk = dO'.U - z
+ * (the "consistent" normalised backward, kata/spd/flash_delta.py:1084-1108).
+ * z != NULL selects the reference's flash_delta_bwd(..., do, z) contract instead: dout is the
+ * already-scaled dO' and z the centring term; o, den and normalize are then unused.
+ * E == NULL: the erase term is recomputed into the workspace (as the reference does).
+ * Replaces flash_delta_bwd (kata/spd/flash_delta.py:830-895) with K17-K21 (:267-827). */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* beta;
+  const float* U;
+  const float* E;    /* or NULL */
+  const float* o;
+  const float* den;
+  const float* dout; /* (B,T,H,Dv) fp32 */
+  const float* z;    /* (B,T,H) fp32 or NULL */
+  float* dq;         /* (B,T,H,D) fp32 [out] */
+  float* dk;         /* (B,T,H,D) fp32 [out] */
+  float* dv;         /* (B,T,H,Dv) fp32 [out] */
+  float* dbeta;      /* (B,T,H) fp32 [out] */
+  void* workspace;
+  size_t workspace_bytes;
+  int dtype;
+  int B, T, H, D, Dv;
+  int M;
+  int normalize;
+  float scale;
+  float eps;
+} kata_delta_bwd_args;
+
+KATA_API size_t kata_delta_bwd_workspace_bytes(const kata_delta_bwd_args* args);
+KATA_API int kata_delta_bwd(const kata_delta_bwd_args* args, kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

@@ -49,6 +49,26 @@ class AttnBwdArgs(ctypes.Structure):
     ]
 
 
+class DeltaFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("beta", c_void_p),
+        ("U", c_void_p), ("E", c_void_p), ("o", c_void_p), ("den", c_void_p),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("D", c_int), ("Dv", c_int),
+        ("M", c_int), ("normalize", c_int), ("scale", c_float), ("eps", c_float), ("phases", c_int),
+    ]
+
+
+class DeltaBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("beta", c_void_p),
+        ("U", c_void_p), ("E", c_void_p), ("o", c_void_p), ("den", c_void_p), ("dout", c_void_p), ("z", c_void_p),
+        ("dq", c_void_p), ("dk", c_void_p), ("dv", c_void_p), ("dbeta", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("D", c_int), ("Dv", c_int),
+        ("M", c_int), ("normalize", c_int), ("scale", c_float), ("eps", c_float),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -76,6 +96,12 @@ def lib() -> ctypes.CDLL:
             L.kata_attn_bwd_noalloc.argtypes = [ctypes.POINTER(AttnBwdArgs), c_void_p]
             L.kata_attn_bwd_workspace_bytes.restype = c_size_t
             L.kata_attn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnBwdArgs)]
+            L.kata_delta_fwd.restype = c_int
+            L.kata_delta_fwd.argtypes = [ctypes.POINTER(DeltaFwdArgs), c_void_p]
+            L.kata_delta_bwd.restype = c_int
+            L.kata_delta_bwd.argtypes = [ctypes.POINTER(DeltaBwdArgs), c_void_p]
+            L.kata_delta_bwd_workspace_bytes.restype = c_size_t
+            L.kata_delta_bwd_workspace_bytes.argtypes = [ctypes.POINTER(DeltaBwdArgs)]
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:

@@ -30,6 +30,17 @@ def golden():
     return out
 
 
+@pytest.fixture(scope="session")
+def golden_delta():
+    """Dict case -> dict of arrays from tests/golden/delta_golden.npz (reference U solve)."""
+    z = np.load(GOLDEN / "delta_golden.npz")
+    out: dict[str, dict[str, np.ndarray]] = {}
+    for key in z.files:
+        case, name = key.split("/")
+        out.setdefault(case, {})[name] = z[key]
+    return out
+
+
 def attn_case_meta(rec):
     B, T, HQ, H, D, Dv, M, is_sum, decay = (int(x) for x in rec["meta"])
     return dict(B=B, T=T, HQ=HQ, H=H, D=D, Dv=Dv, M=M, score="sum" if is_sum else "concat", decay=bool(decay))

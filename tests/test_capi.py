@@ -73,6 +73,29 @@ def test_host_side_validation(L):
     assert L.kata_attn_bwd(b, None) == -1  # decay without dc
 
 
+def test_delta_host_side_validation(L):
+    from linatt_b200 import _lib
+
+    assert L.kata_delta_fwd(None, None) == -1
+    a = _lib.DeltaFwdArgs(dtype=5, B=1, T=8, H=1, D=64, Dv=64, M=4, scale=1.0)
+    assert L.kata_delta_fwd(a, None) == -2
+    a = _lib.DeltaFwdArgs(dtype=1, B=1, T=8, H=1, D=64, Dv=64, M=3, scale=1.0)
+    assert L.kata_delta_fwd(a, None) == -3  # D % M
+    a = _lib.DeltaFwdArgs(dtype=1, B=1, T=8, H=1, D=64, Dv=64, M=8, scale=1.0)
+    assert L.kata_delta_fwd(a, None) == -8  # M*M > 16
+    a = _lib.DeltaFwdArgs(dtype=1, B=1, T=8, H=1, D=64, Dv=64, M=4, scale=1.0)
+    assert L.kata_delta_fwd(a, None) == -1  # null pointers
+    a = _lib.DeltaFwdArgs(q=16, k=16, v=16, beta=16, U=16, dtype=1, B=1, T=8, H=1, D=64, Dv=64, M=4, phases=3)
+    assert L.kata_delta_fwd(a, None) == -1  # bad phases
+    b = _lib.DeltaBwdArgs(q=16, k=16, v=16, beta=16, U=16, o=16, den=16, dout=16, dq=16, dk=16, dv=16, dbeta=16,
+                          dtype=1, B=2, T=8, H=3, D=64, Dv=32, M=4)
+    # dnum, dU, Y, E (B*T*H*Dv each) + z (B*T*H), fp32
+    assert L.kata_delta_bwd_workspace_bytes(b) == 4 * (4 * 48 * 32 + 48)
+    assert L.kata_delta_bwd(b, None) == -5
+    b.o = None
+    assert L.kata_delta_bwd(b, None) == -1  # normalised path needs o, den unless z is given
+
+
 def test_product_path_refuses_cpu_tensors():
     import torch
 
@@ -81,3 +104,8 @@ def test_product_path_refuses_cpu_tensors():
     q = torch.randn(1, 8, 1, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         parallel_kata_attn(q, q, q, num_groups=4)
+
+    from linatt_b200.spd import flash_delta
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        flash_delta(q, q, q, q[..., 0], 4)
