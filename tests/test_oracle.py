@@ -129,3 +129,64 @@ def test_delta_oracle_gradients_finite_difference():
             args_m = [xm if a is arr else a for a in (q, k, v, beta)]
             num = (f(*args_p) - f(*args_m)) / (2 * eps)
             assert abs(num - res[gname][idx]) < 1e-6 * max(1.0, abs(num)), gname
+
+
+# ------------------------------------------------------------------------------------------------
+# Gated delta rule (fla chunk_gated_delta_rule)
+# ------------------------------------------------------------------------------------------------
+def _gdn_golden():
+    from tests.conftest import GOLDEN
+
+    z = np.load(GOLDEN / "gdn_golden.npz")
+    out = {}
+    for key in z.files:
+        case, name = key.split("/")
+        out.setdefault(case, {})[name] = z[key]
+    return out
+
+
+@pytest.mark.parametrize("case", ["basic", "chunk_t128", "varlen"])
+def test_gdn_oracle_matches_fla_naive(case):
+    from oracle import gdn_oracle as go
+
+    rec = _gdn_golden()[case]
+    res = go.gdn(rec["q"], rec["k"], rec["v"], rec["g"], rec["beta"], initial_state=rec.get("h0"),
+                 output_final_state=True, cu_seqlens=rec.get("cu_seqlens"), grad_out=rec["do"],
+                 grad_final=rec["dht"])
+    assert ko.rel_l2(res["o"], rec["o"]) < 1e-5
+    assert ko.rel_l2(res["final_state"], rec["ht"]) < 1e-5
+    for n in ("dq", "dk", "dv", "dg", "dbeta") + (("dh0",) if "h0" in rec else ()):
+        assert ko.rel_l2(res[n], rec[n]) < 1e-5, n
+    if "o_chunk" in rec:  # fla's chunked naive form agrees with its recurrent form
+        assert ko.rel_l2(rec["o_chunk"], rec["o"]) < 1e-5
+
+
+def test_gdn_oracle_gate_and_l2norm_finite_difference():
+    """The in-kernel gate and q/k l2norm options: gradients of the oracle against central
+    differences (the options are prologue transforms; fla's formulas are restated)."""
+    from oracle import gdn_oracle as go
+
+    rng = np.random.default_rng(7)
+    B, T, H, HV, K, V = 1, 9, 1, 2, 4, 3
+    q, k = (rng.standard_normal((B, T, H, K)) for _ in range(2))
+    v = rng.standard_normal((B, T, HV, V))
+    g = rng.standard_normal((B, T, HV))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((B, T, HV))))
+    A_log, dt_bias = rng.standard_normal(HV) * 0.3, rng.standard_normal(HV) * 0.3
+    do_ = rng.standard_normal((B, T, HV, V))
+    kw = dict(use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=A_log, dt_bias=dt_bias)
+    res = go.gdn(q, k, v, g, beta, grad_out=do_, **kw)
+
+    def f(**over):
+        args = dict(q=q, k=k, v=v, g=g, beta=beta, **kw)
+        args.update(over)
+        return float((go.gdn(**args)["o"] * do_).sum())
+
+    eps = 1e-6
+    for name, arr, idx in (("q", q, (0, 5, 0, 2)), ("k", k, (0, 3, 0, 1)), ("g", g, (0, 4, 1)),
+                           ("A_log", A_log, (1,)), ("dt_bias", dt_bias, (0,))):
+        xp, xm = arr.copy(), arr.copy()
+        xp[idx] += eps
+        xm[idx] -= eps
+        num = (f(**{name: xp}) - f(**{name: xm})) / (2 * eps)
+        assert abs(num - res["d" + name][idx]) < 1e-6 * max(1.0, abs(num)), name
