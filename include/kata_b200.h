@@ -214,6 +214,73 @@ typedef struct {
 KATA_API size_t kata_delta_bwd_workspace_bytes(const kata_delta_bwd_args* args);
 KATA_API int kata_delta_bwd(const kata_delta_bwd_args* args, kata_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Gated delta rule (GDN), forward: per (sequence, value head), for t in order
+ *   S <- exp(g_t) S;  u_t = beta_t (v_t - S^T k_t);  S <- S + k_t u_t^T;  o_t = scale S^T q_t
+ * computed chunk-wise (64 tokens) in the WY form.  Replaces fla's chunk_gated_delta_rule_fwd
+ * (fla/ops/gated_delta_rule/chunk.py:29-114, the arithmetic of chunk_gated_delta_rule :365-526),
+ * which the reference calls for its gated_deltanet models; fla is third-party (pinned 0.5.0,
+ * scripts/setup.sh:27).  Token tensors are time-major; with cu_seqlens (B == 1) the tokens of
+ * sequence n are [cu_seqlens[n], cu_seqlens[n+1]) and chunk_offsets[n] is the index of its first
+ * 64-token chunk (chunk_offsets[N] == num_chunks).  Without cu_seqlens N == B and
+ * num_chunks == B * ceil(T/64).  This build covers K == V == 64.
+ * A receives, per token row, its row of the chunk's (I + L)^{-1} (fla's A); the backward takes it.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;             /* (B,T,H,K)  dtype */
+  const void* k;             /* (B,T,H,K)  dtype */
+  const void* v;             /* (B,T,HV,V) dtype */
+  const float* g;            /* (B,T,HV) per-token log gate (not cumulated) */
+  const float* beta;         /* (B,T,HV) */
+  const float* h0;           /* (N,HV,K,V) initial state or NULL */
+  void* o;                   /* (B,T,HV,V) dtype [out] */
+  float* ht;                 /* (N,HV,K,V) final state [out] or NULL */
+  float* A;                  /* (B,T,HV,64) [out] */
+  const int* cu_seqlens;     /* (N+1) int32 device or NULL */
+  const int* chunk_offsets;  /* (N+1) int32 device or NULL (iff cu_seqlens is NULL) */
+  void* workspace;
+  size_t workspace_bytes;
+  int dtype;
+  int B, T, H, HV, K, V;
+  int N, num_chunks;
+  float scale;               /* fla default K^-0.5 */
+} kata_gdn_fwd_args;
+
+KATA_API size_t kata_gdn_fwd_workspace_bytes(const kata_gdn_fwd_args* args);
+KATA_API int kata_gdn_fwd(const kata_gdn_fwd_args* args, kata_stream_t stream);
+
+/* Gated delta rule, backward: dq, dk (per q/k head, summed over its value heads), dv, dg (per-token
+ * log gate), dbeta, dh0, all fp32, from the forward's inputs, its A and dO (+ d final state).
+ * Replaces fla's chunk_gated_delta_rule_bwd (fla/ops/gated_delta_rule/chunk.py:117-236). */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* h0;           /* or NULL */
+  const float* A;            /* the forward's A */
+  const void* dout;          /* (B,T,HV,V) dtype */
+  const float* dht;          /* (N,HV,K,V) or NULL */
+  float* dq;                 /* (B,T,H,K) [out] */
+  float* dk;                 /* (B,T,H,K) [out] */
+  float* dv;                 /* (B,T,HV,V) [out] */
+  float* dg;                 /* (B,T,HV) [out] */
+  float* dbeta;              /* (B,T,HV) [out] */
+  float* dh0;                /* (N,HV,K,V) [out] or NULL */
+  const int* cu_seqlens;
+  const int* chunk_offsets;
+  void* workspace;
+  size_t workspace_bytes;
+  int dtype;
+  int B, T, H, HV, K, V;
+  int N, num_chunks;
+  float scale;
+} kata_gdn_bwd_args;
+
+KATA_API size_t kata_gdn_bwd_workspace_bytes(const kata_gdn_bwd_args* args);
+KATA_API int kata_gdn_bwd(const kata_gdn_bwd_args* args, kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

@@ -69,6 +69,27 @@ class DeltaBwdArgs(ctypes.Structure):
     ]
 
 
+class GdnFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("g", c_void_p), ("beta", c_void_p), ("h0", c_void_p),
+        ("o", c_void_p), ("ht", c_void_p), ("A", c_void_p), ("cu_seqlens", c_void_p), ("chunk_offsets", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HV", c_int), ("K", c_int), ("V", c_int),
+        ("N", c_int), ("num_chunks", c_int), ("scale", c_float),
+    ]
+
+
+class GdnBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("g", c_void_p), ("beta", c_void_p), ("h0", c_void_p),
+        ("A", c_void_p), ("dout", c_void_p), ("dht", c_void_p), ("dq", c_void_p), ("dk", c_void_p),
+        ("dv", c_void_p), ("dg", c_void_p), ("dbeta", c_void_p), ("dh0", c_void_p),
+        ("cu_seqlens", c_void_p), ("chunk_offsets", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HV", c_int), ("K", c_int), ("V", c_int),
+        ("N", c_int), ("num_chunks", c_int), ("scale", c_float),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -102,6 +123,13 @@ def lib() -> ctypes.CDLL:
             L.kata_delta_bwd.argtypes = [ctypes.POINTER(DeltaBwdArgs), c_void_p]
             L.kata_delta_bwd_workspace_bytes.restype = c_size_t
             L.kata_delta_bwd_workspace_bytes.argtypes = [ctypes.POINTER(DeltaBwdArgs)]
+            for nm, st in (("fwd", GdnFwdArgs), ("bwd", GdnBwdArgs)):
+                f = getattr(L, f"kata_gdn_{nm}")
+                f.restype = c_int
+                f.argtypes = [ctypes.POINTER(st), c_void_p]
+                w = getattr(L, f"kata_gdn_{nm}_workspace_bytes")
+                w.restype = c_size_t
+                w.argtypes = [ctypes.POINTER(st)]
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:

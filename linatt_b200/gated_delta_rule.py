@@ -1,0 +1,219 @@
+"""Gated delta rule (GDN) -- drop-in for ``fla.ops.gated_delta_rule`` as the reference uses it.
+
+The reference's gated_deltanet models call fla's ``chunk_gated_delta_rule``
+(``fla/ops/gated_delta_rule/chunk.py:365-526``; fla is third-party, pinned 0.5.0 by
+``scripts/setup.sh:27``) through ``fla/layers/gated_deltanet.py:266-278``.  This module provides
+the same entry point, argument for argument:
+
+  chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
+                         output_final_state=False, use_qk_l2norm_in_kernel=False,
+                         cu_seqlens=None, cu_seqlens_cpu=None, cp_context=None,
+                         transpose_state_layout=False, **kwargs) -> (o, final_state)
+
+with ``kwargs`` use_gate_in_kernel / A_log / dt_bias (g <- -exp(A_log) softplus(g + dt_bias)),
+plus ``ChunkGatedDeltaRuleFunction`` and the alias ``chunk_gdn``.  All recurrence arithmetic runs
+in ``libkata_b200.so`` (``kata_gdn_fwd`` / ``kata_gdn_bwd``).  The q/k l2norm and the in-kernel
+gate are applied as differentiable torch prologues before the library call.  Context parallelism
+(``cp_context``) is fla's own multi-GPU scheme and is not provided.  The kernels work on 64-wide
+heads; narrower q/k/v heads are zero-padded to 64 (exact), wider ones are not supported yet.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+__all__ = ["chunk_gated_delta_rule", "chunk_gdn", "ChunkGatedDeltaRuleFunction"]
+
+CHUNK = 64
+
+
+def _dtype(*ts):
+    dt = ts[0].dtype
+    for t in ts[1:]:
+        dt = torch.promote_types(dt, t.dtype)
+    if dt not in _lib.DTYPE:
+        raise TypeError(f"unsupported dtype {dt}; expected float32, bfloat16 or float16")
+    return dt
+
+
+def _chunk_tables(cu_seqlens, cu_seqlens_cpu, B, T, dev):
+    """(N, num_chunks, cu int32 device or None, chunk offsets int32 device or None)."""
+    if cu_seqlens is None:
+        return B, B * ((T + CHUNK - 1) // CHUNK), None, None
+    cs = (cu_seqlens_cpu if cu_seqlens_cpu is not None else cu_seqlens.cpu()).to(torch.int64)
+    lens = cs[1:] - cs[:-1]
+    co = torch.zeros(len(lens) + 1, dtype=torch.int64)
+    co[1:] = torch.cumsum((lens + CHUNK - 1) // CHUNK, 0)
+    return (len(lens), int(co[-1]), cu_seqlens.to(device=dev, dtype=torch.int32).contiguous(),
+            co.to(device=dev, dtype=torch.int32))
+
+
+KDIM = 64  # key / value width of the kernels; narrower heads are zero-padded (exact)
+
+
+def _pad_last(x, n):
+    return x if x is None or x.shape[-1] == n else F.pad(x, (0, n - x.shape[-1]))
+
+
+def _pad_state(h):
+    if h is None or (h.shape[-2] == KDIM and h.shape[-1] == KDIM):
+        return h
+    return F.pad(h, (0, KDIM - h.shape[-1], 0, KDIM - h.shape[-2])).contiguous()
+
+
+def _check_width(K, V):
+    if K > KDIM or V > KDIM:
+        raise NotImplementedError(f"linatt_b200 gated delta rule covers head widths up to {KDIM} (got K={K}, V={V})")
+
+
+def _fwd(q, k, v, g, beta, scale, h0, want_final, tables):
+    dev = _lib.require_cuda(q, k, v, g, beta, h0)
+    K0, V0 = q.shape[-1], v.shape[-1]
+    _check_width(K0, V0)
+    q, k, v = (_pad_last(x, KDIM).contiguous() for x in (q, k, v))
+    h0 = _pad_state(h0)
+    B, T, H, K = q.shape
+    HV, V = v.shape[2], v.shape[3]
+    N, NC, cu, co = tables
+    dt = _dtype(q, k, v)
+    o = torch.empty(B, T, HV, V, device=dev, dtype=dt)
+    A = torch.empty(B, T, HV, CHUNK, device=dev, dtype=torch.float32)
+    ht = torch.empty(N, HV, K, V, device=dev, dtype=torch.float32) if want_final else None
+    a = _lib.GdnFwdArgs(
+        q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), g=g.data_ptr(), beta=beta.data_ptr(), h0=_lib.ptr(h0),
+        o=o.data_ptr(), ht=_lib.ptr(ht), A=A.data_ptr(), cu_seqlens=_lib.ptr(cu), chunk_offsets=_lib.ptr(co),
+        workspace=None, workspace_bytes=0, dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HV=HV, K=K, V=V, N=N,
+        num_chunks=NC, scale=float(scale))
+    L = _lib.lib()
+    ws = torch.empty(int(L.kata_gdn_fwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(dev):
+        _lib.check(L.kata_gdn_fwd(a, _lib.stream_handle(dev)), "kata_gdn_fwd")
+    if V0 != V:
+        o = o[..., :V0]
+    if ht is not None and (K0 != K or V0 != V):
+        ht = ht[..., :K0, :V0].contiguous()
+    return o, A, ht
+
+
+def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables):
+    dev = _lib.require_cuda(q, k, v, g, beta, A, h0, do, dht)
+    K0, V0 = q.shape[-1], v.shape[-1]
+    dt = _dtype(q, k, v)
+    q, k, v = (_pad_last(x, KDIM).contiguous() for x in (q, k, v))
+    h0 = _pad_state(h0)
+    do = _pad_last(do.to(dt), KDIM).contiguous()
+    dht = _pad_state(None if dht is None else dht.float())
+    B, T, H, K = q.shape
+    HV, V = v.shape[2], v.shape[3]
+    N, NC, cu, co = tables
+    f32 = dict(device=dev, dtype=torch.float32)
+    dq = torch.empty(B, T, H, K, **f32)
+    dk = torch.empty(B, T, H, K, **f32)
+    dv = torch.empty(B, T, HV, V, **f32)
+    dg = torch.empty(B, T, HV, **f32)
+    db = torch.empty(B, T, HV, **f32)
+    dh0 = torch.empty(N, HV, K, V, **f32) if h0 is not None else None
+    dht = None if dht is None else dht.float().contiguous()
+    a = _lib.GdnBwdArgs(
+        q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), g=g.data_ptr(), beta=beta.data_ptr(), h0=_lib.ptr(h0),
+        A=A.data_ptr(), dout=do.data_ptr(), dht=_lib.ptr(dht), dq=dq.data_ptr(), dk=dk.data_ptr(),
+        dv=dv.data_ptr(), dg=dg.data_ptr(), dbeta=db.data_ptr(), dh0=_lib.ptr(dh0), cu_seqlens=_lib.ptr(cu),
+        chunk_offsets=_lib.ptr(co), workspace=None, workspace_bytes=0, dtype=_lib.DTYPE[dt], B=B, T=T, H=H,
+        HV=HV, K=K, V=V, N=N, num_chunks=NC, scale=float(scale))
+    L = _lib.lib()
+    ws = torch.empty(int(L.kata_gdn_bwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    with torch.cuda.device(dev):
+        _lib.check(L.kata_gdn_bwd(a, _lib.stream_handle(dev)), "kata_gdn_bwd")
+    if K0 != K or V0 != V:
+        dq, dk, dv = dq[..., :K0], dk[..., :K0], dv[..., :V0]
+        dh0 = None if dh0 is None else dh0[..., :K0, :V0]
+    return dq, dk, dv, dg, db, dh0
+
+
+class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
+    """Same argument list as fla's ChunkGatedDeltaRuleFunction (chunk.py:238-362); the l2norm and
+    gate options arrive already applied by ``chunk_gated_delta_rule``."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens=None,
+                cu_seqlens_cpu=None, use_qk_l2norm_in_kernel=False, cp_context=None, transpose_state_layout=False,
+                use_gate_in_kernel=False, A_log=None, dt_bias=None):
+        if cp_context is not None:
+            raise NotImplementedError("cp_context (fla context parallelism) is not provided by linatt_b200")
+        B, T = q.shape[:2]
+        dt = _dtype(q, k, v)
+        qc, kc, vc = (x.to(dt).contiguous() for x in (q, k, v))
+        gc, bc = g.float().contiguous(), beta.float().contiguous()
+        h0 = None
+        if initial_state is not None:
+            h0 = initial_state.float()
+            h0 = (h0.transpose(-1, -2) if transpose_state_layout else h0).contiguous()
+        tables = _chunk_tables(cu_seqlens, cu_seqlens_cpu, B, T, q.device)
+        o, A, ht = _fwd(qc, kc, vc, gc, bc, scale, h0, output_final_state, tables)
+        if ht is not None and transpose_state_layout:
+            ht = ht.transpose(-1, -2).contiguous()
+        ctx.save_for_backward(qc, kc, vc, gc, bc, A, h0)
+        ctx.tables = tables
+        ctx.scale = scale
+        ctx.transpose_state_layout = transpose_state_layout
+        ctx.dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, beta.dtype,
+                      None if initial_state is None else initial_state.dtype)
+        return o.to(q.dtype), ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        qc, kc, vc, gc, bc, A, h0 = ctx.saved_tensors
+        if dht is not None and ctx.transpose_state_layout:
+            dht = dht.transpose(-1, -2)
+        dq, dk, dv, dg, db, dh0 = _bwd(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables)
+        tq, tk, tv, tg, tb, th = ctx.dtypes
+        if dh0 is not None:
+            dh0 = (dh0.transpose(-1, -2) if ctx.transpose_state_layout else dh0).to(th)
+        return (dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), db.to(tb), None, dh0, None, None, None, None, None,
+                None, None, None, None)
+
+
+def _l2norm(x):
+    # fla/modules/l2norm.py:42,140: y = x / sqrt(sum(x^2) + 1e-6), computed in fp32, returned in x.dtype
+    xf = x.float()
+    return (xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + 1e-6)).to(x.dtype)
+
+
+def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None, output_final_state=False,
+                           use_qk_l2norm_in_kernel=False, cu_seqlens=None, cu_seqlens_cpu=None, cp_context=None,
+                           transpose_state_layout=False, **kwargs):
+    """Returns (o (B,T,HV,V) in q's dtype, final_state (N,HV,K,V) fp32 or None)."""
+    if q.shape[2] != k.shape[2]:
+        raise ValueError(f"q and k must have the same number of heads, got {q.shape[2]} and {k.shape[2]}")
+    H, HV = q.shape[2], v.shape[2]
+    if HV % H != 0:
+        raise ValueError(f"num_v_heads (HV={HV}) must be divisible by num_heads (H={H})")
+    if "head_first" in kwargs:
+        raise DeprecationWarning("head_first has been removed. Inputs must be in `[B, T, H, ...]` format.")
+    if cp_context is not None:
+        raise NotImplementedError("cp_context (fla context parallelism) is not provided by linatt_b200")
+    if cu_seqlens is not None:
+        if q.shape[0] != 1:
+            raise ValueError(f"The batch size is expected to be 1 rather than {q.shape[0]} when using `cu_seqlens`.")
+        if initial_state is not None and initial_state.shape[0] != len(cu_seqlens) - 1:
+            raise ValueError(f"The number of initial states is expected to be equal to the number of input "
+                             f"sequences, i.e., {len(cu_seqlens) - 1} rather than {initial_state.shape[0]}.")
+    if kwargs.get("use_gate_in_kernel", False):
+        A_log, dt_bias = kwargs.get("A_log"), kwargs.get("dt_bias")
+        assert A_log is not None, "A_log must be provided when use_gate_in_kernel=True."
+        x = g.float() + (dt_bias.float() if dt_bias is not None else 0.0)
+        g = -A_log.float().exp() * F.softplus(x)
+    if use_qk_l2norm_in_kernel:
+        q, k = _l2norm(q), _l2norm(k)
+    if scale is None:
+        scale = k.shape[-1] ** -0.5
+    return ChunkGatedDeltaRuleFunction.apply(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens,
+                                             cu_seqlens_cpu, False, None, transpose_state_layout, False, None, None)
+
+
+chunk_gdn = chunk_gated_delta_rule
