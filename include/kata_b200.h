@@ -272,6 +272,9 @@ typedef struct {
   const int* chunk_offsets;
   void* workspace;
   size_t workspace_bytes;
+  const void* fwd_workspace; /* the forward call's workspace, unchanged since, or NULL: with it the
+                                backward reuses the forward's chunk states instead of recomputing
+                                them (and needs a smaller workspace) */
   int dtype;
   int B, T, H, HV, K, V;
   int N, num_chunks;

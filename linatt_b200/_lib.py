@@ -85,6 +85,7 @@ class GdnBwdArgs(ctypes.Structure):
         ("A", c_void_p), ("dout", c_void_p), ("dht", c_void_p), ("dq", c_void_p), ("dk", c_void_p),
         ("dv", c_void_p), ("dg", c_void_p), ("dbeta", c_void_p), ("dh0", c_void_p),
         ("cu_seqlens", c_void_p), ("chunk_offsets", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("fwd_workspace", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HV", c_int), ("K", c_int), ("V", c_int),
         ("N", c_int), ("num_chunks", c_int), ("scale", c_float),
     ]

@@ -148,14 +148,32 @@ __device__ __forceinline__ float row_reduce(float x) {
   return x;
 }
 
-// Load rows [bos, bos+len) of a (tokens, heads, 64) tensor (head `h`) into a 64 x LD tile,
-// zero-filling rows >= len.
+// Load 64 rows of 64 values into a 64 x LD fp32 tile: row r starts at base + r * stride (elements);
+// rows >= len are zero.  Vector loads (16 bytes), all issued before any shared store.
+template <typename T>
+__device__ __forceinline__ void load_rows(float* s, const T* base, size_t stride, int len) {
+  constexpr int VEC = 16 / sizeof(T);       // elements per 16-byte load
+  constexpr int PERROW = 64 / VEC;
+  constexpr int PER = CH * PERROW / NT;     // loads per thread
+  uint4 buf[PER];
+#pragma unroll
+  for (int m = 0; m < PER; ++m) {
+    const int idx = threadIdx.x + NT * m, r = idx / PERROW, c = (idx % PERROW) * VEC;
+    buf[m] = r < len ? *reinterpret_cast<const uint4*>(base + r * stride + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int m = 0; m < PER; ++m) {
+    const int idx = threadIdx.x + NT * m, r = idx / PERROW, c = (idx % PERROW) * VEC;
+    const T* e = reinterpret_cast<const T*>(&buf[m]);
+#pragma unroll
+    for (int x = 0; x < VEC; ++x) s[r * LD + c + x] = to_f32<T>(e[x]);
+  }
+}
+
+// Rows [bos, bos+len) of a (tokens, heads, 64) tensor, head h.
 template <typename T>
 __device__ __forceinline__ void load_tile(float* s, const T* base, int heads, int h, int bos, int len) {
-  for (int i = threadIdx.x; i < CH * 64; i += NT) {
-    const int r = i >> 6, c = i & 63;
-    s[r * LD + c] = r < len ? to_f32<T>(base[(static_cast<size_t>(bos + r) * heads + h) * 64 + c]) : 0.f;
-  }
+  load_rows<T>(s, base + (static_cast<size_t>(bos) * heads + h) * 64, static_cast<size_t>(heads) * 64, len);
 }
 
 __device__ __forceinline__ void load_vec(float* s, const float* base, int heads, int h, int bos, int len) {
@@ -231,18 +249,24 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(GdnParams p) {
     if (threadIdx.x < 192) {
       float* col = threadIdx.x < 64 ? sX0 + threadIdx.x : (threadIdx.x < 128 ? sX1 + threadIdx.x - 64 : sX2 + threadIdx.x - 128);
       for (int i = 1; i < CH; ++i) {
-        float acc = 0.f;
-        for (int j = 0; j < i; ++j) acc = fmaf(sL[i * LD + j], col[j * LD], acc);
-        col[i * LD] -= acc;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int j = 0;
+        for (; j + 3 < i; j += 4) {
+          a0 = fmaf(sL[i * LD + j], col[j * LD], a0);
+          a1 = fmaf(sL[i * LD + j + 1], col[(j + 1) * LD], a1);
+          a2 = fmaf(sL[i * LD + j + 2], col[(j + 2) * LD], a2);
+          a3 = fmaf(sL[i * LD + j + 3], col[(j + 3) * LD], a3);
+        }
+        for (; j < i; ++j) a0 = fmaf(sL[i * LD + j], col[j * LD], a0);
+        col[i * LD] -= (a0 + a1) + (a2 + a3);
       }
     }
     __syncthreads();
   } else {
     // Tm given (the forward's A): W = Tm X1, U0 = Tm X2
-    for (int i = threadIdx.x; i < CH * 64; i += NT) {
-      const int r = i >> 6, c = i & 63;
-      sX0[r * LD + c] = r < cp.len ? p.A[(static_cast<size_t>(cp.bos + r) * p.HV + hv) * CH + c] : (r == c ? 1.f : 0.f);
-    }
+    load_tile<float>(sX0, p.A, p.HV, hv, cp.bos, cp.len);
+    __syncthreads();
+    for (int i = cp.len + threadIdx.x; i < CH; i += NT) sX0[i * LD + i] = 1.f;
     __syncthreads();
     float w[4][4], uu[4][4];
     zero(w);
@@ -265,74 +289,138 @@ __global__ void __launch_bounds__(NT) gdn_prep_kernel(GdnParams p) {
 }
 
 // ------------------------------------------------------------------------------------------------
+// Asynchronous global -> shared copies (16 bytes; src_bytes 0 zero-fills) for the chunk pipelines.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(pred ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool pred) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(pred ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+constexpr int LDW = 68;  // fp32 row of W tiles in the scans (16-byte aligned, rows 4 banks apart)
+
+// 64 rows x 64 values of a (tokens, heads, 64) tensor, row stride `rs` elements in shared memory.
+template <typename T>
+__device__ __forceinline__ void cp_rows64(T* dst, int rs, const T* base, int heads, int h, int t0, int len) {
+  constexpr int VEC = 16 / sizeof(T), PERROW = 64 / VEC, PER = CH * PERROW / NT;
+#pragma unroll
+  for (int m = 0; m < PER; ++m) {
+    const int idx = threadIdx.x + NT * m, r = idx / PERROW, c = (idx % PERROW) * VEC;
+    const int rr = r < len ? r : 0;
+    cp_async16(dst + r * rs + c, base + (static_cast<size_t>(t0 + rr) * heads + h) * 64 + c, r < len);
+  }
+}
+// 64 rows x VS values (columns v0..v0+VS) of a (tokens, heads, 64) tensor, dense VS-wide rows.
+template <typename T>
+__device__ __forceinline__ void cp_rows_slice(T* dst, const T* base, int heads, int h, int v0, int t0, int len) {
+  constexpr int VEC = 16 / sizeof(T), PERROW = VS / VEC;
+  for (int idx = threadIdx.x; idx < CH * PERROW; idx += NT) {
+    const int r = idx / PERROW, c = (idx % PERROW) * VEC;
+    const int rr = r < len ? r : 0;
+    cp_async16(dst + r * VS + c, base + (static_cast<size_t>(t0 + rr) * heads + h) * 64 + v0 + c, r < len);
+  }
+}
+__device__ __forceinline__ void cp_vec64(float* dst, const float* base, int heads, int h, int t0, int len) {
+  if (threadIdx.x < CH) {
+    const int r = threadIdx.x, rr = r < len ? r : 0;
+    cp_async4(dst + r, base + static_cast<size_t>(t0 + rr) * heads + h, r < len);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // state: sequential over the chunks of one sequence; CTA = (16-column slice of V, n*HV + hv).
-// Stores S0 of every chunk (hS) and u = U0 - W S0; final state to ht.
+// Stores S0 of every chunk (hS) and u = U0 - W S0; final state to ht.  The next chunk's W, k, U0
+// and gamma stream into the other half of a double buffer while this chunk computes.
 // ------------------------------------------------------------------------------------------------
 template <typename T>
+struct StateSmem {
+  float W[2][CH * LDW];
+  T k[2][CH * (64 + 16 / sizeof(T))];
+  float U0[2][CH * VS];
+  float gam[2][CH];
+  float S[DK * LDS_];
+  float Ut[CH * LDS_];
+};
+
+template <typename T>
 __global__ void __launch_bounds__(NT) gdn_state_kernel(GdnParams p) {
-  extern __shared__ float sm[];
-  float* sW = sm;                 // 64 x LD
-  float* sKt = sW + TILE;         // k e^{gamma_C - gamma}
-  float* sS = sKt + TILE;         // K x VS state slice
-  float* sU = sS + DK * LDS_;     // 64 x VS
-  float* sGam = sU + CH * LDS_;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  StateSmem<T>& sm = *reinterpret_cast<StateSmem<T>*>(smraw);
+  constexpr int KR = 64 + 16 / sizeof(T);
   const int v0 = blockIdx.x * VS;
   const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
   int bos, eos, c0, nc;
   seq_range(p, n, bos, eos, c0, nc);
-  const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;  // rows tr + 16r, column tc
+  const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;
+  const T* kb = static_cast<const T*>(p.k);
+  auto issue = [&](int j, int b) {
+    const int t0 = bos + j * CH, len = min(CH, eos - t0);
+    cp_rows64<float>(sm.W[b], LDW, p.W, p.HV, hv, t0, len);
+    cp_rows64<T>(sm.k[b], KR, kb, p.H, hq, t0, len);
+    cp_rows_slice<float>(sm.U0[b], p.U0, p.HV, hv, v0, t0, len);
+    cp_vec64(sm.gam[b], p.gam, p.HV, hv, t0, len);
+    cp_async_commit();
+  };
+  if (nc > 0) issue(0, 0);
   for (int i = threadIdx.x; i < DK * VS; i += NT) {
     const int kk = i / VS, c = i % VS;
-    sS[kk * LDS_ + c] = p.h0 ? p.h0[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] : 0.f;
+    sm.S[kk * LDS_ + c] = p.h0 ? p.h0[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] : 0.f;
   }
   for (int j = 0; j < nc; ++j) {
-    const int gc = c0 + j, t0 = bos + j * CH, len = min(CH, eos - t0);
-    __syncthreads();
-    load_vec(sGam, p.gam, p.HV, hv, t0, len);
-    for (int i = threadIdx.x; i < CH * 64; i += NT) {
-      const int r = i >> 6, c = i & 63;
-      const size_t row = static_cast<size_t>(t0 + r) * p.HV + hv;
-      sW[r * LD + c] = r < len ? p.W[row * DK + c] : 0.f;
+    const int b = j & 1, gc = c0 + j, t0 = bos + j * CH, len = min(CH, eos - t0);
+    if (j + 1 < nc) {
+      issue(j + 1, b ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
-    const float gC = sGam[len - 1];
-    for (int i = threadIdx.x; i < CH * 64; i += NT) {
-      const int r = i >> 6, c = i & 63;
-      sKt[r * LD + c] = r < len ? to_f32<T>(static_cast<const T*>(p.k)[(static_cast<size_t>(t0 + r) * p.H + hq) * DK + c]) *
-                                      __expf(gC - sGam[r])
-                                : 0.f;
-    }
-    // S0 of this chunk
+    const float gC = sm.gam[b][len - 1];
     float* hs = p.hS + (static_cast<size_t>(gc) * p.HV + hv) * DK * DV;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) hs[(tr + 16 * r) * DV + v0 + tc] = sS[(tr + 16 * r) * LDS_ + tc];
-    // u = U0 - W S0
+    for (int r = 0; r < 4; ++r) hs[(tr + 16 * r) * DV + v0 + tc] = sm.S[(tr + 16 * r) * LDS_ + tc];
+    // u = U0 - W S0 ; Ut = e^{gamma_C - gamma} u
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int kk = 0; kk < DK; ++kk) {
+      const float sv = sm.S[kk * LDS_ + tc];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] = fmaf(sm.W[b][(tr + 16 * r) * LDW + kk], sv, acc[r]);
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int i = tr + 16 * r;
-      float acc = 0.f;
-      for (int kk = 0; kk < DK; ++kk) acc = fmaf(sW[i * LD + kk], sS[kk * LDS_ + tc], acc);
-      const size_t row = static_cast<size_t>(t0 + i) * p.HV + hv;
-      const float uu = i < len ? p.U0[row * DV + v0 + tc] - acc : 0.f;
-      sU[i * LDS_ + tc] = uu;
-      if (i < len) p.u[row * DV + v0 + tc] = uu;
+      const float uu = i < len ? sm.U0[b][i * VS + tc] - acc[r] : 0.f;
+      if (i < len) p.u[(static_cast<size_t>(t0 + i) * p.HV + hv) * DV + v0 + tc] = uu;
+      sm.Ut[i * LDS_ + tc] = uu * __expf(gC - sm.gam[b][i]);
     }
     __syncthreads();
-    // S = e^{gamma_C} S + Kt^T u
+    // S = e^{gamma_C} S + k^T Ut
     const float eC = __expf(gC);
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int i = 0; i < CH; ++i) {
+      const float uv = sm.Ut[i * LDS_ + tc];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) sacc[r] = fmaf(to_f32<T>(sm.k[b][i * KR + tr + 16 * r]), uv, sacc[r]);
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int kk = tr + 16 * r;
-      float acc = 0.f;
-      for (int i = 0; i < CH; ++i) acc = fmaf(sKt[i * LD + kk], sU[i * LDS_ + tc], acc);
-      sS[kk * LDS_ + tc] = eC * sS[kk * LDS_ + tc] + acc;
+      sm.S[kk * LDS_ + tc] = eC * sm.S[kk * LDS_ + tc] + sacc[r];
     }
+    __syncthreads();
   }
-  __syncthreads();
   if (p.ht)
     for (int i = threadIdx.x; i < DK * VS; i += NT) {
       const int kk = i / VS, c = i % VS;
-      p.ht[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] = sS[kk * LDS_ + c];
+      p.ht[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] = sm.S[kk * LDS_ + c];
     }
 }
 
@@ -354,8 +442,7 @@ __global__ void __launch_bounds__(NT) gdn_out_kernel(GdnParams p) {
   load_tile<T>(sK, static_cast<const T*>(p.k), p.H, hq, cp.bos, cp.len);
   load_tile<float>(sU, p.u, p.HV, hv, cp.bos, cp.len);
   load_vec(sGam, p.gam, p.HV, hv, cp.bos, cp.len);
-  const float* hs = p.hS + (static_cast<size_t>(gc) * p.HV + hv) * DK * DV;
-  for (int i = threadIdx.x; i < DK * DV; i += NT) sS[(i >> 6) * LD + (i & 63)] = hs[i];
+  load_rows<float>(sS, p.hS + (static_cast<size_t>(gc) * p.HV + hv) * DK * DV, DV, DK);
   __syncthreads();
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   float acc[4][4], e[4][4];
@@ -431,80 +518,103 @@ __global__ void __launch_bounds__(NT) gdn_dvl_kernel(GdnParams p) {
 
 // ------------------------------------------------------------------------------------------------
 // backward 1: reverse scan of dS; CTA = (16-column slice of V, n*HV + hv).
-//   dS_end(c) stored to hD;  du = dvl + (k e^{gamma_C - gamma}) dS;
-//   dS <- e^{gamma_C} dS + scale (q e^gamma)^T dO - W^T du;  dh0 = dS after the first chunk.
+//   dS_end(c) stored to hD;  du = dvl + e^{gamma_C - gamma} (k dS);
+//   dS <- e^{gamma_C} dS + (scale e^gamma q)^T dO - W^T du;  dh0 = dS after the first chunk.
+// The previous chunk's W, k, q, dvl, dO and gamma are prefetched into a double buffer.
 // ------------------------------------------------------------------------------------------------
 template <typename T>
+struct DstateSmem {
+  float W[2][CH * LDW];
+  T k[2][CH * (64 + 16 / sizeof(T))];
+  T q[2][CH * (64 + 16 / sizeof(T))];
+  float dvl[2][CH * VS];
+  T dO[2][CH * VS];
+  float gam[2][CH];
+  float S[DK * LDS_];
+  float DU[CH * LDS_];
+  float f[CH];
+};
+
+template <typename T>
 __global__ void __launch_bounds__(NT) gdn_dstate_kernel(GdnParams p) {
-  extern __shared__ float sm[];
-  float* sW = sm;
-  float* sKt = sW + TILE;
-  float* sQt = sKt + TILE;
-  float* sS = sQt + TILE;        // dS slice, K x VS
-  float* sDU = sS + DK * LDS_;   // 64 x VS
-  float* sDO = sDU + CH * LDS_;  // 64 x VS
-  float* sGam = sDO + CH * LDS_;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  DstateSmem<T>& sm = *reinterpret_cast<DstateSmem<T>*>(smraw);
+  constexpr int KR = 64 + 16 / sizeof(T);
   const int v0 = blockIdx.x * VS;
   const int n = blockIdx.y / p.HV, hv = blockIdx.y % p.HV, hq = hv / (p.HV / p.H);
   int bos, eos, c0, nc;
   seq_range(p, n, bos, eos, c0, nc);
   const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;
+  const T* kb = static_cast<const T*>(p.k);
+  const T* qb = static_cast<const T*>(p.q);
+  const T* dob = static_cast<const T*>(p.dout);
+  auto issue = [&](int j, int b) {
+    const int t0 = bos + j * CH, len = min(CH, eos - t0);
+    cp_rows64<float>(sm.W[b], LDW, p.W, p.HV, hv, t0, len);
+    cp_rows64<T>(sm.k[b], KR, kb, p.H, hq, t0, len);
+    cp_rows64<T>(sm.q[b], KR, qb, p.H, hq, t0, len);
+    cp_rows_slice<float>(sm.dvl[b], p.dvl, p.HV, hv, v0, t0, len);
+    cp_rows_slice<T>(sm.dO[b], dob, p.HV, hv, v0, t0, len);
+    cp_vec64(sm.gam[b], p.gam, p.HV, hv, t0, len);
+    cp_async_commit();
+  };
+  if (nc > 0) issue(nc - 1, 0);
   for (int i = threadIdx.x; i < DK * VS; i += NT) {
     const int kk = i / VS, c = i % VS;
-    sS[kk * LDS_ + c] = p.dht ? p.dht[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] : 0.f;
+    sm.S[kk * LDS_ + c] = p.dht ? p.dht[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] : 0.f;
   }
-  const T* qb = static_cast<const T*>(p.q);
-  const T* kb = static_cast<const T*>(p.k);
-  const T* dob = static_cast<const T*>(p.dout);
-  for (int j = nc - 1; j >= 0; --j) {
-    const int gc = c0 + j, t0 = bos + j * CH, len = min(CH, eos - t0);
-    __syncthreads();
-    load_vec(sGam, p.gam, p.HV, hv, t0, len);
-    __syncthreads();
-    const float gC = sGam[len - 1];
-    for (int i = threadIdx.x; i < CH * 64; i += NT) {
-      const int r = i >> 6, c = i & 63;
-      const size_t rq = (static_cast<size_t>(t0 + r) * p.H + hq) * DK + c;
-      const size_t rv = static_cast<size_t>(t0 + r) * p.HV + hv;
-      const bool ok = r < len;
-      sW[r * LD + c] = ok ? p.W[rv * DK + c] : 0.f;
-      sKt[r * LD + c] = ok ? to_f32<T>(kb[rq]) * __expf(gC - sGam[r]) : 0.f;
-      sQt[r * LD + c] = ok ? to_f32<T>(qb[rq]) * __expf(sGam[r]) * p.scale : 0.f;
+  for (int it = 0; it < nc; ++it) {
+    const int j = nc - 1 - it, b = it & 1, gc = c0 + j, t0 = bos + j * CH, len = min(CH, eos - t0);
+    if (j > 0) {
+      issue(j - 1, b ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    for (int i = threadIdx.x; i < CH * VS; i += NT) {
-      const int r = i / VS, c = i % VS;
-      sDO[r * LDS_ + c] = r < len ? to_f32<T>(dob[(static_cast<size_t>(t0 + r) * p.HV + hv) * DV + v0 + c]) : 0.f;
-    }
+    __syncthreads();
+    const float gC = sm.gam[b][len - 1];
+    if (threadIdx.x < CH) sm.f[threadIdx.x] = threadIdx.x < len ? p.scale * __expf(sm.gam[b][threadIdx.x]) : 0.f;
     float* hd = p.hD + (static_cast<size_t>(gc) * p.HV + hv) * DK * DV;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) hd[(tr + 16 * r) * DV + v0 + tc] = sS[(tr + 16 * r) * LDS_ + tc];
-    __syncthreads();
+    for (int r = 0; r < 4; ++r) hd[(tr + 16 * r) * DV + v0 + tc] = sm.S[(tr + 16 * r) * LDS_ + tc];
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int kk = 0; kk < DK; ++kk) {
+      const float sv = sm.S[kk * LDS_ + tc];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] = fmaf(to_f32<T>(sm.k[b][(tr + 16 * r) * KR + kk]), sv, acc[r]);
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int i = tr + 16 * r;
-      float acc = 0.f;
-      for (int kk = 0; kk < DK; ++kk) acc = fmaf(sKt[i * LD + kk], sS[kk * LDS_ + tc], acc);
-      const size_t row = static_cast<size_t>(t0 + i) * p.HV + hv;
-      const float d = i < len ? p.dvl[row * DV + v0 + tc] + acc : 0.f;
-      sDU[i * LDS_ + tc] = d;
-      if (i < len) p.du[row * DV + v0 + tc] = d;
+      const float d = i < len ? sm.dvl[b][i * VS + tc] + __expf(gC - sm.gam[b][i]) * acc[r] : 0.f;
+      sm.DU[i * LDS_ + tc] = d;
+      if (i < len) p.du[(static_cast<size_t>(t0 + i) * p.HV + hv) * DV + v0 + tc] = d;
     }
     __syncthreads();
     const float eC = __expf(gC);
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int i = 0; i < CH; ++i) {
+      const float dov = sm.f[i] * to_f32<T>(sm.dO[b][i * VS + tc]);
+      const float duv = sm.DU[i * LDS_ + tc];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int kk = tr + 16 * r;
+        sacc[r] = fmaf(to_f32<T>(sm.q[b][i * KR + kk]), dov, fmaf(-sm.W[b][i * LDW + kk], duv, sacc[r]));
+      }
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int kk = tr + 16 * r;
-      float acc = 0.f;
-      for (int i = 0; i < CH; ++i)
-        acc = fmaf(sQt[i * LD + kk], sDO[i * LDS_ + tc], fmaf(-sW[i * LD + kk], sDU[i * LDS_ + tc], acc));
-      sS[kk * LDS_ + tc] = eC * sS[kk * LDS_ + tc] + acc;
+      sm.S[kk * LDS_ + tc] = eC * sm.S[kk * LDS_ + tc] + sacc[r];
     }
+    __syncthreads();
   }
-  __syncthreads();
   if (p.dh0)
     for (int i = threadIdx.x; i < DK * VS; i += NT) {
       const int kk = i / VS, c = i % VS;
-      p.dh0[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] = sS[kk * LDS_ + c];
+      p.dh0[((static_cast<size_t>(n) * p.HV + hv) * DK + kk) * DV + v0 + c] = sm.S[kk * LDS_ + c];
     }
 }
 
@@ -539,14 +649,9 @@ __global__ void __launch_bounds__(NT) gdn_grad_kernel(GdnParams p) {
   load_tile<float>(sDU, p.du, p.HV, hv, cp.bos, len);
   load_tile<T>(sDO, static_cast<const T*>(p.dout), p.HV, hv, cp.bos, len);
   const size_t st = (static_cast<size_t>(gc) * p.HV + hv) * DK * DV;
-  for (int i = threadIdx.x; i < DK * DV; i += NT) {
-    sS[(i >> 6) * LD + (i & 63)] = p.hS[st + i];
-    sD[(i >> 6) * LD + (i & 63)] = p.hD[st + i];
-  }
-  for (int i = threadIdx.x; i < CH * CH; i += NT) {
-    const int r = i >> 6, c = i & 63;
-    sT[r * LD + c] = r < len ? p.A[(static_cast<size_t>(cp.bos + r) * p.HV + hv) * CH + c] : (r == c ? 1.f : 0.f);
-  }
+  load_rows<float>(sS, p.hS + st, DV, DK);
+  load_rows<float>(sD, p.hD + st, DV, DK);
+  load_tile<float>(sT, p.A, p.HV, hv, cp.bos, len);
   load_vec(sGam, p.gam, p.HV, hv, cp.bos, len);
   load_vec(sB, p.beta, p.HV, hv, cp.bos, len);
   for (int i = threadIdx.x; i < CH; i += NT) {
@@ -555,9 +660,12 @@ __global__ void __launch_bounds__(NT) gdn_grad_kernel(GdnParams p) {
   }
   if (threadIdx.x == 0) sRed[0] = 0.f;
   __syncthreads();
-  if (len < CH)  // rows past the end hold gamma_last (their g is 0)
+  if (len < CH)  // rows past the end: gamma_last (their g is 0) and identity rows of Tm
     for (int i = threadIdx.x; i < CH; i += NT)
-      if (i >= len) sGam[i] = sGam[len - 1];
+      if (i >= len) {
+        sGam[i] = sGam[len - 1];
+        sT[i * LD + i] = 1.f;
+      }
   __syncthreads();
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   const float gC = sGam[CH - 1];
@@ -607,12 +715,8 @@ __global__ void __launch_bounds__(NT) gdn_grad_kernel(GdnParams p) {
   }
   __syncthreads();
   // (5) dL = -(Y_V U0^T + Y_K W^T) (j < i); load U0 -> sT, W -> X1
-  for (int i = threadIdx.x; i < CH * 64; i += NT) {
-    const int r = i >> 6, c = i & 63;
-    const size_t row = static_cast<size_t>(cp.bos + r) * p.HV + hv;
-    sT[r * LD + c] = r < len ? p.U0[row * DV + c] : 0.f;
-    X1[r * LD + c] = r < len ? p.W[row * DK + c] : 0.f;
-  }
+  load_tile<float>(sT, p.U0, p.HV, hv, cp.bos, len);
+  load_tile<float>(X1, p.W, p.HV, hv, cp.bos, len);
   __syncthreads();
   zero(t);
   mm<false, true>(t, X2, sT);
@@ -778,10 +882,10 @@ __global__ void __launch_bounds__(NT) gdn_grad_kernel(GdnParams p) {
 }
 
 constexpr size_t kSmemPrep = sizeof(float) * (5 * TILE + 3 * CH);
-constexpr size_t kSmemState = sizeof(float) * (2 * TILE + DK * LDS_ + CH * LDS_ + CH);
+
 constexpr size_t kSmemOut = sizeof(float) * (5 * TILE + CH);
 constexpr size_t kSmemDvl = sizeof(float) * (4 * TILE + CH);
-constexpr size_t kSmemDstate = sizeof(float) * (3 * TILE + DK * LDS_ + 2 * CH * LDS_ + CH);
+
 constexpr size_t kSmemGrad = sizeof(float) * (11 * TILE + 4 * CH + 4);
 
 template <typename K>
@@ -793,10 +897,12 @@ int launch(K kernel, dim3 grid, size_t smem, cudaStream_t st, const GdnParams& p
 }
 
 struct WsLayout {
-  size_t gam, W, U0, u, hS, dvl, du, hD, total;
+  size_t gam, W, U0, u, hS, dvl, du, hD, fwd_total, total;
 };
 
-WsLayout ws_layout(int B, int T, int HV, int NC, bool bwd) {
+// Forward part (gam, W, U0, u, hS) then, for the backward, its own part (dvl, du, hD).  With
+// `reuse` the forward part lives in the forward call's workspace and is not counted here.
+WsLayout ws_layout(int B, int T, int HV, int NC, bool bwd, bool reuse = false) {
   const size_t rows = static_cast<size_t>(B) * T * HV;
   const size_t st = static_cast<size_t>(NC) * HV * DK * DV;
   auto al = [](size_t x) { return (x + 63) & ~static_cast<size_t>(63); };  // 256-byte aligned (floats)
@@ -807,7 +913,9 @@ WsLayout ws_layout(int B, int T, int HV, int NC, bool bwd) {
   w.U0 = o; o += al(rows * DV);
   w.u = o; o += al(rows * DV);
   w.hS = o; o += al(st);
+  w.fwd_total = o * sizeof(float);
   if (bwd) {
+    if (reuse) o = 0;
     w.dvl = o; o += al(rows * DV);
     w.du = o; o += al(rows * DV);
     w.hD = o; o += al(st);
@@ -829,23 +937,26 @@ int check_dims(int dtype, int B, int T, int H, int HV, int K, int V, int N, int 
 template <typename T>
 int fwd_typed(GdnParams p, cudaStream_t st) {
   int e = launch(gdn_prep_kernel<T>, dim3(p.NC, p.HV), kSmemPrep, st, p);
-  if (!e) e = launch(gdn_state_kernel<T>, dim3(DV / VS, p.N * p.HV), kSmemState, st, p);
+  if (!e) e = launch(gdn_state_kernel<T>, dim3(DV / VS, p.N * p.HV), sizeof(StateSmem<T>), st, p);
   if (!e) e = launch(gdn_out_kernel<T>, dim3(p.NC, p.HV), kSmemOut, st, p);
   return e;
 }
 
 template <typename T>
-int bwd_typed(GdnParams p, cudaStream_t st) {
+int bwd_typed(GdnParams p, bool reuse, cudaStream_t st) {
   const size_t rows = static_cast<size_t>(p.B) * p.T;
   if (p.gva) {
     int e = from_cuda(cudaMemsetAsync(p.dq, 0, rows * p.H * DK * sizeof(float), st));
     if (!e) e = from_cuda(cudaMemsetAsync(p.dk, 0, rows * p.H * DK * sizeof(float), st));
     if (e) return e;
   }
-  int e = launch(gdn_prep_kernel<T>, dim3(p.NC, p.HV), kSmemPrep, st, p);
-  if (!e) e = launch(gdn_state_kernel<T>, dim3(DV / VS, p.N * p.HV), kSmemState, st, p);
+  int e = KATA_OK;
+  if (!reuse) {  // recompute gamma, W, U0 (from the saved Tm), then u and the chunk states
+    e = launch(gdn_prep_kernel<T>, dim3(p.NC, p.HV), kSmemPrep, st, p);
+    if (!e) e = launch(gdn_state_kernel<T>, dim3(DV / VS, p.N * p.HV), sizeof(StateSmem<T>), st, p);
+  }
   if (!e) e = launch(gdn_dvl_kernel<T>, dim3(p.NC, p.HV), kSmemDvl, st, p);
-  if (!e) e = launch(gdn_dstate_kernel<T>, dim3(DV / VS, p.N * p.HV), kSmemDstate, st, p);
+  if (!e) e = launch(gdn_dstate_kernel<T>, dim3(DV / VS, p.N * p.HV), sizeof(DstateSmem<T>), st, p);
   if (!e) e = launch(gdn_grad_kernel<T>, dim3(p.NC, p.HV), kSmemGrad, st, p);
   return e;
 }
@@ -857,25 +968,26 @@ int dispatch_fwd(int dtype, const GdnParams& p, cudaStream_t st) {
     default: return fwd_typed<__half>(p, st);
   }
 }
-int dispatch_bwd(int dtype, const GdnParams& p, cudaStream_t st) {
+int dispatch_bwd(int dtype, const GdnParams& p, bool reuse, cudaStream_t st) {
   switch (dtype) {
-    case KATA_DTYPE_F32: return bwd_typed<float>(p, st);
-    case KATA_DTYPE_BF16: return bwd_typed<__nv_bfloat16>(p, st);
-    default: return bwd_typed<__half>(p, st);
+    case KATA_DTYPE_F32: return bwd_typed<float>(p, reuse, st);
+    case KATA_DTYPE_BF16: return bwd_typed<__nv_bfloat16>(p, reuse, st);
+    default: return bwd_typed<__half>(p, reuse, st);
   }
 }
 
-void bind_ws(GdnParams& p, void* ws, const WsLayout& w, bool bwd) {
-  float* f = static_cast<float*>(ws);
+void bind_ws(GdnParams& p, void* ws, const WsLayout& w, bool bwd, void* fwd_ws = nullptr) {
+  float* f = static_cast<float*>(fwd_ws ? fwd_ws : ws);
   p.gam = f + w.gam;
   p.W = f + w.W;
   p.U0 = f + w.U0;
   p.u = f + w.u;
   p.hS = f + w.hS;
   if (bwd) {
-    p.dvl = f + w.dvl;
-    p.du = f + w.du;
-    p.hD = f + w.hD;
+    float* b = static_cast<float*>(ws);
+    p.dvl = b + w.dvl;
+    p.du = b + w.du;
+    p.hD = b + w.hD;
   }
 }
 
@@ -923,7 +1035,7 @@ extern "C" int kata_gdn_fwd(const kata_gdn_fwd_args* a, kata_stream_t stream) {
 
 extern "C" size_t kata_gdn_bwd_workspace_bytes(const kata_gdn_bwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->HV < 1 || a->num_chunks < 1) return 0;
-  return ws_layout(a->B, a->T, a->HV, a->num_chunks, true).total;
+  return ws_layout(a->B, a->T, a->HV, a->num_chunks, true, a->fwd_workspace != nullptr).total;
 }
 
 extern "C" int kata_gdn_bwd(const kata_gdn_bwd_args* a, kata_stream_t stream) {
@@ -934,7 +1046,8 @@ extern "C" int kata_gdn_bwd(const kata_gdn_bwd_args* a, kata_stream_t stream) {
   if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->A || !a->dout || !a->dq || !a->dk || !a->dv || !a->dg ||
       !a->dbeta)
     return KATA_ERR_INVALID;
-  const WsLayout w = ws_layout(a->B, a->T, a->HV, a->num_chunks, true);
+  const bool reuse = a->fwd_workspace != nullptr;
+  const WsLayout w = ws_layout(a->B, a->T, a->HV, a->num_chunks, true, reuse);
   if (!a->workspace || a->workspace_bytes < w.total) return KATA_ERR_WORKSPACE;
   GdnParams p{};
   p.q = a->q;
@@ -963,6 +1076,6 @@ extern "C" int kata_gdn_bwd(const kata_gdn_bwd_args* a, kata_stream_t stream) {
   p.scale = a->scale;
   p.a_given = 1;
   p.gva = a->HV != a->H;
-  bind_ws(p, a->workspace, w, true);
-  return dispatch_bwd(a->dtype, p, reinterpret_cast<cudaStream_t>(stream));
+  bind_ws(p, a->workspace, w, true, const_cast<void*>(a->fwd_workspace));
+  return dispatch_bwd(a->dtype, p, reuse, reinterpret_cast<cudaStream_t>(stream));
 }

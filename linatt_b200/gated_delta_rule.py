@@ -96,10 +96,10 @@ def _fwd(q, k, v, g, beta, scale, h0, want_final, tables):
         o = o[..., :V0]
     if ht is not None and (K0 != K or V0 != V):
         ht = ht[..., :K0, :V0].contiguous()
-    return o, A, ht
+    return o, A, ht, ws
 
 
-def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables):
+def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=None):
     dev = _lib.require_cuda(q, k, v, g, beta, A, h0, do, dht)
     K0, V0 = q.shape[-1], v.shape[-1]
     dt = _dtype(q, k, v)
@@ -122,8 +122,8 @@ def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables):
         q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), g=g.data_ptr(), beta=beta.data_ptr(), h0=_lib.ptr(h0),
         A=A.data_ptr(), dout=do.data_ptr(), dht=_lib.ptr(dht), dq=dq.data_ptr(), dk=dk.data_ptr(),
         dv=dv.data_ptr(), dg=dg.data_ptr(), dbeta=db.data_ptr(), dh0=_lib.ptr(dh0), cu_seqlens=_lib.ptr(cu),
-        chunk_offsets=_lib.ptr(co), workspace=None, workspace_bytes=0, dtype=_lib.DTYPE[dt], B=B, T=T, H=H,
-        HV=HV, K=K, V=V, N=N, num_chunks=NC, scale=float(scale))
+        chunk_offsets=_lib.ptr(co), workspace=None, workspace_bytes=0, fwd_workspace=_lib.ptr(fwd_ws),
+        dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HV=HV, K=K, V=V, N=N, num_chunks=NC, scale=float(scale))
     L = _lib.lib()
     ws = torch.empty(int(L.kata_gdn_bwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -154,10 +154,12 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
             h0 = initial_state.float()
             h0 = (h0.transpose(-1, -2) if transpose_state_layout else h0).contiguous()
         tables = _chunk_tables(cu_seqlens, cu_seqlens_cpu, B, T, q.device)
-        o, A, ht = _fwd(qc, kc, vc, gc, bc, scale, h0, output_final_state, tables)
+        o, A, ht, ws = _fwd(qc, kc, vc, gc, bc, scale, h0, output_final_state, tables)
         if ht is not None and transpose_state_layout:
             ht = ht.transpose(-1, -2).contiguous()
-        ctx.save_for_backward(qc, kc, vc, gc, bc, A, h0)
+        # Besides fla's saved set (q, k, v, g, beta, A, initial state) the forward's workspace (chunk
+        # states, u, W, U0, gamma) is kept, so the backward does not recompute the forward scan.
+        ctx.save_for_backward(qc, kc, vc, gc, bc, A, h0, ws)
         ctx.tables = tables
         ctx.scale = scale
         ctx.transpose_state_layout = transpose_state_layout
@@ -167,10 +169,10 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do, dht):
-        qc, kc, vc, gc, bc, A, h0 = ctx.saved_tensors
+        qc, kc, vc, gc, bc, A, h0, ws = ctx.saved_tensors
         if dht is not None and ctx.transpose_state_layout:
             dht = dht.transpose(-1, -2)
-        dq, dk, dv, dg, db, dh0 = _bwd(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables)
+        dq, dk, dv, dg, db, dh0 = _bwd(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables, fwd_ws=ws)
         tq, tk, tv, tg, tb, th = ctx.dtypes
         if dh0 is not None:
             dh0 = (dh0.transpose(-1, -2) if ctx.transpose_state_layout else dh0).to(th)

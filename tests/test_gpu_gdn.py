@@ -159,3 +159,19 @@ def test_gdn_bf16_config2_full_size():
     for n in GRADS:
         e = rel_l2(np64(got[n]), ref[n])
         assert e < 1e-2, f"{n}: rel-L2 {e:.3e}"
+
+
+def test_gdn_backward_recompute_path_matches_reuse():
+    """The C ABI's backward without the forward workspace (recomputing the chunk states from the
+    saved A) gives the same gradients as the autograd path, which passes the forward workspace."""
+    from linatt_b200 import gated_delta_rule as gdr
+
+    B, T, H, K, V = 2, 300, 2, 64, 64
+    q, k, v, g, beta, do, s0, dht = draw(12, B, T, H, H, K, V, h0=True)
+    qc, kc, vc, gc, bc, s0c, doc, dhtc = (x.cuda().contiguous() for x in (q, k, v, g, beta, s0, do, dht))
+    tables = gdr._chunk_tables(None, None, B, T, qc.device)
+    o, A, ht, ws = gdr._fwd(qc, kc, vc, gc, bc, K ** -0.5, s0c, True, tables)
+    a = gdr._bwd(qc, kc, vc, gc, bc, A, K ** -0.5, s0c, doc, dhtc, tables, fwd_ws=ws)
+    b = gdr._bwd(qc, kc, vc, gc, bc, A, K ** -0.5, s0c, doc, dhtc, tables, fwd_ws=None)
+    for x, y in zip(a, b):
+        assert rel_l2(np64(x), np64(y)) < 1e-6
