@@ -284,6 +284,29 @@ typedef struct {
 KATA_API size_t kata_gdn_bwd_workspace_bytes(const kata_gdn_bwd_args* args);
 KATA_API int kata_gdn_bwd(const kata_gdn_bwd_args* args, kata_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Sequence-parallel KATA-SPD (concat score) building blocks.  No counterpart in the reference (its
+ * "parallel" means parallel over T inside one GPU); they implement the cross-shard prefix of a
+ * sequence split contiguously across ranks.  With psi(x)[g,a,b] = scale * x_{g,a} x_{g,b}
+ * (F = M E^2 features), A[t,s] = psi(q_t).psi(k_s); earlier shards contribute psi(q_t)^T P with
+ * P = sum_s psi(k_s) [v_s | 1].  Feature tensors are head-major (B,H,T,F) bf16.
+ * ------------------------------------------------------------------------------------------- */
+/* R = psi(x) for x (B,T,H,D) of `dtype`; (D/M) % 8 == 0; R 16-byte aligned. */
+KATA_API int kata_sp_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
+                              kata_stream_t stream);
+/* dx (B,T,H,D) fp32 (+)= factor * sum_b G[g,b,a] x_{g,b}: the gradient of psi for a feature
+ * gradient G (B,H,T,F) bf16 that is symmetric in (a,b) (factor = 2 * scale). */
+KATA_API int kata_sp_contract(const void* G, const void* x, float* dx, int dtype, int B, int T, int H, int D, int M,
+                              float factor, int accumulate, kata_stream_t stream);
+/* o = (o_local * den_local' + X) / D',  D = den_local + y  (z' = z if z > 0 else 1), where
+ * XY (B,H,T,ldxy) fp32 holds X in columns [0,Dv) and y in column Dv; o_local, o (B,T,H,Dv) dtype,
+ * den_local, D (B,T,H) fp32. */
+KATA_API int kata_sp_combine(const void* o_local, const float* den_local, const float* XY, void* o, float* D_out,
+                             int dtype, int B, int T, int H, int Dv, int ldxy, kata_stream_t stream);
+/* W1 (B,H,T,ldw) bf16 = [dO/D' | -<dO,o>/D' | 0 ...] for o, dO (B,T,H,Dv) dtype and D (B,T,H). */
+KATA_API int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in, void* W1, int dtype, int B, int T,
+                              int H, int Dv, int ldw, kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

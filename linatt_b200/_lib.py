@@ -131,6 +131,14 @@ def lib() -> ctypes.CDLL:
                 w = getattr(L, f"kata_gdn_{nm}_workspace_bytes")
                 w.restype = c_size_t
                 w.argtypes = [ctypes.POINTER(st)]
+            L.kata_sp_features.restype = c_int
+            L.kata_sp_features.argtypes = [c_void_p, c_void_p] + [c_int] * 6 + [c_float, c_void_p]
+            L.kata_sp_contract.restype = c_int
+            L.kata_sp_contract.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 6 + [c_float, c_int, c_void_p]
+            L.kata_sp_combine.restype = c_int
+            L.kata_sp_combine.argtypes = [c_void_p] * 5 + [c_int] * 6 + [c_void_p]
+            L.kata_sp_bwd_prep.restype = c_int
+            L.kata_sp_bwd_prep.argtypes = [c_void_p] * 4 + [c_int] * 6 + [c_void_p]
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:

@@ -1,0 +1,204 @@
+// sp_state.cu -- per-token kernels of the sequence-parallel KATA-SPD path.
+//
+// With the concat score A[t,s] = sum_g (scale q_g[t].k_g[s])^2 and the quadratic feature map
+//   psi(x)[g,a,b] = scale * (x_{g,a} x_{g,b})           (F = M E^2 features, E = D/M)
+// A[t,s] = psi(q_t).psi(k_s), so the keys of earlier sequence shards enter a shard's queries only
+// through the state P = sum_s psi(k_s) [v_s | 1] (F x (Dv+1)).  These kernels expand features,
+// contract feature gradients back to q/k, and combine the shard-local attention with the prefix
+// term; the F-contractions themselves are plain GEMMs.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "attn_common.cuh"
+#include "host_util.h"
+#include "kata_b200.h"
+
+namespace kata {
+namespace {
+
+constexpr int NT = 256;
+constexpr int TOK = 8;  // tokens per CTA of the feature kernel
+
+// R (B,H,T,F) bf16, R[.., g E^2 + a E + b] = scale * (x_a * x_b)  (product first: exactly symmetric)
+template <typename T>
+__global__ void __launch_bounds__(NT) sp_features_kernel(const T* __restrict__ x, __nv_bfloat16* __restrict__ R,
+                                                         int B, int Tn, int H, int D, int M, float scale) {
+  extern __shared__ float xs[];  // TOK x D
+  const int E = D / M, F = M * E * E, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int t0 = blockIdx.x * TOK;
+  for (int i = threadIdx.x; i < TOK * D; i += NT) {
+    const int j = i / D, d = i % D, t = t0 + j;
+    xs[i] = t < Tn ? to_f32<T>(x[((static_cast<size_t>(b) * Tn + t) * H + h) * D + d]) : 0.f;
+  }
+  __syncthreads();
+  const int chunks = F / 8;
+  for (int c = threadIdx.x; c < TOK * chunks; c += NT) {
+    const int j = c / chunks, f0 = (c % chunks) * 8, t = t0 + j;
+    if (t >= Tn) continue;
+    const int g = f0 / (E * E), a = (f0 % (E * E)) / E, b0 = f0 % E;
+    const float* xr = xs + j * D + g * E;
+    const float xa = xr[a];
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float p0 = scale * (xa * xr[b0 + 2 * i]);
+      const float p1 = scale * (xa * xr[b0 + 2 * i + 1]);
+      const __nv_bfloat162 v = __floats2bfloat162_rn(p0, p1);
+      w[i] = *reinterpret_cast<const uint32_t*>(&v);
+    }
+    *reinterpret_cast<uint4*>(R + (static_cast<size_t>(bh) * Tn + t) * F + f0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// dx_{g,a} (+)= factor * sum_b G[g,b,a] x_{g,b}, G = dR of one (token, head), symmetric in (a,b).
+// One warp per (token, head): lanes walk a, the warp walks b (coalesced rows of G).
+template <typename T>
+__global__ void __launch_bounds__(NT) sp_contract_kernel(const __nv_bfloat16* __restrict__ G, const T* __restrict__ x,
+                                                         float* __restrict__ dx, int B, int Tn, int H, int D, int M,
+                                                         float factor, int accumulate) {
+  const int warp = (blockIdx.x * NT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long total = static_cast<long>(B) * H * Tn;
+  if (warp >= total) return;
+  const int bh = warp / Tn, t = warp % Tn, b = bh / H, h = bh % H;
+  const int E = D / M, F = M * E * E;
+  const size_t xo = ((static_cast<size_t>(b) * Tn + t) * H + h) * D;
+  const __nv_bfloat16* g = G + (static_cast<size_t>(bh) * Tn + t) * F;
+  for (int gi = 0; gi < M; ++gi) {
+    for (int a0 = 0; a0 < E; a0 += 32) {
+      const int a = a0 + lane;
+      float acc = 0.f;
+      for (int bb = 0; bb < E; ++bb) {
+        const float xb = to_f32<T>(x[xo + gi * E + bb]);
+        if (a < E) acc = fmaf(__bfloat162float(g[gi * E * E + bb * E + a]), xb, acc);
+      }
+      if (a < E) {
+        float* o = dx + xo + gi * E + a;
+        *o = accumulate ? *o + factor * acc : factor * acc;
+      }
+    }
+  }
+}
+
+// o = (o_loc * den_loc' + X) / D',  D = den_loc + y   (x' = x if x > 0 else 1);  XY (B*H, T, ldxy)
+template <typename T>
+__global__ void __launch_bounds__(NT) sp_combine_kernel(const T* __restrict__ oloc, const float* __restrict__ den,
+                                                        const float* __restrict__ XY, T* __restrict__ o,
+                                                        float* __restrict__ Dout, int B, int Tn, int H, int Dv,
+                                                        int ldxy) {
+  const int warp = (blockIdx.x * NT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long total = static_cast<long>(B) * Tn * H;
+  if (warp >= total) return;
+  const int h = warp % H, t = (warp / H) % Tn, b = warp / (H * Tn);
+  const size_t row = (static_cast<size_t>(b) * Tn + t) * H + h;
+  const float* xy = XY + ((static_cast<size_t>(b) * H + h) * Tn + t) * ldxy;
+  const float dl = den[row];
+  const float Dt = dl + xy[Dv];
+  const float nl = dl > 0.f ? dl : 1.f;
+  const float inv = 1.f / (Dt > 0.f ? Dt : 1.f);
+  for (int c = lane; c < Dv; c += 32) o[row * Dv + c] = from_f32<T>((to_f32<T>(oloc[row * Dv + c]) * nl + xy[c]) * inv);
+  if (lane == 0) Dout[row] = Dt;
+}
+
+// W1 (B*H, T, ldw) bf16 = [dO / D' | -delta / D' | 0...],  delta = <dO, o>
+template <typename T>
+__global__ void __launch_bounds__(NT) sp_bwd_prep_kernel(const T* __restrict__ o, const T* __restrict__ dout,
+                                                         const float* __restrict__ Dn, __nv_bfloat16* __restrict__ W1,
+                                                         int B, int Tn, int H, int Dv, int ldw) {
+  const int warp = (blockIdx.x * NT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long total = static_cast<long>(B) * Tn * H;
+  if (warp >= total) return;
+  const int h = warp % H, t = (warp / H) % Tn, b = warp / (H * Tn);
+  const size_t row = (static_cast<size_t>(b) * Tn + t) * H + h;
+  __nv_bfloat16* w = W1 + ((static_cast<size_t>(b) * H + h) * Tn + t) * ldw;
+  const float Dt = Dn[row];
+  const float inv = 1.f / (Dt > 0.f ? Dt : 1.f);
+  float delta = 0.f;
+  for (int c = lane; c < Dv; c += 32) {
+    const float g = to_f32<T>(dout[row * Dv + c]);
+    delta = fmaf(g, to_f32<T>(o[row * Dv + c]), delta);
+    w[c] = __float2bfloat16_rn(g * inv);
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) delta += __shfl_xor_sync(0xffffffffu, delta, off);
+  for (int c = Dv + lane; c < ldw; c += 32) w[c] = __float2bfloat16_rn(c == Dv ? -delta * inv : 0.f);
+}
+
+int check(int dtype, int B, int T, int H, int D, int M) {
+  if (dtype != KATA_DTYPE_F32 && dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (B < 1 || T < 1 || H < 1 || D < 1 || M < 1 || D % M) return KATA_ERR_SHAPE;
+  if ((D / M) % 8) return KATA_ERR_UNSUPPORTED;
+  return KATA_OK;
+}
+
+unsigned warp_blocks(long warps) { return static_cast<unsigned>((warps * 32 + NT - 1) / NT); }
+
+}  // namespace
+}  // namespace kata
+
+using namespace kata;
+
+extern "C" int kata_sp_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
+                                kata_stream_t stream) {
+  int e = check(dtype, B, T, H, D, M);
+  if (e) return e;
+  if (!x || !R) return KATA_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(R) % 16) return KATA_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid((T + TOK - 1) / TOK, B * H);
+  const size_t smem = sizeof(float) * TOK * D;
+  auto* r = static_cast<__nv_bfloat16*>(R);
+  switch (dtype) {
+    case KATA_DTYPE_F32: sp_features_kernel<float><<<grid, NT, smem, st>>>(static_cast<const float*>(x), r, B, T, H, D, M, scale); break;
+    case KATA_DTYPE_BF16: sp_features_kernel<__nv_bfloat16><<<grid, NT, smem, st>>>(static_cast<const __nv_bfloat16*>(x), r, B, T, H, D, M, scale); break;
+    default: sp_features_kernel<__half><<<grid, NT, smem, st>>>(static_cast<const __half*>(x), r, B, T, H, D, M, scale); break;
+  }
+  return from_cuda(cudaGetLastError());
+}
+
+extern "C" int kata_sp_contract(const void* G, const void* x, float* dx, int dtype, int B, int T, int H, int D, int M,
+                                float factor, int accumulate, kata_stream_t stream) {
+  int e = check(dtype, B, T, H, D, M);
+  if (e) return e;
+  if (!G || !x || !dx) return KATA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = warp_blocks(static_cast<long>(B) * H * T);
+  const auto* g = static_cast<const __nv_bfloat16*>(G);
+  switch (dtype) {
+    case KATA_DTYPE_F32: sp_contract_kernel<float><<<blocks, NT, 0, st>>>(g, static_cast<const float*>(x), dx, B, T, H, D, M, factor, accumulate); break;
+    case KATA_DTYPE_BF16: sp_contract_kernel<__nv_bfloat16><<<blocks, NT, 0, st>>>(g, static_cast<const __nv_bfloat16*>(x), dx, B, T, H, D, M, factor, accumulate); break;
+    default: sp_contract_kernel<__half><<<blocks, NT, 0, st>>>(g, static_cast<const __half*>(x), dx, B, T, H, D, M, factor, accumulate); break;
+  }
+  return from_cuda(cudaGetLastError());
+}
+
+extern "C" int kata_sp_combine(const void* o_local, const float* den_local, const float* XY, void* o, float* D_out,
+                               int dtype, int B, int T, int H, int Dv, int ldxy, kata_stream_t stream) {
+  if (dtype != KATA_DTYPE_F32 && dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (B < 1 || T < 1 || H < 1 || Dv < 1 || ldxy < Dv + 1) return KATA_ERR_SHAPE;
+  if (!o_local || !den_local || !XY || !o || !D_out) return KATA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = warp_blocks(static_cast<long>(B) * H * T);
+  switch (dtype) {
+    case KATA_DTYPE_F32: sp_combine_kernel<float><<<blocks, NT, 0, st>>>(static_cast<const float*>(o_local), den_local, XY, static_cast<float*>(o), D_out, B, T, H, Dv, ldxy); break;
+    case KATA_DTYPE_BF16: sp_combine_kernel<__nv_bfloat16><<<blocks, NT, 0, st>>>(static_cast<const __nv_bfloat16*>(o_local), den_local, XY, static_cast<__nv_bfloat16*>(o), D_out, B, T, H, Dv, ldxy); break;
+    default: sp_combine_kernel<__half><<<blocks, NT, 0, st>>>(static_cast<const __half*>(o_local), den_local, XY, static_cast<__half*>(o), D_out, B, T, H, Dv, ldxy); break;
+  }
+  return from_cuda(cudaGetLastError());
+}
+
+extern "C" int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in, void* W1, int dtype, int B, int T,
+                                int H, int Dv, int ldw, kata_stream_t stream) {
+  if (dtype != KATA_DTYPE_F32 && dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (B < 1 || T < 1 || H < 1 || Dv < 1 || ldw < Dv + 1) return KATA_ERR_SHAPE;
+  if (!o || !dout || !D_in || !W1) return KATA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = warp_blocks(static_cast<long>(B) * H * T);
+  auto* w = static_cast<__nv_bfloat16*>(W1);
+  switch (dtype) {
+    case KATA_DTYPE_F32: sp_bwd_prep_kernel<float><<<blocks, NT, 0, st>>>(static_cast<const float*>(o), static_cast<const float*>(dout), D_in, w, B, T, H, Dv, ldw); break;
+    case KATA_DTYPE_BF16: sp_bwd_prep_kernel<__nv_bfloat16><<<blocks, NT, 0, st>>>(static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), D_in, w, B, T, H, Dv, ldw); break;
+    default: sp_bwd_prep_kernel<__half><<<blocks, NT, 0, st>>>(static_cast<const __half*>(o), static_cast<const __half*>(dout), D_in, w, B, T, H, Dv, ldw); break;
+  }
+  return from_cuda(cudaGetLastError());
+}

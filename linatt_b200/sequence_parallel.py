@@ -1,0 +1,234 @@
+"""Sequence-parallel causal KATA-SPD attention (concat score) over a contiguous split of T.
+
+No counterpart exists in the reference: ``kata/parallel_kata_attn.py`` is "parallel" over T within
+one GPU (its docstring, :1-22).  This module is the long-context multi-GPU path: rank r of a
+process group holds tokens [r*T/R, (r+1)*T/R) of every head and computes
+
+    o_t = (n_t + psi(q_t)^T P) / D_t',   D_t = d_t + psi(q_t)^T z,   x' = x if x > 0 else 1
+
+where n_t / d_t are the shard-local causal numerator / denominator (the flash kernels of
+``linatt_b200.parallel_kata_attn``), psi(x)[g,a,b] = scale * x_{g,a} x_{g,b} is the quadratic feature
+map with A[t,s] = psi(q_t).psi(k_s), and [P | z] = sum over earlier shards of psi(k_s) [v_s | 1]
+(an F x (Dv+1) state per head, F = M E^2).  The only exchange is that state: an exclusive prefix
+over ranks in the forward and an exclusive suffix of its gradient in the backward, each an NCCL
+all-gather issued before the shard-local attention kernel so that it overlaps it.
+
+The shard-local backward is the single-GPU kernel run with the final o and D: its
+dA = (dO.v - <dO,o>) / D is then exactly the local block of the full gradient.  Feature expansion,
+its gradient contraction and the combine step are kernels of ``libkata_b200.so``; the F-wide
+contractions are bf16 GEMMs with fp32 output (cuBLAS through torch.bmm).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from . import parallel_kata_attn as pka
+
+__all__ = ["sp_kata_attn", "SPKataAttnFunction", "exclusive_prefix_sum", "exclusive_suffix_sum",
+           "gather_states", "sp_forward_local", "sp_forward_combine", "sp_backward_prep", "sp_backward",
+           "sp_backward_local", "sp_backward_cross"]
+
+
+# ------------------------------------------------------------------------------------------------
+# exchange (host logic; any backend)
+# ------------------------------------------------------------------------------------------------
+class _Gathered:
+    def __init__(self, bufs, work, world):
+        self.bufs, self.work, self.world = bufs, work, world
+
+    def wait(self) -> torch.Tensor:
+        if self.work is not None:
+            self.work.wait()
+        return self.bufs if isinstance(self.bufs, torch.Tensor) else torch.stack(self.bufs)
+
+
+def gather_states(x: torch.Tensor, group=None, async_op: bool = False) -> _Gathered:
+    """All ranks' ``x`` stacked along a new leading dim (rank order); ``.wait()`` returns it."""
+    world = dist.get_world_size(group)
+    x = x.contiguous()
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        work = dist.all_gather_into_tensor(out, x, group=group, async_op=async_op)
+        return _Gathered(out, work, world)
+    outs = [torch.empty_like(x) for _ in range(world)]
+    work = dist.all_gather(outs, x, group=group, async_op=async_op)
+    return _Gathered(outs, work, world)
+
+
+def exclusive_prefix_sum(stacked: torch.Tensor, rank: int) -> torch.Tensor | None:
+    """sum_{r < rank} stacked[r]  (None for rank 0)."""
+    return stacked[:rank].sum(0) if rank > 0 else None
+
+
+def exclusive_suffix_sum(stacked: torch.Tensor, rank: int) -> torch.Tensor | None:
+    """sum_{r > rank} stacked[r]  (None for the last rank)."""
+    return stacked[rank + 1:].sum(0) if rank + 1 < stacked.shape[0] else None
+
+
+# ------------------------------------------------------------------------------------------------
+# shard-local pieces (GPU)
+# ------------------------------------------------------------------------------------------------
+def _ldw(Dv: int) -> int:
+    return (Dv + 1 + 7) // 8 * 8  # [v | 1 | zero pad] width, a multiple of 8 for the GEMMs
+
+
+def _features(x, M, scale):
+    B, T, H, D = x.shape
+    E = D // M
+    R = torch.empty(B * H, T, M * E * E, device=x.device, dtype=torch.bfloat16)
+    _lib.check(_lib.lib().kata_sp_features(x.data_ptr(), R.data_ptr(), _lib.DTYPE[x.dtype], B, T, H, D, M,
+                                           float(scale), _lib.stream_handle(x.device)), "kata_sp_features")
+    return R
+
+
+def _contract(G, x, dx, M, scale):
+    B, T, H, D = x.shape
+    _lib.check(_lib.lib().kata_sp_contract(G.data_ptr(), x.data_ptr(), dx.data_ptr(), _lib.DTYPE[x.dtype], B, T, H,
+                                           D, M, 2.0 * float(scale), 1, _lib.stream_handle(x.device)),
+               "kata_sp_contract")
+
+
+def _v1(v, ldw):
+    B, T, H, Dv = v.shape
+    out = torch.zeros(B, H, T, ldw, device=v.device, dtype=torch.bfloat16)
+    out[..., :Dv] = v.permute(0, 2, 1, 3)
+    out[..., Dv] = 1.0
+    return out.view(B * H, T, ldw)
+
+
+def _scale(D, M, scale):
+    return 1.0 / math.sqrt(D // M) if scale is None else float(scale)
+
+
+def sp_forward_local(q, k, v, num_groups, scale, want_state=True):
+    """Shard-local causal attention and this shard's state contribution.
+    Returns (o_local, den_local, S) with S = psi(K)^T [V | 1] (B*H, F, ldw) fp32 (None if not wanted)."""
+    scale = _scale(q.shape[-1], num_groups, scale)
+    S = None
+    if want_state:
+        Rk = _features(k, num_groups, scale)
+        S = torch.bmm(Rk.transpose(1, 2), _v1(v, _ldw(v.shape[-1])), out_dtype=torch.float32)
+        del Rk
+    o_loc, den = pka._fwd(q, k, v, num_groups, scale, "concat")
+    return o_loc, den, S
+
+
+def sp_forward_combine(q, o_loc, den_loc, P, num_groups, scale):
+    """Final (o, D) of a shard from its local result and the prefix state P (None: first shard)."""
+    if P is None:
+        return o_loc, den_loc
+    scale = _scale(q.shape[-1], num_groups, scale)
+    B, T, H, Dv = o_loc.shape
+    XY = torch.bmm(_features(q, num_groups, scale), P.to(torch.bfloat16), out_dtype=torch.float32)
+    o = torch.empty_like(o_loc)
+    D = torch.empty_like(den_loc)
+    _lib.check(_lib.lib().kata_sp_combine(o_loc.data_ptr(), den_loc.data_ptr(), XY.data_ptr(), o.data_ptr(),
+                                          D.data_ptr(), _lib.DTYPE[o_loc.dtype], B, T, H, Dv, XY.shape[-1],
+                                          _lib.stream_handle(q.device)), "kata_sp_combine")
+    return o, D
+
+
+def sp_backward_prep(q, o, D, do, num_groups, scale, want_dP=True):
+    """W1 = [dO/D' | -<dO,o>/D' | 0] and this shard's gradient of its prefix state, dP = psi(Q)^T W1."""
+    B, T, H, Dv = o.shape
+    ldw = _ldw(Dv)
+    W1 = torch.empty(B * H, T, ldw, device=o.device, dtype=torch.bfloat16)
+    _lib.check(_lib.lib().kata_sp_bwd_prep(o.data_ptr(), do.data_ptr(), D.data_ptr(), W1.data_ptr(),
+                                           _lib.DTYPE[o.dtype], B, T, H, Dv, ldw, _lib.stream_handle(o.device)),
+               "kata_sp_bwd_prep")
+    dP = None
+    if want_dP:
+        scale = _scale(q.shape[-1], num_groups, scale)
+        dP = torch.bmm(_features(q, num_groups, scale).transpose(1, 2), W1, out_dtype=torch.float32)
+    return W1, dP
+
+
+def sp_backward_cross(q, k, v, W1, P, dS, dq, dk, dv, num_groups, scale):
+    """Adds to the fp32 dq, dk, dv of a shard the prefix term (through P, the bf16 prefix state)
+    and the state term (through dS = the sum of later shards' dP)."""
+    scale = _scale(q.shape[-1], num_groups, scale)
+    B, T, H, Dv = v.shape
+    if P is not None:
+        dRq = torch.bmm(W1, P.to(torch.bfloat16).transpose(1, 2))  # (B*H, T, F) bf16
+        _contract(dRq, q, dq, num_groups, scale)
+        del dRq
+    if dS is not None:
+        dSb = dS.to(torch.bfloat16)
+        Rk = _features(k, num_groups, scale)
+        dvs = torch.bmm(Rk, dSb, out_dtype=torch.float32)[..., :Dv]
+        dv += dvs.reshape(B, H, T, Dv).permute(0, 2, 1, 3)
+        del Rk, dvs
+        dRk = torch.bmm(_v1(v, W1.shape[-1]), dSb.transpose(1, 2))  # (B*H, T, F) bf16
+        _contract(dRk, k, dk, num_groups, scale)
+
+
+def sp_backward_local(q, k, v, o, D, do, num_groups, scale):
+    """The shard-local block of the gradient: the flash backward run with the final o and D."""
+    dq, dk, dv, _ = pka._bwd(q, k, v, o, D, do, num_groups, _scale(q.shape[-1], num_groups, scale), "concat")
+    return dq.float(), dk.float(), dv.float()
+
+
+def sp_backward(q, k, v, o, D, do, W1, P, dS, num_groups, scale):
+    """dq, dk, dv (fp32) of a shard: local block + prefix term + state term."""
+    dq, dk, dv = sp_backward_local(q, k, v, o, D, do, num_groups, scale)
+    sp_backward_cross(q, k, v, W1, P, dS, dq, dk, dv, num_groups, scale)
+    return dq, dk, dv
+
+
+# ------------------------------------------------------------------------------------------------
+# autograd op
+# ------------------------------------------------------------------------------------------------
+class SPKataAttnFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, num_groups, scale, group):
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        q, k, v = (x.contiguous() for x in (q, k, v))
+        scale = _scale(q.shape[-1], num_groups, scale)
+        B, T, H, Dv = v.shape
+        F = num_groups * (q.shape[-1] // num_groups) ** 2
+        last = rank == world - 1
+        # state first, so that its all-gather overlaps the shard-local attention kernel
+        if not last:
+            Rk = _features(k, num_groups, scale)
+            S = torch.bmm(Rk.transpose(1, 2), _v1(v, _ldw(Dv)), out_dtype=torch.float32)
+            del Rk
+        else:  # the last shard's state feeds nobody
+            S = torch.zeros(B * H, F, _ldw(Dv), device=q.device, dtype=torch.float32)
+        pending = gather_states(S, group, async_op=True)
+        o_loc, den_loc = pka._fwd(q, k, v, num_groups, scale, "concat")
+        P = exclusive_prefix_sum(pending.wait(), rank)
+        o, D = sp_forward_combine(q, o_loc, den_loc, P, num_groups, scale)
+        Pb = P.to(torch.bfloat16) if P is not None else None
+        ctx.save_for_backward(q, k, v, o, D, Pb)
+        ctx.num_groups, ctx.scale, ctx.group, ctx.rank, ctx.world = num_groups, scale, group, rank, world
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, D, Pb = ctx.saved_tensors
+        do = do.to(o.dtype).contiguous()
+        W1, dP = sp_backward_prep(q, o, D, do, ctx.num_groups, ctx.scale, want_dP=ctx.rank > 0)
+        if dP is None:  # the first shard's prefix gradient feeds nobody
+            F = ctx.num_groups * (q.shape[-1] // ctx.num_groups) ** 2
+            dP = torch.zeros(W1.shape[0], F, W1.shape[-1], device=q.device, dtype=torch.float32)
+        pending = gather_states(dP, ctx.group, async_op=True)
+        dq, dk, dv = sp_backward_local(q, k, v, o, D, do, ctx.num_groups, ctx.scale)
+        dS = exclusive_suffix_sum(pending.wait(), ctx.rank)
+        sp_backward_cross(q, k, v, W1, Pb, dS, dq, dk, dv, ctx.num_groups, ctx.scale)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
+
+
+def sp_kata_attn(q, k, v, num_groups=4, scale=None, group=None):
+    """Causal concat-score KATA-SPD attention of a sequence split contiguously over the ranks of
+    ``group`` (rank order = sequence order).  q, k, v: this rank's (B, T/R, H, D) shard, time-major;
+    returns this rank's shard of o.  With one rank it is ``parallel_kata_attn``."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return pka.parallel_kata_attn(q, k, v, num_groups=num_groups, scale=scale)
+    if q.shape[2] != k.shape[2]:
+        raise NotImplementedError("sequence-parallel path: q and k must have the same number of heads")
+    return SPKataAttnFunction.apply(q, k, v, num_groups, scale, group)
