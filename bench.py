@@ -383,6 +383,164 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------
+# auxiliary workloads (not the headline line): config 4 sequence parallel, config 2 gated delta
+# ------------------------------------------------------------------------------------------------
+def _timed_steps(torch, dist, world, dev, step, K, W):
+    """W untimed steps, then K steps between barriers; returns the max over ranks of the ms."""
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        for i in range(K):
+            step(W + i)
+        e.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = s.elapsed_time(e)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, clk.summary()
+
+
+def run_sp(args, rank: int, world: int, local: int) -> None:
+    """Config 4: B=1, T=131072, H=16, D=Dv=128, M=4 concat, bf16, T split contiguously over the
+    ranks (strong scaling); one step = forward + backward through sp_kata_attn."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    from linatt_b200.sequence_parallel import sp_kata_attn
+
+    Bs, Ts, Hs, Ds, Ms = 1, 131072, 16, 128, 4
+    Tl = Ts // world
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    sets = []
+    for _ in range(2):
+        qkv = [(torch.randn(Bs, Tl, Hs, Ds, device=dev, generator=g) / math.sqrt(Ds)).bfloat16() for _ in range(3)]
+        sets.append(qkv + [torch.randn(Bs, Tl, Hs, Ds, device=dev, generator=g).bfloat16()])
+
+    def step(i):
+        q, k, v, do = sets[i % 2]
+        leaves = [x.requires_grad_(True) for x in (q, k, v)]
+        o = sp_kata_attn(*leaves, num_groups=Ms)
+        o.backward(do)
+        for x in leaves:
+            x.grad = None
+
+    ms, clk = _timed_steps(torch, dist, world, dev, step, args.steps, args.warmup)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, src = load_peaks()
+    step_ms = ms / args.steps
+    flops = 7 * Hs * 2.0 * pairs(Ts) * Ds  # 7 GEMM-equivalents of the whole causal problem
+    ach = flops / (step_ms / 1e3) / 1e12
+    line = {
+        "metric": "KATA-SPD sequence-parallel fwd+bwd tokens/s at B1·T131072·H16·D128 (config 4)",
+        "value": Bs * Ts / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "sequence-parallel KATA-SPD fwd+bwd, concat M=4, causal, bf16 (config 4)",
+                   "global_batch": Bs, "seq_len": Ts, "heads": Hs, "head_dim": Ds, "num_groups": Ms,
+                   "parallelism": f"contiguous T split x{world}, prefix state all-gather over NCCL",
+                   "l2": "2 rotating input sets per rank plus GB-sized intermediates per step"},
+        "roofline": {"bound": "tensor", "achieved": ach / world, "peak": peak, "unit": "TFLOP/s",
+                     "frac": ach / world / peak, "traffic": None, "peak_source": src,
+                     "note": "full-problem causal FLOPs (246 TFLOP) / step time / GPUs"},
+        "clocks": clk, "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gdn(args, rank: int, world: int, local: int) -> None:
+    """Config 2: chunked gated delta rule fwd+bwd, B=8, T=2048, H=12, K=V=64, bf16 inputs with
+    fp32 state, per GPU (weak scaling over B); one step through chunk_gated_delta_rule + backward."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from linatt_b200.gated_delta_rule import chunk_gated_delta_rule
+
+    Bg, Tg, Hg, Kg = 8, 2048, 12, 64
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    sets = []
+    for _ in range(4):
+        q = torch.randn(Bg, Tg, Hg, Kg, device=dev, generator=g).bfloat16()
+        k = F.normalize(torch.randn(Bg, Tg, Hg, Kg, device=dev, generator=g), dim=-1).bfloat16()
+        v = torch.randn(Bg, Tg, Hg, Kg, device=dev, generator=g).bfloat16()
+        beta = torch.sigmoid(torch.randn(Bg, Tg, Hg, device=dev, generator=g))
+        gate = -F.softplus(torch.randn(Bg, Tg, Hg, device=dev, generator=g))
+        do = torch.randn(Bg, Tg, Hg, Kg, device=dev, generator=g).bfloat16()
+        sets.append((q, k, v, gate, beta, do))
+
+    def step(i):
+        q, k, v, gate, beta, do = sets[i % 4]
+        leaves = [x.requires_grad_(True) for x in (q, k, v, gate, beta)]
+        o, _ = chunk_gated_delta_rule(*leaves)
+        o.backward(do)
+        for x in leaves:
+            x.grad = None
+
+    ms, clk = _timed_steps(torch, dist, world, dev, step, args.steps, args.warmup)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak_hbm = 6651.7
+    p = ROOT / "MEASURED_PEAKS.json"
+    src = "fallback"
+    if p.exists():
+        try:
+            peak_hbm, src = float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    step_ms = ms / args.steps
+    n = Bg * Tg * Hg
+    # algorithmic bytes: read q,k,v (bf16) + g,beta (fp32) twice (fwd, bwd), dO once; write o, dq, dk, dv
+    # (bf16) and dg, dbeta (fp32)
+    alg_bytes = 2 * n * (3 * Kg * 2 + 8) + n * Kg * 2 + 4 * n * Kg * 2 + 2 * n * 4
+    ach = alg_bytes / (step_ms / 1e3) / 1e9
+    line = {
+        "metric": "gated delta rule fwd+bwd tokens/s/GPU at B8·T2048·H12·K=V=64 (config 2)",
+        "value": world * Bg * Tg / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "chunk_gated_delta_rule fwd+bwd (config 2)", "batch_per_gpu": Bg, "seq_len": Tg,
+                   "heads": Hg, "head_dim": Kg, "parallelism": f"batch shard x{world}, no collective",
+                   "l2": "4 rotating input sets of 151 MB (q, k, v, dO bf16; g, beta fp32)"},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak_hbm, "unit": "GB/s", "frac": ach / peak_hbm,
+                     "traffic": None, "peak_source": src,
+                     "algorithmic_bytes_per_step": alg_bytes,
+                     "tflops_per_gpu": 39.5e9 / (step_ms / 1e3) / 1e12},
+        "clocks": clk, "gpu_launches": 8 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -394,6 +552,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--num-groups", type=int, default=4, help="M (the benchmark metric is quoted at M=4)")
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn"], default="attn",
+                    help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2")
     ap.add_argument("--batch", type=int, default=16,
                     help="B per GPU (the metric is quoted at 16; smaller values only for profiler captures)")
     args = ap.parse_args()
@@ -407,6 +567,10 @@ def main() -> None:
         ap.error("--gpus N > 1 must be launched with torchrun (one process per GPU)")
     if args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.workload == "sp":
+        run_sp(args, rank, world, local)
+    elif args.workload == "gdn":
+        run_gdn(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 
