@@ -25,7 +25,8 @@ import torch.nn.functional as F
 
 from . import _lib
 
-__all__ = ["chunk_gated_delta_rule", "chunk_gdn", "ChunkGatedDeltaRuleFunction"]
+__all__ = ["chunk_gated_delta_rule", "chunk_gdn", "ChunkGatedDeltaRuleFunction", "fused_recurrent_gated_delta_rule",
+           "fused_recurrent_gdn"]
 
 CHUNK = 64
 
@@ -219,3 +220,30 @@ def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None, out
 
 
 chunk_gdn = chunk_gated_delta_rule
+
+
+def fused_recurrent_gated_delta_rule(q, k, v, g=None, gk=None, gv=None, beta=None, scale=None, initial_state=None,
+                                     output_final_state=False, use_qk_l2norm_in_kernel=False,
+                                     use_gate_in_kernel=False, A_log=None, dt_bias=None, cu_seqlens=None,
+                                     transpose_state_layout=False):
+    """fla's token-recurrent entry point (``fla/ops/gated_delta_rule/fused_recurrent.py``), used by
+    ``GatedDeltaNet`` in its ``fused_recurrent`` mode.  The recurrence is the same, so it runs on
+    the chunked kernels; the per-key / per-value gates ``gk`` / ``gv`` are not provided."""
+    if gk is not None or gv is not None:
+        raise NotImplementedError("linatt_b200: per-key / per-value gates (gk, gv) are not provided")
+    if beta is None:
+        beta = torch.ones_like(q[..., 0])
+        if v.shape[2] != q.shape[2]:
+            beta = beta.repeat_interleave(v.shape[2] // q.shape[2], dim=2)
+    if g is None:
+        if use_gate_in_kernel:
+            raise ValueError("`g` (raw pre-activation) must be provided when `use_gate_in_kernel=True`.")
+        g = torch.zeros(v.shape[:3], device=v.device, dtype=torch.float32)
+    return chunk_gated_delta_rule(q, k, v, g, beta, scale=scale, initial_state=initial_state,
+                                  output_final_state=output_final_state,
+                                  use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel, cu_seqlens=cu_seqlens,
+                                  transpose_state_layout=transpose_state_layout,
+                                  use_gate_in_kernel=use_gate_in_kernel, A_log=A_log, dt_bias=dt_bias)
+
+
+fused_recurrent_gdn = fused_recurrent_gated_delta_rule

@@ -175,3 +175,15 @@ def test_gdn_backward_recompute_path_matches_reuse():
     b = gdr._bwd(qc, kc, vc, gc, bc, A, K ** -0.5, s0c, doc, dhtc, tables, fwd_ws=None)
     for x, y in zip(a, b):
         assert rel_l2(np64(x), np64(y)) < 1e-6
+
+
+def test_fused_recurrent_entry_point_matches_oracle():
+    from linatt_b200.gated_delta_rule import fused_recurrent_gated_delta_rule
+
+    B, T, H, K, V = 2, 40, 2, 64, 64
+    q, k, v, g, beta, do, s0, dht = draw(21, B, T, H, H, K, V, h0=True)
+    o, ht = fused_recurrent_gated_delta_rule(q.cuda(), k.cuda(), v.cuda(), g=g.cuda(), beta=beta.cuda(),
+                                             initial_state=s0.cuda(), output_final_state=True)
+    ref = oracle(q, k, v, g, beta, do, h0=s0, dht=dht)
+    assert rel_l2(np64(o), ref["o"]) < 1e-5
+    assert rel_l2(np64(ht), ref["final_state"]) < 1e-5
