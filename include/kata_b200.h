@@ -154,6 +154,10 @@ KATA_API int kata_attn_bwd_noalloc(const kata_attn_bwd_args* args, kata_stream_t
  * Replaces flash_delta_U (kata/spd/flash_delta.py:186-212, kernel K14 :27-183),
  * flash_delta_readout (:975-983, K15 :900-972) and flash_delta_den (:1049-1057, K16 :988-1046),
  * i.e. _FlashDelta.forward (:1062-1081).  The reference requires T % 64 == 0; any T >= 1 works here.
+ * kappa is the attention "sum" score, so the readout runs on the attention kernels (tensor cores for
+ * bf16/fp16), and U comes from an O(T) chunk scan over the E^2-feature state sum psi(k) U^T
+ * (psi(x)[a,b] = scale sum_g x_{g,a} x_{g,b}) instead of the reference's O(T^2) chunk loop.
+ * Supported: M <= 4, D/M a multiple of 8 with (D/M)^2 <= 4096, D <= 256, Dv a multiple of 16 <= 256.
  * Outputs are fp32 like the reference's.  E = tril(kappa(k,k),-1) U (the erase term) is written
  * when E != NULL.  phases: 0 = U (+E) then o and den; 1 = U (+E) only (flash_delta_U);
  * 2 = readout from a given U: o when o != NULL (flash_delta_readout), den when den != NULL
@@ -175,8 +179,11 @@ typedef struct {
   float scale;       /* reference default 1/E */
   float eps;
   int phases;
+  void* workspace;           /* kata_delta_fwd_workspace_bytes(args) bytes of device memory */
+  size_t workspace_bytes;
 } kata_delta_fwd_args;
 
+KATA_API size_t kata_delta_fwd_workspace_bytes(const kata_delta_fwd_args* args);
 KATA_API int kata_delta_fwd(const kata_delta_fwd_args* args, kata_stream_t stream);
 
 /* SPD delta rule, backward: dq, dk, dv, dbeta (fp32) from the forward's U (and o, den) and dO.

@@ -55,6 +55,7 @@ class DeltaFwdArgs(ctypes.Structure):
         ("U", c_void_p), ("E", c_void_p), ("o", c_void_p), ("den", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("D", c_int), ("Dv", c_int),
         ("M", c_int), ("normalize", c_int), ("scale", c_float), ("eps", c_float), ("phases", c_int),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -120,6 +121,8 @@ def lib() -> ctypes.CDLL:
             L.kata_attn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnBwdArgs)]
             L.kata_delta_fwd.restype = c_int
             L.kata_delta_fwd.argtypes = [ctypes.POINTER(DeltaFwdArgs), c_void_p]
+            L.kata_delta_fwd_workspace_bytes.restype = c_size_t
+            L.kata_delta_fwd_workspace_bytes.argtypes = [ctypes.POINTER(DeltaFwdArgs)]
             L.kata_delta_bwd.restype = c_int
             L.kata_delta_bwd.argtypes = [ctypes.POINTER(DeltaBwdArgs), c_void_p]
             L.kata_delta_bwd_workspace_bytes.restype = c_size_t

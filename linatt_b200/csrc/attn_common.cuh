@@ -56,6 +56,9 @@ struct AttnBwdParams {
   int G;
   float scale;
   int phases;  // 0 both passes, 1 dq pass, 2 dk/dv pass
+  // Internal callers only (not in the C ABI): per-row delta_t given instead of <o_t, dO_t>
+  // (o is then not read and may be null).  (B,T,HQ) fp32.
+  const float* delta_in;
 };
 
 }  // namespace kata

@@ -169,10 +169,11 @@ __global__ void __launch_bounds__(NTH) attn_bwd_dq_simt(AttnBwdParams p) {
   for (int r = warp; r < BQ; r += 8) {
     const int t = t0 + r;
     float acc = 0.f;
-    if (t < T_)
+    if (t < T_ && !p.delta_in)
       for (int j = lane; j < Dv; j += 32)
         acc = fmaf(to_f32<T>(o[static_cast<size_t>(t) * sqv + j]), to_f32<T>(dO[static_cast<size_t>(t) * sqv + j]), acc);
     for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (t < T_ && p.delta_in) acc = p.delta_in[rowq + static_cast<size_t>(t) * p.HQ];
     if (lane == 0) {
       sDelta[r] = acc;
       float dn = (t < T_) ? p.den[rowq + static_cast<size_t>(t) * p.HQ] : 1.f;

@@ -278,7 +278,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
     // ---- delta_t = <o_t, dO_t> over this thread's half of Dv, then exchanged
     float dpart = 0.f;
-    if (live) {
+    if (live && p.delta_in) {
+      dpart = hc == 0 ? p.delta_in[rowidx] : 0.f;
+    } else if (live) {
       constexpr int HV = DV / 2;
       const T* orow = static_cast<const T*>(p.o) + rowidx * DV + hc * HV;
       const T* grow = static_cast<const T*>(p.dout) + rowidx * DV + hc * HV;
@@ -672,7 +674,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
     // ---- delta_t = <o_t, dO_t> over this thread's half of Dv, then exchanged
     float dpart = 0.f;
-    if (live) {
+    if (live && p.delta_in) {
+      dpart = hc == 0 ? p.delta_in[rowidx] : 0.f;
+    } else if (live) {
       constexpr int HV = DV / 2;
       const T* orow = static_cast<const T*>(p.o) + rowidx * DV + hc * HV;
       const T* grow = static_cast<const T*>(p.dout) + rowidx * DV + hc * HV;

@@ -1,6 +1,7 @@
 // capi_attn.cu -- C-ABI entry points for causal KATA-SPD attention: argument validation and
 // dispatch between the tcgen05 tensor-core kernels and the fp32-exact SIMT kernels.
 #include "attn_common.cuh"
+#include "attn_internal.h"
 #include "host_util.h"
 
 namespace kata {
@@ -63,11 +64,12 @@ extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
   return tc_bwd_workspace_bytes(a->B, a->T, a->HQ);
 }
 
-extern "C" int kata_attn_bwd(const kata_attn_bwd_args* a, kata_stream_t stream) {
+int kata::attn_bwd_impl(const kata_attn_bwd_args* a, const float* delta_in, kata_stream_t stream) {
   if (!a) return KATA_ERR_INVALID;
   int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
   if (e) return e;
-  if (!a->q || !a->k || !a->v || !a->o || !a->den || !a->dout || !a->dq || !a->dk || !a->dv) return KATA_ERR_INVALID;
+  if (!a->q || !a->k || !a->v || (!a->o && !delta_in) || !a->den || !a->dout || !a->dq || !a->dk || !a->dv)
+    return KATA_ERR_INVALID;
   if (a->c && !a->dc) return KATA_ERR_INVALID;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) || !aligned16(a->dout) ||
       !aligned16(a->dq) || !aligned16(a->dk) || !aligned16(a->dv))
@@ -80,8 +82,12 @@ extern "C" int kata_attn_bwd(const kata_attn_bwd_args* a, kata_stream_t stream) 
   if (alg < 0) return alg;
   AttnBwdParams p{a->q,  a->k,  a->v,  a->o,  a->den, a->dout, a->c,  a->dq, a->dk,           a->dv,
                   a->dc, static_cast<float*>(a->workspace), a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
-                  a->HQ / a->H, a->scale, a->phases};
+                  a->HQ / a->H, a->scale, a->phases, delta_in};
   if (a->phases < 0 || a->phases > 2) return KATA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return alg == 1 ? tc_attn_bwd(p, a->dtype, sum, st) : simt_attn_bwd(p, a->dtype, sum, st);
+}
+
+extern "C" int kata_attn_bwd(const kata_attn_bwd_args* a, kata_stream_t stream) {
+  return kata::attn_bwd_impl(a, nullptr, stream);
 }

@@ -1,0 +1,849 @@
+// delta_scan.cu -- SPD delta rule ("flash_delta", kata/spd/flash_delta.py) on B200.
+//
+// Kernel value (all M*M group pairs, E = D/M):  kappa(x,y) = sum_{g,h} (scale x_g . y_h)^2,
+// which is exactly the "sum" score of the attention kernels, and which factors through the
+// E^2-dimensional map psi(x)[a,b] = scale * sum_g x_{g,a} x_{g,b}:  kappa(x,y) = psi(x).psi(y)
+// (its upper triangle, off-diagonal entries weighted by sqrt 2, is what the scans use).
+//   L = tril(kappa(k,k), -1),  U = (I + diag(beta) L)^{-1} diag(beta) V,  num = tril(kappa(q,k)) U
+// Forward
+//   prep    (chunk-parallel): Tm_c = (I + diag(beta) L_cc)^{-1} for every 64-row chunk
+//   u_scan  (sequential over chunks, O(T)): E_c = psi(K_c) H_c + L_cc U_c with the state
+//           H_c = sum_{c'<c} psi(K_c')^T U_c'  (F x Dv, F = E^2), U_c = Tm_c beta (V_c - psi(K_c) H_c)
+//   readout: the attention forward (sum score) with v := U gives num / den' and den
+// Backward (dO' = dO/(den+eps), z = <dO,o>/(den+eps) when normalised)
+//   attention backward (sum score, v := U, den := den+eps, delta := <dO,o>): dq, the key-role dk
+//           and dU = tril(kappa(q,k))^T dO'
+//   y_scan  (reverse, O(T)): Y_c = Tm_c^T (dU_c - psi(K_c) G_c),  G_c = sum_{c'>c} psi(K_c')^T (beta Y)_c'
+//   attention backward with q := k, v := U, dO := -beta Y, den := 1, delta := 0: both roles of the
+//           erase kernel A_kk (its diagonal term, which L excludes, is subtracted in finalize)
+//   finalize: dk = sum of the three, dv = beta Y, dbeta = Y.(V - E)
+// The reference computes the same quantities with Triton K14-K21 (kata/spd/flash_delta.py:27-1116);
+// its O(T^2) chunk loops become the O(T) state scans here.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "attn_common.cuh"
+#include "attn_internal.h"
+#include "host_util.h"
+
+namespace kata {
+namespace {
+
+constexpr int C = 64;     // chunk rows
+constexpr int NT = 256;   // threads
+constexpr int LDT = 65;   // padded fp32 row of a 64-wide tile
+
+struct DP {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* beta;
+  float* U;
+  float* E;
+  float* Tm;        // (B,T,H,64)
+  float* Lm;        // (B,T,H,64): kappa(k_i, k_j) for j < i within the chunk, 0 elsewhere
+  const void* dU;   // (B,T,H,Dv) dtype (attention dv output)
+  float* Y;         // (B,T,H,Dv)
+  int B, T, H, D, Dv, M;
+  float scale;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_rows(float* s, int lds, const T* base, size_t stride, int t0, int n, int cols,
+                                          int T_) {
+  for (int i = threadIdx.x; i < n * cols; i += NT) {
+    const int r = i / cols, c = i - r * cols, t = t0 + r;
+    s[r * lds + c] = t < T_ ? to_f32<T>(base[static_cast<size_t>(t) * stride + c]) : 0.f;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// prep: Tm = (I + diag(beta) L_cc)^{-1}, L_cc[i][j] = kappa(k_i, k_j) (j < i).  grid (chunks, B*H).
+// ------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(NT) delta_prep_kernel(DP p) {
+  extern __shared__ float sm[];
+  const int D = p.D, M = p.M, E = D / M, ldk = D + 1;
+  float* sK = sm;                 // 64 x (D+1)
+  float* sL = sK + C * ldk;       // 64 x 65: L, then the identity -> Tm columns
+  float* sX = sL + C * LDT;       // 64 x 65
+  float* sB = sX + C * LDT;
+  const int c0 = blockIdx.x * C, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;  // + t*H
+  const T* k = static_cast<const T*>(p.k) + rowbase * D;
+  load_rows<T>(sK, ldk, k, static_cast<size_t>(p.H) * D, c0, C, D, p.T);
+  for (int i = threadIdx.x; i < C; i += NT) sB[i] = c0 + i < p.T ? p.beta[(rowbase + static_cast<size_t>(c0 + i) * p.H)] : 0.f;
+  __syncthreads();
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  float kap[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) kap[r][c] = 0.f;
+  for (int g = 0; g < M; ++g)
+    for (int hh = 0; hh < M; ++hh) {
+      float s[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[r][c] = 0.f;
+      for (int e = 0; e < E; ++e) {
+        float a[4], bb[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) a[r] = sK[(ty + 16 * r) * ldk + g * E + e];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) bb[c] = sK[(tx + 16 * c) * ldk + hh * E + e];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) s[r][c] = fmaf(a[r], bb[c], s[r][c]);
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float x = p.scale * s[r][c];
+          kap[r][c] = fmaf(x, x, kap[r][c]);
+        }
+    }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = ty + 16 * r, j = tx + 16 * c;
+      sL[i * LDT + j] = j < i ? sB[i] * kap[r][c] : 0.f;
+      sX[i * LDT + j] = i == j ? 1.f : 0.f;
+      if (c0 + i < p.T) p.Lm[(rowbase + static_cast<size_t>(c0 + i) * p.H) * C + j] = j < i ? kap[r][c] : 0.f;
+    }
+  __syncthreads();
+  // forward substitution per column of the identity: x_i -= sum_{j<i} L_ij x_j
+  if (threadIdx.x < C) {
+    float* col = sX + threadIdx.x;
+    for (int i = threadIdx.x + 1; i < C; ++i) {
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int j = threadIdx.x;  // Tm is lower triangular: column c is zero above row c
+      for (; j + 3 < i; j += 4) {
+        a0 = fmaf(sL[i * LDT + j], col[j * LDT], a0);
+        a1 = fmaf(sL[i * LDT + j + 1], col[(j + 1) * LDT], a1);
+        a2 = fmaf(sL[i * LDT + j + 2], col[(j + 2) * LDT], a2);
+        a3 = fmaf(sL[i * LDT + j + 3], col[(j + 3) * LDT], a3);
+      }
+      for (; j < i; ++j) a0 = fmaf(sL[i * LDT + j], col[j * LDT], a0);
+      col[i * LDT] = -((a0 + a1) + (a2 + a3));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < C * C; i += NT) {
+    const int r = i >> 6, c = i & 63, t = c0 + r;
+    if (t < p.T) p.Tm[(rowbase + static_cast<size_t>(t) * p.H) * C + c] = sX[r * LDT + c];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// 64 rows x `cols` values (row t0 + r at base + (t0 + r) * stride) into an fp32 tile with row stride
+// lds; rows past T are zero.  16-byte vector loads, four in flight per thread.
+// ------------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load_tile_v(float* s, int lds, const T* base, size_t stride, int t0, int cols, int T_) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int cpr = cols / VEC, total = C * cpr;
+  for (int i0 = 0; i0 < total; i0 += NT * 4) {
+    uint4 buf[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int idx = i0 + threadIdx.x + NT * m, r = idx / cpr, c = (idx - r * cpr) * VEC;
+      buf[m] = (idx < total && t0 + r < T_)
+                   ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t0 + r) * stride + c)
+                   : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int idx = i0 + threadIdx.x + NT * m, r = idx / cpr, c = (idx - r * cpr) * VEC;
+      if (idx < total) {
+        const T* e = reinterpret_cast<const T*>(&buf[m]);
+#pragma unroll
+        for (int x = 0; x < VEC; ++x) s[r * lds + c + x] = to_f32<T>(e[x]);
+      }
+    }
+  }
+}
+
+// psi over the upper triangle a <= b (psi(x).psi(y) = kappa(x,y)):
+//   psi_f(x) = w_ab * scale * sum_g x_{g,a} x_{g,b},  w = 1 (a == b) or sqrt(2) (a < b),
+// features numbered row by row, f = start(a) + (b - a), start(a) = a E - a (a - 1) / 2, and padded
+// with zeros to a multiple of 64.  Rows of the chunk x features [f0, f0 + FB).
+__device__ __forceinline__ int tri_start(int a, int E) { return a * E - (a * (a - 1)) / 2; }
+
+__device__ __forceinline__ void build_psi(float* sPsi, int ldp, const float* sK, int ldk, int E, int M, int f0, int FB,
+                                          float scale) {
+  const int Fsym = E * (E + 1) / 2;
+  const float e2 = static_cast<float>(2 * E + 1);
+  for (int idx = threadIdx.x; idx < C * FB; idx += NT) {
+    const int i = idx / FB, fl = idx - i * FB, f = f0 + fl;
+    float val = 0.f;
+    if (f < Fsym) {
+      int a = static_cast<int>((e2 - sqrtf(e2 * e2 - 8.f * static_cast<float>(f))) * 0.5f);
+      a = a < 0 ? 0 : (a >= E ? E - 1 : a);
+      if (tri_start(a, E) > f) --a;
+      if (a + 1 < E && tri_start(a + 1, E) <= f) ++a;
+      const int bcol = a + (f - tri_start(a, E));
+      const float* kr = sK + i * ldk;
+      float acc = 0.f;
+      for (int g = 0; g < M; ++g) acc = fmaf(kr[g * E + a], kr[g * E + bcol], acc);
+      val = (a == bcol ? scale : scale * 1.41421356237309515f) * acc;
+    }
+    sPsi[i * ldp + fl] = val;
+  }
+}
+
+// X (64 x VS) += sign * psi (64 x FB) . S[f0 : f0+FB] (FB x VS); thread (ty, tx): rows ty + 16 r,
+// columns tx + 16 cc.
+template <int VS>
+__device__ __forceinline__ void psi_times_state(float* X, const float* sPsi, int ldp, const float* S, int f0, int FB,
+                                                float sign) {
+  constexpr int CPT = VS / 16;
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  float acc[4][CPT];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = 0.f;
+#pragma unroll 4
+  for (int f = 0; f < FB; ++f) {
+    float a[4], b[CPT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) a[r] = sPsi[(ty + 16 * r) * ldp + f];
+#pragma unroll
+    for (int cc = 0; cc < CPT; ++cc) b[cc] = S[(f0 + f) * VS + tx + 16 * cc];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = fmaf(a[r], b[cc], acc[r][cc]);
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int cc = 0; cc < CPT; ++cc) X[(ty + 16 * r) * VS + tx + 16 * cc] += sign * acc[r][cc];
+}
+
+// S[f0 : f0+FB] (FB x VS) += psi^T (FB x 64) . W (64 x VS)
+template <int VS>
+__device__ __forceinline__ void state_update(float* S, const float* sPsi, int ldp, const float* W, int f0, int FB) {
+  constexpr int CPT = VS / 16;
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  for (int r0 = 0; r0 < FB / 16; r0 += 4) {
+    float acc[4][CPT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < C; ++i) {
+      float a[4], b[CPT];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) a[r] = sPsi[i * ldp + ty + 16 * (r0 + r)];
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) b[cc] = W[i * VS + tx + 16 * cc];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = fmaf(a[r], b[cc], acc[r][cc]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) S[(f0 + ty + 16 * (r0 + r)) * VS + tx + 16 * cc] += acc[r][cc];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// u_scan (forward): U, E for every chunk, in order.  CTA = (VS-column slice of Dv, b*h); the
+// F x VS state H lives in shared memory.
+// ------------------------------------------------------------------------------------------------
+template <typename T, int VS>
+__global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
+  extern __shared__ float sm[];
+  const int D = p.D, M = p.M, E = D / M, ldk = D + 1, ldp = FB + 1;
+  constexpr int CPT = VS / 16;
+  float* sH = sm;                    // F x VS
+  float* sPsi = sH + F * VS;         // 64 x (FB+1)
+  float* sK = sPsi + C * ldp;        // 64 x (D+1)
+  float* sT = sK + C * ldk;          // 64 x 65 (Tm)
+  float* sL = sT + C * LDT;          // 64 x 65 (kappa, strictly lower)
+  float* sR = sL + C * LDT;          // 64 x VS: rhs, then U
+  float* sE = sR + C * VS;           // 64 x VS
+  float* sB = sE + C * VS;           // 64
+  const int v0 = blockIdx.x * VS, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;
+  const T* k = static_cast<const T*>(p.k) + rowbase * D;
+  const T* v = static_cast<const T*>(p.v) + rowbase * p.Dv + v0;
+  for (int i = threadIdx.x; i < F * VS; i += NT) sH[i] = 0.f;
+  const int nch = (p.T + C - 1) / C;
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  for (int ch = 0; ch < nch; ++ch) {
+    const int c0 = ch * C;
+    __syncthreads();
+    load_tile_v<T>(sK, ldk, k, static_cast<size_t>(p.H) * D, c0, D, p.T);
+    load_tile_v<float>(sT, LDT, p.Tm + rowbase * C, static_cast<size_t>(p.H) * C, c0, C, p.T);
+    load_tile_v<float>(sL, LDT, p.Lm + rowbase * C, static_cast<size_t>(p.H) * C, c0, C, p.T);
+    load_tile_v<T>(sR, VS, v, static_cast<size_t>(p.H) * p.Dv, c0, VS, p.T);  // V slice
+    for (int i = threadIdx.x; i < C; i += NT)
+      sB[i] = c0 + i < p.T ? p.beta[rowbase + static_cast<size_t>(c0 + i) * p.H] : 0.f;
+    for (int i = threadIdx.x; i < C * VS; i += NT) sE[i] = 0.f;
+    // E = psi(K) H, block by block over the features
+    for (int f0 = 0; f0 < F; f0 += FB) {
+      __syncthreads();
+      build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+      __syncthreads();
+      psi_times_state<VS>(sE, sPsi, ldp, sH, f0, FB, 1.f);
+    }
+    __syncthreads();
+    // rhs = beta (V - E) in place of V
+    for (int i = threadIdx.x; i < C * VS; i += NT) sR[i] = sB[i / VS] * (sR[i] - sE[i]);
+    __syncthreads();
+    // U = Tm rhs  (Tm lower triangular)
+    float u[4][CPT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = ty + 16 * r;
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) {
+        float acc = 0.f;
+        for (int j = 0; j <= i; ++j) acc = fmaf(sT[i * LDT + j], sR[j * VS + tx + 16 * cc], acc);
+        u[r][cc] = acc;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) sR[(ty + 16 * r) * VS + tx + 16 * cc] = u[r][cc];
+    __syncthreads();
+    // E_i += sum_{j<i} kappa(k_i, k_j) U_j ; store U, E
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = ty + 16 * r, t = c0 + i;
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) {
+        const int c = tx + 16 * cc;
+        float acc = 0.f;
+        for (int j = 0; j < i; ++j) acc = fmaf(sL[i * LDT + j], sR[j * VS + c], acc);
+        if (t < p.T) {
+          const size_t o = (rowbase + static_cast<size_t>(t) * p.H) * p.Dv + v0 + c;
+          p.U[o] = u[r][cc];
+          if (p.E) p.E[o] = sE[i * VS + c] + acc;
+        }
+      }
+    }
+    // H += psi(K)^T U  (psi of the last feature block is still in shared memory)
+    for (int f0 = F - FB; f0 >= 0; f0 -= FB) {
+      if (f0 != F - FB) {
+        __syncthreads();
+        build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+      }
+      __syncthreads();
+      state_update<VS>(sH, sPsi, ldp, sR, f0, FB);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// y_scan (backward): Y_c = Tm_c^T (dU_c - psi(K_c) G),  G += psi(K_c)^T (beta Y_c), reverse order
+// ------------------------------------------------------------------------------------------------
+template <typename T, int VS>
+__global__ void __launch_bounds__(NT) delta_y_scan_kernel(DP p, int F, int FB) {
+  extern __shared__ float sm[];
+  const int D = p.D, M = p.M, E = D / M, ldk = D + 1, ldp = FB + 1;
+  constexpr int CPT = VS / 16;
+  float* sG = sm;
+  float* sPsi = sG + F * VS;
+  float* sK = sPsi + C * ldp;
+  float* sT = sK + C * ldk;
+  float* sX = sT + C * LDT;   // 64 x VS: dU - psi G, then beta Y
+  float* sB = sX + C * VS;
+  const int v0 = blockIdx.x * VS, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;
+  const T* k = static_cast<const T*>(p.k) + rowbase * D;
+  const T* dU = static_cast<const T*>(p.dU) + rowbase * p.Dv + v0;
+  for (int i = threadIdx.x; i < F * VS; i += NT) sG[i] = 0.f;
+  const int nch = (p.T + C - 1) / C;
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  for (int ch = nch - 1; ch >= 0; --ch) {
+    const int c0 = ch * C;
+    __syncthreads();
+    load_tile_v<T>(sK, ldk, k, static_cast<size_t>(p.H) * D, c0, D, p.T);
+    load_tile_v<float>(sT, LDT, p.Tm + rowbase * C, static_cast<size_t>(p.H) * C, c0, C, p.T);
+    load_tile_v<T>(sX, VS, dU, static_cast<size_t>(p.H) * p.Dv, c0, VS, p.T);
+    for (int i = threadIdx.x; i < C; i += NT)
+      sB[i] = c0 + i < p.T ? p.beta[rowbase + static_cast<size_t>(c0 + i) * p.H] : 0.f;
+    for (int f0 = 0; f0 < F; f0 += FB) {
+      __syncthreads();
+      build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+      __syncthreads();
+      psi_times_state<VS>(sX, sPsi, ldp, sG, f0, FB, -1.f);
+    }
+    __syncthreads();
+    // Y = Tm^T X  (Y_i = sum_{j>=i} Tm[j][i] X_j)
+    float y[4][CPT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = ty + 16 * r;
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) {
+        float acc = 0.f;
+        for (int j = i; j < C; ++j) acc = fmaf(sT[j * LDT + i], sX[j * VS + tx + 16 * cc], acc);
+        y[r][cc] = acc;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int i = ty + 16 * r, t = c0 + i;
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) {
+        const int c = tx + 16 * cc;
+        if (t < p.T) p.Y[(rowbase + static_cast<size_t>(t) * p.H) * p.Dv + v0 + c] = y[r][cc];
+        sX[i * VS + c] = sB[i] * y[r][cc];
+      }
+    }
+    for (int f0 = F - FB; f0 >= 0; f0 -= FB) {
+      if (f0 != F - FB) {
+        __syncthreads();
+        build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+      }
+      __syncthreads();
+      state_update<VS>(sG, sPsi, ldp, sX, f0, FB);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// elementwise helpers (one warp per token row)
+// ------------------------------------------------------------------------------------------------
+// out[r, :] = f(in[r, :]) * (rowscale ? -rowscale[r] : 1), converted to T
+template <typename T, typename S>
+__global__ void __launch_bounds__(NT) delta_cvt_kernel(const S* __restrict__ in, T* __restrict__ out,
+                                                       const float* __restrict__ neg_rowscale, long rows, int cols) {
+  const long warp = (static_cast<long>(blockIdx.x) * NT + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float f = neg_rowscale ? -neg_rowscale[warp] : 1.f;
+  for (int c = lane; c < cols; c += 32) out[warp * cols + c] = from_f32<T>(f * to_f32<S>(in[warp * cols + c]));
+}
+
+// den' and delta for the first attention backward; ones / zeros for the second
+__global__ void __launch_bounds__(NT) delta_bwd_vecs_kernel(const float* __restrict__ dout, const float* __restrict__ o,
+                                                            const float* __restrict__ den, const float* __restrict__ z,
+                                                            float* __restrict__ den1, float* __restrict__ del1,
+                                                            float* __restrict__ ones, float* __restrict__ zeros,
+                                                            long rows, int Dv, int normalize, float eps) {
+  const long warp = (static_cast<long>(blockIdx.x) * NT + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  float d = 0.f;
+  if (!z && normalize)
+    for (int c = lane; c < Dv; c += 32) d = fmaf(dout[warp * Dv + c], o[warp * Dv + c], d);
+#pragma unroll
+  for (int off = 16; off; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+  if (lane == 0) {
+    den1[warp] = (!z && normalize) ? den[warp] + eps : 1.f;
+    del1[warp] = z ? z[warp] : d;
+    ones[warp] = 1.f;
+    zeros[warp] = 0.f;
+  }
+}
+
+// o = normalize ? num / (den + eps) : num,  num = o_attn * den'  (den' = den if den > 0 else 1)
+template <typename T>
+__global__ void __launch_bounds__(NT) delta_readout_finish_kernel(const T* __restrict__ oa, const float* __restrict__ den,
+                                                                  float* __restrict__ o, long rows, int Dv, int normalize,
+                                                                  float eps) {
+  const long warp = (static_cast<long>(blockIdx.x) * NT + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float dn = den[warp];
+  const float f = (dn > 0.f ? dn : 1.f) * (normalize ? 1.f / (dn + eps) : 1.f);
+  for (int c = lane; c < Dv; c += 32) o[warp * Dv + c] = f * to_f32<T>(oa[warp * Dv + c]);
+}
+
+// dq, dk, dv, dbeta.  dk = dk1 (key role of A_qk) + dq2 + dk2 (both roles of A_kk) minus the
+// diagonal term of the second call, 2 dA_ss dkappa(x, k_s)/dx |_{x = k_s}, dA_ss = -beta_s Y_s.U_s.
+template <typename T>
+__global__ void __launch_bounds__(NT) delta_finish_kernel(const T* __restrict__ dq1, const T* __restrict__ dk1,
+                                                          const T* __restrict__ dq2, const T* __restrict__ dk2,
+                                                          const T* __restrict__ kk, const T* __restrict__ vv,
+                                                          const float* __restrict__ beta, const float* __restrict__ U,
+                                                          const float* __restrict__ Ew, const float* __restrict__ Y,
+                                                          float* __restrict__ dq, float* __restrict__ dk,
+                                                          float* __restrict__ dv, float* __restrict__ dbeta, long rows,
+                                                          int D, int Dv, int M, float scale) {
+  extern __shared__ float sk[];  // per warp: D values of k
+  const long warp = (static_cast<long>(blockIdx.x) * NT + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  if (warp >= rows) return;
+  float* kr = sk + wl * D;
+  for (int c = lane; c < D; c += 32) kr[c] = to_f32<T>(kk[warp * D + c]);
+  __syncwarp();
+  const float bt = beta[warp];
+  float yu = 0.f, db = 0.f;
+  for (int c = lane; c < Dv; c += 32) {
+    const float y = Y[warp * Dv + c];
+    yu = fmaf(y, U[warp * Dv + c], yu);
+    db = fmaf(y, to_f32<T>(vv[warp * Dv + c]) - Ew[warp * Dv + c], db);
+    dv[warp * Dv + c] = bt * y;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    yu += __shfl_xor_sync(0xffffffffu, yu, off);
+    db += __shfl_xor_sync(0xffffffffu, db, off);
+  }
+  if (lane == 0) dbeta[warp] = db;
+  const float dass = -bt * yu;
+  const int E = D / M;
+  for (int c = lane; c < D; c += 32) {
+    const int g = c / E;
+    // dkappa(x,y)/dx_g at x = y = k: 2 scale^2 sum_h (k_g . k_h) k_h
+    float dg = 0.f;
+    for (int hh = 0; hh < M; ++hh) {
+      float ip = 0.f;
+      for (int e = 0; e < E; ++e) ip = fmaf(kr[g * E + e], kr[hh * E + e], ip);
+      dg = fmaf(ip, kr[hh * E + (c - g * E)], dg);
+    }
+    dg *= 2.f * scale * scale;
+    dq[warp * D + c] = to_f32<T>(dq1[warp * D + c]);
+    dk[warp * D + c] = to_f32<T>(dk1[warp * D + c]) + to_f32<T>(dq2[warp * D + c]) + to_f32<T>(dk2[warp * D + c]) -
+                       2.f * dass * dg;
+  }
+}
+
+unsigned warp_blocks(long rows) { return static_cast<unsigned>((rows * 32 + NT - 1) / NT); }
+
+size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Value columns per scan CTA: 16 when the CTAs then fill the GPU, wider slices otherwise would
+// only serialise more work per CTA.  Dv must be a multiple of 16.
+int pick_vs(int F, int Dv) {
+  (void)F;
+  return Dv % 16 == 0 ? 16 : 0;
+}
+
+// Number of psi features: the upper triangle of E x E, padded to a multiple of 64.
+int feat_dim(int E) { return (E * (E + 1) / 2 + 63) / 64 * 64; }
+// Feature block held in shared memory at a time (a multiple of 64 dividing F).
+int pick_fb(int F) { return F <= 256 ? F : ((F <= 1024 && F % 128 == 0) ? 128 : 64); }
+
+size_t scan_smem(int F, int FB, int D, int vs, bool y);
+size_t scan_smem(int F, int FB, int D, int vs, bool y) {
+  const size_t f = static_cast<size_t>(F) * vs + C * (FB + 1) + C * (D + 1) + C * LDT * (y ? 1 : 2) + C +
+                   C * vs * (y ? 1 : 2);
+  return f * sizeof(float);
+}
+
+template <typename K>
+int launch_k(K kernel, dim3 grid, size_t smem, cudaStream_t st, const DP& p, int F, int FB) {
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return KATA_ERR_CUDA;
+  kernel<<<grid, NT, smem, st>>>(p, F, FB);
+  return from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int run_prep(const DP& p, cudaStream_t st) {
+  const size_t smem = sizeof(float) * (C * (p.D + 1) + 2 * C * LDT + C);
+  auto kern = delta_prep_kernel<T>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return KATA_ERR_CUDA;
+  kern<<<dim3((p.T + C - 1) / C, p.B * p.H), NT, smem, st>>>(p);
+  return from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int run_u_scan(const DP& p, cudaStream_t st) {
+  const int E = p.D / p.M, F = feat_dim(E), FB = pick_fb(F);
+  const dim3 grid(p.Dv / 16, p.B * p.H);
+  return launch_k(delta_u_scan_kernel<T, 16>, grid, scan_smem(F, FB, p.D, 16, false), st, p, F, FB);
+}
+
+template <typename T>
+int run_y_scan(const DP& p, cudaStream_t st) {
+  const int E = p.D / p.M, F = feat_dim(E), FB = pick_fb(F);
+  const dim3 grid(p.Dv / 16, p.B * p.H);
+  return launch_k(delta_y_scan_kernel<T, 16>, grid, scan_smem(F, FB, p.D, 16, true), st, p, F, FB);
+}
+
+int check(int dtype, int B, int T, int H, int D, int Dv, int M) {
+  if (dtype != KATA_DTYPE_F32 && dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (B < 1 || T < 1 || H < 1 || D < 1 || Dv < 1 || M < 1 || D % M) return KATA_ERR_SHAPE;
+  const int E = D / M;
+  if (M > 4 || D > 256 || Dv > 256 || Dv % 16 || E % 8 || E > 64) return KATA_ERR_UNSUPPORTED;
+  if (scan_smem(feat_dim(E), pick_fb(feat_dim(E)), D, 16, false) > 227 * 1024) return KATA_ERR_UNSUPPORTED;
+  return KATA_OK;
+}
+
+size_t esz(int dtype) { return dtype == KATA_DTYPE_F32 ? 4 : 2; }
+
+// ---- workspace layouts (byte offsets, 256-aligned) ------------------------------------------------
+struct FwdWs {
+  size_t Tm, Lm, Ub, oa, E, zv, total;
+};
+FwdWs fwd_ws(int dtype, int B, int T, int H, int D, int Dv) {
+  const size_t rows = static_cast<size_t>(B) * T * H;
+  FwdWs w{};
+  size_t o = 0;
+  w.Tm = o; o += al256(rows * C * 4);
+  w.Lm = o; o += al256(rows * C * 4);
+  w.Ub = o; o += al256(rows * (Dv > D ? Dv : D) * esz(dtype));
+  w.oa = o; o += al256(rows * (Dv > D ? Dv : D) * esz(dtype));
+  w.E = o; o += al256(rows * Dv * 4);
+  w.zv = o; o += al256(rows * D * esz(dtype));
+  w.total = o;
+  return w;
+}
+
+struct BwdWs2 {
+  size_t Tm, Lm, Ub, dOb, den1, del1, ones, zeros, attn, dq1, dk1, dU, Y, Yb, dq2, dk2, dv2, E, Us, total;
+};
+BwdWs2 bwd_ws(int dtype, int B, int T, int H, int D, int Dv, size_t attn_bytes) {
+  const size_t rows = static_cast<size_t>(B) * T * H, es = esz(dtype);
+  BwdWs2 w{};
+  size_t o = 0;
+  w.Tm = o; o += al256(rows * C * 4);
+  w.Lm = o; o += al256(rows * C * 4);
+  w.Ub = o; o += al256(rows * Dv * es);
+  w.dOb = o; o += al256(rows * Dv * es);
+  w.den1 = o; o += al256(rows * 4);
+  w.del1 = o; o += al256(rows * 4);
+  w.ones = o; o += al256(rows * 4);
+  w.zeros = o; o += al256(rows * 4);
+  w.attn = o; o += al256(attn_bytes);
+  w.dq1 = o; o += al256(rows * D * es);
+  w.dk1 = o; o += al256(rows * D * es);
+  w.dU = o; o += al256(rows * Dv * es);
+  w.Y = o; o += al256(rows * Dv * 4);
+  w.Yb = o; o += al256(rows * Dv * es);
+  w.dq2 = o; o += al256(rows * D * es);
+  w.dk2 = o; o += al256(rows * D * es);
+  w.dv2 = o; o += al256(rows * Dv * es);
+  w.E = o; o += al256(rows * Dv * 4);
+  w.Us = o; o += al256(rows * Dv * 4);
+  w.total = o;
+  return w;
+}
+
+size_t attn_ws_bytes(int B, int T, int H) {
+  kata_attn_bwd_args a{};
+  a.B = B;
+  a.T = T;
+  a.HQ = H;
+  return kata_attn_bwd_workspace_bytes(&a);
+}
+
+template <typename T>
+int cvt(const void* in, bool in_f32, void* out, const float* neg_rowscale, long rows, int cols, cudaStream_t st) {
+  if (in_f32)
+    delta_cvt_kernel<T, float><<<warp_blocks(rows), NT, 0, st>>>(static_cast<const float*>(in), static_cast<T*>(out),
+                                                                 neg_rowscale, rows, cols);
+  else
+    delta_cvt_kernel<T, T><<<warp_blocks(rows), NT, 0, st>>>(static_cast<const T*>(in), static_cast<T*>(out),
+                                                             neg_rowscale, rows, cols);
+  return from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int fwd_typed(const kata_delta_fwd_args* a, cudaStream_t st) {
+  const FwdWs w = fwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  const long rows = static_cast<long>(a->B) * a->T * a->H;
+  DP p{};
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.beta = a->beta;
+  p.U = a->U;
+  p.E = a->E;
+  p.Tm = reinterpret_cast<float*>(ws + w.Tm);
+  p.Lm = reinterpret_cast<float*>(ws + w.Lm);
+  p.B = a->B;
+  p.T = a->T;
+  p.H = a->H;
+  p.D = a->D;
+  p.Dv = a->Dv;
+  p.M = a->M;
+  p.scale = a->scale;
+  int e = KATA_OK;
+  if (a->phases != 2) {
+    e = run_prep<T>(p, st);
+    if (!e) e = run_u_scan<T>(p, st);
+    if (e || a->phases == 1) return e;
+  }
+  if (!a->o && !a->den) return KATA_OK;
+  // readout through the attention forward (sum score): o_attn = num / den', den
+  const bool den_only = a->U == nullptr;
+  const int dv = den_only ? a->D : a->Dv;
+  void* vb = ws + (den_only ? w.zv : w.Ub);
+  if (den_only)
+    e = from_cuda(cudaMemsetAsync(vb, 0, static_cast<size_t>(rows) * a->D * esz(a->dtype), st));
+  else
+    e = cvt<T>(a->U, true, vb, nullptr, rows, a->Dv, st);
+  if (e) return e;
+  float* den = a->den ? a->den : reinterpret_cast<float*>(ws + w.E);  // E slot is free here
+  kata_attn_fwd_args f{};
+  f.q = a->q;
+  f.k = a->k;
+  f.v = vb;
+  f.o = ws + w.oa;
+  f.den = den;
+  f.dtype = a->dtype;
+  f.B = a->B;
+  f.T = a->T;
+  f.H = a->H;
+  f.HQ = a->H;
+  f.D = a->D;
+  f.Dv = dv;
+  f.M = a->M;
+  f.score = KATA_SCORE_SUM;
+  f.algo = KATA_ALGO_AUTO;
+  f.scale = a->scale;
+  e = kata_attn_fwd(&f, reinterpret_cast<kata_stream_t>(st));
+  if (e || den_only || !a->o) return e;
+  delta_readout_finish_kernel<T><<<warp_blocks(rows), NT, 0, st>>>(static_cast<const T*>(f.o), den, a->o, rows, a->Dv,
+                                                                  a->normalize, a->eps);
+  return from_cuda(cudaGetLastError());
+}
+
+template <typename T>
+int bwd_typed(const kata_delta_bwd_args* a, cudaStream_t st) {
+  const size_t attn_bytes = attn_ws_bytes(a->B, a->T, a->H);
+  const BwdWs2 w = bwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv, attn_bytes);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  auto F32 = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
+  const long rows = static_cast<long>(a->B) * a->T * a->H;
+  DP p{};
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.beta = a->beta;
+  p.Tm = F32(w.Tm);
+  p.Lm = F32(w.Lm);
+  p.B = a->B;
+  p.T = a->T;
+  p.H = a->H;
+  p.D = a->D;
+  p.Dv = a->Dv;
+  p.M = a->M;
+  p.scale = a->scale;
+  int e = run_prep<T>(p, st);
+  const float* Ew = a->E;
+  if (!e && !Ew) {  // recompute the erase term with the forward scan
+    p.U = F32(w.Us);
+    p.E = F32(w.E);
+    e = run_u_scan<T>(p, st);
+    Ew = F32(w.E);
+  }
+  if (!e) e = cvt<T>(a->U, true, ws + w.Ub, nullptr, rows, a->Dv, st);
+  if (!e) e = cvt<T>(a->dout, true, ws + w.dOb, nullptr, rows, a->Dv, st);
+  if (e) return e;
+  delta_bwd_vecs_kernel<<<warp_blocks(rows), NT, 0, st>>>(a->dout, a->o, a->den, a->z, F32(w.den1), F32(w.del1),
+                                                          F32(w.ones), F32(w.zeros), rows, a->Dv,
+                                                          a->z ? 0 : a->normalize, a->eps);
+  if ((e = from_cuda(cudaGetLastError()))) return e;
+  // attention backward 1: A_qk with v := U
+  kata_attn_bwd_args g{};
+  g.q = a->q;
+  g.k = a->k;
+  g.v = ws + w.Ub;
+  g.o = nullptr;
+  g.den = F32(w.den1);
+  g.dout = ws + w.dOb;
+  g.dq = ws + w.dq1;
+  g.dk = ws + w.dk1;
+  g.dv = ws + w.dU;
+  g.workspace = ws + w.attn;
+  g.workspace_bytes = attn_bytes;
+  g.dtype = a->dtype;
+  g.B = a->B;
+  g.T = a->T;
+  g.H = a->H;
+  g.HQ = a->H;
+  g.D = a->D;
+  g.Dv = a->Dv;
+  g.M = a->M;
+  g.score = KATA_SCORE_SUM;
+  g.algo = KATA_ALGO_AUTO;
+  g.scale = a->scale;
+  e = attn_bwd_impl(&g, F32(w.del1), reinterpret_cast<kata_stream_t>(st));
+  if (e) return e;
+  // reverse scan for Y
+  p.dU = ws + w.dU;
+  p.Y = F32(w.Y);
+  if ((e = run_y_scan<T>(p, st))) return e;
+  if ((e = cvt<T>(F32(w.Y), true, ws + w.Yb, a->beta, rows, a->Dv, st))) return e;  // -beta Y
+  // attention backward 2: A_kk (q := k) with dO := -beta Y
+  g.q = a->k;
+  g.den = F32(w.ones);
+  g.dout = ws + w.Yb;
+  g.dq = ws + w.dq2;
+  g.dk = ws + w.dk2;
+  g.dv = ws + w.dv2;
+  e = attn_bwd_impl(&g, F32(w.zeros), reinterpret_cast<kata_stream_t>(st));
+  if (e) return e;
+  const size_t smem = sizeof(float) * (NT / 32) * a->D;
+  delta_finish_kernel<T><<<warp_blocks(rows), NT, smem, st>>>(
+      static_cast<const T*>(static_cast<const void*>(ws + w.dq1)), static_cast<const T*>(static_cast<const void*>(ws + w.dk1)),
+      static_cast<const T*>(static_cast<const void*>(ws + w.dq2)), static_cast<const T*>(static_cast<const void*>(ws + w.dk2)),
+      static_cast<const T*>(a->k), static_cast<const T*>(a->v), a->beta, a->U, Ew, F32(w.Y), a->dq, a->dk, a->dv,
+      a->dbeta, rows, a->D, a->Dv, a->M, a->scale);
+  return from_cuda(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace kata
+
+using namespace kata;
+
+extern "C" size_t kata_delta_fwd_workspace_bytes(const kata_delta_fwd_args* a) {
+  if (!a || a->B < 1 || a->T < 1 || a->H < 1 || a->D < 1 || a->Dv < 1) return 0;
+  return fwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv).total;
+}
+
+extern "C" int kata_delta_fwd(const kata_delta_fwd_args* a, kata_stream_t stream) {
+  if (!a) return KATA_ERR_INVALID;
+  int e = check(a->dtype, a->B, a->T, a->H, a->D, a->Dv, a->M);
+  if (e) return e;
+  if (a->phases < 0 || a->phases > 2 || !a->q || !a->k) return KATA_ERR_INVALID;
+  if (a->phases != 2 && (!a->v || !a->beta || !a->U)) return KATA_ERR_INVALID;
+  if (a->phases == 0 && (!a->o || !a->den)) return KATA_ERR_INVALID;
+  if (a->phases == 2 && a->o && !a->U) return KATA_ERR_INVALID;
+  if (a->phases == 2 && a->normalize && a->o && !a->den) return KATA_ERR_INVALID;
+  if (!a->workspace || a->workspace_bytes < kata_delta_fwd_workspace_bytes(a)) return KATA_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case KATA_DTYPE_F32: return fwd_typed<float>(a, st);
+    case KATA_DTYPE_BF16: return fwd_typed<__nv_bfloat16>(a, st);
+    default: return fwd_typed<__half>(a, st);
+  }
+}
+
+extern "C" size_t kata_delta_bwd_workspace_bytes(const kata_delta_bwd_args* a) {
+  if (!a || a->B < 1 || a->T < 1 || a->H < 1 || a->D < 1 || a->Dv < 1) return 0;
+  return bwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv, attn_ws_bytes(a->B, a->T, a->H)).total;
+}
+
+extern "C" int kata_delta_bwd(const kata_delta_bwd_args* a, kata_stream_t stream) {
+  if (!a) return KATA_ERR_INVALID;
+  int e = check(a->dtype, a->B, a->T, a->H, a->D, a->Dv, a->M);
+  if (e) return e;
+  if (!a->q || !a->k || !a->v || !a->beta || !a->U || !a->dout || !a->dq || !a->dk || !a->dv || !a->dbeta)
+    return KATA_ERR_INVALID;
+  if (!a->z && a->normalize && (!a->o || !a->den)) return KATA_ERR_INVALID;
+  if (!a->workspace || a->workspace_bytes < kata_delta_bwd_workspace_bytes(a)) return KATA_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case KATA_DTYPE_F32: return bwd_typed<float>(a, st);
+    case KATA_DTYPE_BF16: return bwd_typed<__nv_bfloat16>(a, st);
+    default: return bwd_typed<__half>(a, st);
+  }
+}

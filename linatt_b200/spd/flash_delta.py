@@ -1,4 +1,4 @@
-"""SPD delta rule (DeltaKATA), O(T^2) flash form -- drop-in for ``kata/spd/flash_delta.py``.
+"""SPD delta rule (DeltaKATA) -- drop-in for ``kata/spd/flash_delta.py``.
 
 Same public names and signatures as the reference module:
   flash_delta(q, k, v, beta, M, scale=None, C=64, normalize=False, eps=1e-5) -> o      (:1111-1116)
@@ -12,10 +12,13 @@ Math (time-major (B,T,H,D) inputs; kappa(x,y) = sum_{g,h} (scale x_g . y_h)^2, s
   U = (I + diag(beta) tril(kappa(k,k),-1))^{-1} diag(beta) v,  o = tril(kappa(q,k)) U
   normalize: den_t = sum_{s<=t} kappa(q_t,k_s), o = num/(den+eps), with the reference's consistent
   backward (dO' = dO/den, dA_qk centred by z_t = <dO_t,o_t>/den_t).
-All compute runs in ``libkata_b200.so`` (``kata_delta_fwd`` / ``kata_delta_bwd``).  Differences
-from the reference: T need not be a multiple of C (C, warps and BM are accepted and ignored), and
-every product is fp32 (the reference rounds its inter-chunk products to bf16).  o and the
-gradients come out fp32 and are cast to the input dtypes exactly as the reference does.
+All compute runs in ``libkata_b200.so`` (``kata_delta_fwd`` / ``kata_delta_bwd``): the kernel value
+is the attention "sum" score, so the readout and every O(T^2) gradient product run on the attention
+kernels (tcgen05 tensor cores for bf16 / fp16 inputs, fp32-exact CUDA cores for fp32 inputs), and
+the triangular solves for U and its adjoint run as O(T) chunk scans over the E^2-feature state.
+Differences from the reference: T need not be a multiple of C (C, warps and BM are accepted and
+ignored); o and the gradients come out fp32 and are cast to the input dtypes exactly as the
+reference does.
 """
 
 from __future__ import annotations
@@ -52,12 +55,12 @@ def _prep(dt, *ts):
     return [None if t is None else t.to(dt).contiguous() for t in ts]
 
 
-def _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases, U=None, want_o=True, want_den=True):
+def _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases, U=None, want_o=True, want_den=True, want_E=False):
     dev = _lib.require_cuda(q, k, v, beta, U)
     B, T, H, D = q.shape
     if k.shape != q.shape:
         raise ValueError(f"k shape {tuple(k.shape)} != q shape {tuple(q.shape)}")
-    Dv = v.shape[-1] if v is not None else (U.shape[-1] if U is not None else 8)
+    Dv = v.shape[-1] if v is not None else (U.shape[-1] if U is not None else D)
     dt = _qkv_dtype(q, k, v)
     qc, kc, vc = _prep(dt, q, k, v)
     bc = None if beta is None else beta.float().contiguous()
@@ -68,29 +71,33 @@ def _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases, U=None, want_o=Tr
         U = None if U is None else U.float().contiguous()
     o = torch.empty(B, T, H, Dv, **f32) if want_o else None
     den = torch.empty(B, T, H, **f32) if want_den else None
+    E = torch.empty(B, T, H, Dv, **f32) if want_E else None
     a = _lib.DeltaFwdArgs(
-        q=qc.data_ptr(), k=kc.data_ptr(), v=_lib.ptr(vc), beta=_lib.ptr(bc), U=_lib.ptr(U), E=None,
+        q=qc.data_ptr(), k=kc.data_ptr(), v=_lib.ptr(vc), beta=_lib.ptr(bc), U=_lib.ptr(U), E=_lib.ptr(E),
         o=_lib.ptr(o), den=_lib.ptr(den), dtype=_lib.DTYPE[dt], B=B, T=T, H=H, D=D, Dv=Dv, M=M,
         normalize=int(bool(normalize)), scale=_scale(D, M, scale), eps=float(eps), phases=phases)
+    L = _lib.lib()
+    ws = torch.empty(int(L.kata_delta_fwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     with torch.cuda.device(dev):
-        _lib.check(_lib.lib().kata_delta_fwd(a, _lib.stream_handle(dev)), "kata_delta_fwd")
-    return U, o, den
+        _lib.check(L.kata_delta_fwd(a, _lib.stream_handle(dev)), "kata_delta_fwd")
+    return (U, o, den, E) if want_E else (U, o, den)
 
 
-def _bwd_call(q, k, v, beta, U, do, M, scale, normalize, eps, o=None, den=None, z=None):
-    dev = _lib.require_cuda(q, k, v, beta, U, do, o, den, z)
+def _bwd_call(q, k, v, beta, U, do, M, scale, normalize, eps, o=None, den=None, z=None, E=None):
+    dev = _lib.require_cuda(q, k, v, beta, U, do, o, den, z, E)
     B, T, H, D = q.shape
     Dv = v.shape[-1]
     dt = _qkv_dtype(q, k, v)
     qc, kc, vc = _prep(dt, q, k, v)
-    bc, Uc, doc, oc, denc, zc = _prep(torch.float32, beta, U, do, o, den, z)
+    bc, Uc, doc, oc, denc, zc, Ec = _prep(torch.float32, beta, U, do, o, den, z, E)
     f32 = dict(device=dev, dtype=torch.float32)
     dq = torch.empty(B, T, H, D, **f32)
     dk = torch.empty(B, T, H, D, **f32)
     dv = torch.empty(B, T, H, Dv, **f32)
     dbeta = torch.empty(B, T, H, **f32)
     a = _lib.DeltaBwdArgs(
-        q=qc.data_ptr(), k=kc.data_ptr(), v=vc.data_ptr(), beta=bc.data_ptr(), U=Uc.data_ptr(), E=None,
+        q=qc.data_ptr(), k=kc.data_ptr(), v=vc.data_ptr(), beta=bc.data_ptr(), U=Uc.data_ptr(), E=_lib.ptr(Ec),
         o=_lib.ptr(oc), den=_lib.ptr(denc), dout=doc.data_ptr(), z=_lib.ptr(zc), dq=dq.data_ptr(),
         dk=dk.data_ptr(), dv=dv.data_ptr(), dbeta=dbeta.data_ptr(), workspace=None, workspace_bytes=0,
         dtype=_lib.DTYPE[dt], B=B, T=T, H=H, D=D, Dv=Dv, M=M, normalize=int(bool(normalize)),
@@ -134,22 +141,26 @@ def flash_delta_bwd(q, k, v, beta, U, do, M, scale=None, C=64, z=None):
 class _FlashDelta(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, beta, M, scale, C, normalize, eps):
-        U, o, den = _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases=0)
+        U, o, den, E = _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases=0, want_E=True)
+        # Besides the reference's saved set (q, k, v, beta, U [, den, o]) the erase term E is kept so
+        # that the backward does not repeat the forward scan.
         if normalize:
-            ctx.save_for_backward(q, k, v, beta, U, den, o)
+            ctx.save_for_backward(q, k, v, beta, U, den, o, E)
         else:
-            ctx.save_for_backward(q, k, v, beta, U)
+            ctx.save_for_backward(q, k, v, beta, U, E)
         ctx.M, ctx.scale, ctx.C, ctx.normalize, ctx.eps = M, scale, C, normalize, eps
         return o
 
     @staticmethod
     def backward(ctx, do):
         if ctx.normalize:
-            q, k, v, beta, U, den, o = ctx.saved_tensors
-            dq, dk, dv, db = _bwd_call(q, k, v, beta, U, do, ctx.M, ctx.scale, True, ctx.eps, o=o, den=den)
+            q, k, v, beta, U, den, o, E = ctx.saved_tensors
+            dq, dk, dv, db = _bwd_call(q, k, v, beta, U, do, ctx.M, ctx.scale, True, ctx.eps, o=o, den=den, E=E)
         else:
-            q, k, v, beta, U = ctx.saved_tensors
-            dq, dk, dv, db = flash_delta_bwd(q, k, v, beta, U, do, ctx.M, ctx.scale, ctx.C)
+            q, k, v, beta, U, E = ctx.saved_tensors
+            B, T, H, _ = q.shape
+            z = torch.zeros(B, T, H, device=q.device, dtype=torch.float32)
+            dq, dk, dv, db = _bwd_call(q, k, v, beta, U, do, ctx.M, ctx.scale, False, 0.0, z=z, E=E)
         return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), db.to(beta.dtype), None, None, None, None, None
 
 

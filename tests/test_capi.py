@@ -89,10 +89,13 @@ def test_delta_host_side_validation(L):
     assert L.kata_delta_fwd(a, None) == -1  # bad phases
     b = _lib.DeltaBwdArgs(q=16, k=16, v=16, beta=16, U=16, o=16, den=16, dout=16, dq=16, dk=16, dv=16, dbeta=16,
                           dtype=1, B=2, T=8, H=3, D=64, Dv=32, M=4)
-    # dnum, dU, Y, E (B*T*H*Dv each) + z (B*T*H), fp32
-    assert L.kata_delta_bwd_workspace_bytes(b) == 4 * (4 * 48 * 32 + 48)
+    assert L.kata_delta_bwd_workspace_bytes(b) > 4 * 48 * (64 + 32)  # at least Tm and Y
     assert L.kata_delta_bwd(b, None) == -5
+    f = _lib.DeltaFwdArgs(q=16, k=16, v=16, beta=16, U=16, o=16, den=16, dtype=1, B=2, T=8, H=3, D=64, Dv=32, M=4)
+    assert L.kata_delta_fwd_workspace_bytes(f) > 0
+    assert L.kata_delta_fwd(f, None) == -5
     b.o = None
+    b.normalize = 1
     assert L.kata_delta_bwd(b, None) == -1  # normalised path needs o, den unless z is given
 
 

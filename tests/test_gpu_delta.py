@@ -135,7 +135,8 @@ def test_full_size_properties_layer_geometry():
     U = flash_delta_U(qc, kc, vc, bc, M, scale=0.5)
     assert torch.isfinite(U).all()
     # E = tril(A_kk,-1) U via the readout of k against k minus the diagonal term kappa(k_t,k_t) U_t
-    num_kk = flash_delta_readout(kc, kc, U, M, scale=0.5)
+    # (the check's readout runs on fp32 copies of the same bf16 keys: the fp32-exact kernels)
+    num_kk = flash_delta_readout(kc.float(), kc.float(), U, M, scale=0.5)
     kf = kc.float().reshape(B, T, H, M, D // M)
     ip = torch.einsum("bthge,bthfe->bthgf", kf, kf) * 0.5
     diag = (ip * ip).sum((-1, -2))
