@@ -181,6 +181,8 @@ typedef struct {
   int phases;
   void* workspace;           /* kata_delta_fwd_workspace_bytes(args) bytes of device memory */
   size_t workspace_bytes;
+  float* state;              /* (B,H,E*E,Dv) fp32 [out] or NULL: the final state sum_t psi(k_t) U_t^T with
+                                psi(x)[a,b] = scale sum_g x_{g,a} x_{g,b} (flash_delta_state's S) */
 } kata_delta_fwd_args;
 
 KATA_API size_t kata_delta_fwd_workspace_bytes(const kata_delta_fwd_args* args);

@@ -55,7 +55,7 @@ class DeltaFwdArgs(ctypes.Structure):
         ("U", c_void_p), ("E", c_void_p), ("o", c_void_p), ("den", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("D", c_int), ("Dv", c_int),
         ("M", c_int), ("normalize", c_int), ("scale", c_float), ("eps", c_float), ("phases", c_int),
-        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("state", c_void_p),
     ]
 
 

@@ -45,6 +45,7 @@ struct DP {
   float* Lm;        // (B,T,H,64): kappa(k_i, k_j) for j < i within the chunk, 0 elsewhere
   const void* dU;   // (B,T,H,Dv) dtype (attention dv output)
   float* Y;         // (B,T,H,Dv)
+  float* S;         // (B,H,E*E,Dv) final state, or null
   int B, T, H, D, Dv, M;
   float scale;
 };
@@ -344,6 +345,20 @@ __global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
       }
       __syncthreads();
       state_update<VS>(sH, sPsi, ldp, sR, f0, FB);
+    }
+  }
+  if (p.S) {  // final state, unpacked to the full E x E feature grid: S[a,b] = S[b,a] = H_f / w_ab
+    __syncthreads();
+    const int Fsym = E * (E + 1) / 2;
+    float* out = p.S + static_cast<size_t>(bh) * E * E * p.Dv + v0;
+    for (int idx = threadIdx.x; idx < Fsym * VS; idx += NT) {
+      const int f = idx / VS, c = idx % VS;
+      int a = 0;
+      while (a + 1 < E && tri_start(a + 1, E) <= f) ++a;
+      const int bcol = a + (f - tri_start(a, E));
+      const float val = sH[f * VS + c] * (a == bcol ? 1.f : 0.70710678118654752f);
+      out[static_cast<size_t>(a * E + bcol) * p.Dv + c] = val;
+      out[static_cast<size_t>(bcol * E + a) * p.Dv + c] = val;
     }
   }
 }
@@ -666,6 +681,7 @@ int fwd_typed(const kata_delta_fwd_args* a, cudaStream_t st) {
   p.E = a->E;
   p.Tm = reinterpret_cast<float*>(ws + w.Tm);
   p.Lm = reinterpret_cast<float*>(ws + w.Lm);
+  p.S = a->state;
   p.B = a->B;
   p.T = a->T;
   p.H = a->H;

@@ -55,7 +55,8 @@ def _prep(dt, *ts):
     return [None if t is None else t.to(dt).contiguous() for t in ts]
 
 
-def _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases, U=None, want_o=True, want_den=True, want_E=False):
+def _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases, U=None, want_o=True, want_den=True, want_E=False,
+              state=None):
     dev = _lib.require_cuda(q, k, v, beta, U)
     B, T, H, D = q.shape
     if k.shape != q.shape:
@@ -75,7 +76,8 @@ def _fwd_call(q, k, v, beta, M, scale, normalize, eps, phases, U=None, want_o=Tr
     a = _lib.DeltaFwdArgs(
         q=qc.data_ptr(), k=kc.data_ptr(), v=_lib.ptr(vc), beta=_lib.ptr(bc), U=_lib.ptr(U), E=_lib.ptr(E),
         o=_lib.ptr(o), den=_lib.ptr(den), dtype=_lib.DTYPE[dt], B=B, T=T, H=H, D=D, Dv=Dv, M=M,
-        normalize=int(bool(normalize)), scale=_scale(D, M, scale), eps=float(eps), phases=phases)
+        normalize=int(bool(normalize)), scale=_scale(D, M, scale), eps=float(eps), phases=phases,
+        state=_lib.ptr(state))
     L = _lib.lib()
     ws = torch.empty(int(L.kata_delta_fwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()

@@ -145,3 +145,31 @@ def test_full_size_properties_layer_geometry():
     rhs = bc.float()[..., None] * (vc.float() - E)
     e = ((lhs - rhs).norm() / rhs.norm()).item()
     assert e < 1e-4, e
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
+def test_flash_delta_state_head_major_matches_oracle(dtype, tol):
+    """flash_delta_state (head-major, raw numerator) and spd_delta_state_v2's U and final state."""
+    from linatt_b200.spd import flash_delta_state
+    from linatt_b200.spd.chunk_state_v2 import spd_delta_state_v2
+
+    B, T, H, D, Dv, M, scale = 2, 150, 2, 64, 64, 4, 0.5
+    q, k, v, beta, dout = draw(31, B, T, H, D, Dv, dtype)
+    ref = oracle(q, k, v, beta, dout, M, scale, False)
+    hm = lambda x: x.transpose(1, 2).contiguous().cuda()
+    qh, kh, vh, bh = (hm(x).requires_grad_(True) for x in (q, k, v, beta))
+    o = flash_delta_state(qh, kh, vh, bh, M, scale=scale)
+    assert o.shape == (B, H, T, Dv) and o.dtype == torch.float32
+    o.backward(hm(dout))
+    tm = lambda x: x.detach().transpose(1, 2).cpu().double().numpy()
+    assert rel_l2(tm(o), ref["o"]) < tol
+    for name, g in (("dq", qh.grad), ("dk", kh.grad), ("dv", vh.grad), ("dbeta", bh.grad)):
+        assert rel_l2(tm(g), ref[name]) < tol, name
+    o2, U, S = spd_delta_state_v2(qh.detach(), kh.detach(), vh.detach(), bh.detach(), M, scale=scale, return_us=True)
+    assert rel_l2(tm(U), ref["U"]) < tol
+    # S = sum_t psi(k_t) U_t^T, psi(x)[a,b] = scale sum_g x_{g,a} x_{g,b}
+    E = D // M
+    kf = k.double().reshape(B, T, H, M, E)
+    psi = scale * torch.einsum("bthga,bthgc->bthac", kf, kf).reshape(B, T, H, E * E)
+    Sref = torch.einsum("bthf,bthv->bhfv", psi, torch.from_numpy(ref["U"])).reshape(B * H, E * E, Dv)
+    assert rel_l2(S.cpu().double().numpy(), Sref.numpy()) < tol
