@@ -24,6 +24,12 @@ int encode_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64
   EncodeTiledFn enc = get_encode_tiled();
   if (!enc) return KATA_ERR_DRIVER;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return KATA_ERR_ALIGN;
+  // The encoder is a driver-API call and needs a current context on this thread.  A thread that
+  // has made no CUDA runtime call yet (e.g. a framework's autograd worker whose buffers came from
+  // a cache) has none, and the encoder then fails with CUDA_ERROR_INVALID_CONTEXT; setting the
+  // current device binds that device's primary context to the thread.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return KATA_ERR_CUDA;
   cuuint64_t gdim[5];
   cuuint64_t gstr[4];
   cuuint32_t bdim[5];

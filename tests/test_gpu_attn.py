@@ -205,3 +205,26 @@ def test_config3_full_size_forward():
         o_ref, den_ref = ko.attn_fwd(qs, ks, vs, 4)
         assert ko.rel_l2(o[b:b + 1, :, h:h + 1].float().cpu().numpy(), o_ref) < 1e-2
         assert ko.rel_l2(den[b:b + 1, :, h:h + 1].cpu().numpy(), den_ref) < 1e-3
+
+
+def test_backward_in_a_fresh_process():
+    """The backward runs on the framework's autograd worker thread.  In a fresh process that thread
+    may not have a current CUDA context when the library encodes its tensor maps (the buffers it
+    gets can come from the allocator's cache, so no runtime call binds one): the library must bind
+    the device's context itself.  Run a first forward + backward in a new interpreter."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    code = (
+        "import torch, linatt_b200.parallel_kata_attn as pka\n"
+        "x = [torch.randn(1, 300, 2, 128, device='cuda').bfloat16().requires_grad_(True) for _ in range(3)]\n"
+        "o = pka.parallel_kata_attn(*x, num_groups=4)\n"
+        "o.backward(torch.randn_like(o))\n"
+        "torch.cuda.synchronize()\n"
+        "assert all(torch.isfinite(t.grad).all() for t in x)\n"
+        "print('FRESH_OK')\n"
+    )
+    root = Path(__file__).resolve().parent.parent
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "FRESH_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
