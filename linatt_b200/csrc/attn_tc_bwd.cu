@@ -66,6 +66,13 @@ struct BwdSmem {
   static constexpr int KV_OFF_VEC = KV_OFF_T + 2 * T_BYTES;   // 2 stages x {rden, delta*rden} x 128 fp32
   static constexpr int KV_OFF_BARS = KV_OFF_VEC + 2 * 2 * kTile * 4;
   static constexpr int KV_TOTAL = KV_OFF_BARS + 256;          // DkvBars lives here (no static smem)
+  // dkdv ring kernel: K, V resident; a ring of four dO/Q tiles (two query tiles); no W/P tiles
+  // (they stay in tensor memory)
+  static constexpr int KR_RING = 4;
+  static constexpr int KR_OFF_RING = KV_OFF_RING;
+  static constexpr int KR_OFF_VEC = KR_OFF_RING + KR_RING * ITEM;
+  static constexpr int KR_OFF_BARS = KR_OFF_VEC + 2 * 2 * kTile * 4;
+  static constexpr int KR_TOTAL = KR_OFF_BARS + 256;
 };
 
 struct DqBars {
@@ -92,7 +99,26 @@ struct DkvBars {
   int abort_flag;
 };
 
+struct DkvRingBars {
+  uint64_t kv_full;
+  uint64_t vec_full[2], vec_empty[2];
+  uint64_t ring_full[4], ring_empty[4];
+  uint64_t i_full[2], i_free[2];
+  uint64_t acc_done, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
 __device__ __forceinline__ float2 u2f2(uint32_t a, uint32_t b) { return make_float2(__uint_as_float(a), __uint_as_float(b)); }
+
+// bf16 pair <-> float2 for values kept in registers between the items of one tile
+__device__ __forceinline__ uint32_t bf2_pack(float2 v) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 bf2_unpack(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
 
 // ================================================================================================
 // dq kernel
@@ -1254,6 +1280,390 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ================================================================================================
+// dk / dv kernel, ring form (no decay)
+// ================================================================================================
+// TMEM: a ring of two 128-column slots that the items of every (key tile, query tile) pair pass
+// through in order -- dN^T = V dO^T, then the transposed score parts S^T_0..S^T_{NP-1} (rows: keys)
+// -- with dK at columns 256..383 and dV at 384..511.  The compute warps read dN^T once per pair and
+// keep dA'^T = 2 scale^2 (dN - delta)/den (masked) in registers as bf16 pairs next to the fp32 sum
+// of squared parts; each S^T_p slot is overwritten in place by W^T_p = S^T_p dA'^T (packed bf16,
+// columns [0,32) and [64,96) of the slot), and the last part's slot also receives P^T = A/den in the
+// other half (columns [32,64) and [96,128)).  The issuer reuses a slot only after the compute warps
+// release it, issuing first the dK chain of the W it holds (and, for the last part, the dV chain of
+// P) as tensor-memory-operand MMAs; MMAs of one CTA execute in issue order.
+template <typename T, int D, int DV, int M, bool SUM>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_dkdv_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                          AttnBwdParams p) {
+  constexpr int E = D / M;
+  constexpr int CW = BoxW<E>::value;
+  constexpr int NBOX = D / CW;
+  constexpr int VCW = BoxW<DV>::value;
+  constexpr int NVBOX = DV / VCW;
+  constexpr int NP = SUM ? M * M : M;
+  constexpr int kItems = 1 + NP;
+  constexpr int kR = 4;  // dO / Q ring depth
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kColDK = 256, kColDV = 384;
+  using L = BwdSmem<D, DV>;
+  static_assert(sizeof(DkvRingBars) <= 256, "barrier block");
+  static_assert(L::KR_RING == kR, "ring depth");
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  DkvRingBars& bars = *reinterpret_cast<DkvRingBars*>(smem + L::KR_OFF_BARS);
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kStatusWaitTimeout + 1);
+    return;
+  }
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T_ = p.T;
+  const int nqt = (T_ + kTile - 1) / kTile;
+  const int kj = static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int s0 = kj * kTile;
+  const int nq = nqt - kj;
+  const int nwork = p.G * nq;
+  const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
+  WaitCtx wc{p.status, &bars.abort_flag};
+
+  if (threadIdx.x == 0) {
+    bars.abort_flag = 0;
+    mbar_init(&bars.kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.vec_full[i], 1);
+      mbar_init(&bars.vec_empty[i], 8);
+      mbar_init(&bars.i_full[i], 1);
+      mbar_init(&bars.i_free[i], 8);
+    }
+    for (int i = 0; i < kR; ++i) {
+      mbar_init(&bars.ring_full[i], 1);
+      mbar_init(&bars.ring_empty[i], 1);
+    }
+    mbar_init(&bars.acc_done, 1);
+    mbar_init(&bars.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+  float* vec = reinterpret_cast<float*>(smem + L::KR_OFF_VEC);  // [stage][0: rden, 1: delta*rden][128]
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmO);
+      mbar_arrive_expect_tx(&bars.kv_full, L::Q_BYTES + L::O_BYTES);
+      for (int bx = 0; bx < NBOX; ++bx)
+        tma_load_4d(smem + L::KV_OFF_K + bx * (kTile * CW * 2), &tmK, &bars.kv_full, bx * CW, h, s0, b);
+      for (int bx = 0; bx < NVBOX; ++bx)
+        tma_load_4d(smem + L::KV_OFF_V + bx * (kTile * VCW * 2), &tmV, &bars.kv_full, bx * VCW, h, s0, b);
+      int r = 0, nv = 0;
+      bool ok = true;
+      for (int n = 0; n < nwork && ok; ++n) {
+        const int hq = h * p.G + n / nq;
+        const int ti = (kj + n % nq) * kTile;
+        const int vs = n & 1;
+        if (!mbar_wait(&bars.vec_empty[vs], ((n >> 1) & 1) ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + ti;
+        mbar_arrive_expect_tx(&bars.vec_full[vs], 2 * kTile * 4);
+        bulk_load(vec + (vs * 2 + 0) * kTile, ws.rden + hm, kTile * 4, &bars.vec_full[vs]);
+        bulk_load(vec + (vs * 2 + 1) * kTile, ws.dr + hm, kTile * 4, &bars.vec_full[vs]);
+        nv = n + 1;
+        for (int item = 0; item < 2; ++item, ++r) {  // dO_n then Q_n (dN is the first MMA of a pair)
+          const int slot = r % kR;
+          if (!mbar_wait(&bars.ring_empty[slot], ((r / kR) & 1) ^ 1, wc)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + L::KR_OFF_RING + slot * L::ITEM;
+          if (item == 0) {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
+            for (int bx = 0; bx < NVBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmO, &bars.ring_full[slot], bx * VCW, hq, ti, b);
+          } else {
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
+            for (int bx = 0; bx < NBOX; ++bx)
+              tma_load_4d(dst + bx * (kTile * CW * 2), &tmQ, &bars.ring_full[slot], bx * CW, hq, ti, b);
+          }
+        }
+      }
+      if (!ok) {
+        for (int rr = (r > kR ? r - kR : 0); rr < r; ++rr) mbar_drain(&bars.ring_full[rr % kR], (rr / kR) & 1);
+        for (int n = (nv > 2 ? nv - 2 : 0); n < nv; ++n) mbar_drain(&bars.vec_full[n & 1], (n >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
+      const uint32_t id_dk = umma_idesc_f16(128, E, kBF16, false, true);
+      const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
+      const uint32_t sK = smem_u32(smem + L::KV_OFF_K);
+      const uint32_t sV = smem_u32(smem + L::KV_OFF_V);
+      const uint32_t sRing = smem_u32(smem + L::KR_OFF_RING);
+      bool ok = mbar_wait(&bars.kv_full, 0, wc);
+      // Item `it` lives in slot it % 2; before reuse, the pending chains of item it - 2 are issued.
+      int it = 0, x = 0;
+      uint32_t use_par = 0;
+      for (int n = 0; ok && n <= nwork; ++n) {
+        const int n_items = (n < nwork) ? kItems : 2;  // after the last pair: two drain claims
+        const int slotO = (2 * n) % kR, slotQ = (2 * n + 1) % kR;
+        for (int q = 0; q < n_items; ++q) {
+          if (it >= 2) {
+            if (!mbar_wait(&bars.i_free[x], use_par ^ 1, wc)) {
+              ok = false;
+              break;
+            }
+            const int prev = it - 2;
+            const int pq = prev % kItems;
+            if (pq > 0) {
+              const int pn = prev / kItems, pp = pq - 1;
+              const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+              const bool first = (pn == 0) && (!SUM || ga == 0);
+              const uint32_t psQ = sRing + static_cast<uint32_t>((2 * pn + 1) % kR) * L::ITEM;
+              const uint64_t qd = mnmajor_desc<CW>(psQ, ga * E / CW, 0);
+              const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
+              tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < kTile / 16; ++kk)
+                umma_ts(tbase + kColDK + gb * E, wa + packed_col(kk), qd + mnstep<CW>(kk), id_dk,
+                        (!first || kk > 0) ? 1u : 0u);
+              if (pp == NP - 1) {  // dV += P^T dO, then this pair's dO and Q tiles are free
+                const int psO = (2 * pn) % kR;
+                const uint64_t od = mnmajor_desc<VCW>(sRing + static_cast<uint32_t>(psO) * L::ITEM, 0, 0);
+#pragma unroll
+                for (int kk = 0; kk < kTile / 16; ++kk)
+                  umma_ts(tbase + kColDV, wa + packed_col(kk) + 32u, od + mnstep<VCW>(kk), id_dv,
+                          (pn > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&bars.ring_empty[psO]);
+                umma_commit(&bars.ring_empty[(2 * pn + 1) % kR]);
+              }
+            }
+          }
+          if (n == nwork) {
+            ++it;
+            if (++x == 2) { x = 0; use_par ^= 1; }
+            continue;
+          }
+          if (q == 0) {  // dN^T = V dO_n^T
+            if (!mbar_wait(&bars.ring_full[slotO], ((2 * n) / kR) & 1, wc)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t vd = kmajor_desc<VCW>(sV, 0, DV, 0);
+            const uint64_t od = kmajor_desc<VCW>(sRing + static_cast<uint32_t>(slotO) * L::ITEM, 0, DV, 0);
+#pragma unroll
+            for (int kk = 0; kk < DV / 16; ++kk)
+              umma_ss(tbase + x * 128u, vd + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit(&bars.i_full[x]);
+            if (!mbar_wait(&bars.ring_full[slotQ], ((2 * n + 1) / kR) & 1, wc)) {  // Q_n for the parts
+              ok = false;
+              break;
+            }
+          } else {  // S^T_p = K_b Q_a^T
+            const int pp = q - 1;
+            const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+            tc_fence_after();
+            const uint64_t kd = kmajor_desc<CW>(sK, gb, E, 0);
+            const uint64_t qd = kmajor_desc<CW>(sRing + static_cast<uint32_t>(slotQ) * L::ITEM, ga, E, 0);
+#pragma unroll
+            for (int kk = 0; kk < E / 16; ++kk)
+              umma_ss(tbase + x * 128u, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit(&bars.i_full[x]);
+          }
+          ++it;
+          if (++x == 2) {
+            x = 0;
+            use_par ^= 1;
+          }
+        }
+      }
+      if (ok) umma_commit(&bars.acc_done);
+      umma_commit(&bars.drain);
+      mbar_drain(&bars.drain, 0);
+    }
+  } else {
+    const int cw = warp - kComputeWarp0;
+    const int hc = cw >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // key row within the tile
+    const int sg = s0 + row;
+    const bool live = sg < T_;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float w_scale = 2.f * p.scale * p.scale;
+    const float2 wsc2 = make_float2(w_scale, w_scale);
+    const float scale2 = p.scale * p.scale;
+    bool ok = true;
+    int it = 0;
+    for (int n = 0; n < nwork && ok; ++n) {
+      const int qi = kj + n % nq;
+      const bool diag = (qi == kj);
+      const int vs = n & 1;
+      const float* v_rd = vec + (vs * 2 + 0) * kTile;
+      const float* v_dr = vec + (vs * 2 + 1) * kTile;
+      if (!mbar_wait(&bars.vec_full[vs], (n >> 1) & 1, wc)) {
+        ok = false;
+        break;
+      }
+      uint32_t dap[32];  // dA'^T of this thread's 64 query columns, bf16 pairs
+      {
+        const int x = it & 1;
+        if (!mbar_wait(&bars.i_full[x], (it >> 1) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t nbase = lane_addr + x * 128u + hc * 64u;
+        uint32_t rn[2][16];
+        tmem_ld16(nbase, rn[0]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cur = c & 1;
+          if (c < 3) tmem_ld16(nbase + (c + 1) * 16u, rn[cur ^ 1]);
+          const int cbase = hc * 64 + c * 16;
+#pragma unroll
+          for (int x4 = 0; x4 < 4; ++x4) {
+            const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
+            const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
+            float2 d0 = fmul2(ffma2(u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]), make_float2(rd.x, rd.y),
+                                    make_float2(-dr.x, -dr.y)), wsc2);
+            float2 d1 = fmul2(ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
+                                    make_float2(-dr.z, -dr.w)), wsc2);
+            if (diag) {  // causal: query t >= key s
+              const int tl = cbase + 4 * x4;
+              if (tl < row) d0.x = 0.f;
+              if (tl + 1 < row) d0.y = 0.f;
+              if (tl + 2 < row) d1.x = 0.f;
+              if (tl + 3 < row) d1.y = 0.f;
+            }
+            dap[8 * c + 2 * x4] = bf2_pack(d0);
+            dap[8 * c + 2 * x4 + 1] = bf2_pack(d1);
+          }
+          if (c < 3) tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.i_free[x]);
+        ++it;
+      }
+      float2 acc[32];
+      for (int pp = 0; pp < NP; ++pp, ++it) {
+        const int x = it & 1;
+        if (!mbar_wait(&bars.i_full[x], (it >> 1) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sbase = lane_addr + x * 128u + hc * 64u;
+        uint32_t rs[2][16];
+        tmem_ld16(sbase, rs[0]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cur = c & 1;
+          if (c < 3) tmem_ld16(sbase + (c + 1) * 16u, rs[cur ^ 1]);
+          uint32_t wv[8];
+#pragma unroll
+          for (int x2 = 0; x2 < 8; ++x2) {
+            const float2 sv = u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]);
+            acc[8 * c + x2] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x2]);
+            const float2 w = fmul2(sv, bf2_unpack(dap[8 * c + x2]));
+            wv[x2] = pack2<T>(w.x, w.y);
+          }
+          tmem_st8(sbase + c * 8u, wv);  // columns of S already in registers
+          if (c < 3) tmem_wait_ld();
+        }
+        if (pp == NP - 1) {  // P^T = scale^2 A / den into the other half of the slot (all S is read)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int cbase = hc * 64 + c * 16;
+            uint32_t pv[8];
+#pragma unroll
+            for (int x2 = 0; x2 < 8; ++x2) {
+              const int tl = cbase + 2 * x2;
+              const float2 rd = *reinterpret_cast<const float2*>(v_rd + tl);
+              float a0 = scale2 * acc[8 * c + x2].x * rd.x, a1 = scale2 * acc[8 * c + x2].y * rd.y;
+              if (diag) {
+                if (tl < row) a0 = 0.f;
+                if (tl + 1 < row) a1 = 0.f;
+              }
+              pv[x2] = pack2<T>(a0, a1);
+            }
+            tmem_st8(sbase + 32u + c * 8u, pv);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars.i_free[x]);
+          if (pp == NP - 1) mbar_arrive(&bars.vec_empty[vs]);
+        }
+      }
+    }
+    // ---- epilogue: dK, dV -> global
+    named_bar_sync(1, 256);
+    if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
+      tc_fence_after();
+      constexpr int HD = D / 2, HV = DV / 2;
+      const size_t rowkv = (static_cast<size_t>(b) * T_ + sg) * p.H + h;
+      T* dkrow = static_cast<T*>(p.dk) + rowkv * D + hc * HD;
+      T* dvrow = static_cast<T*>(p.dv) + rowkv * DV + hc * HV;
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + kColDK + hc * HD + c0, r);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
+          }
+        }
+      }
+#pragma unroll
+      for (int c0 = 0; c0 < HV; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + kColDV + hc * HV + c0, r);
+        tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int v2 = 0; v2 < 2; ++v2) {
+            uint4 w;
+            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            *reinterpret_cast<uint4*>(dvrow + c0 + 8 * v2) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+// ================================================================================================
 // host side
 // ================================================================================================
 template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
@@ -1280,8 +1690,9 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   if (p.phases != 1) {
-    auto kern = attn_bwd_dkdv_tc<T, D, DV, M, SUM, DECAY>;
-    const size_t smem = L::KV_TOTAL;  // no alignment slack: the kernel has no static shared memory
+    // decay (dc column sums) keeps the shared-memory W/P form; otherwise the tensor-memory ring
+    auto kern = DECAY ? attn_bwd_dkdv_tc<T, D, DV, M, SUM, DECAY> : attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM>;
+    const size_t smem = DECAY ? L::KV_TOTAL : L::KR_TOTAL;  // no static shared memory: no alignment slack
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
