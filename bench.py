@@ -541,6 +541,69 @@ def run_gdn(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_delta(args, rank: int, world: int, local: int) -> None:
+    """SPD delta rule (flash_delta) fwd+bwd at the 200M-model mixer geometry: B=8, T=2048, H=12,
+    D=Dv=64, M=4, scale 0.5, normalised, bf16 inputs, per GPU (weak scaling over B)."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from linatt_b200.spd import flash_delta
+
+    Bd, Td, Hd, Dd, Md = 8, 2048, 12, 64, 4
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    sets = []
+    for _ in range(4):
+        q = F.normalize(torch.randn(Bd, Td, Hd, Dd, device=dev, generator=g), dim=-1).bfloat16()
+        k = F.normalize(torch.randn(Bd, Td, Hd, Dd, device=dev, generator=g), dim=-1).bfloat16()
+        v = torch.randn(Bd, Td, Hd, Dd, device=dev, generator=g).bfloat16()
+        beta = torch.sigmoid(torch.randn(Bd, Td, Hd, device=dev, generator=g)).bfloat16()
+        do = torch.randn(Bd, Td, Hd, Dd, device=dev, generator=g)
+        sets.append((q, k, v, beta, do))
+
+    def step(i):
+        q, k, v, beta, do = sets[i % 4]
+        leaves = [x.requires_grad_(True) for x in (q, k, v, beta)]
+        o = flash_delta(*leaves, Md, scale=0.5, normalize=True)
+        o.backward(do)
+        for x in leaves:
+            x.grad = None
+
+    ms, clk = _timed_steps(torch, dist, world, dev, step, args.steps, args.warmup)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, src = load_peaks()
+    step_ms = ms / args.steps
+    # attention-kernel work of the step (sum score, M*M = 16 parts of E = 16, i.e. 2 GEMM-eq of
+    # K = 256 per pair): readout (S + PV) and two backward calls (S recompute, dN, dQ, dK, dV each),
+    # counted as GEMM-equivalents 2*P*D per (b,h) like the attention bench; scans excluded
+    gemm_eq = Bd * Hd * 2.0 * pairs(Td) * Dd
+    flops = (2 + 2 * 5) * gemm_eq * (Md * Md * (Dd // Md)) / Dd
+    line = {
+        "metric": "SPD delta rule fwd+bwd tokens/s/GPU at B8·T2048·H12·D64, M=4 (mixer geometry)",
+        "value": world * Bd * Td / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "flash_delta fwd+bwd, normalised, scale 0.5", "batch_per_gpu": Bd, "seq_len": Td,
+                   "heads": Hd, "head_dim": Dd, "num_groups": Md, "parallelism": f"batch shard x{world}",
+                   "l2": "4 rotating input sets of 151 MB"},
+        "roofline": {"bound": "tensor", "achieved": flops / (step_ms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": flops / (step_ms / 1e3) / 1e12 / peak, "traffic": None, "peak_source": src,
+                     "note": "attention-kernel GEMM work only (the O(T) scans are not counted)"},
+        "clocks": clk, "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -552,8 +615,9 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--num-groups", type=int, default=4, help="M (the benchmark metric is quoted at M=4)")
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
-    ap.add_argument("--workload", choices=["attn", "sp", "gdn"], default="attn",
-                    help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2")
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta"], default="attn",
+                    help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
+                         "delta: the SPD delta rule at the mixer geometry")
     ap.add_argument("--batch", type=int, default=16,
                     help="B per GPU (the metric is quoted at 16; smaller values only for profiler captures)")
     args = ap.parse_args()
@@ -571,6 +635,8 @@ def main() -> None:
         run_sp(args, rank, world, local)
     elif args.workload == "gdn":
         run_gdn(args, rank, world, local)
+    elif args.workload == "delta":
+        run_delta(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 

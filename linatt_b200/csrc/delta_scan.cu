@@ -173,36 +173,47 @@ __device__ __forceinline__ void load_tile_v(float* s, int lds, const T* base, si
 // psi over the upper triangle a <= b (psi(x).psi(y) = kappa(x,y)):
 //   psi_f(x) = w_ab * scale * sum_g x_{g,a} x_{g,b},  w = 1 (a == b) or sqrt(2) (a < b),
 // features numbered row by row, f = start(a) + (b - a), start(a) = a E - a (a - 1) / 2, and padded
-// with zeros to a multiple of 64.  Rows of the chunk x features [f0, f0 + FB).
+// with zeros to a multiple of 64.  The scans keep a table of (a, b) per feature (0xffff: padding)
+// and build psi in blocks of 64 features.
+constexpr int FB = 64;       // feature block
+constexpr int LDP = FB + 4;  // psi tile row: 16-byte aligned for vector reads along the features
+
 __device__ __forceinline__ int tri_start(int a, int E) { return a * E - (a * (a - 1)) / 2; }
 
-__device__ __forceinline__ void build_psi(float* sPsi, int ldp, const float* sK, int ldk, int E, int M, int f0, int FB,
-                                          float scale) {
+__device__ __forceinline__ void build_feature_table(unsigned short* tab, int E, int F) {
   const int Fsym = E * (E + 1) / 2;
-  const float e2 = static_cast<float>(2 * E + 1);
-  for (int idx = threadIdx.x; idx < C * FB; idx += NT) {
-    const int i = idx / FB, fl = idx - i * FB, f = f0 + fl;
-    float val = 0.f;
-    if (f < Fsym) {
-      int a = static_cast<int>((e2 - sqrtf(e2 * e2 - 8.f * static_cast<float>(f))) * 0.5f);
-      a = a < 0 ? 0 : (a >= E ? E - 1 : a);
-      if (tri_start(a, E) > f) --a;
-      if (a + 1 < E && tri_start(a + 1, E) <= f) ++a;
-      const int bcol = a + (f - tri_start(a, E));
-      const float* kr = sK + i * ldk;
-      float acc = 0.f;
-      for (int g = 0; g < M; ++g) acc = fmaf(kr[g * E + a], kr[g * E + bcol], acc);
-      val = (a == bcol ? scale : scale * 1.41421356237309515f) * acc;
-    }
-    sPsi[i * ldp + fl] = val;
+  for (int a = threadIdx.x; a < E; a += NT) {
+    const int st = tri_start(a, E);
+    for (int bcol = a; bcol < E; ++bcol) tab[st + bcol - a] = static_cast<unsigned short>((a << 8) | bcol);
+  }
+  for (int f = Fsym + threadIdx.x; f < F; f += NT) tab[f] = 0xffff;
+}
+
+// psi of the 64 chunk rows for features [f0, f0 + 64): thread = (feature tid & 63, rows tid >> 6 + 4 k)
+__device__ __forceinline__ void build_psi(float* sPsi, const float* sK, int ldk, int E, int M, int f0,
+                                          const unsigned short* tab, float scale) {
+  const int fl = threadIdx.x & (FB - 1);
+  const unsigned t = tab[f0 + fl];
+  if (t == 0xffffu) {
+#pragma unroll 4
+    for (int i = threadIdx.x >> 6; i < C; i += NT / FB) sPsi[i * LDP + fl] = 0.f;
+    return;
+  }
+  const int a = static_cast<int>(t >> 8), bcol = static_cast<int>(t & 0xffu);
+  const float w = a == bcol ? scale : scale * 1.41421356237309515f;
+#pragma unroll 4
+  for (int i = threadIdx.x >> 6; i < C; i += NT / FB) {
+    const float* kr = sK + i * ldk;
+    float acc = 0.f;
+    for (int g = 0; g < M; ++g) acc = fmaf(kr[g * E + a], kr[g * E + bcol], acc);
+    sPsi[i * LDP + fl] = w * acc;
   }
 }
 
-// X (64 x VS) += sign * psi (64 x FB) . S[f0 : f0+FB] (FB x VS); thread (ty, tx): rows ty + 16 r,
-// columns tx + 16 cc.
+// X (64 x VS) += sign * psi (64 x 64) . S[f0 : f0+64] (64 x VS); thread (ty, tx): rows ty + 16 r,
+// columns tx + 16 cc; psi read four features at a time.
 template <int VS>
-__device__ __forceinline__ void psi_times_state(float* X, const float* sPsi, int ldp, const float* S, int f0, int FB,
-                                                float sign) {
+__device__ __forceinline__ void psi_times_state(float* X, const float* sPsi, const float* S, int f0, float sign) {
   constexpr int CPT = VS / 16;
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   float acc[4][CPT];
@@ -210,17 +221,27 @@ __device__ __forceinline__ void psi_times_state(float* X, const float* sPsi, int
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = 0.f;
-#pragma unroll 4
-  for (int f = 0; f < FB; ++f) {
-    float a[4], b[CPT];
+#pragma unroll 2
+  for (int f = 0; f < FB; f += 4) {
+    float4 a[4];
+    float b[4][CPT];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) a[r] = sPsi[(ty + 16 * r) * ldp + f];
+    for (int r = 0; r < 4; ++r) a[r] = *reinterpret_cast<const float4*>(sPsi + (ty + 16 * r) * LDP + f);
 #pragma unroll
-    for (int cc = 0; cc < CPT; ++cc) b[cc] = S[(f0 + f) * VS + tx + 16 * cc];
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) b[j][cc] = S[(f0 + f + j) * VS + tx + 16 * cc];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = fmaf(a[r], b[cc], acc[r][cc]);
+      for (int cc = 0; cc < CPT; ++cc) {
+        float x = acc[r][cc];
+        x = fmaf(a[r].x, b[0][cc], x);
+        x = fmaf(a[r].y, b[1][cc], x);
+        x = fmaf(a[r].z, b[2][cc], x);
+        x = fmaf(a[r].w, b[3][cc], x);
+        acc[r][cc] = x;
+      }
   }
 #pragma unroll
   for (int r = 0; r < 4; ++r)
@@ -228,34 +249,35 @@ __device__ __forceinline__ void psi_times_state(float* X, const float* sPsi, int
     for (int cc = 0; cc < CPT; ++cc) X[(ty + 16 * r) * VS + tx + 16 * cc] += sign * acc[r][cc];
 }
 
-// S[f0 : f0+FB] (FB x VS) += psi^T (FB x 64) . W (64 x VS)
+// S[f0 : f0+64] (64 x VS) += psi^T (64 x 64) . W (64 x VS); thread (ty, tx): features 4 ty + j,
+// columns tx + 16 cc.
 template <int VS>
-__device__ __forceinline__ void state_update(float* S, const float* sPsi, int ldp, const float* W, int f0, int FB) {
+__device__ __forceinline__ void state_update(float* S, const float* sPsi, const float* W, int f0) {
   constexpr int CPT = VS / 16;
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-  for (int r0 = 0; r0 < FB / 16; r0 += 4) {
-    float acc[4][CPT];
+  float acc[4][CPT];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = 0.f;
+    for (int cc = 0; cc < CPT; ++cc) acc[j][cc] = 0.f;
 #pragma unroll 4
-    for (int i = 0; i < C; ++i) {
-      float a[4], b[CPT];
+  for (int i = 0; i < C; ++i) {
+    const float4 a = *reinterpret_cast<const float4*>(sPsi + i * LDP + 4 * ty);
+    float b[CPT];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) a[r] = sPsi[i * ldp + ty + 16 * (r0 + r)];
+    for (int cc = 0; cc < CPT; ++cc) b[cc] = W[i * VS + tx + 16 * cc];
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) b[cc] = W[i * VS + tx + 16 * cc];
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int cc = 0; cc < CPT; ++cc) acc[r][cc] = fmaf(a[r], b[cc], acc[r][cc]);
+    for (int cc = 0; cc < CPT; ++cc) {
+      acc[0][cc] = fmaf(a.x, b[cc], acc[0][cc]);
+      acc[1][cc] = fmaf(a.y, b[cc], acc[1][cc]);
+      acc[2][cc] = fmaf(a.z, b[cc], acc[2][cc]);
+      acc[3][cc] = fmaf(a.w, b[cc], acc[3][cc]);
     }
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) S[(f0 + ty + 16 * (r0 + r)) * VS + tx + 16 * cc] += acc[r][cc];
   }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int cc = 0; cc < CPT; ++cc) S[(f0 + 4 * ty + j) * VS + tx + 16 * cc] += acc[j][cc];
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -263,23 +285,25 @@ __device__ __forceinline__ void state_update(float* S, const float* sPsi, int ld
 // F x VS state H lives in shared memory.
 // ------------------------------------------------------------------------------------------------
 template <typename T, int VS>
-__global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
-  extern __shared__ float sm[];
-  const int D = p.D, M = p.M, E = D / M, ldk = D + 1, ldp = FB + 1;
+__global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F) {
+  extern __shared__ __align__(16) float sm[];
+  const int D = p.D, M = p.M, E = D / M, ldk = D + 1;
   constexpr int CPT = VS / 16;
   float* sH = sm;                    // F x VS
-  float* sPsi = sH + F * VS;         // 64 x (FB+1)
-  float* sK = sPsi + C * ldp;        // 64 x (D+1)
+  float* sPsi = sH + F * VS;         // 64 x LDP
+  float* sK = sPsi + C * LDP;        // 64 x (D+1)
   float* sT = sK + C * ldk;          // 64 x 65 (Tm)
   float* sL = sT + C * LDT;          // 64 x 65 (kappa, strictly lower)
   float* sR = sL + C * LDT;          // 64 x VS: rhs, then U
   float* sE = sR + C * VS;           // 64 x VS
   float* sB = sE + C * VS;           // 64
+  unsigned short* sTab = reinterpret_cast<unsigned short*>(sB + C);  // F
   const int v0 = blockIdx.x * VS, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;
   const T* k = static_cast<const T*>(p.k) + rowbase * D;
   const T* v = static_cast<const T*>(p.v) + rowbase * p.Dv + v0;
   for (int i = threadIdx.x; i < F * VS; i += NT) sH[i] = 0.f;
+  build_feature_table(sTab, E, F);
   const int nch = (p.T + C - 1) / C;
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   for (int ch = 0; ch < nch; ++ch) {
@@ -295,9 +319,9 @@ __global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
     // E = psi(K) H, block by block over the features
     for (int f0 = 0; f0 < F; f0 += FB) {
       __syncthreads();
-      build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+      build_psi(sPsi, sK, ldk, E, M, f0, sTab, p.scale);
       __syncthreads();
-      psi_times_state<VS>(sE, sPsi, ldp, sH, f0, FB, 1.f);
+      psi_times_state<VS>(sE, sPsi, sH, f0, 1.f);
     }
     __syncthreads();
     // rhs = beta (V - E) in place of V
@@ -341,10 +365,10 @@ __global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
     for (int f0 = F - FB; f0 >= 0; f0 -= FB) {
       if (f0 != F - FB) {
         __syncthreads();
-        build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+        build_psi(sPsi, sK, ldk, E, M, f0, sTab, p.scale);
       }
       __syncthreads();
-      state_update<VS>(sH, sPsi, ldp, sR, f0, FB);
+      state_update<VS>(sH, sPsi, sR, f0);
     }
   }
   if (p.S) {  // final state, unpacked to the full E x E feature grid: S[a,b] = S[b,a] = H_f / w_ab
@@ -353,9 +377,7 @@ __global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
     float* out = p.S + static_cast<size_t>(bh) * E * E * p.Dv + v0;
     for (int idx = threadIdx.x; idx < Fsym * VS; idx += NT) {
       const int f = idx / VS, c = idx % VS;
-      int a = 0;
-      while (a + 1 < E && tri_start(a + 1, E) <= f) ++a;
-      const int bcol = a + (f - tri_start(a, E));
+      const int a = sTab[f] >> 8, bcol = sTab[f] & 0xff;
       const float val = sH[f * VS + c] * (a == bcol ? 1.f : 0.70710678118654752f);
       out[static_cast<size_t>(a * E + bcol) * p.Dv + c] = val;
       out[static_cast<size_t>(bcol * E + a) * p.Dv + c] = val;
@@ -367,21 +389,23 @@ __global__ void __launch_bounds__(NT) delta_u_scan_kernel(DP p, int F, int FB) {
 // y_scan (backward): Y_c = Tm_c^T (dU_c - psi(K_c) G),  G += psi(K_c)^T (beta Y_c), reverse order
 // ------------------------------------------------------------------------------------------------
 template <typename T, int VS>
-__global__ void __launch_bounds__(NT) delta_y_scan_kernel(DP p, int F, int FB) {
-  extern __shared__ float sm[];
-  const int D = p.D, M = p.M, E = D / M, ldk = D + 1, ldp = FB + 1;
+__global__ void __launch_bounds__(NT) delta_y_scan_kernel(DP p, int F) {
+  extern __shared__ __align__(16) float sm[];
+  const int D = p.D, M = p.M, E = D / M, ldk = D + 1;
   constexpr int CPT = VS / 16;
   float* sG = sm;
   float* sPsi = sG + F * VS;
-  float* sK = sPsi + C * ldp;
+  float* sK = sPsi + C * LDP;
   float* sT = sK + C * ldk;
   float* sX = sT + C * LDT;   // 64 x VS: dU - psi G, then beta Y
   float* sB = sX + C * VS;
+  unsigned short* sTab = reinterpret_cast<unsigned short*>(sB + C);
   const int v0 = blockIdx.x * VS, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;
   const T* k = static_cast<const T*>(p.k) + rowbase * D;
   const T* dU = static_cast<const T*>(p.dU) + rowbase * p.Dv + v0;
   for (int i = threadIdx.x; i < F * VS; i += NT) sG[i] = 0.f;
+  build_feature_table(sTab, E, F);
   const int nch = (p.T + C - 1) / C;
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   for (int ch = nch - 1; ch >= 0; --ch) {
@@ -394,9 +418,9 @@ __global__ void __launch_bounds__(NT) delta_y_scan_kernel(DP p, int F, int FB) {
       sB[i] = c0 + i < p.T ? p.beta[rowbase + static_cast<size_t>(c0 + i) * p.H] : 0.f;
     for (int f0 = 0; f0 < F; f0 += FB) {
       __syncthreads();
-      build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+      build_psi(sPsi, sK, ldk, E, M, f0, sTab, p.scale);
       __syncthreads();
-      psi_times_state<VS>(sX, sPsi, ldp, sG, f0, FB, -1.f);
+      psi_times_state<VS>(sX, sPsi, sG, f0, -1.f);
     }
     __syncthreads();
     // Y = Tm^T X  (Y_i = sum_{j>=i} Tm[j][i] X_j)
@@ -425,10 +449,10 @@ __global__ void __launch_bounds__(NT) delta_y_scan_kernel(DP p, int F, int FB) {
     for (int f0 = F - FB; f0 >= 0; f0 -= FB) {
       if (f0 != F - FB) {
         __syncthreads();
-        build_psi(sPsi, ldp, sK, ldk, E, M, f0, FB, p.scale);
+        build_psi(sPsi, sK, ldk, E, M, f0, sTab, p.scale);
       }
       __syncthreads();
-      state_update<VS>(sG, sPsi, ldp, sX, f0, FB);
+      state_update<VS>(sG, sPsi, sX, f0);
     }
   }
 }
@@ -536,31 +560,23 @@ unsigned warp_blocks(long rows) { return static_cast<unsigned>((rows * 32 + NT -
 
 size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Value columns per scan CTA: 16 when the CTAs then fill the GPU, wider slices otherwise would
-// only serialise more work per CTA.  Dv must be a multiple of 16.
-int pick_vs(int F, int Dv) {
-  (void)F;
-  return Dv % 16 == 0 ? 16 : 0;
-}
-
-// Number of psi features: the upper triangle of E x E, padded to a multiple of 64.
+// Value columns per scan CTA: 32 when the F x 32 state fits beside the tiles (two CTAs per SM at
+// E = 16), else 16.
 int feat_dim(int E) { return (E * (E + 1) / 2 + 63) / 64 * 64; }
-// Feature block held in shared memory at a time (a multiple of 64 dividing F).
-int pick_fb(int F) { return F <= 256 ? F : ((F <= 1024 && F % 128 == 0) ? 128 : 64); }
+int pick_vs(int F, int Dv) { return (Dv % 32 == 0 && F <= 640) ? 32 : 16; }
 
-size_t scan_smem(int F, int FB, int D, int vs, bool y);
-size_t scan_smem(int F, int FB, int D, int vs, bool y) {
-  const size_t f = static_cast<size_t>(F) * vs + C * (FB + 1) + C * (D + 1) + C * LDT * (y ? 1 : 2) + C +
+size_t scan_smem(int F, int D, int vs, bool y) {
+  const size_t f = static_cast<size_t>(F) * vs + C * LDP + C * (D + 1) + C * LDT * (y ? 1 : 2) + C +
                    C * vs * (y ? 1 : 2);
-  return f * sizeof(float);
+  return f * sizeof(float) + static_cast<size_t>(F) * sizeof(unsigned short);
 }
 
 template <typename K>
-int launch_k(K kernel, dim3 grid, size_t smem, cudaStream_t st, const DP& p, int F, int FB) {
+int launch_k(K kernel, dim3 grid, size_t smem, cudaStream_t st, const DP& p, int F) {
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return KATA_ERR_CUDA;
-  kernel<<<grid, NT, smem, st>>>(p, F, FB);
+  kernel<<<grid, NT, smem, st>>>(p, F);
   return from_cuda(cudaGetLastError());
 }
 
@@ -577,16 +593,18 @@ int run_prep(const DP& p, cudaStream_t st) {
 
 template <typename T>
 int run_u_scan(const DP& p, cudaStream_t st) {
-  const int E = p.D / p.M, F = feat_dim(E), FB = pick_fb(F);
-  const dim3 grid(p.Dv / 16, p.B * p.H);
-  return launch_k(delta_u_scan_kernel<T, 16>, grid, scan_smem(F, FB, p.D, 16, false), st, p, F, FB);
+  const int F = feat_dim(p.D / p.M), vs = pick_vs(F, p.Dv);
+  const dim3 grid(p.Dv / vs, p.B * p.H);
+  if (vs == 32) return launch_k(delta_u_scan_kernel<T, 32>, grid, scan_smem(F, p.D, 32, false), st, p, F);
+  return launch_k(delta_u_scan_kernel<T, 16>, grid, scan_smem(F, p.D, 16, false), st, p, F);
 }
 
 template <typename T>
 int run_y_scan(const DP& p, cudaStream_t st) {
-  const int E = p.D / p.M, F = feat_dim(E), FB = pick_fb(F);
-  const dim3 grid(p.Dv / 16, p.B * p.H);
-  return launch_k(delta_y_scan_kernel<T, 16>, grid, scan_smem(F, FB, p.D, 16, true), st, p, F, FB);
+  const int F = feat_dim(p.D / p.M), vs = pick_vs(F, p.Dv);
+  const dim3 grid(p.Dv / vs, p.B * p.H);
+  if (vs == 32) return launch_k(delta_y_scan_kernel<T, 32>, grid, scan_smem(F, p.D, 32, true), st, p, F);
+  return launch_k(delta_y_scan_kernel<T, 16>, grid, scan_smem(F, p.D, 16, true), st, p, F);
 }
 
 int check(int dtype, int B, int T, int H, int D, int Dv, int M) {
@@ -594,7 +612,7 @@ int check(int dtype, int B, int T, int H, int D, int Dv, int M) {
   if (B < 1 || T < 1 || H < 1 || D < 1 || Dv < 1 || M < 1 || D % M) return KATA_ERR_SHAPE;
   const int E = D / M;
   if (M > 4 || D > 256 || Dv > 256 || Dv % 16 || E % 8 || E > 64) return KATA_ERR_UNSUPPORTED;
-  if (scan_smem(feat_dim(E), pick_fb(feat_dim(E)), D, 16, false) > 227 * 1024) return KATA_ERR_UNSUPPORTED;
+  if (scan_smem(feat_dim(E), D, pick_vs(feat_dim(E), Dv), false) > 227 * 1024) return KATA_ERR_UNSUPPORTED;
   return KATA_OK;
 }
 
