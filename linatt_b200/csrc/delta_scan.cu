@@ -50,12 +50,32 @@ struct DP {
   float scale;
 };
 
+// ------------------------------------------------------------------------------------------------
+// 64 rows x `cols` values (row t0 + r at base + (t0 + r) * stride) into an fp32 tile with row stride
+// lds; rows past T are zero.  16-byte vector loads, four in flight per thread.
+// ------------------------------------------------------------------------------------------------
 template <typename T>
-__device__ __forceinline__ void load_rows(float* s, int lds, const T* base, size_t stride, int t0, int n, int cols,
-                                          int T_) {
-  for (int i = threadIdx.x; i < n * cols; i += NT) {
-    const int r = i / cols, c = i - r * cols, t = t0 + r;
-    s[r * lds + c] = t < T_ ? to_f32<T>(base[static_cast<size_t>(t) * stride + c]) : 0.f;
+__device__ __forceinline__ void load_tile_v(float* s, int lds, const T* base, size_t stride, int t0, int cols, int T_) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int cpr = cols / VEC, total = C * cpr;
+  for (int i0 = 0; i0 < total; i0 += NT * 4) {
+    uint4 buf[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int idx = i0 + threadIdx.x + NT * m, r = idx / cpr, c = (idx - r * cpr) * VEC;
+      buf[m] = (idx < total && t0 + r < T_)
+                   ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t0 + r) * stride + c)
+                   : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int idx = i0 + threadIdx.x + NT * m, r = idx / cpr, c = (idx - r * cpr) * VEC;
+      if (idx < total) {
+        const T* e = reinterpret_cast<const T*>(&buf[m]);
+#pragma unroll
+        for (int x = 0; x < VEC; ++x) s[r * lds + c + x] = to_f32<T>(e[x]);
+      }
+    }
   }
 }
 
@@ -73,7 +93,7 @@ __global__ void __launch_bounds__(NT) delta_prep_kernel(DP p) {
   const int c0 = blockIdx.x * C, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;  // + t*H
   const T* k = static_cast<const T*>(p.k) + rowbase * D;
-  load_rows<T>(sK, ldk, k, static_cast<size_t>(p.H) * D, c0, C, D, p.T);
+  load_tile_v<T>(sK, ldk, k, static_cast<size_t>(p.H) * D, c0, D, p.T);
   for (int i = threadIdx.x; i < C; i += NT) sB[i] = c0 + i < p.T ? p.beta[(rowbase + static_cast<size_t>(c0 + i) * p.H)] : 0.f;
   __syncthreads();
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
@@ -138,35 +158,6 @@ __global__ void __launch_bounds__(NT) delta_prep_kernel(DP p) {
   for (int i = threadIdx.x; i < C * C; i += NT) {
     const int r = i >> 6, c = i & 63, t = c0 + r;
     if (t < p.T) p.Tm[(rowbase + static_cast<size_t>(t) * p.H) * C + c] = sX[r * LDT + c];
-  }
-}
-
-// ------------------------------------------------------------------------------------------------
-// 64 rows x `cols` values (row t0 + r at base + (t0 + r) * stride) into an fp32 tile with row stride
-// lds; rows past T are zero.  16-byte vector loads, four in flight per thread.
-// ------------------------------------------------------------------------------------------------
-template <typename T>
-__device__ __forceinline__ void load_tile_v(float* s, int lds, const T* base, size_t stride, int t0, int cols, int T_) {
-  constexpr int VEC = 16 / sizeof(T);
-  const int cpr = cols / VEC, total = C * cpr;
-  for (int i0 = 0; i0 < total; i0 += NT * 4) {
-    uint4 buf[4];
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int idx = i0 + threadIdx.x + NT * m, r = idx / cpr, c = (idx - r * cpr) * VEC;
-      buf[m] = (idx < total && t0 + r < T_)
-                   ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(t0 + r) * stride + c)
-                   : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int idx = i0 + threadIdx.x + NT * m, r = idx / cpr, c = (idx - r * cpr) * VEC;
-      if (idx < total) {
-        const T* e = reinterpret_cast<const T*>(&buf[m]);
-#pragma unroll
-        for (int x = 0; x < VEC; ++x) s[r * lds + c + x] = to_f32<T>(e[x]);
-      }
-    }
   }
 }
 

@@ -27,7 +27,7 @@ namespace {
 constexpr int CH = 64;    // chunk length
 constexpr int DK = 64;    // key dim (this build)
 constexpr int DV = 64;    // value dim (this build)
-constexpr int LD = 65;    // padded row of every 64-wide fp32 shared tile
+constexpr int LD = 68;    // row of every 64-wide fp32 shared tile: 16-byte aligned, rows 4 banks apart
 constexpr int TILE = CH * LD;
 constexpr int NT = 256;   // threads of every kernel
 constexpr int VS = 16;    // value columns per CTA of the sequential scans
@@ -107,22 +107,42 @@ __device__ __forceinline__ void seq_range(const GdnParams& p, int n, int& bos, i
   }
 }
 
-// ---- 64x64 fp32 tile products from shared memory (LD-padded): thread (ty, tx) owns rows ty+16r,
-// columns tx+16c.  A(i,k) = TA ? A[k][i] : A[i][k];  B(k,j) = TB ? B[j][k] : B[k][j].
+// ---- 64x64 fp32 tile products from shared memory (LD-strided rows): thread (ty, tx) owns rows
+// ty+16r, columns tx+16c.  A(i,k) = TA ? A[k][i] : A[i][k];  B(k,j) = TB ? B[j][k] : B[k][j].
+// Operands stored row-major along k (A with TA false, B with TB true) are read four k at a time
+// with 16-byte loads.
 template <bool TA, bool TB>
 __device__ __forceinline__ void mm(float (&acc)[4][4], const float* A, const float* B) {
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-#pragma unroll 8
-  for (int k = 0; k < 64; ++k) {
-    float a[4], b[4];
+#pragma unroll 2
+  for (int k = 0; k < 64; k += 4) {
+    float a[4][4], b[4][4];  // a[r][j] = A(row ty+16r, k+j),  b[c][j] = B(k+j, col tx+16c)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) a[r] = TA ? A[k * LD + ty + 16 * r] : A[(ty + 16 * r) * LD + k];
+    for (int r = 0; r < 4; ++r) {
+      if (!TA) {
+        const float4 v = *reinterpret_cast<const float4*>(A + (ty + 16 * r) * LD + k);
+        a[r][0] = v.x; a[r][1] = v.y; a[r][2] = v.z; a[r][3] = v.w;
+      } else {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) b[c] = TB ? B[(tx + 16 * c) * LD + k] : B[k * LD + tx + 16 * c];
+        for (int j = 0; j < 4; ++j) a[r][j] = A[(k + j) * LD + ty + 16 * r];
+      }
+    }
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int c = 0; c < 4; ++c) {
+      if (TB) {
+        const float4 v = *reinterpret_cast<const float4*>(B + (tx + 16 * c) * LD + k);
+        b[c][0] = v.x; b[c][1] = v.y; b[c][2] = v.z; b[c][3] = v.w;
+      } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(a[r], b[c], acc[r][c]);
+        for (int j = 0; j < 4; ++j) b[c][j] = B[(k + j) * LD + tx + 16 * c];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(a[r][j], b[c][j], acc[r][c]);
   }
 }
 
@@ -207,7 +227,7 @@ __device__ __forceinline__ void chunk_cumsum(float* sGam, const float* sg) {
 // ------------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(NT) gdn_prep_kernel(GdnParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   float* sK = sm;            // k rows
   float* sL = sK + TILE;     // L, then Tm
   float* sX0 = sL + TILE;    // identity -> Tm
@@ -429,7 +449,7 @@ __global__ void __launch_bounds__(NT) gdn_state_kernel(GdnParams p) {
 // ------------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(NT) gdn_out_kernel(GdnParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   float* sQ = sm;
   float* sK = sQ + TILE;
   float* sS = sK + TILE;
@@ -479,7 +499,7 @@ __global__ void __launch_bounds__(NT) gdn_out_kernel(GdnParams p) {
 // ------------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(NT) gdn_dvl_kernel(GdnParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   float* sQ = sm;
   float* sK = sQ + TILE;
   float* sDO = sK + TILE;
@@ -623,7 +643,7 @@ __global__ void __launch_bounds__(NT) gdn_dstate_kernel(GdnParams p) {
 // ------------------------------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(NT) gdn_grad_kernel(GdnParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   float* sQ = sm;
   float* sK = sQ + TILE;
   float* sU = sK + TILE;
