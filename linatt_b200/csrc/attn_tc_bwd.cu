@@ -57,6 +57,7 @@ struct BwdSmem {
   static constexpr int DQ_OFF_RING = DQ_OFF_O + O_BYTES;
   static constexpr int DQ_OFF_W = DQ_OFF_RING + kRing * ITEM;
   static constexpr int DQ_TOTAL = DQ_OFF_W + T_BYTES;
+  static constexpr int DQR_TOTAL = DQ_OFF_RING + 4 * ITEM;  // dq ring kernel: four K/V slots, no W tile
   // dkdv kernel: K, V resident; ring of Q/dO tiles; two tiles that alternately receive W^T_p
   // (for dK) and P^T (for dV), in the order W_0..W_{NP-1}, P, W_0, ... of the query tiles
   static constexpr int KV_OFF_K = 0;
@@ -500,9 +501,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // pairs), which the dQ chain reads as its A operand.  Before the issuer reuses a slot it waits for
 // the compute warps to release it and, if it held a W, issues that W's dQ chain first (MMAs of one
 // CTA execute in issue order).  So score MMAs run up to two items ahead of the compute warps.
+constexpr int kRingDQ = 4;  // K/V ring depth of the dq ring kernel (two key tiles in flight)
+
 struct DqRingBars {
   uint64_t qo_full;
-  uint64_t ring_full[kRing], ring_empty[kRing];
+  uint64_t ring_full[kRingDQ], ring_empty[kRingDQ];
   uint64_t i_full[3], i_free[3];
   uint64_t acc_done, drain;
   uint32_t tmem_base;
@@ -541,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     bars.abort_flag = 0;
     mbar_init(&bars.qo_full, 1);
-    for (int i = 0; i < kRing; ++i) {
+    for (int i = 0; i < kRingDQ; ++i) {
       mbar_init(&bars.ring_full[i], 1);
       mbar_init(&bars.ring_empty[i], 1);
     }
@@ -577,8 +580,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < nk && ok; ++j) {
         for (int item = 0; item < 2; ++item, ++r) {  // V_j then K_j
-          const int slot = r % kRing;
-          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
+          const int slot = r % kRingDQ;
+          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRingDQ) & 1) ^ 1, wc)) {
             ok = false;
             break;
           }
@@ -595,8 +598,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) {
-        for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
-          mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
+        for (int rr = (r > kRingDQ ? r - kRingDQ : 0); rr < r; ++rr)
+          mbar_drain(&bars.ring_full[rr % kRingDQ], (rr / kRingDQ) & 1);
       }
     }
   } else if (warp == 1) {
@@ -628,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int pj = prev / kItems, pp = pq - 1;
               const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
               const bool first = (pj == 0) && (!SUM || gb == 0);
-              const int kslot = (2 * pj + 1) % kRing;
+              const int kslot = (2 * pj + 1) % kRingDQ;
               const uint64_t kd = mnmajor_desc<CW>(sRing + kslot * L::ITEM, gb * E / CW, 0);
               const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
               tc_fence_after();
@@ -646,8 +649,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // ---- issue item (j, q) into slot x
           if (q == 0) {  // dN = dO V_j^T
-            const int slotV = r % kRing;
-            if (!mbar_wait(&bars.ring_full[slotV], (r / kRing) & 1, wc)) {
+            const int slotV = r % kRingDQ;
+            if (!mbar_wait(&bars.ring_full[slotV], (r / kRingDQ) & 1, wc)) {
               ok = false;
               break;
             }
@@ -660,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit(&bars.i_full[x]);
             umma_commit(&bars.ring_empty[slotV]);
             r += 1;
-            if (!mbar_wait(&bars.ring_full[r % kRing], (r / kRing) & 1, wc)) {  // K_j
+            if (!mbar_wait(&bars.ring_full[r % kRingDQ], (r / kRingDQ) & 1, wc)) {  // K_j
               ok = false;
               break;
             }
@@ -668,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {  // S_p = Q_a K_b^T
             const int pp = q - 1;
             const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-            const int slotK = (2 * j + 1) % kRing;
+            const int slotK = (2 * j + 1) % kRingDQ;
             tc_fence_after();
             const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0);
             const uint64_t kd = kmajor_desc<CW>(sRing + slotK * L::ITEM, gb, E, 0);
@@ -1303,7 +1306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NVBOX = DV / VCW;
   constexpr int NP = SUM ? M * M : M;
   constexpr int kItems = 1 + NP;
-  constexpr int kR = 4;  // dO / Q ring depth
+  constexpr int kR = 4;  // dO / Q ring depth (two query tiles in flight)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kColDK = 256, kColDV = 384;
   using L = BwdSmem<D, DV>;
@@ -1682,7 +1685,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (p.phases != 2) {
     // decay needs sum_p S_p^2 for its dc row sums and keeps the two-slot kernel; otherwise the ring
     auto kern = DECAY ? attn_bwd_dq_tc<T, D, DV, M, SUM, DECAY> : attn_bwd_dq_ring_tc<T, D, DV, M, SUM>;
-    const size_t smem = L::DQ_TOTAL + 1024;
+    const size_t smem = (DECAY ? L::DQ_TOTAL : L::DQR_TOTAL) + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
