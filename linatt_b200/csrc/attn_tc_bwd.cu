@@ -607,32 +607,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int kItems = 1 + NP;  // items per key tile: dN, then S_0..S_{NP-1}
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
       const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
-      const uint32_t sQ = smem_u32(smem + L::DQ_OFF_Q);
-      const uint32_t sO = smem_u32(smem + L::DQ_OFF_O);
       const uint32_t sRing = smem_u32(smem + L::DQ_OFF_RING);
+      // Descriptor bases; every operand below is a compile-time or ring-slot-multiple offset from
+      // one of these (no descriptor is rebuilt inside the loops).
+      const uint64_t od0 = kmajor_desc<VCW>(smem_u32(smem + L::DQ_OFF_O), 0, DV, 0);  // dO, K-major
+      const uint64_t qd0 = kmajor_desc<CW>(smem_u32(smem + L::DQ_OFF_Q), 0, E, 0);    // Q, K-major
+      const uint64_t rv0 = kmajor_desc<VCW>(sRing, 0, DV, 0);  // V in ring slot 0, K-major
+      const uint64_t rk0 = kmajor_desc<CW>(sRing, 0, E, 0);    // K in ring slot 0, K-major
+      const uint64_t rkm0 = mnmajor_desc<CW>(sRing, 0, 0);     // K in ring slot 0, MN-major
       bool ok = mbar_wait(&bars.qo_full, 0, wc);
-      // Item `it` lives in slot it % 3.  The previous occupant of that slot is item it - 3; if it was
-      // a score part, its W is in the slot and its dQ chain is issued before the slot is reused.
+      // Item `it` = j * kItems + q lives in slot it % 3.  The previous occupant of that slot is item
+      // it - 3; if it was a score part, its W is in the slot and its dQ chain is issued before the
+      // slot is reused.  After the last tile, three claims drain the pending chains.  The ring
+      // holds V_j at position 2j and K_j at 2j + 1 (kRingDQ = 4: slot (2j + c) & 3, use parity
+      // (j >> 1) & 1).
+      static_assert(kRingDQ == 4, "ring positions below assume four slots");
       int it = 0, x = 0;       // x = it % 3
       uint32_t use_par = 0;    // parity of (it / 3), i.e. of the current use of slot x
-      int r = 0;
-      for (int j = 0; ok && j <= nk; ++j) {
-        const int n_items = (j < nk) ? kItems : 3;  // after the last tile: three drain claims
-        for (int q = 0; q < n_items; ++q) {
+      const int n_claims = nk * kItems + 3;
+      for (int j = 0; ok && it < n_claims; ++j) {
+#pragma unroll
+        for (int q = 0; q < kItems; ++q) {
+          if (it >= n_claims) break;
           // ---- claim slot x for item it
           if (it >= 3) {
             if (!mbar_wait(&bars.i_free[x], use_par ^ 1, wc)) {
               ok = false;
               break;
             }
-            const int prev = it - 3;
-            const int pq = prev % kItems;
-            if (pq > 0) {  // issue the pending dQ chain of score part pq - 1 of tile prev / kItems
-              const int pj = prev / kItems, pp = pq - 1;
+            // item it - 3: type pq and tile j + pdj, both compile-time offsets of (j, q)
+            const int pq = ((q - 3) % kItems + kItems) % kItems;
+            const int pdj = (q - 3 - pq) / kItems;
+            if (pq > 0) {  // issue the pending dQ chain of score part pq - 1 of tile j + pdj
+              const int pj = j + pdj, pp = pq - 1;
               const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
               const bool first = (pj == 0) && (!SUM || gb == 0);
-              const int kslot = (2 * pj + 1) % kRingDQ;
-              const uint64_t kd = mnmajor_desc<CW>(sRing + kslot * L::ITEM, gb * E / CW, 0);
+              const int kslot = (2 * pj + 1) & 3;
+              const uint64_t kd = rkm0 + desc_units(static_cast<uint32_t>(kslot) * L::ITEM) + mnmajor_boff<CW>(gb * E / CW);
               const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
               tc_fence_after();
 #pragma unroll
@@ -642,42 +653,41 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (pp == NP - 1) umma_commit(&bars.ring_empty[kslot]);  // K tile no longer needed
             }
           }
-          if (j == nk) {  // drain claim only
+          if (j >= nk) {  // drain claim only
             ++it;
             if (++x == 3) { x = 0; use_par ^= 1; }
             continue;
           }
           // ---- issue item (j, q) into slot x
+          const uint32_t ring_par = static_cast<uint32_t>(j >> 1) & 1u;
+          const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
           if (q == 0) {  // dN = dO V_j^T
-            const int slotV = r % kRingDQ;
-            if (!mbar_wait(&bars.ring_full[slotV], (r / kRingDQ) & 1, wc)) {
+            const int slotV = (2 * j) & 3;
+            if (!mbar_wait(&bars.ring_full[slotV], ring_par, wc)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t od = kmajor_desc<VCW>(sO, 0, DV, 0);
-            const uint64_t vd = kmajor_desc<VCW>(sRing + slotV * L::ITEM, 0, DV, 0);
+            const uint64_t vd = rv0 + desc_units(static_cast<uint32_t>(slotV) * L::ITEM);
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk)
-              umma_ss(tbase + x * 128u, od + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+              umma_ss(sd, od0 + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
             umma_commit(&bars.i_full[x]);
             umma_commit(&bars.ring_empty[slotV]);
-            r += 1;
-            if (!mbar_wait(&bars.ring_full[r % kRingDQ], (r / kRingDQ) & 1, wc)) {  // K_j
+            if (!mbar_wait(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
               ok = false;
               break;
             }
-            r += 1;
           } else {  // S_p = Q_a K_b^T
             const int pp = q - 1;
             const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-            const int slotK = (2 * j + 1) % kRingDQ;
+            const int slotK = (2 * j + 1) & 3;
             tc_fence_after();
-            const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0);
-            const uint64_t kd = kmajor_desc<CW>(sRing + slotK * L::ITEM, gb, E, 0);
+            const uint64_t qd = qd0 + kmajor_goff<CW>(ga, E);
+            const uint64_t kd = rk0 + desc_units(static_cast<uint32_t>(slotK) * L::ITEM) + kmajor_goff<CW>(gb, E);
 #pragma unroll
             for (int kk = 0; kk < E / 16; ++kk)
-              umma_ss(tbase + x * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+              umma_ss(sd, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
             umma_commit(&bars.i_full[x]);
           }
           ++it;
@@ -1412,30 +1422,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
       const uint32_t id_dk = umma_idesc_f16(128, E, kBF16, false, true);
       const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
-      const uint32_t sK = smem_u32(smem + L::KV_OFF_K);
-      const uint32_t sV = smem_u32(smem + L::KV_OFF_V);
       const uint32_t sRing = smem_u32(smem + L::KR_OFF_RING);
+      // Descriptor bases; every operand below is a compile-time or ring-slot-multiple offset from
+      // one of these (no descriptor is rebuilt inside the loops).
+      const uint64_t kd0 = kmajor_desc<CW>(smem_u32(smem + L::KV_OFF_K), 0, E, 0);     // K, K-major
+      const uint64_t vd0 = kmajor_desc<VCW>(smem_u32(smem + L::KV_OFF_V), 0, DV, 0);  // V, K-major
+      const uint64_t ro0 = kmajor_desc<VCW>(sRing, 0, DV, 0);  // dO in ring slot 0, K-major
+      const uint64_t rom0 = mnmajor_desc<VCW>(sRing, 0, 0);    // dO in ring slot 0, MN-major
+      const uint64_t rq0 = kmajor_desc<CW>(sRing, 0, E, 0);    // Q in ring slot 0, K-major
+      const uint64_t rqm0 = mnmajor_desc<CW>(sRing, 0, 0);     // Q in ring slot 0, MN-major
       bool ok = mbar_wait(&bars.kv_full, 0, wc);
-      // Item `it` lives in slot it % 2; before reuse, the pending chains of item it - 2 are issued.
+      // Item `it` = n * kItems + q lives in slot it % 2; before reuse, the pending chains of item
+      // it - 2 are issued.  After the last pair, two claims drain the pending chains.  The ring
+      // holds dO_n at position 2n and Q_n at 2n + 1 (kR = 4: slot (2n + c) & 3, use parity
+      // (n >> 1) & 1).
+      static_assert(kR == 4, "ring positions below assume four slots");
       int it = 0, x = 0;
       uint32_t use_par = 0;
-      for (int n = 0; ok && n <= nwork; ++n) {
-        const int n_items = (n < nwork) ? kItems : 2;  // after the last pair: two drain claims
-        const int slotO = (2 * n) % kR, slotQ = (2 * n + 1) % kR;
-        for (int q = 0; q < n_items; ++q) {
+      const int n_claims = nwork * kItems + 2;
+      for (int n = 0; ok && it < n_claims; ++n) {
+        const int slotO = (2 * n) & 3, slotQ = (2 * n + 1) & 3;
+        const uint32_t ring_par = static_cast<uint32_t>(n >> 1) & 1u;
+#pragma unroll
+        for (int q = 0; q < kItems; ++q) {
+          if (it >= n_claims) break;
           if (it >= 2) {
             if (!mbar_wait(&bars.i_free[x], use_par ^ 1, wc)) {
               ok = false;
               break;
             }
-            const int prev = it - 2;
-            const int pq = prev % kItems;
+            // item it - 2: type pq and pair n + pdn, both compile-time offsets of (n, q)
+            const int pq = ((q - 2) % kItems + kItems) % kItems;
+            const int pdn = (q - 2 - pq) / kItems;
             if (pq > 0) {
-              const int pn = prev / kItems, pp = pq - 1;
+              const int pn = n + pdn, pp = pq - 1;
               const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
               const bool first = (pn == 0) && (!SUM || ga == 0);
-              const uint32_t psQ = sRing + static_cast<uint32_t>((2 * pn + 1) % kR) * L::ITEM;
-              const uint64_t qd = mnmajor_desc<CW>(psQ, ga * E / CW, 0);
+              const int psQ = (2 * pn + 1) & 3;
+              const uint64_t qd = rqm0 + desc_units(static_cast<uint32_t>(psQ) * L::ITEM) + mnmajor_boff<CW>(ga * E / CW);
               const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
               tc_fence_after();
 #pragma unroll
@@ -1443,35 +1467,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_ts(tbase + kColDK + gb * E, wa + packed_col(kk), qd + mnstep<CW>(kk), id_dk,
                         (!first || kk > 0) ? 1u : 0u);
               if (pp == NP - 1) {  // dV += P^T dO, then this pair's dO and Q tiles are free
-                const int psO = (2 * pn) % kR;
-                const uint64_t od = mnmajor_desc<VCW>(sRing + static_cast<uint32_t>(psO) * L::ITEM, 0, 0);
+                const int psO = (2 * pn) & 3;
+                const uint64_t od = rom0 + desc_units(static_cast<uint32_t>(psO) * L::ITEM);
 #pragma unroll
                 for (int kk = 0; kk < kTile / 16; ++kk)
                   umma_ts(tbase + kColDV, wa + packed_col(kk) + 32u, od + mnstep<VCW>(kk), id_dv,
                           (pn > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&bars.ring_empty[psO]);
-                umma_commit(&bars.ring_empty[(2 * pn + 1) % kR]);
+                umma_commit(&bars.ring_empty[psQ]);
               }
             }
           }
-          if (n == nwork) {
+          if (n >= nwork) {
             ++it;
             if (++x == 2) { x = 0; use_par ^= 1; }
             continue;
           }
+          const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
           if (q == 0) {  // dN^T = V dO_n^T
-            if (!mbar_wait(&bars.ring_full[slotO], ((2 * n) / kR) & 1, wc)) {
+            if (!mbar_wait(&bars.ring_full[slotO], ring_par, wc)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t vd = kmajor_desc<VCW>(sV, 0, DV, 0);
-            const uint64_t od = kmajor_desc<VCW>(sRing + static_cast<uint32_t>(slotO) * L::ITEM, 0, DV, 0);
+            const uint64_t od = ro0 + desc_units(static_cast<uint32_t>(slotO) * L::ITEM);
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk)
-              umma_ss(tbase + x * 128u, vd + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+              umma_ss(sd, vd0 + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
             umma_commit(&bars.i_full[x]);
-            if (!mbar_wait(&bars.ring_full[slotQ], ((2 * n + 1) / kR) & 1, wc)) {  // Q_n for the parts
+            if (!mbar_wait(&bars.ring_full[slotQ], ring_par, wc)) {  // Q_n for the parts
               ok = false;
               break;
             }
@@ -1479,11 +1503,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pp = q - 1;
             const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
             tc_fence_after();
-            const uint64_t kd = kmajor_desc<CW>(sK, gb, E, 0);
-            const uint64_t qd = kmajor_desc<CW>(sRing + static_cast<uint32_t>(slotQ) * L::ITEM, ga, E, 0);
+            const uint64_t kd = kd0 + kmajor_goff<CW>(gb, E);
+            const uint64_t qd = rq0 + desc_units(static_cast<uint32_t>(slotQ) * L::ITEM) + kmajor_goff<CW>(ga, E);
 #pragma unroll
             for (int kk = 0; kk < E / 16; ++kk)
-              umma_ss(tbase + x * 128u, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+              umma_ss(sd, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
             umma_commit(&bars.i_full[x]);
           }
           ++it;

@@ -48,6 +48,24 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int box0, int kk
                         box_bytes, 8u * CW * 2u, CW * 2);
 }
 
+// Descriptor arithmetic without rebuilding descriptors.  The start-address field holds the byte
+// address >> 4 in the low bits, so moving an operand by a multiple of 16 bytes is a plain add of
+// (bytes >> 4) to the descriptor (no carry out of the 14-bit field: shared-memory addresses stay
+// below 256 KB).  The MMA issuer is one thread whose every integer op is on the critical path of
+// the tensor pipe (a descriptor rebuilt per chain costs more issue time than a 128x128x16 MMA
+// takes to execute), so the issue loops use a base descriptor plus these compile-time offsets.
+__host__ __device__ constexpr uint64_t desc_units(uint32_t bytes) { return static_cast<uint64_t>(bytes >> 4); }
+// Offset of K-major group g (columns [g*E, (g+1)*E)) from group 0 of the same tile.
+template <int CW>
+__host__ __device__ constexpr uint64_t kmajor_goff(int g, int E) {
+  return desc_units(static_cast<uint32_t>((g * E / CW) * (kTile * CW * 2) + (g * E % CW) * 2));
+}
+// Offset of the MN-major N extent starting at box `box0` from box 0 of the same tile.
+template <int CW>
+__host__ __device__ constexpr uint64_t mnmajor_boff(int box0) {
+  return desc_units(static_cast<uint32_t>(box0 * kTile * CW * 2));
+}
+
 // K-major descriptor of K-step kk of a [128][128] 16-bit tile written by threads as two
 // 128B-swizzled boxes of 64 columns (P / dA tiles).
 __device__ __forceinline__ uint64_t kmajor128_desc(uint32_t base, int kk) {

@@ -152,64 +152,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_qk = umma_idesc_f16(128, kBK, kBF16, false, false);
       const uint32_t idesc_pv = umma_idesc_f16(128, DV, kBF16, false, true);
-      const uint32_t sQ = smem_u32(smem + L::OFF_Q);
+      // Descriptor bases (group 0, stage 0); every operand below is a compile-time or stage-multiple
+      // offset from one of these, so no descriptor is rebuilt inside the loops.
+      const uint64_t qd0 = kmajor_desc<CW>(smem_u32(smem + L::OFF_Q), 0, E, 0);
+      const uint64_t kd0 = kmajor_desc<CW>(smem_u32(smem + L::OFF_K), 0, E, 0);
+      const uint64_t vd0 = mnmajor_desc<VCW>(smem_u32(smem + L::OFF_V), 0, 0);
       bool ok = mbar_wait(&bars.q_full, 0, wc);
-      // O += P_i V_i with P_i read from TMEM slot `sl`
-      auto issue_pv = [&](int i, int sl) -> bool {
-        const int st = i % kStages;
+      // O += P_i V_i with P_i read from TMEM slot `sl`; V_i is in stage `vst` (use parity `vpar`)
+      auto issue_pv = [&](int i, int vst, uint32_t vpar, int sl) -> bool {
         if (!mbar_wait(&bars.p_full[i & 1], (i >> 1) & 1, wc)) return false;
-        if (!mbar_wait(&bars.v_full[st], (i / kStages) & 1, wc)) return false;
+        if (!mbar_wait(&bars.v_full[vst], vpar, wc)) return false;
         tc_fence_after();
-        const uint32_t sV = smem_u32(smem + L::OFF_V + st * L::V_BYTES);
-        const uint64_t vd = mnmajor_desc<VCW>(sV, 0, 0);
-        const uint32_t pa = tbase + sl * 128u;
+        const uint64_t vd = vd0 + desc_units(static_cast<uint32_t>(vst) * L::V_BYTES);
+        const uint32_t pa = tbase + static_cast<uint32_t>(sl) * 128u;
         const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
           umma_ts(tbase + kOCol, pa + packed_col(kk), vd + mnstep<VCW>(kk), idesc_pv, kk > 0 ? 1u : acc0);
-        umma_commit(&bars.v_empty[st]);
+        umma_commit(&bars.v_empty[vst]);
         return true;
       };
-      int u = 0;
-      int pend = -1, pend_slot = 0;  // key tile whose P*V chain is not issued yet, and its slot
+      // Score part u (u = j*NP + pp) goes to slot u % kSlots; the counters below carry the slot,
+      // the key stage j % kStages and the parities of their current uses.
+      int slot = 0, st = 0;
+      uint32_t slot_par = 0, st_par = 0;
+      // key tile whose P*V chain is not issued yet: its slot, V stage and stage parity
+      int pend = -1, pend_slot = 0, pend_st = 0;
+      uint32_t pend_par = 0;
       for (int j = 0; ok && j < nk; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&bars.k_full[st], (j / kStages) & 1, wc)) {
+        if (!mbar_wait(&bars.k_full[st], st_par, wc)) {
           ok = false;
           break;
         }
-        const uint32_t sK = smem_u32(smem + L::OFF_K + st * L::K_BYTES);
-        for (int pp = 0; pp < NP; ++pp, ++u) {
-          const int slot = u % kSlots;
-          if (pend >= 0 && slot == pend_slot) {
-            if (!issue_pv(pend, pend_slot)) {
+        const uint64_t kd = kd0 + desc_units(static_cast<uint32_t>(st) * L::K_BYTES);
+        int last_slot = 0;
+#pragma unroll
+        for (int pp = 0; pp < NP; ++pp) {
+          // The previous tile's P occupies the slot of its last part, (j*NP - 1) % kSlots, which
+          // part pp of this tile reaches first at pp = kSlots - 1: its P*V chain is issued before.
+          if (pp == kSlots - 1 && pend >= 0) {
+            if (!issue_pv(pend, pend_st, pend_par, pend_slot)) {
               ok = false;
               break;
             }
             pend = -1;
           }
-          if (!mbar_wait(&bars.s_free[slot], ((u / kSlots) & 1) ^ 1, wc)) {
+          if (!mbar_wait(&bars.s_free[slot], slot_par ^ 1, wc)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0), kd = kmajor_desc<CW>(sK, gb, E, 0);
+          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;  // constants once unrolled
+          const uint64_t qd = qd0 + kmajor_goff<CW>(ga, E), kdp = kd + kmajor_goff<CW>(gb, E);
+          const uint32_t sd = tbase + static_cast<uint32_t>(slot) * 128u;
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss(tbase + slot * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), idesc_qk, kk > 0 ? 1u : 0u);
+            umma_ss(sd, qd + kstep<CW>(kk), kdp + kstep<CW>(kk), idesc_qk, kk > 0 ? 1u : 0u);
           umma_commit(&bars.s_full[slot]);
+          last_slot = slot;
+          if (++slot == kSlots) {
+            slot = 0;
+            slot_par ^= 1;
+          }
         }
         if (!ok) break;
         umma_commit(&bars.k_empty[st]);
-        if (pend >= 0 && !issue_pv(pend, pend_slot)) {
+        if (pend >= 0 && !issue_pv(pend, pend_st, pend_par, pend_slot)) {
           ok = false;
           break;
         }
         pend = j;
-        pend_slot = (u - 1) % kSlots;
+        pend_slot = last_slot;
+        pend_st = st;
+        pend_par = st_par;
+        if (++st == kStages) {
+          st = 0;
+          st_par ^= 1;
+        }
       }
-      if (ok && pend >= 0) ok = issue_pv(pend, pend_slot);
+      if (ok && pend >= 0) ok = issue_pv(pend, pend_st, pend_par, pend_slot);
       if (ok) umma_commit(&bars.o_full);
       // drain outstanding MMAs before the CTA can retire
       umma_commit(&bars.drain);
