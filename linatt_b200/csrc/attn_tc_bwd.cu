@@ -120,6 +120,12 @@ __device__ __forceinline__ uint32_t bf2_pack(float2 v) {
 __device__ __forceinline__ float2 bf2_unpack(uint32_t u) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
 }
+// Packed bf16 product (round to nearest even), one instruction for two elements.
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 // ================================================================================================
 // dq kernel
@@ -739,9 +745,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (hc == 0) ws.delta[rowidx] = delta;
     }
     if (hc == 0) {  // every row of the tile, including rows past T (rden 1, delta 0)
+      // For the ring dk/dv kernel, pre-scaled: scale^2 / den and -scale^2 delta / den, so that
+      // there P^T = sum S^2 * v0 and dA''^T = dN * v0 + v1 are one packed op each (dK is doubled
+      // in its epilogue: W = 2 S dA'').
       const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
-      ws.rden[hm] = rden;
-      ws.dr[hm] = live ? delta * rden : 0.f;
+      const float scale2 = p.scale * p.scale;
+      ws.rden[hm] = rden * scale2;
+      ws.dr[hm] = live ? -delta * rden * scale2 : 0.f;
     }
     const float w_scale = 2.f * p.scale * p.scale;
     const float2 rden_w = make_float2(rden * w_scale, rden * w_scale);
@@ -1529,9 +1539,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sg = s0 + row;
     const bool live = sg < T_;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    const float w_scale = 2.f * p.scale * p.scale;
-    const float2 wsc2 = make_float2(w_scale, w_scale);
-    const float scale2 = p.scale * p.scale;
+    // The vectors hold v0 = scale^2 / den and v1 = -scale^2 delta / den per query (written by the
+    // dq pass), so dA''^T = dN^T v0 + v1 and P^T = v0 sum_p (S^T_p)^2; W''^T_p = S^T_p dA''^T is
+    // half of the true W^T_p, and the dK epilogue doubles the accumulator.
     bool ok = true;
     int it = 0;
     for (int n = 0; n < nwork && ok; ++n) {
@@ -1565,10 +1575,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x4 = 0; x4 < 4; ++x4) {
             const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
             const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
-            float2 d0 = fmul2(ffma2(u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]), make_float2(rd.x, rd.y),
-                                    make_float2(-dr.x, -dr.y)), wsc2);
-            float2 d1 = fmul2(ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
-                                    make_float2(-dr.z, -dr.w)), wsc2);
+            float2 d0 = ffma2(u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]), make_float2(rd.x, rd.y),
+                              make_float2(dr.x, dr.y));
+            float2 d1 = ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
+                              make_float2(dr.z, dr.w));
             if (diag) {  // causal: query t >= key s
               const int tl = cbase + 4 * x4;
               if (tl < row) d0.x = 0.f;
@@ -1607,8 +1617,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x2 = 0; x2 < 8; ++x2) {
             const float2 sv = u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]);
             acc[8 * c + x2] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x2]);
-            const float2 w = fmul2(sv, bf2_unpack(dap[8 * c + x2]));
-            wv[x2] = pack2<T>(w.x, w.y);
+            if constexpr (kBF16) {  // S rounded to bf16, packed product (same operand precision as the MMA)
+              wv[x2] = bf2_mul(pack2<T>(sv.x, sv.y), dap[8 * c + x2]);
+            } else {
+              const float2 w = fmul2(sv, bf2_unpack(dap[8 * c + x2]));
+              wv[x2] = pack2<T>(w.x, w.y);
+            }
           }
           tmem_st8(sbase + c * 8u, wv);  // columns of S already in registers
           if (c < 3) tmem_wait_ld();
@@ -1621,8 +1635,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int x2 = 0; x2 < 8; ++x2) {
               const int tl = cbase + 2 * x2;
-              const float2 rd = *reinterpret_cast<const float2*>(v_rd + tl);
-              float a0 = scale2 * acc[8 * c + x2].x * rd.x, a1 = scale2 * acc[8 * c + x2].y * rd.y;
+              const float2 a = fmul2(acc[8 * c + x2], *reinterpret_cast<const float2*>(v_rd + tl));
+              float a0 = a.x, a1 = a.y;
               if (diag) {
                 if (tl < row) a0 = 0.f;
                 if (tl + 1 < row) a1 = 0.f;
@@ -1654,14 +1668,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[16];
         tmem_ld16(lane_addr + kColDK + hc * HD + c0, r);
         tmem_wait_ld();
-        if (live) {
+        if (live) {  // dK = 2 * (sum of W''^T Q)
+          const auto f = [&](int i) { return 2.f * __uint_as_float(r[i]); };
 #pragma unroll
           for (int v2 = 0; v2 < 2; ++v2) {
             uint4 w;
-            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
-            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
-            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
-            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+            w.x = pack2<T>(f(8 * v2 + 0), f(8 * v2 + 1));
+            w.y = pack2<T>(f(8 * v2 + 2), f(8 * v2 + 3));
+            w.z = pack2<T>(f(8 * v2 + 4), f(8 * v2 + 5));
+            w.w = pack2<T>(f(8 * v2 + 6), f(8 * v2 + 7));
             *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
           }
         }
