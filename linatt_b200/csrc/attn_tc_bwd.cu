@@ -26,6 +26,12 @@ namespace {
 
 constexpr int kThreads = 320;
 constexpr int kComputeWarp0 = 2;
+// The dq ring kernel adds an eleventh warp that issues the dQ chains; warp 10 runs on the third
+// scheduler (warp % 4 == 2), apart from the score issuer (warp 1).  (The dk/dv ring kernel keeps
+// one issuer: with only two TMEM slots, a second issuer's chain would have to complete before the
+// slot could be refilled, where a single issuer may queue the refill behind it in order.)
+constexpr int kThreadsRing = 352;
+constexpr int kChainWarp = 10;
 constexpr int kRing = 3;
 
 struct BwdWs {
@@ -504,23 +510,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 // -- dN = dO V^T, then the score parts S_0..S_{NP-1} -- and dQ at columns 384..511.  The compute
 // warps read dN once per tile and keep dA' = 2 scale^2 (dN - delta)/den (masked) in registers, so
 // the dN slot is handed back at once; each S_p slot is overwritten in place by W_p = S_p dA' (bf16
-// pairs), which the dQ chain reads as its A operand.  Before the issuer reuses a slot it waits for
-// the compute warps to release it and, if it held a W, issues that W's dQ chain first (MMAs of one
-// CTA execute in issue order).  So score MMAs run up to two items ahead of the compute warps.
+// pairs), which the dQ chain reads as its A operand.  Two issuers on different schedulers: the
+// score issuer (warp 1) issues dN and the score parts; the chain issuer (warp 10) waits for the
+// compute warps to release each slot, issues the dQ chain of the W it holds, and signals w_done,
+// after which the score issuer may refill the slot.  One thread's MMAs run in issue order, so the
+// dQ accumulation order is that of the single-issuer form.  Score MMAs run up to two items ahead.
 constexpr int kRingDQ = 4;  // K/V ring depth of the dq ring kernel (two key tiles in flight)
 
 struct DqRingBars {
   uint64_t qo_full;
   uint64_t ring_full[kRingDQ], ring_empty[kRingDQ];
-  uint64_t i_full[3], i_free[3];
-  uint64_t acc_done, drain;
+  uint64_t i_full[3], i_free[3], w_done[3];
+  uint64_t acc_done, drain, drain2;
   uint32_t tmem_base;
   int abort_flag;
   float xch_delta[2][kTile];
 };
 
 template <typename T, int D, int DV, int M, bool SUM>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsRing, 1)
     attn_bwd_dq_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                         AttnBwdParams p) {
@@ -532,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kColDQ = 384;
+  constexpr int kItems = 1 + NP;  // items per key tile: dN, then S_0..S_{NP-1}
   using L = BwdSmem<D, DV>;
 
   extern __shared__ uint8_t smem_raw[];
@@ -558,8 +567,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars.i_full[i], 1);
       mbar_init(&bars.i_free[i], 8);
     }
+    for (int i = 0; i < 3; ++i) mbar_init(&bars.w_done[i], 1);
     mbar_init(&bars.acc_done, 1);
     mbar_init(&bars.drain, 1);
+    mbar_init(&bars.drain2, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -610,9 +621,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr int kItems = 1 + NP;  // items per key tile: dN, then S_0..S_{NP-1}
+      // Score issuer: dN and the score parts.  Item `it` = j * kItems + q lives in slot it % 3; the
+      // slot is reused once the chain warp has released the item three back (w_done: its dQ chain,
+      // if any, has completed).  The ring holds V_j at position 2j and K_j at 2j + 1 (kRingDQ = 4:
+      // slot (2j + c) & 3, use parity (j >> 1) & 1).
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
-      const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
       const uint32_t sRing = smem_u32(smem + L::DQ_OFF_RING);
       // Descriptor bases; every operand below is a compile-time or ring-slot-multiple offset from
       // one of these (no descriptor is rebuilt inside the loops).
@@ -620,52 +633,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t qd0 = kmajor_desc<CW>(smem_u32(smem + L::DQ_OFF_Q), 0, E, 0);    // Q, K-major
       const uint64_t rv0 = kmajor_desc<VCW>(sRing, 0, DV, 0);  // V in ring slot 0, K-major
       const uint64_t rk0 = kmajor_desc<CW>(sRing, 0, E, 0);    // K in ring slot 0, K-major
-      const uint64_t rkm0 = mnmajor_desc<CW>(sRing, 0, 0);     // K in ring slot 0, MN-major
-      bool ok = mbar_wait(&bars.qo_full, 0, wc);
-      // Item `it` = j * kItems + q lives in slot it % 3.  The previous occupant of that slot is item
-      // it - 3; if it was a score part, its W is in the slot and its dQ chain is issued before the
-      // slot is reused.  After the last tile, three claims drain the pending chains.  The ring
-      // holds V_j at position 2j and K_j at 2j + 1 (kRingDQ = 4: slot (2j + c) & 3, use parity
-      // (j >> 1) & 1).
       static_assert(kRingDQ == 4, "ring positions below assume four slots");
+      bool ok = mbar_wait(&bars.qo_full, 0, wc);
       int it = 0, x = 0;       // x = it % 3
       uint32_t use_par = 0;    // parity of (it / 3), i.e. of the current use of slot x
-      const int n_claims = nk * kItems + 3;
-      for (int j = 0; ok && it < n_claims; ++j) {
+      for (int j = 0; ok && j < nk; ++j) {
+        const uint32_t ring_par = static_cast<uint32_t>(j >> 1) & 1u;
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
-          if (it >= n_claims) break;
-          // ---- claim slot x for item it
-          if (it >= 3) {
-            if (!mbar_wait(&bars.i_free[x], use_par ^ 1, wc)) {
-              ok = false;
-              break;
-            }
-            // item it - 3: type pq and tile j + pdj, both compile-time offsets of (j, q)
-            const int pq = ((q - 3) % kItems + kItems) % kItems;
-            const int pdj = (q - 3 - pq) / kItems;
-            if (pq > 0) {  // issue the pending dQ chain of score part pq - 1 of tile j + pdj
-              const int pj = j + pdj, pp = pq - 1;
-              const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-              const bool first = (pj == 0) && (!SUM || gb == 0);
-              const int kslot = (2 * pj + 1) & 3;
-              const uint64_t kd = rkm0 + desc_units(static_cast<uint32_t>(kslot) * L::ITEM) + mnmajor_boff<CW>(gb * E / CW);
-              const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
-              tc_fence_after();
-#pragma unroll
-              for (int kk = 0; kk < kTile / 16; ++kk)
-                umma_ts(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
-                        (!first || kk > 0) ? 1u : 0u);
-              if (pp == NP - 1) umma_commit(&bars.ring_empty[kslot]);  // K tile no longer needed
-            }
+          if (it >= 3 && !mbar_wait(&bars.w_done[x], use_par ^ 1, wc)) {
+            ok = false;
+            break;
           }
-          if (j >= nk) {  // drain claim only
-            ++it;
-            if (++x == 3) { x = 0; use_par ^= 1; }
-            continue;
-          }
-          // ---- issue item (j, q) into slot x
-          const uint32_t ring_par = static_cast<uint32_t>(j >> 1) & 1u;
           const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
           if (q == 0) {  // dN = dO V_j^T
             const int slotV = (2 * j) & 3;
@@ -703,9 +682,52 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (ok) umma_commit(&bars.acc_done);
       umma_commit(&bars.drain);
       mbar_drain(&bars.drain, 0);
+    }
+  } else if (warp == kChainWarp) {
+    if (lane == 0) {
+      // Chain issuer (a scheduler of its own, so its issue stream does not queue behind the score
+      // issuer's): for every item in order, once the compute warps release the slot, the dQ chain
+      // of the W it holds (score parts), then w_done for the score issuer.  All dQ MMAs come from
+      // this thread, so they execute in order; the K tile of key tile j is released after its
+      // last chain.
+      const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
+      const uint64_t rkm0 = mnmajor_desc<CW>(smem_u32(smem + L::DQ_OFF_RING), 0, 0);  // K in ring slot 0, MN-major
+      bool ok = true;
+      int x = 0;
+      uint32_t use_par = 0;
+      for (int j = 0; ok && j < nk; ++j) {
+#pragma unroll
+        for (int q = 0; q < kItems; ++q) {
+          if (!mbar_wait(&bars.i_free[x], use_par, wc)) {
+            ok = false;
+            break;
+          }
+          if (q > 0) {
+            const int pp = q - 1;
+            const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
+            const bool first = (j == 0) && (!SUM || gb == 0);
+            const int kslot = (2 * j + 1) & 3;
+            const uint64_t kd = rkm0 + desc_units(static_cast<uint32_t>(kslot) * L::ITEM) + mnmajor_boff<CW>(gb * E / CW);
+            const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk)
+              umma_ts(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
+                      (!first || kk > 0) ? 1u : 0u);
+            if (pp == NP - 1) umma_commit(&bars.ring_empty[kslot]);  // K tile no longer needed
+          }
+          umma_commit(&bars.w_done[x]);
+          if (++x == 3) {
+            x = 0;
+            use_par ^= 1;
+          }
+        }
+      }
+      if (ok) umma_commit(&bars.acc_done);
+      umma_commit(&bars.drain2);
+      mbar_drain(&bars.drain2, 0);
     }
   } else {
     const int cw = warp - kComputeWarp0;
@@ -1728,7 +1750,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
-    kern<<<dim3(nt, p.B * p.HQ), kThreads, smem, st>>>(tq, tk, tv, to, p);
+    kern<<<dim3(nt, p.B * p.HQ), DECAY ? kThreads : kThreadsRing, smem, st>>>(tq, tk, tv, to, p);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   if (p.phases != 1) {
