@@ -264,22 +264,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        // two 32-column chunks; the second chunk's load is in flight while the first is squared
+        // both 32-column chunks in flight at once (one load latency per part), then the slot goes
+        // back to the issuer before the squares are accumulated
         uint32_t r0[32], r1[32];
         const uint32_t a = lane_addr + slot * 128u + hc * 64u;
         tmem_ld32(a, r0);
-        tmem_wait_ld();
         tmem_ld32(a + 32u, r1);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
-          acc[i] = pp == 0 ? fmul2(x0, x0) : ffma2(x0, x0, acc[i]);
-        }
         tmem_wait_ld();
         if (pp < NP - 1) {  // the last part's slot receives P and is released after it
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars.s_free[slot]);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+          acc[i] = pp == 0 ? fmul2(x0, x0) : ffma2(x0, x0, acc[i]);
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
