@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
       // Score issuer: dN and the score parts.  Item `it` = j * kItems + q lives in slot it % 3; the
       // slot is reused once the chain warp has released the item three back (w_done: its dQ chain,
       // if any, has completed).  The ring holds V_j at position 2j and K_j at 2j + 1 (kRingDQ = 4:
@@ -634,21 +634,21 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       const uint64_t rv0 = kmajor_desc<VCW>(sRing, 0, DV, 0);  // V in ring slot 0, K-major
       const uint64_t rk0 = kmajor_desc<CW>(sRing, 0, E, 0);    // K in ring slot 0, K-major
       static_assert(kRingDQ == 4, "ring positions below assume four slots");
-      bool ok = mbar_wait(&bars.qo_full, 0, wc);
+      bool ok = mbar_wait_w(&bars.qo_full, 0, wc);
       int it = 0, x = 0;       // x = it % 3
       uint32_t use_par = 0;    // parity of (it / 3), i.e. of the current use of slot x
       for (int j = 0; ok && j < nk; ++j) {
         const uint32_t ring_par = static_cast<uint32_t>(j >> 1) & 1u;
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
-          if (it >= 3 && !mbar_wait(&bars.w_done[x], use_par ^ 1, wc)) {
+          if (it >= 3 && !mbar_wait_w(&bars.w_done[x], use_par ^ 1, wc)) {
             ok = false;
             break;
           }
           const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
           if (q == 0) {  // dN = dO V_j^T
             const int slotV = (2 * j) & 3;
-            if (!mbar_wait(&bars.ring_full[slotV], ring_par, wc)) {
+            if (!mbar_wait_w(&bars.ring_full[slotV], ring_par, wc)) {
               ok = false;
               break;
             }
@@ -656,10 +656,10 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             const uint64_t vd = rv0 + desc_units(static_cast<uint32_t>(slotV) * L::ITEM);
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk)
-              umma_ss(sd, od0 + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
-            umma_commit(&bars.i_full[x]);
-            umma_commit(&bars.ring_empty[slotV]);
-            if (!mbar_wait(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
+              umma_ss_w(sd, od0 + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit_w(&bars.i_full[x]);
+            umma_commit_w(&bars.ring_empty[slotV]);
+            if (!mbar_wait_w(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
               ok = false;
               break;
             }
@@ -672,8 +672,8 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             const uint64_t kd = rk0 + desc_units(static_cast<uint32_t>(slotK) * L::ITEM) + kmajor_goff<CW>(gb, E);
 #pragma unroll
             for (int kk = 0; kk < E / 16; ++kk)
-              umma_ss(sd, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
-            umma_commit(&bars.i_full[x]);
+              umma_ss_w(sd, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit_w(&bars.i_full[x]);
           }
           ++it;
           if (++x == 3) {
@@ -682,11 +682,11 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
           }
         }
       }
-      umma_commit(&bars.drain);
+      umma_commit_w(&bars.drain);
       mbar_drain(&bars.drain, 0);
     }
   } else if (warp == kChainWarp) {
-    if (lane == 0) {
+    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
       // Chain issuer (a scheduler of its own, so its issue stream does not queue behind the score
       // issuer's): for every item in order, once the compute warps release the slot, the dQ chain
       // of the W it holds (score parts), then w_done for the score issuer.  All dQ MMAs come from
@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       for (int j = 0; ok && j < nk; ++j) {
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
-          if (!mbar_wait(&bars.i_free[x], use_par, wc)) {
+          if (!mbar_wait_w(&bars.i_free[x], use_par, wc)) {
             ok = false;
             break;
           }
@@ -714,19 +714,19 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < kTile / 16; ++kk)
-              umma_ts(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
+              umma_ts_w(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
                       (!first || kk > 0) ? 1u : 0u);
-            if (pp == NP - 1) umma_commit(&bars.ring_empty[kslot]);  // K tile no longer needed
+            if (pp == NP - 1) umma_commit_w(&bars.ring_empty[kslot]);  // K tile no longer needed
           }
-          umma_commit(&bars.w_done[x]);
+          umma_commit_w(&bars.w_done[x]);
           if (++x == 3) {
             x = 0;
             use_par ^= 1;
           }
         }
       }
-      if (ok) umma_commit(&bars.acc_done);
-      umma_commit(&bars.drain2);
+      if (ok) umma_commit_w(&bars.acc_done);
+      umma_commit_w(&bars.drain2);
       mbar_drain(&bars.drain2, 0);
     }
   } else {
@@ -1450,7 +1450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
       const uint32_t id_dk = umma_idesc_f16(128, E, kBF16, false, true);
       const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
@@ -1463,7 +1463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t rom0 = mnmajor_desc<VCW>(sRing, 0, 0);    // dO in ring slot 0, MN-major
       const uint64_t rq0 = kmajor_desc<CW>(sRing, 0, E, 0);    // Q in ring slot 0, K-major
       const uint64_t rqm0 = mnmajor_desc<CW>(sRing, 0, 0);     // Q in ring slot 0, MN-major
-      bool ok = mbar_wait(&bars.kv_full, 0, wc);
+      bool ok = mbar_wait_w(&bars.kv_full, 0, wc);
       // Item `it` = n * kItems + q lives in slot it % 2; before reuse, the pending chains of item
       // it - 2 are issued.  After the last pair, two claims drain the pending chains.  The ring
       // holds dO_n at position 2n and Q_n at 2n + 1 (kR = 4: slot (2n + c) & 3, use parity
@@ -1479,7 +1479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q = 0; q < kItems; ++q) {
           if (it >= n_claims) break;
           if (it >= 2) {
-            if (!mbar_wait(&bars.i_free[x], use_par ^ 1, wc)) {
+            if (!mbar_wait_w(&bars.i_free[x], use_par ^ 1, wc)) {
               ok = false;
               break;
             }
@@ -1496,17 +1496,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < kTile / 16; ++kk)
-                umma_ts(tbase + kColDK + gb * E, wa + packed_col(kk), qd + mnstep<CW>(kk), id_dk,
+                umma_ts_w(tbase + kColDK + gb * E, wa + packed_col(kk), qd + mnstep<CW>(kk), id_dk,
                         (!first || kk > 0) ? 1u : 0u);
               if (pp == NP - 1) {  // dV += P^T dO, then this pair's dO and Q tiles are free
                 const int psO = (2 * pn) & 3;
                 const uint64_t od = rom0 + desc_units(static_cast<uint32_t>(psO) * L::ITEM);
 #pragma unroll
                 for (int kk = 0; kk < kTile / 16; ++kk)
-                  umma_ts(tbase + kColDV, wa + packed_col(kk) + 32u, od + mnstep<VCW>(kk), id_dv,
+                  umma_ts_w(tbase + kColDV, wa + packed_col(kk) + 32u, od + mnstep<VCW>(kk), id_dv,
                           (pn > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&bars.ring_empty[psO]);
-                umma_commit(&bars.ring_empty[psQ]);
+                umma_commit_w(&bars.ring_empty[psO]);
+                umma_commit_w(&bars.ring_empty[psQ]);
               }
             }
           }
@@ -1517,7 +1517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
           if (q == 0) {  // dN^T = V dO_n^T
-            if (!mbar_wait(&bars.ring_full[slotO], ring_par, wc)) {
+            if (!mbar_wait_w(&bars.ring_full[slotO], ring_par, wc)) {
               ok = false;
               break;
             }
@@ -1525,9 +1525,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t od = ro0 + desc_units(static_cast<uint32_t>(slotO) * L::ITEM);
 #pragma unroll
             for (int kk = 0; kk < DV / 16; ++kk)
-              umma_ss(sd, vd0 + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
-            umma_commit(&bars.i_full[x]);
-            if (!mbar_wait(&bars.ring_full[slotQ], ring_par, wc)) {  // Q_n for the parts
+              umma_ss_w(sd, vd0 + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit_w(&bars.i_full[x]);
+            if (!mbar_wait_w(&bars.ring_full[slotQ], ring_par, wc)) {  // Q_n for the parts
               ok = false;
               break;
             }
@@ -1539,8 +1539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t qd = rq0 + desc_units(static_cast<uint32_t>(slotQ) * L::ITEM) + kmajor_goff<CW>(ga, E);
 #pragma unroll
             for (int kk = 0; kk < E / 16; ++kk)
-              umma_ss(sd, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
-            umma_commit(&bars.i_full[x]);
+              umma_ss_w(sd, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_commit_w(&bars.i_full[x]);
           }
           ++it;
           if (++x == 2) {
@@ -1549,8 +1549,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (ok) umma_commit(&bars.acc_done);
-      umma_commit(&bars.drain);
+      if (ok) umma_commit_w(&bars.acc_done);
+      umma_commit_w(&bars.drain);
       mbar_drain(&bars.drain, 0);
     }
   } else {

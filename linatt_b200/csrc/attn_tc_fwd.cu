@@ -8,7 +8,8 @@
 // One CTA per (128-query tile, batch*head).  Warp roles (320 threads):
 //   warp 0      TMA producer: Q once, K and V tiles through 3-stage rings (4-D tensor maps over
 //               the time-major (B,T,H,D) tensors, so rows past T are zero-filled per batch).
-//   warp 1      TMEM owner + single-thread MMA issuer: for each key tile, one tcgen05.mma chain
+//   warp 1      TMEM owner + MMA issuer (the whole warp runs the issue loop, one elected lane
+//               issues every MMA and commit): for each key tile, one tcgen05.mma chain
 //               per score part into a 3-slot TMEM ring (128 fp32 columns per slot), then the
 //               P*V chain into the O accumulator (columns 384..384+Dv).  P is read straight from
 //               tensor memory (A operand in TMEM), so P never touches shared memory.
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
       const uint32_t idesc_qk = umma_idesc_f16(128, kBK, kBF16, false, false);
       const uint32_t idesc_pv = umma_idesc_f16(128, DV, kBF16, false, true);
       // Descriptor bases (group 0, stage 0); every operand below is a compile-time or stage-multiple
@@ -157,19 +158,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t qd0 = kmajor_desc<CW>(smem_u32(smem + L::OFF_Q), 0, E, 0);
       const uint64_t kd0 = kmajor_desc<CW>(smem_u32(smem + L::OFF_K), 0, E, 0);
       const uint64_t vd0 = mnmajor_desc<VCW>(smem_u32(smem + L::OFF_V), 0, 0);
-      bool ok = mbar_wait(&bars.q_full, 0, wc);
+      bool ok = mbar_wait_w(&bars.q_full, 0, wc);
       // O += P_i V_i with P_i read from TMEM slot `sl`; V_i is in stage `vst` (use parity `vpar`)
       auto issue_pv = [&](int i, int vst, uint32_t vpar, int sl) -> bool {
-        if (!mbar_wait(&bars.p_full[i & 1], (i >> 1) & 1, wc)) return false;
-        if (!mbar_wait(&bars.v_full[vst], vpar, wc)) return false;
+        if (!mbar_wait_w(&bars.p_full[i & 1], (i >> 1) & 1, wc)) return false;
+        if (!mbar_wait_w(&bars.v_full[vst], vpar, wc)) return false;
         tc_fence_after();
         const uint64_t vd = vd0 + desc_units(static_cast<uint32_t>(vst) * L::V_BYTES);
         const uint32_t pa = tbase + static_cast<uint32_t>(sl) * 128u;
         const uint32_t acc0 = i > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_ts(tbase + kOCol, pa + packed_col(kk), vd + mnstep<VCW>(kk), idesc_pv, kk > 0 ? 1u : acc0);
-        umma_commit(&bars.v_empty[vst]);
+          umma_ts_w(tbase + kOCol, pa + packed_col(kk), vd + mnstep<VCW>(kk), idesc_pv, kk > 0 ? 1u : acc0);
+        umma_commit_w(&bars.v_empty[vst]);
         return true;
       };
       // Score part u (u = j*NP + pp) goes to slot u % kSlots; the counters below carry the slot,
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pend = -1, pend_slot = 0, pend_st = 0;
       uint32_t pend_par = 0;
       for (int j = 0; ok && j < nk; ++j) {
-        if (!mbar_wait(&bars.k_full[st], st_par, wc)) {
+        if (!mbar_wait_w(&bars.k_full[st], st_par, wc)) {
           ok = false;
           break;
         }
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             pend = -1;
           }
-          if (!mbar_wait(&bars.s_free[slot], slot_par ^ 1, wc)) {
+          if (!mbar_wait_w(&bars.s_free[slot], slot_par ^ 1, wc)) {
             ok = false;
             break;
           }
@@ -207,8 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sd = tbase + static_cast<uint32_t>(slot) * 128u;
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss(sd, qd + kstep<CW>(kk), kdp + kstep<CW>(kk), idesc_qk, kk > 0 ? 1u : 0u);
-          umma_commit(&bars.s_full[slot]);
+            umma_ss_w(sd, qd + kstep<CW>(kk), kdp + kstep<CW>(kk), idesc_qk, kk > 0 ? 1u : 0u);
+          umma_commit_w(&bars.s_full[slot]);
           last_slot = slot;
           if (++slot == kSlots) {
             slot = 0;
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit(&bars.k_empty[st]);
+        umma_commit_w(&bars.k_empty[st]);
         if (pend >= 0 && !issue_pv(pend, pend_st, pend_par, pend_slot)) {
           ok = false;
           break;
@@ -231,9 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (ok && pend >= 0) ok = issue_pv(pend, pend_st, pend_par, pend_slot);
-      if (ok) umma_commit(&bars.o_full);
+      if (ok) umma_commit_w(&bars.o_full);
       // drain outstanding MMAs before the CTA can retire
-      umma_commit(&bars.drain);
+      umma_commit_w(&bars.drain);
       mbar_drain(&bars.drain, 0);
     }
   } else {

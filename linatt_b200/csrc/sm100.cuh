@@ -99,6 +99,12 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
   return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, w.status, w.abort);
 }
+// Warp-uniform bounded wait for a warp that issues with the _w forms below: every lane waits and
+// the result is the AND over the warp, so no lane leaves a loop that the others continue (a lane
+// that timed out and a lane that saw the phase complete both take the abort path).
+__device__ __forceinline__ bool mbar_wait_w(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, w));
+}
 
 // Bounded wait used only on the abort path to let in-flight copies / MMAs land before the CTA
 // retires (100 ms limit, ignores the abort flag).
@@ -222,6 +228,39 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
                : "memory");
+}
+
+// Warp-wide issue: all 32 lanes of the issuing warp run the issue loop with identical (warp-
+// uniform) operands and one lane, chosen by elect.sync, issues the MMA / commit.  Measured on
+// B200, an issue loop run this way issues at the tensor rate (42 cycles per N=32 MMA, waits and
+// commits included) where the same loop on one lane takes 82, and holds up twice as well against
+// compute warps on the same scheduler.  The elected lane is the same (the lowest) every time, so
+// one thread issues every MMA and commit: their in-order execution is kept.  Every lane must
+// reach each call converged (full member mask); waits in such loops use mbar_wait_w.
+__device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit_w(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
