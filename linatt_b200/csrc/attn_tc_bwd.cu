@@ -235,17 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
       const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
       const uint32_t sQ = smem_u32(smem + L::DQ_OFF_Q);
       const uint32_t sO = smem_u32(smem + L::DQ_OFF_O);
-      bool ok = mbar_wait(&bars.qo_full, 0, wc);
+      bool ok = mbar_wait_w(&bars.qo_full, 0, wc);
       int r = 0, u = 0;
       for (int j = 0; ok && j < nk; ++j) {
         // dN = dO V^T  (the compute warps released the previous tile's dN / dA')
         const int slotV = r % kRing;
-        if (!mbar_wait(&bars.ring_full[slotV], (r / kRing) & 1, wc) || !mbar_wait(&bars.dn_free, (j & 1) ^ 1, wc)) {
+        if (!mbar_wait_w(&bars.ring_full[slotV], (r / kRing) & 1, wc) || !mbar_wait_w(&bars.dn_free, (j & 1) ^ 1, wc)) {
           ok = false;
           break;
         }
@@ -255,13 +255,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t od = kmajor_desc<VCW>(sO, 0, DV, 0), vd = kmajor_desc<VCW>(sV, 0, DV, 0);
 #pragma unroll
           for (int kk = 0; kk < DV / 16; ++kk)
-            umma_ss(tbase + kColDN, od + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_ss_w(tbase + kColDN, od + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars.dn_full);
-        umma_commit(&bars.ring_empty[slotV]);
+        umma_commit_w(&bars.dn_full);
+        umma_commit_w(&bars.ring_empty[slotV]);
         ++r;
         const int slotK = r % kRing;
-        if (!mbar_wait(&bars.ring_full[slotK], (r / kRing) & 1, wc)) {
+        if (!mbar_wait_w(&bars.ring_full[slotK], (r / kRing) & 1, wc)) {
           ok = false;
           break;
         }
@@ -270,14 +270,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto issue_dq = [&](int pp, int uu) -> bool {
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
           const int slot = uu & 1;
-          if (!mbar_wait(&bars.w_full[slot], (uu >> 1) & 1, wc)) return false;
+          if (!mbar_wait_w(&bars.w_full[slot], (uu >> 1) & 1, wc)) return false;
           tc_fence_after();
           const bool first = (j == 0) && (!SUM || gb == 0);
           const uint64_t kd = mnmajor_desc<CW>(sK, gb * E / CW, 0);
           const uint32_t wa = tbase + slot * 128u;
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ts(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
+            umma_ts_w(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
                     (!first || kk > 0) ? 1u : 0u);
           return true;
         };
@@ -287,8 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0), kd = kmajor_desc<CW>(sK, gb, E, 0);
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss(tbase + slot * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
-          umma_commit(&bars.s_full[slot]);
+            umma_ss_w(tbase + slot * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+          umma_commit_w(&bars.s_full[slot]);
           if (pp > 0 && !issue_dq(pp - 1, u - 1)) {
             ok = false;
             break;
@@ -298,11 +298,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        umma_commit(&bars.ring_empty[slotK]);
+        umma_commit_w(&bars.ring_empty[slotK]);
         ++r;
       }
-      if (ok) umma_commit(&bars.acc_done);
-      umma_commit(&bars.drain);
+      if (ok) umma_commit_w(&bars.acc_done);
+      umma_commit_w(&bars.drain);
       mbar_drain(&bars.drain, 0);
     }
   } else {
@@ -1000,19 +1000,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
       const uint32_t id_dk = umma_idesc_f16(128, E, kBF16, false, true);
       const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
       const uint32_t sK = smem_u32(smem + L::KV_OFF_K);
       const uint32_t sV = smem_u32(smem + L::KV_OFF_V);
       const uint32_t sT = smem_u32(smem + L::KV_OFF_T);
-      bool ok = mbar_wait(&bars.kv_full, 0, wc);
+      bool ok = mbar_wait_w(&bars.kv_full, 0, wc);
       int r = 0, u = 0, g = 0;  // g counts uses of the two W/P tiles (tile g & 1, use g >> 1)
       for (int n = 0; ok && n < nwork; ++n, r += 2) {
         const int slotQ = r % kRing, slotO = (r + 1) % kRing;
-        if (!mbar_wait(&bars.ring_full[slotO], ((r + 1) / kRing) & 1, wc) ||
-            !mbar_wait(&bars.dn_empty, (n & 1) ^ 1, wc)) {
+        if (!mbar_wait_w(&bars.ring_full[slotO], ((r + 1) / kRing) & 1, wc) ||
+            !mbar_wait_w(&bars.dn_empty, (n & 1) ^ 1, wc)) {
           ok = false;
           break;
         }
@@ -1023,10 +1023,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t vd = kmajor_desc<VCW>(sV, 0, DV, 0), od = kmajor_desc<VCW>(sO, 0, DV, 0);
 #pragma unroll
           for (int kk = 0; kk < DV / 16; ++kk)
-            umma_ss(tbase + kColDN, vd + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
+            umma_ss_w(tbase + kColDN, vd + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars.dn_full);
-        if (!mbar_wait(&bars.ring_full[slotQ], (r / kRing) & 1, wc)) {
+        umma_commit_w(&bars.dn_full);
+        if (!mbar_wait_w(&bars.ring_full[slotQ], (r / kRing) & 1, wc)) {
           ok = false;
           break;
         }
@@ -1034,21 +1034,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto issue_dk = [&](int pp, int uu) -> bool {
           const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
           const int tb = g & 1;
-          if (!mbar_wait(&bars.t_full[tb], (g >> 1) & 1, wc)) return false;
+          if (!mbar_wait_w(&bars.t_full[tb], (g >> 1) & 1, wc)) return false;
           tc_fence_after();
           const bool first = (n == 0) && (!SUM || ga == 0);
           const uint64_t wd = kmajor128_desc(sT + tb * L::T_BYTES, 0), qd = mnmajor_desc<CW>(sQ, ga * E / CW, 0);
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ss(tbase + kColDK + gb * E, wd + kstep<64>(kk), qd + mnstep<CW>(kk), id_dk,
+            umma_ss_w(tbase + kColDK + gb * E, wd + kstep<64>(kk), qd + mnstep<CW>(kk), id_dk,
                     (!first || kk > 0) ? 1u : 0u);
-          umma_commit(&bars.t_empty[tb]);
+          umma_commit_w(&bars.t_empty[tb]);
           ++g;
           (void)uu;
           return true;
         };
         for (int pp = 0; pp < NP; ++pp, ++u) {
-          if (!mbar_wait(&bars.s_empty, (u & 1) ^ 1, wc)) {
+          if (!mbar_wait_w(&bars.s_empty, (u & 1) ^ 1, wc)) {
             ok = false;
             break;
           }
@@ -1057,8 +1057,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t kd = kmajor_desc<CW>(sK, gb, E, 0), qd = kmajor_desc<CW>(sQ, ga, E, 0);
 #pragma unroll
           for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss(tbase, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
-          umma_commit(&bars.s_full);
+            umma_ss_w(tbase, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
+          umma_commit_w(&bars.s_full);
           if (pp > 0 && !issue_dk(pp - 1, u - 1)) {
             ok = false;
             break;
@@ -1068,10 +1068,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        umma_commit(&bars.ring_empty[slotQ]);
+        umma_commit_w(&bars.ring_empty[slotQ]);
         // dV += P^T dO
         const int tbp = g & 1;
-        if (!mbar_wait(&bars.t_full[tbp], (g >> 1) & 1, wc)) {
+        if (!mbar_wait_w(&bars.t_full[tbp], (g >> 1) & 1, wc)) {
           ok = false;
           break;
         }
@@ -1081,14 +1081,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acc0 = n > 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ss(tbase + kColDV, pd + kstep<64>(kk), od + mnstep<VCW>(kk), id_dv, kk > 0 ? 1u : acc0);
+            umma_ss_w(tbase + kColDV, pd + kstep<64>(kk), od + mnstep<VCW>(kk), id_dv, kk > 0 ? 1u : acc0);
         }
-        umma_commit(&bars.t_empty[tbp]);
+        umma_commit_w(&bars.t_empty[tbp]);
         ++g;
-        umma_commit(&bars.ring_empty[slotO]);
+        umma_commit_w(&bars.ring_empty[slotO]);
       }
-      if (ok) umma_commit(&bars.acc_done);
-      umma_commit(&bars.drain);
+      if (ok) umma_commit_w(&bars.acc_done);
+      umma_commit_w(&bars.drain);
       mbar_drain(&bars.drain, 0);
     }
   } else {
