@@ -154,7 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NVBOX = DV / VCW;
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr bool kHoist = (NP > 1) && !DECAY;
+  // dA' (decay factor folded in) is computed once per key tile and kept in the dN slot for the
+  // remaining parts; with decay also for one part, as the dc row sums read it back.
+  constexpr bool kHoist = (NP > 1) || DECAY;
   constexpr uint32_t kColDN = 256, kColDQ = 384;
   using L = BwdSmem<D, DV>;
 
@@ -368,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       float2 acc[32];  // DECAY only: sum_p S_p^2 for this thread's 64 columns
+      uint32_t clamp_m[2] = {0u, 0u};  // DECAY only: columns with c_t - c_s > 0 (no dc contribution)
       for (int pp = 0; pp < NP; ++pp, ++u) {
         const int slot = u & 1;
         if (!mbar_wait(&bars.s_full[slot], (u >> 1) & 1, wc)) {
@@ -404,17 +407,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (s0 + 1 > row) da[x].y = 0.f;
               }
             }
-            if (DECAY) {
+            if (DECAY) {  // once per tile: decay factor exp(min(c_t - c_s, 0)) into dA'
 #pragma unroll
               for (int x = 0; x < 8; ++x) {
                 const int sg = j * kTile + cbase + 2 * x;
                 const float cs0 = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
                 const float cs1 = sg + 1 < T_ ? __ldg(cb + static_cast<size_t>(sg + 1) * p.HQ) : 0.f;
-                da[x].x *= __expf(fminf(c_t - cs0, 0.f));
-                da[x].y *= __expf(fminf(c_t - cs1, 0.f));
-                const float2 sv = u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]);
-                const float2 sq = fmul2(sv, sv);
-                acc[8 * c + x] = pp == 0 ? sq : fadd2(acc[8 * c + x], sq);
+                const float x0 = c_t - cs0, x1 = c_t - cs1;
+                da[x].x *= __expf(fminf(x0, 0.f));
+                da[x].y *= __expf(fminf(x1, 0.f));
+                const int bit = c * 16 + 2 * x;  // column within this thread's 64
+                if (x0 > 0.f) clamp_m[bit >> 5] |= 1u << (bit & 31);
+                if (x1 > 0.f) clamp_m[(bit + 1) >> 5] |= 1u << ((bit + 1) & 31);
               }
             }
             if (kHoist) {  // keep dA' for the remaining parts of this tile
@@ -433,8 +437,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t wv[8];
 #pragma unroll
           for (int x = 0; x < 8; ++x) {
-            const float2 w = fmul2(u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]), da[x]);
+            const float2 sv = u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]);
+            const float2 w = fmul2(sv, da[x]);
             wv[x] = pack2<T>(w.x, w.y);
+            if (DECAY) acc[8 * c + x] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x]);
           }
           tmem_st8(sbase + c * 8u, wv);
           if (c < 3) tmem_wait_ld();
@@ -446,26 +452,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       if (DECAY) {
-        // R_t += sum_s dA * A  over pairs with c_t - c_s <= 0 (A includes the decay factor)
+        // R_t += sum_s (dN - delta) rden scale^2 e A  over pairs with c_t - c_s <= 0, where the
+        // dN slot now holds dA'_dec = 2 scale^2 (dN - delta) rden e (causally masked): the term is
+        // 0.5 dA'_dec sum_p S_p^2.  Keys past T have S = 0.
+        float2 r2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t rn[32];
           tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
           tmem_wait_ld();
-          const int cbase = hc * 64 + c * 32;
 #pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const int s0 = cbase + x;
-            const int sg = j * kTile + s0;
-            if (diag && s0 > row) continue;
-            const float cs = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
-            const float xd = c_t - cs;
-            if (xd > 0.f) continue;
-            const float2 a2 = acc[(s0 - hc * 64) >> 1];
-            const float av = scale2 * ((x & 1) ? a2.y : a2.x) * __expf(xd);
-            rsum += (__uint_as_float(rn[x]) - delta) * rden * av;
+          for (int x = 0; x < 16; ++x) {
+            const int bit = c * 32 + 2 * x;
+            float2 d = u2f2(rn[2 * x], rn[2 * x + 1]);
+            if (clamp_m[bit >> 5] & (1u << (bit & 31))) d.x = 0.f;
+            if (clamp_m[(bit + 1) >> 5] & (1u << ((bit + 1) & 31))) d.y = 0.f;
+            r2 = ffma2(d, acc[c * 16 + x], r2);
           }
         }
+        rsum += 0.5f * (r2.x + r2.y);
       }
       tc_fence_before();
       __syncwarp();
@@ -891,7 +896,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kColDN = 128, kColDK = 256, kColDV = 384;
-  constexpr bool kHoist = (NP > 1) && !DECAY;
+  // dA' (decay factor folded in) is computed once per query tile and kept in the dN slot for the
+  // remaining parts; with decay also for one part, as the dc column sums read it back.
+  constexpr bool kHoist = (NP > 1) || DECAY;
   using L = BwdSmem<D, DV>;
   static_assert(sizeof(DkvBars) <= 256, "barrier block");
 
@@ -1249,11 +1256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float x0 = ct0 - c_s, x1 = ct1 - c_s;
             a0 *= __expf(fminf(x0, 0.f));
             a1 *= __expf(fminf(x1, 0.f));
-            const float2 dr = *reinterpret_cast<const float2*>(v_dr + tl);
-            const float da0 = fmaf(__uint_as_float(rn[2 * x]), rd.x, -dr.x);
-            const float da1 = fmaf(__uint_as_float(rn[2 * x + 1]), rd.y, -dr.y);
-            if (x0 <= 0.f) csum += da0 * a0;
-            if (x1 <= 0.f) csum += da1 * a1;
+            // the dN slot holds dA'_dec = 2 scale^2 (dN - delta) rden e (causally masked), so
+            // (dN - delta) rden * A = 0.5 dA'_dec sum_p S_p^2
+            if (x0 <= 0.f) csum += 0.5f * __uint_as_float(rn[2 * x]) * acc[8 * c + x].x;
+            if (x1 <= 0.f) csum += 0.5f * __uint_as_float(rn[2 * x + 1]) * acc[8 * c + x].y;
           }
           pv[x] = pack2<T>(a0 * rd.x, a1 * rd.y);
         }
