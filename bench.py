@@ -13,7 +13,9 @@ shape with no data-path collective ("scaling": "weak"); the step time is the max
 Printed JSON line (rank 0):
   value     whole-job tokens/s with inputs resident in HBM (device-timed with CUDA events)
   e2e       the same metric through the public autograd API with pinned host buffers, including
-            the host->device copy of q, k, v, dO and the device->host copy of o, dq, dk, dv
+            every step's host->device copy of q, k, v, dO and device->host copy of o, dq, dk, dv;
+            steps are pipelined (upload / compute / download on three streams, as a training
+            loop prefetches), and the last step's outputs are checked against a lone run
   roofline  the dominant kernel: algorithmic TFLOP per launch / its mean CUDA-event duration,
             against the measured bf16 peak (MEASURED_PEAKS.json); traffic from the committed ncu
             summary when available
@@ -311,42 +313,83 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     # ---------------- e2e through the public autograd API with pinned host buffers
     e2e = None
     if not args.no_e2e:
+        # Every step copies its four inputs host -> device (pinned), runs forward + backward through
+        # the public autograd op and copies o, dq, dk, dv back to pinned host memory.  The steps are
+        # pipelined the way a training loop prefetches its next batch: uploads on one stream (into
+        # two alternating device input sets), compute on the current stream, downloads on a third,
+        # ordered by events, so step i+1's upload, step i's compute and step i-1's download overlap
+        # (the two copy directions run on separate copy engines).
         host = [tuple(x.cpu().pin_memory() for x in s) for s in sets[:2]]
-        outs = [torch.empty(B, T, H, DV, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+        outs = [[torch.empty(B, T, H, DV, dtype=torch.bfloat16).pin_memory() for _ in range(4)] for _ in range(2)]
+        dev_in = [tuple(torch.empty_like(x, device=dev) for x in host[0]) for _ in range(2)]
+        s_cmp = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        fn = pka.parallel_kata_attn_sum if SCORE == "sum" else pka.parallel_kata_attn
 
-        def e2e_step(i):
-            qh, kh, vh, doh = host[i % 2]
-            q = qh.to(dev, non_blocking=True).requires_grad_(True)
-            k = kh.to(dev, non_blocking=True).requires_grad_(True)
-            v = vh.to(dev, non_blocking=True).requires_grad_(True)
-            do = doh.to(dev, non_blocking=True)
-            fn = pka.parallel_kata_attn_sum if SCORE == "sum" else pka.parallel_kata_attn
-            o = fn(q, k, v, num_groups=M)
-            o.backward(do)
-            for dst, src in zip(outs, (o.detach(), q.grad, k.grad, v.grad)):
-                dst.copy_(src, non_blocking=True)
+        def e2e_run(n, start_ev=None):
+            """n pipelined steps; returns the event on the current stream after the last download."""
+            ev_in, ev_cmp, ev_out = {}, {}, {}
+            if start_ev is not None:
+                s_in.wait_event(start_ev)
+            for i in range(n + 2):
+                if i < n:  # upload step i (its input set was last read by step i - 2's compute)
+                    with torch.cuda.stream(s_in):
+                        if i >= 2:
+                            s_in.wait_event(ev_cmp[i - 2])
+                        for dst, src in zip(dev_in[i % 2], host[i % 2]):
+                            dst.copy_(src, non_blocking=True)
+                        ev_in[i] = torch.cuda.Event()
+                        ev_in[i].record(s_in)
+                j = i - 1
+                if 0 <= j < n:  # compute step j
+                    s_cmp.wait_event(ev_in[j])
+                    qd, kd, vd, dod = dev_in[j % 2]
+                    q, k, v = (x.detach().requires_grad_(True) for x in (qd, kd, vd))
+                    o = fn(q, k, v, num_groups=M)
+                    o.backward(dod)
+                    res = (o.detach(), q.grad, k.grad, v.grad)
+                    ev_cmp[j] = torch.cuda.Event()
+                    ev_cmp[j].record(s_cmp)
+                    with torch.cuda.stream(s_out):  # download step j
+                        s_out.wait_event(ev_cmp[j])
+                        for dst, src in zip(outs[j % 2], res):
+                            src.record_stream(s_out)
+                            dst.copy_(src, non_blocking=True)
+                        ev_out[j] = torch.cuda.Event()
+                        ev_out[j].record(s_out)
+            s_cmp.wait_event(ev_out[n - 1])
+            s_cmp.wait_stream(s_in)
+            return ev_out
 
-        for i in range(max(2, args.warmup)):
-            e2e_step(i)
+        e2e_run(max(2, args.warmup))
         torch.cuda.synchronize()
         Ke = max(5, min(K, 20))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        e0.record()
-        for i in range(Ke):
-            e2e_step(i)
-        e1.record()
+        e0.record(s_cmp)
+        e2e_run(Ke, start_ev=e0)
+        e1.record(s_cmp)
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1)
+        # untimed check of the pipeline's ordering: the last step's downloaded o, dq, dk, dv equal
+        # those of the same step run alone (the kernels are deterministic: no atomics)
+        last = Ke - 1
+        q, k, v, dod = (x.to(dev) for x in host[last % 2])
+        q, k, v = (x.requires_grad_(True) for x in (q, k, v))
+        o = fn(q, k, v, num_groups=M)
+        o.backward(dod)
+        e2e_match = all(torch.equal(h, r.detach().cpu()) for h, r in zip(outs[last % 2], (o, q.grad, k.grad, v.grad)))
+        del q, k, v, dod, o
         if world > 1:
             t = torch.tensor([e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
         elem = B * T * H * D * 2
         e2e = {"value": world * B * T * Ke / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": 4 * elem,
-               "d2h_bytes_per_step": 4 * elem, "steps": Ke, "ms_per_step": e_ms / Ke}
+               "d2h_bytes_per_step": 4 * elem, "steps": Ke, "ms_per_step": e_ms / Ke,
+               "pipelined": "upload / compute / download on three streams", "outputs_match": bool(e2e_match)}
 
     if world > 1:
         dist.barrier()
