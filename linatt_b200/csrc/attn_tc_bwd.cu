@@ -7,16 +7,19 @@
 //   dq_a = sum_b W_(a,b) k_b,  dk_b = sum_a W_(a,b)^T q_a,  dv = P^T dO
 //   dc_t = sum_s G[t,s] - sum_t' G[t',t],  G = dA * A on pairs with c_t - c_s <= 0
 //
-// Two kernels, each warp-specialised like the forward (warp 0 TMA, warp 1 TMEM owner and single
-// MMA issuer, warps 2..9 two compute warpgroups splitting the 128 columns of every score tile):
-//   dq kernel   one CTA per (query tile, batch*query head).  TMEM: S ring 2x128, dN = dO V^T (128),
-//               dQ (D).  Prologue computes delta and writes delta, 1/den and delta/den to the
-//               workspace for the second kernel; with decay it also writes dc_t = sum_s G[t,s].
+// Two kernels, each warp-specialised like the forward (warp 0 TMA, warp 1 TMEM owner and MMA
+// issuer, warps 2..9 two compute warpgroups splitting the 128 columns of every score tile):
+//   dq kernel   one CTA per (query tile, batch*query head).  dN = dO V^T and the score parts pass
+//               through a 3-slot TMEM ring, dQ accumulates at columns 384..; W_p goes back into
+//               its slot as the TMEM operand of the dQ chains, which a second issuer warp (warp 10)
+//               issues.  Prologue computes delta and writes delta and the per-query vectors for the
+//               second kernel; with decay it also writes dc_t = sum_s G[t,s].
 //   dkdv kernel one CTA per (key tile, batch*kv head) looping over the query tiles of every query
-//               head of its GQA group.  TMEM: S^T (128), dN^T = V dO^T (128), dK (D), dV (Dv).
-//               W^T and P^T are written as 128B-swizzled K-major smem tiles that feed
-//               dK += W^T Q (Q read MN-major) and dV += P^T dO (dO read MN-major); with decay it
-//               atomically subtracts sum_t G[t,s] from dc.
+//               head of its GQA group.  dN^T and the transposed score parts pass through a 2-slot
+//               TMEM ring, dK and dV accumulate at columns 256.. and 384..; W^T_p and, for the last
+//               part, P^T go back into the slot as the TMEM operands of dK += W^T Q and
+//               dV += P^T dO (Q, dO read MN-major); with decay it atomically subtracts
+//               sum_t G[t,s] from dc.
 // Every mbarrier wait is bounded; named barriers are only used outside the main loops so that an
 // aborting warp never strands the others.
 #include "attn_tc_common.cuh"
@@ -32,7 +35,6 @@ constexpr int kComputeWarp0 = 2;
 // slot could be refilled, where a single issuer may queue the refill behind it in order.)
 constexpr int kThreadsRing = 352;
 constexpr int kChainWarp = 10;
-constexpr int kRing = 3;
 
 struct BwdWs {
   // workspace views (fp32), each 16-byte aligned:
@@ -56,54 +58,21 @@ struct BwdSmem {
   static constexpr int Q_BYTES = kTile * D * 2;
   static constexpr int O_BYTES = kTile * DV * 2;
   static constexpr int ITEM = Q_BYTES > O_BYTES ? Q_BYTES : O_BYTES;
-  static constexpr int T_BYTES = kTile * kTile * 2;  // P / W tiles
-  // dq kernel: Q, dO resident; ring of K/V tiles; W tile
+  // dq kernel: Q, dO resident; a ring of four K/V tiles (two key tiles)
   static constexpr int DQ_OFF_Q = 0;
   static constexpr int DQ_OFF_O = DQ_OFF_Q + Q_BYTES;
   static constexpr int DQ_OFF_RING = DQ_OFF_O + O_BYTES;
-  static constexpr int DQ_OFF_W = DQ_OFF_RING + kRing * ITEM;
-  static constexpr int DQ_TOTAL = DQ_OFF_W + T_BYTES;
-  static constexpr int DQR_TOTAL = DQ_OFF_RING + 4 * ITEM;  // dq ring kernel: four K/V slots, no W tile
-  // dkdv kernel: K, V resident; ring of Q/dO tiles; two tiles that alternately receive W^T_p
-  // (for dK) and P^T (for dV), in the order W_0..W_{NP-1}, P, W_0, ... of the query tiles
+  static constexpr int DQR_TOTAL = DQ_OFF_RING + 4 * ITEM;
+  // dkdv kernel: K, V resident; a ring of four dO/Q tiles (two query tiles); the W / P operands
+  // stay in tensor memory
   static constexpr int KV_OFF_K = 0;
   static constexpr int KV_OFF_V = KV_OFF_K + Q_BYTES;
   static constexpr int KV_OFF_RING = KV_OFF_V + O_BYTES;
-  static constexpr int KV_OFF_T = KV_OFF_RING + kRing * ITEM;  // 2 x T_BYTES
-  static constexpr int KV_OFF_VEC = KV_OFF_T + 2 * T_BYTES;   // 2 stages x {rden, delta*rden} x 128 fp32
-  static constexpr int KV_OFF_BARS = KV_OFF_VEC + 2 * 2 * kTile * 4;
-  static constexpr int KV_TOTAL = KV_OFF_BARS + 256;          // DkvBars lives here (no static smem)
-  // dkdv ring kernel: K, V resident; a ring of four dO/Q tiles (two query tiles); no W/P tiles
-  // (they stay in tensor memory)
   static constexpr int KR_RING = 4;
   static constexpr int KR_OFF_RING = KV_OFF_RING;
   static constexpr int KR_OFF_VEC = KR_OFF_RING + KR_RING * ITEM;
   static constexpr int KR_OFF_BARS = KR_OFF_VEC + 2 * 2 * kTile * 4;
   static constexpr int KR_TOTAL = KR_OFF_BARS + 256;
-};
-
-struct DqBars {
-  uint64_t qo_full;
-  uint64_t ring_full[kRing], ring_empty[kRing];
-  uint64_t dn_full, dn_free;
-  uint64_t s_full[2], w_full[2];
-  uint64_t acc_done, drain;
-  uint32_t tmem_base;
-  int abort_flag;
-  float xch_delta[2][kTile];
-  float xch_r[2][kTile];
-};
-
-struct DkvBars {
-  uint64_t kv_full;
-  uint64_t vec_full[2], vec_empty[2];
-  uint64_t ring_full[kRing], ring_empty[kRing];
-  uint64_t dn_full, dn_empty;
-  uint64_t s_full, s_empty;
-  uint64_t t_full[2], t_empty[2];  // the two smem tiles that alternately hold W^T_p and P^T
-  uint64_t acc_done, drain;
-  uint32_t tmem_base;
-  int abort_flag;
 };
 
 struct DkvRingBars {
@@ -134,382 +103,7 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
 }
 
 // ================================================================================================
-// dq kernel
-// ================================================================================================
-// TMEM: score slots at columns 0 and 128, dN at 256, dQ at 384.  W_p (bf16 pairs) is written over
-// the first 32 columns of each half of its own score slot and read from there as the A operand of
-// dQ_a += W_p K_b.  A score MMA reuses a slot only after the dQ chain that reads the W in it was
-// issued (same-CTA MMAs execute in order), and that chain waited for the W to be complete.
-// Without decay and with several parts, part 0 replaces dN by dA' = 2 scale^2 (dN - delta)/den
-// (masked) in tensor memory so the other parts skip that arithmetic.
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_bwd_dq_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                   AttnBwdParams p) {
-  constexpr int E = D / M;
-  constexpr int CW = BoxW<E>::value;
-  constexpr int NBOX = D / CW;
-  constexpr int VCW = BoxW<DV>::value;
-  constexpr int NVBOX = DV / VCW;
-  constexpr int NP = SUM ? M * M : M;
-  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  // dA' (decay factor folded in) is computed once per key tile and kept in the dN slot for the
-  // remaining parts; with decay also for one part, as the dc row sums read it back.
-  constexpr bool kHoist = (NP > 1) || DECAY;
-  constexpr uint32_t kColDN = 256, kColDQ = 384;
-  using L = BwdSmem<D, DV>;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ DqBars bars;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int T_ = p.T;
-  const int nqt = (T_ + kTile - 1) / kTile;
-  const int qi = nqt - 1 - static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y, b = bh / p.HQ, hq = bh % p.HQ, h = hq / p.G;
-  const int t0 = qi * kTile;
-  const int nk = qi + 1;
-  WaitCtx wc{p.status, &bars.abort_flag};
-
-  if (threadIdx.x == 0) {
-    bars.abort_flag = 0;
-    mbar_init(&bars.qo_full, 1);
-    for (int i = 0; i < kRing; ++i) {
-      mbar_init(&bars.ring_full[i], 1);
-      mbar_init(&bars.ring_empty[i], 1);
-    }
-    mbar_init(&bars.dn_full, 1);
-    mbar_init(&bars.dn_free, 8);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars.s_full[i], 1);
-      mbar_init(&bars.w_full[i], 8);
-    }
-    mbar_init(&bars.acc_done, 1);
-    mbar_init(&bars.drain, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(&bars.tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = bars.tmem_base;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      tma_prefetch_desc(&tmO);
-      mbar_arrive_expect_tx(&bars.qo_full, L::Q_BYTES + L::O_BYTES);
-      for (int bx = 0; bx < NBOX; ++bx)
-        tma_load_4d(smem + L::DQ_OFF_Q + bx * (kTile * CW * 2), &tmQ, &bars.qo_full, bx * CW, hq, t0, b);
-      for (int bx = 0; bx < NVBOX; ++bx)
-        tma_load_4d(smem + L::DQ_OFF_O + bx * (kTile * VCW * 2), &tmO, &bars.qo_full, bx * VCW, hq, t0, b);
-      int r = 0;
-      bool ok = true;
-      for (int j = 0; j < nk && ok; ++j) {
-        for (int item = 0; item < 2; ++item, ++r) {  // V_j then K_j
-          const int slot = r % kRing;
-          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
-            ok = false;
-            break;
-          }
-          uint8_t* dst = smem + L::DQ_OFF_RING + slot * L::ITEM;
-          if (item == 0) {
-            mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
-            for (int bx = 0; bx < NVBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmV, &bars.ring_full[slot], bx * VCW, h, j * kTile, b);
-          } else {
-            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
-            for (int bx = 0; bx < NBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, j * kTile, b);
-          }
-        }
-      }
-      if (!ok) {
-        for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
-          mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
-      }
-    }
-  } else if (warp == 1) {
-    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
-      const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
-      const uint32_t id_dq = umma_idesc_f16(128, E, kBF16, false, true);
-      const uint32_t sQ = smem_u32(smem + L::DQ_OFF_Q);
-      const uint32_t sO = smem_u32(smem + L::DQ_OFF_O);
-      bool ok = mbar_wait_w(&bars.qo_full, 0, wc);
-      int r = 0, u = 0;
-      for (int j = 0; ok && j < nk; ++j) {
-        // dN = dO V^T  (the compute warps released the previous tile's dN / dA')
-        const int slotV = r % kRing;
-        if (!mbar_wait_w(&bars.ring_full[slotV], (r / kRing) & 1, wc) || !mbar_wait_w(&bars.dn_free, (j & 1) ^ 1, wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sV = smem_u32(smem + L::DQ_OFF_RING + slotV * L::ITEM);
-        {
-          const uint64_t od = kmajor_desc<VCW>(sO, 0, DV, 0), vd = kmajor_desc<VCW>(sV, 0, DV, 0);
-#pragma unroll
-          for (int kk = 0; kk < DV / 16; ++kk)
-            umma_ss_w(tbase + kColDN, od + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
-        }
-        umma_commit_w(&bars.dn_full);
-        umma_commit_w(&bars.ring_empty[slotV]);
-        ++r;
-        const int slotK = r % kRing;
-        if (!mbar_wait_w(&bars.ring_full[slotK], (r / kRing) & 1, wc)) {
-          ok = false;
-          break;
-        }
-        const uint32_t sK = smem_u32(smem + L::DQ_OFF_RING + slotK * L::ITEM);
-        // dQ_a += W_p K_b with W_p read from TMEM (slot of part uu)
-        auto issue_dq = [&](int pp, int uu) -> bool {
-          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          const int slot = uu & 1;
-          if (!mbar_wait_w(&bars.w_full[slot], (uu >> 1) & 1, wc)) return false;
-          tc_fence_after();
-          const bool first = (j == 0) && (!SUM || gb == 0);
-          const uint64_t kd = mnmajor_desc<CW>(sK, gb * E / CW, 0);
-          const uint32_t wa = tbase + slot * 128u;
-#pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ts_w(tbase + kColDQ + ga * E, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq,
-                    (!first || kk > 0) ? 1u : 0u);
-          return true;
-        };
-        for (int pp = 0; pp < NP; ++pp, ++u) {
-          const int slot = u & 1;
-          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          const uint64_t qd = kmajor_desc<CW>(sQ, ga, E, 0), kd = kmajor_desc<CW>(sK, gb, E, 0);
-#pragma unroll
-          for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss_w(tbase + slot * 128u, qd + kstep<CW>(kk), kd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
-          umma_commit_w(&bars.s_full[slot]);
-          if (pp > 0 && !issue_dq(pp - 1, u - 1)) {
-            ok = false;
-            break;
-          }
-        }
-        if (!ok || !issue_dq(NP - 1, u - 1)) {
-          ok = false;
-          break;
-        }
-        umma_commit_w(&bars.ring_empty[slotK]);
-        ++r;
-      }
-      if (ok) umma_commit_w(&bars.acc_done);
-      umma_commit_w(&bars.drain);
-      mbar_drain(&bars.drain, 0);
-    }
-  } else {
-    const int cw = warp - kComputeWarp0;
-    const int hc = cw >> 2;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int tg = t0 + row;
-    const bool live = tg < T_;
-    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    const size_t rowidx = (static_cast<size_t>(b) * T_ + tg) * p.HQ + hq;  // (b, tg, hq)
-    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
-    // ---- delta_t = <o_t, dO_t> over this thread's half of Dv, then exchanged
-    float dpart = 0.f;
-    if (live && p.delta_in) {
-      dpart = hc == 0 ? p.delta_in[rowidx] : 0.f;
-    } else if (live) {
-      constexpr int HV = DV / 2;
-      const T* orow = static_cast<const T*>(p.o) + rowidx * DV + hc * HV;
-      const T* grow = static_cast<const T*>(p.dout) + rowidx * DV + hc * HV;
-#pragma unroll
-      for (int c8 = 0; c8 < HV; c8 += 8) {
-        const uint4 a = *reinterpret_cast<const uint4*>(orow + c8);
-        const uint4 g = *reinterpret_cast<const uint4*>(grow + c8);
-        const T* ah = reinterpret_cast<const T*>(&a);
-        const T* gh = reinterpret_cast<const T*>(&g);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) dpart = fmaf(to_f32<T>(ah[e]), to_f32<T>(gh[e]), dpart);
-      }
-    }
-    bars.xch_delta[hc][row] = dpart;
-    named_bar_sync(1, 256);
-    const float delta = bars.xch_delta[0][row] + bars.xch_delta[1][row];
-    float rden = 1.f;
-    if (live) {
-      const float dn = p.den[rowidx];
-      rden = 1.f / (dn > 0.f ? dn : 1.f);
-      if (hc == 0) ws.delta[rowidx] = delta;
-    }
-    if (hc == 0) {  // every row of the tile, including rows past T (rden 1, delta 0)
-      const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
-      ws.rden[hm] = rden;
-      ws.dr[hm] = live ? delta * rden : 0.f;
-    }
-    const float w_scale = 2.f * p.scale * p.scale;
-    const float scale2 = p.scale * p.scale;
-    // dA' = dN * rden_w - dr_w = 2 scale^2 (dN - delta) / den
-    const float2 rden_w = make_float2(rden * w_scale, rden * w_scale);
-    const float2 ndr_w = make_float2(-delta * rden * w_scale, -delta * rden * w_scale);
-    float c_t = 0.f;
-    const float* cb = nullptr;
-    if (DECAY) {
-      cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
-      c_t = live ? cb[static_cast<size_t>(tg) * p.HQ] : 0.f;
-    }
-    float rsum = 0.f;
-    bool ok = true;
-    int u = 0;
-    for (int j = 0; j < nk && ok; ++j) {
-      const bool diag = (j == qi);
-      if (!mbar_wait(&bars.dn_full, j & 1, wc)) {
-        ok = false;
-        break;
-      }
-      float2 acc[32];  // DECAY only: sum_p S_p^2 for this thread's 64 columns
-      uint32_t clamp_m[2] = {0u, 0u};  // DECAY only: columns with c_t - c_s > 0 (no dc contribution)
-      for (int pp = 0; pp < NP; ++pp, ++u) {
-        const int slot = u & 1;
-        if (!mbar_wait(&bars.s_full[slot], (u >> 1) & 1, wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // Software-pipelined over four 16-column chunks (loads of chunk c+1 in flight while chunk c
-        // is processed).  W chunk c goes to packed slot columns [8c, 8c+8) of this half, which hold
-        // S values already in registers; dA' (hoisted) overwrites dN chunk c in place.
-        uint32_t rs[2][16], rn[2][16];
-        const uint32_t sbase = lane_addr + slot * 128u + hc * 64u;
-        const uint32_t nbase = lane_addr + kColDN + hc * 64u;
-        tmem_ld16(sbase, rs[0]);
-        tmem_ld16(nbase, rn[0]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cur = c & 1;
-          if (c < 3) {
-            tmem_ld16(sbase + (c + 1) * 16u, rs[cur ^ 1]);
-            tmem_ld16(nbase + (c + 1) * 16u, rn[cur ^ 1]);
-          }
-          const int cbase = hc * 64 + c * 16;  // key column within the tile
-          float2 da[8];
-          if (!kHoist || pp == 0) {
-#pragma unroll
-            for (int x = 0; x < 8; ++x) da[x] = ffma2(u2f2(rn[cur][2 * x], rn[cur][2 * x + 1]), rden_w, ndr_w);
-            if (diag) {
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const int s0 = cbase + 2 * x;
-                if (s0 > row) da[x].x = 0.f;
-                if (s0 + 1 > row) da[x].y = 0.f;
-              }
-            }
-            if (DECAY) {  // once per tile: decay factor exp(min(c_t - c_s, 0)) into dA'
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const int sg = j * kTile + cbase + 2 * x;
-                const float cs0 = sg < T_ ? __ldg(cb + static_cast<size_t>(sg) * p.HQ) : 0.f;
-                const float cs1 = sg + 1 < T_ ? __ldg(cb + static_cast<size_t>(sg + 1) * p.HQ) : 0.f;
-                const float x0 = c_t - cs0, x1 = c_t - cs1;
-                da[x].x *= __expf(fminf(x0, 0.f));
-                da[x].y *= __expf(fminf(x1, 0.f));
-                const int bit = c * 16 + 2 * x;  // column within this thread's 64
-                if (x0 > 0.f) clamp_m[bit >> 5] |= 1u << (bit & 31);
-                if (x1 > 0.f) clamp_m[(bit + 1) >> 5] |= 1u << ((bit + 1) & 31);
-              }
-            }
-            if (kHoist) {  // keep dA' for the remaining parts of this tile
-              uint32_t dw[16];
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                dw[2 * x] = __float_as_uint(da[x].x);
-                dw[2 * x + 1] = __float_as_uint(da[x].y);
-              }
-              tmem_st16(nbase + c * 16u, dw);
-            }
-          } else {
-#pragma unroll
-            for (int x = 0; x < 8; ++x) da[x] = u2f2(rn[cur][2 * x], rn[cur][2 * x + 1]);
-          }
-          uint32_t wv[8];
-#pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            const float2 sv = u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]);
-            const float2 w = fmul2(sv, da[x]);
-            wv[x] = pack2<T>(w.x, w.y);
-            if (DECAY) acc[8 * c + x] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x]);
-          }
-          tmem_st8(sbase + c * 8u, wv);
-          if (c < 3) tmem_wait_ld();
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.w_full[slot]);
-      }
-      if (!ok) break;
-      if (DECAY) {
-        // R_t += sum_s (dN - delta) rden scale^2 e A  over pairs with c_t - c_s <= 0, where the
-        // dN slot now holds dA'_dec = 2 scale^2 (dN - delta) rden e (causally masked): the term is
-        // 0.5 dA'_dec sum_p S_p^2.  Keys past T have S = 0.
-        float2 r2 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t rn[32];
-          tmem_ld32(lane_addr + kColDN + hc * 64u + c * 32u, rn);
-          tmem_wait_ld();
-#pragma unroll
-          for (int x = 0; x < 16; ++x) {
-            const int bit = c * 32 + 2 * x;
-            float2 d = u2f2(rn[2 * x], rn[2 * x + 1]);
-            if (clamp_m[bit >> 5] & (1u << (bit & 31))) d.x = 0.f;
-            if (clamp_m[(bit + 1) >> 5] & (1u << ((bit + 1) & 31))) d.y = 0.f;
-            r2 = ffma2(d, acc[c * 16 + x], r2);
-          }
-        }
-        rsum += 0.5f * (r2.x + r2.y);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars.dn_free);
-    }
-    // ---- epilogue: dQ -> global; dc_t = row sum of G
-    if (DECAY) bars.xch_r[hc][row] = rsum;
-    named_bar_sync(1, 256);
-    if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
-      tc_fence_after();
-      constexpr int HD = D / 2;
-      T* dqrow = static_cast<T*>(p.dq) + rowidx * D + hc * HD;
-#pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(lane_addr + kColDQ + hc * HD + c0, r);
-        tmem_wait_ld();
-        if (live) {
-#pragma unroll
-          for (int v2 = 0; v2 < 2; ++v2) {
-            uint4 w;
-            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
-            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
-            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
-            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
-            *reinterpret_cast<uint4*>(dqrow + c0 + 8 * v2) = w;
-          }
-        }
-      }
-      if (DECAY && live && hc == 0) p.dc[rowidx] = bars.xch_r[0][row] + bars.xch_r[1][row];
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tbase, 512);
-}
-
-// ================================================================================================
-// dq kernel, ring form (no decay)
+// dq kernel (tensor-memory ring)
 // ================================================================================================
 // TMEM: a ring of three 128-column slots that the items of every key tile pass through in order
 // -- dN = dO V^T, then the score parts S_0..S_{NP-1} -- and dQ at columns 384..511.  The compute
@@ -529,10 +123,10 @@ struct DqRingBars {
   uint64_t acc_done, drain, drain2;
   uint32_t tmem_base;
   int abort_flag;
-  float xch_delta[2][kTile];
+  float xch_delta[2][kTile];  // halves of delta_t; with decay, at the end, halves of the dc row sums
 };
 
-template <typename T, int D, int DV, int M, bool SUM>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
 __global__ void __launch_bounds__(kThreadsRing, 1)
     attn_bwd_dq_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -783,11 +377,21 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
     const float w_scale = 2.f * p.scale * p.scale;
     const float2 rden_w = make_float2(rden * w_scale, rden * w_scale);
     const float2 ndr_w = make_float2(-delta * rden * w_scale, -delta * rden * w_scale);
+    // decay: e(t,s) = exp(min(c_t - c_s, 0)) is folded into dA' once per key tile; the dc row sum
+    // R_t = sum_s (dN - delta) rden A_ts over pairs with c_t - c_s <= 0 is 0.5 sum_s dA'_dec S^2
+    float c_t = 0.f;
+    const float* cb = nullptr;
+    if (DECAY) {
+      cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
+      c_t = live ? cb[static_cast<size_t>(tg) * p.HQ] : 0.f;
+    }
+    float2 r2 = make_float2(0.f, 0.f);
     bool ok = true;
     int it = 0;
     for (int j = 0; j < nk && ok; ++j) {
       const bool diag = (j == qi);
       float2 da[32];  // dA' of this thread's 64 key columns
+      uint32_t cm[2] = {0u, 0u};  // decay: columns with c_t - c_s > 0 (no dc contribution)
       {
         const int x = it % 3;
         if (!mbar_wait(&bars.i_full[x], (it / 3) & 1, wc)) {
@@ -819,7 +423,21 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             if (s0 + 1 > row) da[x2].y = 0.f;
           }
         }
+        if (DECAY) {
+#pragma unroll
+          for (int x2 = 0; x2 < 32; ++x2) {
+            const int sk = j * kTile + hc * 64 + 2 * x2;
+            const float cs0 = sk < T_ ? __ldg(cb + static_cast<size_t>(sk) * p.HQ) : 0.f;
+            const float cs1 = sk + 1 < T_ ? __ldg(cb + static_cast<size_t>(sk + 1) * p.HQ) : 0.f;
+            const float x0 = c_t - cs0, x1 = c_t - cs1;
+            da[x2].x *= __expf(fminf(x0, 0.f));
+            da[x2].y *= __expf(fminf(x1, 0.f));
+            if (x0 > 0.f) cm[x2 >> 4] |= 1u << ((2 * x2) & 31);
+            if (x1 > 0.f) cm[x2 >> 4] |= 1u << ((2 * x2 + 1) & 31);
+          }
+        }
       }
+      const bool any_clamp = DECAY && (cm[0] | cm[1]) != 0u;
       for (int pp = 0; pp < NP; ++pp, ++it) {
         const int x = it % 3;
         if (!mbar_wait(&bars.i_full[x], (it / 3) & 1, wc)) {
@@ -838,8 +456,18 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
           uint32_t wv[8];
 #pragma unroll
           for (int x2 = 0; x2 < 8; ++x2) {
-            const float2 w = fmul2(u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]), da[8 * c + x2]);
+            const float2 sv = u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]);
+            const float2 w = fmul2(sv, da[8 * c + x2]);
             wv[x2] = pack2<T>(w.x, w.y);
+            if (DECAY) {
+              float2 dm = da[8 * c + x2];
+              if (any_clamp) {
+                const int bit = 16 * c + 2 * x2;
+                if (cm[bit >> 5] & (1u << (bit & 31))) dm.x = 0.f;
+                if (cm[bit >> 5] & (1u << ((bit + 1) & 31))) dm.y = 0.f;
+              }
+              r2 = ffma2(fmul2(sv, sv), dm, r2);
+            }
           }
           tmem_st8(sbase + c * 8u, wv);  // columns of S already in registers
           if (c < 3) tmem_wait_ld();
@@ -850,8 +478,13 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
         if (lane == 0) mbar_arrive(&bars.i_free[x]);
       }
     }
-    // ---- epilogue: dQ -> global
+    // ---- epilogue: dQ -> global; decay: dc_t = R_t (the dk/dv pass adds the column part).  The
+    // delta exchange slots are free again: every compute warp read them right after the first named
+    // barrier, before it released its first item, and no warp gets past the first three items
+    // before all warps have released the first one.
+    if (DECAY) bars.xch_delta[hc][row] = 0.5f * (r2.x + r2.y);
     named_bar_sync(1, 256);
+    if (DECAY && ok && live && hc == 0) p.dc[rowidx] = bars.xch_delta[0][row] + bars.xch_delta[1][row];
     if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
       tc_fence_after();
       constexpr int HD = D / 2;
@@ -881,457 +514,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
 }
 
 // ================================================================================================
-// dk / dv kernel
-// ================================================================================================
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_bwd_dkdv_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                     AttnBwdParams p) {
-  constexpr int E = D / M;
-  constexpr int CW = BoxW<E>::value;
-  constexpr int NBOX = D / CW;
-  constexpr int VCW = BoxW<DV>::value;
-  constexpr int NVBOX = DV / VCW;
-  constexpr int NP = SUM ? M * M : M;
-  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kColDN = 128, kColDK = 256, kColDV = 384;
-  // dA' (decay factor folded in) is computed once per query tile and kept in the dN slot for the
-  // remaining parts; with decay also for one part, as the dc column sums read it back.
-  constexpr bool kHoist = (NP > 1) || DECAY;
-  using L = BwdSmem<D, DV>;
-  static_assert(sizeof(DkvBars) <= 256, "barrier block");
-
-  // The whole shared footprint is dynamic (no static __shared__), so the dynamic window starts at
-  // the CTA's shared base, which is 1024-byte aligned; checked below rather than assumed.
-  extern __shared__ __align__(1024) uint8_t smem[];
-  DkvBars& bars = *reinterpret_cast<DkvBars*>(smem + L::KV_OFF_BARS);
-  if ((smem_u32(smem) & 1023u) != 0) {
-    if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kStatusWaitTimeout + 1);
-    return;
-  }
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int T_ = p.T;
-  const int nqt = (T_ + kTile - 1) / kTile;
-  const int kj = static_cast<int>(blockIdx.x);  // small j = most work, launched first
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int s0 = kj * kTile;
-  const int nq = nqt - kj;     // query tiles kj..nqt-1 per query head
-  const int nwork = p.G * nq;  // (query head, query tile) items
-  const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
-  WaitCtx wc{p.status, &bars.abort_flag};
-
-  if (threadIdx.x == 0) {
-    bars.abort_flag = 0;
-    mbar_init(&bars.kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars.vec_full[i], 1);
-      mbar_init(&bars.vec_empty[i], 8);
-    }
-    for (int i = 0; i < kRing; ++i) {
-      mbar_init(&bars.ring_full[i], 1);
-      mbar_init(&bars.ring_empty[i], 1);
-    }
-    mbar_init(&bars.dn_full, 1);
-    mbar_init(&bars.dn_empty, 8);
-    mbar_init(&bars.s_full, 1);
-    mbar_init(&bars.s_empty, 8);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars.t_full[i], 8);
-      mbar_init(&bars.t_empty[i], 1);
-    }
-    mbar_init(&bars.acc_done, 1);
-    mbar_init(&bars.drain, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(&bars.tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = bars.tmem_base;
-  float* vec = reinterpret_cast<float*>(smem + L::KV_OFF_VEC);  // [stage][0: rden, 1: delta*rden][128]
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      tma_prefetch_desc(&tmO);
-      mbar_arrive_expect_tx(&bars.kv_full, L::Q_BYTES + L::O_BYTES);
-      for (int bx = 0; bx < NBOX; ++bx)
-        tma_load_4d(smem + L::KV_OFF_K + bx * (kTile * CW * 2), &tmK, &bars.kv_full, bx * CW, h, s0, b);
-      for (int bx = 0; bx < NVBOX; ++bx)
-        tma_load_4d(smem + L::KV_OFF_V + bx * (kTile * VCW * 2), &tmV, &bars.kv_full, bx * VCW, h, s0, b);
-      int r = 0, nv = 0;
-      bool ok = true;
-      for (int n = 0; n < nwork && ok; ++n) {
-        const int hq = h * p.G + n / nq;
-        const int ti = (kj + n % nq) * kTile;
-        // per-query vectors of this tile: rden and delta*rden (512 B each, contiguous)
-        const int vs = n & 1;
-        if (!mbar_wait(&bars.vec_empty[vs], ((n >> 1) & 1) ^ 1, wc)) {
-          ok = false;
-          break;
-        }
-        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + ti;
-        mbar_arrive_expect_tx(&bars.vec_full[vs], 2 * kTile * 4);
-        bulk_load(vec + (vs * 2 + 0) * kTile, ws.rden + hm, kTile * 4, &bars.vec_full[vs]);
-        bulk_load(vec + (vs * 2 + 1) * kTile, ws.dr + hm, kTile * 4, &bars.vec_full[vs]);
-        nv = n + 1;
-        for (int item = 0; item < 2; ++item, ++r) {  // Q_i then dO_i
-          const int slot = r % kRing;
-          if (!mbar_wait(&bars.ring_empty[slot], ((r / kRing) & 1) ^ 1, wc)) {
-            ok = false;
-            break;
-          }
-          uint8_t* dst = smem + L::KV_OFF_RING + slot * L::ITEM;
-          if (item == 0) {
-            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
-            for (int bx = 0; bx < NBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * CW * 2), &tmQ, &bars.ring_full[slot], bx * CW, hq, ti, b);
-          } else {
-            mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
-            for (int bx = 0; bx < NVBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmO, &bars.ring_full[slot], bx * VCW, hq, ti, b);
-          }
-        }
-      }
-      if (!ok) {
-        for (int rr = (r > kRing ? r - kRing : 0); rr < r; ++rr)
-          mbar_drain(&bars.ring_full[rr % kRing], (rr / kRing) & 1);
-        for (int n = (nv > 2 ? nv - 2 : 0); n < nv; ++n) mbar_drain(&bars.vec_full[n & 1], (n >> 1) & 1);
-      }
-    }
-  } else if (warp == 1) {
-    {  // warp-wide issue (every lane runs the loop; one elected lane issues)
-      const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
-      const uint32_t id_dk = umma_idesc_f16(128, E, kBF16, false, true);
-      const uint32_t id_dv = umma_idesc_f16(128, DV, kBF16, false, true);
-      const uint32_t sK = smem_u32(smem + L::KV_OFF_K);
-      const uint32_t sV = smem_u32(smem + L::KV_OFF_V);
-      const uint32_t sT = smem_u32(smem + L::KV_OFF_T);
-      bool ok = mbar_wait_w(&bars.kv_full, 0, wc);
-      int r = 0, u = 0, g = 0;  // g counts uses of the two W/P tiles (tile g & 1, use g >> 1)
-      for (int n = 0; ok && n < nwork; ++n, r += 2) {
-        const int slotQ = r % kRing, slotO = (r + 1) % kRing;
-        if (!mbar_wait_w(&bars.ring_full[slotO], ((r + 1) / kRing) & 1, wc) ||
-            !mbar_wait_w(&bars.dn_empty, (n & 1) ^ 1, wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sO = smem_u32(smem + L::KV_OFF_RING + slotO * L::ITEM);
-        // dN^T = V dO^T  (rows: keys, cols: queries)
-        {
-          const uint64_t vd = kmajor_desc<VCW>(sV, 0, DV, 0), od = kmajor_desc<VCW>(sO, 0, DV, 0);
-#pragma unroll
-          for (int kk = 0; kk < DV / 16; ++kk)
-            umma_ss_w(tbase + kColDN, vd + kstep<VCW>(kk), od + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
-        }
-        umma_commit_w(&bars.dn_full);
-        if (!mbar_wait_w(&bars.ring_full[slotQ], (r / kRing) & 1, wc)) {
-          ok = false;
-          break;
-        }
-        const uint32_t sQ = smem_u32(smem + L::KV_OFF_RING + slotQ * L::ITEM);
-        auto issue_dk = [&](int pp, int uu) -> bool {
-          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          const int tb = g & 1;
-          if (!mbar_wait_w(&bars.t_full[tb], (g >> 1) & 1, wc)) return false;
-          tc_fence_after();
-          const bool first = (n == 0) && (!SUM || ga == 0);
-          const uint64_t wd = kmajor128_desc(sT + tb * L::T_BYTES, 0), qd = mnmajor_desc<CW>(sQ, ga * E / CW, 0);
-#pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ss_w(tbase + kColDK + gb * E, wd + kstep<64>(kk), qd + mnstep<CW>(kk), id_dk,
-                    (!first || kk > 0) ? 1u : 0u);
-          umma_commit_w(&bars.t_empty[tb]);
-          ++g;
-          (void)uu;
-          return true;
-        };
-        for (int pp = 0; pp < NP; ++pp, ++u) {
-          if (!mbar_wait_w(&bars.s_empty, (u & 1) ^ 1, wc)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
-          const uint64_t kd = kmajor_desc<CW>(sK, gb, E, 0), qd = kmajor_desc<CW>(sQ, ga, E, 0);
-#pragma unroll
-          for (int kk = 0; kk < E / 16; ++kk)
-            umma_ss_w(tbase, kd + kstep<CW>(kk), qd + kstep<CW>(kk), id_nn, kk > 0 ? 1u : 0u);
-          umma_commit_w(&bars.s_full);
-          if (pp > 0 && !issue_dk(pp - 1, u - 1)) {
-            ok = false;
-            break;
-          }
-        }
-        if (!ok || !issue_dk(NP - 1, u - 1)) {
-          ok = false;
-          break;
-        }
-        umma_commit_w(&bars.ring_empty[slotQ]);
-        // dV += P^T dO
-        const int tbp = g & 1;
-        if (!mbar_wait_w(&bars.t_full[tbp], (g >> 1) & 1, wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        {
-          const uint64_t pd = kmajor128_desc(sT + tbp * L::T_BYTES, 0), od = mnmajor_desc<VCW>(sO, 0, 0);
-          const uint32_t acc0 = n > 0 ? 1u : 0u;
-#pragma unroll
-          for (int kk = 0; kk < kTile / 16; ++kk)
-            umma_ss_w(tbase + kColDV, pd + kstep<64>(kk), od + mnstep<VCW>(kk), id_dv, kk > 0 ? 1u : acc0);
-        }
-        umma_commit_w(&bars.t_empty[tbp]);
-        ++g;
-        umma_commit_w(&bars.ring_empty[slotO]);
-      }
-      if (ok) umma_commit_w(&bars.acc_done);
-      umma_commit_w(&bars.drain);
-      mbar_drain(&bars.drain, 0);
-    }
-  } else {
-    const int cw = warp - kComputeWarp0;
-    const int hc = cw >> 2;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // key row within the tile
-    const int sg = s0 + row;
-    const bool live = sg < T_;
-    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
-    const float w_scale = 2.f * p.scale * p.scale;
-    const float2 wsc2 = make_float2(w_scale, w_scale);
-    const float scale2 = p.scale * p.scale;
-    const uint32_t sT = smem_u32(smem + L::KV_OFF_T);
-    bool ok = true;
-    int u = 0, g = 0;  // g: uses of the two W/P tiles, in the issuer's order
-    float csum = 0.f;
-    for (int n = 0; n < nwork && ok; ++n) {
-      const int hq = h * p.G + n / nq;
-      const int qi = kj + n % nq;
-      const bool diag = (qi == kj);
-      const int vs = n & 1;
-      const float* v_rd = vec + (vs * 2 + 0) * kTile;
-      const float* v_dr = vec + (vs * 2 + 1) * kTile;
-      float c_s = 0.f;
-      const float* cb = nullptr;
-      if (DECAY) {
-        cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
-        c_s = live ? cb[static_cast<size_t>(sg) * p.HQ] : 0.f;
-      }
-      if (!mbar_wait(&bars.vec_full[vs], (n >> 1) & 1, wc) || !mbar_wait(&bars.dn_full, n & 1, wc)) {
-        ok = false;
-        break;
-      }
-      float2 acc[32];
-      for (int pp = 0; pp < NP; ++pp, ++u) {
-        const int tb = g & 1;
-        const uint32_t sW = sT + tb * L::T_BYTES;
-        if (!mbar_wait(&bars.s_full, u & 1, wc) || !mbar_wait(&bars.t_empty[tb], ((g >> 1) & 1) ^ 1, wc)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // Software-pipelined over four 16-column chunks: the TMEM loads of chunk c+1 are in
-        // flight while chunk c is processed; the score slot is released as soon as the last
-        // chunk of S has landed in registers.
-        uint32_t rs[2][16], rn[2][16];
-        tmem_ld16(lane_addr + hc * 64u, rs[0]);
-        tmem_ld16(lane_addr + kColDN + hc * 64u, rn[0]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cur = c & 1;
-          const uint32_t dcol = kColDN + hc * 64u + c * 16u;
-          if (c < 3) {
-            tmem_ld16(lane_addr + hc * 64u + (c + 1) * 16u, rs[cur ^ 1]);
-            tmem_ld16(lane_addr + dcol + 16u, rn[cur ^ 1]);
-          }
-          const int cbase = hc * 64 + c * 16;  // query column within the tile
-          float2 da[8];
-          if (!kHoist || pp == 0) {
-            // dA' = 2 scale^2 (dN rden - delta rden) (* decay), masked: t >= s on the diagonal
-#pragma unroll
-            for (int x4 = 0; x4 < 4; ++x4) {
-              const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
-              const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
-              const float2 nv0 = u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]);
-              const float2 nv1 = u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]);
-              da[2 * x4] = fmul2(ffma2(nv0, make_float2(rd.x, rd.y), make_float2(-dr.x, -dr.y)), wsc2);
-              da[2 * x4 + 1] = fmul2(ffma2(nv1, make_float2(rd.z, rd.w), make_float2(-dr.z, -dr.w)), wsc2);
-            }
-            if (diag) {
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const int tl = cbase + 2 * x;
-                if (tl < row) da[x].x = 0.f;
-                if (tl + 1 < row) da[x].y = 0.f;
-              }
-            }
-            if (DECAY) {
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const int tq = qi * kTile + cbase + 2 * x;
-                const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
-                const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
-                da[x].x *= __expf(fminf(ct0 - c_s, 0.f));
-                da[x].y *= __expf(fminf(ct1 - c_s, 0.f));
-              }
-            }
-            if (kHoist) {  // keep dA' for the remaining parts of this query tile
-              uint32_t dw[16];
-#pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                dw[2 * x] = __float_as_uint(da[x].x);
-                dw[2 * x + 1] = __float_as_uint(da[x].y);
-              }
-              tmem_st16(lane_addr + dcol, dw);
-            }
-          } else {
-#pragma unroll
-            for (int x = 0; x < 8; ++x) da[x] = u2f2(rn[cur][2 * x], rn[cur][2 * x + 1]);
-          }
-          uint32_t wv[8];
-#pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            const float2 sv = u2f2(rs[cur][2 * x], rs[cur][2 * x + 1]);
-            acc[8 * c + x] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x]);
-            const float2 w = fmul2(sv, da[x]);
-            wv[x] = pack2<T>(w.x, w.y);
-          }
-          st_tile128(sW, row, cbase, wv[0], wv[1], wv[2], wv[3]);
-          st_tile128(sW, row, cbase + 8, wv[4], wv[5], wv[6], wv[7]);
-          if (c < 3) {
-            tmem_wait_ld();
-            if (c == 2) {  // all of S is in registers: hand the slot back to the issuer
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&bars.s_empty);
-            }
-          }
-        }
-        if (kHoist && pp == 0) tmem_wait_st();
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.t_full[tb]);
-        ++g;
-      }
-      if (!ok) break;
-      // P^T = A / den  (and, with decay, the column part of dc)
-      const int tbp = g & 1;
-      const uint32_t sP = sT + tbp * L::T_BYTES;
-      if (!mbar_wait(&bars.t_empty[tbp], ((g >> 1) & 1) ^ 1, wc)) {
-        ok = false;
-        break;
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int cbase = hc * 64 + c * 16;
-        uint32_t rn[16];
-        if (DECAY) {
-          tmem_ld16(lane_addr + kColDN + hc * 64u + c * 16u, rn);
-          tmem_wait_ld();
-        }
-        uint32_t pv[8];
-#pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          const int tl = cbase + 2 * x;
-          const float2 rd = *reinterpret_cast<const float2*>(v_rd + tl);
-          float a0 = scale2 * acc[8 * c + x].x, a1 = scale2 * acc[8 * c + x].y;
-          if (diag) {
-            if (tl < row) a0 = 0.f;
-            if (tl + 1 < row) a1 = 0.f;
-          }
-          if (DECAY) {
-            const int tq = qi * kTile + tl;
-            const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
-            const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
-            const float x0 = ct0 - c_s, x1 = ct1 - c_s;
-            a0 *= __expf(fminf(x0, 0.f));
-            a1 *= __expf(fminf(x1, 0.f));
-            // the dN slot holds dA'_dec = 2 scale^2 (dN - delta) rden e (causally masked), so
-            // (dN - delta) rden * A = 0.5 dA'_dec sum_p S_p^2
-            if (x0 <= 0.f) csum += 0.5f * __uint_as_float(rn[2 * x]) * acc[8 * c + x].x;
-            if (x1 <= 0.f) csum += 0.5f * __uint_as_float(rn[2 * x + 1]) * acc[8 * c + x].y;
-          }
-          pv[x] = pack2<T>(a0 * rd.x, a1 * rd.y);
-        }
-        st_tile128(sP, row, cbase, pv[0], pv[1], pv[2], pv[3]);
-        st_tile128(sP, row, cbase + 8, pv[4], pv[5], pv[6], pv[7]);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars.t_full[tbp]);
-        mbar_arrive(&bars.dn_empty);
-        mbar_arrive(&bars.vec_empty[vs]);
-      }
-      ++g;
-      if (DECAY && (n % nq == nq - 1)) {
-        // last query tile of this query head: dc_s -= sum_t G[t, s]
-        if (live) atomicAdd(p.dc + (static_cast<size_t>(b) * T_ + sg) * p.HQ + hq, -csum);
-        csum = 0.f;
-      }
-    }
-    // ---- epilogue: dK, dV -> global
-    named_bar_sync(1, 256);
-    if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
-      tc_fence_after();
-      constexpr int HD = D / 2, HV = DV / 2;
-      const size_t rowkv = (static_cast<size_t>(b) * T_ + sg) * p.H + h;
-      T* dkrow = static_cast<T*>(p.dk) + rowkv * D + hc * HD;
-      T* dvrow = static_cast<T*>(p.dv) + rowkv * DV + hc * HV;
-#pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(lane_addr + kColDK + hc * HD + c0, r);
-        tmem_wait_ld();
-        if (live) {
-#pragma unroll
-          for (int v2 = 0; v2 < 2; ++v2) {
-            uint4 w;
-            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
-            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
-            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
-            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
-            *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
-          }
-        }
-      }
-#pragma unroll
-      for (int c0 = 0; c0 < HV; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(lane_addr + kColDV + hc * HV + c0, r);
-        tmem_wait_ld();
-        if (live) {
-#pragma unroll
-          for (int v2 = 0; v2 < 2; ++v2) {
-            uint4 w;
-            w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
-            w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
-            w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
-            w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
-            *reinterpret_cast<uint4*>(dvrow + c0 + 8 * v2) = w;
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tbase, 512);
-}
-
-// ================================================================================================
-// dk / dv kernel, ring form (no decay)
+// dk / dv kernel (tensor-memory ring)
 // ================================================================================================
 // TMEM: a ring of two 128-column slots that the items of every (key tile, query tile) pair pass
 // through in order -- dN^T = V dO^T, then the transposed score parts S^T_0..S^T_{NP-1} (rows: keys)
@@ -1342,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // other half (columns [32,64) and [96,128)).  The issuer reuses a slot only after the compute warps
 // release it, issuing first the dK chain of the W it holds (and, for the last part, the dV chain of
 // P) as tensor-memory-operand MMAs; MMAs of one CTA execute in issue order.
-template <typename T, int D, int DV, int M, bool SUM>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_dkdv_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -1570,6 +753,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The vectors hold v0 = scale^2 / den and v1 = -scale^2 delta / den per query (written by the
     // dq pass), so dA''^T = dN^T v0 + v1 and P^T = v0 sum_p (S^T_p)^2; W''^T_p = S^T_p dA''^T is
     // half of the true W^T_p, and the dK epilogue doubles the accumulator.
+    // decay: e(t,s) = exp(min(c_t - c_s, 0)) is folded into dA''^T when it is formed and again
+    // into P^T; the column part of dc, sum_t (dN - delta) rden A_ts over pairs with c_t - c_s <= 0,
+    // is sum_t dA''_dec S^2 (S^2 summed over the parts), added to dc once per query head.
+    float csum = 0.f;
     bool ok = true;
     int it = 0;
     for (int n = 0; n < nwork && ok; ++n) {
@@ -1578,6 +765,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int vs = n & 1;
       const float* v_rd = vec + (vs * 2 + 0) * kTile;
       const float* v_dr = vec + (vs * 2 + 1) * kTile;
+      const float* cb = nullptr;
+      float c_s = 0.f;
+      if (DECAY) {
+        const int hq = h * p.G + n / nq;
+        cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
+        c_s = live ? cb[static_cast<size_t>(sg) * p.HQ] : 0.f;
+      }
       if (!mbar_wait(&bars.vec_full[vs], (n >> 1) & 1, wc)) {
         ok = false;
         break;
@@ -1613,6 +807,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (tl + 1 < row) d0.y = 0.f;
               if (tl + 2 < row) d1.x = 0.f;
               if (tl + 3 < row) d1.y = 0.f;
+            }
+            if (DECAY) {
+              const int tq = qi * kTile + cbase + 4 * x4;
+              const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
+              const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
+              const float ct2 = tq + 2 < T_ ? __ldg(cb + static_cast<size_t>(tq + 2) * p.HQ) : 0.f;
+              const float ct3 = tq + 3 < T_ ? __ldg(cb + static_cast<size_t>(tq + 3) * p.HQ) : 0.f;
+              d0.x *= __expf(fminf(ct0 - c_s, 0.f));
+              d0.y *= __expf(fminf(ct1 - c_s, 0.f));
+              d1.x *= __expf(fminf(ct2 - c_s, 0.f));
+              d1.y *= __expf(fminf(ct3 - c_s, 0.f));
             }
             dap[8 * c + 2 * x4] = bf2_pack(d0);
             dap[8 * c + 2 * x4 + 1] = bf2_pack(d1);
@@ -1665,6 +870,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int tl = cbase + 2 * x2;
               const float2 a = fmul2(acc[8 * c + x2], *reinterpret_cast<const float2*>(v_rd + tl));
               float a0 = a.x, a1 = a.y;
+              if (DECAY) {
+                const int tq = qi * kTile + tl;
+                const float x0 = (tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f) - c_s;
+                const float x1 = (tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f) - c_s;
+                a0 *= __expf(fminf(x0, 0.f));
+                a1 *= __expf(fminf(x1, 0.f));
+                const float2 dd = bf2_unpack(dap[8 * c + x2]);  // dA''_dec, causally masked
+                if (x0 <= 0.f) csum = fmaf(dd.x, acc[8 * c + x2].x, csum);
+                if (x1 <= 0.f) csum = fmaf(dd.y, acc[8 * c + x2].y, csum);
+              }
               if (diag) {
                 if (tl < row) a0 = 0.f;
                 if (tl + 1 < row) a1 = 0.f;
@@ -1681,6 +896,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&bars.i_free[x]);
           if (pp == NP - 1) mbar_arrive(&bars.vec_empty[vs]);
         }
+      }
+      if (DECAY && n % nq == nq - 1) {  // last query tile of this query head: dc_s -= column sum
+        if (ok && live) atomicAdd(p.dc + (static_cast<size_t>(b) * T_ + sg) * p.HQ + h * p.G + n / nq, -csum);
+        csum = 0.f;
       }
     }
     // ---- epilogue: dK, dV -> global
@@ -1750,19 +969,19 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (e) return e;
   const int nt = (p.T + kTile - 1) / kTile;
   if (p.phases != 2) {
-    // decay needs sum_p S_p^2 for its dc row sums and keeps the two-slot kernel; otherwise the ring
-    auto kern = DECAY ? attn_bwd_dq_tc<T, D, DV, M, SUM, DECAY> : attn_bwd_dq_ring_tc<T, D, DV, M, SUM>;
-    const size_t smem = (DECAY ? L::DQ_TOTAL : L::DQR_TOTAL) + 1024;
+    // dq pass: tensor-memory ring with two issuers (decay: dc row sums written here)
+    auto kern = attn_bwd_dq_ring_tc<T, D, DV, M, SUM, DECAY>;
+    const size_t smem = L::DQR_TOTAL + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
-    kern<<<dim3(nt, p.B * p.HQ), DECAY ? kThreads : kThreadsRing, smem, st>>>(tq, tk, tv, to, p);
+    kern<<<dim3(nt, p.B * p.HQ), kThreadsRing, smem, st>>>(tq, tk, tv, to, p);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   if (p.phases != 1) {
-    // decay (dc column sums) keeps the shared-memory W/P form; otherwise the tensor-memory ring
-    auto kern = DECAY ? attn_bwd_dkdv_tc<T, D, DV, M, SUM, DECAY> : attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM>;
-    const size_t smem = DECAY ? L::KV_TOTAL : L::KR_TOTAL;  // no static shared memory: no alignment slack
+    // dk/dv pass: tensor-memory ring (decay: dc column sums added here)
+    auto kern = attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM, DECAY>;
+    const size_t smem = L::KR_TOTAL;  // no static shared memory: no alignment slack
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
