@@ -101,7 +101,8 @@ KATA_API int kata_attn_fwd(const kata_attn_fwd_args* args, kata_stream_t stream)
  * (kata/parallel_kata_attn.py:755-901, kata/kernels/parallel_kata_sum.py), the PyTorch
  * fallbacks parallel_kata_attn_bwd (:49-146) / parallel_kata_attn_bwd_sum_torch (:579-653),
  * and the autograd recompute of the decayed form (_KataDecayFunction.backward, :329-347).
- * workspace: kata_attn_bwd_workspace_bytes(args) bytes of device memory (may be 0 -> NULL ok).
+ * workspace: kata_attn_bwd_workspace_bytes(args) bytes of device memory (may be 0 -> NULL ok);
+ * the size depends on B, T, HQ and on whether c is given (decay adds a head-major copy of c).
  * ------------------------------------------------------------------------------------------- */
 typedef struct {
   const void* q;     /* (B,T,HQ,D)  dtype */

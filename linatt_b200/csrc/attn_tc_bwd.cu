@@ -38,19 +38,22 @@ constexpr int kChainWarp = 10;
 
 struct BwdWs {
   // workspace views (fp32), each 16-byte aligned:
-  //   delta (B,T,HQ) | rden (B,HQ,Tp) | delta*rden (B,HQ,Tp)   with Tp = T rounded up to 128,
-  // so that the 128 values of every query tile are one contiguous, in-bounds, 512-byte run that a
-  // bulk copy can move into shared memory (rows past T hold rden = 1, delta*rden = 0).
+  //   delta (B,T,HQ) | rden (B,HQ,Tp) | delta*rden (B,HQ,Tp) [| c (B,HQ,Tp), decay only]
+  // with Tp = T rounded up to 128, so that the 128 values of every tile are one contiguous,
+  // in-bounds, 512-byte run that a bulk copy can move into shared memory (rows past T hold
+  // rden = 1, delta*rden = 0, c = 0).  The head-major copy of the decay cumsum c lets both kernels
+  // stage a tile's 128 values with one bulk copy instead of 128 strided loads per thread.
   float* delta;
   float* rden;
   float* dr;
+  float* cT;
   int Tp;
 };
 __host__ __device__ inline BwdWs ws_views(float* base, int B, int T, int HQ) {
   const int Tp = (T + 127) & ~127;
   const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
   const size_t n1 = static_cast<size_t>(B) * HQ * Tp;
-  return BwdWs{base, base + n0, base + n0 + n1, Tp};
+  return BwdWs{base, base + n0, base + n0 + n1, base + n0 + 2 * n1, Tp};
 }
 
 template <int D, int DV>
@@ -62,7 +65,8 @@ struct BwdSmem {
   static constexpr int DQ_OFF_Q = 0;
   static constexpr int DQ_OFF_O = DQ_OFF_Q + Q_BYTES;
   static constexpr int DQ_OFF_RING = DQ_OFF_O + O_BYTES;
-  static constexpr int DQR_TOTAL = DQ_OFF_RING + 4 * ITEM;
+  static constexpr int DQ_OFF_C = DQ_OFF_RING + 4 * ITEM;  // decay only: c of the key tile in ring slot r
+  static constexpr int dqr_total(bool decay) { return DQ_OFF_C + (decay ? 4 * kTile * 4 : 0); }
   // dkdv kernel: K, V resident; a ring of four dO/Q tiles (two query tiles); the W / P operands
   // stay in tensor memory
   static constexpr int KV_OFF_K = 0;
@@ -71,8 +75,10 @@ struct BwdSmem {
   static constexpr int KR_RING = 4;
   static constexpr int KR_OFF_RING = KV_OFF_RING;
   static constexpr int KR_OFF_VEC = KR_OFF_RING + KR_RING * ITEM;
-  static constexpr int KR_OFF_BARS = KR_OFF_VEC + 2 * 2 * kTile * 4;
-  static constexpr int KR_TOTAL = KR_OFF_BARS + 256;
+  // [stage][v0, v1 (, c with decay)][128]; the barrier block follows the vectors
+  static constexpr int kr_nvec(bool decay) { return decay ? 3 : 2; }
+  static constexpr int kr_off_bars(bool decay) { return KR_OFF_VEC + 2 * kr_nvec(decay) * kTile * 4; }
+  static constexpr int kr_total(bool decay) { return kr_off_bars(decay) + 256; }
 };
 
 struct DkvRingBars {
@@ -100,6 +106,18 @@ __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
+}
+
+// Head-major copy of the decay cumsum: cT[(b*HQ + hq)*Tp + t] = c[(b*T + t)*HQ + hq], 0 past T.
+__global__ void decay_c_transpose(const float* __restrict__ c, float* __restrict__ cT, int B, int T, int HQ, int Tp) {
+  const size_t n = static_cast<size_t>(B) * Tp * HQ;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int hq = static_cast<int>(i % HQ);
+    const size_t bt = i / HQ;
+    const int t = static_cast<int>(bt % Tp), b = static_cast<int>(bt / Tp);
+    cT[(static_cast<size_t>(b) * HQ + hq) * Tp + t] = t < T ? c[(static_cast<size_t>(b) * T + t) * HQ + hq] : 0.f;
+  }
 }
 
 // ================================================================================================
@@ -207,9 +225,16 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             for (int bx = 0; bx < NVBOX; ++bx)
               tma_load_4d(dst + bx * (kTile * VCW * 2), &tmV, &bars.ring_full[slot], bx * VCW, h, j * kTile, b);
           } else {
-            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
+            // with decay, the key tile's c (head-major copy) rides with K_j, whose slot is held
+            // until the tile's last dQ chain, i.e. after the compute warps have read it
+            mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES + (DECAY ? kTile * 4 : 0));
             for (int bx = 0; bx < NBOX; ++bx)
               tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, j * kTile, b);
+            if (DECAY)
+              bulk_load(smem + L::DQ_OFF_C + slot * (kTile * 4),
+                        ws_views(p.delta, p.B, T_, p.HQ).cT + (static_cast<size_t>(b) * p.HQ + hq) *
+                            static_cast<size_t>((T_ + 127) & ~127) + static_cast<size_t>(j) * kTile,
+                        kTile * 4, &bars.ring_full[slot]);
           }
         }
       }
@@ -425,10 +450,17 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
         }
         if (DECAY) {
 #pragma unroll
+          // the key tile's c, staged with K_j: wait for that load (the slot is not refilled before
+          // the tile's last dQ chain, which follows this warp's release of the tile's parts)
+          if (!mbar_wait(&bars.ring_full[(2 * j + 1) & 3], static_cast<uint32_t>(j >> 1) & 1u, wc)) {
+            ok = false;
+            break;
+          }
+          const float* cs = reinterpret_cast<const float*>(smem + L::DQ_OFF_C + ((2 * j + 1) & 3) * (kTile * 4)) + hc * 64;
+#pragma unroll
           for (int x2 = 0; x2 < 32; ++x2) {
-            const int sk = j * kTile + hc * 64 + 2 * x2;
-            const float cs0 = sk < T_ ? __ldg(cb + static_cast<size_t>(sk) * p.HQ) : 0.f;
-            const float cs1 = sk + 1 < T_ ? __ldg(cb + static_cast<size_t>(sk + 1) * p.HQ) : 0.f;
+            const float2 csv = *reinterpret_cast<const float2*>(cs + 2 * x2);
+            const float cs0 = csv.x, cs1 = csv.y;
             const float x0 = c_t - cs0, x1 = c_t - cs1;
             da[x2].x *= __expf(fminf(x0, 0.f));
             da[x2].y *= __expf(fminf(x1, 0.f));
@@ -545,7 +577,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(L::KR_RING == kR, "ring depth");
 
   extern __shared__ __align__(1024) uint8_t smem[];
-  DkvRingBars& bars = *reinterpret_cast<DkvRingBars*>(smem + L::KR_OFF_BARS);
+  constexpr int kNV = L::kr_nvec(DECAY);  // per-query vectors per stage
+  DkvRingBars& bars = *reinterpret_cast<DkvRingBars*>(smem + L::kr_off_bars(DECAY));
   if ((smem_u32(smem) & 1023u) != 0) {
     if (threadIdx.x == 0 && p.status) atomicCAS(p.status, 0, kStatusWaitTimeout + 1);
     return;
@@ -587,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars.tmem_base;
-  float* vec = reinterpret_cast<float*>(smem + L::KR_OFF_VEC);  // [stage][0: rden, 1: delta*rden][128]
+  float* vec = reinterpret_cast<float*>(smem + L::KR_OFF_VEC);  // [stage][0: v0, 1: v1, 2: c (decay)][128]
 
   if (warp == 0) {
     if (lane == 0) {
@@ -611,9 +644,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + ti;
-        mbar_arrive_expect_tx(&bars.vec_full[vs], 2 * kTile * 4);
-        bulk_load(vec + (vs * 2 + 0) * kTile, ws.rden + hm, kTile * 4, &bars.vec_full[vs]);
-        bulk_load(vec + (vs * 2 + 1) * kTile, ws.dr + hm, kTile * 4, &bars.vec_full[vs]);
+        mbar_arrive_expect_tx(&bars.vec_full[vs], (DECAY ? 3 : 2) * kTile * 4);
+        bulk_load(vec + (vs * kNV + 0) * kTile, ws.rden + hm, kTile * 4, &bars.vec_full[vs]);
+        bulk_load(vec + (vs * kNV + 1) * kTile, ws.dr + hm, kTile * 4, &bars.vec_full[vs]);
+        if (DECAY) bulk_load(vec + (vs * kNV + 2) * kTile, ws.cT + hm, kTile * 4, &bars.vec_full[vs]);
         nv = n + 1;
         for (int item = 0; item < 2; ++item, ++r) {  // dO_n then Q_n (dN is the first MMA of a pair)
           const int slot = r % kR;
@@ -763,15 +797,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qi = kj + n % nq;
       const bool diag = (qi == kj);
       const int vs = n & 1;
-      const float* v_rd = vec + (vs * 2 + 0) * kTile;
-      const float* v_dr = vec + (vs * 2 + 1) * kTile;
-      const float* cb = nullptr;
+      const float* v_rd = vec + (vs * kNV + 0) * kTile;
+      const float* v_dr = vec + (vs * kNV + 1) * kTile;
+      const float* v_c = vec + (vs * kNV + 2) * kTile;  // decay: c of the query tile
       float c_s = 0.f;
-      if (DECAY) {
-        const int hq = h * p.G + n / nq;
-        cb = p.c + static_cast<size_t>(b) * T_ * p.HQ + hq;
-        c_s = live ? cb[static_cast<size_t>(sg) * p.HQ] : 0.f;
-      }
+      if (DECAY && live) c_s = p.c[(static_cast<size_t>(b) * T_ + sg) * p.HQ + h * p.G + n / nq];
       if (!mbar_wait(&bars.vec_full[vs], (n >> 1) & 1, wc)) {
         ok = false;
         break;
@@ -809,15 +839,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (tl + 3 < row) d1.y = 0.f;
             }
             if (DECAY) {
-              const int tq = qi * kTile + cbase + 4 * x4;
-              const float ct0 = tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f;
-              const float ct1 = tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f;
-              const float ct2 = tq + 2 < T_ ? __ldg(cb + static_cast<size_t>(tq + 2) * p.HQ) : 0.f;
-              const float ct3 = tq + 3 < T_ ? __ldg(cb + static_cast<size_t>(tq + 3) * p.HQ) : 0.f;
-              d0.x *= __expf(fminf(ct0 - c_s, 0.f));
-              d0.y *= __expf(fminf(ct1 - c_s, 0.f));
-              d1.x *= __expf(fminf(ct2 - c_s, 0.f));
-              d1.y *= __expf(fminf(ct3 - c_s, 0.f));
+              const float4 ct = *reinterpret_cast<const float4*>(v_c + cbase + 4 * x4);
+              d0.x *= __expf(fminf(ct.x - c_s, 0.f));
+              d0.y *= __expf(fminf(ct.y - c_s, 0.f));
+              d1.x *= __expf(fminf(ct.z - c_s, 0.f));
+              d1.y *= __expf(fminf(ct.w - c_s, 0.f));
             }
             dap[8 * c + 2 * x4] = bf2_pack(d0);
             dap[8 * c + 2 * x4 + 1] = bf2_pack(d1);
@@ -871,9 +897,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float2 a = fmul2(acc[8 * c + x2], *reinterpret_cast<const float2*>(v_rd + tl));
               float a0 = a.x, a1 = a.y;
               if (DECAY) {
-                const int tq = qi * kTile + tl;
-                const float x0 = (tq < T_ ? __ldg(cb + static_cast<size_t>(tq) * p.HQ) : 0.f) - c_s;
-                const float x1 = (tq + 1 < T_ ? __ldg(cb + static_cast<size_t>(tq + 1) * p.HQ) : 0.f) - c_s;
+                const float2 ct = *reinterpret_cast<const float2*>(v_c + tl);
+                const float x0 = ct.x - c_s, x1 = ct.y - c_s;
                 a0 *= __expf(fminf(x0, 0.f));
                 a1 *= __expf(fminf(x1, 0.f));
                 const float2 dd = bf2_unpack(dap[8 * c + x2]);  // dA''_dec, causally masked
@@ -968,10 +993,15 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (!e) e = make_tm_tokens(&to, p.dout, p.B, p.T, p.HQ, DV, VCW);
   if (e) return e;
   const int nt = (p.T + kTile - 1) / kTile;
+  if (DECAY) {  // head-major copy of c for both passes' bulk copies
+    const BwdWs ws = ws_views(p.delta, p.B, p.T, p.HQ);
+    decay_c_transpose<<<296, 256, 0, st>>>(p.c, ws.cT, p.B, p.T, p.HQ, ws.Tp);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
   if (p.phases != 2) {
     // dq pass: tensor-memory ring with two issuers (decay: dc row sums written here)
     auto kern = attn_bwd_dq_ring_tc<T, D, DV, M, SUM, DECAY>;
-    const size_t smem = L::DQR_TOTAL + 1024;
+    const size_t smem = L::dqr_total(DECAY) + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
@@ -981,7 +1011,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (p.phases != 1) {
     // dk/dv pass: tensor-memory ring (decay: dc column sums added here)
     auto kern = attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM, DECAY>;
-    const size_t smem = L::KR_TOTAL;  // no static shared memory: no alignment slack
+    const size_t smem = L::kr_total(DECAY);  // no static shared memory: no alignment slack
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
@@ -1026,10 +1056,10 @@ int bwd_dims(const AttnBwdParams& p, bool sum, cudaStream_t st) {
 
 }  // namespace
 
-size_t tc_bwd_workspace_bytes(int B, int T, int HQ) {
+size_t tc_bwd_workspace_bytes(int B, int T, int HQ, bool decay) {
   const size_t Tp = (static_cast<size_t>(T) + 127) & ~static_cast<size_t>(127);
   const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
-  return sizeof(float) * (n0 + 2 * static_cast<size_t>(B) * HQ * Tp);
+  return sizeof(float) * (n0 + (decay ? 3 : 2) * static_cast<size_t>(B) * HQ * Tp);
 }
 
 bool tc_bwd_supported(int dtype, int D, int Dv, int M, bool sum) {

@@ -12,7 +12,7 @@ bool tc_fwd_supported(int dtype, int D, int Dv, int M, bool sum);
 bool tc_bwd_supported(int dtype, int D, int Dv, int M, bool sum);
 int tc_attn_fwd(const AttnFwdParams& p, int dtype, bool sum, cudaStream_t st);
 int tc_attn_bwd(const AttnBwdParams& p, int dtype, bool sum, cudaStream_t st);
-size_t tc_bwd_workspace_bytes(int B, int T, int HQ);
+size_t tc_bwd_workspace_bytes(int B, int T, int HQ, bool decay);
 }  // namespace kata
 
 using namespace kata;
@@ -60,8 +60,9 @@ extern "C" int kata_attn_fwd(const kata_attn_fwd_args* a, kata_stream_t stream) 
 extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->HQ < 1) return 0;
   // fp32 delta = <o, dO> per (b, t, hq), plus 1/den and delta/den in a padded head-major layout
-  // for the tensor-core key-tile kernel (the SIMT kernels use the first part only)
-  return tc_bwd_workspace_bytes(a->B, a->T, a->HQ);
+  // for the tensor-core key-tile kernel, and with decay (c given) a head-major copy of c (the SIMT
+  // kernels use the first part only)
+  return tc_bwd_workspace_bytes(a->B, a->T, a->HQ, a->c != nullptr);
 }
 
 int kata::attn_bwd_impl(const kata_attn_bwd_args* a, const float* delta_in, kata_stream_t stream) {
