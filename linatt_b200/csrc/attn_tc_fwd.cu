@@ -56,7 +56,7 @@ struct FwdBarriers {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  float den_x[2][kBT];  // partial row sums of the two column halves
+  alignas(16) float den_x[2][kBT];  // partial row sums of the two column halves (decay: c staging)
 };
 
 template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
@@ -310,13 +310,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (DECAY) {
+        // The 64 key columns' c values (strided by HQ in global memory) are staged per warp, 32 at a
+        // time, in the warp's own 32 floats of den_x (the row-sum exchange, idle until the epilogue;
+        // each warp writes only its slice there too): one load per lane, then broadcast reads.
+        float* cbuf = &bars.den_x[hc][quarter * 32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int s0 = s_base + 2 * i;
-          const float cs0 = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
-          const float cs1 = (s0 + 1 < T_) ? __ldg(cbase + static_cast<size_t>(s0 + 1) * p.HQ) : 0.f;
-          acc[i].x *= __expf(fminf(c_t - cs0, 0.f));
-          acc[i].y *= __expf(fminf(c_t - cs1, 0.f));
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int s0 = s_base + h2 * 32 + lane;
+          cbuf[lane] = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 cs = *reinterpret_cast<const float4*>(cbuf + 4 * i);
+            float2& a0 = acc[h2 * 16 + 2 * i];
+            float2& a1 = acc[h2 * 16 + 2 * i + 1];
+            a0.x *= __expf(fminf(c_t - cs.x, 0.f));
+            a0.y *= __expf(fminf(c_t - cs.y, 0.f));
+            a1.x *= __expf(fminf(c_t - cs.z, 0.f));
+            a1.y *= __expf(fminf(c_t - cs.w, 0.f));
+          }
+          __syncwarp();  // every lane has read the slice before it is rewritten
         }
       }
 #pragma unroll
