@@ -147,6 +147,8 @@ def test_config1_fp32(M, variant):
     (1, 257, 2, 2, 128, 2, "sum", False),
     (1, 300, 2, 2, 128, 4, "sum", False),
     (1, 300, 2, 2, 64, 4, "concat", True),
+    (1, 300, 4, 2, 128, 2, "concat", True),
+    (2, 257, 2, 2, 128, 1, "concat", True),
     (1, 520, 1, 1, 128, 8, "concat", False),
 ])
 def test_half_precision_vs_oracle(dtype, B, T, HQ, H, D, M, score, decay):
@@ -162,6 +164,20 @@ def test_half_precision_vs_oracle(dtype, B, T, HQ, H, D, M, score, decay):
         for n in ("dq", "dk"):
             assert np.abs(got[n]).max() < 1e-2
         return
+    assert_close(got, ref, TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decay_non_monotone_c_vs_oracle(dtype):
+    """Decay with a cumsum c that rises as well as falls: pairs with c_t - c_s > 0 take the clamp
+    exp(min(., 0)) = 1 and contribute nothing to dc (GQA, several query and key tiles)."""
+    pka = _pka("auto")
+    B, T, HQ, H, D, M = 1, 300, 4, 2, 128, 2
+    q, k, v, _, do = draw(41, B, T, HQ, H, D, D, dtype)
+    g = torch.Generator().manual_seed(42)
+    c = (0.3 * torch.randn(B, T, HQ, generator=g)).cumsum(1)
+    got = run(pka, q, k, v, do, M, "concat", c)
+    ref = oracle(q.float(), k.float(), v.float(), do.float(), M, "concat", c)
     assert_close(got, ref, TOL[dtype])
 
 
