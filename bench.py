@@ -45,6 +45,7 @@ sys.path.insert(0, str(ROOT))
 B, T, H, D, DV = 16, 4096, 8, 128, 128
 M = 4          # num_groups of the headline configuration (overridable with --num-groups)
 SCORE = "concat"
+DECAY = False  # --decay: auxiliary line of the decayed form (parallel_kata_attn_decay)
 METRIC = "KATA attn fwd+bwd tokens/s/GPU at B16·T4096·H8·D128; % of bf16 TC peak"
 UNIT = "tokens/s"
 
@@ -64,7 +65,8 @@ def alg_flops():
 
 def workload_config(n_gpus: int) -> dict:
     return {
-        "workload": f"KATA-SPD flash attention fwd+bwd, {SCORE} score M={M}, causal, bf16 (config 3)",
+        "workload": f"KATA-SPD flash attention fwd+bwd, {SCORE} score M={M}, causal, bf16 (config 3)"
+                    + (", decay (c = cumsum of -softplus(N(0,1)) log-decays, dc computed)" if DECAY else ""),
         "batch_per_gpu": B, "global_batch": B * n_gpus, "seq_len": T, "heads": H, "head_dim": D,
         "value_dim": DV, "num_groups": M, "score": SCORE,
         "parallelism": f"batch*head shard x{n_gpus}, no collective",
@@ -214,6 +216,10 @@ class AbiStep:
         self.dk = torch.empty_like(self.dq)
         self.dv = torch.empty(B, T, H, DV, device=dev, dtype=torch.bfloat16)
         self.status = _lib.status_word(dev)
+        if DECAY:  # decayed form: c (B,T,H) fp32 input, dc output
+            g = torch.Generator(device=dev).manual_seed(99)
+            self.c = (-torch.nn.functional.softplus(torch.randn(B, T, H, device=dev, generator=g))).cumsum(1)
+            self.dc = torch.empty(B, T, H, device=dev, dtype=torch.float32)
         scale = 1.0 / math.sqrt(D // M)
         sc = _lib.SCORE[SCORE]
         self.fa = _lib.AttnFwdArgs(o=self.o.data_ptr(), den=self.den.data_ptr(), status=self.status.data_ptr(),
@@ -221,6 +227,9 @@ class AbiStep:
         self.ba = _lib.AttnBwdArgs(o=self.o.data_ptr(), den=self.den.data_ptr(), dq=self.dq.data_ptr(),
                                    dk=self.dk.data_ptr(), dv=self.dv.data_ptr(), status=self.status.data_ptr(),
                                    dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=DV, M=M, score=sc, algo=1, scale=scale)
+        if DECAY:
+            self.fa.c = self.ba.c = self.c.data_ptr()
+            self.ba.dc = self.dc.data_ptr()
         nbytes = self.L.kata_attn_bwd_workspace_bytes(self.ba)
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.ba.workspace = self.ws.data_ptr()
@@ -406,7 +415,7 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
     dom = max(kern_ms, key=kern_ms.get)
     ach = kernels[dom]["tflops"]
     roofline = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                "frac": ach / peak, "traffic": load_traffic(dom), "peak_source": peak_src,
+                "frac": ach / peak, "traffic": None if DECAY else load_traffic(dom), "peak_source": peak_src,
                 "step_tflops": STEP_FLOPS / (ms_step / 1e3) / 1e12,
                 "step_frac": STEP_FLOPS / (ms_step / 1e3) / 1e12 / peak, "kernels": kernels}
 
@@ -658,14 +667,20 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--num-groups", type=int, default=4, help="M (the benchmark metric is quoted at M=4)")
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
+    ap.add_argument("--decay", action="store_true",
+                    help="auxiliary line: the decayed form (device-timed only; no e2e / CPU legs)")
     ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta"], default="attn",
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
                          "delta: the SPD delta rule at the mixer geometry")
     ap.add_argument("--batch", type=int, default=16,
                     help="B per GPU (the metric is quoted at 16; smaller values only for profiler captures)")
     args = ap.parse_args()
-    global M, SCORE, B
-    M, SCORE, B = args.num_groups, args.score, args.batch
+    global M, SCORE, B, DECAY
+    M, SCORE, B, DECAY = args.num_groups, args.score, args.batch, args.decay
+    if DECAY:
+        if SCORE != "concat":
+            ap.error("--decay pairs with the concat score only (as in the reference)")
+        args.no_e2e = args.no_cpu_baseline = True
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
