@@ -66,7 +66,8 @@ struct BwdSmem {
   static constexpr int DQ_OFF_O = DQ_OFF_Q + Q_BYTES;
   static constexpr int DQ_OFF_RING = DQ_OFF_O + O_BYTES;
   static constexpr int DQ_OFF_C = DQ_OFF_RING + 4 * ITEM;  // decay only: c of the key tile in ring slot r
-  static constexpr int dqr_total(bool decay) { return DQ_OFF_C + (decay ? 4 * kTile * 4 : 0); }
+  static constexpr int DQ_OFF_F = DQ_OFF_C + 4 * kTile * 4;  // decay only: per-compute-warp column factors
+  static constexpr int dqr_total(bool decay) { return DQ_OFF_C + (decay ? 4 * kTile * 4 + 8 * 64 * 4 : 0); }
   // dkdv kernel: K, V resident; a ring of four dO/Q tiles (two query tiles); the W / P operands
   // stay in tensor memory
   static constexpr int KV_OFF_K = 0;
@@ -449,24 +450,44 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
           }
         }
         if (DECAY) {
-#pragma unroll
           // the key tile's c, staged with K_j: wait for that load (the slot is not refilled before
           // the tile's last dQ chain, which follows this warp's release of the tile's parts)
-          if (!mbar_wait(&bars.ring_full[(2 * j + 1) & 3], static_cast<uint32_t>(j >> 1) & 1u, wc)) {
+          if (!mbar_wait_w(&bars.ring_full[(2 * j + 1) & 3], static_cast<uint32_t>(j >> 1) & 1u, wc)) {
             ok = false;
             break;
           }
           const float* cs = reinterpret_cast<const float*>(smem + L::DQ_OFF_C + ((2 * j + 1) & 3) * (kTile * 4)) + hc * 64;
+          // Factored decay: with lo = min of c over this warp's 64 columns, a row with c_t <= lo has
+          // every c_t - c_s <= 0 and e = exp(c_t - lo) * exp(lo - c_s), both factors <= 1 (no
+          // overflow; an underflow only flushes values below 1e-38).  The column factors are made
+          // once per warp (two per lane) instead of one exponential per element and thread.
+          float* fb = reinterpret_cast<float*>(smem + L::DQ_OFF_F) + (warp - kComputeWarp0) * 64;
+          const float2 cl = *reinterpret_cast<const float2*>(cs + 2 * lane);
+          float lo = fminf(cl.x, cl.y);
 #pragma unroll
-          for (int x2 = 0; x2 < 32; ++x2) {
-            const float2 csv = *reinterpret_cast<const float2*>(cs + 2 * x2);
-            const float cs0 = csv.x, cs1 = csv.y;
-            const float x0 = c_t - cs0, x1 = c_t - cs1;
-            da[x2].x *= __expf(fminf(x0, 0.f));
-            da[x2].y *= __expf(fminf(x1, 0.f));
-            if (x0 > 0.f) cm[x2 >> 4] |= 1u << ((2 * x2) & 31);
-            if (x1 > 0.f) cm[x2 >> 4] |= 1u << ((2 * x2 + 1) & 31);
+          for (int o = 16; o > 0; o >>= 1) lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+          *reinterpret_cast<float2*>(fb + 2 * lane) = make_float2(__expf(lo - cl.x), __expf(lo - cl.y));
+          __syncwarp();
+          if (!__any_sync(0xffffffffu, c_t > lo)) {
+            const float rt = __expf(c_t - lo);
+#pragma unroll
+            for (int x4 = 0; x4 < 16; ++x4) {
+              const float4 f = *reinterpret_cast<const float4*>(fb + 4 * x4);
+              da[2 * x4] = fmul2(da[2 * x4], make_float2(rt * f.x, rt * f.y));
+              da[2 * x4 + 1] = fmul2(da[2 * x4 + 1], make_float2(rt * f.z, rt * f.w));
+            }
+          } else {  // some row of this warp has c_t > c_s somewhere: exponentials per element
+#pragma unroll
+            for (int x2 = 0; x2 < 32; ++x2) {
+              const float2 csv = *reinterpret_cast<const float2*>(cs + 2 * x2);
+              const float x0 = c_t - csv.x, x1 = c_t - csv.y;
+              da[x2].x *= __expf(fminf(x0, 0.f));
+              da[x2].y *= __expf(fminf(x1, 0.f));
+              if (x0 > 0.f) cm[x2 >> 4] |= 1u << ((2 * x2) & 31);
+              if (x1 > 0.f) cm[x2 >> 4] |= 1u << ((2 * x2 + 1) & 31);
+            }
           }
+          __syncwarp();  // every lane has read the factors before the next tile rewrites them
         }
       }
       const bool any_clamp = DECAY && (cm[0] | cm[1]) != 0u;

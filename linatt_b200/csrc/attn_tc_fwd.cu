@@ -310,26 +310,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (DECAY) {
-        // The 64 key columns' c values (strided by HQ in global memory) are staged per warp, 32 at a
-        // time, in the warp's own 32 floats of den_x (the row-sum exchange, idle until the epilogue;
-        // each warp writes only its slice there too): one load per lane, then broadcast reads.
-        float* cbuf = &bars.den_x[hc][quarter * 32];
+        // The 64 key columns' c values (strided by HQ in global memory) are loaded per warp, 32 at a
+        // time, one per lane.  Factored decay: with lo = the warp minimum of those 32 values, a row
+        // with c_t <= lo has every c_t - c_s <= 0 and e = exp(c_t - lo) * exp(lo - c_s), both
+        // factors <= 1 (no overflow; an underflow only flushes values below 1e-38), so the column
+        // factors go to the warp's own 32 floats of den_x (the row-sum exchange, idle until the
+        // epilogue; each warp writes only its slice there too) and each row takes one exponential.
+        // If any row of the warp has c_t > lo, the warp takes exponentials per element, with c_s
+        // from the lane that loaded it.
+        float* fbuf = &bars.den_x[hc][quarter * 32];
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           const int s0 = s_base + h2 * 32 + lane;
-          cbuf[lane] = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
-          __syncwarp();
+          const float cl = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
+          float lo = cl;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 cs = *reinterpret_cast<const float4*>(cbuf + 4 * i);
-            float2& a0 = acc[h2 * 16 + 2 * i];
-            float2& a1 = acc[h2 * 16 + 2 * i + 1];
-            a0.x *= __expf(fminf(c_t - cs.x, 0.f));
-            a0.y *= __expf(fminf(c_t - cs.y, 0.f));
-            a1.x *= __expf(fminf(c_t - cs.z, 0.f));
-            a1.y *= __expf(fminf(c_t - cs.w, 0.f));
+          for (int o = 16; o > 0; o >>= 1) lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+          if (!__any_sync(0xffffffffu, c_t > lo)) {
+            fbuf[lane] = __expf(lo - cl);
+            __syncwarp();
+            const float rt = __expf(c_t - lo);
+            const float2 rt2 = make_float2(rt, rt);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 f = *reinterpret_cast<const float4*>(fbuf + 4 * i);
+              acc[h2 * 16 + 2 * i] = fmul2(acc[h2 * 16 + 2 * i], fmul2(rt2, make_float2(f.x, f.y)));
+              acc[h2 * 16 + 2 * i + 1] = fmul2(acc[h2 * 16 + 2 * i + 1], fmul2(rt2, make_float2(f.z, f.w)));
+            }
+            __syncwarp();  // every lane has read the slice before it is rewritten
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float cs0 = __shfl_sync(0xffffffffu, cl, 2 * i);
+              const float cs1 = __shfl_sync(0xffffffffu, cl, 2 * i + 1);
+              acc[h2 * 16 + i].x *= __expf(fminf(c_t - cs0, 0.f));
+              acc[h2 * 16 + i].y *= __expf(fminf(c_t - cs1, 0.f));
+            }
           }
-          __syncwarp();  // every lane has read the slice before it is rewritten
         }
       }
 #pragma unroll
