@@ -258,6 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < nk && ok; ++j) {
       float2 acc[32];
       int slot = 0;
+      float cpre[2] = {0.f, 0.f};  // decay: this lane's two key columns' c, loaded ahead of the parts
+      if (DECAY) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int s0 = j * kBK + hc * 64 + h2 * 32 + lane;
+          cpre[h2] = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
+        }
+      }
       for (int pp = 0; pp < NP; ++pp, ++u) {
         slot = u % kSlots;
         if (!mbar_wait(&bars.s_full[slot], (u / kSlots) & 1, wc)) {
@@ -310,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (DECAY) {
-        // The 64 key columns' c values (strided by HQ in global memory) are loaded per warp, 32 at a
-        // time, one per lane.  Factored decay: with lo = the warp minimum of those 32 values, a row
+        // The 64 key columns' c values (strided by HQ in global memory) were loaded at the start of
+        // the tile, one per lane for each half of 32.  Factored decay: with lo = the warp minimum of those 32 values, a row
         // with c_t <= lo has every c_t - c_s <= 0 and e = exp(c_t - lo) * exp(lo - c_s), both
         // factors <= 1 (no overflow; an underflow only flushes values below 1e-38), so the column
         // factors go to the warp's own 32 floats of den_x (the row-sum exchange, idle until the
@@ -321,8 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* fbuf = &bars.den_x[hc][quarter * 32];
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const int s0 = s_base + h2 * 32 + lane;
-          const float cl = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
+          const float cl = cpre[h2];
           float lo = cl;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
