@@ -812,6 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // into P^T; the column part of dc, sum_t (dN - delta) rden A_ts over pairs with c_t - c_s <= 0,
     // is sum_t dA''_dec S^2 (S^2 summed over the parts), added to dc once per query head.
     float csum = 0.f;
+    float c_s = 0.f;  // decay: c of this thread's key row for the current query head
     bool ok = true;
     int it = 0;
     for (int n = 0; n < nwork && ok; ++n) {
@@ -821,8 +822,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* v_rd = vec + (vs * kNV + 0) * kTile;
       const float* v_dr = vec + (vs * kNV + 1) * kTile;
       const float* v_c = vec + (vs * kNV + 2) * kTile;  // decay: c of the query tile
-      float c_s = 0.f;
-      if (DECAY && live) c_s = p.c[(static_cast<size_t>(b) * T_ + sg) * p.HQ + h * p.G + n / nq];
+      if (DECAY && live && n % nq == 0)  // this row's c for the query head of pairs n .. n + nq - 1
+        c_s = p.c[(static_cast<size_t>(b) * T_ + sg) * p.HQ + h * p.G + n / nq];
       if (!mbar_wait(&bars.vec_full[vs], (n >> 1) & 1, wc)) {
         ok = false;
         break;
