@@ -430,7 +430,7 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(world), "roofline": roofline, "cpu_baseline": cpu,
-        "e2e": e2e, "clocks": clk.summary(), "gpu_launches": 3 * K,
+        "e2e": e2e, "clocks": clk.summary(), "gpu_launches": (4 if DECAY else 3) * K,  # decay: + c transpose
     }
     print(json.dumps(line), flush=True)
 
