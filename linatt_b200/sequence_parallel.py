@@ -78,6 +78,7 @@ def _ldw(Dv: int) -> int:
 
 
 def _features(x, M, scale):
+    x = x.contiguous()  # the kernel reads dense (B, T, H, D) rows
     B, T, H, D = x.shape
     E = D // M
     R = torch.empty(B * H, T, M * E * E, device=x.device, dtype=torch.bfloat16)
@@ -87,6 +88,7 @@ def _features(x, M, scale):
 
 
 def _contract(G, x, dx, M, scale):
+    x = x.contiguous()  # dx is a dense fp32 (B, T, H, D) buffer made by the caller
     B, T, H, D = x.shape
     _lib.check(_lib.lib().kata_sp_contract(G.data_ptr(), x.data_ptr(), dx.data_ptr(), _lib.DTYPE[x.dtype], B, T, H,
                                            D, M, 2.0 * float(scale), 1, _lib.stream_handle(x.device)),
