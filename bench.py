@@ -85,6 +85,17 @@ def load_peaks() -> tuple[float, str]:
     return 1590.0, "fallback"
 
 
+def load_hbm_peak() -> tuple[float, str]:
+    """Measured copy bandwidth (GB/s) of this pool's B200s, else the earlier pool measurement."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
 def load_traffic(kernel: str):
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
@@ -562,14 +573,7 @@ def run_gdn(args, rank: int, world: int, local: int) -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
-    peak_hbm = 6651.7
-    p = ROOT / "MEASURED_PEAKS.json"
-    src = "fallback"
-    if p.exists():
-        try:
-            peak_hbm, src = float(json.loads(p.read_text())["hbm_gbs"]), "measured"
-        except Exception:
-            pass
+    peak_hbm, src = load_hbm_peak()
     step_ms = ms / args.steps
     n = Bg * Tg * Hg
     # algorithmic bytes: read q,k,v (bf16) + g,beta (fp32) twice (fwd, bwd), dO once; write o, dq, dk, dv
@@ -656,6 +660,61 @@ def run_delta(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_decode(args, rank: int, world: int, local: int) -> None:
+    """Generation step of the concat-score attention on the feature state (kata_attn_decode) at the
+    headline geometry: B=16 sequences, H=8, D=Dv=128, M=4, after a T=4096 prefix (whose state is
+    built before timing).  One step = one new token per sequence and head: one kata_decode_step
+    launch that reads and rewrites the 285 MB fp32 state (larger than L2) in place."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from linatt_b200.kata_decode import kata_attn_decode, kata_attn_state
+
+    Tp, K, W = 4096, args.steps, args.warmup
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    k0 = torch.randn(B, Tp, H, D, device=dev, generator=g).bfloat16()
+    v0 = torch.randn(B, Tp, H, DV, device=dev, generator=g).bfloat16()
+    S = kata_attn_state(k0, v0, num_groups=M)
+    del k0, v0
+    toks = [torch.randn(K + W, B, H, d, device=dev, generator=g).bfloat16() for d in (D, D, DV)]
+
+    def step(i):
+        kata_attn_decode(toks[0][i], toks[1][i], toks[2][i], S, num_groups=M)
+
+    ms, clk = _timed_steps(torch, dist, world, dev, step, K, W)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, src = load_hbm_peak()
+    step_ms = ms / K
+    state_bytes = S.numel() * 4
+    nbytes = 2 * state_bytes + B * H * (2 * D + 2 * DV) * 2  # state read + write, q k v o
+    ach = nbytes / (step_ms / 1e3) / 1e9
+    line = {
+        "metric": "KATA attn decode tokens/s/GPU at B16·H8·D128, M=4, after a 4096-token prefix",
+        "value": world * B / (step_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "kata_attn_decode: one token per sequence on the fp32 feature state, concat M=4",
+                   "batch_per_gpu": B, "heads": H, "head_dim": D, "num_groups": M, "prefix": Tp,
+                   "state_MB": state_bytes / 1e6, "parallelism": f"batch shard x{world}",
+                   "l2": f"the {state_bytes / 1e6:.0f} MB state is larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                     "frac": ach / peak, "traffic": None, "peak_source": src,
+                     "note": "algorithmic bytes: the state read and written once, plus q, k, v, o"},
+        "clocks": clk, "gpu_launches": K,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -669,9 +728,10 @@ def main() -> None:
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
     ap.add_argument("--decay", action="store_true",
                     help="auxiliary line: the decayed form (device-timed only; no e2e / CPU legs)")
-    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta"], default="attn",
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode"], default="attn",
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
-                         "delta: the SPD delta rule at the mixer geometry")
+                         "delta: the SPD delta rule at the mixer geometry; decode: one-token generation "
+                         "steps on the recurrent feature state")
     ap.add_argument("--batch", type=int, default=16,
                     help="B per GPU (the metric is quoted at 16; smaller values only for profiler captures)")
     args = ap.parse_args()
@@ -695,6 +755,8 @@ def main() -> None:
         run_gdn(args, rank, world, local)
     elif args.workload == "delta":
         run_delta(args, rank, world, local)
+    elif args.workload == "decode":
+        run_decode(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 

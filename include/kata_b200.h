@@ -317,6 +317,25 @@ KATA_API int kata_sp_combine(const void* o_local, const float* den_local, const 
 KATA_API int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in, void* W1, int dtype, int B, int T,
                               int H, int Dv, int ldw, kata_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Decode (generation) step of KATA-SPD attention, concat score, H == HQ, no decay.  No counterpart
+ * in the reference: its quadratic-feature branch keeps no recurrent state (kata/layer.py:421-492
+ * sets final_state = None; :532-537 caches it), so each generated token re-runs causal attention
+ * over the whole prefix.  The state of
+ * a prefix is S = sum_s psi(k_s) [v_s | 1], (B*H, F, lds) fp32, F = M (D/M)^2, columns [0,Dv) the
+ * value sums, column Dv the key-feature sum, columns above Dv zero (lds % 4 == 0, lds >= Dv + 1,
+ * lds <= 1024).  One call takes one new token per (batch, head):
+ *   S += psi(k) [v | 1]  (in place),  [X | y] = psi(q)^T S,  o = X / y' (y' = y if y > 0 else 1),
+ * i.e. o is the token's row of the full causal attention.  q, k (B,H,D) and v, o (B,H,Dv) of
+ * `dtype`; den (B,H) fp32 receives y (may be NULL).  `work` is 16-byte aligned, of
+ * kata_decode_workspace_bytes(...) bytes; its first 4*B*H bytes (per-head tickets) must be zero
+ * before the call and every call leaves them zero, so calls that share it run in stream order and
+ * a workspace reused for a larger B*H is zeroed again first.  D <= 2048. */
+KATA_API size_t kata_decode_workspace_bytes(int B, int H, int D, int Dv, int M, int lds);
+KATA_API int kata_decode_step(const void* q, const void* k, const void* v, float* state, void* o, float* den,
+                              void* work, int dtype, int B, int H, int D, int Dv, int M, int lds, float scale,
+                              kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

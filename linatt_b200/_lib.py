@@ -142,6 +142,10 @@ def lib() -> ctypes.CDLL:
             L.kata_sp_combine.argtypes = [c_void_p] * 5 + [c_int] * 6 + [c_void_p]
             L.kata_sp_bwd_prep.restype = c_int
             L.kata_sp_bwd_prep.argtypes = [c_void_p] * 4 + [c_int] * 6 + [c_void_p]
+            L.kata_decode_workspace_bytes.restype = c_size_t
+            L.kata_decode_workspace_bytes.argtypes = [c_int] * 6
+            L.kata_decode_step.restype = c_int
+            L.kata_decode_step.argtypes = [c_void_p] * 7 + [c_int] * 7 + [c_float, c_void_p]
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:
