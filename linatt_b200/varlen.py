@@ -1,0 +1,84 @@
+"""Packed-sequence (varlen) form of causal KATA-SPD attention.
+
+Documents are packed along T as (1, T_total, H, D) with ``cu_seqlens`` = [0, l_0, l_0+l_1, ...]
+(int, N+1 entries), the layout of the reference's per-document data preparation and of the
+``seq_lengths`` / ``seq_starts`` arguments sketched in its unused Hopper kernel
+(``kata/kernels/parallel_kata_hopper.py:18-44``).  Token t of document n attends to the tokens
+s <= t of document n only.
+
+Each document is scattered into its own row of a zero-padded (N, T_max, H, D) batch, the flash
+kernels run on that batch, and the rows are gathered back.  Padding sits after each document's
+last token, so causality keeps it out of every real row: the outputs and gradients equal those of
+one call per document.  The cost is the padding (sum of T_max - l_n tokens) and one scatter /
+gather pass over q, k, v, o (and their gradients); the gradients flow through the index ops.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .parallel_kata_attn import parallel_kata_attn, parallel_kata_attn_decay, parallel_kata_attn_sum
+
+__all__ = ["varlen_index", "pack_rows", "unpack_rows", "parallel_kata_attn_varlen"]
+
+
+def varlen_index(cu_seqlens: torch.Tensor, max_seqlen: int | None = None, total: int | None = None):
+    """(dst, N, T_max): dst[t] = n * T_max + (t - cu_seqlens[n]) for packed token t of document n.
+    ``total`` (= cu_seqlens[-1]) and ``max_seqlen`` spare the device-to-host reads of cu_seqlens."""
+    cu = cu_seqlens.to(torch.int64)
+    if cu.dim() != 1 or cu.numel() < 2:
+        raise ValueError("cu_seqlens must be 1-D with at least two entries")
+    lens = cu[1:] - cu[:-1]
+    N = lens.numel()
+    if max_seqlen is None:
+        cpu = cu.cpu()
+        if int(cpu[0]) != 0 or bool(((cpu[1:] - cpu[:-1]) < 0).any()):
+            raise ValueError("cu_seqlens must start at 0 and be non-decreasing")
+        max_seqlen = int((cpu[1:] - cpu[:-1]).max())
+    T = int(cu[-1]) if total is None else int(total)
+    seq = torch.repeat_interleave(torch.arange(N, device=cu.device), lens, output_size=T)
+    pos = torch.arange(seq.numel(), device=cu.device) - cu[seq]
+    return seq * max_seqlen + pos, N, max(int(max_seqlen), 1)
+
+
+def pack_rows(x: torch.Tensor, dst: torch.Tensor, N: int, T_max: int) -> torch.Tensor:
+    """(1, T_total, *rest) packed -> (N, T_max, *rest) zero-padded (differentiable)."""
+    flat = x[0]
+    out = flat.new_zeros((N * T_max,) + tuple(flat.shape[1:]))
+    return out.index_copy(0, dst, flat).view((N, T_max) + tuple(flat.shape[1:]))
+
+
+def unpack_rows(y: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    """(N, T_max, *rest) -> (1, T_total, *rest) (differentiable)."""
+    return y.reshape((-1,) + tuple(y.shape[2:])).index_select(0, dst).unsqueeze(0)
+
+
+def parallel_kata_attn_varlen(q, k, v, cu_seqlens, num_groups=4, scale=None, score="concat", c=None,
+                              max_seqlen=None):
+    """Causal KATA-SPD attention over packed documents.
+
+    q (1, T_total, HQ, D), k (1, T_total, H, D), v (1, T_total, H, Dv); ``cu_seqlens`` (N+1) int;
+    ``score`` "concat" or "sum"; ``c`` (1, T_total, HQ) fp32 cumulative log-decay (concat score,
+    per document: the decay factor only ever compares tokens of one document).  ``max_seqlen``
+    (the longest document) avoids a device-to-host read of ``cu_seqlens``.  Returns o
+    (1, T_total, HQ, Dv) in v's dtype; autograd gives dq, dk, dv (and dc).
+    """
+    if q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError(f"packed inputs are (1, T_total, H, D); got q {tuple(q.shape)}")
+    if score not in ("concat", "sum"):
+        raise ValueError(f"score must be 'concat' or 'sum', got {score!r}")
+    if c is not None and score != "concat":
+        raise ValueError("decay pairs with the concat score only")
+    if max_seqlen is None:  # validates cu_seqlens on the host, including its total
+        cpu = cu_seqlens.cpu().to(torch.int64)
+        if int(cpu[-1]) != q.shape[1]:
+            raise ValueError(f"cu_seqlens covers {int(cpu[-1])} tokens, q has {q.shape[1]}")
+    dst, N, T_max = varlen_index(cu_seqlens.to(q.device), max_seqlen, total=q.shape[1])
+    qp, kp, vp = (pack_rows(x, dst, N, T_max) for x in (q, k, v))
+    if c is not None:
+        o = parallel_kata_attn_decay(qp, kp, vp, pack_rows(c, dst, N, T_max), num_groups=num_groups, scale=scale)
+    elif score == "sum":
+        o = parallel_kata_attn_sum(qp, kp, vp, num_groups=num_groups, scale=scale)
+    else:
+        o = parallel_kata_attn(qp, kp, vp, num_groups=num_groups, scale=scale)
+    return unpack_rows(o, dst)
