@@ -318,23 +318,43 @@ KATA_API int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in
                               int H, int Dv, int ldw, kata_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
- * Decode (generation) step of KATA-SPD attention, concat score, H == HQ, no decay.  No counterpart
- * in the reference: its quadratic-feature branch keeps no recurrent state (kata/layer.py:421-492
- * sets final_state = None; :532-537 caches it), so each generated token re-runs causal attention
- * over the whole prefix.  The state of
- * a prefix is S = sum_s psi(k_s) [v_s | 1], (B*H, F, lds) fp32, F = M (D/M)^2, columns [0,Dv) the
- * value sums, column Dv the key-feature sum, columns above Dv zero (lds % 4 == 0, lds >= Dv + 1,
- * lds <= 1024).  One call takes one new token per (batch, head):
- *   S += psi(k) [v | 1]  (in place),  [X | y] = psi(q)^T S,  o = X / y' (y' = y if y > 0 else 1),
- * i.e. o is the token's row of the full causal attention.  q, k (B,H,D) and v, o (B,H,Dv) of
- * `dtype`; den (B,H) fp32 receives y (may be NULL).  `work` is 16-byte aligned, of
- * kata_decode_workspace_bytes(...) bytes; its first 4*B*H bytes (per-head tickets) must be zero
- * before the call and every call leaves them zero, so calls that share it run in stream order and
- * a workspace reused for a larger B*H is zeroed again first.  D <= 2048. */
-KATA_API size_t kata_decode_workspace_bytes(int B, int H, int D, int Dv, int M, int lds);
-KATA_API int kata_decode_step(const void* q, const void* k, const void* v, float* state, void* o, float* den,
-                              void* work, int dtype, int B, int H, int D, int Dv, int M, int lds, float scale,
-                              kata_stream_t stream);
+ * Decode (generation) step of KATA-SPD attention.  No counterpart in the reference: its
+ * quadratic-feature branch keeps no recurrent state (kata/layer.py:421-492 sets final_state = None;
+ * :532-537 caches it), so each generated token re-runs causal attention over the whole prefix.
+ * Both scores are psi(q).psi(k) for quadratic features psi (E = D/M):
+ *   concat  psi(x)[g,a,b] = scale x_{g,a} x_{g,b}        F = M E^2
+ *   sum     psi(x)[a,b]   = scale sum_g x_{g,a} x_{g,b}  F = E^2
+ * The state of a prefix is S = sum_s w_s psi(k_s) [v_s | 1], (B*HS, F, lds) fp32: columns [0,Dv)
+ * the weighted value sums, column Dv the weighted key-feature sum, columns above Dv zero
+ * (lds % 4 == 0, Dv + 1 <= lds <= 1024).  Without decay (g == NULL) w_s = 1 and there is one state
+ * per key/value head (HS = H), shared by its HQ/H in {1,2,4,8} query heads.  With decay, g (B,HQ)
+ * fp32 is the token's log-decay c_t - c_{t-1}, w_s = exp(c_t - c_s), and the state is per query
+ * head (HS = HQ); this equals the reference's exp(min(c_t - c_s, 0)) whenever c is non-increasing,
+ * as the layer's c = cumsum(-exp(A_log) softplus(dt)) is (kata/layer.py:440-447).  One call takes
+ * one new token per (batch, head):
+ *   S = exp(g) S + psi(k) [v | 1]  (in place),  [X | y] = psi(q)^T S,  o = X / y' (y' = y if y > 0
+ * else 1), i.e. o is the token's row of the full causal attention.  q (B,HQ,D), k (B,H,D),
+ * v (B,H,Dv), o (B,HQ,Dv) of `dtype`; den (B,HQ) fp32 receives y (may be NULL).  `work` is
+ * 16-byte aligned, of kata_decode_workspace_bytes(args) bytes; its first 4*B*HS bytes (tickets)
+ * must be zero before the call and every call leaves them zero, so calls that share it run in
+ * stream order, and a workspace reused for a larger B*HS is zeroed again first.  D <= 256.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;  /* (B,HQ) per-token log-decay, or NULL                 */
+  float* state;    /* (B*HS, F, lds) fp32, updated in place              */
+  void* o;
+  float* den;      /* may be NULL                                        */
+  void* work;
+  int dtype, B, HQ, H, D, Dv, M, lds;
+  int score;       /* KATA_SCORE_*                                       */
+  float scale;
+} kata_decode_args;
+
+KATA_API size_t kata_decode_workspace_bytes(const kata_decode_args* args);
+KATA_API int kata_decode_step(const kata_decode_args* args, kata_stream_t stream);
 
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);

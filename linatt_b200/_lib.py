@@ -30,6 +30,15 @@ c_float = ctypes.c_float
 c_size_t = ctypes.c_size_t
 
 
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("g", c_void_p), ("state", c_void_p),
+        ("o", c_void_p), ("den", c_void_p), ("work", c_void_p),
+        ("dtype", c_int), ("B", c_int), ("HQ", c_int), ("H", c_int), ("D", c_int), ("Dv", c_int),
+        ("M", c_int), ("lds", c_int), ("score", c_int), ("scale", c_float),
+    ]
+
+
 class AttnFwdArgs(ctypes.Structure):
     _fields_ = [
         ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("c", c_void_p),
@@ -143,9 +152,9 @@ def lib() -> ctypes.CDLL:
             L.kata_sp_bwd_prep.restype = c_int
             L.kata_sp_bwd_prep.argtypes = [c_void_p] * 4 + [c_int] * 6 + [c_void_p]
             L.kata_decode_workspace_bytes.restype = c_size_t
-            L.kata_decode_workspace_bytes.argtypes = [c_int] * 6
+            L.kata_decode_workspace_bytes.argtypes = [ctypes.POINTER(DecodeArgs)]
             L.kata_decode_step.restype = c_int
-            L.kata_decode_step.argtypes = [c_void_p] * 7 + [c_int] * 7 + [c_float, c_void_p]
+            L.kata_decode_step.argtypes = [ctypes.POINTER(DecodeArgs), c_void_p]
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:
