@@ -79,6 +79,8 @@ def _fwd(q, k, v, num_groups, scale, score, c=None):
     qc, kc, vc = (x.to(dt).contiguous() for x in (q, k, v))
     o = torch.empty(B, T, HQ, d_v, device=dev, dtype=dt)
     den = torch.empty(B, T, HQ, device=dev, dtype=torch.float32)
+    if B == 0 or T == 0:  # empty batch or sequence: nothing to launch (the reference's grid is empty)
+        return o.to(v.dtype), den
     cc = None
     if c is not None:
         if c.shape != (B, T, HQ):
@@ -113,6 +115,8 @@ def _bwd(q, k, v, o, den, do, num_groups, scale, score, c=None):
     dv = torch.empty(B, T, H, d_v, device=dev, dtype=dt)
     cc = c.float().contiguous() if c is not None else None
     dc = torch.empty(B, T, HQ, device=dev, dtype=torch.float32) if c is not None else None
+    if B == 0 or T == 0:  # empty batch or sequence: nothing to launch
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dc
     st = _lib.status_word(dev)
     a = _lib.AttnBwdArgs(
         q=qc.data_ptr(), k=kc.data_ptr(), v=vc.data_ptr(), o=oc.data_ptr(), den=denc.data_ptr(),

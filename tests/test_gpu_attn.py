@@ -197,6 +197,31 @@ def test_tensor_core_forward_writes_every_output():
     assert torch.isfinite(o.float()).all() and torch.isfinite(den).all()
 
 
+@pytest.mark.parametrize("B,T", [(0, 64), (2, 0)])
+@pytest.mark.parametrize("variant", ["concat", "sum", "decay"])
+def test_empty_inputs_give_empty_outputs(B, T, variant):
+    """An empty batch or sequence returns empty o and empty gradients, as the reference's empty
+    launch grid does; nothing is launched."""
+    pka = _pka("auto")
+    q = torch.randn(B, T, 2, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, T, 2, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, T, 2, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    if variant == "decay":
+        c = torch.zeros(B, T, 2, device="cuda", requires_grad=True)
+        o = pka.parallel_kata_attn_decay(q, k, v, c, num_groups=2)
+    elif variant == "sum":
+        o = pka.parallel_kata_attn_sum(q, k, v, num_groups=4)
+    else:
+        o = pka.parallel_kata_attn(q, k, v, num_groups=4)
+    assert o.shape == (B, T, 2, 128) and o.dtype == torch.bfloat16
+    o.sum().backward()
+    assert q.grad.shape == q.shape and k.grad.shape == k.shape and v.grad.shape == v.shape
+    if variant == "decay":
+        assert c.grad.shape == c.shape
+    o2, den = pka.parallel_kata_attn_fwd(q.detach(), k.detach(), v.detach(), num_groups=4)
+    assert o2.shape == (B, T, 2, 128) and den.shape == (B, T, 2)
+
+
 # --------------------------------------------------------------------------------------------
 # config 3 at full size (B=16, T=4096, H=8, D=Dv=128, M=4, bf16): size-independent properties
 # --------------------------------------------------------------------------------------------
