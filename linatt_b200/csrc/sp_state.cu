@@ -18,36 +18,47 @@ namespace kata {
 namespace {
 
 constexpr int NT = 256;
-constexpr int TOK = 8;  // tokens per CTA of the feature kernel
+constexpr int TOK = 16;  // tokens per CTA of the feature kernel
 
-// R (B,H,T,F) bf16, R[.., g E^2 + a E + b] = scale * (x_a * x_b)  (product first: exactly symmetric)
+// R (B,H,T,F) bf16, R[.., g E^2 + a E + b] = scale * (x_a * x_b)  (product first: exactly symmetric).
+// HBM-bound on the writes (F bf16 per token and head).  A thread owns fixed 8-feature chunks, so the
+// chunk's (g, a, b0) offsets are computed once, and streams over the CTA's tokens: two 16-byte
+// shared loads and one 16-byte coalesced store per chunk and token.  With fewer chunks than
+// threads, the threads split the tokens instead.
 template <typename T>
 __global__ void __launch_bounds__(NT) sp_features_kernel(const T* __restrict__ x, __nv_bfloat16* __restrict__ R,
                                                          int B, int Tn, int H, int D, int M, float scale) {
   extern __shared__ float xs[];  // TOK x D
-  const int E = D / M, F = M * E * E, bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int t0 = blockIdx.x * TOK;
-  for (int i = threadIdx.x; i < TOK * D; i += NT) {
+  const int E = D / M, EE = E * E, F = M * EE, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int t0 = blockIdx.x * TOK, tid = threadIdx.x;
+  for (int i = tid; i < TOK * D; i += NT) {
     const int j = i / D, d = i % D, t = t0 + j;
     xs[i] = t < Tn ? to_f32<T>(x[((static_cast<size_t>(b) * Tn + t) * H + h) * D + d]) : 0.f;
   }
   __syncthreads();
   const int chunks = F / 8;
-  for (int c = threadIdx.x; c < TOK * chunks; c += NT) {
-    const int j = c / chunks, f0 = (c % chunks) * 8, t = t0 + j;
-    if (t >= Tn) continue;
-    const int g = f0 / (E * E), a = (f0 % (E * E)) / E, b0 = f0 % E;
-    const float* xr = xs + j * D + g * E;
-    const float xa = xr[a];
-    uint32_t w[4];
+  const bool wide = chunks >= NT;
+  const int js = wide ? 1 : NT / chunks;  // token stride
+  if (!wide && tid >= js * chunks) return;
+  const int j0 = wide ? 0 : tid / chunks;
+  for (int ci = wide ? tid : tid % chunks; ci < chunks; ci += NT) {
+    const int f0 = ci * 8, g = f0 / EE, a = (f0 - g * EE) / E, b0 = f0 % E;
+    const int oa = g * E + a, ob = g * E + b0;  // ob is a multiple of 8: 32-byte aligned rows of xs
+    __nv_bfloat16* out = R + (static_cast<size_t>(bh) * Tn + t0) * F + f0;
+    for (int j = j0; j < TOK && t0 + j < Tn; j += js) {
+      const float* xr = xs + j * D;
+      const float xa = xr[oa];
+      const float4 lo = *reinterpret_cast<const float4*>(xr + ob);
+      const float4 hi = *reinterpret_cast<const float4*>(xr + ob + 4);
+      const float xb[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float p0 = scale * (xa * xr[b0 + 2 * i]);
-      const float p1 = scale * (xa * xr[b0 + 2 * i + 1]);
-      const __nv_bfloat162 v = __floats2bfloat162_rn(p0, p1);
-      w[i] = *reinterpret_cast<const uint32_t*>(&v);
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(scale * (xa * xb[2 * i]), scale * (xa * xb[2 * i + 1]));
+        w[i] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+      *reinterpret_cast<uint4*>(out + static_cast<size_t>(j) * F) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    *reinterpret_cast<uint4*>(R + (static_cast<size_t>(bh) * Tn + t) * F + f0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -144,6 +155,7 @@ extern "C" int kata_sp_features(const void* x, void* R, int dtype, int B, int T,
   if (e) return e;
   if (!x || !R) return KATA_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(R) % 16) return KATA_ERR_ALIGN;
+  if (sizeof(float) * TOK * D > 48 * 1024) return KATA_ERR_UNSUPPORTED;  // the CTA's rows of x in shared memory
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const dim3 grid((T + TOK - 1) / TOK, B * H);
   const size_t smem = sizeof(float) * TOK * D;

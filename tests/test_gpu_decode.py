@@ -192,3 +192,17 @@ def test_decode_kernel_rejects_bad_state():
         kata_attn_decode(q[:, 0], k[:, 0], v[:, 0], bad, num_groups=4)
     with pytest.raises(ValueError):  # decay with the sum score
         kata_attn_decode(q[:, 0], k[:, 0], v[:, 0], bad, num_groups=4, score="sum", g=torch.zeros(1, 2, device="cuda"))
+
+
+@pytest.mark.parametrize("B,T,H,D,M,dtype", [(2, 37, 3, 128, 4, torch.bfloat16), (1, 70, 2, 64, 4, torch.float32),
+                                             (2, 16, 1, 64, 1, torch.float16), (1, 5, 2, 128, 2, torch.bfloat16)])
+def test_feature_kernel_is_exact(B, T, H, D, M, dtype):
+    """psi(x) from the feature kernel equals the torch fp32 statement rounded to bf16, bit for bit."""
+    from linatt_b200.kata_decode import state_features
+
+    g = torch.Generator().manual_seed(T * D + M)
+    x = torch.randn(B, T, H, D, generator=g).to(dtype).cuda()
+    scale = 1.0 / (D // M) ** 0.5
+    R = state_features(x, M, scale, "concat")
+    ref = _psi(x.permute(0, 2, 1, 3).reshape(B * H * T, D), M, scale, "concat").to(torch.bfloat16)
+    assert torch.equal(R.reshape(B * H * T, -1), ref)
