@@ -91,6 +91,50 @@ __global__ void __launch_bounds__(NT) sp_contract_kernel(const __nv_bfloat16* __
   }
 }
 
+// The same contraction with 16-byte loads, for E/8 dividing 32 (E = 16, 32, ..., 256).  One warp
+// per (token, head); LPR = E/8 lanes cover one row b of G_g (8 consecutive a each), so a warp load
+// reads 32/LPR whole rows = 512 contiguous bytes.  Each lane accumulates its 8 a's over the rows
+// b = lane/LPR + i*(32/LPR); the lanes sharing the same a's then combine by shuffles.
+template <typename T, int LPR>
+__global__ void __launch_bounds__(NT) sp_contract_vec_kernel(const __nv_bfloat16* __restrict__ G,
+                                                             const T* __restrict__ x, float* __restrict__ dx, int B,
+                                                             int Tn, int H, int D, int M, float factor,
+                                                             int accumulate) {
+  constexpr int E = LPR * 8, RPP = 32 / LPR;  // rows per pass
+  const int warp = (blockIdx.x * NT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long total = static_cast<long>(B) * H * Tn;
+  if (warp >= total) return;
+  const int bh = warp / Tn, t = warp % Tn, b = bh / H, h = bh % H;
+  const size_t xo = ((static_cast<size_t>(b) * Tn + t) * H + h) * D;
+  const __nv_bfloat16* g = G + (static_cast<size_t>(bh) * Tn + t) * static_cast<size_t>(M) * E * E;
+  const int a0 = (lane % LPR) * 8, r0 = lane / LPR;
+  for (int gi = 0; gi < M; ++gi) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const __nv_bfloat16* gg = g + static_cast<size_t>(gi) * E * E;
+#pragma unroll 4
+    for (int bb = r0; bb < E; bb += RPP) {
+      const uint4 w = *reinterpret_cast<const uint4*>(gg + bb * E + a0);
+      const float xb = to_f32<T>(x[xo + gi * E + bb]);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+        acc[2 * i] = fmaf(f.x, xb, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(f.y, xb, acc[2 * i + 1]);
+      }
+    }
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
+    if (r0 == 0) {
+      float* o = dx + xo + gi * E + a0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = accumulate ? o[i] + factor * acc[i] : factor * acc[i];
+    }
+  }
+}
+
 // o = (o_loc * den_loc' + X) / D',  D = den_loc + y   (x' = x if x > 0 else 1);  XY (B*H, T, ldxy)
 template <typename T>
 __global__ void __launch_bounds__(NT) sp_combine_kernel(const T* __restrict__ oloc, const float* __restrict__ den,
@@ -135,6 +179,18 @@ __global__ void __launch_bounds__(NT) sp_bwd_prep_kernel(const T* __restrict__ o
   for (int c = Dv + lane; c < ldw; c += 32) w[c] = __float2bfloat16_rn(c == Dv ? -delta * inv : 0.f);
 }
 
+template <typename T>
+void launch_contract_vec(int E, unsigned blocks, cudaStream_t st, const __nv_bfloat16* g, const T* x, float* dx, int B,
+                         int Tn, int H, int D, int M, float factor, int accumulate) {
+  switch (E) {
+    case 16: sp_contract_vec_kernel<T, 2><<<blocks, NT, 0, st>>>(g, x, dx, B, Tn, H, D, M, factor, accumulate); break;
+    case 32: sp_contract_vec_kernel<T, 4><<<blocks, NT, 0, st>>>(g, x, dx, B, Tn, H, D, M, factor, accumulate); break;
+    case 64: sp_contract_vec_kernel<T, 8><<<blocks, NT, 0, st>>>(g, x, dx, B, Tn, H, D, M, factor, accumulate); break;
+    case 128: sp_contract_vec_kernel<T, 16><<<blocks, NT, 0, st>>>(g, x, dx, B, Tn, H, D, M, factor, accumulate); break;
+    default: sp_contract_vec_kernel<T, 32><<<blocks, NT, 0, st>>>(g, x, dx, B, Tn, H, D, M, factor, accumulate); break;
+  }
+}
+
 int check(int dtype, int B, int T, int H, int D, int M) {
   if (dtype != KATA_DTYPE_F32 && dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
   if (B < 1 || T < 1 || H < 1 || D < 1 || M < 1 || D % M) return KATA_ERR_SHAPE;
@@ -176,6 +232,16 @@ extern "C" int kata_sp_contract(const void* G, const void* x, float* dx, int dty
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const unsigned blocks = warp_blocks(static_cast<long>(B) * H * T);
   const auto* g = static_cast<const __nv_bfloat16*>(G);
+  const int E = D / M;
+  if (E == 16 || E == 32 || E == 64 || E == 128 || E == 256) {
+    if (reinterpret_cast<uintptr_t>(G) % 16) return KATA_ERR_ALIGN;
+    switch (dtype) {
+      case KATA_DTYPE_F32: launch_contract_vec<float>(E, blocks, st, g, static_cast<const float*>(x), dx, B, T, H, D, M, factor, accumulate); break;
+      case KATA_DTYPE_BF16: launch_contract_vec<__nv_bfloat16>(E, blocks, st, g, static_cast<const __nv_bfloat16*>(x), dx, B, T, H, D, M, factor, accumulate); break;
+      default: launch_contract_vec<__half>(E, blocks, st, g, static_cast<const __half*>(x), dx, B, T, H, D, M, factor, accumulate); break;
+    }
+    return from_cuda(cudaGetLastError());
+  }
   switch (dtype) {
     case KATA_DTYPE_F32: sp_contract_kernel<float><<<blocks, NT, 0, st>>>(g, static_cast<const float*>(x), dx, B, T, H, D, M, factor, accumulate); break;
     case KATA_DTYPE_BF16: sp_contract_kernel<__nv_bfloat16><<<blocks, NT, 0, st>>>(g, static_cast<const __nv_bfloat16*>(x), dx, B, T, H, D, M, factor, accumulate); break;

@@ -99,3 +99,30 @@ def test_sp_nccl_two_ranks():
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "SP_OK" in r.stdout
+
+
+@pytest.mark.parametrize("D,M,dtype,accumulate", [(128, 4, torch.bfloat16, 0), (64, 4, torch.float32, 1),
+                                                  (128, 2, torch.float16, 1), (96, 4, torch.bfloat16, 0),
+                                                  (256, 8, torch.bfloat16, 1)])
+def test_feature_gradient_contraction_vs_torch(D, M, dtype, accumulate):
+    """kata_sp_contract: dx_{g,a} (+)= factor * sum_b G[g,b,a] x_{g,b} against torch fp32 (rel-L2
+    <= 1e-5), on the 16-byte path (E = 16, 32, 64) and the general one (E = 24)."""
+    from linatt_b200 import _lib
+
+    B, T, H = 2, 37, 3
+    E = D // M
+    g = torch.Generator().manual_seed(D * M + accumulate)
+    x = torch.randn(B, T, H, D, generator=g).to(dtype).cuda()
+    G = torch.randn(B * H, T, M * E * E, generator=g).bfloat16().cuda()
+    dx0 = torch.randn(B, T, H, D, generator=g).cuda()
+    dx = dx0.clone()
+    factor = 0.37
+    _lib.check(_lib.lib().kata_sp_contract(G.data_ptr(), x.data_ptr(), dx.data_ptr(), _lib.DTYPE[dtype], B, T, H, D,
+                                           M, factor, accumulate, torch.cuda.current_stream().cuda_stream),
+               "kata_sp_contract")
+    Gr = G.float().view(B, H, T, M, E, E)  # [.., g, b, a]
+    xr = x.float().permute(0, 2, 1, 3).reshape(B, H, T, M, E)
+    ref = factor * torch.einsum("bhtgca,bhtgc->bhtga", Gr, xr).reshape(B, H, T, D).permute(0, 2, 1, 3)
+    if accumulate:
+        ref = ref + dx0
+    assert ko.rel_l2(dx.cpu().numpy(), ref.cpu().numpy()) < 1e-5
