@@ -42,17 +42,17 @@ __all__ = ["kata_attn_state", "kata_attn_step", "kata_attn_decode", "state_featu
 # Decode workspaces (per-state tickets + chunk partials), one per (device, stream).  A call leaves
 # the tickets of its geometry zero, so a workspace is zeroed again only when the geometry changes
 # (its ticket slots may then hold partials of the earlier geometry).
-_work: dict[tuple[int, int], tuple[torch.Tensor, tuple]] = {}
+_workspaces: dict[tuple[int, int], tuple[torch.Tensor, tuple]] = {}
 
 
 def _workspace(dev, nbytes, geometry):
     key = (dev.index, _lib.stream_handle(dev))
-    w, geo = _work.get(key, (None, None))
+    w, geo = _workspaces.get(key, (None, None))
     if w is None or w.numel() < nbytes:
         w = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=dev)
     elif geo != geometry:
         w.zero_()
-    _work[key] = (w, geometry)
+    _workspaces[key] = (w, geometry)
     return w
 
 
