@@ -304,6 +304,11 @@ KATA_API int kata_gdn_bwd(const kata_gdn_bwd_args* args, kata_stream_t stream);
 /* R = psi(x) for x (B,T,H,D) of `dtype`; (D/M) % 8 == 0; R 16-byte aligned. */
 KATA_API int kata_sp_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
                               kata_stream_t stream);
+/* R = psi_sum(x), the sum score's features psi[a,b] = scale * sum_g x_{g,a} x_{g,b} (F = E^2), for x
+ * (B,T,H,D) of `dtype`, R (B,H,T,F) bf16; (D/M) % 8 == 0; R 16-byte aligned.  Used for the state of
+ * the sum score's decode path (the reference's parallel_kata_attn_sum score, kata/parallel_kata_attn.py:737). */
+KATA_API int kata_sum_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
+                               kata_stream_t stream);
 /* dx (B,T,H,D) fp32 (+)= factor * sum_b G[g,b,a] x_{g,b}: the gradient of psi for a feature
  * gradient G (B,H,T,F) bf16 that is symmetric in (a,b) (factor = 2 * scale). */
 KATA_API int kata_sp_contract(const void* G, const void* x, float* dx, int dtype, int B, int T, int H, int D, int M,

@@ -145,6 +145,8 @@ def lib() -> ctypes.CDLL:
                 w.argtypes = [ctypes.POINTER(st)]
             L.kata_sp_features.restype = c_int
             L.kata_sp_features.argtypes = [c_void_p, c_void_p] + [c_int] * 6 + [c_float, c_void_p]
+            L.kata_sum_features.restype = c_int
+            L.kata_sum_features.argtypes = [c_void_p, c_void_p] + [c_int] * 6 + [c_float, c_void_p]
             L.kata_sp_contract.restype = c_int
             L.kata_sp_contract.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 6 + [c_float, c_int, c_void_p]
             L.kata_sp_combine.restype = c_int

@@ -24,12 +24,13 @@ constexpr int TOK = 16;  // tokens per CTA of the feature kernel
 // HBM-bound on the writes (F bf16 per token and head).  A thread owns fixed 8-feature chunks, so the
 // chunk's (g, a, b0) offsets are computed once, and streams over the CTA's tokens: two 16-byte
 // shared loads and one 16-byte coalesced store per chunk and token.  With fewer chunks than
-// threads, the threads split the tokens instead.
-template <typename T>
+// threads, the threads split the tokens instead.  SUM: the sum score's features
+// psi[a,b] = scale * sum_g x_{g,a} x_{g,b} (F = E^2), summed in group order with fused multiply-adds.
+template <typename T, bool SUM>
 __global__ void __launch_bounds__(NT) sp_features_kernel(const T* __restrict__ x, __nv_bfloat16* __restrict__ R,
                                                          int B, int Tn, int H, int D, int M, float scale) {
   extern __shared__ float xs[];  // TOK x D
-  const int E = D / M, EE = E * E, F = M * EE, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int E = D / M, EE = E * E, F = SUM ? EE : M * EE, bh = blockIdx.y, b = bh / H, h = bh % H;
   const int t0 = blockIdx.x * TOK, tid = threadIdx.x;
   for (int i = tid; i < TOK * D; i += NT) {
     const int j = i / D, d = i % D, t = t0 + j;
@@ -42,11 +43,30 @@ __global__ void __launch_bounds__(NT) sp_features_kernel(const T* __restrict__ x
   if (!wide && tid >= js * chunks) return;
   const int j0 = wide ? 0 : tid / chunks;
   for (int ci = wide ? tid : tid % chunks; ci < chunks; ci += NT) {
-    const int f0 = ci * 8, g = f0 / EE, a = (f0 - g * EE) / E, b0 = f0 % E;
+    const int f0 = ci * 8, g = SUM ? 0 : f0 / EE, a = (f0 - g * EE) / E, b0 = f0 % E;
     const int oa = g * E + a, ob = g * E + b0;  // ob is a multiple of 8: 32-byte aligned rows of xs
     __nv_bfloat16* out = R + (static_cast<size_t>(bh) * Tn + t0) * F + f0;
     for (int j = j0; j < TOK && t0 + j < Tn; j += js) {
       const float* xr = xs + j * D;
+      if constexpr (SUM) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int gg = 0; gg < M; ++gg) {
+          const float xa = xr[gg * E + a];
+          const float4 lo = *reinterpret_cast<const float4*>(xr + gg * E + b0);
+          const float4 hi = *reinterpret_cast<const float4*>(xr + gg * E + b0 + 4);
+          const float xb[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = fmaf(xa, xb[i], acc[i]);
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __nv_bfloat162 v = __floats2bfloat162_rn(scale * acc[2 * i], scale * acc[2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(j) * F) = make_uint4(w[0], w[1], w[2], w[3]);
+        continue;
+      }
       const float xa = xr[oa];
       const float4 lo = *reinterpret_cast<const float4*>(xr + ob);
       const float4 hi = *reinterpret_cast<const float4*>(xr + ob + 4);
@@ -205,8 +225,11 @@ unsigned warp_blocks(long warps) { return static_cast<unsigned>((warps * 32 + NT
 
 using namespace kata;
 
-extern "C" int kata_sp_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
-                                kata_stream_t stream) {
+namespace kata {
+namespace {
+template <bool SUM>
+int launch_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
+                    kata_stream_t stream) {
   int e = check(dtype, B, T, H, D, M);
   if (e) return e;
   if (!x || !R) return KATA_ERR_INVALID;
@@ -217,11 +240,23 @@ extern "C" int kata_sp_features(const void* x, void* R, int dtype, int B, int T,
   const size_t smem = sizeof(float) * TOK * D;
   auto* r = static_cast<__nv_bfloat16*>(R);
   switch (dtype) {
-    case KATA_DTYPE_F32: sp_features_kernel<float><<<grid, NT, smem, st>>>(static_cast<const float*>(x), r, B, T, H, D, M, scale); break;
-    case KATA_DTYPE_BF16: sp_features_kernel<__nv_bfloat16><<<grid, NT, smem, st>>>(static_cast<const __nv_bfloat16*>(x), r, B, T, H, D, M, scale); break;
-    default: sp_features_kernel<__half><<<grid, NT, smem, st>>>(static_cast<const __half*>(x), r, B, T, H, D, M, scale); break;
+    case KATA_DTYPE_F32: sp_features_kernel<float, SUM><<<grid, NT, smem, st>>>(static_cast<const float*>(x), r, B, T, H, D, M, scale); break;
+    case KATA_DTYPE_BF16: sp_features_kernel<__nv_bfloat16, SUM><<<grid, NT, smem, st>>>(static_cast<const __nv_bfloat16*>(x), r, B, T, H, D, M, scale); break;
+    default: sp_features_kernel<__half, SUM><<<grid, NT, smem, st>>>(static_cast<const __half*>(x), r, B, T, H, D, M, scale); break;
   }
   return from_cuda(cudaGetLastError());
+}
+}  // namespace
+}  // namespace kata
+
+extern "C" int kata_sp_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
+                                kata_stream_t stream) {
+  return launch_features<false>(x, R, dtype, B, T, H, D, M, scale, stream);
+}
+
+extern "C" int kata_sum_features(const void* x, void* R, int dtype, int B, int T, int H, int D, int M, float scale,
+                                 kata_stream_t stream) {
+  return launch_features<true>(x, R, dtype, B, T, H, D, M, scale, stream);
 }
 
 extern "C" int kata_sp_contract(const void* G, const void* x, float* dx, int dtype, int B, int T, int H, int D, int M,

@@ -64,11 +64,20 @@ def _check_score(score, c):
 
 
 def state_features(x, num_groups, scale, score="concat"):
-    """psi(x) of x (B,T,H,D): (B*H, T, F) bf16 (head-major)."""
+    """psi(x) of x (B,T,H,D): (B*H, T, F) bf16 (head-major), by the feature kernels
+    (``kata_sp_features`` / ``kata_sum_features``) when E = D/M is a multiple of 8."""
     if score == "concat":
         return _features(x, num_groups, scale)
     B, T, H, D = x.shape
     E = D // num_groups
+    if E % 8 == 0:
+        dev = _lib.require_cuda(x)
+        xc = x.contiguous()
+        R = torch.empty(B * H, T, E * E, device=dev, dtype=torch.bfloat16)
+        _lib.check(_lib.lib().kata_sum_features(xc.data_ptr(), R.data_ptr(), _lib.DTYPE[xc.dtype], B, T, H, D,
+                                                num_groups, float(scale), _lib.stream_handle(dev)),
+                   "kata_sum_features")
+        return R
     xg = x.float().view(B, T, H, num_groups, E)
     R = torch.einsum("bthga,bthgc->bhtac", xg, xg).mul_(scale)
     return R.reshape(B * H, T, E * E).to(torch.bfloat16)

@@ -206,3 +206,19 @@ def test_feature_kernel_is_exact(B, T, H, D, M, dtype):
     R = state_features(x, M, scale, "concat")
     ref = _psi(x.permute(0, 2, 1, 3).reshape(B * H * T, D), M, scale, "concat").to(torch.bfloat16)
     assert torch.equal(R.reshape(B * H * T, -1), ref)
+
+
+@pytest.mark.parametrize("B,T,H,D,M,dtype", [(2, 37, 3, 128, 4, torch.bfloat16), (1, 70, 2, 64, 2, torch.float32),
+                                             (2, 20, 1, 64, 4, torch.float16), (1, 5, 2, 256, 8, torch.bfloat16)])
+def test_sum_feature_kernel_vs_torch(B, T, H, D, M, dtype):
+    """The sum score's features scale * sum_g x_{g,a} x_{g,b} from the kernel against the torch fp32
+    statement rounded to bf16 (only the fp32 summation order may differ: rel-L2 <= 1e-3)."""
+    from linatt_b200.kata_decode import state_features
+
+    g = torch.Generator().manual_seed(T * D + M + 1)
+    x = torch.randn(B, T, H, D, generator=g).to(dtype).cuda()
+    scale = 1.0 / (D // M) ** 0.5
+    R = state_features(x, M, scale, "sum")
+    ref = _psi(x.permute(0, 2, 1, 3).reshape(B * H * T, D), M, scale, "sum")
+    assert R.shape == (B * H, T, (D // M) ** 2) and R.dtype == torch.bfloat16
+    assert _rel(R.reshape(B * H * T, -1), ref.bfloat16()) < 1e-3
