@@ -91,6 +91,13 @@ typedef struct {
 
 KATA_API int kata_attn_fwd(const kata_attn_fwd_args* args, kata_stream_t stream);
 
+/* Kernel family that kata_attn_fwd / kata_attn_bwd would run for these arguments (only the shape,
+ * dtype, score, decay and algo fields are read; no pointer is touched): KATA_ALGO_TC (tcgen05) or
+ * KATA_ALGO_SIMT (fp32 CUDA cores), or a negative KATA_ERR_* code.  Lets a binding tell a caller
+ * when a bf16/f16 problem falls outside the tensor-core envelope and runs on the much slower SIMT
+ * kernels.  No counterpart in the reference (its Triton kernels have a single path). */
+KATA_API int kata_attn_algo(const kata_attn_fwd_args* args);
+
 /* ---------------------------------------------------------------------------------------------
  * Causal normalised KATA-SPD attention, backward.
  *   delta_t = <o_t, dO_t>;  dA[t,s] = (dO_t.v_s - delta_t) / den_t  (causal);
@@ -141,9 +148,12 @@ KATA_API int kata_attn_bwd(const kata_attn_bwd_args* args, kata_stream_t stream)
  * 16 MiB file-scope device array of the library instead (held on every GPU that loads the
  * library until the process exits).  Problems whose kata_attn_bwd_workspace_bytes() exceeds
  * 16 MiB are rejected with KATA_ERR_SCRATCH_LIMIT.  The first call on a device resolves the
- * array's address for that device, so make it outside any stream capture.  All calls on a device
- * share the array: calls whose kernels overlap on the GPU race on it.  The caller still passes
- * every input and output buffer; this path calls no allocating routine. */
+ * array's address for that device, so make it outside any stream capture; the address is kept for
+ * the life of the process, so the device must not be reset (cudaDeviceReset) between calls.  All
+ * calls on a device share the array: calls whose kernels overlap on the GPU race on it.  Only the
+ * full backward is accepted (phases must be 0; 1 and 2 return KATA_ERR_INVALID), because a
+ * dk/dv-only pass would read whatever the previous call on the device left in the shared array.
+ * The caller still passes every input and output buffer; this path calls no allocating routine. */
 KATA_API int kata_attn_bwd_noalloc(const kata_attn_bwd_args* args, kata_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------

@@ -122,6 +122,8 @@ def lib() -> ctypes.CDLL:
             L.kata_abi_version.restype = c_int
             L.kata_attn_fwd.restype = c_int
             L.kata_attn_fwd.argtypes = [ctypes.POINTER(AttnFwdArgs), c_void_p]
+            L.kata_attn_algo.restype = c_int
+            L.kata_attn_algo.argtypes = [ctypes.POINTER(AttnFwdArgs)]
             L.kata_attn_bwd.restype = c_int
             L.kata_attn_bwd.argtypes = [ctypes.POINTER(AttnBwdArgs), c_void_p]
             L.kata_attn_bwd_noalloc.restype = c_int

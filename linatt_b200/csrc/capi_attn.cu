@@ -57,6 +57,18 @@ extern "C" int kata_attn_fwd(const kata_attn_fwd_args* a, kata_stream_t stream) 
   return alg == 1 ? tc_attn_fwd(p, a->dtype, sum, st) : simt_attn_fwd(p, a->dtype, sum, st);
 }
 
+extern "C" int kata_attn_algo(const kata_attn_fwd_args* a) {
+  if (!a) return KATA_ERR_INVALID;
+  int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
+  if (e) return e;
+  const bool sum = a->score == KATA_SCORE_SUM;
+  const bool tc_ok = tc_fwd_supported(a->dtype, a->D, a->Dv, a->M, sum) &&
+                     tc_bwd_supported(a->dtype, a->D, a->Dv, a->M, sum) && !(a->c && sum);
+  const int alg = choose_algo(a->algo, tc_ok, simt_supported(a->D, a->Dv, a->M, sum), a->dtype);
+  if (alg < 0) return alg;
+  return alg == 1 ? KATA_ALGO_TC : KATA_ALGO_SIMT;
+}
+
 extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->HQ < 1) return 0;
   // fp32 delta = <o, dO> per (b, t, hq), plus 1/den and delta/den in a padded head-major layout

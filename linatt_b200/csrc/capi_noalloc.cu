@@ -19,6 +19,13 @@
 //    different streams without ordering) race on it.  Nothing in it has to start at zero: the
 //    dq pass writes every entry the dk/dv pass later reads, and the array keeps whatever the
 //    last call left there;
+//  * only the full backward (phases == 0) is accepted.  A dk/dv-only call (phases == 2) would
+//    read what the last call on the device left in the shared array, possibly another
+//    problem's, so it is rejected with KATA_ERR_INVALID, as is the dq-only pass (phases == 1)
+//    that would exist only to feed it;
+//  * the address is resolved once per device ordinal and kept for the life of the process: a
+//    caller that resets the device (cudaDeviceReset) or switches that ordinal to another
+//    context must not call this entry point afterwards;
 //  * no cudaMalloc, cudaFree or any other allocating routine is called on this path.
 #include <mutex>
 
@@ -58,6 +65,7 @@ int scratch_address(void** out) {
 
 extern "C" int kata_attn_bwd_noalloc(const kata_attn_bwd_args* args, kata_stream_t stream) {
   if (!args) return KATA_ERR_INVALID;
+  if (args->phases != 0) return KATA_ERR_INVALID;
   const size_t need = kata_attn_bwd_workspace_bytes(args);
   if (need > kata::kNoAllocScratchBytes) return KATA_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;

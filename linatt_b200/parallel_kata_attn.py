@@ -20,6 +20,7 @@ code; fp32 inputs take the fp32-exact CUDA-core kernels.
 from __future__ import annotations
 
 import math
+import warnings
 
 import torch
 
@@ -62,6 +63,26 @@ def _common_dtype(*ts: torch.Tensor) -> torch.dtype:
     return dt
 
 
+_SIMT_WARNED: set = set()
+
+
+def _warn_if_simt(a, dt) -> None:
+    """Warn once per shape class when a 16-bit call leaves the tensor-core envelope: AUTO then runs
+    the fp32 CUDA-core kernels, an order of magnitude slower than the tcgen05 path."""
+    if dt == torch.float32 or ALGO != "auto":
+        return
+    if _lib.lib().kata_attn_algo(a) != _lib.ALGO["simt"]:
+        return
+    key = (a.D, a.Dv, a.M, a.score, bool(a.c))
+    if key in _SIMT_WARNED:
+        return
+    _SIMT_WARNED.add(key)
+    warnings.warn(
+        f"KATA attention with D={a.D}, Dv={a.Dv}, M={a.M}, score={'sum' if a.score else 'concat'}"
+        f"{', decay' if a.c else ''} is outside the tensor-core envelope and runs on the fp32 CUDA-core "
+        "kernels (much slower)", RuntimeWarning, stacklevel=4)
+
+
 def _fwd(q, k, v, num_groups, scale, score, c=None):
     dev = _lib.require_cuda(q, k, v, c)
     B, T, HQ, d_k = q.shape
@@ -91,6 +112,7 @@ def _fwd(q, k, v, num_groups, scale, score, c=None):
         q=qc.data_ptr(), k=kc.data_ptr(), v=vc.data_ptr(), c=_lib.ptr(cc), o=o.data_ptr(), den=den.data_ptr(),
         status=st.data_ptr(), dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HQ=HQ, D=d_k, Dv=d_v, M=num_groups,
         score=_lib.SCORE[score], algo=_lib.ALGO[ALGO], scale=float(scale))
+    _warn_if_simt(a, dt)
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().kata_attn_fwd(a, _lib.stream_handle(dev)), "kata_attn_fwd")
     if _lib.SYNC_CHECK:

@@ -60,7 +60,10 @@ def parallel_kata_attn_varlen(q, k, v, cu_seqlens, num_groups=4, scale=None, sco
     q (1, T_total, HQ, D), k (1, T_total, H, D), v (1, T_total, H, Dv); ``cu_seqlens`` (N+1) int;
     ``score`` "concat" or "sum"; ``c`` (1, T_total, HQ) fp32 cumulative log-decay (concat score,
     per document: the decay factor only ever compares tokens of one document).  ``max_seqlen``
-    (the longest document) avoids a device-to-host read of ``cu_seqlens``.  Returns o
+    (the longest document) avoids a device-to-host read of ``cu_seqlens``; with a device-resident
+    ``cu_seqlens`` and ``max_seqlen`` given, the caller guarantees that cu_seqlens starts at 0, is
+    non-decreasing, ends at T_total and has no document longer than max_seqlen (a CPU cu_seqlens
+    is always checked).  Returns o
     (1, T_total, HQ, Dv) in v's dtype; autograd gives dq, dk, dv (and dc).
     """
     if q.dim() != 4 or q.shape[0] != 1:
@@ -69,10 +72,20 @@ def parallel_kata_attn_varlen(q, k, v, cu_seqlens, num_groups=4, scale=None, sco
         raise ValueError(f"score must be 'concat' or 'sum', got {score!r}")
     if c is not None and score != "concat":
         raise ValueError("decay pairs with the concat score only")
-    if max_seqlen is None:  # validates cu_seqlens on the host, including its total
+    if max_seqlen is None or cu_seqlens.device.type == "cpu":
+        # validate cu_seqlens on the host whenever that costs no device-to-host read: start at 0,
+        # non-decreasing, total == q.shape[1], and no document longer than max_seqlen (a shorter
+        # max_seqlen would make documents collide in the padded batch)
         cpu = cu_seqlens.cpu().to(torch.int64)
+        if cpu.dim() != 1 or cpu.numel() < 2:
+            raise ValueError("cu_seqlens must be 1-D with at least two entries")
+        lens = cpu[1:] - cpu[:-1]
+        if int(cpu[0]) != 0 or bool((lens < 0).any()):
+            raise ValueError("cu_seqlens must start at 0 and be non-decreasing")
         if int(cpu[-1]) != q.shape[1]:
             raise ValueError(f"cu_seqlens covers {int(cpu[-1])} tokens, q has {q.shape[1]}")
+        if max_seqlen is not None and int(lens.max()) > int(max_seqlen):
+            raise ValueError(f"max_seqlen {max_seqlen} is below the longest document ({int(lens.max())})")
     dst, N, T_max = varlen_index(cu_seqlens.to(q.device), max_seqlen, total=q.shape[1])
     qp, kp, vp = (pack_rows(x, dst, N, T_max) for x in (q, k, v))
     if c is not None:

@@ -18,8 +18,9 @@ backward uses it for d(beta).
 
 Parity: ``tests/golden/make_golden_delta.py`` runs the reference's U solve (Triton K14, Triton CPU
 interpreter) and pins this module at single-chunk size; the interpreter cannot run the
-reference's bf16 tensor-core dots of the readout and backward, so those rows rest on this
-restatement.
+reference's bf16 tensor-core dots of the readout and backward, so this module is also checked
+against fixtures that the reference's own Triton kernels produced on a B200
+(``tests/golden/make_golden_delta_gpu.py``).
 """
 
 from __future__ import annotations

@@ -73,6 +73,49 @@ def test_host_side_validation(L):
     assert L.kata_attn_bwd(b, None) == -1  # decay without dc
 
 
+def test_algo_query_reports_the_kernel_family(L):
+    from linatt_b200 import _lib
+
+    def algo(**kw):
+        base = dict(dtype=1, B=1, T=8, H=1, HQ=1, D=128, Dv=128, M=4, score=0, algo=0, scale=1.0)
+        base.update(kw)
+        return L.kata_attn_algo(_lib.AttnFwdArgs(**base))
+
+    assert algo() == 1                      # bf16 in the envelope: tcgen05
+    assert algo(dtype=0) == 2               # fp32: the fp32-exact CUDA-core kernels
+    assert algo(D=256) == 2                 # offset-gated width D != Dv: outside the envelope
+    assert algo(D=256, algo=1) == -8        # forcing tensor cores there is refused
+    assert algo(M=3) == -3
+
+
+def test_bf16_outside_the_envelope_warns_once(monkeypatch):
+    import linatt_b200.parallel_kata_attn as pka
+    from linatt_b200 import _lib
+
+    monkeypatch.setattr(pka, "_SIMT_WARNED", set())
+    a = _lib.AttnFwdArgs(dtype=1, B=1, T=8, H=1, HQ=1, D=256, Dv=128, M=4, score=0, algo=0, scale=1.0)
+    with pytest.warns(RuntimeWarning, match="outside the tensor-core envelope"):
+        pka._warn_if_simt(a, pka.torch.bfloat16)
+    import warnings
+
+    with warnings.catch_warnings():
+        warnings.simplefilter("error")
+        pka._warn_if_simt(a, pka.torch.bfloat16)  # second time: silent
+        a.D, a.Dv = 128, 128
+        pka._warn_if_simt(a, pka.torch.bfloat16)  # tensor-core shape: silent
+
+
+def test_noalloc_accepts_only_the_full_backward(L):
+    from linatt_b200 import _lib
+
+    # phases 1 and 2 would split the backward across calls that share the library's one scratch
+    # array, so the dk/dv pass could read another call's delta and 1/den: both are refused on the host
+    for phases in (1, 2):
+        b = _lib.AttnBwdArgs(q=16, k=16, v=16, o=16, den=16, dout=16, dq=16, dk=16, dv=16, dtype=1, B=1, T=8, H=1,
+                             HQ=1, D=64, Dv=64, M=4, score=0, algo=0, scale=1.0, phases=phases)
+        assert L.kata_attn_bwd_noalloc(b, None) == -1
+
+
 def test_delta_host_side_validation(L):
     from linatt_b200 import _lib
 

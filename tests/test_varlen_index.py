@@ -34,3 +34,13 @@ def test_varlen_index_with_given_max_and_total_matches():
 def test_varlen_index_rejects_bad_cu_seqlens(cu):
     with pytest.raises(ValueError):
         varlen_index(torch.tensor(cu))
+
+
+@pytest.mark.parametrize("cu,max_seqlen,msg", [([0, 3, 10], 5, "below the longest"), ([0, 3, 9], 7, "covers"),
+                                               ([0, 4, 2, 10], 8, "non-decreasing")])
+def test_varlen_api_checks_host_cu_seqlens_even_with_max_seqlen(cu, max_seqlen, msg):
+    from linatt_b200.varlen import parallel_kata_attn_varlen
+
+    q = torch.zeros(1, 10, 1, 64)
+    with pytest.raises(ValueError, match=msg):
+        parallel_kata_attn_varlen(q, q, q, torch.tensor(cu), max_seqlen=max_seqlen)
