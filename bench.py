@@ -22,6 +22,10 @@ Printed JSON line (rank 0):
   cpu_baseline  the reference's CPU path (its PyTorch fp32 functions, restated in
             oracle/kata_cpu_ref.py) on this host's cores, on a bounded sample of (b,h) slices
   clocks    SM clock median / max and throttle reasons sampled through NVML during the timing
+  sp        config 4 on the same ranks (B=1, T=131072, H=16, D=Dv=128, M=4): T split contiguously
+            over the N GPUs (strong scaling, the one path with a collective: the prefix state is
+            all-gathered over NCCL); its step time, tokens/s, the all-gather alone and the
+            shard-local flash kernels alone (a few steps of its own after the headline timing)
 
 L2: three rotating input sets of 537 MB each (bf16 q, k, v, dO of 134 MB apiece) are cycled, each
 larger than the 126 MB L2, so no step reads inputs left in L2 by the previous step.
@@ -411,6 +415,14 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
                "d2h_bytes_per_step": 4 * elem, "steps": Ke, "ms_per_step": e_ms / Ke,
                "pipelined": "upload / compute / download on three streams", "outputs_match": bool(e2e_match)}
 
+    # config 4 (sequence parallel over the same ranks): its own short run, so that every scaling
+    # run of this bench also records the long-context path that communicates
+    sp = None
+    if not args.no_sp:
+        del step
+        torch.cuda.empty_cache()
+        sp = sp_measure(torch, dist, world, rank, dev, max(3, min(K, args.sp_steps)), 3)
+
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -442,6 +454,7 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(world), "roofline": roofline, "cpu_baseline": cpu,
         "e2e": e2e, "clocks": clk.summary(), "gpu_launches": (4 if DECAY else 3) * K,  # decay: + c transpose
+        "sp": sp,
     }
     print(json.dumps(line), flush=True)
 
@@ -475,21 +488,25 @@ def _timed_steps(torch, dist, world, dev, step, K, W):
     return ms, clk.summary()
 
 
-def run_sp(args, rank: int, world: int, local: int) -> None:
-    """Config 4: B=1, T=131072, H=16, D=Dv=128, M=4 concat, bf16, T split contiguously over the
-    ranks (strong scaling); one step = forward + backward through sp_kata_attn."""
-    import torch
-    import torch.distributed as dist
+SP_SHAPE = (1, 131072, 16, 128, 4)  # config 4: B, T, H, D=Dv, M
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-    from linatt_b200.sequence_parallel import sp_kata_attn
+def sp_flops() -> float:
+    Bs, Ts, Hs, Ds, _ = SP_SHAPE
+    return 7 * Bs * Hs * 2.0 * pairs(Ts) * Ds  # 7 GEMM-equivalents of the whole causal problem
 
-    Bs, Ts, Hs, Ds, Ms = 1, 131072, 16, 128, 4
+
+def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    """Config 4 (B=1, T=131072, H=16, D=Dv=128, M=4 concat, bf16), T split contiguously over the
+    ranks (strong scaling); one step = forward + backward through sp_kata_attn.  Besides the step
+    time: the NCCL all-gather of one state-sized buffer alone (each step runs two, one per
+    direction, each issued before and overlapped with the shard-local flash kernels) and the
+    shard-local flash forward + backward alone.  Every rank runs the same collectives in the same
+    order.  Returns the `sp` object of the JSON line (meaningful on rank 0)."""
+    from linatt_b200 import parallel_kata_attn as pka
+    from linatt_b200.sequence_parallel import gather_states, sp_kata_attn
+
+    Bs, Ts, Hs, Ds, Ms = SP_SHAPE
     Tl = Ts // world
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     sets = []
@@ -505,29 +522,72 @@ def run_sp(args, rank: int, world: int, local: int) -> None:
         for x in leaves:
             x.grad = None
 
-    ms, clk = _timed_steps(torch, dist, world, dev, step, args.steps, args.warmup)
+    ms, clk = _timed_steps(torch, dist, world, dev, step, steps, warmup)
+    step_ms = ms / steps
+
+    def local(i):  # the shard-local flash kernels alone (what the exchange overlaps)
+        q, k, v, do = sets[i % 2]
+        o, den = pka._fwd(q, k, v, Ms, None, "concat")
+        pka._bwd(q, k, v, o, den, do, Ms, None, "concat")
+
+    local_ms, _ = _timed_steps(torch, dist, world, dev, local, steps, 1)
+    gather_ms = None
+    F = Ms * (Ds // Ms) ** 2
+    if world > 1:
+        buf = torch.zeros(Bs * Hs, F, Ds + 8, device=dev)
+        gather_ms, _ = _timed_steps(torch, dist, world, dev, lambda i: gather_states(buf).wait(), steps, 2)
+        gather_ms /= steps
+        del buf
+    del sets
+    torch.cuda.empty_cache()
+    ach = sp_flops() / (step_ms / 1e3) / 1e12
+    return {
+        "workload": "sequence-parallel KATA-SPD fwd+bwd, concat M=4, causal, bf16 (config 4)",
+        "global_batch": Bs, "seq_len": Ts, "heads": Hs, "head_dim": Ds, "num_groups": Ms,
+        "parallelism": f"contiguous T split x{world}" + (", prefix state all-gather over NCCL" if world > 1 else ""),
+        "scaling": "strong", "steps": steps, "warmup": warmup, "ms_per_step": step_ms,
+        "value": Bs * Ts / (step_ms / 1e3), "unit": UNIT,
+        "local_flash_fwd_bwd_ms": local_ms / steps,
+        "state_allgather_ms": gather_ms,
+        "state_bytes_per_rank": Bs * Hs * F * (Ds + 8) * 4,
+        "full_problem_tflops_per_gpu": ach / world,
+        "note": "full_problem_tflops counts the 246 TFLOP of the whole causal problem; the sharded job "
+                "executes less (cross-shard blocks go through the O(T F Dv) state), so it is not a "
+                "tensor-core utilisation figure",
+        "clocks": clk,
+    }
+
+
+def run_sp(args, rank: int, world: int, local: int) -> None:
+    """Standalone line of config 4 (see sp_measure)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    sp = sp_measure(torch, dist, world, rank, dev, args.steps, args.warmup)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    Bs, Ts, Hs, Ds, Ms = SP_SHAPE
     peak, src = load_peaks()
-    step_ms = ms / args.steps
-    flops = 7 * Hs * 2.0 * pairs(Ts) * Ds  # 7 GEMM-equivalents of the whole causal problem
-    ach = flops / (step_ms / 1e3) / 1e12
     line = {
         "metric": "KATA-SPD sequence-parallel fwd+bwd tokens/s at B1·T131072·H16·D128 (config 4)",
-        "value": Bs * Ts / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
+        "value": sp["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sp["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "sequence-parallel KATA-SPD fwd+bwd, concat M=4, causal, bf16 (config 4)",
-                   "global_batch": Bs, "seq_len": Ts, "heads": Hs, "head_dim": Ds, "num_groups": Ms,
-                   "parallelism": f"contiguous T split x{world}, prefix state all-gather over NCCL",
-                   "l2": "2 rotating input sets per rank plus GB-sized intermediates per step"},
-        "roofline": {"bound": "tensor", "achieved": ach / world, "peak": peak, "unit": "TFLOP/s",
-                     "frac": ach / world / peak, "traffic": None, "peak_source": src,
-                     "note": "full-problem causal FLOPs (246 TFLOP) / step time / GPUs"},
-        "clocks": clk, "gpu_launches": None,
+        "config": {k: sp[k] for k in ("workload", "global_batch", "seq_len", "heads", "head_dim", "num_groups",
+                                      "parallelism")},
+        "roofline": {"bound": "tensor", "achieved": sp["full_problem_tflops_per_gpu"], "peak": peak,
+                     "unit": "TFLOP/s", "frac": sp["full_problem_tflops_per_gpu"] / peak, "traffic": None,
+                     "peak_source": src, "note": sp["note"]},
+        "sp": sp, "clocks": sp["clocks"], "gpu_launches": None,
     }
     print(json.dumps(line), flush=True)
 
@@ -724,6 +784,8 @@ def main() -> None:
     ap.add_argument("--cpu-slices", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sp", action="store_true", help="skip the config-4 sequence-parallel object of the line")
+    ap.add_argument("--sp-steps", type=int, default=6, help="timed steps of the config-4 object (>= 3)")
     ap.add_argument("--num-groups", type=int, default=4, help="M (the benchmark metric is quoted at M=4)")
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
     ap.add_argument("--decay", action="store_true",
@@ -740,7 +802,7 @@ def main() -> None:
     if DECAY:
         if SCORE != "concat":
             ap.error("--decay pairs with the concat score only (as in the reference)")
-        args.no_e2e = args.no_cpu_baseline = True
+        args.no_e2e = args.no_cpu_baseline = args.no_sp = True
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

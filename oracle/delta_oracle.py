@@ -82,3 +82,42 @@ def flash_delta(q, k, v, beta, M, scale=None, normalize=False, eps=1e-5, grad_ou
         total.backward()
         res.update(dq=q.grad.numpy(), dk=k.grad.numpy(), dv=v.grad.numpy(), dbeta=beta.grad.numpy())
     return res
+
+
+def state_lin(q, k, v, M, scale=None, grad_out=None):
+    """Linear SPD numerator o = tril(kappa(q, k)) v and its gradients (float64), head-major
+    (B, H, T, D) inputs, restating kata/spd/chunk_state_lin.py:1-12 (the chunked-state kernel
+    computes exactly this raw numerator) and its backward (:437-504).  Returns a dict o [, dq, dk, dv]."""
+    q, k, v = (torch.as_tensor(np.asarray(x), dtype=torch.float64) for x in (q, k, v))
+    B, H, T, D = q.shape
+    scale = 1.0 / (D // M) if scale is None else float(scale)
+    want = grad_out is not None
+    q, k, v = (x.clone().requires_grad_(want) for x in (q, k, v))
+    o = torch.zeros(B, H, T, v.shape[-1], dtype=torch.float64)
+    outs = []
+    for b in range(B):
+        for h in range(H):
+            outs.append(torch.tril(_kappa(q[b, h], k[b, h], M, scale)) @ v[b, h])
+    o = torch.stack(outs).reshape(B, H, T, -1)
+    res = {"o": o.detach().numpy()}
+    if want:
+        o.backward(torch.as_tensor(np.asarray(grad_out), dtype=torch.float64))
+        res.update(dq=q.grad.numpy(), dk=k.grad.numpy(), dv=v.grad.numpy())
+    return res
+
+
+def chunk_scan(q, k, v, M, scale=None, eps=1e-6):
+    """Normalised sum-score forward of kata/spd/chunk_scan.py:295-406 (sum mode), head-major:
+    den = max(sum_{s<=t} kappa, eps), o = tril(kappa) v / den (its output kernel, :166-177)."""
+    q, k, v = (torch.as_tensor(np.asarray(x), dtype=torch.float64) for x in (q, k, v))
+    B, H, T, D = q.shape
+    scale = 1.0 / (D // M) if scale is None else float(scale)
+    o = torch.zeros(B, H, T, v.shape[-1], dtype=torch.float64)
+    den = torch.zeros(B, H, T, dtype=torch.float64)
+    for b in range(B):
+        for h in range(H):
+            P = torch.tril(_kappa(q[b, h], k[b, h], M, scale))
+            d = P.sum(1).clamp_min(eps)
+            o[b, h] = (P @ v[b, h]) / d[:, None]
+            den[b, h] = d
+    return {"o": o.numpy(), "den": den.numpy()}

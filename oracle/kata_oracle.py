@@ -125,6 +125,56 @@ def attn_bwd(q, k, v, do, M, scale=None, score="concat", c=None):
     return dq, dk, dv, dc
 
 
+def attn_tail_window(qh, kh, vh, doh, M, w, scale=None, chunk=8192):
+    """Exact concat-score forward and backward restricted to the last ``w`` tokens of one long head.
+
+    qh, kh, vh, doh (T, D/Dv) for one (batch, head).  Row t of o, den, delta and dq depends on row t
+    against every key s <= t, and the key rows s >= T - w of dk and dv depend only on queries t >= s,
+    all inside the window; so this is exact for the window at any T while memory stays
+    O(w * chunk).  Same formulas as ``attn_fwd`` / ``attn_bwd`` (kata/parallel_kata_attn.py:49-146).
+    Returns dict o, den, dq (rows T-w..T-1) and dk, dv (key rows T-w..T-1), float64.
+    """
+    qh, kh, vh, doh = (np.asarray(x, dtype=np.float64) for x in (qh, kh, vh, doh))
+    T, D = qh.shape
+    E = D // M
+    if scale is None:
+        scale = 1.0 / np.sqrt(E)
+    t0 = T - w
+    qr, dor = qh[t0:], doh[t0:]
+    rows = np.arange(t0, T)[:, None]
+
+    def blocks():
+        for s0 in range(0, T, chunk):
+            s1 = min(T, s0 + chunk)
+            qk = [scale * (qr[:, g * E:(g + 1) * E] @ kh[s0:s1, g * E:(g + 1) * E].T) for g in range(M)]
+            mask = (np.arange(s0, s1)[None, :] <= rows)
+            yield s0, s1, qk, sum(p * p for p in qk) * mask, mask
+
+    den = np.zeros(w)
+    num = np.zeros((w, vh.shape[1]))
+    for s0, s1, _, A, _ in blocks():
+        den += A.sum(1)
+        num += A @ vh[s0:s1]
+    rden = 1.0 / np.where(den > 0, den, 1.0)
+    o = num * rden[:, None]
+    delta = (o * dor).sum(1)
+    dq = np.zeros((w, D))
+    dk = np.zeros((w, D))
+    dv = np.zeros((w, vh.shape[1]))
+    for s0, s1, qk, A, mask in blocks():
+        dA = (dor @ vh[s0:s1].T - delta[:, None]) * rden[:, None] * mask
+        for g in range(M):
+            W = 2.0 * scale * qk[g] * dA
+            dq[:, g * E:(g + 1) * E] += W @ kh[s0:s1, g * E:(g + 1) * E]
+            if s1 > t0:  # key rows inside the window
+                a = max(s0, t0)
+                dk[a - t0:s1 - t0, g * E:(g + 1) * E] += W[:, a - s0:].T @ qr[:, g * E:(g + 1) * E]
+        if s1 > t0:
+            a = max(s0, t0)
+            dv[a - t0:s1 - t0] += (A[:, a - s0:] * rden[:, None]).T @ dor
+    return {"o": o, "den": den, "dq": dq, "dk": dk, "dv": dv}
+
+
 def augment_offset(q, k, off, M):
     """Offset gate packing (kata/layer.py:268-282): append off_t to each q group and 1 to each k
     group, zero-pad every group to Ep = max(16, 2**bit_length(E)); returns (q_in, k_in)."""

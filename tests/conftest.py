@@ -41,6 +41,24 @@ def golden_delta():
     return out
 
 
+@pytest.fixture(scope="session")
+def golden_delta_gpu():
+    """Dict case -> dict of arrays from tests/golden/delta_golden_gpu.npz: the reference's own Triton
+    flash_delta (U, readout, den, o and all gradients) run on a B200 by make_golden_delta_gpu.py."""
+    return load_delta_gpu_golden()
+
+
+def load_delta_gpu_golden():
+    z = np.load(GOLDEN / "delta_golden_gpu.npz")
+    out: dict[str, dict[str, np.ndarray]] = {}
+    for key in z.files:
+        if "/" not in key:
+            continue
+        case, name = key.split("/")
+        out.setdefault(case, {})[name] = z[key]
+    return out
+
+
 def attn_case_meta(rec):
     B, T, HQ, H, D, Dv, M, is_sum, decay = (int(x) for x in rec["meta"])
     return dict(B=B, T=T, HQ=HQ, H=H, D=D, Dv=Dv, M=M, score="sum" if is_sum else "concat", decay=bool(decay))

@@ -248,6 +248,37 @@ def test_config3_full_size_forward():
         assert ko.rel_l2(den[b:b + 1, :, h:h + 1].cpu().numpy(), den_ref) < 1e-3
 
 
+def test_config3_full_size_backward():
+    """Config 3 backward at full size: T = 4096 means 32 key tiles per query tile, where the fp32
+    TMEM accumulation of dQ / dK over many tiles and the bf16 rounding of P and W could drift.
+    Checks linearity in dO over the whole problem and dq / dk / dv on two (b, h) slices against
+    the fp64 oracle at full T (about 30 s of CPU per slice)."""
+    pka = _pka("auto")
+    B, T, H, D, M = 16, 4096, 8, 128, 4
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q, k, v = ((torch.randn(B, T, H, D, device="cuda", generator=g) / math.sqrt(D)).bfloat16() for _ in range(3))
+    do = torch.randn(B, T, H, D, device="cuda", generator=g).bfloat16()
+    o, den = pka.parallel_kata_attn_fwd(q, k, v, num_groups=M)
+    dq, dk, dv = pka.parallel_kata_attn_bwd(q, k, v, o, den, do, M, None)
+    torch.cuda.synchronize()
+    for x in (dq, dk, dv):
+        assert torch.isfinite(x.float()).all()
+    # every gradient is linear in dO: grads(dO + dO') == grads(dO) + grads(dO') within bf16 rounding
+    do2 = torch.roll(do, 1, dims=0)
+    g2 = pka.parallel_kata_attn_bwd(q, k, v, o, den, do2, M, None)
+    g12 = pka.parallel_kata_attn_bwd(q, k, v, o, den, (do.float() + do2.float()).bfloat16(), M, None)
+    for name, a, b, c in zip(("dq", "dk", "dv"), (dq, dk, dv), g2, g12):
+        e = ko.rel_l2(c.float().cpu().numpy(), (a.float() + b.float()).cpu().numpy())
+        assert e < 1e-2, f"{name} not linear in dO: {e:.3e}"
+    # full-T oracle on two (b, h) slices
+    for b, h in ((0, 0), (15, 7)):
+        sl = lambda x: x[b:b + 1, :, h:h + 1].float().cpu().numpy()  # noqa: E731
+        rdq, rdk, rdv, _ = ko.attn_bwd(sl(q), sl(k), sl(v), sl(do), M)
+        for name, got, ref in (("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+            e = ko.rel_l2(sl(got), ref)
+            assert e < 1e-2, f"slice ({b},{h}) {name}: rel-L2 {e:.3e}"
+
+
 def test_backward_in_a_fresh_process():
     """The backward runs on the framework's autograd worker thread.  In a fresh process that thread
     may not have a current CUDA context when the library encodes its tensor maps (the buffers it

@@ -96,6 +96,30 @@ def test_flash_delta_U_matches_reference_golden(golden_delta):
         assert e < 1e-5, f"{name}: rel-L2 {e:.3e}"
 
 
+@pytest.mark.parametrize("case", ["m4_norm", "m4_raw", "m2_norm_default_scale", "m1_raw"])
+def test_flash_delta_matches_reference_run_on_gpu(golden_delta_gpu, case):
+    """The kernels against the reference's own Triton flash_delta on a B200, same bf16 inputs:
+    U, the readout numerator, den, o and dq, dk, dv, dbeta through autograd (rel-L2 <= 1e-2)."""
+    from linatt_b200.spd import flash_delta
+    from linatt_b200.spd.flash_delta import flash_delta_den, flash_delta_readout, flash_delta_U
+
+    rec = golden_delta_gpu[case]
+    B, T, H, D, Dv, M, scale, norm = rec["meta"]
+    M, scale, norm = int(M), (None if scale < 0 else float(scale)), bool(norm)
+    t = lambda x, dt=torch.bfloat16: torch.from_numpy(x).to(dt).cuda()  # noqa: E731
+    q, k, v, beta = t(rec["q"]), t(rec["k"]), t(rec["v"]), t(rec["beta"])
+    got = {"U": flash_delta_U(q, k, v, beta, M, scale=scale)}
+    got["num"] = flash_delta_readout(q, k, got["U"], M, scale=scale)
+    got["den"] = flash_delta_den(q, k, M, scale=scale)
+    leaves = [x.clone().requires_grad_(True) for x in (q, k, v, beta)]
+    o = flash_delta(*leaves, M, scale=scale, normalize=norm)
+    o.backward(t(rec["do"], torch.float32))
+    got.update(o=o.detach(), dq=leaves[0].grad, dk=leaves[1].grad, dv=leaves[2].grad, dbeta=leaves[3].grad)
+    for name, x in got.items():
+        e = rel_l2(x.float().cpu().double().numpy(), rec[name])
+        assert e < 1e-2, f"{case} {name}: rel-L2 {e:.3e}"
+
+
 def test_component_functions_match_oracle():
     from linatt_b200.spd.flash_delta import flash_delta_U, flash_delta_bwd, flash_delta_den, flash_delta_readout
 

@@ -90,6 +90,40 @@ def test_sp_emulated_matches_oracle():
         assert ko.rel_l2(f(g), r) < 1e-2, name
 
 
+def test_config4_full_size_emulated_ranks():
+    """Config 4 at its size (B=1, T=131072, H=16, D=Dv=128, M=4, bf16): R in {2, 4, 8} emulated
+    ranks against the single-GPU kernels over the whole sequence (o, den, dq, dk, dv), and both
+    against the exact fp64 oracle on the last 256 tokens of two heads.  At this length the
+    cross-shard state sums up to 114 688 tokens in fp32 before the bf16 GEMM; the tail window is
+    where that matters most (its queries see every earlier shard)."""
+    B, T, H, D, M = 1, 131072, 16, 128, 4
+    g = torch.Generator(device="cuda").manual_seed(44)
+    q, k, v = ((torch.randn(B, T, H, D, device="cuda", generator=g) / D ** 0.5).bfloat16() for _ in range(3))
+    do = torch.randn(B, T, H, D, device="cuda", generator=g).bfloat16()
+    ref = full(q, k, v, do, M)
+    torch.cuda.synchronize()
+    w = 256
+    f = lambda x, h: x[0, :, h].float().cpu().numpy()  # noqa: E731
+    oracle = {h: ko.attn_tail_window(f(q, h), f(k, h), f(v, h), f(do, h), M, w) for h in (0, 15)}
+
+    def check_tail(outs, tag):
+        for h, r in oracle.items():
+            for name, got in zip(("o", "den", "dq", "dk", "dv"), outs):
+                x = got[0, T - w:, h].float().cpu().numpy()
+                e = ko.rel_l2(x, r[name])
+                assert e < 1e-2, f"{tag} head {h} tail {name}: rel-L2 {e:.3e}"
+
+    check_tail(ref, "single GPU")
+    for R in (2, 4, 8):
+        got = emulate(q, k, v, do, R, M)
+        for name, a, b in zip(("o", "den", "dq", "dk", "dv"), got, ref):
+            e = rel(a, b)
+            assert e < 1e-2, f"R={R} {name}: rel-L2 {e:.3e} against the single-GPU kernels"
+        check_tail(got, f"R={R}")
+        del got
+        torch.cuda.empty_cache()
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs (the real NCCL path)")
 def test_sp_nccl_two_ranks():
     n = min(torch.cuda.device_count(), 4)

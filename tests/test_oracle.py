@@ -105,6 +105,29 @@ def test_delta_oracle_matches_reference_U(case):
     assert ko.rel_l2(rec["beta"][..., None] * (rec["v"] - res["E"]), res["U"]) < 1e-10
 
 
+@pytest.mark.parametrize("case", ["m4_norm", "m4_raw", "m2_norm_default_scale", "m1_raw"])
+def test_delta_oracle_matches_reference_run_on_gpu(case):
+    """The whole delta rule against the reference's own Triton flash_delta run on a B200
+    (tests/golden/make_golden_delta_gpu.py): multi-chunk U, the readout numerator, den, o for both
+    normalize settings, and dq, dk, dv, dbeta.  The reference casts its inter-chunk products and
+    readout operands to bf16 and returns bf16 gradients, so it sits a few 1e-3 (rel-L2) from the
+    exact fp64 restatement: the tolerance is the bf16 bar, 1e-2."""
+    from oracle import delta_oracle as do
+    from tests.conftest import load_delta_gpu_golden
+
+    rec = load_delta_gpu_golden()[case]
+    B, T, H, D, Dv, M, scale, norm = rec["meta"]
+    scale = None if scale < 0 else float(scale)
+    raw = do.flash_delta(rec["q"], rec["k"], rec["v"], rec["beta"], int(M), scale)
+    full = do.flash_delta(rec["q"], rec["k"], rec["v"], rec["beta"], int(M), scale, normalize=bool(norm),
+                          eps=1e-5, grad_out=rec["do"])
+    pairs = [("U", raw["U"]), ("num", raw["o"]), ("den", raw["den"]), ("o", full["o"])]
+    pairs += [(g, full[g]) for g in ("dq", "dk", "dv", "dbeta")]
+    for name, ref in pairs:
+        e = ko.rel_l2(ref, rec[name])
+        assert e < 1e-2, f"{case} {name}: rel-L2 {e:.3e}"
+
+
 def test_delta_oracle_gradients_finite_difference():
     from oracle import delta_oracle as do
 
@@ -190,3 +213,15 @@ def test_gdn_oracle_gate_and_l2norm_finite_difference():
         xm[idx] -= eps
         num = (f(**{name: xp}) - f(**{name: xm})) / (2 * eps)
         assert abs(num - res["d" + name][idx]) < 1e-6 * max(1.0, abs(num)), name
+
+
+def test_tail_window_oracle_matches_the_full_oracle():
+    """attn_tail_window (used for the config-4 check at T = 131072) is exact for the last w rows."""
+    rng = np.random.default_rng(1)
+    T, D, w = 300, 64, 40
+    q, k, v, do = (rng.standard_normal((1, T, 1, D)) / 8 for _ in range(4))
+    o, den = ko.attn_fwd(q, k, v, 4)
+    dq, dk, dv, _ = ko.attn_bwd(q, k, v, do, 4)
+    r = ko.attn_tail_window(q[0, :, 0], k[0, :, 0], v[0, :, 0], do[0, :, 0], 4, w, chunk=64)
+    for name, full in (("o", o), ("den", den), ("dq", dq), ("dk", dk), ("dv", dv)):
+        assert ko.rel_l2(r[name], full[0, -w:, 0]) < 1e-12, name
