@@ -387,6 +387,13 @@ KATA_API int kata_abi_version(void);
 KATA_API int kata_selftest_umma(const void* A, const void* B, float* D, int M, int N, int K, int a_mn, int b_mn,
                        int a_sw, int b_sw, int a_tmem, kata_stream_t stream);
 
+/* Diagnostic: the same with M == 64 (the 64-token chunk tiles of the gated delta rule), both operands
+ * in 128-byte swizzled shared memory, and the accumulator at TMEM lane offset lane_off (0 or 16):
+ * checks that row m of an M = 64 accumulator sits in lane (m % 16) + 32 * (m / 16) + lane_off.
+ * No counterpart in the reference. */
+KATA_API int kata_selftest_umma_m64(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
+                                    int lane_off, kata_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

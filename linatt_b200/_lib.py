@@ -161,6 +161,8 @@ def lib() -> ctypes.CDLL:
             L.kata_decode_step.argtypes = [ctypes.POINTER(DecodeArgs), c_void_p]
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
+            L.kata_selftest_umma_m64.restype = c_int
+            L.kata_selftest_umma_m64.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 5 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:
                 raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
             _lib = L

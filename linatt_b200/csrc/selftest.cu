@@ -12,6 +12,7 @@ namespace {
 struct SelftestParams {
   int M, N, K;
   int a_mn, b_mn, a_sw, b_sw, a_tmem;
+  int lane_off;  // M == 64 only: TMEM lane offset of the accumulator (0 or 16)
   const __nv_bfloat16* A;  // for the a_tmem path (row-major M x K or K x M)
   float* D;
   int* status;
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(128, 1)
           umma_ts(tbase, tbase + a_col + static_cast<uint32_t>(kk * 8), bd, idesc, kk > 0);
         } else {
           const uint64_t ad = operand_desc(baseA, p.a_mn != 0, cwA, p.a_mn ? p.K : p.M, kk);
-          umma_ss(tbase, ad, bd, idesc, kk > 0);
+          umma_ss(tbase + (static_cast<uint32_t>(p.lane_off) << 16), ad, bd, idesc, kk > 0);
         }
       }
       umma_commit(&bar_mma);
@@ -123,12 +124,17 @@ __global__ void __launch_bounds__(128, 1)
   const bool ok = mbar_wait(&bar_mma, 0, wc);
   tc_fence_after();
   if (ok) {
-    const int row = tid;
+    // M = 128: row = TMEM lane.  M = 64 (one CTA): row m sits in lane (m % 16) + 32 * (m / 16) +
+    // lane_off, i.e. the first (or, with lane_off 16, the second) half of every warp's 32 lanes.
+    const int lane = tid & 31;
+    const bool mine = p.M == 128 || (lane & 16) == p.lane_off;
+    const int row = p.M == 128 ? tid : warp * 16 + (lane & 15);
     for (int n0 = 0; n0 < p.N; n0 += 16) {
       uint32_t r[16];
       tmem_ld16(tbase + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(n0), r);
       tmem_wait_ld();
-      for (int j = 0; j < 16; ++j) p.D[static_cast<size_t>(row) * p.N + n0 + j] = __uint_as_float(r[j]);
+      if (mine)
+        for (int j = 0; j < 16; ++j) p.D[static_cast<size_t>(row) * p.N + n0 + j] = __uint_as_float(r[j]);
     }
   }
   tc_fence_before();
@@ -139,12 +145,31 @@ __global__ void __launch_bounds__(128, 1)
 }  // namespace
 }  // namespace kata
 
+namespace {
+int selftest_launch(const void* A, const void* B, float* D, int M, int N, int K, int a_mn, int b_mn, int a_sw,
+                    int b_sw, int a_tmem, int lane_off, kata_stream_t stream);
+}  // namespace
+
 extern "C" int kata_selftest_umma(const void* A, const void* B, float* D, int M, int N, int K, int a_mn, int b_mn,
                                   int a_sw, int b_sw, int a_tmem, kata_stream_t stream) {
+  if (M != 128) return KATA_ERR_SHAPE;
+  return selftest_launch(A, B, D, M, N, K, a_mn, b_mn, a_sw, b_sw, a_tmem, 0, stream);
+}
+
+extern "C" int kata_selftest_umma_m64(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
+                                      int lane_off, kata_stream_t stream) {
+  if (lane_off != 0 && lane_off != 16) return KATA_ERR_INVALID;
+  return selftest_launch(A, B, D, 64, N, K, a_mn, b_mn, 128, 128, 0, lane_off, stream);
+}
+
+namespace {
+int selftest_launch(const void* A, const void* B, float* D, int M, int N, int K, int a_mn, int b_mn, int a_sw,
+                    int b_sw, int a_tmem, int lane_off, kata_stream_t stream) {
   using namespace kata;
   if (!A || !B || !D) return KATA_ERR_INVALID;
   auto sw_ok = [](int s) { return s == 32 || s == 64 || s == 128; };
-  if (M != 128 || N < 16 || N > 256 || N % 16 || K < 16 || K > 256 || K % 16 || !sw_ok(a_sw) || !sw_ok(b_sw))
+  if ((M != 128 && M != 64) || (M == 64 && a_tmem) || N < 16 || N > 256 || N % 16 || K < 16 || K > 256 ||
+      K % 16 || !sw_ok(a_sw) || !sw_ok(b_sw))
     return KATA_ERR_SHAPE;
   const int cwA = a_sw / 2, cwB = b_sw / 2;
   if ((a_mn ? M : K) % cwA || (b_mn ? N : K) % cwB) return KATA_ERR_SHAPE;
@@ -167,7 +192,8 @@ extern "C" int kata_selftest_umma(const void* A, const void* B, float* D, int M,
     int e = encode_tmap_16bit(&tmB, B, 4, dims, strides, box, b_sw);
     if (e) return e;
   }
-  SelftestParams p{M, N, K, a_mn, b_mn, a_sw, b_sw, a_tmem, static_cast<const __nv_bfloat16*>(A), D, nullptr};
+  SelftestParams p{M, N, K, a_mn, b_mn, a_sw, b_sw, a_tmem, lane_off, static_cast<const __nv_bfloat16*>(A), D,
+                   nullptr};
   const size_t smem = ((static_cast<size_t>(M) * K * 2 + 1023) & ~size_t(1023)) + static_cast<size_t>(N) * K * 2 + 1024;
   cudaError_t ce = cudaFuncSetAttribute(selftest_umma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem));
@@ -175,3 +201,4 @@ extern "C" int kata_selftest_umma(const void* A, const void* B, float* D, int M,
   selftest_umma_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(tmA, tmB, p);
   return from_cuda(cudaGetLastError());
 }
+}  // namespace

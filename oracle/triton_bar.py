@@ -17,7 +17,10 @@ Workloads (seeded synthetic inputs with the benchmark shapes):
          dq_M4, dkdv_M4), unmodified.  Ours: kata_attn_fwd, kata_attn_bwd phases 1 (dq) and 2 (dk/dv).
   gdn    config 2: fla's chunk_gated_delta_rule (fla/ops/gated_delta_rule/chunk.py:365, Triton;
          third-party, installed) forward + backward at B=8, T=2048, H=12, K=V=64, bf16 inputs,
-         against linatt_b200.gated_delta_rule.chunk_gated_delta_rule.
+         against linatt_b200.gated_delta_rule.chunk_gated_delta_rule.  fla 0.5.1 dispatches some
+         backward pieces to an optional TileLang backend when tilelang is importable; on B200 that
+         backend's chunk_bwd_dqkwg raised a misaligned-address fault, so this script sets
+         FLA_DISABLE_BACKEND_DISPATCH=1 (fla's own switch) and times fla's default Triton kernels.
   delta  the SPD delta rule at the 200M mixer geometry (B=8, T=2048, H=12, D=Dv=64, M=4, scale 0.5,
          normalised, bf16 inputs): the reference's flash_delta (kata/spd/flash_delta.py:1111)
          forward + backward against linatt_b200.spd.flash_delta.
@@ -34,6 +37,7 @@ import argparse
 import importlib
 import json
 import math
+import os
 import statistics
 import sys
 import types
@@ -243,6 +247,7 @@ def main() -> None:
     ap.add_argument("--what", default="attn,gdn,delta")
     ap.add_argument("--reps", type=int, default=20)
     a = ap.parse_args()
+    os.environ["FLA_DISABLE_BACKEND_DISPATCH"] = "1"  # fla's Triton kernels, not its TileLang backend
     ref = load_reference(a.reference_root.resolve())
     torch.cuda.init()
     out = {"gpu": torch.cuda.get_device_name(0)}

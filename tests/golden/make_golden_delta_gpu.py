@@ -23,7 +23,9 @@ own Triton kernels on the same kind of inputs (bf16, head-major (B, H, T, D)), i
 
   * spd_state_lin   (kata/spd/chunk_state_lin.py:507-510): o and dq, dk, dv (autograd)
   * spd_chunk_scan  (kata/spd/chunk_scan.py:295-406, sum mode): o, den
-  * flash_delta_state (kata/spd/chunk_state_v2.py:385-387): o and dq, dk, dv, dbeta (autograd)
+  * flash_delta_state (kata/spd/chunk_state_v2.py:385-387): o and dq, dk, dv, dbeta (its forward
+    kernel launched without the H argument its launcher wrongly passes, then its own backward
+    spd_delta_state_bwd, :770-813)
 
 The reference checkout is given on the command line and is imported by file path; it is not part
 of this repository.
@@ -103,6 +105,26 @@ def main():
         print(f"wrote {path} ({path.stat().st_size / 1e6:.2f} MB)")
 
 
+def delta_state_forward(m, q, k, v, beta, M, scale):
+    """flash_delta_state's forward, (o, U, S).  Its launcher spd_delta_state_v2 passes H= to
+    _state_v2_kernel, whose signature has no H (kata/spd/chunk_state_v2.py:340 vs :372-390), so at
+    HEAD it raises; this replicates that launcher's tile choices and launch without the H argument."""
+    B, H, T, D = q.shape
+    DV = v.shape[-1]
+    E = D // M
+    scale = 1.0 / E if scale is None else scale
+    DVB = DV
+    BI = max(1, 256 // E)
+    while E % BI != 0:
+        BI //= 2
+    o = torch.empty(B, H, T, DV, device=q.device, dtype=torch.float32)
+    S = torch.zeros(B * H, E * E, DV, device=q.device, dtype=torch.float32)
+    U = torch.empty(B, H, T, DV, device=q.device, dtype=torch.float32)
+    m._state_v2_kernel[(B * H,)](q.contiguous(), k.contiguous(), v.contiguous(), beta.contiguous(), o, U, S,
+                                 scale ** 0.5, T, D=D, E=E, M=M, DV=DV, DVB=DVB, C=64, E2=E * E, BI=BI, WRITE_U=True)
+    return o, U, S
+
+
 def run_spd_case(mods, dev, i, case, out):
     name, fn, B, H, T, D, Dv, M, scale = case
     g = torch.Generator().manual_seed(4000 + i)
@@ -119,12 +141,13 @@ def run_spd_case(mods, dev, i, case, out):
         leaves = [x.clone().requires_grad_(True) for x in ((q, k, v) if fn == "state_lin" else (q, k, v, beta))]
         if fn == "state_lin":
             o = mods["state_lin"].spd_state_lin(*leaves, M, scale=scale)
+            o.backward(do.to(o.dtype))
+            tensors.update(o=o.detach(), dq=leaves[0].grad, dk=leaves[1].grad, dv=leaves[2].grad)
         else:
-            o = mods["delta_state"].flash_delta_state(*leaves, M, scale=scale)
-        o.backward(do.to(o.dtype))
-        tensors.update(o=o.detach(), dq=leaves[0].grad, dk=leaves[1].grad, dv=leaves[2].grad)
-        if fn == "delta_state":
-            tensors["dbeta"] = leaves[3].grad
+            m = mods["delta_state"]
+            o, U, S = delta_state_forward(m, q, k, v, beta, M, scale)
+            dq, dk, dv, db = m.spd_delta_state_bwd(q, k, v, beta, do, U, S, M, scale=scale, C=64)
+            tensors.update(o=o, dq=dq, dk=dk, dv=dv, dbeta=db)
     torch.cuda.synchronize()
     for key, val in tensors.items():
         out[f"{name}/{key}"] = val.float().cpu().numpy()

@@ -47,3 +47,30 @@ def test_umma_selftest(N, K, a_mn, b_mn, a_sw, b_sw, a_tmem):
     err = (D - ref).norm() / ref.norm()
     assert torch.isfinite(D).all()
     assert err < 1e-5, f"rel err {err.item():.3e}"
+
+
+# (N, K, a_mn, b_mn, lane_off): the M = 64 tiles of the tensor-core gated delta rule
+CASES64 = [(64, 64, 0, 0, 0), (64, 64, 0, 0, 16), (64, 64, 1, 0, 0), (64, 64, 0, 1, 16), (64, 64, 1, 1, 0),
+           (128, 64, 0, 0, 16), (64, 128, 0, 1, 0)]
+
+
+@pytest.mark.parametrize("N,K,a_mn,b_mn,lane_off", CASES64)
+def test_umma_selftest_m64(N, K, a_mn, b_mn, lane_off):
+    from linatt_b200 import _lib
+
+    L = _lib.lib()
+    M = 64
+    g = torch.Generator(device="cuda").manual_seed(N * 7 + K + lane_off)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    As = A.t().contiguous() if a_mn else A.contiguous()
+    Bs = B.t().contiguous() if b_mn else B.contiguous()
+    D = torch.full((M, N), float("nan"), device="cuda")
+    rc = L.kata_selftest_umma_m64(As.data_ptr(), Bs.data_ptr(), D.data_ptr(), N, K, a_mn, b_mn, lane_off,
+                                  torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "kata_selftest_umma_m64")
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().t()
+    assert torch.isfinite(D).all()
+    err = (D - ref).norm() / ref.norm()
+    assert err < 1e-5, f"rel err {err.item():.3e}"
