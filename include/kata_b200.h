@@ -264,6 +264,8 @@ typedef struct {
   int B, T, H, HV, K, V;
   int N, num_chunks;
   float scale;               /* fla default K^-0.5 */
+  int algo;                  /* KATA_ALGO_*: AUTO = tcgen05 kernels for bf16/f16 inputs, fp32-exact CUDA-core
+                                kernels for fp32 inputs; TC / SIMT force one (TC needs 16-bit inputs) */
 } kata_gdn_fwd_args;
 
 KATA_API size_t kata_gdn_fwd_workspace_bytes(const kata_gdn_fwd_args* args);
@@ -299,6 +301,8 @@ typedef struct {
   int B, T, H, HV, K, V;
   int N, num_chunks;
   float scale;
+  int algo;                  /* KATA_ALGO_*, as in the forward; the backward must use the forward's family
+                                when fwd_workspace is given (the two families lay the workspace out differently) */
 } kata_gdn_bwd_args;
 
 KATA_API size_t kata_gdn_bwd_workspace_bytes(const kata_gdn_bwd_args* args);
@@ -376,7 +380,7 @@ KATA_API const char* kata_strerror(int code);
 
 /* ABI revision of this header; bumped on any incompatible change. */
 KATA_API int kata_abi_version(void);
-#define KATA_ABI_VERSION 1
+#define KATA_ABI_VERSION 2
 
 /* Diagnostic: D(M x N, fp32, row-major) = A * B^T through one CTA of TMA loads and tcgen05 MMAs.
  * A is (M x K) bf16, stored K-contiguous when a_mn == 0 or as (K x M) M-contiguous when a_mn == 1;

@@ -22,7 +22,7 @@ KATA_OK = 0
 DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 ALGO = {"auto": 0, "tc": 1, "simt": 2}
 SCORE = {"concat": 0, "sum": 1}
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int
@@ -85,7 +85,7 @@ class GdnFwdArgs(ctypes.Structure):
         ("o", c_void_p), ("ht", c_void_p), ("A", c_void_p), ("cu_seqlens", c_void_p), ("chunk_offsets", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HV", c_int), ("K", c_int), ("V", c_int),
-        ("N", c_int), ("num_chunks", c_int), ("scale", c_float),
+        ("N", c_int), ("num_chunks", c_int), ("scale", c_float), ("algo", c_int),
     ]
 
 
@@ -97,7 +97,7 @@ class GdnBwdArgs(ctypes.Structure):
         ("cu_seqlens", c_void_p), ("chunk_offsets", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("fwd_workspace", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HV", c_int), ("K", c_int), ("V", c_int),
-        ("N", c_int), ("num_chunks", c_int), ("scale", c_float),
+        ("N", c_int), ("num_chunks", c_int), ("scale", c_float), ("algo", c_int),
     ]
 
 

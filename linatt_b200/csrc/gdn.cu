@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include "attn_common.cuh"
+#include "gdn_tc.h"
 #include "host_util.h"
 #include "kata_b200.h"
 
@@ -1011,6 +1012,14 @@ void bind_ws(GdnParams& p, void* ws, const WsLayout& w, bool bwd, void* fwd_ws =
   }
 }
 
+// Kernel family: 1 = tensor cores (16-bit inputs), 2 = fp32-exact CUDA cores, or a negative error.
+int gdn_family(int algo, int dtype) {
+  if (algo == KATA_ALGO_TC) return dtype == KATA_DTYPE_F32 ? KATA_ERR_UNSUPPORTED : 1;
+  if (algo == KATA_ALGO_SIMT) return 2;
+  if (algo != KATA_ALGO_AUTO) return KATA_ERR_INVALID;
+  return dtype == KATA_DTYPE_F32 ? 2 : 1;
+}
+
 }  // namespace
 }  // namespace kata
 
@@ -1018,6 +1027,7 @@ using namespace kata;
 
 extern "C" size_t kata_gdn_fwd_workspace_bytes(const kata_gdn_fwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->HV < 1 || a->num_chunks < 1) return 0;
+  if (gdn_family(a->algo, a->dtype) == 1) return gdn_tc_fwd_workspace_bytes(a->B, a->T, a->HV, a->num_chunks);
   return ws_layout(a->B, a->T, a->HV, a->num_chunks, false).total;
 }
 
@@ -1027,6 +1037,9 @@ extern "C" int kata_gdn_fwd(const kata_gdn_fwd_args* a, kata_stream_t stream) {
                      a->chunk_offsets);
   if (e) return e;
   if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->o || !a->A) return KATA_ERR_INVALID;
+  const int fam = gdn_family(a->algo, a->dtype);
+  if (fam < 0) return fam;
+  if (fam == 1) return gdn_tc_fwd(a, reinterpret_cast<cudaStream_t>(stream));
   const WsLayout w = ws_layout(a->B, a->T, a->HV, a->num_chunks, false);
   if (!a->workspace || a->workspace_bytes < w.total) return KATA_ERR_WORKSPACE;
   GdnParams p{};
@@ -1055,6 +1068,8 @@ extern "C" int kata_gdn_fwd(const kata_gdn_fwd_args* a, kata_stream_t stream) {
 
 extern "C" size_t kata_gdn_bwd_workspace_bytes(const kata_gdn_bwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->HV < 1 || a->num_chunks < 1) return 0;
+  if (gdn_family(a->algo, a->dtype) == 1)
+    return gdn_tc_bwd_workspace_bytes(a->B, a->T, a->HV, a->num_chunks, a->fwd_workspace != nullptr);
   return ws_layout(a->B, a->T, a->HV, a->num_chunks, true, a->fwd_workspace != nullptr).total;
 }
 
@@ -1066,6 +1081,9 @@ extern "C" int kata_gdn_bwd(const kata_gdn_bwd_args* a, kata_stream_t stream) {
   if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->A || !a->dout || !a->dq || !a->dk || !a->dv || !a->dg ||
       !a->dbeta)
     return KATA_ERR_INVALID;
+  const int fam = gdn_family(a->algo, a->dtype);
+  if (fam < 0) return fam;
+  if (fam == 1) return gdn_tc_bwd(a, reinterpret_cast<cudaStream_t>(stream));
   const bool reuse = a->fwd_workspace != nullptr;
   const WsLayout w = ws_layout(a->B, a->T, a->HV, a->num_chunks, true, reuse);
   if (!a->workspace || a->workspace_bytes < w.total) return KATA_ERR_WORKSPACE;

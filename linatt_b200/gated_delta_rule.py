@@ -30,6 +30,10 @@ __all__ = ["chunk_gated_delta_rule", "chunk_gdn", "ChunkGatedDeltaRuleFunction",
 
 CHUNK = 64
 
+# Kernel family of every call ("auto" | "tc" | "simt"): auto runs the tcgen05 kernels for bf16 / fp16
+# inputs and the fp32-exact CUDA-core kernels for fp32 inputs.  Tests switch it to run one family.
+ALGO = "auto"
+
 
 def _dtype(*ts):
     dt = ts[0].dtype
@@ -87,7 +91,7 @@ def _fwd(q, k, v, g, beta, scale, h0, want_final, tables):
         q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), g=g.data_ptr(), beta=beta.data_ptr(), h0=_lib.ptr(h0),
         o=o.data_ptr(), ht=_lib.ptr(ht), A=A.data_ptr(), cu_seqlens=_lib.ptr(cu), chunk_offsets=_lib.ptr(co),
         workspace=None, workspace_bytes=0, dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HV=HV, K=K, V=V, N=N,
-        num_chunks=NC, scale=float(scale))
+        num_chunks=NC, scale=float(scale), algo=_lib.ALGO[ALGO])
     L = _lib.lib()
     ws = torch.empty(int(L.kata_gdn_fwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -124,7 +128,8 @@ def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=None):
         A=A.data_ptr(), dout=do.data_ptr(), dht=_lib.ptr(dht), dq=dq.data_ptr(), dk=dk.data_ptr(),
         dv=dv.data_ptr(), dg=dg.data_ptr(), dbeta=db.data_ptr(), dh0=_lib.ptr(dh0), cu_seqlens=_lib.ptr(cu),
         chunk_offsets=_lib.ptr(co), workspace=None, workspace_bytes=0, fwd_workspace=_lib.ptr(fwd_ws),
-        dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HV=HV, K=K, V=V, N=N, num_chunks=NC, scale=float(scale))
+        dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HV=HV, K=K, V=V, N=N, num_chunks=NC, scale=float(scale),
+        algo=_lib.ALGO[ALGO])
     L = _lib.lib()
     ws = torch.empty(int(L.kata_gdn_bwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
