@@ -607,7 +607,7 @@ def run_gdn(args, rank: int, world: int, local: int) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     from linatt_b200.gated_delta_rule import chunk_gated_delta_rule
 
-    Bg, Tg, Hg, Kg = 8, 2048, 12, 64
+    Bg, Tg, Hg, Kg = args.gdn_batch, 2048, 12, 64
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     sets = []
     for _ in range(4):
@@ -794,6 +794,8 @@ def main() -> None:
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
                          "delta: the SPD delta rule at the mixer geometry; decode: one-token generation "
                          "steps on the recurrent feature state")
+    ap.add_argument("--gdn-batch", type=int, default=8,
+                    help="B per GPU of --workload gdn (config 2 is quoted at 8; smaller only for profiler captures)")
     ap.add_argument("--batch", type=int, default=16,
                     help="B per GPU (the metric is quoted at 16; smaller values only for profiler captures)")
     args = ap.parse_args()

@@ -17,17 +17,11 @@ Inputs follow the layer (kata/layer.py:399-418): q, k, v, beta cast to bf16, T a
 q, k L2-normalised per head, beta = sigmoid(N(0,1)); dO ~ N(0,1) fp32.  Every tensor is stored as
 float32 (bf16 values are exact in it) in ``tests/golden/delta_golden_gpu.npz``.
 
-``--what spd`` adds the head-major O(T) siblings of the same package, each run by the reference's
-own Triton kernels on the same kind of inputs (bf16, head-major (B, H, T, D)), into
-``tests/golden/spd_golden_gpu.npz``:
-
-  * spd_state_lin   (kata/spd/chunk_state_lin.py:507-510): o and dq, dk, dv (its forward kernel
-    launched through its JIT function, since its autotuner names a missing argument, then its own
-    backward kernels)
-  * spd_chunk_scan  (kata/spd/chunk_scan.py:295-406, sum mode): o, den
-  * flash_delta_state (kata/spd/chunk_state_v2.py:385-387): o and dq, dk, dv, dbeta (its forward
-    kernel launched without the H argument its launcher wrongly passes, then its own backward
-    spd_delta_state_bwd, :770-813)
+``--what spd`` adds the head-major sibling ``spd_chunk_scan`` (kata/spd/chunk_scan.py:295-406, sum
+mode: o, den), run by the reference's own Triton kernels on the same kind of inputs (bf16,
+head-major (B, H, T, D)), into ``tests/golden/spd_golden_gpu.npz``.  ``spd_state_lin``
+(chunk_state_lin.py) and ``flash_delta_state`` (chunk_state_v2.py) have launch helpers here as well
+(each works around a launcher bug at HEAD), but their kernels do not fit on a B200 (see SPD_CASES).
 
 The reference checkout is given on the command line and is imported by file path; it is not part
 of this repository.
@@ -57,14 +51,14 @@ CASES = [
 
 
 # (name, function, B, H, T, D, Dv, M, scale)
+# spd_state_lin's and flash_delta_state's own Triton kernels do not fit on a B200: compiled for
+# sm_100 they ask for 608-736 of the SM's 512 tensor-memory columns and Triton refuses to launch
+# them (OutOfResources).  Their functions are pinned through flash_delta instead (the readout
+# numerator tril(kappa(q,k)) U, and the raw-numerator delta rule); the launch helpers below are kept
+# for a GPU where they fit.
 SPD_CASES = [
-    ("lin_m4", "state_lin", 1, 2, 256, 64, 64, 4, 0.5),
-    ("lin_m2_default_scale", "state_lin", 2, 1, 128, 32, 32, 2, None),
     ("scan_m4", "chunk_scan", 1, 2, 256, 64, 64, 4, 0.5),
     ("scan_m2_default_scale", "chunk_scan", 2, 1, 128, 32, 32, 2, None),
-    # flash_delta_state's own Triton kernel does not fit on a B200 (it asks for 608-736 of the 512
-    # tensor-memory columns); its function is the raw-numerator delta rule, pinned through flash_delta
-    ("state_m4", "delta_state", 1, 2, 256, 64, 64, 4, 0.5),
 ]
 
 
@@ -112,8 +106,9 @@ def state_lin_reference(m, q, k, v, do, M, scale):
     """spd_state_lin forward and backward.  Its forward kernel's autotuner names a reset_to_zero
     argument "S" that the kernel does not have (kata/spd/chunk_state_lin.py:22-23 vs :26-33), so at
     HEAD _StateLin.forward raises KeyError; the forward kernel is launched here through its JIT
-    function with one of its own configs (num_warps=4, num_stages=1) on a zeroed state, and the
-    backward kernels exactly as _StateLin.backward launches them (:437-504)."""
+    function with one of its own configs (num_warps=4, num_stages=1) on a zeroed state.  Its
+    backward launcher passes H= to both backward kernels, whose signatures have no H (:465-484 vs
+    :166-184, :308-325), so they are launched with _StateLin.backward's other arguments."""
     B, H, T, D = q.shape
     DV = v.shape[-1]
     E, E2, BI = m._lin_params(D, M, None)
@@ -129,10 +124,8 @@ def state_lin_reference(m, q, k, v, do, M, scale):
     dq, dk1, dv1, dk2, dv2 = (torch.empty_like(x) for x in (q, k, v, k, v))
     Hst = torch.zeros(B * H, E2, DV, **f32)
     Rst = torch.zeros(B * H, E2, DV, **f32)
-    m._lin_bwd_p1_kernel[(B * H,)](q, k, v, do, dq, dk1, dv1, Hst, ss, T, H=H, D=D, E=E, M=M, DV=DV, C=64, E2=E2,
-                                   BI=BI)
-    m._lin_bwd_p2_kernel[(B * H,)](q, k, v, do, dk2, dv2, Rst, ss, T, H=H, D=D, E=E, M=M, DV=DV, C=64, E2=E2,
-                                   BI=BI)
+    m._lin_bwd_p1_kernel[(B * H,)](q, k, v, do, dq, dk1, dv1, Hst, ss, T, D=D, E=E, M=M, DV=DV, C=64, E2=E2, BI=BI)
+    m._lin_bwd_p2_kernel[(B * H,)](q, k, v, do, dk2, dv2, Rst, ss, T, D=D, E=E, M=M, DV=DV, C=64, E2=E2, BI=BI)
     return o, dq, dk1 + dk2, dv1 + dv2
 
 
