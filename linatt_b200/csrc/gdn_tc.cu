@@ -460,17 +460,82 @@ __global__ void __launch_bounds__(128) gdn_tc_prep_kernel(Params p, int items) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// state: sequential over the chunks of one sequence; CTA = one (sequence, value head).
+// Column-split scans.  A sequential chunk scan is latency-bound: every chunk is two dependent MMA
+// round trips plus a row-wise update.  So a CTA takes one half of the 64 value columns (the two
+// halves of a head are independent), each MMA is issued twice, into TMEM lane offsets 0 and 16 of
+// the same columns, and thread (warp w, lane l) handles row 16w + (l & 15) and the 16 value columns
+// vh * 32 + 16 * (l >> 4) .. +16: every lane works, on a quarter of a row.  The B-operand tiles that
+// the threads write (state, u~, ...) carry only the CTA's 32 columns; the other columns stay zero and
+// their MMA outputs are never read.
+// ------------------------------------------------------------------------------------------------
+// tcgen05.ld / st take one TMEM address for the whole warp, so a lane half cannot name its own
+// columns: the warp loads the CTA's 32 columns and each lane half keeps its 16 (h = lane >> 4).
+__device__ __forceinline__ void ld_quarter(uint32_t taddr, int h, float (&x)[16]) {
+  uint32_t a[32];
+  tmem_ld32(taddr, a);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(h ? a[16 + j] : a[j]);
+}
+// 16 values into row r, columns [c0, c0 + 16) of a tile (c0 a multiple of 8).
+template <typename T>
+__device__ __forceinline__ void st_row16(uint8_t* tile, int r, int c0, const float (&x)[16]) {
+  const uint32_t base = smem_u32(tile);
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+    st_shared_v4(base + toff(r, c0 + 8 * c), pack2<T>(x[8 * c], x[8 * c + 1]), pack2<T>(x[8 * c + 2], x[8 * c + 3]),
+                 pack2<T>(x[8 * c + 4], x[8 * c + 5]), pack2<T>(x[8 * c + 6], x[8 * c + 7]));
+}
+template <typename T>
+__device__ __forceinline__ void ld_row16(const uint8_t* tile, int r, int c0, float (&x)[16]) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const uint4 u4 = *reinterpret_cast<const uint4*>(tile + toff(r, c0 + 8 * c));
+    const T* e = reinterpret_cast<const T*>(&u4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[8 * c + j] = to_f32<T>(e[j]);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st_g16x16(void* dst, const float (&x)[16]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+    d[c] = make_uint4(pack2<T>(x[8 * c], x[8 * c + 1]), pack2<T>(x[8 * c + 2], x[8 * c + 3]),
+                      pack2<T>(x[8 * c + 4], x[8 * c + 5]), pack2<T>(x[8 * c + 6], x[8 * c + 7]));
+}
+// 64 rows x 32 fp32 columns [c0, c0 + 32) of a (tokens, heads, 64) tensor into a dense [64][32] array.
+__device__ __forceinline__ void cpa_f32_half(float* dst, const float* base, int heads, int h, int c0, int t0, int len) {
+  const uint32_t d = smem_u32(dst);
+  for (int idx = threadIdx.x; idx < 512; idx += blockDim.x) {
+    const int r = idx >> 3, c = idx & 7;
+    const int rr = r < len ? r : 0;
+    cp_async16(d + (r * 32 + 4 * c) * 4, base + (static_cast<size_t>(t0 + rr) * heads + h) * 64 + c0 + 4 * c, r < len);
+  }
+}
+__device__ __forceinline__ void zero_tile(uint8_t* tile) {
+  const uint32_t base = smem_u32(tile);
+  for (int i = threadIdx.x; i < static_cast<int>(TB / 16); i += blockDim.x) st_shared_v4(base + 16 * i, 0u, 0u, 0u, 0u);
+}
+// The same MMA into lane offsets 0 and 16 (both lane halves of every warp receive all 64 rows).
+template <bool BF, bool AMN, bool BMN>
+__device__ __forceinline__ void mma64x2(uint32_t d, const void* a, const void* b, bool acc) {
+  mma64<BF, AMN, BMN>(d, a, b, acc);
+  mma64<BF, AMN, BMN>(d + (16u << 16), a, b, acc);
+}
+
+// ------------------------------------------------------------------------------------------------
+// state: sequential over the chunks of one sequence; CTA = (sequence, value head, value half).
 //   hS[c] = S (16-bit);  u = U0 - W S;  S <- e^{gamma_C} S + K^T diag(e^{gamma_C - gamma}) u
-// The fp32 state lives in registers: thread (warp w, lane l < 16) owns key row 16w + l.  The next
-// chunk's W, k, U0 and gamma stream into the other half of a double buffer (cp.async).
+// The fp32 state lives in registers (16 values per thread).  The next chunk's W, k, U0 and gamma
+// stream into the other half of a double buffer (cp.async).
 // ------------------------------------------------------------------------------------------------
 struct StateSmem {
   uint8_t tW[2][TB];
   uint8_t tK[2][TB];
-  uint8_t tS[TB];  // state, [key][value]
+  uint8_t tS[TB];  // state, [key][value] (this CTA's 32 columns)
   uint8_t tU[TB];  // e^{gamma_C - gamma} u, [token][value]
-  float U0[2][CH * CH];
+  float U0[2][CH * 32];
   float gam[2][CH];
   uint64_t bar;
   uint32_t tmem;
@@ -483,14 +548,15 @@ __global__ void __launch_bounds__(128) gdn_tc_state_kernel(Params p) {
   StateSmem& sm = *reinterpret_cast<StateSmem*>(align1k(smraw));
   constexpr bool BF = is_bf16<T>();
   const int tid = threadIdx.x, ln = tid & 31;
-  const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV, hq = hv / (p.HV / p.H);
+  const int vh = blockIdx.x & 1, nh = blockIdx.x >> 1;
+  const int n = nh / p.HV, hv = nh % p.HV, hq = hv / (p.HV / p.H);
   int bos, eos, c0, nc;
   seq_range(p, n, bos, eos, c0, nc);
   auto issue = [&](int j, int b) {
     const int t0 = bos + j * CH, len = min(CH, eos - t0);
     cpa_tile(sm.tW[b], p.W, p.HV, hv, t0, len);
     cpa_tile(sm.tK[b], p.k, p.H, hq, t0, len);
-    cpa_f32(sm.U0[b], p.U0, p.HV, hv, t0, len);
+    cpa_f32_half(sm.U0[b], p.U0, p.HV, hv, 32 * vh, t0, len);
     cpa_vec(sm.gam[b], p.gam, p.HV, hv, t0, len);
     cp_async_commit();
   };
@@ -504,15 +570,18 @@ __global__ void __launch_bounds__(128) gdn_tc_state_kernel(Params p) {
     tmem_relinquish();
   }
   if (nc > 0) issue(0, 0);
+  zero_tile(sm.tS);
+  zero_tile(sm.tU);
+  __syncthreads();
   const RowMap rm = rowmap();
-  const bool owner = ln < 16;  // lanes 16-31 hold no row of a single-tile accumulator
   const int m = rm.row;
-  float S[64];
+  const int vc = 32 * vh + 16 * (ln >> 4);  // this thread's first value column
+  float S[16];
   {
-    const float* h0 = p.h0 ? p.h0 + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64 : nullptr;
+    const float* h0 = p.h0 ? p.h0 + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64 + vc : nullptr;
 #pragma unroll
-    for (int c = 0; c < 64; ++c) S[c] = h0 ? h0[c] : 0.f;
-    if (owner) st_row<T>(sm.tS, m, S);
+    for (int c = 0; c < 16; ++c) S[c] = h0 ? h0[c] : 0.f;
+    st_row16<T>(sm.tS, m, vc, S);
   }
   tc_fence_before();
   __syncthreads();
@@ -528,52 +597,55 @@ __global__ void __launch_bounds__(128) gdn_tc_state_kernel(Params p) {
     } else {
       cp_async_wait<0>();
     }
-    if (owner) st_g16<T>(static_cast<T*>(p.hS) + ((static_cast<size_t>(gc) * p.HV + hv) * 64 + m) * 64, S);
+    st_g16x16<T>(static_cast<T*>(p.hS) + ((static_cast<size_t>(gc) * p.HV + hv) * 64 + m) * 64 + vc, S);
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, false, true>(tbase, sm.tW[b], sm.tS, false);  // W S
+      mma64x2<BF, false, true>(tbase, sm.tW[b], sm.tS, false);  // W S
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     const float gC = sm.gam[b][len - 1];
     {
-      float x[64];
-      ld64(tbase + rm.lane, x);
+      float x[16];
+      ld_quarter(tbase + rm.lane + 32 * vh, ln >> 4, x);
       const int r = m;
-      if (owner) {
-        const bool in = r < len;
-        const float f = in ? __expf(gC - sm.gam[b][r]) : 0.f;
+      const bool in = r < len;
+      const float f = in ? __expf(gC - sm.gam[b][r]) : 0.f;
+      const float* u0 = sm.U0[b] + r * 32 + (vc - 32 * vh);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = sm.U0[b][r * 64 + c] - x[c];
-        if (in) st_g16<T>(static_cast<T*>(p.u) + (static_cast<size_t>(t0 + r) * p.HV + hv) * 64, x);
+      for (int c = 0; c < 16; ++c) x[c] = u0[c] - x[c];
+      if (in) st_g16x16<T>(static_cast<T*>(p.u) + (static_cast<size_t>(t0 + r) * p.HV + hv) * 64 + vc, x);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] *= f;
-        st_row<T>(sm.tU, r, x);
-      }
+      for (int c = 0; c < 16; ++c) x[c] *= f;
+      st_row16<T>(sm.tU, r, vc, x);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, true, true>(tbase + 64, sm.tK[b], sm.tU, false);  // K^T u~
+      mma64x2<BF, true, true>(tbase + 64, sm.tK[b], sm.tU, false);  // K^T u~
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
-      float x[64];
-      ld64(tbase + rm.lane + 64, x);
+      float x[16];
+      ld_quarter(tbase + rm.lane + 64 + 32 * vh, ln >> 4, x);
       const float eC = __expf(gC);
 #pragma unroll
-      for (int c = 0; c < 64; ++c) S[c] = fmaf(eC, S[c], x[c]);
-      if (owner) st_row<T>(sm.tS, m, S);
+      for (int c = 0; c < 16; ++c) S[c] = fmaf(eC, S[c], x[c]);
+      st_row16<T>(sm.tS, m, vc, S);
     }
     tc_fence_before();
     __syncthreads();
   }
-  if (ok && p.ht && owner) st_g32(p.ht + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64, S);
+  if (ok && p.ht) {
+    float* d = p.ht + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64 + vc;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) d[c] = S[c];
+  }
   cp_async_wait<0>();
   if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
   tc_fence_before();
@@ -780,7 +852,7 @@ __global__ void __launch_bounds__(128) gdn_tc_dvl_kernel(Params p, int items) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// backward 1: reverse scan of dS; CTA = one (sequence, value head).
+// backward 1: reverse scan of dS; CTA = (sequence, value head, value half), column split as above.
 //   hD[c] = dS (16-bit);  du = dvl + e^{gamma_C - gamma} (K dS);
 //   dS <- e^{gamma_C} dS + q^T diag(scale e^gamma) dO - W^T du;  dh0 = dS after the first chunk.
 // ------------------------------------------------------------------------------------------------
@@ -789,10 +861,10 @@ struct DstateSmem {
   uint8_t tK[2][TB];
   uint8_t tQ[2][TB];
   uint8_t tO[2][TB];
-  uint8_t tDS[TB];   // dS, [key][value]
+  uint8_t tDS[TB];   // dS, [key][value] (this CTA's 32 columns)
   uint8_t tOs[TB];   // scale e^gamma dO, [token][value]
   uint8_t tDU[TB];   // -du, [token][value]
-  float dvl[2][CH * CH];
+  float dvl[2][CH * 32];
   float gam[2][CH];
   uint64_t bar;
   uint32_t tmem;
@@ -805,7 +877,8 @@ __global__ void __launch_bounds__(128) gdn_tc_dstate_kernel(Params p) {
   DstateSmem& sm = *reinterpret_cast<DstateSmem*>(align1k(smraw));
   constexpr bool BF = is_bf16<T>();
   const int tid = threadIdx.x, ln = tid & 31;
-  const int n = blockIdx.x / p.HV, hv = blockIdx.x % p.HV, hq = hv / (p.HV / p.H);
+  const int vh = blockIdx.x & 1, nh = blockIdx.x >> 1;
+  const int n = nh / p.HV, hv = nh % p.HV, hq = hv / (p.HV / p.H);
   int bos, eos, c0, nc;
   seq_range(p, n, bos, eos, c0, nc);
   auto issue = [&](int j, int b) {
@@ -814,7 +887,7 @@ __global__ void __launch_bounds__(128) gdn_tc_dstate_kernel(Params p) {
     cpa_tile(sm.tK[b], p.k, p.H, hq, t0, len);
     cpa_tile(sm.tQ[b], p.q, p.H, hq, t0, len);
     cpa_tile(sm.tO[b], p.dout, p.HV, hv, t0, len);
-    cpa_f32(sm.dvl[b], p.dvl, p.HV, hv, t0, len);
+    cpa_f32_half(sm.dvl[b], p.dvl, p.HV, hv, 32 * vh, t0, len);
     cpa_vec(sm.gam[b], p.gam, p.HV, hv, t0, len);
     cp_async_commit();
   };
@@ -828,15 +901,19 @@ __global__ void __launch_bounds__(128) gdn_tc_dstate_kernel(Params p) {
     tmem_relinquish();
   }
   if (nc > 0) issue(nc - 1, 0);
+  zero_tile(sm.tDS);
+  zero_tile(sm.tOs);
+  zero_tile(sm.tDU);
+  __syncthreads();
   const RowMap rm = rowmap();
-  const bool owner = ln < 16;
   const int m = rm.row;
-  float dS[64];
+  const int vc = 32 * vh + 16 * (ln >> 4);
+  float dS[16];
   {
-    const float* d0 = p.dht ? p.dht + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64 : nullptr;
+    const float* d0 = p.dht ? p.dht + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64 + vc : nullptr;
 #pragma unroll
-    for (int c = 0; c < 64; ++c) dS[c] = d0 ? d0[c] : 0.f;
-    if (owner) st_row<T>(sm.tDS, m, dS);
+    for (int c = 0; c < 16; ++c) dS[c] = d0 ? d0[c] : 0.f;
+    st_row16<T>(sm.tDS, m, vc, dS);
   }
   tc_fence_before();
   __syncthreads();
@@ -852,63 +929,66 @@ __global__ void __launch_bounds__(128) gdn_tc_dstate_kernel(Params p) {
     } else {
       cp_async_wait<0>();
     }
-    if (owner) st_g16<T>(static_cast<T*>(p.hD) + ((static_cast<size_t>(gc) * p.HV + hv) * 64 + m) * 64, dS);
+    st_g16x16<T>(static_cast<T*>(p.hD) + ((static_cast<size_t>(gc) * p.HV + hv) * 64 + m) * 64 + vc, dS);
     __syncthreads();  // the chunk's tiles (cp.async) are complete in every thread's view
-    if (owner) {  // dO rows scaled by scale e^gamma
+    {  // dO rows scaled by scale e^gamma (this thread's 16 columns)
       const int r = m;
-      float x[64];
-      ld_row<T>(sm.tO[b], r, x);
+      float x[16];
+      ld_row16<T>(sm.tO[b], r, vc, x);
       const float f = r < len ? p.scale * __expf(sm.gam[b][r]) : 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) x[c] *= f;
-      st_row<T>(sm.tOs, r, x);
+      for (int c = 0; c < 16; ++c) x[c] *= f;
+      st_row16<T>(sm.tOs, r, vc, x);
     }
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, false, true>(tbase, sm.tK[b], sm.tDS, false);       // K dS
-      mma64<BF, true, true>(tbase + 64, sm.tQ[b], sm.tOs, false);   // q^T dO~
+      mma64x2<BF, false, true>(tbase, sm.tK[b], sm.tDS, false);      // K dS
+      mma64x2<BF, true, true>(tbase + 64, sm.tQ[b], sm.tOs, false);  // q^T dO~
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     const float gC = sm.gam[b][len - 1];
     {
-      float x[64];
-      ld64(tbase + rm.lane, x);
+      float x[16];
+      ld_quarter(tbase + rm.lane + 32 * vh, ln >> 4, x);
       const int r = m;
-      if (owner) {
-        const bool in = r < len;
-        const float f = in ? __expf(gC - sm.gam[b][r]) : 0.f;
+      const bool in = r < len;
+      const float f = in ? __expf(gC - sm.gam[b][r]) : 0.f;
+      const float* dv = sm.dvl[b] + r * 32 + (vc - 32 * vh);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = in ? fmaf(f, x[c], sm.dvl[b][r * 64 + c]) : 0.f;
-        if (in) st_g16<T>(static_cast<T*>(p.du) + (static_cast<size_t>(t0 + r) * p.HV + hv) * 64, x);
+      for (int c = 0; c < 16; ++c) x[c] = in ? fmaf(f, x[c], dv[c]) : 0.f;
+      if (in) st_g16x16<T>(static_cast<T*>(p.du) + (static_cast<size_t>(t0 + r) * p.HV + hv) * 64 + vc, x);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = -x[c];
-        st_row<T>(sm.tDU, r, x);
-      }
+      for (int c = 0; c < 16; ++c) x[c] = -x[c];
+      st_row16<T>(sm.tDU, r, vc, x);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, true, true>(tbase + 64, sm.tW[b], sm.tDU, true);  // - W^T du
+      mma64x2<BF, true, true>(tbase + 64, sm.tW[b], sm.tDU, true);  // - W^T du
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
-      float x[64];
-      ld64(tbase + rm.lane + 64, x);
+      float x[16];
+      ld_quarter(tbase + rm.lane + 64 + 32 * vh, ln >> 4, x);
       const float eC = __expf(gC);
 #pragma unroll
-      for (int c = 0; c < 64; ++c) dS[c] = fmaf(eC, dS[c], x[c]);
-      if (owner) st_row<T>(sm.tDS, m, dS);
+      for (int c = 0; c < 16; ++c) dS[c] = fmaf(eC, dS[c], x[c]);
+      st_row16<T>(sm.tDS, m, vc, dS);
     }
     tc_fence_before();
     __syncthreads();
   }
-  if (ok && p.dh0 && owner) st_g32(p.dh0 + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64, dS);
+  if (ok && p.dh0) {
+    float* d = p.dh0 + ((static_cast<size_t>(n) * p.HV + hv) * 64 + m) * 64 + vc;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) d[c] = dS[c];
+  }
   cp_async_wait<0>();
   if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
   tc_fence_before();
@@ -917,20 +997,58 @@ __global__ void __launch_bounds__(128) gdn_tc_dstate_kernel(Params p) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// backward 2: per-chunk dq, dk, dv, dbeta, dg.  One chunk per CTA, 128 threads; rows of the M = 64
-// accumulators are handled by lanes 0-15 of the four warps.  TMEM columns (64 each):
-//   A0 du S0^T -> Y_K,  A1 K K^T,  A2 Q K^T,  A3 dO u^T,  A4 dq,  A5 dk,  A6 Tm^T du -> dL'.
+// backward 2: per-chunk dq, dk, dv, dbeta, dg.  One chunk per CTA, 128 threads.  Every MMA is issued
+// into both TMEM lane halves (mma64x2), and thread (warp w, lane l) handles row 16w + (l & 15),
+// columns 32 * (l >> 4) .. +32; row sums are combined across the two halves at the end.  TMEM
+// columns (64 each): A0 du S0^T -> Y_K, A1 K K^T, A2 Q K^T, A3 dO u^T, A4 dq, A5 dk, A6 Tm^T du -> dL'.
 // ------------------------------------------------------------------------------------------------
 struct GradSmem {
   uint8_t tQ[TB], tK[TB], tO[TB], tU[TB], tDU[TB], tS0[TB], tHD[TB], tTm[TB], tU0[TB], tW[TB];
   uint8_t tDW[TB];  // dW, later P
   uint8_t tYV[TB], tYK[TB], tM[TB];
-  float F[CH][CH + 1];  // per-row contributions whose column sums enter dgamma_j
+  float F[CH][CH + 1];  // per-element contributions whose column sums enter dgamma_j
   float gam[CH], beta[CH], dgam[CH], red[4];
   uint64_t bar;
   uint32_t tmem;
   int abort;
 };
+
+// Columns [32h, 32h + 32) of this thread's TMEM lane (h = lane half).  tcgen05.ld / st take one
+// address per warp, so the warp loads both halves and each lane keeps its own; a store writes the
+// thread's 32 values into both halves of its lane (the half a lane does not own is never read).
+__device__ __forceinline__ void ld_half(uint32_t taddr, int h, float (&x)[32]) {
+  uint32_t a[32], b[32];
+  tmem_ld32(taddr, a);
+  tmem_ld32(taddr + 32, b);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(h ? b[j] : a[j]);
+}
+__device__ __forceinline__ void st_half(uint32_t taddr, const float (&x)[32]) {
+  uint32_t a[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) a[j] = __float_as_uint(x[j]);
+  tmem_st32(taddr, a);
+  tmem_st32(taddr + 32, a);
+}
+template <typename T>
+__device__ __forceinline__ void st_row32(uint8_t* tile, int r, int c0, const float (&x)[32]) {
+  const uint32_t base = smem_u32(tile);
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    st_shared_v4(base + toff(r, c0 + 8 * c), pack2<T>(x[8 * c], x[8 * c + 1]), pack2<T>(x[8 * c + 2], x[8 * c + 3]),
+                 pack2<T>(x[8 * c + 4], x[8 * c + 5]), pack2<T>(x[8 * c + 6], x[8 * c + 7]));
+}
+template <typename T>
+__device__ __forceinline__ void ld_row32(const uint8_t* tile, int r, int c0, float (&x)[32]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 u4 = *reinterpret_cast<const uint4*>(tile + toff(r, c0 + 8 * c));
+    const T* e = reinterpret_cast<const T*>(&u4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[8 * c + j] = to_f32<T>(e[j]);
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
@@ -985,87 +1103,99 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
   uint32_t phase = 0;
   bool ok = true;
   const RowMap rm = rowmap();
-  const bool owner = ln < 16;
-  const int r = rm.row;
+  const int r = rm.row, hh = ln >> 4, ch = 32 * hh;  // this thread's row, lane half and first column
+  const bool lead = ln < 16;                  // one of the two threads of a row writes per-row values
   const float gC = sm.gam[CH - 1], gr = sm.gam[r], br = sm.beta[r], egr = __expf(gr);
-  float dgr = 0.f, dbr = 0.f, tot = 0.f;
+  float dgr = 0.f, dbr = 0.f, tot = 0.f;  // this thread's half-row parts
+  const bool in = r < len;
+  const size_t rowv = static_cast<size_t>(cp.bos + (in ? r : 0)) * p.HV + hv;
   do {
     if (tid == 0) {
-      mma64<BF, false, false>(A0, sm.tDU, sm.tS0, false);  // du S0^T  (= -dW)
-      mma64<BF, false, false>(A1, sm.tK, sm.tK, false);    // K K^T
-      mma64<BF, false, false>(A2, sm.tQ, sm.tK, false);    // Q K^T
-      mma64<BF, false, false>(A3, sm.tO, sm.tU, false);    // dO u^T
-      mma64<BF, false, false>(A4, sm.tO, sm.tS0, false);   // dO S0^T
-      mma64<BF, false, false>(A5, sm.tU, sm.tHD, false);   // u dS_end^T
-      mma64<BF, true, true>(A6, sm.tTm, sm.tDU, false);    // Tm^T du  (= Y_V)
+      mma64x2<BF, false, false>(A0, sm.tDU, sm.tS0, false);  // du S0^T  (= -dW)
+      mma64x2<BF, false, false>(A1, sm.tK, sm.tK, false);    // K K^T
+      mma64x2<BF, false, false>(A2, sm.tQ, sm.tK, false);    // Q K^T
+      mma64x2<BF, false, false>(A3, sm.tO, sm.tU, false);    // dO u^T
+      mma64x2<BF, false, false>(A4, sm.tO, sm.tS0, false);   // dO S0^T
+      mma64x2<BF, false, false>(A5, sm.tU, sm.tHD, false);   // u dS_end^T
+      mma64x2<BF, true, true>(A6, sm.tTm, sm.tDU, false);    // Tm^T du  (= Y_V)
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
-    const bool in = r < len;
-    const size_t rowv = static_cast<size_t>(cp.bos + (in ? r : 0)) * p.HV + hv;
     {
-      float x[64];
-      ld64(A0 + rm.lane, x);  // dW = -(du S0^T)
+      float x[32];
+      ld_half(A0 + rm.lane, hh, x);  // dW = -(du S0^T)
 #pragma unroll
-      for (int c = 0; c < 64; ++c) x[c] = -x[c];
-      if (owner) st_row<T>(sm.tDW, r, x);
-      ld64(A6 + rm.lane, x);  // Y_V
-      if (owner) {
-        st_row<T>(sm.tYV, r, x);
-        float vv[64];
-        ld_g16<T>(static_cast<const T*>(p.v) + rowv * 64, vv, in);
-        float s1 = 0.f;
+      for (int c = 0; c < 32; ++c) x[c] = -x[c];
+      st_row32<T>(sm.tDW, r, ch, x);
+      ld_half(A6 + rm.lane, hh, x);  // Y_V
+      st_row32<T>(sm.tYV, r, ch, x);
+      float vv[32];
+      {
+        const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v) + rowv * 64 + ch);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) s1 = fmaf(vv[c], x[c], s1);
-        dbr += s1;
+        for (int c = 0; c < 4; ++c) {
+          const uint4 u4 = in ? s4[c] : make_uint4(0u, 0u, 0u, 0u);
+          const T* e = reinterpret_cast<const T*>(&u4);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] *= br;
-        if (in) st_g32(p.dv + rowv * 64, x);
+          for (int j = 0; j < 8; ++j) vv[8 * c + j] = to_f32<T>(e[j]);
+        }
       }
-    }
-    {
-      float t[64], e[64];
-      ld64(A3 + rm.lane, t);  // dO_r . u_j
-      ld64(A2 + rm.lane, e);  // q_r . k_j
-      float rs = 0.f;
-#pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const float mp = j <= r ? p.scale * __expf(gr - sm.gam[j]) * t[j] : 0.f;
-        t[j] = mp;
-        const float mg = mp * e[j];
-        rs += mg;
-        if (owner) sm.F[r][j] = mg;
-      }
-      dgr += rs;
-      if (owner) st_row<T>(sm.tM, r, t);
-    }
-    {
-      float x[64], qq[64];
-      ld64(A4 + rm.lane, x);  // dO S0^T: dq term scale e^gamma (dO S0^T)
-      ld_row<T>(sm.tQ, r, qq);
       float s1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < 32; ++c) s1 = fmaf(vv[c], x[c], s1);
+      dbr += s1;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) x[c] *= br;
+      if (in) {
+        float4* d = reinterpret_cast<float4*>(p.dv + rowv * 64 + ch);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+      }
+    }
+    {
+      float t[32], e[32];
+      ld_half(A3 + rm.lane, hh, t);  // dO_r . u_j
+      ld_half(A2 + rm.lane, hh, e);  // q_r . k_j
+      float rs = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = ch + jj;
+        const float mp = j <= r ? p.scale * __expf(gr - sm.gam[j]) * t[jj] : 0.f;
+        t[jj] = mp;
+        const float mg = mp * e[jj];
+        rs += mg;
+        sm.F[r][j] = mg;
+      }
+      dgr += rs;
+      st_row32<T>(sm.tM, r, ch, t);
+    }
+    {
+      float x[32], qq[32];
+      ld_half(A4 + rm.lane, hh, x);  // dq term scale e^gamma (dO S0^T)
+      ld_row32<T>(sm.tQ, r, ch, qq);
+      float s1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
         x[c] *= p.scale * egr;
         s1 = fmaf(qq[c], x[c], s1);
       }
       dgr += s1;
-      st64(A4 + rm.lane, x);
+      st_half(A4 + rm.lane, x);
     }
     {
-      float x[64], kk[64];
-      ld64(A5 + rm.lane, x);  // u dS_end^T: dk term e^{gamma_C - gamma} (u dS_end^T)
-      ld_row<T>(sm.tK, r, kk);
+      float x[32], kk[32];
+      ld_half(A5 + rm.lane, hh, x);  // dk term e^{gamma_C - gamma} (u dS_end^T)
+      ld_row32<T>(sm.tK, r, ch, kk);
       const float f = __expf(gC - gr);
       float s1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < 32; ++c) {
         x[c] *= f;
         s1 = fmaf(kk[c], x[c], s1);
       }
       dgr -= s1;
-      tot += owner ? s1 : 0.f;
-      st64(A5 + rm.lane, x);
+      tot += s1;
+      st_half(A5 + rm.lane, x);
     }
     tmem_wait_st();
     fence_proxy_async_smem();
@@ -1073,27 +1203,27 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, true, true>(A0, sm.tTm, sm.tDW, false);  // Y_K = Tm^T dW
-      mma64<BF, false, true>(A4, sm.tM, sm.tK, true);    // dq += M' K
-      mma64<BF, true, true>(A5, sm.tM, sm.tQ, true);     // dk += M'^T Q
+      mma64x2<BF, true, true>(A0, sm.tTm, sm.tDW, false);  // Y_K = Tm^T dW
+      mma64x2<BF, false, true>(A4, sm.tM, sm.tK, true);    // dq += M' K
+      mma64x2<BF, true, true>(A5, sm.tM, sm.tQ, true);     // dk += M'^T Q
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
-      float x[64], kk[64], d[64];
-      ld64(A0 + rm.lane, x);  // Y_K
-      ld64(A5 + rm.lane, d);
-      ld_row<T>(sm.tK, r, kk);
-      if (owner) st_row<T>(sm.tYK, r, x);
+      float x[32], kk[32], d[32];
+      ld_half(A0 + rm.lane, hh, x);  // Y_K
+      ld_half(A5 + rm.lane, hh, d);
+      ld_row32<T>(sm.tK, r, ch, kk);
+      st_row32<T>(sm.tYK, r, ch, x);
       float s1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < 32; ++c) {
         s1 = fmaf(kk[c], x[c], s1);
         d[c] = fmaf(br * egr, x[c], d[c]);
       }
       dbr += egr * s1;
       dgr += br * egr * s1;
-      st64(A5 + rm.lane, d);
+      st_half(A5 + rm.lane, d);
     }
     tmem_wait_st();
     fence_proxy_async_smem();
@@ -1101,69 +1231,77 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, false, false>(A6, sm.tYV, sm.tU0, false);  // Y_V U0^T
-      mma64<BF, false, false>(A6, sm.tYK, sm.tW, true);    // + Y_K W^T  (= -dL)
+      mma64x2<BF, false, false>(A6, sm.tYV, sm.tU0, false);  // Y_V U0^T
+      mma64x2<BF, false, false>(A6, sm.tYK, sm.tW, true);    // + Y_K W^T  (= -dL)
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
-      float t[64], e[64];
-      ld64(A6 + rm.lane, t);
-      ld64(A1 + rm.lane, e);
+      float t[32], e[32];
+      ld_half(A6 + rm.lane, hh, t);
+      ld_half(A1 + rm.lane, hh, e);
       float db = 0.f, dg = 0.f;
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = ch + jj;
         float P = 0.f;
         if (j < r) {
-          const float dl = -t[j];
+          const float dl = -t[jj];
           const float dec = __expf(gr - sm.gam[j]);
-          const float E = dec * e[j];
+          const float E = dec * e[jj];
           db = fmaf(dl, E, db);
           const float G = br * dl * E;
           dg += G;
-          if (owner) sm.F[r][j] += G;
+          sm.F[r][j] += G;
           P = br * dl * dec;
         }
-        t[j] = P;
+        t[jj] = P;
       }
       dbr += db;
       dgr += dg;
-      if (owner) st_row<T>(sm.tDW, r, t);
+      st_row32<T>(sm.tDW, r, ch, t);
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64<BF, false, true>(A5, sm.tDW, sm.tK, true);  // dk += P K
-      mma64<BF, true, true>(A5, sm.tDW, sm.tK, true);   // dk += P^T K
+      mma64x2<BF, false, true>(A5, sm.tDW, sm.tK, true);  // dk += P K
+      mma64x2<BF, true, true>(A5, sm.tDW, sm.tK, true);   // dk += P^T K
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
-      float x[64];
-      ld64(A4 + rm.lane, x);
-      const size_t off = (static_cast<size_t>(cp.bos + (in ? r : 0)) * p.H + hq) * 64;
-      if (owner && in) {
+      float x[32];
+      const size_t off = (static_cast<size_t>(cp.bos + (in ? r : 0)) * p.H + hq) * 64 + ch;
+      ld_half(A4 + rm.lane, hh, x);
+      if (in) {
         if (p.gva) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) atomicAdd(p.dq + off + c, x[c]);
+          for (int c = 0; c < 32; ++c) atomicAdd(p.dq + off + c, x[c]);
         } else {
-          st_g32(p.dq + off, x);
+          float4* d = reinterpret_cast<float4*>(p.dq + off);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
         }
       }
-      ld64(A5 + rm.lane, x);
-      if (owner && in) {
+      ld_half(A5 + rm.lane, hh, x);
+      if (in) {
         if (p.gva) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) atomicAdd(p.dk + off + c, x[c]);
+          for (int c = 0; c < 32; ++c) atomicAdd(p.dk + off + c, x[c]);
         } else {
-          st_g32(p.dk + off, x);
+          float4* d = reinterpret_cast<float4*>(p.dk + off);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
         }
       }
     }
-    // dgamma: row terms + column sums, then the state-leaving terms on gamma_C
-    if (owner) {
+    // combine the two half-rows, then dgamma: row terms + column sums + the terms on gamma_C
+    dgr += __shfl_xor_sync(0xffffffffu, dgr, 16);
+    dbr += __shfl_xor_sync(0xffffffffu, dbr, 16);
+    tot += __shfl_xor_sync(0xffffffffu, tot, 16);
+    if (lead) {
       sm.dgam[r] = dgr;
       atomicAdd(&sm.red[0], tot);
     }
@@ -1202,7 +1340,7 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
       if (i0 < len) p.dg[static_cast<size_t>(cp.bos + i0) * p.HV + hv] = excl + a;
       if (i1 < len) p.dg[static_cast<size_t>(cp.bos + i1) * p.HV + hv] = excl + b2;
     }
-    if (owner && in) p.dbeta[rowv] = dbr;
+    if (lead && in) p.dbeta[rowv] = dbr;
   } while (0);
   if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
   tc_fence_before();
@@ -1277,7 +1415,7 @@ template <typename T>
 int fwd_typed(const Params& p, cudaStream_t st) {
   const int items = p.NC * p.HV, pairs = (items + 1) / 2;
   int e = launch2(gdn_tc_prep_kernel<T>, pairs, smem_of(sizeof(PrepSmem)), st, p, items);
-  if (!e) e = launch(gdn_tc_state_kernel<T>, p.N * p.HV, smem_of(sizeof(StateSmem)), st, p);
+  if (!e) e = launch(gdn_tc_state_kernel<T>, 2 * p.N * p.HV, smem_of(sizeof(StateSmem)), st, p);
   if (!e) e = launch2(gdn_tc_out_kernel<T>, pairs, smem_of(sizeof(OutSmem)), st, p, items);
   return e;
 }
@@ -1294,10 +1432,10 @@ int bwd_typed(const Params& p, bool reuse, cudaStream_t st) {
   int e = KATA_OK;
   if (!reuse) {  // rebuild gamma, W, U0 from the saved Tm, then u and the chunk states
     e = launch2(gdn_tc_prep_kernel<T>, pairs, smem_of(sizeof(PrepSmem)), st, p, items);
-    if (!e) e = launch(gdn_tc_state_kernel<T>, p.N * p.HV, smem_of(sizeof(StateSmem)), st, p);
+    if (!e) e = launch(gdn_tc_state_kernel<T>, 2 * p.N * p.HV, smem_of(sizeof(StateSmem)), st, p);
   }
   if (!e) e = launch2(gdn_tc_dvl_kernel<T>, pairs, smem_of(sizeof(DvlSmem)), st, p, items);
-  if (!e) e = launch(gdn_tc_dstate_kernel<T>, p.N * p.HV, smem_of(sizeof(DstateSmem)), st, p);
+  if (!e) e = launch(gdn_tc_dstate_kernel<T>, 2 * p.N * p.HV, smem_of(sizeof(DstateSmem)), st, p);
   if (!e) e = launch(gdn_tc_grad_kernel<T>, p.NC * p.HV, smem_of(sizeof(GradSmem)), st, p);
   return e;
 }

@@ -51,7 +51,7 @@ def test_umma_selftest(N, K, a_mn, b_mn, a_sw, b_sw, a_tmem):
 
 # (N, K, a_mn, b_mn, lane_off): the M = 64 tiles of the tensor-core gated delta rule
 CASES64 = [(64, 64, 0, 0, 0), (64, 64, 0, 0, 16), (64, 64, 1, 0, 0), (64, 64, 0, 1, 16), (64, 64, 1, 1, 0),
-           (128, 64, 0, 0, 16), (64, 128, 0, 1, 0)]
+           (128, 64, 0, 0, 16), (64, 128, 0, 1, 0), (64, 64, 1, 0, 16), (64, 64, 1, 1, 16), (64, 128, 1, 0, 16)]
 
 
 @pytest.mark.parametrize("N,K,a_mn,b_mn,lane_off", CASES64)
