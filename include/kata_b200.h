@@ -284,9 +284,9 @@ typedef struct {
   const float* A;            /* the forward's A */
   const void* dout;          /* (B,T,HV,V) dtype */
   const float* dht;          /* (N,HV,K,V) or NULL */
-  float* dq;                 /* (B,T,H,K) [out] */
-  float* dk;                 /* (B,T,H,K) [out] */
-  float* dv;                 /* (B,T,HV,V) [out] */
+  void* dq;                  /* (B,T,H,K) [out], fp32 or grad_dtype */
+  void* dk;                  /* (B,T,H,K) [out] */
+  void* dv;                  /* (B,T,HV,V) [out] */
   float* dg;                 /* (B,T,HV) [out] */
   float* dbeta;              /* (B,T,HV) [out] */
   float* dh0;                /* (N,HV,K,V) [out] or NULL */
@@ -303,6 +303,9 @@ typedef struct {
   float scale;
   int algo;                  /* KATA_ALGO_*, as in the forward; the backward must use the forward's family
                                 when fwd_workspace is given (the two families lay the workspace out differently) */
+  int grad_dtype;            /* KATA_DTYPE_F32 (0): dq, dk, dv are fp32.  The input dtype: dq, dk, dv are written
+                                in it (tensor-core family with H == HV only, else KATA_ERR_UNSUPPORTED); dg,
+                                dbeta, dh0 stay fp32 */
 } kata_gdn_bwd_args;
 
 KATA_API size_t kata_gdn_bwd_workspace_bytes(const kata_gdn_bwd_args* args);

@@ -97,7 +97,7 @@ class GdnBwdArgs(ctypes.Structure):
         ("cu_seqlens", c_void_p), ("chunk_offsets", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("fwd_workspace", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HV", c_int), ("K", c_int), ("V", c_int),
-        ("N", c_int), ("num_chunks", c_int), ("scale", c_float), ("algo", c_int),
+        ("N", c_int), ("num_chunks", c_int), ("scale", c_float), ("algo", c_int), ("grad_dtype", c_int),
     ]
 
 

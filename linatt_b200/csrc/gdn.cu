@@ -1083,6 +1083,8 @@ extern "C" int kata_gdn_bwd(const kata_gdn_bwd_args* a, kata_stream_t stream) {
     return KATA_ERR_INVALID;
   const int fam = gdn_family(a->algo, a->dtype);
   if (fam < 0) return fam;
+  if (a->grad_dtype != KATA_DTYPE_F32 && (a->grad_dtype != a->dtype || fam != 1 || a->HV != a->H))
+    return a->grad_dtype == a->dtype ? KATA_ERR_UNSUPPORTED : KATA_ERR_DTYPE;
   if (fam == 1) return gdn_tc_bwd(a, reinterpret_cast<cudaStream_t>(stream));
   const bool reuse = a->fwd_workspace != nullptr;
   const WsLayout w = ws_layout(a->B, a->T, a->HV, a->num_chunks, true, reuse);
@@ -1099,9 +1101,9 @@ extern "C" int kata_gdn_bwd(const kata_gdn_bwd_args* a, kata_stream_t stream) {
   p.co = a->chunk_offsets;
   p.dout = a->dout;
   p.dht = a->dht;
-  p.dq = a->dq;
-  p.dk = a->dk;
-  p.dv = a->dv;
+  p.dq = static_cast<float*>(a->dq);
+  p.dk = static_cast<float*>(a->dk);
+  p.dv = static_cast<float*>(a->dv);
   p.dg = a->dg;
   p.dbeta = a->dbeta;
   p.dh0 = a->dh0;

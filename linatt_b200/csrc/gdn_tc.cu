@@ -53,16 +53,16 @@ struct Params {
   void* hS;    // (NC, HV, 64, 64) 16-bit: state entering each chunk
   const void* dout;
   const float* dht;
-  float* dq;
-  float* dk;
-  float* dv;
+  void* dq;    // fp32, or 16-bit when grad16
+  void* dk;
+  void* dv;
   float* dg;
   float* dbeta;
   float* dh0;
   float* dvl;  // (rows, 64) fp32
   void* du;    // (rows, 64) 16-bit
   void* hD;    // (NC, HV, 64, 64) 16-bit: gradient of the state leaving each chunk
-  int B, T, H, HV, N, NC, a_given, gva;
+  int B, T, H, HV, N, NC, a_given, gva, grad16;
   float scale;
 };
 
@@ -103,6 +103,24 @@ __device__ __forceinline__ void seq_range(const Params& p, int n, int& bos, int&
     nc = (p.T + CH - 1) / CH;
     c0 = n * nc;
   }
+}
+
+// Chunk item (= chunk index * HV + value head) of slot s of a two-chunk CTA: scalars, so that no
+// per-slot array is indexed with a runtime slot (which would put it in local memory).
+struct Item {
+  int gc, bos, len, hv, hq;
+};
+__device__ __forceinline__ Item item_of(const Params& p, int s, int items) {
+  const int item = 2 * blockIdx.x + s;
+  const bool valid = item < items;
+  Item it;
+  it.gc = valid ? item / p.HV : 0;
+  it.hv = valid ? item % p.HV : 0;
+  it.hq = it.hv / (p.HV / p.H);
+  const ChunkPos cp = chunk_pos(p, it.gc);
+  it.bos = cp.bos;
+  it.len = valid ? cp.len : 0;
+  return it;
 }
 
 __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
@@ -333,18 +351,10 @@ __global__ void __launch_bounds__(128) gdn_tc_prep_kernel(Params p, int items) {
   PrepSmem& sm = *reinterpret_cast<PrepSmem*>(align1k(smraw));
   constexpr bool BF = is_bf16<T>();
   const int tid = threadIdx.x;
-  int bos[2], len[2], hv[2], hq[2];
-#pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    const int item = 2 * blockIdx.x + s;
-    const bool valid = item < items;
-    const int gc = valid ? item / p.HV : 0;
-    hv[s] = valid ? item % p.HV : 0;
-    hq[s] = hv[s] / (p.HV / p.H);
-    const ChunkPos cp = chunk_pos(p, gc);
-    bos[s] = cp.bos;
-    len[s] = valid ? cp.len : 0;
-  }
+  // two views of the chunk pair: by column / load row (slot tid >> 6) and by accumulator row (slot =
+  // lane half)
+  const Item ia = item_of(p, tid >> 6, items);
+  const Item ib = item_of(p, (tid & 31) >> 4, items);
   if (tid == 0) {
     sm.abort = 0;
     mbar_init(&sm.bar, 1);
@@ -357,12 +367,12 @@ __global__ void __launch_bounds__(128) gdn_tc_prep_kernel(Params p, int items) {
   float gsum;
   {
     const int s = tid >> 6, r = tid & 63;
-    const bool ok = r < len[s];
-    const size_t tok = static_cast<size_t>(bos[s] + (ok ? r : 0));
-    cp_row(sm.tK[s], r, static_cast<const T*>(p.k) + (tok * p.H + hq[s]) * 64, ok);
-    cp_row(sm.tV[s], r, static_cast<const T*>(p.v) + (tok * p.HV + hv[s]) * 64, ok);
-    sm.beta[s][r] = ok ? p.beta[tok * p.HV + hv[s]] : 0.f;
-    sm.gam[s][r] = ok ? p.g[tok * p.HV + hv[s]] : 0.f;
+    const bool ok = r < ia.len;
+    const size_t tok = static_cast<size_t>(ia.bos + (ok ? r : 0));
+    cp_row(sm.tK[s], r, static_cast<const T*>(p.k) + (tok * p.H + ia.hq) * 64, ok);
+    cp_row(sm.tV[s], r, static_cast<const T*>(p.v) + (tok * p.HV + ia.hv) * 64, ok);
+    sm.beta[s][r] = ok ? p.beta[tok * p.HV + ia.hv] : 0.f;
+    sm.gam[s][r] = ok ? p.g[tok * p.HV + ia.hv] : 0.f;
   }
   tc_fence_before();
   __syncthreads();
@@ -416,15 +426,17 @@ __global__ void __launch_bounds__(128) gdn_tc_prep_kernel(Params p, int items) {
       float x[64];
       solve_column(sm.L[s], c, x);
       uint8_t* tt = sm.tT[s];
+      float* arow = p.A + (static_cast<size_t>(ia.bos) * p.HV + ia.hv) * 64 + c;
+      const size_t astride = static_cast<size_t>(p.HV) * 64;
 #pragma unroll
       for (int r = 0; r < 64; ++r) {
         *reinterpret_cast<T*>(tt + toff(r, c)) = from_f32<T>(x[r]);
-        if (r < len[s]) p.A[(static_cast<size_t>(bos[s] + r) * p.HV + hv[s]) * 64 + c] = x[r];
+        if (r < ia.len) arow[r * astride] = x[r];
       }
     } else {  // the forward's Tm; rows past a ragged chunk's end are identity rows
       const int s = tid >> 6, r = tid & 63;
-      const bool in = r < len[s];
-      cvt_row<T>(sm.tT[s], r, p.A + (static_cast<size_t>(bos[s] + (in ? r : 0)) * p.HV + hv[s]) * 64, in,
+      const bool in = r < ia.len;
+      cvt_row<T>(sm.tT[s], r, p.A + (static_cast<size_t>(ia.bos + (in ? r : 0)) * p.HV + ia.hv) * 64, in,
                  in ? -1 : r);
     }
     fence_proxy_async_smem();
@@ -441,8 +453,8 @@ __global__ void __launch_bounds__(128) gdn_tc_prep_kernel(Params p, int items) {
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
       const int s = rm.slot, r = rm.row;
-      const bool in = r < len[s];
-      const size_t row = static_cast<size_t>(bos[s] + (in ? r : 0)) * p.HV + hv[s];
+      const bool in = r < ib.len;
+      const size_t row = static_cast<size_t>(ib.bos + (in ? r : 0)) * p.HV + ib.hv;
       float x[64];
       ld64(tbase + rm.lane, x);
       if (in) st_g16<T>(static_cast<T*>(p.W) + row * 64, x);
@@ -674,18 +686,8 @@ __global__ void __launch_bounds__(128) gdn_tc_out_kernel(Params p, int items) {
   OutSmem& sm = *reinterpret_cast<OutSmem*>(align1k(smraw));
   constexpr bool BF = is_bf16<T>();
   const int tid = threadIdx.x;
-  int bos[2], len[2], hv[2], hq[2], gcs[2];
-#pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    const int item = 2 * blockIdx.x + s;
-    const bool valid = item < items;
-    gcs[s] = valid ? item / p.HV : 0;
-    hv[s] = valid ? item % p.HV : 0;
-    hq[s] = hv[s] / (p.HV / p.H);
-    const ChunkPos cp = chunk_pos(p, gcs[s]);
-    bos[s] = cp.bos;
-    len[s] = valid ? cp.len : 0;
-  }
+  const Item ia = item_of(p, tid >> 6, items);         // load rows
+  const Item ib = item_of(p, (tid & 31) >> 4, items);  // accumulator rows
   if (tid == 0) {
     sm.abort = 0;
     mbar_init(&sm.bar, 1);
@@ -697,14 +699,14 @@ __global__ void __launch_bounds__(128) gdn_tc_out_kernel(Params p, int items) {
   }
   {
     const int s = tid >> 6, r = tid & 63;
-    const bool in = r < len[s];
-    const size_t tok = static_cast<size_t>(bos[s] + (in ? r : 0));
-    cp_row(sm.tQ[s], r, static_cast<const T*>(p.q) + (tok * p.H + hq[s]) * 64, in);
-    cp_row(sm.tK[s], r, static_cast<const T*>(p.k) + (tok * p.H + hq[s]) * 64, in);
-    cp_row(sm.tU[s], r, static_cast<const T*>(p.u) + (tok * p.HV + hv[s]) * 64, in);
-    cp_row(sm.tS[s], r, static_cast<const T*>(p.hS) + ((static_cast<size_t>(gcs[s]) * p.HV + hv[s]) * 64 + r) * 64,
-           len[s] > 0);
-    sm.gam[s][r] = in ? p.gam[tok * p.HV + hv[s]] : 0.f;
+    const bool in = r < ia.len;
+    const size_t tok = static_cast<size_t>(ia.bos + (in ? r : 0));
+    cp_row(sm.tQ[s], r, static_cast<const T*>(p.q) + (tok * p.H + ia.hq) * 64, in);
+    cp_row(sm.tK[s], r, static_cast<const T*>(p.k) + (tok * p.H + ia.hq) * 64, in);
+    cp_row(sm.tU[s], r, static_cast<const T*>(p.u) + (tok * p.HV + ia.hv) * 64, in);
+    cp_row(sm.tS[s], r, static_cast<const T*>(p.hS) + ((static_cast<size_t>(ia.gc) * p.HV + ia.hv) * 64 + r) * 64,
+           ia.len > 0);
+    sm.gam[s][r] = in ? p.gam[tok * p.HV + ia.hv] : 0.f;
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -749,7 +751,7 @@ __global__ void __launch_bounds__(128) gdn_tc_out_kernel(Params p, int items) {
     const float eg = __expf(gr);
 #pragma unroll
     for (int c = 0; c < 64; ++c) x[c] = p.scale * fmaf(eg, a[c], x[c]);
-    if (r < len[s]) st_g16<T>(static_cast<T*>(p.o) + (static_cast<size_t>(bos[s] + r) * p.HV + hv[s]) * 64, x);
+    if (r < ib.len) st_g16<T>(static_cast<T*>(p.o) + (static_cast<size_t>(ib.bos + r) * p.HV + ib.hv) * 64, x);
   } while (0);
   if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
   tc_fence_before();
@@ -777,18 +779,8 @@ __global__ void __launch_bounds__(128) gdn_tc_dvl_kernel(Params p, int items) {
   DvlSmem& sm = *reinterpret_cast<DvlSmem*>(align1k(smraw));
   constexpr bool BF = is_bf16<T>();
   const int tid = threadIdx.x;
-  int bos[2], len[2], hv[2], hq[2];
-#pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    const int item = 2 * blockIdx.x + s;
-    const bool valid = item < items;
-    const int gc = valid ? item / p.HV : 0;
-    hv[s] = valid ? item % p.HV : 0;
-    hq[s] = hv[s] / (p.HV / p.H);
-    const ChunkPos cp = chunk_pos(p, gc);
-    bos[s] = cp.bos;
-    len[s] = valid ? cp.len : 0;
-  }
+  const Item ia = item_of(p, tid >> 6, items);         // load rows
+  const Item ib = item_of(p, (tid & 31) >> 4, items);  // accumulator rows
   if (tid == 0) {
     sm.abort = 0;
     mbar_init(&sm.bar, 1);
@@ -800,12 +792,12 @@ __global__ void __launch_bounds__(128) gdn_tc_dvl_kernel(Params p, int items) {
   }
   {
     const int s = tid >> 6, r = tid & 63;
-    const bool in = r < len[s];
-    const size_t tok = static_cast<size_t>(bos[s] + (in ? r : 0));
-    cp_row(sm.tQ[s], r, static_cast<const T*>(p.q) + (tok * p.H + hq[s]) * 64, in);
-    cp_row(sm.tK[s], r, static_cast<const T*>(p.k) + (tok * p.H + hq[s]) * 64, in);
-    cp_row(sm.tO[s], r, static_cast<const T*>(p.dout) + (tok * p.HV + hv[s]) * 64, in);
-    sm.gam[s][r] = in ? p.gam[tok * p.HV + hv[s]] : 0.f;
+    const bool in = r < ia.len;
+    const size_t tok = static_cast<size_t>(ia.bos + (in ? r : 0));
+    cp_row(sm.tQ[s], r, static_cast<const T*>(p.q) + (tok * p.H + ia.hq) * 64, in);
+    cp_row(sm.tK[s], r, static_cast<const T*>(p.k) + (tok * p.H + ia.hq) * 64, in);
+    cp_row(sm.tO[s], r, static_cast<const T*>(p.dout) + (tok * p.HV + ia.hv) * 64, in);
+    sm.gam[s][r] = in ? p.gam[tok * p.HV + ia.hv] : 0.f;
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -843,7 +835,7 @@ __global__ void __launch_bounds__(128) gdn_tc_dvl_kernel(Params p, int items) {
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     float x[64];
     ld64(tbase + rm.lane + 64, x);
-    if (j < len[s]) st_g32(p.dvl + (static_cast<size_t>(bos[s] + j) * p.HV + hv[s]) * 64, x);
+    if (j < ib.len) st_g32(p.dvl + (static_cast<size_t>(ib.bos + j) * p.HV + ib.hv) * 64, x);
   } while (0);
   if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
   tc_fence_before();
@@ -997,65 +989,75 @@ __global__ void __launch_bounds__(128) gdn_tc_dstate_kernel(Params p) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// backward 2: per-chunk dq, dk, dv, dbeta, dg.  One chunk per CTA, 128 threads.  Every MMA is issued
-// into both TMEM lane halves (mma64x2), and thread (warp w, lane l) handles row 16w + (l & 15),
-// columns 32 * (l >> 4) .. +32; row sums are combined across the two halves at the end.  TMEM
-// columns (64 each): A0 du S0^T -> Y_K, A1 K K^T, A2 Q K^T, A3 dO u^T, A4 dq, A5 dk, A6 Tm^T du -> dL'.
+// backward 2: per-chunk dq, dk, dv, dbeta, dg.  One chunk per CTA of 256 threads, two CTAs per SM (so
+// one CTA's loads and MMAs overlap the other's epilogues): at most four accumulators live in 256
+// TMEM columns (R0..R3), and twelve 16-bit tiles (U0 and W arrive late, into the tiles of dO and u).
+// Every MMA is issued into both TMEM lane halves (mma64x2).  Warp w reads the lanes of subpartition
+// w % 4 and columns 32 (w / 4) .. +32, of which its lane half h keeps 16: thread (w, l) handles row
+// 16 (w % 4) + (l & 15) and columns 32 (w / 4) + 16 h .. +16.  Row sums combine the four threads of a
+// row (shuffle + shared memory); column sums reduce the 16 rows of a half-warp by shuffles.
+//   batch 1a: R0 du S0^T (-dW), R1 Tm^T du (Y_V), R2 dO u^T, R3 Q K^T
+//   batch 1b: R0 dO S0^T (dq), R2 u dS_end^T (dk), R3 Tm^T dW (Y_K)
+//   batch 2:  R0 += M' K, R2 += M'^T Q, R1 = Y_V U0^T + Y_K W^T (-dL), R3 K K^T
+//   batch 3:  R2 += P K + P^T K
 // ------------------------------------------------------------------------------------------------
 struct GradSmem {
-  uint8_t tQ[TB], tK[TB], tO[TB], tU[TB], tDU[TB], tS0[TB], tHD[TB], tTm[TB], tU0[TB], tW[TB];
+  uint8_t tQ[TB], tK[TB], tO[TB], tU[TB], tDU[TB], tS0[TB], tHD[TB], tTm[TB];
   uint8_t tDW[TB];  // dW, later P
   uint8_t tYV[TB], tYK[TB], tM[TB];
-  float F[CH][CH + 1];  // per-element contributions whose column sums enter dgamma_j
+  float colpart[4][CH];  // column sums of the dgamma_j terms, per subpartition (16 rows each)
+  float part[3][2][CH];  // per-row partial sums (dgamma, dbeta, tot) of the two column groups
   float gam[CH], beta[CH], dgam[CH], red[4];
   uint64_t bar;
   uint32_t tmem;
   int abort;
 };
 
-// Columns [32h, 32h + 32) of this thread's TMEM lane (h = lane half).  tcgen05.ld / st take one
-// address per warp, so the warp loads both halves and each lane keeps its own; a store writes the
-// thread's 32 values into both halves of its lane (the half a lane does not own is never read).
-__device__ __forceinline__ void ld_half(uint32_t taddr, int h, float (&x)[32]) {
-  uint32_t a[32], b[32];
-  tmem_ld32(taddr, a);
-  tmem_ld32(taddr + 32, b);
-  tmem_wait_ld();
+// 16 columns of this thread's TMEM lane (its lane half h of the warp's 32 columns at taddr) and the
+// matching store, written into both 16-column halves (the half a lane does not own is never read).
+__device__ __forceinline__ void st_quarter(uint32_t taddr, const float (&x)[16]) {
+  uint32_t a[16];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(h ? b[j] : a[j]);
+  for (int j = 0; j < 16; ++j) a[j] = __float_as_uint(x[j]);
+  tmem_st16(taddr, a);
+  tmem_st16(taddr + 16, a);
 }
-__device__ __forceinline__ void st_half(uint32_t taddr, const float (&x)[32]) {
-  uint32_t a[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) a[j] = __float_as_uint(x[j]);
-  tmem_st32(taddr, a);
-  tmem_st32(taddr + 32, a);
-}
+
+// 16 gradient values at element offset `off` of an fp32 or (grad16) 16-bit output.
 template <typename T>
-__device__ __forceinline__ void st_row32(uint8_t* tile, int r, int c0, const float (&x)[32]) {
-  const uint32_t base = smem_u32(tile);
+__device__ __forceinline__ void st_grad16(void* base, size_t off, const float (&x)[16], int grad16) {
+  if (grad16) {
+    st_g16x16<T>(static_cast<T*>(base) + off, x);
+  } else {
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(base) + off);
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
-    st_shared_v4(base + toff(r, c0 + 8 * c), pack2<T>(x[8 * c], x[8 * c + 1]), pack2<T>(x[8 * c + 2], x[8 * c + 3]),
-                 pack2<T>(x[8 * c + 4], x[8 * c + 5]), pack2<T>(x[8 * c + 6], x[8 * c + 7]));
-}
-template <typename T>
-__device__ __forceinline__ void ld_row32(const uint8_t* tile, int r, int c0, float (&x)[32]) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint4 u4 = *reinterpret_cast<const uint4*>(tile + toff(r, c0 + 8 * c));
-    const T* e = reinterpret_cast<const T*>(&u4);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[8 * c + j] = to_f32<T>(e[j]);
+    for (int c = 0; c < 4; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
   }
 }
 
+// Sum over the 16 rows of a half-warp of each of the thread's 16 column values; lane (l & 15) == j of
+// the half ends with column j's sum in the return value.
+__device__ __forceinline__ float colsum16(const float (&c)[16]) {
+  const int me = threadIdx.x & 15;
+  float mine = 0.f;
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    float v = c[jj];
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    if (jj == me) mine = v;
+  }
+  return mine;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
+__global__ void __launch_bounds__(256, 2) gdn_tc_grad_kernel(Params p) {
   extern __shared__ uint8_t smraw[];
   GradSmem& sm = *reinterpret_cast<GradSmem*>(align1k(smraw));
   constexpr bool BF = is_bf16<T>();
-  const int tid = threadIdx.x, ln = tid & 31;
+  const int tid = threadIdx.x, ln = tid & 31, w = tid >> 5;
   const int gc = blockIdx.x / p.HV, hv = blockIdx.x % p.HV, hq = hv / (p.HV / p.H);
   const ChunkPos cp = chunk_pos(p, gc);
   const int len = cp.len;
@@ -1064,30 +1066,30 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
     mbar_init(&sm.bar, 1);
     fence_mbar_init();
   }
-  if (tid < 32) {
-    tmem_alloc(&sm.tmem, 512);
+  if (w == 0) {
+    tmem_alloc(&sm.tmem, 256);
     tmem_relinquish();
   }
-  {  // loads: thread = (half, row); half 0 the token tiles, half 1 the state / WY tiles
-    const int r = tid & 63, half = tid >> 6;
+  {  // loads: thread = (group, row)
+    const int r = tid & 63, grp = tid >> 6;
     const bool in = r < len;
     const size_t tok = static_cast<size_t>(cp.bos + (in ? r : 0));
     const size_t rowv = tok * p.HV + hv;
     const size_t st = (static_cast<size_t>(gc) * p.HV + hv) * 64 * 64;
-    if (half == 0) {
+    if (grp == 0) {
       cp_row(sm.tQ, r, static_cast<const T*>(p.q) + (tok * p.H + hq) * 64, in);
       cp_row(sm.tK, r, static_cast<const T*>(p.k) + (tok * p.H + hq) * 64, in);
-      cp_row(sm.tO, r, static_cast<const T*>(p.dout) + rowv * 64, in);
-      cp_row(sm.tU, r, static_cast<const T*>(p.u) + rowv * 64, in);
-      cp_row(sm.tDU, r, static_cast<const T*>(p.du) + rowv * 64, in);
       sm.gam[r] = in ? p.gam[rowv] : 0.f;
       sm.beta[r] = in ? p.beta[rowv] : 0.f;
-    } else {
+    } else if (grp == 1) {
+      cp_row(sm.tO, r, static_cast<const T*>(p.dout) + rowv * 64, in);
+      cp_row(sm.tU, r, static_cast<const T*>(p.u) + rowv * 64, in);
+    } else if (grp == 2) {
+      cp_row(sm.tDU, r, static_cast<const T*>(p.du) + rowv * 64, in);
       cp_row(sm.tS0, r, static_cast<const T*>(p.hS) + st + r * 64, true);
       cp_row(sm.tHD, r, static_cast<const T*>(p.hD) + st + r * 64, true);
-      cp_row(sm.tW, r, static_cast<const T*>(p.W) + rowv * 64, in);
+    } else {
       cvt_row<T>(sm.tTm, r, p.A + rowv * 64, in, in ? -1 : r);
-      cvt_row<T>(sm.tU0, r, p.U0 + rowv * 64, in, -1);
     }
     if (tid < 4) sm.red[tid] = 0.f;
   }
@@ -1098,42 +1100,38 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
   if (tid < CH && tid >= len) sm.gam[tid] = sm.gam[len - 1];  // rows past the end: gamma_last (g = 0)
   __syncthreads();
   const uint32_t tbase = sm.tmem;
-  const uint32_t A0 = tbase, A1 = tbase + 64, A2 = tbase + 128, A3 = tbase + 192, A4 = tbase + 256,
-                 A5 = tbase + 320, A6 = tbase + 384;
+  const int spq = w & 3, cg = w >> 2, hh = ln >> 4;
+  const int r = 16 * spq + (ln & 15), ch = 32 * cg + 16 * hh;  // this thread's row and first column
+  const uint32_t T0 = tbase + (static_cast<uint32_t>(32 * spq) << 16) + 32 * cg;  // warp-uniform TMEM address
+  const uint32_t R0 = T0, R1 = T0 + 64, R2 = T0 + 128, R3 = T0 + 192;
   uint32_t phase = 0;
   bool ok = true;
-  const RowMap rm = rowmap();
-  const int r = rm.row, hh = ln >> 4, ch = 32 * hh;  // this thread's row, lane half and first column
-  const bool lead = ln < 16;                  // one of the two threads of a row writes per-row values
   const float gC = sm.gam[CH - 1], gr = sm.gam[r], br = sm.beta[r], egr = __expf(gr);
-  float dgr = 0.f, dbr = 0.f, tot = 0.f;  // this thread's half-row parts
+  float dgr = 0.f, dbr = 0.f, tot = 0.f;  // this thread's parts of the row sums
   const bool in = r < len;
   const size_t rowv = static_cast<size_t>(cp.bos + (in ? r : 0)) * p.HV + hv;
   do {
     if (tid == 0) {
-      mma64x2<BF, false, false>(A0, sm.tDU, sm.tS0, false);  // du S0^T  (= -dW)
-      mma64x2<BF, false, false>(A1, sm.tK, sm.tK, false);    // K K^T
-      mma64x2<BF, false, false>(A2, sm.tQ, sm.tK, false);    // Q K^T
-      mma64x2<BF, false, false>(A3, sm.tO, sm.tU, false);    // dO u^T
-      mma64x2<BF, false, false>(A4, sm.tO, sm.tS0, false);   // dO S0^T
-      mma64x2<BF, false, false>(A5, sm.tU, sm.tHD, false);   // u dS_end^T
-      mma64x2<BF, true, true>(A6, sm.tTm, sm.tDU, false);    // Tm^T du  (= Y_V)
+      mma64x2<BF, false, false>(tbase, sm.tDU, sm.tS0, false);     // du S0^T  (= -dW)
+      mma64x2<BF, true, true>(tbase + 64, sm.tTm, sm.tDU, false);  // Tm^T du  (= Y_V)
+      mma64x2<BF, false, false>(tbase + 128, sm.tO, sm.tU, false);  // dO u^T
+      mma64x2<BF, false, false>(tbase + 192, sm.tQ, sm.tK, false);  // Q K^T
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
-    {
-      float x[32];
-      ld_half(A0 + rm.lane, hh, x);  // dW = -(du S0^T)
+    {  // epilogue 1a
+      float x[16];
+      ld_quarter(R0, hh, x);  // dW = -(du S0^T)
 #pragma unroll
-      for (int c = 0; c < 32; ++c) x[c] = -x[c];
-      st_row32<T>(sm.tDW, r, ch, x);
-      ld_half(A6 + rm.lane, hh, x);  // Y_V
-      st_row32<T>(sm.tYV, r, ch, x);
-      float vv[32];
+      for (int c = 0; c < 16; ++c) x[c] = -x[c];
+      st_row16<T>(sm.tDW, r, ch, x);
+      ld_quarter(R1, hh, x);  // Y_V
+      st_row16<T>(sm.tYV, r, ch, x);
+      float vv[16];
       {
         const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v) + rowv * 64 + ch);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           const uint4 u4 = in ? s4[c] : make_uint4(0u, 0u, 0u, 0u);
           const T* e = reinterpret_cast<const T*>(&u4);
 #pragma unroll
@@ -1142,60 +1140,75 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
       }
       float s1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) s1 = fmaf(vv[c], x[c], s1);
+      for (int c = 0; c < 16; ++c) s1 = fmaf(vv[c], x[c], s1);
       dbr += s1;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) x[c] *= br;
-      if (in) {
-        float4* d = reinterpret_cast<float4*>(p.dv + rowv * 64 + ch);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
-      }
-    }
-    {
-      float t[32], e[32];
-      ld_half(A3 + rm.lane, hh, t);  // dO_r . u_j
-      ld_half(A2 + rm.lane, hh, e);  // q_r . k_j
+      for (int c = 0; c < 16; ++c) x[c] *= br;
+      if (in) st_grad16<T>(p.dv, rowv * 64 + ch, x, p.grad16);
+      float t[16], e[16];
+      ld_quarter(R2, hh, t);  // dO_r . u_j
+      ld_quarter(R3, hh, e);  // q_r . k_j
       float rs = 0.f;
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
+      for (int jj = 0; jj < 16; ++jj) {
         const int j = ch + jj;
         const float mp = j <= r ? p.scale * __expf(gr - sm.gam[j]) * t[jj] : 0.f;
         t[jj] = mp;
-        const float mg = mp * e[jj];
-        rs += mg;
-        sm.F[r][j] = mg;
+        e[jj] *= mp;  // Mg_rj = M'_rj (q_r . k_j): into dgamma_r, out of dgamma_j
+        rs += e[jj];
       }
       dgr += rs;
-      st_row32<T>(sm.tM, r, ch, t);
+      st_row16<T>(sm.tM, r, ch, t);
+      const float cs = colsum16(e);
+      sm.colpart[spq][ch + (ln & 15)] = cs;
     }
-    {
-      float x[32], qq[32];
-      ld_half(A4 + rm.lane, hh, x);  // dq term scale e^gamma (dO S0^T)
-      ld_row32<T>(sm.tQ, r, ch, qq);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma64x2<BF, false, false>(tbase, sm.tO, sm.tS0, false);         // dO S0^T
+      mma64x2<BF, false, false>(tbase + 128, sm.tU, sm.tHD, false);   // u dS_end^T
+      mma64x2<BF, true, true>(tbase + 192, sm.tTm, sm.tDW, false);    // Y_K = Tm^T dW
+      umma_commit(&sm.bar);
+    }
+    if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
+    {  // U0 and W into the tiles of dO and u (their last reader, batch 1b, has completed)
+      const int rr = tid & 63, grp = tid >> 6;
+      const bool rin = rr < len;
+      const size_t rv = static_cast<size_t>(cp.bos + (rin ? rr : 0)) * p.HV + hv;
+      if (grp == 0) cvt_row<T>(sm.tO, rr, p.U0 + rv * 64, rin, -1);
+      else if (grp == 1) cp_row(sm.tU, rr, static_cast<const T*>(p.W) + rv * 64, rin);
+    }
+    {  // epilogue 1b
+      float x[16], y[16], qq[16], kk[16];
+      ld_quarter(R0, hh, x);  // dq term scale e^gamma (dO S0^T)
+      ld_row16<T>(sm.tQ, r, ch, qq);
       float s1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < 16; ++c) {
         x[c] *= p.scale * egr;
         s1 = fmaf(qq[c], x[c], s1);
       }
       dgr += s1;
-      st_half(A4 + rm.lane, x);
-    }
-    {
-      float x[32], kk[32];
-      ld_half(A5 + rm.lane, hh, x);  // dk term e^{gamma_C - gamma} (u dS_end^T)
-      ld_row32<T>(sm.tK, r, ch, kk);
+      st_quarter(R0, x);
+      ld_quarter(R2, hh, x);  // dk term e^{gamma_C - gamma} (u dS_end^T)
+      ld_quarter(R3, hh, y);  // Y_K
+      ld_row16<T>(sm.tK, r, ch, kk);
+      st_row16<T>(sm.tYK, r, ch, y);
       const float f = __expf(gC - gr);
-      float s1 = 0.f;
+      float s2 = 0.f, s3 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < 16; ++c) {
         x[c] *= f;
-        s1 = fmaf(kk[c], x[c], s1);
+        s2 = fmaf(kk[c], x[c], s2);
+        s3 = fmaf(kk[c], y[c], s3);
+        x[c] = fmaf(br * egr, y[c], x[c]);  // + beta e^gamma Y_K
       }
-      dgr -= s1;
-      tot += s1;
-      st_half(A5 + rm.lane, x);
+      dgr += br * egr * s3 - s2;
+      dbr += egr * s3;
+      tot += s2;
+      st_quarter(R2, x);
     }
     tmem_wait_st();
     fence_proxy_async_smem();
@@ -1203,107 +1216,81 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64x2<BF, true, true>(A0, sm.tTm, sm.tDW, false);  // Y_K = Tm^T dW
-      mma64x2<BF, false, true>(A4, sm.tM, sm.tK, true);    // dq += M' K
-      mma64x2<BF, true, true>(A5, sm.tM, sm.tQ, true);     // dk += M'^T Q
+      mma64x2<BF, false, true>(tbase, sm.tM, sm.tK, true);           // dq += M' K
+      mma64x2<BF, true, true>(tbase + 128, sm.tM, sm.tQ, true);      // dk += M'^T Q
+      mma64x2<BF, false, false>(tbase + 64, sm.tYV, sm.tO, false);   // Y_V U0^T
+      mma64x2<BF, false, false>(tbase + 64, sm.tYK, sm.tU, true);    // + Y_K W^T  (= -dL)
+      mma64x2<BF, false, false>(tbase + 192, sm.tK, sm.tK, false);   // K K^T
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
-    {
-      float x[32], kk[32], d[32];
-      ld_half(A0 + rm.lane, hh, x);  // Y_K
-      ld_half(A5 + rm.lane, hh, d);
-      ld_row32<T>(sm.tK, r, ch, kk);
-      st_row32<T>(sm.tYK, r, ch, x);
-      float s1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        s1 = fmaf(kk[c], x[c], s1);
-        d[c] = fmaf(br * egr, x[c], d[c]);
-      }
-      dbr += egr * s1;
-      dgr += br * egr * s1;
-      st_half(A5 + rm.lane, d);
-    }
-    tmem_wait_st();
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma64x2<BF, false, false>(A6, sm.tYV, sm.tU0, false);  // Y_V U0^T
-      mma64x2<BF, false, false>(A6, sm.tYK, sm.tW, true);    // + Y_K W^T  (= -dL)
-      umma_commit(&sm.bar);
-    }
-    if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
-    {
-      float t[32], e[32];
-      ld_half(A6 + rm.lane, hh, t);
-      ld_half(A1 + rm.lane, hh, e);
+    {  // epilogue 2
+      float t[16], e[16];
+      ld_quarter(R1, hh, t);
+      ld_quarter(R3, hh, e);
       float db = 0.f, dg = 0.f;
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
+      for (int jj = 0; jj < 16; ++jj) {
         const int j = ch + jj;
-        float P = 0.f;
+        float P = 0.f, G = 0.f;
         if (j < r) {
           const float dl = -t[jj];
           const float dec = __expf(gr - sm.gam[j]);
           const float E = dec * e[jj];
           db = fmaf(dl, E, db);
-          const float G = br * dl * E;
+          G = br * dl * E;
           dg += G;
-          sm.F[r][j] += G;
           P = br * dl * dec;
         }
         t[jj] = P;
+        e[jj] = G;
       }
       dbr += db;
       dgr += dg;
-      st_row32<T>(sm.tDW, r, ch, t);
+      st_row16<T>(sm.tDW, r, ch, t);
+      const float cs = colsum16(e);
+      sm.colpart[spq][ch + (ln & 15)] += cs;
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma64x2<BF, false, true>(A5, sm.tDW, sm.tK, true);  // dk += P K
-      mma64x2<BF, true, true>(A5, sm.tDW, sm.tK, true);   // dk += P^T K
+      mma64x2<BF, false, true>(tbase + 128, sm.tDW, sm.tK, true);  // dk += P K
+      mma64x2<BF, true, true>(tbase + 128, sm.tDW, sm.tK, true);   // dk += P^T K
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
     {
-      float x[32];
+      float x[16];
       const size_t off = (static_cast<size_t>(cp.bos + (in ? r : 0)) * p.H + hq) * 64 + ch;
-      ld_half(A4 + rm.lane, hh, x);
+      ld_quarter(R0, hh, x);
       if (in) {
         if (p.gva) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) atomicAdd(p.dq + off + c, x[c]);
+          for (int c = 0; c < 16; ++c) atomicAdd(static_cast<float*>(p.dq) + off + c, x[c]);
         } else {
-          float4* d = reinterpret_cast<float4*>(p.dq + off);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+          st_grad16<T>(p.dq, off, x, p.grad16);
         }
       }
-      ld_half(A5 + rm.lane, hh, x);
+      ld_quarter(R2, hh, x);
       if (in) {
         if (p.gva) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) atomicAdd(p.dk + off + c, x[c]);
+          for (int c = 0; c < 16; ++c) atomicAdd(static_cast<float*>(p.dk) + off + c, x[c]);
         } else {
-          float4* d = reinterpret_cast<float4*>(p.dk + off);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) d[c] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+          st_grad16<T>(p.dk, off, x, p.grad16);
         }
       }
     }
-    // combine the two half-rows, then dgamma: row terms + column sums + the terms on gamma_C
+    // row sums: the two lane halves of a warp (shuffle), then the two column groups (shared memory)
     dgr += __shfl_xor_sync(0xffffffffu, dgr, 16);
     dbr += __shfl_xor_sync(0xffffffffu, dbr, 16);
     tot += __shfl_xor_sync(0xffffffffu, tot, 16);
-    if (lead) {
-      sm.dgam[r] = dgr;
-      atomicAdd(&sm.red[0], tot);
+    if (hh == 0) {
+      sm.part[0][cg][r] = dgr;
+      sm.part[1][cg][r] = dbr;
+      sm.part[2][cg][r] = tot;
     }
     {
       float sd = 0.f;  // <S0, dS_end>
@@ -1319,9 +1306,10 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
     }
     __syncthreads();
     if (tid < CH) {
-      float col = 0.f;
-      for (int i = 0; i < CH; ++i) col += sm.F[i][tid];
-      sm.dgam[tid] -= col;
+      const float col = sm.colpart[0][tid] + sm.colpart[1][tid] + sm.colpart[2][tid] + sm.colpart[3][tid];
+      sm.dgam[tid] = sm.part[0][0][tid] + sm.part[0][1][tid] - col;
+      atomicAdd(&sm.red[0], sm.part[2][0][tid] + sm.part[2][1][tid]);
+      if (tid < len) p.dbeta[static_cast<size_t>(cp.bos + tid) * p.HV + hv] = sm.part[1][0][tid] + sm.part[1][1][tid];
     }
     __syncthreads();
     if (tid == 0) sm.dgam[CH - 1] += sm.red[0] + __expf(gC) * sm.red[1];
@@ -1340,22 +1328,21 @@ __global__ void __launch_bounds__(128) gdn_tc_grad_kernel(Params p) {
       if (i0 < len) p.dg[static_cast<size_t>(cp.bos + i0) * p.HV + hv] = excl + a;
       if (i1 < len) p.dg[static_cast<size_t>(cp.bos + i1) * p.HV + hv] = excl + b2;
     }
-    if (lead && in) p.dbeta[rowv] = dbr;
   } while (0);
   if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) tmem_dealloc(tbase, 512);
+  if (w == 0) tmem_dealloc(tbase, 256);
 }
 
 // ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
 template <typename K>
-int launch(K kernel, int grid, size_t smem, cudaStream_t st, const Params& p) {
+int launch(K kernel, int grid, size_t smem, cudaStream_t st, const Params& p, int threads = 128) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return KATA_ERR_CUDA;
-  kernel<<<grid, 128, smem, st>>>(p);
+  kernel<<<grid, threads, smem, st>>>(p);
   return from_cuda(cudaGetLastError());
 }
 template <typename K>
@@ -1436,7 +1423,7 @@ int bwd_typed(const Params& p, bool reuse, cudaStream_t st) {
   }
   if (!e) e = launch2(gdn_tc_dvl_kernel<T>, pairs, smem_of(sizeof(DvlSmem)), st, p, items);
   if (!e) e = launch(gdn_tc_dstate_kernel<T>, 2 * p.N * p.HV, smem_of(sizeof(DstateSmem)), st, p);
-  if (!e) e = launch(gdn_tc_grad_kernel<T>, p.NC * p.HV, smem_of(sizeof(GradSmem)), st, p);
+  if (!e) e = launch(gdn_tc_grad_kernel<T>, p.NC * p.HV, smem_of(sizeof(GradSmem)), st, p, 256);
   return e;
 }
 
@@ -1519,6 +1506,7 @@ int gdn_tc_bwd(const kata_gdn_bwd_args* a, cudaStream_t st) {
   p.scale = a->scale;
   p.a_given = 1;
   p.gva = a->HV != a->H;
+  p.grad16 = a->grad_dtype != KATA_DTYPE_F32;
   bind(p, a->workspace, w, true, a->fwd_workspace);
   return a->dtype == KATA_DTYPE_BF16 ? bwd_typed<__nv_bfloat16>(p, reuse, st) : bwd_typed<__half>(p, reuse, st);
 }

@@ -104,7 +104,7 @@ def _fwd(q, k, v, g, beta, scale, h0, want_final, tables):
     return o, A, ht, ws
 
 
-def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=None):
+def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=None, grad16=False):
     dev = _lib.require_cuda(q, k, v, g, beta, A, h0, do, dht)
     K0, V0 = q.shape[-1], v.shape[-1]
     dt = _dtype(q, k, v)
@@ -116,9 +116,13 @@ def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=None):
     HV, V = v.shape[2], v.shape[3]
     N, NC, cu, co = tables
     f32 = dict(device=dev, dtype=torch.float32)
-    dq = torch.empty(B, T, H, K, **f32)
-    dk = torch.empty(B, T, H, K, **f32)
-    dv = torch.empty(B, T, HV, V, **f32)
+    # 16-bit gradients straight from the tensor-core kernels (no fp32 round trip) when they run and no
+    # value-head group accumulates into a shared q/k head
+    grad16 = grad16 and dt != torch.float32 and ALGO != "simt" and HV == H
+    gq = dict(device=dev, dtype=dt if grad16 else torch.float32)
+    dq = torch.empty(B, T, H, K, **gq)
+    dk = torch.empty(B, T, H, K, **gq)
+    dv = torch.empty(B, T, HV, V, **gq)
     dg = torch.empty(B, T, HV, **f32)
     db = torch.empty(B, T, HV, **f32)
     dh0 = torch.empty(N, HV, K, V, **f32) if h0 is not None else None
@@ -129,7 +133,7 @@ def _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=None):
         dv=dv.data_ptr(), dg=dg.data_ptr(), dbeta=db.data_ptr(), dh0=_lib.ptr(dh0), cu_seqlens=_lib.ptr(cu),
         chunk_offsets=_lib.ptr(co), workspace=None, workspace_bytes=0, fwd_workspace=_lib.ptr(fwd_ws),
         dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HV=HV, K=K, V=V, N=N, num_chunks=NC, scale=float(scale),
-        algo=_lib.ALGO[ALGO])
+        algo=_lib.ALGO[ALGO], grad_dtype=_lib.DTYPE[dt] if grad16 else 0)
     L = _lib.lib()
     ws = torch.empty(int(L.kata_gdn_bwd_workspace_bytes(a)), device=dev, dtype=torch.uint8)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -178,8 +182,10 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
         qc, kc, vc, gc, bc, A, h0, ws = ctx.saved_tensors
         if dht is not None and ctx.transpose_state_layout:
             dht = dht.transpose(-1, -2)
-        dq, dk, dv, dg, db, dh0 = _bwd(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables, fwd_ws=ws)
         tq, tk, tv, tg, tb, th = ctx.dtypes
+        same = tq == tk == tv == qc.dtype
+        dq, dk, dv, dg, db, dh0 = _bwd(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables, fwd_ws=ws,
+                                       grad16=same)
         if dh0 is not None:
             dh0 = (dh0.transpose(-1, -2) if ctx.transpose_state_layout else dh0).to(th)
         return (dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), db.to(tb), None, dh0, None, None, None, None, None,
