@@ -462,6 +462,7 @@ template <typename T>
 int dispatch_dims(const AttnFwdParams& p, bool sum, cudaStream_t st) {
   if (p.D == 128 && p.Dv == 128) return dispatch_m<T, 128, 128>(p, sum, st);
   if (p.D == 64 && p.Dv == 64) return dispatch_m<T, 64, 64>(p, sum, st);
+  if (p.D == 128 && p.Dv == 64) return dispatch_m<T, 128, 64>(p, sum, st);
   return KATA_ERR_UNSUPPORTED;
 }
 
@@ -469,7 +470,8 @@ int dispatch_dims(const AttnFwdParams& p, bool sum, cudaStream_t st) {
 
 bool tc_fwd_supported(int dtype, int D, int Dv, int M, bool sum) {
   if (dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return false;
-  if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128))) return false;
+  // (128, 64): the offset-gated heads of the 200M geometry (M groups of 16 padded to 32, v of 64)
+  if (!((D == 64 && Dv == 64) || (D == 128 && Dv == 128) || (D == 128 && Dv == 64))) return false;
   if (!(M == 1 || M == 2 || M == 4 || M == 8) || D % M) return false;
   if ((D / M) % 16) return false;
   if (sum && M * M > 16) return false;

@@ -134,6 +134,35 @@ def test_config1_fp32(M, variant):
 
 
 # --------------------------------------------------------------------------------------------
+# offset gate at the 200M geometry on the tensor cores: 64-wide heads, M = 4 groups of 16, each
+# packed with the offset to 32 (kata/layer.py:268-282) -> q/k 128 wide, v 64 wide
+# --------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("HQ,H,decay", [(2, 2, False), (4, 2, False), (2, 2, True)])
+def test_offset_gate_bf16_tensor_cores(HQ, H, decay):
+    from linatt_b200 import _lib
+
+    pka = _pka("auto")
+    B, T, M = 2, 300, 4
+    q, k, v, c, do = draw(31 + HQ, B, T, HQ, H, 64, 64, torch.float32)
+    g = torch.Generator().manual_seed(5)
+    off = torch.sigmoid(torch.randn(B, T, HQ, generator=g))
+    # the packing appends off_t to each query group and 1 to each key group (per key head: the
+    # offset of the head's first query head, as the layer's GQA layout would give it)
+    qn, _ = ko.augment_offset(q.numpy(), q.numpy(), off.numpy(), M)
+    _, kn = ko.augment_offset(k.numpy(), k.numpy(), off[:, :, ::HQ // H].contiguous().numpy(), M)
+    qb, kb, vb, dob = (torch.from_numpy(x).bfloat16() if isinstance(x, np.ndarray) else x.bfloat16()
+                       for x in (qn, kn, v, do))
+    assert qb.shape[-1] == 128 and vb.shape[-1] == 64
+    a = _lib.AttnFwdArgs(dtype=1, B=B, T=T, H=H, HQ=HQ, D=128, Dv=64, M=M, score=0, algo=0, scale=1.0,
+                         c=16 if decay else None)
+    assert _lib.lib().kata_attn_algo(a) == 1  # the tcgen05 kernels, not the fp32 CUDA-core fallback
+    cc = c if decay else None
+    got = run(pka, qb, kb, vb, dob, M, "concat", cc)
+    ref = oracle(qb.float(), kb.float(), vb.float(), dob.float(), M, "concat", cc)
+    assert_close(got, ref, 1e-2)
+
+
+# --------------------------------------------------------------------------------------------
 # bf16 / fp16 tensor-core kernels: shapes, ragged T, GQA, sum, decay
 # --------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
