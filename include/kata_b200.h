@@ -339,6 +339,28 @@ KATA_API int kata_sp_combine(const void* o_local, const float* den_local, const 
 KATA_API int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in, void* W1, int dtype, int B, int T,
                               int H, int Dv, int ldw, kata_stream_t stream);
 
+/* Quadratic-feature contractions on the tensor cores, psi formed in shared memory (never written to
+ * global memory).  psi is the concat map above (F = M E^2), or for score == KATA_SCORE_SUM in
+ * kata_sp_state the sum map psi[a,b] = scale sum_g x_{g,a} x_{g,b} (F = E^2).  x is a (B,T,H,D) 16-bit
+ * token tensor (q or k) with E = D / M in {16, 32} and D in {64, 128} (sum score: M <= 4); W is
+ * (B*H, T, ldw) bf16 and P^T (B*H, ldw, F) bf16, ldw a multiple of 8, <= 144.  All pointers 16-byte
+ * aligned.  No counterpart in the reference (these replace GEMMs on a materialised psi).
+ *   kata_sp_state:  S[f, n] = sum_t psi(x_t)[f] W[t, n] for W of H*G heads (W head w reads x head w / G),
+ *                   stored as S^T (B*H*G, ldw, F) fp32 (trans = 1) or S (B*H*G, F, lds) fp32 (trans = 0;
+ *                   columns ldw..lds-1 zeroed, lds % 4 == 0)
+ *   kata_sp_apply:  Y[t, n] = sum_f psi(x_t)[f] P[f, n] for x of H heads and P of H/G heads (x head h reads
+ *                   P head h / G); dv_mode 0 stores Y (B*H, T, ldw) fp32, dv_mode 1 adds Y[:, :Dv] into
+ *                   dv (B,T,H,Dv) fp32 (passed as Y)
+ *   kata_sp_grad:   dx[t, g E + a] += factor * sum_b (W P^T)[t, (g,a,b)] x[t, g E + b]  (dx (B,T,H,D)
+ *                   fp32; for a P symmetric in (a, b) and factor = 2 scale this is the gradient of psi;
+ *                   F a multiple of 256) */
+KATA_API int kata_sp_state(const void* x, const void* W, float* S, int dtype, int B, int T, int H, int G, int D,
+                           int M, int score, int ldw, float scale, int trans, int lds, kata_stream_t stream);
+KATA_API int kata_sp_apply(const void* x, const void* P, float* Y, int dtype, int B, int T, int H, int G, int D,
+                           int M, int ldw, float scale, int dv_mode, int Dv, kata_stream_t stream);
+KATA_API int kata_sp_grad(const void* W, const void* P, const void* x, float* dx, int dtype, int B, int T, int H,
+                          int D, int M, int ldw, float factor, kata_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Decode (generation) step of KATA-SPD attention.  No counterpart in the reference: its
  * quadratic-feature branch keeps no recurrent state (kata/layer.py:421-492 sets final_state = None;

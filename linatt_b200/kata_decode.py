@@ -95,19 +95,32 @@ def kata_attn_state(k, v, num_groups=4, scale=None, score="concat", c=None, HQ=N
     if D % num_groups:
         raise ValueError(f"head dim {D} is not a multiple of num_groups={num_groups}")
     scale = _scale(D, num_groups, scale)
-    Rk = state_features(k, num_groups, scale, score)
     V1 = _v1(v, _ldw(v.shape[-1]))
-    if c is None:
-        return torch.bmm(Rk.transpose(1, 2), V1, out_dtype=torch.float32)
-    HQ = c.shape[2] if HQ is None else HQ
-    if c.shape != (B, T, HQ) or HQ % H:
-        raise ValueError(f"c must be (B, T, HQ) with HQ a multiple of H={H}, got {tuple(c.shape)}")
-    G = HQ // H
-    w = torch.exp(c[:, -1:, :].float() - c.float())  # (B, T, HQ)
-    w = w.permute(0, 2, 1).reshape(B, H, G, T, 1)
-    V1w = (V1.view(B, H, 1, T, -1).float() * w).to(torch.bfloat16).reshape(B * HQ, T, -1)
-    Rkq = Rk.view(B, H, 1, T, -1).expand(B, H, G, T, Rk.shape[-1]).reshape(B * HQ, T, -1)
-    return torch.bmm(Rkq.transpose(1, 2), V1w, out_dtype=torch.float32)
+    G = 1
+    if c is not None:
+        HQ = c.shape[2] if HQ is None else HQ
+        if c.shape != (B, T, HQ) or HQ % H:
+            raise ValueError(f"c must be (B, T, HQ) with HQ a multiple of H={H}, got {tuple(c.shape)}")
+        G = HQ // H
+        w = torch.exp(c[:, -1:, :].float() - c.float())  # (B, T, HQ)
+        w = w.permute(0, 2, 1).reshape(B, H, G, T, 1)
+        V1 = (V1.view(B, H, 1, T, -1).float() * w).to(torch.bfloat16).reshape(B * HQ, T, -1)
+    E = D // num_groups
+    ldw = V1.shape[-1]
+    tc = (k.dtype in (torch.bfloat16, torch.float16) and E in (16, 32) and ldw <= 144
+          and (num_groups <= 4 if score == "sum" else D in (64, 128)))
+    if tc:  # psi(K)^T V1 on the tensor cores, psi formed in shared memory (kata_sp_state)
+        F = E * E if score == "sum" else num_groups * E * E
+        kc = k.contiguous()
+        S = torch.empty(B * H * G, F, ldw, device=k.device, dtype=torch.float32)
+        _lib.check(_lib.lib().kata_sp_state(kc.data_ptr(), V1.data_ptr(), S.data_ptr(), _lib.DTYPE[k.dtype], B, T, H,
+                                            G, D, num_groups, _lib.SCORE[score], ldw, float(scale), 0, ldw,
+                                            _lib.stream_handle(k.device)), "kata_sp_state")
+        return S
+    Rk = state_features(k, num_groups, scale, score)
+    if G > 1:
+        Rk = Rk.view(B, H, 1, T, -1).expand(B, H, G, T, Rk.shape[-1]).reshape(B * H * G, T, -1)
+    return torch.bmm(Rk.transpose(1, 2), V1, out_dtype=torch.float32)
 
 
 def _combine(q, o_loc, den_loc, XY):

@@ -14,9 +14,13 @@ over ranks in the forward and an exclusive suffix of its gradient in the backwar
 all-gather issued before the shard-local attention kernel so that it overlaps it.
 
 The shard-local backward is the single-GPU kernel run with the final o and D: its
-dA = (dO.v - <dO,o>) / D is then exactly the local block of the full gradient.  Feature expansion,
-its gradient contraction and the combine step are kernels of ``libkata_b200.so``; the F-wide
-contractions are bf16 GEMMs with fp32 output (cuBLAS through torch.bmm).
+dA = (dO.v - <dO,o>) / D is then exactly the local block of the full gradient.  The F-wide
+contractions (the state psi(K)^T [V|1], the prefix term psi(Q) P, their gradients psi(Q)^T W1,
+psi(K) dS and the contractions of W1 P^T, [V|1] dS^T back to dq, dk) are tcgen05 kernels of
+``libkata_b200.so`` that form psi tiles in shared memory (``kata_sp_state`` / ``_apply`` /
+``_grad``); psi is never written to global memory.  States are kept transposed, (B*H, ldw, F).
+Head widths outside those kernels' envelope (E = D/M not in {16, 32}) take the earlier route:
+materialised psi (``kata_sp_features``) and bf16 GEMMs with fp32 output (torch.bmm).
 """
 
 from __future__ import annotations
@@ -107,26 +111,80 @@ def _scale(D, M, scale):
     return 1.0 / math.sqrt(D // M) if scale is None else float(scale)
 
 
+def _tc_ok(x, num_groups, ldw):
+    """The feature-contraction kernels cover 16-bit inputs with E = D/M in {16, 32}, D in {64, 128}."""
+    D = x.shape[-1]
+    return (x.dtype in (torch.bfloat16, torch.float16) and D in (64, 128) and D % num_groups == 0
+            and D // num_groups in (16, 32) and ldw <= 144)
+
+
+def _state(x, W, num_groups, scale):
+    """S^T (B*H, ldw, F) fp32 = (psi(x)^T W)^T for x (B,T,H,D) and W (B*H, T, ldw) bf16."""
+    x = x.contiguous()
+    B, T, H, D = x.shape
+    ldw = W.shape[-1]
+    F = num_groups * (D // num_groups) ** 2
+    if not _tc_ok(x, num_groups, ldw):
+        R = _features(x, num_groups, scale)
+        return torch.bmm(W.transpose(1, 2), R, out_dtype=torch.float32)
+    S = torch.empty(B * H, ldw, F, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.lib().kata_sp_state(x.data_ptr(), W.data_ptr(), S.data_ptr(), _lib.DTYPE[x.dtype], B, T, H, 1, D,
+                                        num_groups, _lib.SCORE["concat"], ldw, float(scale), 1, ldw,
+                                        _lib.stream_handle(x.device)), "kata_sp_state")
+    return S
+
+
+def _apply(x, Pt, num_groups, scale, dv=None):
+    """Y (B*H, T, ldw) fp32 = psi(x) P for P^T = Pt (B*H, ldw, F) bf16; with ``dv`` (B,T,H,Dv) fp32,
+    adds Y[..., :Dv] into it instead (returns None)."""
+    x = x.contiguous()
+    B, T, H, D = x.shape
+    ldw = Pt.shape[1]
+    if not _tc_ok(x, num_groups, ldw):
+        Y = torch.bmm(_features(x, num_groups, scale), Pt.transpose(1, 2), out_dtype=torch.float32)
+        if dv is None:
+            return Y
+        Dv = dv.shape[-1]
+        dv += Y[..., :Dv].reshape(B, H, T, Dv).permute(0, 2, 1, 3)
+        return None
+    Y = dv if dv is not None else torch.empty(B * H, T, ldw, device=x.device, dtype=torch.float32)
+    _lib.check(_lib.lib().kata_sp_apply(x.data_ptr(), Pt.data_ptr(), Y.data_ptr(), _lib.DTYPE[x.dtype], B, T, H, 1, D,
+                                        num_groups, ldw, float(scale), int(dv is not None),
+                                        dv.shape[-1] if dv is not None else 0, _lib.stream_handle(x.device)),
+               "kata_sp_apply")
+    return None if dv is not None else Y
+
+
+def _grad(W, Pt, x, dx, num_groups, scale):
+    """dx (B,T,H,D) fp32 += the gradient through psi(x) of <W P^T, psi(x)> (factor 2 scale)."""
+    x = x.contiguous()
+    B, T, H, D = x.shape
+    ldw = W.shape[-1]
+    if not _tc_ok(x, num_groups, ldw):
+        G = torch.bmm(W, Pt)  # (B*H, T, F) bf16
+        _contract(G, x, dx, num_groups, scale)
+        return
+    _lib.check(_lib.lib().kata_sp_grad(W.data_ptr(), Pt.data_ptr(), x.data_ptr(), dx.data_ptr(), _lib.DTYPE[x.dtype],
+                                       B, T, H, D, num_groups, ldw, 2.0 * float(scale), _lib.stream_handle(x.device)),
+               "kata_sp_grad")
+
+
 def sp_forward_local(q, k, v, num_groups, scale, want_state=True):
     """Shard-local causal attention and this shard's state contribution.
-    Returns (o_local, den_local, S) with S = psi(K)^T [V | 1] (B*H, F, ldw) fp32 (None if not wanted)."""
+    Returns (o_local, den_local, S) with S^T = (psi(K)^T [V | 1])^T (B*H, ldw, F) fp32 (None if not wanted)."""
     scale = _scale(q.shape[-1], num_groups, scale)
-    S = None
-    if want_state:
-        Rk = _features(k, num_groups, scale)
-        S = torch.bmm(Rk.transpose(1, 2), _v1(v, _ldw(v.shape[-1])), out_dtype=torch.float32)
-        del Rk
+    S = _state(k, _v1(v, _ldw(v.shape[-1])), num_groups, scale) if want_state else None
     o_loc, den = pka._fwd(q, k, v, num_groups, scale, "concat")
     return o_loc, den, S
 
 
 def sp_forward_combine(q, o_loc, den_loc, P, num_groups, scale):
-    """Final (o, D) of a shard from its local result and the prefix state P (None: first shard)."""
+    """Final (o, D) of a shard from its local result and the prefix state P^T (None: first shard)."""
     if P is None:
         return o_loc, den_loc
     scale = _scale(q.shape[-1], num_groups, scale)
     B, T, H, Dv = o_loc.shape
-    XY = torch.bmm(_features(q, num_groups, scale), P.to(torch.bfloat16), out_dtype=torch.float32)
+    XY = _apply(q, P.to(torch.bfloat16), num_groups, scale)
     o = torch.empty_like(o_loc)
     D = torch.empty_like(den_loc)
     _lib.check(_lib.lib().kata_sp_combine(o_loc.data_ptr(), den_loc.data_ptr(), XY.data_ptr(), o.data_ptr(),
@@ -136,7 +194,8 @@ def sp_forward_combine(q, o_loc, den_loc, P, num_groups, scale):
 
 
 def sp_backward_prep(q, o, D, do, num_groups, scale, want_dP=True):
-    """W1 = [dO/D' | -<dO,o>/D' | 0] and this shard's gradient of its prefix state, dP = psi(Q)^T W1."""
+    """W1 = [dO/D' | -<dO,o>/D' | 0] and this shard's gradient of its prefix state, dP^T with
+    dP = psi(Q)^T W1."""
     B, T, H, Dv = o.shape
     ldw = _ldw(Dv)
     W1 = torch.empty(B * H, T, ldw, device=o.device, dtype=torch.bfloat16)
@@ -145,28 +204,20 @@ def sp_backward_prep(q, o, D, do, num_groups, scale, want_dP=True):
                "kata_sp_bwd_prep")
     dP = None
     if want_dP:
-        scale = _scale(q.shape[-1], num_groups, scale)
-        dP = torch.bmm(_features(q, num_groups, scale).transpose(1, 2), W1, out_dtype=torch.float32)
+        dP = _state(q, W1, num_groups, _scale(q.shape[-1], num_groups, scale))
     return W1, dP
 
 
 def sp_backward_cross(q, k, v, W1, P, dS, dq, dk, dv, num_groups, scale):
-    """Adds to the fp32 dq, dk, dv of a shard the prefix term (through P, the bf16 prefix state)
-    and the state term (through dS = the sum of later shards' dP)."""
+    """Adds to the fp32 dq, dk, dv of a shard the prefix term (through P^T, the bf16 prefix state)
+    and the state term (through dS^T = the sum of later shards' dP^T)."""
     scale = _scale(q.shape[-1], num_groups, scale)
-    B, T, H, Dv = v.shape
     if P is not None:
-        dRq = torch.bmm(W1, P.to(torch.bfloat16).transpose(1, 2))  # (B*H, T, F) bf16
-        _contract(dRq, q, dq, num_groups, scale)
-        del dRq
+        _grad(W1, P.to(torch.bfloat16), q, dq, num_groups, scale)
     if dS is not None:
         dSb = dS.to(torch.bfloat16)
-        Rk = _features(k, num_groups, scale)
-        dvs = torch.bmm(Rk, dSb, out_dtype=torch.float32)[..., :Dv]
-        dv += dvs.reshape(B, H, T, Dv).permute(0, 2, 1, 3)
-        del Rk, dvs
-        dRk = torch.bmm(_v1(v, W1.shape[-1]), dSb.transpose(1, 2))  # (B*H, T, F) bf16
-        _contract(dRk, k, dk, num_groups, scale)
+        _apply(k, dSb, num_groups, scale, dv=dv)
+        _grad(_v1(v, W1.shape[-1]), dSb, k, dk, num_groups, scale)
 
 
 def sp_backward_local(q, k, v, o, D, do, num_groups, scale):
@@ -196,11 +247,9 @@ class SPKataAttnFunction(torch.autograd.Function):
         last = rank == world - 1
         # state first, so that its all-gather overlaps the shard-local attention kernel
         if not last:
-            Rk = _features(k, num_groups, scale)
-            S = torch.bmm(Rk.transpose(1, 2), _v1(v, _ldw(Dv)), out_dtype=torch.float32)
-            del Rk
+            S = _state(k, _v1(v, _ldw(Dv)), num_groups, scale)
         else:  # the last shard's state feeds nobody
-            S = torch.zeros(B * H, F, _ldw(Dv), device=q.device, dtype=torch.float32)
+            S = torch.zeros(B * H, _ldw(Dv), F, device=q.device, dtype=torch.float32)
         pending = gather_states(S, group, async_op=True)
         o_loc, den_loc = pka._fwd(q, k, v, num_groups, scale, "concat")
         P = exclusive_prefix_sum(pending.wait(), rank)
@@ -217,7 +266,7 @@ class SPKataAttnFunction(torch.autograd.Function):
         W1, dP = sp_backward_prep(q, o, D, do, ctx.num_groups, ctx.scale, want_dP=ctx.rank > 0)
         if dP is None:  # the first shard's prefix gradient feeds nobody
             F = ctx.num_groups * (q.shape[-1] // ctx.num_groups) ** 2
-            dP = torch.zeros(W1.shape[0], F, W1.shape[-1], device=q.device, dtype=torch.float32)
+            dP = torch.zeros(W1.shape[0], W1.shape[-1], F, device=q.device, dtype=torch.float32)
         pending = gather_states(dP, ctx.group, async_op=True)
         dq, dk, dv = sp_backward_local(q, k, v, o, D, do, ctx.num_groups, ctx.scale)
         dS = exclusive_suffix_sum(pending.wait(), ctx.rank)

@@ -155,3 +155,28 @@ def test_product_path_refuses_cpu_tensors():
 
     with pytest.raises(RuntimeError, match="CUDA"):
         flash_delta(q, q, q, q[..., 0], 4)
+
+
+def test_binding_signatures_match_the_header(L):
+    """Every entry point the ctypes binding types has the header's parameter kinds, in order
+    (pointer / int / float): a miscounted argument list would pass garbage through the C ABI."""
+    import re
+
+    from linatt_b200 import _lib
+
+    header = (ROOT / "include" / "kata_b200.h").read_text()
+    checked = 0
+    for m in re.finditer(r"KATA_API\s+[\w\s\*]+?\b(kata_\w+)\s*\((.*?)\);", header, re.S):
+        name, params = m.group(1), m.group(2).strip()
+        fn = getattr(L, name)
+        if fn.argtypes is None:
+            continue
+        kinds = "" if params in ("", "void") else "".join(
+            "p" if ("*" in x or "kata_stream_t" in x) else ("f" if x.strip().startswith("float") else "i")
+            for x in params.split(","))
+        bound = "".join("f" if t is _lib.c_float else ("p" if t in (_lib.c_void_p, ) or hasattr(t, "_type_")
+                                                       and not t in (_lib.c_int, _lib.c_size_t) else "i")
+                        for t in fn.argtypes)
+        assert kinds == bound, f"{name}: header {kinds} vs binding {bound}"
+        checked += 1
+    assert checked >= 15

@@ -1,0 +1,141 @@
+"""The quadratic-feature contractions on the tensor cores (kata_sp_state / kata_sp_apply /
+kata_sp_grad) against torch fp32 on the same operands: psi rounded to bf16 exactly as the kernels
+form it in shared memory (product first, then the scale), W and P^T in bf16.  The kernels sum in
+fp32 in another order than torch, so they agree to fp32 rounding (rel-L2 <= 1e-5).  Covers both
+head widths (E = 16, 32), both row widths of [v | 1 | 0] (ldw 72 and 136 -> N 80 and 144), ragged
+token counts, the transposed and the decode layouts of the state, grouped heads (G = 2), the sum
+score's state, and the dv-accumulating form of apply."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def psi(x, M, scale, score="concat"):
+    """(B,T,H,D) -> (B*H, T, F) bf16, the kernels' feature map."""
+    B, T, H, D = x.shape
+    E = D // M
+    xg = x.float().view(B, T, H, M, E)
+    if score == "sum":
+        R = torch.einsum("bthga,bthgc->bhtac", xg, xg).mul_(scale).reshape(B * H, T, E * E)
+    else:
+        R = (xg[..., :, None] * xg[..., None, :]).mul_(scale).permute(0, 2, 1, 3, 4, 5).reshape(B * H, T, M * E * E)
+    return R.to(torch.bfloat16)
+
+
+def rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / b.norm())
+
+
+def draw(B, T, H, D, ldw, seed, dtype=torch.bfloat16):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = (torch.randn(B, T, H, D, device="cuda", generator=g) / D ** 0.5).to(dtype)
+    W = torch.randn(B * H, T, ldw, device="cuda", generator=g).bfloat16()
+    return x, W
+
+
+@pytest.mark.parametrize("B,T,H,D,M,ldw,score,trans,G", [
+    (1, 300, 2, 128, 4, 136, "concat", 1, 1),
+    (2, 64, 1, 64, 4, 72, "concat", 1, 1),
+    (1, 200, 2, 128, 8, 136, "concat", 0, 1),
+    (1, 130, 2, 64, 2, 136, "concat", 0, 2),
+    (2, 257, 1, 128, 4, 136, "sum", 0, 1),
+    (1, 100, 2, 64, 4, 72, "sum", 0, 2),
+])
+def test_state_matches_torch(B, T, H, D, M, ldw, score, trans, G):
+    from linatt_b200 import _lib
+
+    scale = 0.37
+    x, W = draw(B, T, H, D, ldw, 11 + T)
+    W = torch.randn(B * H * G, T, ldw, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3)).bfloat16()
+    R = psi(x, M, scale, score).float()  # (B*H, T, F)
+    F = R.shape[-1]
+    Rg = R.view(B, H, 1, T, F).expand(B, H, G, T, F).reshape(B * H * G, T, F)
+    ref = torch.bmm(Rg.transpose(1, 2), W.float())  # (B*H*G, F, ldw)
+    lds = ldw + 4
+    S = torch.full((B * H * G, ldw, F) if trans else (B * H * G, F, lds), float("nan"), device="cuda")
+    _lib.check(_lib.lib().kata_sp_state(x.data_ptr(), W.data_ptr(), S.data_ptr(), 1, B, T, H, G, D, M,
+                                        _lib.SCORE[score], ldw, scale, trans, lds,
+                                        torch.cuda.current_stream().cuda_stream), "kata_sp_state")
+    torch.cuda.synchronize()
+    got = S.transpose(1, 2) if trans else S[..., :ldw]
+    assert torch.isfinite(S).all()
+    # the sum score's features add M products before their bf16 rounding, in fp32 in the kernel and
+    # in another order in torch: a few of them round to neighbouring bf16 values (1e-4 bound)
+    assert rel(got, ref) < (1e-4 if score == "sum" else 1e-5)
+    if not trans:
+        assert torch.count_nonzero(S[..., ldw:]) == 0
+
+
+@pytest.mark.parametrize("B,T,H,D,M,ldw,G,dv_mode", [
+    (1, 300, 2, 128, 4, 136, 1, 0),
+    (2, 64, 2, 64, 4, 72, 2, 0),
+    (1, 257, 1, 128, 8, 136, 1, 1),
+    (1, 129, 2, 64, 2, 72, 1, 1),
+])
+def test_apply_matches_torch(B, T, H, D, M, ldw, G, dv_mode):
+    from linatt_b200 import _lib
+
+    scale = 0.61
+    x, _ = draw(B, T, H, D, ldw, 5 + T)
+    R = psi(x, M, scale).float()
+    F = R.shape[-1]
+    Pt = (torch.randn(B * (H // G), ldw, F, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
+          / F ** 0.5).bfloat16()
+    Pg = Pt.float().view(B, H // G, 1, ldw, F).expand(B, H // G, G, ldw, F).reshape(B * H, ldw, F)
+    ref = torch.bmm(R, Pg.transpose(1, 2))  # (B*H, T, ldw)
+    st = torch.cuda.current_stream().cuda_stream
+    if dv_mode:
+        Dv = ldw - 8
+        dv0 = torch.randn(B, T, H, Dv, device="cuda")
+        dv = dv0.clone()
+        _lib.check(_lib.lib().kata_sp_apply(x.data_ptr(), Pt.data_ptr(), dv.data_ptr(), 1, B, T, H, G, D, M, ldw,
+                                            scale, 1, Dv, st), "kata_sp_apply")
+        torch.cuda.synchronize()
+        want = dv0 + ref[..., :Dv].reshape(B, H, T, Dv).permute(0, 2, 1, 3)
+        assert rel(dv - dv0, want - dv0) < 1e-5
+    else:
+        Y = torch.full((B * H, T, ldw), float("nan"), device="cuda")
+        _lib.check(_lib.lib().kata_sp_apply(x.data_ptr(), Pt.data_ptr(), Y.data_ptr(), 1, B, T, H, G, D, M, ldw,
+                                            scale, 0, 0, st), "kata_sp_apply")
+        torch.cuda.synchronize()
+        assert torch.isfinite(Y).all()
+        assert rel(Y, ref) < 1e-5
+
+
+@pytest.mark.parametrize("B,T,H,D,M,ldw", [(1, 300, 2, 128, 4, 136), (2, 64, 1, 64, 4, 72), (1, 257, 1, 128, 8, 136),
+                                           (1, 130, 2, 64, 2, 72)])
+def test_grad_matches_torch(B, T, H, D, M, ldw):
+    from linatt_b200 import _lib
+
+    scale = 0.5
+    x, W = draw(B, T, H, D, ldw, 21 + T)
+    E = D // M
+    F = M * E * E
+    # a P symmetric in (a, b), as every state is
+    P = torch.randn(B * H, ldw, M, E, E, device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+    Pt = ((P + P.transpose(-1, -2)) / (2 * F ** 0.5)).reshape(B * H, ldw, F).bfloat16()
+    G = torch.bmm(W.float(), Pt.float())  # (B*H, T, F) = W P^T
+    Gg = G.view(B, H, T, M, E, E)
+    xg = x.float().view(B, T, H, M, E).permute(0, 2, 1, 3, 4)  # (B, H, T, M, E)
+    ref = 2 * scale * torch.einsum("bhtgab,bhtgb->bhtga", Gg, xg).permute(0, 2, 1, 3, 4).reshape(B, T, H, D)
+    dx0 = torch.randn(B, T, H, D, device="cuda")
+    dx = dx0.clone()
+    _lib.check(_lib.lib().kata_sp_grad(W.data_ptr(), Pt.data_ptr(), x.data_ptr(), dx.data_ptr(), 1, B, T, H, D, M, ldw,
+                                       2 * scale, torch.cuda.current_stream().cuda_stream), "kata_sp_grad")
+    torch.cuda.synchronize()
+    assert rel(dx - dx0, ref) < 1e-5
+
+
+def test_shapes_outside_the_envelope_are_refused():
+    from linatt_b200 import _lib
+
+    L = _lib.lib()
+    # E = 64 (D = 128, M = 2) and ldw > 144 are not covered: the caller takes the materialised route
+    assert L.kata_sp_state(16, 16, 16, 1, 1, 64, 1, 1, 128, 2, 0, 136, 1.0, 1, 136, None) == -3
+    assert L.kata_sp_apply(16, 16, 16, 1, 1, 64, 1, 1, 128, 4, 152, 1.0, 0, 0, None) == -3
+    assert L.kata_sp_grad(16, 16, 16, 16, 0, 1, 64, 1, 128, 4, 136, 1.0, None) == -2
