@@ -489,6 +489,7 @@ def _timed_steps(torch, dist, world, dev, step, K, W):
 
 
 SP_SHAPE = (1, 131072, 16, 128, 4)  # config 4: B, T, H, D=Dv, M
+SP_SEQ = 0  # --sp-seq: a shorter sequence, only for profiler captures
 
 
 def sp_flops() -> float:
@@ -496,7 +497,7 @@ def sp_flops() -> float:
     return 7 * Bs * Hs * 2.0 * pairs(Ts) * Ds  # 7 GEMM-equivalents of the whole causal problem
 
 
-def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int, emulate: int = 0) -> dict:
     """Config 4 (B=1, T=131072, H=16, D=Dv=128, M=4 concat, bf16), T split contiguously over the
     ranks (strong scaling); one step = forward + backward through sp_kata_attn.  Besides the step
     time: the NCCL all-gather of one state-sized buffer alone (each step runs two, one per
@@ -504,10 +505,12 @@ def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int)
     shard-local flash forward + backward alone.  Every rank runs the same collectives in the same
     order.  Returns the `sp` object of the JSON line (meaningful on rank 0)."""
     from linatt_b200 import parallel_kata_attn as pka
-    from linatt_b200.sequence_parallel import gather_states, sp_kata_attn
+    from linatt_b200.sequence_parallel import gather_states, sp_emulate, sp_kata_attn
 
     Bs, Ts, Hs, Ds, Ms = SP_SHAPE
-    Tl = Ts // world
+    if SP_SEQ:
+        Ts = SP_SEQ
+    Tl = Ts // world if not emulate else Ts
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     sets = []
     for _ in range(2):
@@ -516,6 +519,9 @@ def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int)
 
     def step(i):
         q, k, v, do = sets[i % 2]
+        if emulate:  # all R shards one after another on this GPU (exchange formed locally)
+            sp_emulate(q, k, v, do, emulate, Ms)
+            return
         leaves = [x.requires_grad_(True) for x in (q, k, v)]
         o = sp_kata_attn(*leaves, num_groups=Ms)
         o.backward(do)
@@ -527,6 +533,8 @@ def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int)
 
     def local(i):  # the shard-local flash kernels alone (what the exchange overlaps)
         q, k, v, do = sets[i % 2]
+        if emulate:
+            q, k, v, do = (x[:, : Ts // emulate] for x in (q, k, v, do))
         o, den = pka._fwd(q, k, v, Ms, None, "concat")
         pka._bwd(q, k, v, o, den, do, Ms, None, "concat")
 
@@ -544,7 +552,9 @@ def sp_measure(torch, dist, world: int, rank: int, dev, steps: int, warmup: int)
     return {
         "workload": "sequence-parallel KATA-SPD fwd+bwd, concat M=4, causal, bf16 (config 4)",
         "global_batch": Bs, "seq_len": Ts, "heads": Hs, "head_dim": Ds, "num_groups": Ms,
-        "parallelism": f"contiguous T split x{world}" + (", prefix state all-gather over NCCL" if world > 1 else ""),
+        "parallelism": (f"contiguous T split x{emulate}, shards run in turn on one GPU (emulated exchange)"
+                        if emulate else f"contiguous T split x{world}"
+                        + (", prefix state all-gather over NCCL" if world > 1 else "")),
         "scaling": "strong", "steps": steps, "warmup": warmup, "ms_per_step": step_ms,
         "value": Bs * Ts / (step_ms / 1e3), "unit": UNIT,
         "local_flash_fwd_bwd_ms": local_ms / steps,
@@ -569,7 +579,7 @@ def run_sp(args, rank: int, world: int, local: int) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-    sp = sp_measure(torch, dist, world, rank, dev, args.steps, args.warmup)
+    sp = sp_measure(torch, dist, world, rank, dev, args.steps, args.warmup, emulate=args.sp_emulate)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -786,6 +796,10 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-sp", action="store_true", help="skip the config-4 sequence-parallel object of the line")
     ap.add_argument("--sp-steps", type=int, default=6, help="timed steps of the config-4 object (>= 3)")
+    ap.add_argument("--sp-seq", type=int, default=0,
+                    help="--workload sp with a shorter T (config 4 is quoted at 131072; only for profiler captures)")
+    ap.add_argument("--sp-emulate", type=int, default=0,
+                    help="--workload sp on one GPU: run R shards in turn (for profiling the shard kernels)")
     ap.add_argument("--num-groups", type=int, default=4, help="M (the benchmark metric is quoted at M=4)")
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
     ap.add_argument("--decay", action="store_true",
@@ -799,8 +813,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=16,
                     help="B per GPU (the metric is quoted at 16; smaller values only for profiler captures)")
     args = ap.parse_args()
-    global M, SCORE, B, DECAY
-    M, SCORE, B, DECAY = args.num_groups, args.score, args.batch, args.decay
+    global M, SCORE, B, DECAY, SP_SEQ
+    M, SCORE, B, DECAY, SP_SEQ = args.num_groups, args.score, args.batch, args.decay, args.sp_seq
     if DECAY:
         if SCORE != "concat":
             ap.error("--decay pairs with the concat score only (as in the reference)")

@@ -26,7 +26,7 @@ namespace sptc {
 namespace {
 
 constexpr uint32_t kRowB = 128;          // bytes of a 64-element 16-bit row (128-byte swizzle)
-constexpr int kStages = 3;
+constexpr int kStages = 4;  // ring depth of the state / apply pipelines (prefetch distance 2)
 
 __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -158,10 +158,10 @@ __global__ void __launch_bounds__(128, 1) sp_state_kernel(const __grid_constant_
   for (int i = 0; i < nblk && ok; ++i) {
     const int s = i % kStages;
     if (i + 2 < nblk) {
-      // stage (i+2) % 3 held block i-1: its W tile is free once that block's MMAs completed
-      if (tid == 0 && i >= 1) {
+      // stage (i+2) % 4 held block i-2: its W tile is free once that block's MMAs completed
+      if (tid == 0 && i >= 2) {
         WaitCtx wc{p.status, &sm.abort};
-        mbar_wait(&sm.mdone[(i - 1) % kStages], static_cast<uint32_t>(((i - 1) / kStages) & 1), wc);
+        mbar_wait(&sm.mdone[(i - 2) % kStages], static_cast<uint32_t>(((i - 2) / kStages) & 1), wc);
       }
       issue(i + 2);
       cp_async_wait<2>();
@@ -170,8 +170,9 @@ __global__ void __launch_bounds__(128, 1) sp_state_kernel(const __grid_constant_
     } else {
       cp_async_wait<0>();
     }
-    // psi[s] was last read by block i-3's MMAs
-    if (i >= 3 && !(ok = wait_all(&sm.mdone[s], static_cast<uint32_t>(((i - 3) / kStages) & 1), &sm.abort, p.status)))
+    // psi[s] was last read by block i-4's MMAs
+    if (i >= kStages &&
+        !(ok = wait_all(&sm.mdone[s], static_cast<uint32_t>(((i - kStages) / kStages) & 1), &sm.abort, p.status)))
       break;
     __syncthreads();
     {  // row tid of psi[s]: 64 tokens
@@ -324,13 +325,14 @@ __global__ void __launch_bounds__(128, 1) sp_apply_kernel(const __grid_constant_
       const int i = g * BPG + ii;
       const int s = i % kStages;
       if (i + 2 < nblk) {
-        if (tid == 0 && i >= 1) {
+        if (tid == 0 && i >= 2) {  // stage (i+2) % 4 held block i-2
           WaitCtx wc{p.status, &sm.abort};
-          mbar_wait(&sm.mdone[(i - 1) % kStages], static_cast<uint32_t>(((i - 1) / kStages) & 1), wc);
+          mbar_wait(&sm.mdone[(i - 2) % kStages], static_cast<uint32_t>(((i - 2) / kStages) & 1), wc);
         }
         issue(i + 2);
       }
-      if (i >= 3 && !(ok = wait_all(&sm.mdone[s], static_cast<uint32_t>(((i - 3) / kStages) & 1), &sm.abort, p.status)))
+      if (i >= kStages &&
+          !(ok = wait_all(&sm.mdone[s], static_cast<uint32_t>(((i - kStages) / kStages) & 1), &sm.abort, p.status)))
         break;
       {  // row tid of psi[s]: features 64 i .. 64 i + 63 = (g, a0 + j / E, j % E)
         const uint32_t base = smem_u32(sm.psi[s]);
@@ -411,6 +413,7 @@ struct GradSmem {
   static constexpr int NWB = (NW + 63) / 64;
   uint8_t A[NWB][128 * kRowB];
   uint8_t B[2][4][NW * kRowB];
+  float dxs[32][128];  // a group's per-(a, token) results, [a][thread]
   uint64_t afull, bfull[2], mdone[2];
   uint32_t tmem;
   int abort;
@@ -445,19 +448,8 @@ __global__ void __launch_bounds__(128, 1) sp_grad_kernel(const __grid_constant__
     tmem_alloc(&sm.tmem, 512);
     tmem_relinquish();
   }
-  uint32_t xr[D / 2];
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) +
-                                                      ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D);
-#pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 v = tin ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-      xr[4 * c] = v.x;
-      xr[4 * c + 1] = v.y;
-      xr[4 * c + 2] = v.z;
-      xr[4 * c + 3] = v.w;
-    }
-  }
+  // this thread's token row (each group's E values are read when the group starts)
+  const T* xrow = static_cast<const T*>(p.x) + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -495,7 +487,16 @@ __global__ void __launch_bounds__(128, 1) sp_grad_kernel(const __grid_constant__
   constexpr int TPG = EE / 256;  // 256-feature tiles per group
   for (int g = 0; g < p.F / EE && ok; ++g) {
     float xg[E];
-    group_vals<T, E, D>(xr, g, xg);
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(xrow + g * E);
+#pragma unroll
+      for (int c = 0; c < E / 8; ++c) {
+        const uint4 v = tin ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+        const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xg[8 * c + j] = to_f32<T>(e[j]);
+      }
+    }
 #pragma unroll
     for (int ii = 0; ii < TPG; ++ii) {
       const int i = g * TPG + ii;
@@ -519,11 +520,25 @@ __global__ void __launch_bounds__(128, 1) sp_grad_kernel(const __grid_constant__
           float sacc = 0.f;
 #pragma unroll
           for (int j = 0; j < E; ++j) sacc = fmaf(__uint_as_float(r[part * E + j]), xg[j], sacc);
-          if (tin) dxrow[g * E + a] += p.factor * sacc;  // one thread and one tile per element
+          sm.dxs[a][tid] = sacc;  // each a of the group is one tile's: written exactly once
         }
       }
       tc_fence_before();
       __syncthreads();  // the accumulator buffer i & 1 is read: tile i+2's MMAs may overwrite it
+    }
+    if (ok && tin) {  // the group's E values: one read-modify-write of E contiguous floats
+      float4* d4 = reinterpret_cast<float4*>(dxrow + g * E);
+      float4 v[E / 4];
+#pragma unroll
+      for (int c = 0; c < E / 4; ++c) v[c] = d4[c];
+#pragma unroll
+      for (int c = 0; c < E / 4; ++c) {
+        v[c].x = fmaf(p.factor, sm.dxs[4 * c][tid], v[c].x);
+        v[c].y = fmaf(p.factor, sm.dxs[4 * c + 1][tid], v[c].y);
+        v[c].z = fmaf(p.factor, sm.dxs[4 * c + 2][tid], v[c].z);
+        v[c].w = fmaf(p.factor, sm.dxs[4 * c + 3][tid], v[c].w);
+        d4[c] = v[c];
+      }
     }
   }
   if (!ok && tid == 0) {

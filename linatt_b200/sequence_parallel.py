@@ -35,7 +35,7 @@ from . import parallel_kata_attn as pka
 
 __all__ = ["sp_kata_attn", "SPKataAttnFunction", "exclusive_prefix_sum", "exclusive_suffix_sum",
            "gather_states", "sp_forward_local", "sp_forward_combine", "sp_backward_prep", "sp_backward",
-           "sp_backward_local", "sp_backward_cross"]
+           "sp_backward_local", "sp_backward_cross", "sp_emulate"]
 
 
 # ------------------------------------------------------------------------------------------------
@@ -231,6 +231,34 @@ def sp_backward(q, k, v, o, D, do, W1, P, dS, num_groups, scale):
     dq, dk, dv = sp_backward_local(q, k, v, o, D, do, num_groups, scale)
     sp_backward_cross(q, k, v, W1, P, dS, dq, dk, dv, num_groups, scale)
     return dq, dk, dv
+
+
+def sp_emulate(q, k, v, do, R, num_groups, scale=None):
+    """Forward + backward of the sequence-parallel algorithm over R shards of the sequence, run one
+    after another on the current device, with the exchange (exclusive prefix of the states, exclusive
+    suffix of their gradients) formed locally.  Same kernels and arithmetic as R ranks over NCCL;
+    for checking the algorithm and profiling its kernels on one GPU.  Returns (o, D, dq, dk, dv)."""
+    qs, ks, vs, dos = (x.chunk(R, dim=1) for x in (q, k, v, do))
+    loc = [sp_forward_local(qs[r], ks[r], vs[r], num_groups, scale, want_state=r < R - 1) for r in range(R)]
+    states = [S for _, _, S in loc[:-1]]
+    outs, dens, prefixes = [], [], []
+    for r in range(R):
+        P = sum(states[:r]) if r > 0 else None
+        o, D = sp_forward_combine(qs[r], loc[r][0], loc[r][1], P, num_groups, scale)
+        outs.append(o)
+        dens.append(D)
+        prefixes.append(P.to(torch.bfloat16) if P is not None else None)
+    preps = [sp_backward_prep(qs[r], outs[r], dens[r], dos[r].contiguous(), num_groups, scale, want_dP=r > 0)
+             for r in range(R)]
+    grads = []
+    for r in range(R):
+        later = [preps[j][1] for j in range(r + 1, R)]
+        dS = sum(later) if later else None
+        grads.append(sp_backward(qs[r], ks[r], vs[r], outs[r], dens[r], dos[r].contiguous(), preps[r][0],
+                                 prefixes[r], dS, num_groups, scale))
+    cat = lambda xs: torch.cat(xs, dim=1)  # noqa: E731
+    return (cat(outs), cat(dens), cat([g[0] for g in grads]), cat([g[1] for g in grads]),
+            cat([g[2] for g in grads]))
 
 
 # ------------------------------------------------------------------------------------------------

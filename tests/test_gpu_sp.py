@@ -30,27 +30,7 @@ def emulate(q, k, v, do, R, M):
     """Sequence-parallel forward + backward over R emulated ranks on one GPU."""
     from linatt_b200 import sequence_parallel as sp
 
-    qs, ks, vs, dos = (x.chunk(R, dim=1) for x in (q, k, v, do))
-    loc = [sp.sp_forward_local(qs[r], ks[r], vs[r], M, None, want_state=r < R - 1) for r in range(R)]
-    states = [S for _, _, S in loc[:-1]]
-    outs, dens, prefixes = [], [], []
-    for r in range(R):
-        P = sum(states[:r]) if r > 0 else None
-        o, D = sp.sp_forward_combine(qs[r], loc[r][0], loc[r][1], P, M, None)
-        outs.append(o)
-        dens.append(D)
-        prefixes.append(P)
-    preps = [sp.sp_backward_prep(qs[r], outs[r], dens[r], dos[r].contiguous(), M, None, want_dP=r > 0)
-             for r in range(R)]
-    grads = []
-    for r in range(R):
-        later = [preps[j][1] for j in range(r + 1, R)]
-        dS = sum(later) if later else None
-        grads.append(sp.sp_backward(qs[r], ks[r], vs[r], outs[r], dens[r], dos[r].contiguous(), preps[r][0],
-                                    prefixes[r], dS, M, None))
-    cat = lambda xs: torch.cat(xs, dim=1)
-    return (cat(outs), cat(dens), cat([g[0] for g in grads]), cat([g[1] for g in grads]),
-            cat([g[2] for g in grads]))
+    return sp.sp_emulate(q, k, v, do, R, M)
 
 
 def full(q, k, v, do, M):

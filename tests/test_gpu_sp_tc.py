@@ -122,7 +122,7 @@ def test_grad_matches_torch(B, T, H, D, M, ldw):
     G = torch.bmm(W.float(), Pt.float())  # (B*H, T, F) = W P^T
     Gg = G.view(B, H, T, M, E, E)
     xg = x.float().view(B, T, H, M, E).permute(0, 2, 1, 3, 4)  # (B, H, T, M, E)
-    ref = 2 * scale * torch.einsum("bhtgab,bhtgb->bhtga", Gg, xg).permute(0, 2, 1, 3, 4).reshape(B, T, H, D)
+    ref = 2 * scale * torch.einsum("zhtgac,zhtgc->zhtga", Gg, xg).permute(0, 2, 1, 3, 4).reshape(B, T, H, D)
     dx0 = torch.randn(B, T, H, D, device="cuda")
     dx = dx0.clone()
     _lib.check(_lib.lib().kata_sp_grad(W.data_ptr(), Pt.data_ptr(), x.data_ptr(), dx.data_ptr(), 1, B, T, H, D, M, ldw,
