@@ -352,14 +352,15 @@ KATA_API int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in
  *                   P head h / G); dv_mode 0 stores Y (B*H, T, ldw) fp32, dv_mode 1 adds Y[:, :Dv] into
  *                   dv (B,T,H,Dv) fp32 (passed as Y)
  *   kata_sp_grad:   dx[t, g E + a] += factor * sum_b (W P^T)[t, (g,a,b)] x[t, g E + b]  (dx (B,T,H,D)
- *                   fp32; for a P symmetric in (a, b) and factor = 2 scale this is the gradient of psi;
- *                   F a multiple of 256) */
+ *                   fp32; for a P symmetric in (a, b) and factor = 2 scale this is the gradient of psi)
+ * status is the optional device status word (may be NULL) that a timed-out wait writes. */
 KATA_API int kata_sp_state(const void* x, const void* W, float* S, int dtype, int B, int T, int H, int G, int D,
-                           int M, int score, int ldw, float scale, int trans, int lds, kata_stream_t stream);
+                           int M, int score, int ldw, float scale, int trans, int lds, int* status,
+                           kata_stream_t stream);
 KATA_API int kata_sp_apply(const void* x, const void* P, float* Y, int dtype, int B, int T, int H, int G, int D,
-                           int M, int ldw, float scale, int dv_mode, int Dv, kata_stream_t stream);
+                           int M, int ldw, float scale, int dv_mode, int Dv, int* status, kata_stream_t stream);
 KATA_API int kata_sp_grad(const void* W, const void* P, const void* x, float* dx, int dtype, int B, int T, int H,
-                          int D, int M, int ldw, float factor, kata_stream_t stream);
+                          int D, int M, int ldw, float factor, int* status, kata_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Decode (generation) step of KATA-SPD attention.  No counterpart in the reference: its

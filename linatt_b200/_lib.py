@@ -162,11 +162,13 @@ def lib() -> ctypes.CDLL:
             L.kata_selftest_umma.restype = c_int
             L.kata_selftest_umma.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]
             L.kata_sp_state.restype = c_int
-            L.kata_sp_state.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 9 + [c_float, c_int, c_int, c_void_p]
+            L.kata_sp_state.argtypes = ([c_void_p, c_void_p, c_void_p] + [c_int] * 9 +
+                                        [c_float, c_int, c_int, c_void_p, c_void_p])
             L.kata_sp_apply.restype = c_int
-            L.kata_sp_apply.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 8 + [c_float, c_int, c_int, c_void_p]
+            L.kata_sp_apply.argtypes = ([c_void_p, c_void_p, c_void_p] + [c_int] * 8 +
+                                        [c_float, c_int, c_int, c_void_p, c_void_p])
             L.kata_sp_grad.restype = c_int
-            L.kata_sp_grad.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_float, c_void_p]
+            L.kata_sp_grad.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_float, c_void_p, c_void_p]
             L.kata_selftest_umma_m64.restype = c_int
             L.kata_selftest_umma_m64.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 5 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:

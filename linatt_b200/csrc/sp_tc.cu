@@ -7,15 +7,31 @@
 // memory from the 16-bit token rows, rounded to bf16 exactly as a materialised feature tensor would
 // be (product first, then the scale), and feeds them to tcgen05.mma with fp32 accumulation in TMEM.
 //
-//   state  S[f, n]  = sum_t psi(x_t)[f] W[t, n]      M = 128 features, N = NW (the [v | 1 | 0] row
+//   state  S[f, n]  = sum_t psi(x_t)[f] W[t, n]      one CTA per (256 features, head): two M = 128
+//                                                    MMAs per K step, N = NW (the [v | 1 | 0] row
 //                                                    rounded up to 16), K = tokens in blocks of 64
-//   apply  Y[t, n]  = sum_f psi(x_t)[f] P[f, n]      M = 128 tokens, N = NW, K = features (blocks of 64)
+//   apply  Y[t, n]  = sum_f psi(x_t)[f] P[f, n]      one CTA per (256 tokens, head): two M = 128 MMAs,
+//                                                    N = NW, K = features in blocks of 64
 //   grad   dx[t, (g,a)] += c * sum_b (W P^T)[t, (g,a,b)] x[t, (g,b)]
-//                                                    M = 128 tokens, N = 256 features, K = NW
+//                                                    one CTA per (256 features, head, token range):
+//                                                    the P^T slice stays in shared memory, W streams
+//                                                    by 128-token tiles; M = 128, N = 256, K = NW
+// The operand that streams is the one whose reuse the CTA cannot hold: W (tokens) in `state` and
+// `grad`, P^T (features) in `apply`; each CTA makes 256 rows of output per streamed byte, twice the
+// reuse of a single 128-row MMA.
+//
+// Every kernel runs 320 threads: warps 0-7 form psi (or run the epilogue of `grad`), warp 8 issues
+// the TMA loads of a ring of stages, warp 9 issues the MMAs.  Stages are handed over by mbarriers
+// only -- no CTA-wide barrier inside the main loops -- so psi for block i+1 is formed while the MMAs
+// of block i run and the copies of blocks i+2.. are in flight.  Every wait is bounded (2 s); a wait
+// that runs out sets the shared abort flag and the optional device status word, every role leaves
+// its loop, and the CTA waits (bounded) for its own copies and MMAs in flight before it frees TMEM.
+//
 // The state is stored transposed, S^T (B*H, ldw, F) (rows n), so that P^T is the K-major B operand of
 // `apply` and the MN-major B operand of `grad`; the decode path asks `state` for the untransposed
-// (B*H, F, lds) layout instead.  W (B*H, T, ldw) and P^T (B*H, ldw, F) are bf16 and arrive by TMA
-// (no multicast); token rows are read with plain 16-byte loads.  ldw <= 144, a multiple of 8.
+// (B*H, F, lds) layout instead.  W (B*H, T, ldw) and P^T (B*H, ldw, F) are bf16, and the token rows
+// of `state` and `grad` arrive by TMA as well (no multicast); `apply` reads each token's row with
+// plain 16-byte loads.  ldw <= 144, a multiple of 8.
 #include "attn_common.cuh"
 #include "attn_tc_common.cuh"
 #include "host_util.h"
@@ -25,209 +41,236 @@ namespace kata {
 namespace sptc {
 namespace {
 
-constexpr uint32_t kRowB = 128;          // bytes of a 64-element 16-bit row (128-byte swizzle)
-constexpr int kStages = 4;  // ring depth of the state / apply pipelines (prefetch distance 2)
+constexpr uint32_t kRowB = 128;  // bytes of a 64-element 16-bit row (128-byte swizzle)
+constexpr int kCompute = 256;    // psi / epilogue threads: warps 0-7
+constexpr int kProducerWarp = 8;
+constexpr int kIssuerWarp = 9;
+constexpr int kThreads = kCompute + 64;
+constexpr uint32_t kTmemCols = 512;  // two fp32 accumulators of up to 256 columns
 
 __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
 }
-__device__ __forceinline__ uint32_t toff(int r, int c) { return swz_offset(r, c * 2, 128); }
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
           "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-// Uniform bounded wait of all threads of the CTA on one barrier phase; false when any timed out.
-__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
-  WaitCtx wc{status, abort};
-  const bool ok = mbar_wait(bar, parity, wc);
-  return !__syncthreads_or(!ok);
+__device__ __forceinline__ uint32_t par(int phase_index) { return static_cast<uint32_t>(phase_index & 1); }
+
+// Abort path: wait (bounded) for the last phase armed on each barrier of a ring whose uses
+// 0..count-1 went to bars[j % ring], phase j / ring, so that no copy or MMA still writes this CTA's
+// shared memory or TMEM when it exits.
+__device__ void drain_ring(uint64_t* bars, int ring, int count) {
+  for (int k = 1; k <= ring && k <= count; ++k) {
+    const int j = count - k;
+    mbar_drain(&bars[j % ring], par(j / ring));
+  }
 }
 
 struct Params {
-  const void* x;     // (B, T, H, D) 16-bit token rows (q or k)
-  const void* W;     // unused on the device (TMA)
-  float* out;        // state: S^T (B*H, ldw, F) or S (B*H, F, lds);  apply: Y (B*H, T, ldw) or dv (B,T,H,Dv)
-  float* dx;         // grad: (B, T, H, D) fp32, accumulated
-  int* status;
+  const void* x;  // (B, T, H, D) 16-bit token rows (q or k); `apply` reads them directly
+  float* out;     // state: S^T (B*H, ldw, F) or S (B*H, F, lds);  apply: Y (B*H, T, ldw) or dv (B,T,H,Dv)
+  float* dx;      // grad: (B, T, H, D) fp32, accumulated
+  int* status;    // optional device status word
   int B, T, H, D, M, F, ldw, lds, Dv;
-  int G;             // state: W has H*G heads, head hw reads x head hw / G;  apply: P head = x head / G
-  int trans;         // state: 1 = S^T layout, 0 = (F, lds) layout
-  int mode;          // apply: 0 = store Y, 1 = dv += Y[:, :Dv]
-  float scale;       // psi scale
-  float factor;      // grad: c
+  int G;              // state: W has H*G heads, head hw reads x head hw / G;  apply: P head = x head / G
+  int trans;          // state: 1 = S^T layout, 0 = (F, lds) layout
+  int mode;           // apply: 0 = store Y, 1 = dv += Y[:, :Dv]
+  int tiles_per_cta;  // grad: 128-token tiles of one CTA
+  float scale;        // psi scale
+  float factor;       // grad: c
 };
 
-template <typename T>
-__device__ __forceinline__ float bf(T v) { return to_f32<T>(v); }
-
-// Element i (a compile-time index after unrolling) of a token row held as packed 16-bit pairs.
-template <typename T>
-__device__ __forceinline__ float xunpack(uint32_t w, int odd) {
-  const uint16_t hb = odd ? static_cast<uint16_t>(w >> 16) : static_cast<uint16_t>(w & 0xffffu);
-  return to_f32<T>(*reinterpret_cast<const T*>(&hb));
+// N 16-bit values (N a multiple of 8, src 16-byte aligned) to fp32.
+template <typename T, int N>
+__device__ __forceinline__ void load_vals(const T* src, float (&out)[N]) {
+#pragma unroll
+  for (int c = 0; c < N / 8; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + 8 * c);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[8 * c + j] = to_f32<T>(e[j]);
+  }
 }
-// The E values of group g (a runtime value) of the token row: an unrolled compare over the groups,
-// so every register index stays a compile-time constant (no local-memory copy of the row).
-template <typename T, int E, int D>
-__device__ __forceinline__ void group_vals(const uint32_t (&xr)[D / 2], int g, float (&xg)[E]) {
+// The E values of row `row` of a [rows][E] 16-bit tile that TMA wrote with the 2E-byte swizzle (the
+// 16-byte chunks of each row permuted by row, so that a warp reading 32 consecutive rows spreads over
+// all banks), and one element of it.
+template <typename T, int E>
+__device__ __forceinline__ void load_row_swz(const T* tile, int row, float (&out)[E]) {
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(tile);
 #pragma unroll
-  for (int gg = 0; gg < D / E; ++gg)
-    if (gg == g) {
+  for (int c = 0; c < E / 8; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + swz_offset(row, 16 * c, 2 * E));
+    const T* e = reinterpret_cast<const T*>(&v);
 #pragma unroll
-      for (int e = 0; e < E; ++e) xg[e] = xunpack<T>(xr[(gg * E + e) >> 1], (gg * E + e) & 1);
-    }
+    for (int j = 0; j < 8; ++j) out[8 * c + j] = to_f32<T>(e[j]);
+  }
+}
+template <typename T, int E>
+__device__ __forceinline__ float elem_swz(const T* tile, int row, int e) {
+  return to_f32<T>(*reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(tile) + swz_offset(row, 2 * e, 2 * E)));
+}
+__device__ __forceinline__ uint32_t bf16x2(float2 v) { return pack2<__nv_bfloat16>(v.x, v.y); }
+// One arrival per compute warp (barriers of the compute warps count kComputeWarps): the warp's
+// shared-memory writes or reads, ordered by __syncwarp, are released by lane 0's arrive.
+constexpr int kComputeWarps = kCompute / 32;
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
 // ------------------------------------------------------------------------------------------------
-// state: one CTA per (128-feature tile, head); K-loop over the head's tokens in blocks of 64.
-// Thread f of 128 owns feature f0 + f: it forms row f of the K-major psi tile [f][t] for each block.
+// state: one CTA per (256-feature slice, W head); K-loop over the head's tokens in blocks of 64.
+// A = psi^T, MN-major: four 64-feature boxes [64 tokens][128 B]; features 0-127 feed accumulator 0
+// (TMEM columns 0..NW-1), 128-255 accumulator 1 (columns 256..).  B = the W tile, MN-major.
+// Compute thread (t, q) forms token row t of feature box q.
 // ------------------------------------------------------------------------------------------------
 template <typename T, int E, bool SUM, int NW>
 struct StateSmem {
   static constexpr int NWB = (NW + 63) / 64;
-  static constexpr int XW = SUM ? 4 * E : E;  // 16-bit values of a token row held per block (SUM: all M <= 4 groups)
-  uint8_t W[kStages][NWB][64 * kRowB];
-  uint8_t psi[kStages][128 * kRowB];
-  T xs[kStages][64][XW];
-  uint64_t wfull[kStages], mdone[kStages];
+  static constexpr int SW = SUM ? 3 : 4;     // W / token-row ring
+  static constexpr int XW = SUM ? 4 * E : E;  // 16-bit values per token row held (sum: all M <= 4 groups)
+  uint8_t W[SW][NWB][64 * kRowB];
+  uint8_t psi[2][4][64 * kRowB];
+  T xs[SW][64 * XW];  // token rows: concat [64][E] with the 2E-byte swizzle, sum [64][D] dense
+  uint64_t tfull[SW], mdone[SW], pfull[2];
   uint32_t tmem;
   int abort;
 };
 
 template <typename T, int E, bool SUM, int NW>
-__global__ void __launch_bounds__(128, 1) sp_state_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    sp_state_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Params p) {
   using L = StateSmem<T, E, SUM, NW>;
+  constexpr int SW = L::SW, NWB = L::NWB, EE = E * E, CPB = 64 / E;
   extern __shared__ uint8_t smraw[];
   L& sm = *reinterpret_cast<L*>(align1k(smraw));
-  constexpr int EE = E * E;
-  constexpr int NWB = L::NWB;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int HW = p.H * p.G;  // heads of W and of the state
   const int bh = blockIdx.y, b = bh / HW, h = (bh % HW) / p.G;
-  const int f0 = blockIdx.x * 128;
+  const int f0 = blockIdx.x * 256;
   const int g = SUM ? 0 : f0 / EE;
-  const int rem = (f0 + tid) % EE, fa = rem / E, fb = rem % E;
-  const int M = SUM ? p.M : 1;
+  const int a0 = (f0 % EE) / E;  // first a-value of the slice
+  const int xw = SUM ? p.D : E;  // 16-bit values per token row in the tile
   const int nblk = (p.T + 63) / 64;
   if (tid == 0) {
     sm.abort = 0;
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.wfull[s], 1);
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&sm.tfull[s], 1);
       mbar_init(&sm.mdone[s], 1);
     }
+    for (int s = 0; s < 2; ++s) mbar_init(&sm.pfull[s], kComputeWarps);
     fence_mbar_init();
-    tma_prefetch_desc(&tmW);
   }
-  if (warp == 0) {
-    tmem_alloc(&sm.tmem, 256);
+  if (warp == kProducerWarp) {
+    tmem_alloc(&sm.tmem, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = sm.tmem;
-  const T* xb = static_cast<const T*>(p.x);
-  // block j's W tile (TMA, thread 0) and its token rows (cp.async, every thread)
-  auto issue = [&](int j) {
-    const int s = j % kStages;
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&sm.wfull[s], NWB * 64 * kRowB);
-      for (int q = 0; q < NWB; ++q) tma_load_3d(sm.W[s][q], &tmW, &sm.wfull[s], 64 * q, 64 * j, bh);
-    }
-    const int CPR = (SUM ? p.D : E) * 2 / 16;  // 16-byte chunks of the token row this tile needs
-    for (int i = tid; i < 64 * CPR; i += 128) {
-      const int r = i / CPR, c = i % CPR, t = 64 * j + r;
-      const bool ok = t < p.T;
-      const T* src = xb + ((static_cast<size_t>(b) * p.T + (ok ? t : 0)) * p.H + h) * p.D + g * E + 8 * c;
-      cp_async16(smem_u32(&sm.xs[s][r][8 * c]), src, ok);
-    }
-    cp_async_commit();
-  };
-  issue(0);
-  if (nblk > 1) issue(1);
-  constexpr uint32_t idesc = umma_idesc_f16(128, NW, true, false, true);
-  bool ok = true;
-  for (int i = 0; i < nblk && ok; ++i) {
-    const int s = i % kStages;
-    if (i + 2 < nblk) {
-      // stage (i+2) % 4 held block i-2: its W tile is free once that block's MMAs completed
-      if (tid == 0 && i >= 2) {
-        WaitCtx wc{p.status, &sm.abort};
-        mbar_wait(&sm.mdone[(i - 2) % kStages], static_cast<uint32_t>(((i - 2) / kStages) & 1), wc);
-      }
-      issue(i + 2);
-      cp_async_wait<2>();
-    } else if (i + 1 < nblk) {
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    // psi[s] was last read by block i-4's MMAs
-    if (i >= kStages &&
-        !(ok = wait_all(&sm.mdone[s], static_cast<uint32_t>(((i - kStages) / kStages) & 1), &sm.abort, p.status)))
-      break;
-    __syncthreads();
-    {  // row tid of psi[s]: 64 tokens
-      const uint32_t base = smem_u32(sm.psi[s]);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t wv[4];
-#pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          float v2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int t = 8 * c + 2 * e2 + u;
-            if constexpr (SUM) {
-              float acc = 0.f;
-              for (int gg = 0; gg < M; ++gg) acc = fmaf(bf(sm.xs[s][t][gg * E + fa]), bf(sm.xs[s][t][gg * E + fb]), acc);
-              v2[u] = p.scale * acc;
-            } else {
-              v2[u] = p.scale * (bf(sm.xs[s][t][fa]) * bf(sm.xs[s][t][fb]));
-            }
-          }
-          wv[e2] = pack2<__nv_bfloat16>(v2[0], v2[1]);
-        }
-        st_shared_v4(base + toff(tid, 8 * c), wv[0], wv[1], wv[2], wv[3]);
+  const WaitCtx wc{p.status, &sm.abort};
+  int issued = 0, committed = 0;
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmW);
+      tma_prefetch_desc(&tmX);
+      const uint32_t bytes = NWB * 64 * kRowB + 64u * static_cast<uint32_t>(xw) * 2u;
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % SW;
+        if (j >= SW && !mbar_wait(&sm.mdone[s], par((j - SW) / SW), wc)) break;
+        mbar_arrive_expect_tx(&sm.tfull[s], bytes);
+        for (int q = 0; q < NWB; ++q) tma_load_3d(sm.W[s][q], &tmW, &sm.tfull[s], 64 * q, 64 * j, bh);
+        tma_load_4d(sm.xs[s], &tmX, &sm.tfull[s], g * E, h, 64 * j, b);
+        issued = j + 1;
       }
     }
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      WaitCtx wc{p.status, &sm.abort};
-      if (mbar_wait(&sm.wfull[s], static_cast<uint32_t>((i / kStages) & 1), wc)) {
+    __syncwarp();
+  } else if (warp == kIssuerWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(128, NW, true, true, true);
+      for (int i = 0; i < nblk; ++i) {
+        const int s = i % SW, ps = i & 1;
+        if (!mbar_wait(&sm.tfull[s], par(i / SW), wc) || !mbar_wait(&sm.pfull[ps], par(i >> 1), wc)) break;
         tc_fence_after();
-        const uint64_t ad = umma_smem_desc(smem_u32(sm.psi[s]), 16, 1024, 128);
+        const uint64_t ad0 = umma_smem_desc(smem_u32(sm.psi[ps][0]), 64 * kRowB, 1024, 128);
+        const uint64_t ad1 = umma_smem_desc(smem_u32(sm.psi[ps][2]), 64 * kRowB, 1024, 128);
         const uint64_t bd = umma_smem_desc(smem_u32(sm.W[s][0]), 64 * kRowB, 1024, 128);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_ss(tbase, ad + static_cast<uint64_t>(2 * kk), bd + static_cast<uint64_t>(128 * kk), idesc,
-                  (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {  // 16 tokens = 16 rows of 128 B per K step
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_ss(tbase, ad0 + 128u * kk, bd + 128u * kk, idesc, acc);
+          umma_ss(tbase + 256u, ad1 + 128u * kk, bd + 128u * kk, idesc, acc);
+        }
         umma_commit(&sm.mdone[s]);
+        committed = i + 1;
       }
     }
-    ok = !__syncthreads_or(sm.abort != 0);
+    __syncwarp();
+  } else {
+    const int t = tid & 63, q = tid >> 6;  // token row of the block, 64-feature box
+    const int aq = a0 + (64 * q) / E;      // first a-value of the box
+    const float2 s2 = make_float2(p.scale, p.scale);
+    for (int i = 0; i < nblk; ++i) {
+      const int s = i % SW, ps = i & 1;
+      if (!mbar_wait_w(&sm.tfull[s], par(i / SW), wc)) break;
+      if (i >= 2 && !mbar_wait_w(&sm.mdone[(i - 2) % SW], par((i - 2) / SW), wc)) break;  // psi[ps] is free
+      float2 v[32];  // the box row: features 2c, 2c+1 = (a = aq + 2c / E, b = 2c % E and + 1)
+      if constexpr (SUM) {  // rows of xw = D values, unswizzled
+        const T* xr = sm.xs[s] + t * xw;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+          if (gg < p.M) {
+            float xb[E], xa[CPB];
+            load_vals<T, E>(xr + gg * E, xb);
+#pragma unroll
+            for (int k = 0; k < CPB; ++k) xa[k] = to_f32<T>(xr[gg * E + aq + k]);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int k = (2 * c) / E, bb = (2 * c) % E;
+              v[c] = ffma2(make_float2(xa[k], xa[k]), make_float2(xb[bb], xb[bb + 1]), v[c]);
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = fmul2(s2, v[c]);
+      } else {  // rows of E values, 2E-byte swizzle
+        float xb[E], xa[CPB];
+        load_row_swz<T, E>(sm.xs[s], t, xb);
+#pragma unroll
+        for (int k = 0; k < CPB; ++k) xa[k] = elem_swz<T, E>(sm.xs[s], t, aq + k);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int k = (2 * c) / E, bb = (2 * c) % E;
+          v[c] = fmul2(s2, fmul2(make_float2(xa[k], xa[k]), make_float2(xb[bb], xb[bb + 1])));
+        }
+      }
+      const uint32_t base = smem_u32(sm.psi[ps][q]);
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        st_shared_v4(base + swz_offset(t, 16 * c8, 128), bf16x2(v[4 * c8]), bf16x2(v[4 * c8 + 1]),
+                     bf16x2(v[4 * c8 + 2]), bf16x2(v[4 * c8 + 3]));
+      fence_proxy_async_smem();
+      warp_arrive(&sm.pfull[ps]);
+    }
   }
-  if (ok && nblk > 0)
-    ok = wait_all(&sm.mdone[(nblk - 1) % kStages], static_cast<uint32_t>(((nblk - 1) / kStages) & 1), &sm.abort,
-                  p.status);
-  if (ok && nblk > 0) {
+  __syncthreads();
+  if (warp < kProducerWarp && __all_sync(0xffffffffu, sm.abort == 0) &&
+      mbar_wait_w(&sm.mdone[(nblk - 1) % SW], par((nblk - 1) / SW), wc)) {
     tc_fence_after();
-    const int fl = f0 + tid;
-    const uint32_t lane = static_cast<uint32_t>(32 * warp) << 16;
+    const int lq = warp & 3, hh = warp >> 2;
+    const int fl = f0 + 128 * hh + 32 * lq + lane;
+    const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * lq) << 16) + 256u * hh;
     float* out = p.out + static_cast<size_t>(bh) * p.F * (p.trans ? p.ldw : p.lds);
 #pragma unroll
     for (int c0 = 0; c0 < NW; c0 += 16) {
       uint32_t r[16];
-      tmem_ld16(tbase + lane + c0, r);
+      tmem_ld16(taddr + c0, r);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -241,313 +284,347 @@ __global__ void __launch_bounds__(128, 1) sp_state_kernel(const __grid_constant_
     if (!p.trans)
       for (int n = p.ldw; n < p.lds; ++n) out[static_cast<size_t>(fl) * p.lds + n] = 0.f;
   }
-  cp_async_wait<0>();
-  if (!ok && tid == 0)
-    for (int s = 0; s < kStages; ++s) mbar_drain(&sm.mdone[s], 0), mbar_drain(&sm.mdone[s], 1);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 256);
+  if (sm.abort != 0 && lane == 0) {
+    if (warp == kIssuerWarp) drain_ring(sm.mdone, SW, committed);
+    if (warp == kProducerWarp) drain_ring(sm.tfull, SW, issued);
+  }
+  __syncthreads();
+  if (warp == kProducerWarp) tmem_dealloc(tbase, kTmemCols);
 }
 
 // ------------------------------------------------------------------------------------------------
-// apply: one CTA per (128-token tile, head); K-loop over the F features in blocks of 64.  Thread t
-// of 128 owns token t0 + t (its 16-bit row in registers) and forms row t of the K-major psi tile.
+// apply: one CTA per (256-token tile, head); K-loop over the F features in blocks of 64.  A = psi,
+// K-major [256 tokens][64 features]: rows 0-127 feed accumulator 0, rows 128-255 accumulator 1.
+// B = the P^T block [NW rows][64 features], K-major.  Compute thread r owns token t0 + r: it keeps
+// its current group's E values in registers (the next group's are loaded one group ahead).
 // ------------------------------------------------------------------------------------------------
 template <int NW>
 struct ApplySmem {
-  uint8_t P[kStages][NW * kRowB];
-  uint8_t psi[kStages][128 * kRowB];
-  uint64_t pfull[kStages], mdone[kStages];
+  static constexpr int SW = 4;  // P^T ring
+  static constexpr int SP = 3;  // psi ring
+  uint8_t P[SW][NW * kRowB];
+  uint8_t psi[SP][256 * kRowB];
+  uint64_t pfull[SW], mdone[SW], sfull[SP];
   uint32_t tmem;
   int abort;
 };
 
 template <typename T, int E, int D, int NW>
-__global__ void __launch_bounds__(128, 1) sp_apply_kernel(const __grid_constant__ CUtensorMap tmP, Params p) {
+__global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_constant__ CUtensorMap tmP, Params p) {
   using L = ApplySmem<NW>;
+  constexpr int SW = L::SW, SP = L::SP, EE = E * E, BPG = EE / 64;  // 64-feature blocks per group
   extern __shared__ uint8_t smraw[];
   L& sm = *reinterpret_cast<L*>(align1k(smraw));
-  constexpr int EE = E * E;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int bhp = b * (p.H / p.G) + h / p.G;  // the state's head
-  const int t = blockIdx.x * 128 + tid;
-  const bool tin = t < p.T;
+  const int t0 = blockIdx.x * 256;
   const int nblk = p.F / 64;
   if (tid == 0) {
     sm.abort = 0;
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < SW; ++s) {
       mbar_init(&sm.pfull[s], 1);
       mbar_init(&sm.mdone[s], 1);
     }
+    for (int s = 0; s < SP; ++s) mbar_init(&sm.sfull[s], kComputeWarps);
     fence_mbar_init();
-    tma_prefetch_desc(&tmP);
   }
-  if (warp == 0) {
-    tmem_alloc(&sm.tmem, 256);
+  if (warp == kProducerWarp) {
+    tmem_alloc(&sm.tmem, kTmemCols);
     tmem_relinquish();
-  }
-  // this thread's token row, packed 16-bit pairs
-  uint32_t xr[D / 2];
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.x) +
-                                                      ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D);
-#pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 v = tin ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-      xr[4 * c] = v.x;
-      xr[4 * c + 1] = v.y;
-      xr[4 * c + 2] = v.z;
-      xr[4 * c + 3] = v.w;
-    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = sm.tmem;
-  auto issue = [&](int j) {
-    if (tid == 0) {
-      const int s = j % kStages;
-      mbar_arrive_expect_tx(&sm.pfull[s], NW * kRowB);
-      tma_load_3d(sm.P[s], &tmP, &sm.pfull[s], 64 * j, 0, bhp);
-    }
-  };
-  issue(0);
-  if (nblk > 1) issue(1);
-  constexpr uint32_t idesc = umma_idesc_f16(128, NW, true, false, false);
-  constexpr int BPG = EE / 64;  // 64-feature blocks per group
-  bool ok = true;
-  for (int g = 0; g < p.F / EE && ok; ++g) {
-    float xg[E];
-    group_vals<T, E, D>(xr, g, xg);
-#pragma unroll
-    for (int ii = 0; ii < BPG; ++ii) {
-      const int i = g * BPG + ii;
-      const int s = i % kStages;
-      if (i + 2 < nblk) {
-        if (tid == 0 && i >= 2) {  // stage (i+2) % 4 held block i-2
-          WaitCtx wc{p.status, &sm.abort};
-          mbar_wait(&sm.mdone[(i - 2) % kStages], static_cast<uint32_t>(((i - 2) / kStages) & 1), wc);
-        }
-        issue(i + 2);
+  const WaitCtx wc{p.status, &sm.abort};
+  int issued = 0, committed = 0;
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmP);
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % SW;
+        if (j >= SW && !mbar_wait(&sm.mdone[s], par((j - SW) / SW), wc)) break;
+        mbar_arrive_expect_tx(&sm.pfull[s], NW * kRowB);
+        tma_load_3d(sm.P[s], &tmP, &sm.pfull[s], 64 * j, 0, bhp);
+        issued = j + 1;
       }
-      if (i >= kStages &&
-          !(ok = wait_all(&sm.mdone[s], static_cast<uint32_t>(((i - kStages) / kStages) & 1), &sm.abort, p.status)))
-        break;
-      {  // row tid of psi[s]: features 64 i .. 64 i + 63 = (g, a0 + j / E, j % E)
-        const uint32_t base = smem_u32(sm.psi[s]);
-        constexpr int a0 = 0;  // (64 ii) / E is added below as a compile-time offset
+    }
+    __syncwarp();
+  } else if (warp == kIssuerWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(128, NW, true, false, false);
+      for (int i = 0; i < nblk; ++i) {
+        const int s = i % SW, ps = i % SP;
+        if (!mbar_wait(&sm.pfull[s], par(i / SW), wc) || !mbar_wait(&sm.sfull[ps], par(i / SP), wc)) break;
+        tc_fence_after();
+        const uint64_t ad0 = umma_smem_desc(smem_u32(sm.psi[ps]), 16, 1024, 128);
+        const uint64_t ad1 = umma_smem_desc(smem_u32(sm.psi[ps] + 128 * kRowB), 16, 1024, 128);
+        const uint64_t bd = umma_smem_desc(smem_u32(sm.P[s]), 16, 1024, 128);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int kk = 0; kk < 4; ++kk) {  // 16 features = 32 bytes of each row per K step
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_ss(tbase, ad0 + 2u * kk, bd + 2u * kk, idesc, acc);
+          umma_ss(tbase + 256u, ad1 + 2u * kk, bd + 2u * kk, idesc, acc);
+        }
+        umma_commit(&sm.mdone[s]);
+        committed = i + 1;
+      }
+    }
+    __syncwarp();
+  } else {
+    const int r = tid, t = t0 + r;
+    const bool tin = t < p.T;
+    const T* xrow = static_cast<const T*>(p.x) + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D;
+    const float2 s2 = make_float2(p.scale, p.scale);
+    uint4 nxt[E / 8];  // the next group's values, loaded one group ahead
+#pragma unroll
+    for (int c = 0; c < E / 8; ++c)
+      nxt[c] = tin ? reinterpret_cast<const uint4*>(xrow)[c] : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t row_base = smem_u32(sm.psi[0]);
+    bool ok = true;
+    for (int g = 0; g < p.M && ok; ++g) {
+      float xg[E];
+#pragma unroll
+      for (int c = 0; c < E / 8; ++c) {
+        const T* e = reinterpret_cast<const T*>(&nxt[c]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xg[8 * c + j] = to_f32<T>(e[j]);
+      }
+      if (g + 1 < p.M) {
+#pragma unroll
+        for (int c = 0; c < E / 8; ++c)
+          nxt[c] = tin ? reinterpret_cast<const uint4*>(xrow + (g + 1) * E)[c] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int ii = 0; ii < BPG; ++ii) {
+        const int i = g * BPG + ii, ps = i % SP;
+        if (i >= SP && !(ok = mbar_wait_w(&sm.mdone[(i - SP) % SW], par((i - SP) / SW), wc))) break;
+        const uint32_t base = row_base + static_cast<uint32_t>(ps) * (256 * kRowB);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
           uint32_t wv[4];
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
-            const int j0 = 8 * c + 2 * e2;  // feature offset within the block (even)
-            const int a = a0 + (64 * ii + j0) / E, bb = (64 * ii + j0) % E;
-            const float xa = xg[a];
-            wv[e2] = pack2<__nv_bfloat16>(p.scale * (xa * xg[bb]), p.scale * (xa * xg[bb + 1]));
+            const int j0 = 64 * ii + 8 * c8 + 2 * e2;  // feature within the group (even)
+            const int a = j0 / E, bb = j0 % E;
+            wv[e2] = bf16x2(fmul2(s2, fmul2(make_float2(xg[a], xg[a]), make_float2(xg[bb], xg[bb + 1]))));
           }
-          st_shared_v4(base + toff(tid, 8 * c), wv[0], wv[1], wv[2], wv[3]);
+          st_shared_v4(base + swz_offset(r, 16 * c8, 128), wv[0], wv[1], wv[2], wv[3]);
         }
+        fence_proxy_async_smem();
+        warp_arrive(&sm.sfull[ps]);
       }
-      fence_proxy_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        WaitCtx wc{p.status, &sm.abort};
-        if (mbar_wait(&sm.pfull[s], static_cast<uint32_t>((i / kStages) & 1), wc)) {
-          tc_fence_after();
-          const uint64_t ad = umma_smem_desc(smem_u32(sm.psi[s]), 16, 1024, 128);
-          const uint64_t bd = umma_smem_desc(smem_u32(sm.P[s]), 16, 1024, 128);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tbase, ad + static_cast<uint64_t>(2 * kk), bd + static_cast<uint64_t>(2 * kk), idesc,
-                    (i > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&sm.mdone[s]);
-        }
-      }
-      ok = !__syncthreads_or(sm.abort != 0);
-      if (!ok) break;
     }
   }
-  if (ok && nblk > 0)
-    ok = wait_all(&sm.mdone[(nblk - 1) % kStages], static_cast<uint32_t>(((nblk - 1) / kStages) & 1), &sm.abort,
-                  p.status);
-  if (ok && nblk > 0) {
+  __syncthreads();
+  if (warp < kProducerWarp && __all_sync(0xffffffffu, sm.abort == 0) &&
+      mbar_wait_w(&sm.mdone[(nblk - 1) % SW], par((nblk - 1) / SW), wc)) {
     tc_fence_after();
-    const uint32_t lane = static_cast<uint32_t>(32 * warp) << 16;
+    const int lq = warp & 3, hh = warp >> 2;
+    const int t = t0 + 128 * hh + 32 * lq + lane;
+    const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * lq) << 16) + 256u * hh;
+    const bool tin = t < p.T;
+    const bool vec = p.mode == 0 || (p.Dv % 4) == 0;
+    float* row = p.mode == 0 ? p.out + (static_cast<size_t>(bh) * p.T + (tin ? t : 0)) * p.ldw
+                             : p.out + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * p.Dv;
+    const int ncols = p.mode == 0 ? p.ldw : p.Dv;
 #pragma unroll
     for (int c0 = 0; c0 < NW; c0 += 16) {
-      uint32_t r[16];
-      tmem_ld16(tbase + lane + c0, r);
+      uint32_t rv[16];
+      tmem_ld16(taddr + c0, rv);
       tmem_wait_ld();
-      if (tin) {
-        if (p.mode == 0) {
-          float* y = p.out + (static_cast<size_t>(bh) * p.T + t) * p.ldw;
+      if (!tin) continue;
+      if (vec) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c0 + j < p.ldw) y[c0 + j] = __uint_as_float(r[j]);
-        } else {
-          float* dv = p.out + ((static_cast<size_t>(b) * p.T + t) * p.H + h) * p.Dv;
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c0 + j < p.Dv) dv[c0 + j] += __uint_as_float(r[j]);
+        for (int j = 0; j < 16; j += 4) {
+          if (c0 + j < ncols) {
+            float4* d4 = reinterpret_cast<float4*>(row + c0 + j);
+            float4 y = make_float4(__uint_as_float(rv[j]), __uint_as_float(rv[j + 1]), __uint_as_float(rv[j + 2]),
+                                   __uint_as_float(rv[j + 3]));
+            if (p.mode) {
+              const float4 o = *d4;
+              y.x += o.x, y.y += o.y, y.z += o.z, y.w += o.w;
+            }
+            *d4 = y;
+          }
         }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c0 + j < ncols) row[c0 + j] += __uint_as_float(rv[j]);
       }
     }
   }
-  if (!ok && tid == 0)
-    for (int s = 0; s < kStages; ++s) mbar_drain(&sm.mdone[s], 0), mbar_drain(&sm.mdone[s], 1);
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 256);
+  if (sm.abort != 0 && lane == 0) {
+    if (warp == kIssuerWarp) drain_ring(sm.mdone, SW, committed);
+    if (warp == kProducerWarp) drain_ring(sm.pfull, SW, issued);
+  }
+  __syncthreads();
+  if (warp == kProducerWarp) tmem_dealloc(tbase, kTmemCols);
 }
 
 // ------------------------------------------------------------------------------------------------
-// grad: one CTA per (128-token tile, head).  A = W tile (128 tokens x NW, K-major, loaded once);
-// per 256-feature tile, B = P^T (NW rows x 256 features, MN-major, four TMA boxes) and
-// D = W P^T (128 x 256) in one of two TMEM buffers, so the MMAs of tile i+1 run during the epilogue
-// of tile i.  Epilogue: thread t contracts its row of D with its token's group values.
+// grad: one CTA per (256-feature slice, head, range of 128-token tiles).  B = the P^T slice
+// [NW rows][256 features], MN-major, loaded once.  Per tile: A = W [128 tokens][NW], K-major, and
+// the tile's token rows of the slice's group; D = W P^T (128 x 256) in one of two TMEM buffers, so
+// the MMAs of tile j+1 run during the epilogue of tile j.  Epilogue warp w reads token rows
+// 32 (w & 3).. and columns 128 (w >> 2).. (128 / E whole a-values): dx[t, g E + a] gets
+// c * sum_b D[t, (a, b)] x[t, g E + b].
 // ------------------------------------------------------------------------------------------------
-template <int NW>
+template <typename T, int E, int NW>
 struct GradSmem {
   static constexpr int NWB = (NW + 63) / 64;
-  uint8_t A[NWB][128 * kRowB];
-  uint8_t B[2][4][NW * kRowB];
-  float dxs[32][128];  // a group's per-(a, token) results, [a][thread]
-  uint64_t afull, bfull[2], mdone[2];
+  static constexpr int SW = NWB == 3 ? 2 : 3;  // W / token-row ring
+  uint8_t B[4][NW * kRowB];
+  uint8_t A[SW][NWB][128 * kRowB];
+  T xs[SW][128 * E];  // token rows [128][E] of the slice's group, 2E-byte swizzle
+  uint64_t bfull, afull[SW], afree[SW], xfree[SW], mdone[2], accfree[2];
   uint32_t tmem;
   int abort;
 };
 
 template <typename T, int E, int D, int NW>
-__global__ void __launch_bounds__(128, 1) sp_grad_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                         const __grid_constant__ CUtensorMap tmP, Params p) {
-  using L = GradSmem<NW>;
+__global__ void __launch_bounds__(kThreads, 1)
+    sp_grad_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmP,
+                   const __grid_constant__ CUtensorMap tmX, Params p) {
+  using L = GradSmem<T, E, NW>;
+  constexpr int SW = L::SW, NWB = L::NWB, EE = E * E, KSTEPS = NW / 16, NA = 128 / E;
   extern __shared__ uint8_t smraw[];
   L& sm = *reinterpret_cast<L*>(align1k(smraw));
-  constexpr int EE = E * E;
-  constexpr int NWB = L::NWB;
-  constexpr int KSTEPS = NW / 16;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int t0 = blockIdx.x * 128, t = t0 + tid;
-  const bool tin = t < p.T;
-  const int ntile = p.F / 256;
+  const int f0 = blockIdx.x * 256, g = f0 / EE, a0 = (f0 % EE) / E;
+  const int tile0 = blockIdx.z * p.tiles_per_cta;
+  const int ntile = min(p.tiles_per_cta, (p.T + 127) / 128 - tile0);  // >= 1 by the grid's construction
   if (tid == 0) {
     sm.abort = 0;
-    mbar_init(&sm.afull, 1);
+    mbar_init(&sm.bfull, 1);
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&sm.afull[s], 1);
+      mbar_init(&sm.afree[s], 1);
+      mbar_init(&sm.xfree[s], kComputeWarps);
+    }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sm.bfull[s], 1);
       mbar_init(&sm.mdone[s], 1);
+      mbar_init(&sm.accfree[s], kComputeWarps);
     }
     fence_mbar_init();
-    tma_prefetch_desc(&tmW);
-    tma_prefetch_desc(&tmP);
   }
-  if (warp == 0) {
-    tmem_alloc(&sm.tmem, 512);
+  if (warp == kProducerWarp) {
+    tmem_alloc(&sm.tmem, kTmemCols);
     tmem_relinquish();
   }
-  // this thread's token row (each group's E values are read when the group starts)
-  const T* xrow = static_cast<const T*>(p.x) + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = sm.tmem;
-  auto issue_b = [&](int j) {
-    const int s = j & 1;
-    mbar_arrive_expect_tx(&sm.bfull[s], 4 * NW * kRowB);
-    for (int q = 0; q < 4; ++q) tma_load_3d(sm.B[s][q], &tmP, &sm.bfull[s], 256 * j + 64 * q, 0, bh);
-  };
-  constexpr uint32_t idesc = umma_idesc_f16(128, 256, true, false, true);
-  auto issue_mma = [&](int j) {  // thread 0
-    WaitCtx wc{p.status, &sm.abort};
-    if (!mbar_wait(&sm.bfull[j & 1], static_cast<uint32_t>((j >> 1) & 1), wc)) return;
-    tc_fence_after();
-    const uint64_t ad = umma_smem_desc(smem_u32(sm.A[0]), 16, 1024, 128);
-    const uint64_t bd = umma_smem_desc(smem_u32(sm.B[j & 1][0]), NW * kRowB, 1024, 128);
-    const uint32_t d = tbase + 256u * static_cast<uint32_t>(j & 1);
-#pragma unroll
-    for (int kk = 0; kk < KSTEPS; ++kk)
-      umma_ss(d, ad + static_cast<uint64_t>(((kk >> 2) * 128 * kRowB + (kk & 3) * 32) >> 4),
-              bd + static_cast<uint64_t>(128 * kk), idesc, kk > 0 ? 1u : 0u);
-    umma_commit(&sm.mdone[j & 1]);
-  };
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&sm.afull, NWB * 128 * kRowB);
-    for (int q = 0; q < NWB; ++q) tma_load_3d(sm.A[q], &tmW, &sm.afull, 64 * q, t0, bh);
-    issue_b(0);
-    if (ntile > 1) issue_b(1);
-    WaitCtx wc{p.status, &sm.abort};
-    if (mbar_wait(&sm.afull, 0, wc)) issue_mma(0);
-  }
-  bool ok = true;
-  float* dxrow = p.dx + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D;
-  const uint32_t lane = static_cast<uint32_t>(32 * warp) << 16;
-  constexpr int TPG = EE / 256;  // 256-feature tiles per group
-  for (int g = 0; g < p.F / EE && ok; ++g) {
-    float xg[E];
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(xrow + g * E);
-#pragma unroll
-      for (int c = 0; c < E / 8; ++c) {
-        const uint4 v = tin ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-        const T* e = reinterpret_cast<const T*>(&v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) xg[8 * c + j] = to_f32<T>(e[j]);
+  const WaitCtx wc{p.status, &sm.abort};
+  int issued = 0, committed = 0;
+  bool bissued = false;
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmW);
+      tma_prefetch_desc(&tmP);
+      tma_prefetch_desc(&tmX);
+      mbar_arrive_expect_tx(&sm.bfull, 4 * NW * kRowB);
+      for (int q = 0; q < 4; ++q) tma_load_3d(sm.B[q], &tmP, &sm.bfull, f0 + 64 * q, 0, bh);
+      bissued = true;
+      const uint32_t bytes = NWB * 128 * kRowB + 128u * E * 2u;
+      for (int j = 0; j < ntile; ++j) {
+        const int s = j % SW, tok = 128 * (tile0 + j);
+        if (j >= SW && (!mbar_wait(&sm.afree[s], par((j - SW) / SW), wc) ||
+                        !mbar_wait(&sm.xfree[s], par((j - SW) / SW), wc)))
+          break;
+        mbar_arrive_expect_tx(&sm.afull[s], bytes);
+        for (int q = 0; q < NWB; ++q) tma_load_3d(sm.A[s][q], &tmW, &sm.afull[s], 64 * q, tok, bh);
+        tma_load_4d(sm.xs[s], &tmX, &sm.afull[s], g * E, h, tok, b);
+        issued = j + 1;
       }
     }
+    __syncwarp();
+  } else if (warp == kIssuerWarp) {
+    if (lane == 0 && mbar_wait(&sm.bfull, 0, wc)) {
+      constexpr uint32_t idesc = umma_idesc_f16(128, 256, true, false, true);
+      const uint64_t bd = umma_smem_desc(smem_u32(sm.B[0]), NW * kRowB, 1024, 128);
+      for (int j = 0; j < ntile; ++j) {
+        const int s = j % SW, ab = j & 1;
+        if (!mbar_wait(&sm.afull[s], par(j / SW), wc)) break;
+        if (j >= 2 && !mbar_wait(&sm.accfree[ab], par((j - 2) >> 1), wc)) break;
+        tc_fence_after();
+        const uint64_t ad = umma_smem_desc(smem_u32(sm.A[s][0]), 16, 1024, 128);
+        const uint32_t d = tbase + 256u * ab;
 #pragma unroll
-    for (int ii = 0; ii < TPG; ++ii) {
-      const int i = g * TPG + ii;
-      // the MMAs of tile i+1 (its accumulator buffer was last read by tile i-1's epilogue, finished)
-      if (tid == 0 && i + 1 < ntile) issue_mma(i + 1);
-      if (!(ok = wait_all(&sm.mdone[i & 1], static_cast<uint32_t>((i >> 1) & 1), &sm.abort, p.status))) break;
+        for (int kk = 0; kk < KSTEPS; ++kk)
+          umma_ss(d, ad + static_cast<uint64_t>(((kk >> 2) * 128 * kRowB + (kk & 3) * 32) >> 4),
+                  bd + static_cast<uint64_t>(128 * kk), idesc, kk > 0 ? 1u : 0u);
+        umma_commit(&sm.afree[s]);
+        umma_commit(&sm.mdone[ab]);
+        committed = j + 1;
+      }
+    }
+    __syncwarp();
+  } else {
+    const int lq = warp & 3, hh = warp >> 2, r = 32 * lq + lane;
+    const uint32_t lanebase = tbase + (static_cast<uint32_t>(32 * lq) << 16) + 128u * hh;
+    for (int j = 0; j < ntile; ++j) {
+      const int s = j % SW, ab = j & 1;
+      if (!mbar_wait_w(&sm.afull[s], par(j / SW), wc)) break;
+      float xg[E];
+      load_row_swz<T, E>(sm.xs[s], r, xg);
+      warp_arrive(&sm.xfree[s]);
+      if (!mbar_wait_w(&sm.mdone[ab], par(j >> 1), wc)) break;
       tc_fence_after();
-      // B stage i & 1 is free again: prefetch tile i+2 into it
-      if (tid == 0 && i + 2 < ntile) issue_b(i + 2);
-      const uint32_t acc = tbase + lane + 256u * static_cast<uint32_t>(i & 1);
-      // 256 features = 256 / E values of a (from a0 = 256 ii / E), E values of b each
+      float sums[NA];
 #pragma unroll
-      for (int c0 = 0; c0 < 256; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(acc + c0, r);
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t rv[32];
+        tmem_ld32(lanebase + 256u * ab + c0, rv);
         tmem_wait_ld();
 #pragma unroll
         for (int part = 0; part < 32 / E; ++part) {
-          const int col = c0 + part * E;
-          const int a = (256 * ii + col) / E;
           float sacc = 0.f;
 #pragma unroll
-          for (int j = 0; j < E; ++j) sacc = fmaf(__uint_as_float(r[part * E + j]), xg[j], sacc);
-          sm.dxs[a][tid] = sacc;  // each a of the group is one tile's: written exactly once
+          for (int jj = 0; jj < E; ++jj) sacc = fmaf(__uint_as_float(rv[part * E + jj]), xg[jj], sacc);
+          sums[(c0 + part * E) / E] = sacc;
         }
       }
       tc_fence_before();
-      __syncthreads();  // the accumulator buffer i & 1 is read: tile i+2's MMAs may overwrite it
-    }
-    if (ok && tin) {  // the group's E values: one read-modify-write of E contiguous floats
-      float4* d4 = reinterpret_cast<float4*>(dxrow + g * E);
-      float4 v[E / 4];
+      warp_arrive(&sm.accfree[ab]);
+      const int t = 128 * (tile0 + j) + r;
+      if (t < p.T) {
+        float4* d4 = reinterpret_cast<float4*>(p.dx + ((static_cast<size_t>(b) * p.T + t) * p.H + h) * D + g * E +
+                                               a0 + NA * hh);
 #pragma unroll
-      for (int c = 0; c < E / 4; ++c) v[c] = d4[c];
-#pragma unroll
-      for (int c = 0; c < E / 4; ++c) {
-        v[c].x = fmaf(p.factor, sm.dxs[4 * c][tid], v[c].x);
-        v[c].y = fmaf(p.factor, sm.dxs[4 * c + 1][tid], v[c].y);
-        v[c].z = fmaf(p.factor, sm.dxs[4 * c + 2][tid], v[c].z);
-        v[c].w = fmaf(p.factor, sm.dxs[4 * c + 3][tid], v[c].w);
-        d4[c] = v[c];
+        for (int c = 0; c < NA / 4; ++c) {
+          float4 v = d4[c];
+          v.x = fmaf(p.factor, sums[4 * c], v.x);
+          v.y = fmaf(p.factor, sums[4 * c + 1], v.y);
+          v.z = fmaf(p.factor, sums[4 * c + 2], v.z);
+          v.w = fmaf(p.factor, sums[4 * c + 3], v.w);
+          d4[c] = v;
+        }
       }
     }
   }
-  if (!ok && tid == 0) {
-    mbar_drain(&sm.mdone[0], 0), mbar_drain(&sm.mdone[0], 1);
-    mbar_drain(&sm.mdone[1], 0), mbar_drain(&sm.mdone[1], 1);
-  }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tbase, 512);
+  if (sm.abort != 0 && lane == 0) {
+    if (warp == kIssuerWarp) {
+      drain_ring(sm.afree, SW, committed);
+      drain_ring(sm.mdone, 2, committed);
+    }
+    if (warp == kProducerWarp) {
+      if (bissued) mbar_drain(&sm.bfull, 0);
+      drain_ring(sm.afull, SW, issued);
+    }
+  }
+  __syncthreads();
+  if (warp == kProducerWarp) tmem_dealloc(tbase, kTmemCols);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -569,6 +646,16 @@ int map_p(CUtensorMap* m, const void* P, int BH, int ldw, int F, int nw) {
   const uint32_t box[3] = {64, static_cast<uint32_t>(nw), 1};
   return encode_tmap_16bit(m, P, 3, dims, str, box, 128);
 }
+// x (B, T, H, D) 16-bit with boxes of [cols values][1 head][rows tokens][1]; swizzle 0 (dense rows)
+// or 2 cols bytes (cols in {16, 32})
+int map_x(CUtensorMap* m, const void* x, int B, int T, int H, int D, int cols, int rows, int swizzle) {
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(H), static_cast<uint64_t>(T),
+                            static_cast<uint64_t>(B)};
+  const uint64_t str[3] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(H) * D * 2,
+                           static_cast<uint64_t>(T) * H * D * 2};
+  const uint32_t box[4] = {static_cast<uint32_t>(cols), 1, static_cast<uint32_t>(rows), 1};
+  return encode_tmap_16bit(m, x, 4, dims, str, box, swizzle);
+}
 
 template <typename K>
 int launch_cfg(K kernel, size_t smem) {
@@ -576,13 +663,12 @@ int launch_cfg(K kernel, size_t smem) {
 }
 
 template <typename T, int E, bool SUM, int NW>
-int state_launch(const Params& p, const CUtensorMap& tmW, cudaStream_t st) {
-  using L = StateSmem<T, E, SUM, NW>;
+int state_launch(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmX, cudaStream_t st) {
   auto k = sp_state_kernel<T, E, SUM, NW>;
-  const size_t smem = sizeof(L) + 1024;
+  const size_t smem = sizeof(StateSmem<T, E, SUM, NW>) + 1024;
   int e = launch_cfg(k, smem);
   if (e) return e;
-  k<<<dim3(p.F / 128, p.B * p.H * p.G), 128, smem, st>>>(tmW, p);
+  k<<<dim3(p.F / 256, p.B * p.H * p.G), kThreads, smem, st>>>(tmW, tmX, p);
   return from_cuda(cudaGetLastError());
 }
 template <typename T, int E, int D, int NW>
@@ -591,16 +677,19 @@ int apply_launch(const Params& p, const CUtensorMap& tmP, cudaStream_t st) {
   const size_t smem = sizeof(ApplySmem<NW>) + 1024;
   int e = launch_cfg(k, smem);
   if (e) return e;
-  k<<<dim3((p.T + 127) / 128, p.B * p.H), 128, smem, st>>>(tmP, p);
+  k<<<dim3((p.T + 255) / 256, p.B * p.H), kThreads, smem, st>>>(tmP, p);
   return from_cuda(cudaGetLastError());
 }
 template <typename T, int E, int D, int NW>
-int grad_launch(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmP, cudaStream_t st) {
+int grad_launch(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmP, const CUtensorMap& tmX,
+                cudaStream_t st) {
   auto k = sp_grad_kernel<T, E, D, NW>;
-  const size_t smem = sizeof(GradSmem<NW>) + 1024;
+  const size_t smem = sizeof(GradSmem<T, E, NW>) + 1024;
   int e = launch_cfg(k, smem);
   if (e) return e;
-  k<<<dim3((p.T + 127) / 128, p.B * p.H), 128, smem, st>>>(tmW, tmP, p);
+  const int ntt = (p.T + 127) / 128;
+  const dim3 grid(p.F / 256, p.B * p.H, (ntt + p.tiles_per_cta - 1) / p.tiles_per_cta);
+  k<<<grid, kThreads, smem, st>>>(tmW, tmP, tmX, p);
   return from_cuda(cudaGetLastError());
 }
 
@@ -614,35 +703,48 @@ bool shape_ok(int D, int M, int ldw, bool sum) {
   return D == 64 || D == 128;
 }
 
+template <typename T, int E, bool SUM>
+int state_nw(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmX, cudaStream_t st) {
+  return nw_of(p.ldw) == 80 ? state_launch<T, E, SUM, 80>(p, tmW, tmX, st) : state_launch<T, E, SUM, 144>(p, tmW, tmX, st);
+}
 template <typename T>
-int state_dispatch(const Params& p, const CUtensorMap& tmW, bool sum, cudaStream_t st) {
-  const int E = p.D / p.M, nw = nw_of(p.ldw);
-  if (sum) {
-    if (E == 16) return nw == 80 ? state_launch<T, 16, true, 80>(p, tmW, st) : state_launch<T, 16, true, 144>(p, tmW, st);
-    return nw == 80 ? state_launch<T, 32, true, 80>(p, tmW, st) : state_launch<T, 32, true, 144>(p, tmW, st);
-  }
-  if (E == 16) return nw == 80 ? state_launch<T, 16, false, 80>(p, tmW, st) : state_launch<T, 16, false, 144>(p, tmW, st);
-  return nw == 80 ? state_launch<T, 32, false, 80>(p, tmW, st) : state_launch<T, 32, false, 144>(p, tmW, st);
+int state_dispatch(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmX, bool sum, cudaStream_t st) {
+  const int E = p.D / p.M;
+  if (sum) return E == 16 ? state_nw<T, 16, true>(p, tmW, tmX, st) : state_nw<T, 32, true>(p, tmW, tmX, st);
+  return E == 16 ? state_nw<T, 16, false>(p, tmW, tmX, st) : state_nw<T, 32, false>(p, tmW, tmX, st);
+}
+template <typename T, int E, int D>
+int apply_nw(const Params& p, const CUtensorMap& tmP, cudaStream_t st) {
+  return nw_of(p.ldw) == 80 ? apply_launch<T, E, D, 80>(p, tmP, st) : apply_launch<T, E, D, 144>(p, tmP, st);
 }
 template <typename T>
 int apply_dispatch(const Params& p, const CUtensorMap& tmP, cudaStream_t st) {
-  const int E = p.D / p.M, nw = nw_of(p.ldw);
-  if (p.D == 64) {
-    if (E == 16) return nw == 80 ? apply_launch<T, 16, 64, 80>(p, tmP, st) : apply_launch<T, 16, 64, 144>(p, tmP, st);
-    return nw == 80 ? apply_launch<T, 32, 64, 80>(p, tmP, st) : apply_launch<T, 32, 64, 144>(p, tmP, st);
-  }
-  if (E == 16) return nw == 80 ? apply_launch<T, 16, 128, 80>(p, tmP, st) : apply_launch<T, 16, 128, 144>(p, tmP, st);
-  return nw == 80 ? apply_launch<T, 32, 128, 80>(p, tmP, st) : apply_launch<T, 32, 128, 144>(p, tmP, st);
+  const int E = p.D / p.M;
+  if (p.D == 64) return E == 16 ? apply_nw<T, 16, 64>(p, tmP, st) : apply_nw<T, 32, 64>(p, tmP, st);
+  return E == 16 ? apply_nw<T, 16, 128>(p, tmP, st) : apply_nw<T, 32, 128>(p, tmP, st);
+}
+template <typename T, int E, int D>
+int grad_nw(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmP, const CUtensorMap& tmX, cudaStream_t st) {
+  return nw_of(p.ldw) == 80 ? grad_launch<T, E, D, 80>(p, tmW, tmP, tmX, st)
+                            : grad_launch<T, E, D, 144>(p, tmW, tmP, tmX, st);
 }
 template <typename T>
-int grad_dispatch(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmP, cudaStream_t st) {
-  const int E = p.D / p.M, nw = nw_of(p.ldw);
-  if (p.D == 64) {
-    if (E == 16) return nw == 80 ? grad_launch<T, 16, 64, 80>(p, tmW, tmP, st) : grad_launch<T, 16, 64, 144>(p, tmW, tmP, st);
-    return nw == 80 ? grad_launch<T, 32, 64, 80>(p, tmW, tmP, st) : grad_launch<T, 32, 64, 144>(p, tmW, tmP, st);
-  }
-  if (E == 16) return nw == 80 ? grad_launch<T, 16, 128, 80>(p, tmW, tmP, st) : grad_launch<T, 16, 128, 144>(p, tmW, tmP, st);
-  return nw == 80 ? grad_launch<T, 32, 128, 80>(p, tmW, tmP, st) : grad_launch<T, 32, 128, 144>(p, tmW, tmP, st);
+int grad_dispatch(const Params& p, const CUtensorMap& tmW, const CUtensorMap& tmP, const CUtensorMap& tmX,
+                  cudaStream_t st) {
+  const int E = p.D / p.M;
+  if (p.D == 64)
+    return E == 16 ? grad_nw<T, 16, 64>(p, tmW, tmP, tmX, st) : grad_nw<T, 32, 64>(p, tmW, tmP, tmX, st);
+  return E == 16 ? grad_nw<T, 16, 128>(p, tmW, tmP, tmX, st) : grad_nw<T, 32, 128>(p, tmW, tmP, tmX, st);
+}
+
+// 128-token tiles per gradient CTA: 32 (one P^T slice load per 4096 tokens), fewer when the grid
+// would otherwise not fill two waves of the 148 SMs.
+int grad_tiles_per_cta(int F, int BH, int T) {
+  const int ntt = (T + 127) / 128;
+  const long long slices = static_cast<long long>(F / 256) * BH;
+  int tpc = 32;
+  while (tpc > 4 && slices * ((ntt + tpc - 1) / tpc) < 2 * 148) tpc /= 2;
+  return tpc;
 }
 
 bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; }
@@ -654,7 +756,8 @@ bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; }
 using namespace kata;
 
 extern "C" int kata_sp_state(const void* x, const void* W, float* S, int dtype, int B, int T, int H, int G, int D,
-                             int M, int score, int ldw, float scale, int trans, int lds, kata_stream_t stream) {
+                             int M, int score, int ldw, float scale, int trans, int lds, int* status,
+                             kata_stream_t stream) {
   using namespace sptc;
   if (!x || !W || !S) return KATA_ERR_INVALID;
   if (dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
@@ -666,6 +769,7 @@ extern "C" int kata_sp_state(const void* x, const void* W, float* S, int dtype, 
   Params p{};
   p.x = x;
   p.out = S;
+  p.status = status;
   p.B = B;
   p.T = T;
   p.H = H;
@@ -677,15 +781,17 @@ extern "C" int kata_sp_state(const void* x, const void* W, float* S, int dtype, 
   p.G = G;
   p.trans = trans;
   p.scale = scale;
-  CUtensorMap tmW;
+  CUtensorMap tmW, tmX;
   int e = map_w(&tmW, W, B * H * G, T, ldw, 64);
+  if (!e) e = map_x(&tmX, x, B, T, H, D, sum ? D : E, 64, sum ? 0 : 2 * E);
   if (e) return e;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return dtype == KATA_DTYPE_BF16 ? state_dispatch<__nv_bfloat16>(p, tmW, sum, st) : state_dispatch<__half>(p, tmW, sum, st);
+  return dtype == KATA_DTYPE_BF16 ? state_dispatch<__nv_bfloat16>(p, tmW, tmX, sum, st)
+                                  : state_dispatch<__half>(p, tmW, tmX, sum, st);
 }
 
 extern "C" int kata_sp_apply(const void* x, const void* P, float* Y, int dtype, int B, int T, int H, int G, int D,
-                             int M, int ldw, float scale, int dv_mode, int Dv, kata_stream_t stream) {
+                             int M, int ldw, float scale, int dv_mode, int Dv, int* status, kata_stream_t stream) {
   using namespace sptc;
   if (!x || !P || !Y) return KATA_ERR_INVALID;
   if (dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
@@ -696,6 +802,7 @@ extern "C" int kata_sp_apply(const void* x, const void* P, float* Y, int dtype, 
   Params p{};
   p.x = x;
   p.out = Y;
+  p.status = status;
   p.B = B;
   p.T = T;
   p.H = H;
@@ -715,17 +822,17 @@ extern "C" int kata_sp_apply(const void* x, const void* P, float* Y, int dtype, 
 }
 
 extern "C" int kata_sp_grad(const void* W, const void* P, const void* x, float* dx, int dtype, int B, int T, int H,
-                            int D, int M, int ldw, float factor, kata_stream_t stream) {
+                            int D, int M, int ldw, float factor, int* status, kata_stream_t stream) {
   using namespace sptc;
   if (!x || !P || !W || !dx) return KATA_ERR_INVALID;
   if (dtype != KATA_DTYPE_BF16 && dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
   if (B < 1 || T < 1 || H < 1 || !shape_ok(D, M, ldw, false)) return KATA_ERR_SHAPE;
-  if ((M * (D / M) * (D / M)) % 256) return KATA_ERR_SHAPE;
   if (!al16(x) || !al16(P) || !al16(W) || !al16(dx)) return KATA_ERR_ALIGN;
   const int E = D / M;
   Params p{};
   p.x = x;
   p.dx = dx;
+  p.status = status;
   p.B = B;
   p.T = T;
   p.H = H;
@@ -735,11 +842,13 @@ extern "C" int kata_sp_grad(const void* W, const void* P, const void* x, float* 
   p.ldw = ldw;
   p.G = 1;
   p.factor = factor;
-  CUtensorMap tmW, tmP;
+  p.tiles_per_cta = grad_tiles_per_cta(p.F, B * H, T);
+  CUtensorMap tmW, tmP, tmX;
   int e = map_w(&tmW, W, B * H, T, ldw, 128);
   if (!e) e = map_p(&tmP, P, B * H, ldw, p.F, nw_of(ldw));
+  if (!e) e = map_x(&tmX, x, B, T, H, D, E, 128, 2 * E);
   if (e) return e;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return dtype == KATA_DTYPE_BF16 ? grad_dispatch<__nv_bfloat16>(p, tmW, tmP, st)
-                                  : grad_dispatch<__half>(p, tmW, tmP, st);
+  return dtype == KATA_DTYPE_BF16 ? grad_dispatch<__nv_bfloat16>(p, tmW, tmP, tmX, st)
+                                  : grad_dispatch<__half>(p, tmW, tmP, tmX, st);
 }

@@ -115,7 +115,8 @@ def kata_attn_state(k, v, num_groups=4, scale=None, score="concat", c=None, HQ=N
         S = torch.empty(B * H * G, F, ldw, device=k.device, dtype=torch.float32)
         _lib.check(_lib.lib().kata_sp_state(kc.data_ptr(), V1.data_ptr(), S.data_ptr(), _lib.DTYPE[k.dtype], B, T, H,
                                             G, D, num_groups, _lib.SCORE[score], ldw, float(scale), 0, ldw,
-                                            _lib.stream_handle(k.device)), "kata_sp_state")
+                                            _lib.status_word(k.device).data_ptr(), _lib.stream_handle(k.device)),
+                   "kata_sp_state")
         return S
     Rk = state_features(k, num_groups, scale, score)
     if G > 1:

@@ -130,7 +130,8 @@ def _state(x, W, num_groups, scale):
     S = torch.empty(B * H, ldw, F, device=x.device, dtype=torch.float32)
     _lib.check(_lib.lib().kata_sp_state(x.data_ptr(), W.data_ptr(), S.data_ptr(), _lib.DTYPE[x.dtype], B, T, H, 1, D,
                                         num_groups, _lib.SCORE["concat"], ldw, float(scale), 1, ldw,
-                                        _lib.stream_handle(x.device)), "kata_sp_state")
+                                        _lib.status_word(x.device).data_ptr(), _lib.stream_handle(x.device)),
+               "kata_sp_state")
     return S
 
 
@@ -150,8 +151,8 @@ def _apply(x, Pt, num_groups, scale, dv=None):
     Y = dv if dv is not None else torch.empty(B * H, T, ldw, device=x.device, dtype=torch.float32)
     _lib.check(_lib.lib().kata_sp_apply(x.data_ptr(), Pt.data_ptr(), Y.data_ptr(), _lib.DTYPE[x.dtype], B, T, H, 1, D,
                                         num_groups, ldw, float(scale), int(dv is not None),
-                                        dv.shape[-1] if dv is not None else 0, _lib.stream_handle(x.device)),
-               "kata_sp_apply")
+                                        dv.shape[-1] if dv is not None else 0, _lib.status_word(x.device).data_ptr(),
+                                        _lib.stream_handle(x.device)), "kata_sp_apply")
     return None if dv is not None else Y
 
 
@@ -165,7 +166,8 @@ def _grad(W, Pt, x, dx, num_groups, scale):
         _contract(G, x, dx, num_groups, scale)
         return
     _lib.check(_lib.lib().kata_sp_grad(W.data_ptr(), Pt.data_ptr(), x.data_ptr(), dx.data_ptr(), _lib.DTYPE[x.dtype],
-                                       B, T, H, D, num_groups, ldw, 2.0 * float(scale), _lib.stream_handle(x.device)),
+                                       B, T, H, D, num_groups, ldw, 2.0 * float(scale),
+                                       _lib.status_word(x.device).data_ptr(), _lib.stream_handle(x.device)),
                "kata_sp_grad")
 
 

@@ -4,7 +4,8 @@ form it in shared memory (product first, then the scale), W and P^T in bf16.  Th
 fp32 in another order than torch, so they agree to fp32 rounding (rel-L2 <= 1e-5).  Covers both
 head widths (E = 16, 32), both row widths of [v | 1 | 0] (ldw 72 and 136 -> N 80 and 144), ragged
 token counts, the transposed and the decode layouts of the state, grouped heads (G = 2), the sum
-score's state, and the dv-accumulating form of apply."""
+score's state, the dv-accumulating form of apply, and token / feature counts that wrap every stage
+ring of the kernels' pipelines; the device status word stays 0 (no wait ran out)."""
 
 from __future__ import annotations
 
@@ -45,6 +46,7 @@ def draw(B, T, H, D, ldw, seed, dtype=torch.bfloat16):
     (1, 130, 2, 64, 2, 136, "concat", 0, 2),
     (2, 257, 1, 128, 4, 136, "sum", 0, 1),
     (1, 100, 2, 64, 4, 72, "sum", 0, 2),
+    (1, 1000, 1, 128, 4, 72, "concat", 1, 1),
 ])
 def test_state_matches_torch(B, T, H, D, M, ldw, score, trans, G):
     from linatt_b200 import _lib
@@ -57,11 +59,13 @@ def test_state_matches_torch(B, T, H, D, M, ldw, score, trans, G):
     Rg = R.view(B, H, 1, T, F).expand(B, H, G, T, F).reshape(B * H * G, T, F)
     ref = torch.bmm(Rg.transpose(1, 2), W.float())  # (B*H*G, F, ldw)
     lds = ldw + 4
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     S = torch.full((B * H * G, ldw, F) if trans else (B * H * G, F, lds), float("nan"), device="cuda")
     _lib.check(_lib.lib().kata_sp_state(x.data_ptr(), W.data_ptr(), S.data_ptr(), 1, B, T, H, G, D, M,
-                                        _lib.SCORE[score], ldw, scale, trans, lds,
+                                        _lib.SCORE[score], ldw, scale, trans, lds, status.data_ptr(),
                                         torch.cuda.current_stream().cuda_stream), "kata_sp_state")
     torch.cuda.synchronize()
+    assert status.item() == 0
     got = S.transpose(1, 2) if trans else S[..., :ldw]
     assert torch.isfinite(S).all()
     # the sum score's features add M products before their bf16 rounding, in fp32 in the kernel and
@@ -89,26 +93,29 @@ def test_apply_matches_torch(B, T, H, D, M, ldw, G, dv_mode):
     Pg = Pt.float().view(B, H // G, 1, ldw, F).expand(B, H // G, G, ldw, F).reshape(B * H, ldw, F)
     ref = torch.bmm(R, Pg.transpose(1, 2))  # (B*H, T, ldw)
     st = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     if dv_mode:
         Dv = ldw - 8
         dv0 = torch.randn(B, T, H, Dv, device="cuda")
         dv = dv0.clone()
         _lib.check(_lib.lib().kata_sp_apply(x.data_ptr(), Pt.data_ptr(), dv.data_ptr(), 1, B, T, H, G, D, M, ldw,
-                                            scale, 1, Dv, st), "kata_sp_apply")
+                                            scale, 1, Dv, status.data_ptr(), st), "kata_sp_apply")
         torch.cuda.synchronize()
+        assert status.item() == 0
         want = dv0 + ref[..., :Dv].reshape(B, H, T, Dv).permute(0, 2, 1, 3)
         assert rel(dv - dv0, want - dv0) < 1e-5
     else:
         Y = torch.full((B * H, T, ldw), float("nan"), device="cuda")
         _lib.check(_lib.lib().kata_sp_apply(x.data_ptr(), Pt.data_ptr(), Y.data_ptr(), 1, B, T, H, G, D, M, ldw,
-                                            scale, 0, 0, st), "kata_sp_apply")
+                                            scale, 0, 0, status.data_ptr(), st), "kata_sp_apply")
         torch.cuda.synchronize()
+        assert status.item() == 0
         assert torch.isfinite(Y).all()
         assert rel(Y, ref) < 1e-5
 
 
 @pytest.mark.parametrize("B,T,H,D,M,ldw", [(1, 300, 2, 128, 4, 136), (2, 64, 1, 64, 4, 72), (1, 257, 1, 128, 8, 136),
-                                           (1, 130, 2, 64, 2, 72)])
+                                           (1, 130, 2, 64, 2, 72), (1, 1100, 1, 64, 2, 72)])
 def test_grad_matches_torch(B, T, H, D, M, ldw):
     from linatt_b200 import _lib
 
@@ -125,9 +132,12 @@ def test_grad_matches_torch(B, T, H, D, M, ldw):
     ref = 2 * scale * torch.einsum("zhtgac,zhtgc->zhtga", Gg, xg).permute(0, 2, 1, 3, 4).reshape(B, T, H, D)
     dx0 = torch.randn(B, T, H, D, device="cuda")
     dx = dx0.clone()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     _lib.check(_lib.lib().kata_sp_grad(W.data_ptr(), Pt.data_ptr(), x.data_ptr(), dx.data_ptr(), 1, B, T, H, D, M, ldw,
-                                       2 * scale, torch.cuda.current_stream().cuda_stream), "kata_sp_grad")
+                                       2 * scale, status.data_ptr(), torch.cuda.current_stream().cuda_stream),
+               "kata_sp_grad")
     torch.cuda.synchronize()
+    assert status.item() == 0
     assert rel(dx - dx0, ref) < 1e-5
 
 
@@ -136,6 +146,6 @@ def test_shapes_outside_the_envelope_are_refused():
 
     L = _lib.lib()
     # E = 64 (D = 128, M = 2) and ldw > 144 are not covered: the caller takes the materialised route
-    assert L.kata_sp_state(16, 16, 16, 1, 1, 64, 1, 1, 128, 2, 0, 136, 1.0, 1, 136, None) == -3
-    assert L.kata_sp_apply(16, 16, 16, 1, 1, 64, 1, 1, 128, 4, 152, 1.0, 0, 0, None) == -3
-    assert L.kata_sp_grad(16, 16, 16, 16, 0, 1, 64, 1, 128, 4, 136, 1.0, None) == -2
+    assert L.kata_sp_state(16, 16, 16, 1, 1, 64, 1, 1, 128, 2, 0, 136, 1.0, 1, 136, None, None) == -3
+    assert L.kata_sp_apply(16, 16, 16, 1, 1, 64, 1, 1, 128, 4, 152, 1.0, 0, 0, None, None) == -3
+    assert L.kata_sp_grad(16, 16, 16, 16, 0, 1, 64, 1, 128, 4, 136, 1.0, None, None) == -2
