@@ -340,7 +340,9 @@ KATA_API int kata_sp_bwd_prep(const void* o, const void* dout, const float* D_in
                               int H, int Dv, int ldw, kata_stream_t stream);
 
 /* Quadratic-feature contractions on the tensor cores, psi formed in shared memory (never written to
- * global memory).  psi is the concat map above (F = M E^2), or for score == KATA_SCORE_SUM in
+ * global memory) as the bf16 rounding of the unscaled products x_a x_b (sum score: of the fp32 sum over
+ * groups), the scale multiplying the fp32 result.  psi is the concat map above (F = M E^2), or for
+ * score == KATA_SCORE_SUM in
  * kata_sp_state the sum map psi[a,b] = scale sum_g x_{g,a} x_{g,b} (F = E^2).  x is a (B,T,H,D) 16-bit
  * token tensor (q or k) with E = D / M in {16, 32} and D in {64, 128} (sum score: M <= 4); W is
  * (B*H, T, ldw) bf16 and P^T (B*H, ldw, F) bf16, ldw a multiple of 8, <= 144.  All pointers 16-byte

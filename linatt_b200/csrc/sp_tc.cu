@@ -4,14 +4,18 @@
 // psi(x)[a,b] = scale * sum_g x_{g,a} x_{g,b} (sum score, F = E^2), KATA-SPD attention of a query on
 // an earlier block of keys is psi(q)^T P with the additive state P = sum_s psi(k_s) [v_s | 1].  The
 // products here never materialise psi in global memory: every kernel forms its psi tiles in shared
-// memory from the 16-bit token rows, rounded to bf16 exactly as a materialised feature tensor would
-// be (product first, then the scale), and feeds them to tcgen05.mma with fp32 accumulation in TMEM.
+// memory from the 16-bit token rows and feeds them to tcgen05.mma with fp32 accumulation in TMEM.
+// The tiles hold the unscaled products x_a x_b rounded to bf16 (for bf16 rows one packed
+// mul.rn.bf16x2 per two features: the product of two bf16 values is exact in fp32, so this is the
+// same single rounding), or for the sum score the fp32 sum over groups rounded to bf16; the scale
+// multiplies the fp32 result in the epilogue.
 //
 //   state  S[f, n]  = sum_t psi(x_t)[f] W[t, n]      one CTA per (256 features, head): two M = 128
 //                                                    MMAs per K step, N = NW (the [v | 1 | 0] row
 //                                                    rounded up to 16), K = tokens in blocks of 64
 //   apply  Y[t, n]  = sum_f psi(x_t)[f] P[f, n]      one CTA per (256 tokens, head): two M = 128 MMAs,
-//                                                    N = NW, K = features in blocks of 64
+//                                                    N = NW, K = features in blocks of 64; psi goes
+//                                                    to TMEM (the A operand read from tensor memory)
 //   grad   dx[t, (g,a)] += c * sum_b (W P^T)[t, (g,a,b)] x[t, (g,b)]
 //                                                    one CTA per (256 features, head, token range):
 //                                                    the P^T slice stays in shared memory, W streams
@@ -19,6 +23,10 @@
 // The operand that streams is the one whose reuse the CTA cannot hold: W (tokens) in `state` and
 // `grad`, P^T (features) in `apply`; each CTA makes 256 rows of output per streamed byte, twice the
 // reuse of a single 128-row MMA.
+//
+// Shared memory bandwidth (128 B per clock per SM) is what these kernels share out: every M = 128 MMA
+// reads its A and B tiles from it, TMA writes the streamed tiles into it and the psi producers
+// store into it.  `apply`, whose psi rows are token rows (TMEM lanes), keeps psi out of it.
 //
 // Every kernel runs 320 threads: warps 0-7 form psi (or run the epilogue of `grad`), warp 8 issues
 // the TMA loads of a ring of stages, warp 9 issues the MMAs.  Stages are handed over by mbarriers
@@ -32,6 +40,8 @@
 // (B*H, F, lds) layout instead.  W (B*H, T, ldw) and P^T (B*H, ldw, F) are bf16, and the token rows
 // of `state` and `grad` arrive by TMA as well (no multicast); `apply` reads each token's row with
 // plain 16-byte loads.  ldw <= 144, a multiple of 8.
+#include <type_traits>
+
 #include "attn_common.cuh"
 #include "attn_tc_common.cuh"
 #include "host_util.h"
@@ -113,6 +123,26 @@ __device__ __forceinline__ float elem_swz(const T* tile, int row, int e) {
   return to_f32<T>(*reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(tile) + swz_offset(row, 2 * e, 2 * E)));
 }
 __device__ __forceinline__ uint32_t bf16x2(float2 v) { return pack2<__nv_bfloat16>(v.x, v.y); }
+// Two bf16 products a * b, each rounded once to nearest even.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// The 16-bit half `hi` of a word in both halves.
+__device__ __forceinline__ uint32_t bcast16(uint32_t w, int hi) { return __byte_perm(w, 0, hi ? 0x3232 : 0x1010); }
+// The E / 2 words (16-bit pairs) of row `row` of a [rows][E] tile written with the 2E-byte swizzle.
+template <int E>
+__device__ __forceinline__ void load_words_swz(const void* tile, int row, uint32_t (&w)[E / 2]) {
+  const uint8_t* base = static_cast<const uint8_t*>(tile);
+#pragma unroll
+  for (int c = 0; c < E / 8; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + swz_offset(row, 16 * c, 2 * E));
+    w[4 * c] = v.x, w[4 * c + 1] = v.y, w[4 * c + 2] = v.z, w[4 * c + 3] = v.w;
+  }
+}
+template <typename T>
+constexpr bool kIsBf16 = std::is_same<T, __nv_bfloat16>::value;
 // One arrival per compute warp (barriers of the compute warps count kComputeWarps): the warp's
 // shared-memory writes or reads, ordered by __syncwarp, are released by lane 0's arrive.
 constexpr int kComputeWarps = kCompute / 32;
@@ -133,9 +163,10 @@ struct StateSmem {
   static constexpr int SW = SUM ? 3 : 4;     // W / token-row ring
   static constexpr int XW = SUM ? 4 * E : E;  // 16-bit values per token row held (sum: all M <= 4 groups)
   uint8_t W[SW][NWB][64 * kRowB];
-  uint8_t psi[2][4][64 * kRowB];
+  static constexpr int SP = 3;                 // psi ring
+  uint8_t psi[SP][4][64 * kRowB];
   T xs[SW][64 * XW];  // token rows: concat [64][E] with the 2E-byte swizzle, sum [64][D] dense
-  uint64_t tfull[SW], mdone[SW], pfull[2];
+  uint64_t tfull[SW], mdone[SW], pfull[SP];
   uint32_t tmem;
   int abort;
 };
@@ -144,7 +175,7 @@ template <typename T, int E, bool SUM, int NW>
 __global__ void __launch_bounds__(kThreads, 1)
     sp_state_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Params p) {
   using L = StateSmem<T, E, SUM, NW>;
-  constexpr int SW = L::SW, NWB = L::NWB, EE = E * E, CPB = 64 / E;
+  constexpr int SW = L::SW, SP = L::SP, NWB = L::NWB, EE = E * E, CPB = 64 / E;
   extern __shared__ uint8_t smraw[];
   L& sm = *reinterpret_cast<L*>(align1k(smraw));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -161,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.tfull[s], 1);
       mbar_init(&sm.mdone[s], 1);
     }
-    for (int s = 0; s < 2; ++s) mbar_init(&sm.pfull[s], kComputeWarps);
+    for (int s = 0; s < SP; ++s) mbar_init(&sm.pfull[s], kComputeWarps);
     fence_mbar_init();
   }
   if (warp == kProducerWarp) {
@@ -193,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(128, NW, true, true, true);
       for (int i = 0; i < nblk; ++i) {
-        const int s = i % SW, ps = i & 1;
-        if (!mbar_wait(&sm.tfull[s], par(i / SW), wc) || !mbar_wait(&sm.pfull[ps], par(i >> 1), wc)) break;
+        const int s = i % SW, ps = i % SP;
+        if (!mbar_wait(&sm.tfull[s], par(i / SW), wc) || !mbar_wait(&sm.pfull[ps], par(i / SP), wc)) break;
         tc_fence_after();
         const uint64_t ad0 = umma_smem_desc(smem_u32(sm.psi[ps][0]), 64 * kRowB, 1024, 128);
         const uint64_t ad1 = umma_smem_desc(smem_u32(sm.psi[ps][2]), 64 * kRowB, 1024, 128);
@@ -213,16 +244,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int t = tid & 63, q = tid >> 6;  // token row of the block, 64-feature box
     const int aq = a0 + (64 * q) / E;      // first a-value of the box
-    const float2 s2 = make_float2(p.scale, p.scale);
     for (int i = 0; i < nblk; ++i) {
-      const int s = i % SW, ps = i & 1;
+      const int s = i % SW, ps = i % SP;
       if (!mbar_wait_w(&sm.tfull[s], par(i / SW), wc)) break;
-      if (i >= 2 && !mbar_wait_w(&sm.mdone[(i - 2) % SW], par((i - 2) / SW), wc)) break;  // psi[ps] is free
-      float2 v[32];  // the box row: features 2c, 2c+1 = (a = aq + 2c / E, b = 2c % E and + 1)
-      if constexpr (SUM) {  // rows of xw = D values, unswizzled
+      if (i >= SP && !mbar_wait_w(&sm.mdone[(i - SP) % SW], par((i - SP) / SW), wc)) break;  // psi[ps] is free
+      uint32_t v[32];  // the box row as bf16 pairs: features 2c, 2c+1 = (a = aq + 2c / E, b = 2c % E and + 1)
+      if constexpr (SUM) {  // rows of xw = D values, unswizzled; fp32 sums over the groups
         const T* xr = sm.xs[s] + t * xw;
+        float2 acc[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) v[c] = make_float2(0.f, 0.f);
+        for (int c = 0; c < 32; ++c) acc[c] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int gg = 0; gg < 4; ++gg) {
           if (gg < p.M) {
@@ -233,13 +264,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
               const int k = (2 * c) / E, bb = (2 * c) % E;
-              v[c] = ffma2(make_float2(xa[k], xa[k]), make_float2(xb[bb], xb[bb + 1]), v[c]);
+              acc[c] = ffma2(make_float2(xa[k], xa[k]), make_float2(xb[bb], xb[bb + 1]), acc[c]);
             }
           }
         }
 #pragma unroll
-        for (int c = 0; c < 32; ++c) v[c] = fmul2(s2, v[c]);
-      } else {  // rows of E values, 2E-byte swizzle
+        for (int c = 0; c < 32; ++c) v[c] = bf16x2(acc[c]);
+      } else if constexpr (kIsBf16<T>) {  // rows of E values, 2E-byte swizzle: packed bf16 products
+        uint32_t xw2[E / 2], xa[CPB];
+        load_words_swz<E>(sm.xs[s], t, xw2);
+        const uint8_t* xt = reinterpret_cast<const uint8_t*>(sm.xs[s]);
+#pragma unroll
+        for (int k = 0; k < CPB; ++k)
+          xa[k] = bcast16(*reinterpret_cast<const uint16_t*>(xt + swz_offset(t, 2 * (aq + k), 2 * E)), 0);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = bmul2(xa[(2 * c) / E], xw2[((2 * c) % E) / 2]);
+      } else {  // fp16 rows: fp32 products, one rounding to bf16
         float xb[E], xa[CPB];
         load_row_swz<T, E>(sm.xs[s], t, xb);
 #pragma unroll
@@ -247,14 +287,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int k = (2 * c) / E, bb = (2 * c) % E;
-          v[c] = fmul2(s2, fmul2(make_float2(xa[k], xa[k]), make_float2(xb[bb], xb[bb + 1])));
+          v[c] = bf16x2(fmul2(make_float2(xa[k], xa[k]), make_float2(xb[bb], xb[bb + 1])));
         }
       }
       const uint32_t base = smem_u32(sm.psi[ps][q]);
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8)
-        st_shared_v4(base + swz_offset(t, 16 * c8, 128), bf16x2(v[4 * c8]), bf16x2(v[4 * c8 + 1]),
-                     bf16x2(v[4 * c8 + 2]), bf16x2(v[4 * c8 + 3]));
+        st_shared_v4(base + swz_offset(t, 16 * c8, 128), v[4 * c8], v[4 * c8 + 1], v[4 * c8 + 2], v[4 * c8 + 3]);
       fence_proxy_async_smem();
       warp_arrive(&sm.pfull[ps]);
     }
@@ -276,8 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 16; ++j) {
         const int n = c0 + j;
         if (n < p.ldw) {
-          if (p.trans) out[static_cast<size_t>(n) * p.F + fl] = __uint_as_float(r[j]);
-          else out[static_cast<size_t>(fl) * p.lds + n] = __uint_as_float(r[j]);
+          const float y = p.scale * __uint_as_float(r[j]);
+          if (p.trans) out[static_cast<size_t>(n) * p.F + fl] = y;
+          else out[static_cast<size_t>(fl) * p.lds + n] = y;
         }
       }
     }
@@ -295,21 +335,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------------
-// apply: one CTA per (256-token tile, head); K-loop over the F features in blocks of 64.  A = psi,
-// K-major [256 tokens][64 features]: rows 0-127 feed accumulator 0, rows 128-255 accumulator 1.
-// B = the P^T block [NW rows][64 features], K-major.  Compute thread r owns token t0 + r: it keeps
-// its current group's E values in registers (the next group's are loaded one group ahead).
+// apply: one CTA per (256-token tile, head); K-loop over the F features in blocks of 64.  A = psi
+// in TMEM, [128 lanes = tokens][32 columns = 64 features as bf16 pairs] per MMA: tokens 0-127 feed
+// accumulator 0, tokens 128-255 accumulator 1.  B = the P^T block [NW rows][64 features], K-major,
+// in shared memory.  Compute thread r owns token t0 + r (TMEM lane r % 128 of its half's A tile): it
+// keeps its current group's E values in registers (the next group's loaded one group ahead) and
+// writes its 32 psi columns with one tcgen05.st per block.
+// TMEM columns: accumulator 0 at 0, accumulator 1 at 256; the three psi stages take the 32-column
+// halves {144, 176}, {400, 432} and {208, 464} (free for both N = 80 and N = 144).
 // ------------------------------------------------------------------------------------------------
 template <int NW>
 struct ApplySmem {
   static constexpr int SW = 4;  // P^T ring
-  static constexpr int SP = 3;  // psi ring
+  static constexpr int SP = 3;  // psi ring (TMEM)
   uint8_t P[SW][NW * kRowB];
-  uint8_t psi[SP][256 * kRowB];
   uint64_t pfull[SW], mdone[SW], sfull[SP];
   uint32_t tmem;
   int abort;
 };
+__device__ __forceinline__ uint32_t apply_psi_col(int stage, int half) {
+  if (stage == 2) return half ? 464u : 208u;
+  return (stage ? 400u : 144u) + 32u * static_cast<uint32_t>(half);
+}
 
 template <typename T, int E, int D, int NW>
 __global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_constant__ CUtensorMap tmP, Params p) {
@@ -360,14 +407,13 @@ __global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_cons
         const int s = i % SW, ps = i % SP;
         if (!mbar_wait(&sm.pfull[s], par(i / SW), wc) || !mbar_wait(&sm.sfull[ps], par(i / SP), wc)) break;
         tc_fence_after();
-        const uint64_t ad0 = umma_smem_desc(smem_u32(sm.psi[ps]), 16, 1024, 128);
-        const uint64_t ad1 = umma_smem_desc(smem_u32(sm.psi[ps] + 128 * kRowB), 16, 1024, 128);
+        const uint32_t a0 = tbase + apply_psi_col(ps, 0), a1 = tbase + apply_psi_col(ps, 1);
         const uint64_t bd = umma_smem_desc(smem_u32(sm.P[s]), 16, 1024, 128);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {  // 16 features = 32 bytes of each row per K step
+        for (int kk = 0; kk < 4; ++kk) {  // 16 features = 8 TMEM columns of A, 32 bytes of each B row
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_ss(tbase, ad0 + 2u * kk, bd + 2u * kk, idesc, acc);
-          umma_ss(tbase + 256u, ad1 + 2u * kk, bd + 2u * kk, idesc, acc);
+          umma_ts(tbase, a0 + 8u * kk, bd + 2u * kk, idesc, acc);
+          umma_ts(tbase + 256u, a1 + 8u * kk, bd + 2u * kk, idesc, acc);
         }
         umma_commit(&sm.mdone[s]);
         committed = i + 1;
@@ -378,20 +424,23 @@ __global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_cons
     const int r = tid, t = t0 + r;
     const bool tin = t < p.T;
     const T* xrow = static_cast<const T*>(p.x) + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D;
-    const float2 s2 = make_float2(p.scale, p.scale);
     uint4 nxt[E / 8];  // the next group's values, loaded one group ahead
 #pragma unroll
     for (int c = 0; c < E / 8; ++c)
       nxt[c] = tin ? reinterpret_cast<const uint4*>(xrow)[c] : make_uint4(0u, 0u, 0u, 0u);
-    const uint32_t row_base = smem_u32(sm.psi[0]);
+    const uint32_t lane_base = tbase + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
     bool ok = true;
     for (int g = 0; g < p.M && ok; ++g) {
-      float xg[E];
+      uint32_t xw2[E / 2];  // the group's values as 16-bit pairs
+      float xg[kIsBf16<T> ? 1 : E];
 #pragma unroll
       for (int c = 0; c < E / 8; ++c) {
-        const T* e = reinterpret_cast<const T*>(&nxt[c]);
+        xw2[4 * c] = nxt[c].x, xw2[4 * c + 1] = nxt[c].y, xw2[4 * c + 2] = nxt[c].z, xw2[4 * c + 3] = nxt[c].w;
+        if constexpr (!kIsBf16<T>) {
+          const T* e = reinterpret_cast<const T*>(&nxt[c]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) xg[8 * c + j] = to_f32<T>(e[j]);
+          for (int j = 0; j < 8; ++j) xg[8 * c + j] = to_f32<T>(e[j]);
+        }
       }
       if (g + 1 < p.M) {
 #pragma unroll
@@ -402,19 +451,17 @@ __global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_cons
       for (int ii = 0; ii < BPG; ++ii) {
         const int i = g * BPG + ii, ps = i % SP;
         if (i >= SP && !(ok = mbar_wait_w(&sm.mdone[(i - SP) % SW], par((i - SP) / SW), wc))) break;
-        const uint32_t base = row_base + static_cast<uint32_t>(ps) * (256 * kRowB);
+        uint32_t wv[32];  // column c: features 2c, 2c+1 of the block
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t wv[4];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const int j0 = 64 * ii + 8 * c8 + 2 * e2;  // feature within the group (even)
-            const int a = j0 / E, bb = j0 % E;
-            wv[e2] = bf16x2(fmul2(s2, fmul2(make_float2(xg[a], xg[a]), make_float2(xg[bb], xg[bb + 1]))));
-          }
-          st_shared_v4(base + swz_offset(r, 16 * c8, 128), wv[0], wv[1], wv[2], wv[3]);
+        for (int c = 0; c < 32; ++c) {
+          const int j0 = 64 * ii + 2 * c;  // feature within the group (even)
+          const int a = j0 / E, bb = j0 % E;
+          if constexpr (kIsBf16<T>) wv[c] = bmul2(bcast16(xw2[a / 2], a & 1), xw2[bb / 2]);
+          else wv[c] = bf16x2(fmul2(make_float2(xg[a], xg[a]), make_float2(xg[bb], xg[bb + 1])));
         }
-        fence_proxy_async_smem();
+        tmem_st32(lane_base + apply_psi_col(ps, warp >> 2), wv);
+        tmem_wait_st();
+        tc_fence_before();
         warp_arrive(&sm.sfull[ps]);
       }
     }
@@ -442,8 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_cons
         for (int j = 0; j < 16; j += 4) {
           if (c0 + j < ncols) {
             float4* d4 = reinterpret_cast<float4*>(row + c0 + j);
-            float4 y = make_float4(__uint_as_float(rv[j]), __uint_as_float(rv[j + 1]), __uint_as_float(rv[j + 2]),
-                                   __uint_as_float(rv[j + 3]));
+            float4 y = make_float4(p.scale * __uint_as_float(rv[j]), p.scale * __uint_as_float(rv[j + 1]),
+                                   p.scale * __uint_as_float(rv[j + 2]), p.scale * __uint_as_float(rv[j + 3]));
             if (p.mode) {
               const float4 o = *d4;
               y.x += o.x, y.y += o.y, y.z += o.z, y.w += o.w;
@@ -454,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) sp_apply_kernel(const __grid_cons
       } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (c0 + j < ncols) row[c0 + j] += __uint_as_float(rv[j]);
+          if (c0 + j < ncols) row[c0 + j] += p.scale * __uint_as_float(rv[j]);
       }
     }
   }
@@ -577,36 +624,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       float xg[E];
       load_row_swz<T, E>(sm.xs[s], r, xg);
       warp_arrive(&sm.xfree[s]);
+      // this tile's dx values, loaded while the MMAs run
+      const int t = 128 * (tile0 + j) + r;
+      const bool tin = t < p.T;
+      float4* d4 = reinterpret_cast<float4*>(p.dx + ((static_cast<size_t>(b) * p.T + (tin ? t : 0)) * p.H + h) * D +
+                                             g * E + a0 + NA * hh);
+      float4 dv[NA / 4];
+#pragma unroll
+      for (int c = 0; c < NA / 4; ++c) dv[c] = tin ? d4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
       if (!mbar_wait_w(&sm.mdone[ab], par(j >> 1), wc)) break;
       tc_fence_after();
       float sums[NA];
 #pragma unroll
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        uint32_t rv[32];
-        tmem_ld32(lanebase + 256u * ab + c0, rv);
+      for (int c0 = 0; c0 < 128; c0 += 64) {  // two 32-column loads per wait
+        uint32_t rv[64];
+        tmem_ld32(lanebase + 256u * ab + c0, *reinterpret_cast<uint32_t(*)[32]>(rv));
+        tmem_ld32(lanebase + 256u * ab + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(rv + 32));
         tmem_wait_ld();
+        if (c0 == 64) {  // the accumulator buffer is read: tile j+2's MMAs may overwrite it
+          tc_fence_before();
+          warp_arrive(&sm.accfree[ab]);
+        }
 #pragma unroll
-        for (int part = 0; part < 32 / E; ++part) {
+        for (int part = 0; part < 64 / E; ++part) {
           float sacc = 0.f;
 #pragma unroll
           for (int jj = 0; jj < E; ++jj) sacc = fmaf(__uint_as_float(rv[part * E + jj]), xg[jj], sacc);
           sums[(c0 + part * E) / E] = sacc;
         }
       }
-      tc_fence_before();
-      warp_arrive(&sm.accfree[ab]);
-      const int t = 128 * (tile0 + j) + r;
-      if (t < p.T) {
-        float4* d4 = reinterpret_cast<float4*>(p.dx + ((static_cast<size_t>(b) * p.T + t) * p.H + h) * D + g * E +
-                                               a0 + NA * hh);
+      if (tin) {
 #pragma unroll
         for (int c = 0; c < NA / 4; ++c) {
-          float4 v = d4[c];
-          v.x = fmaf(p.factor, sums[4 * c], v.x);
-          v.y = fmaf(p.factor, sums[4 * c + 1], v.y);
-          v.z = fmaf(p.factor, sums[4 * c + 2], v.z);
-          v.w = fmaf(p.factor, sums[4 * c + 3], v.w);
-          d4[c] = v;
+          dv[c].x = fmaf(p.factor, sums[4 * c], dv[c].x);
+          dv[c].y = fmaf(p.factor, sums[4 * c + 1], dv[c].y);
+          dv[c].z = fmaf(p.factor, sums[4 * c + 2], dv[c].z);
+          dv[c].w = fmaf(p.factor, sums[4 * c + 3], dv[c].w);
+          d4[c] = dv[c];
         }
       }
     }

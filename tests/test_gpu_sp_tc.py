@@ -1,6 +1,7 @@
 """The quadratic-feature contractions on the tensor cores (kata_sp_state / kata_sp_apply /
 kata_sp_grad) against torch fp32 on the same operands: psi rounded to bf16 exactly as the kernels
-form it in shared memory (product first, then the scale), W and P^T in bf16.  The kernels sum in
+form it in shared memory (the unscaled products, or the sum score's fp32 group sums), the scale
+applied to the fp32 result, W and P^T in bf16.  The kernels sum in
 fp32 in another order than torch, so they agree to fp32 rounding (rel-L2 <= 1e-5).  Covers both
 head widths (E = 16, 32), both row widths of [v | 1 | 0] (ldw 72 and 136 -> N 80 and 144), ragged
 token counts, the transposed and the decode layouts of the state, grouped heads (G = 2), the sum
@@ -15,15 +16,15 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def psi(x, M, scale, score="concat"):
-    """(B,T,H,D) -> (B*H, T, F) bf16, the kernels' feature map."""
+def psi(x, M, score="concat"):
+    """(B,T,H,D) -> (B*H, T, F) bf16, the kernels' unscaled feature map."""
     B, T, H, D = x.shape
     E = D // M
     xg = x.float().view(B, T, H, M, E)
     if score == "sum":
-        R = torch.einsum("bthga,bthgc->bhtac", xg, xg).mul_(scale).reshape(B * H, T, E * E)
+        R = torch.einsum("bthga,bthgc->bhtac", xg, xg).reshape(B * H, T, E * E)
     else:
-        R = (xg[..., :, None] * xg[..., None, :]).mul_(scale).permute(0, 2, 1, 3, 4, 5).reshape(B * H, T, M * E * E)
+        R = (xg[..., :, None] * xg[..., None, :]).permute(0, 2, 1, 3, 4, 5).reshape(B * H, T, M * E * E)
     return R.to(torch.bfloat16)
 
 
@@ -54,10 +55,10 @@ def test_state_matches_torch(B, T, H, D, M, ldw, score, trans, G):
     scale = 0.37
     x, W = draw(B, T, H, D, ldw, 11 + T)
     W = torch.randn(B * H * G, T, ldw, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3)).bfloat16()
-    R = psi(x, M, scale, score).float()  # (B*H, T, F)
+    R = psi(x, M, score).float()  # (B*H, T, F)
     F = R.shape[-1]
     Rg = R.view(B, H, 1, T, F).expand(B, H, G, T, F).reshape(B * H * G, T, F)
-    ref = torch.bmm(Rg.transpose(1, 2), W.float())  # (B*H*G, F, ldw)
+    ref = scale * torch.bmm(Rg.transpose(1, 2), W.float())  # (B*H*G, F, ldw)
     lds = ldw + 4
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     S = torch.full((B * H * G, ldw, F) if trans else (B * H * G, F, lds), float("nan"), device="cuda")
@@ -86,12 +87,12 @@ def test_apply_matches_torch(B, T, H, D, M, ldw, G, dv_mode):
 
     scale = 0.61
     x, _ = draw(B, T, H, D, ldw, 5 + T)
-    R = psi(x, M, scale).float()
+    R = psi(x, M).float()
     F = R.shape[-1]
     Pt = (torch.randn(B * (H // G), ldw, F, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
           / F ** 0.5).bfloat16()
     Pg = Pt.float().view(B, H // G, 1, ldw, F).expand(B, H // G, G, ldw, F).reshape(B * H, ldw, F)
-    ref = torch.bmm(R, Pg.transpose(1, 2))  # (B*H, T, ldw)
+    ref = scale * torch.bmm(R, Pg.transpose(1, 2))  # (B*H, T, ldw)
     st = torch.cuda.current_stream().cuda_stream
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     if dv_mode:
