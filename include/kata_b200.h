@@ -426,6 +426,14 @@ KATA_API int kata_selftest_umma(const void* A, const void* B, float* D, int M, i
 KATA_API int kata_selftest_umma_m64(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
                                     int lane_off, kata_stream_t stream);
 
+/* Diagnostic: D (256 x N, fp32) = A * B^T through one CTA pair (a cluster of two CTAs running
+ * cta_group::2 MMAs with M = 256).  Each CTA loads its 128 rows of A and its half of B (N/2 rows of a
+ * K-contiguous B, N/2 columns of an N-contiguous one); a_tmem == 1 stages A in tensor memory (only
+ * with a_mn == 0).  N a multiple of 32 in [32, 256]; K a multiple of 16, <= 256.
+ * No counterpart in the reference: it checks the pair layout used by the attention kernels. */
+KATA_API int kata_selftest_umma_pair(const void* A, const void* B, float* D, int N, int K, int a_mn, int b_mn,
+                                     int a_sw, int b_sw, int a_tmem, kata_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -171,6 +171,8 @@ def lib() -> ctypes.CDLL:
             L.kata_sp_grad.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_float, c_void_p, c_void_p]
             L.kata_selftest_umma_m64.restype = c_int
             L.kata_selftest_umma_m64.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 5 + [c_void_p]
+            L.kata_selftest_umma_pair.restype = c_int
+            L.kata_selftest_umma_pair.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]
             if L.kata_abi_version() != ABI_VERSION:
                 raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
             _lib = L
