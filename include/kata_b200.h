@@ -403,6 +403,78 @@ typedef struct {
 KATA_API size_t kata_decode_workspace_bytes(const kata_decode_args* args);
 KATA_API int kata_decode_step(const kata_decode_args* args, kata_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Mixer prologue / epilogue (the operations kata/layer.py runs around the attention op).
+ *
+ * Causal depthwise short convolution with optional SiLU, as fla's ShortConvolution on q, k and v
+ * (kata/layer.py:176-194 builds them, :305-319 applies them):
+ *   y[b,t,c] = act(sum_{i<K} w[c*K + i] x[b, t-K+1+i, c] + bias[c]),  x = 0 before t = 0.
+ * x rows are ldx elements apart (so q, k and v can be read as column ranges of one fused
+ * projection output), y rows ldy apart, dx rows lddx apart; C, the strides and the pointers must
+ * keep 16-byte alignment (C and strides multiples of 8 for 16-bit dtypes, of 4 for fp32).  Math in
+ * fp32; w, bias, dw, dbias fp32; K <= 4.  Backward writes dx (dtype) and dw / dbias (fp32, written,
+ * not accumulated) and needs kata_short_conv_bwd_workspace_bytes() of workspace; results do not
+ * depend on scheduling (fixed-order reduction of per-CTA partials).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* x;        /* (B, T, ldx) dtype: channels [0, C) of each row  */
+  const float* w;       /* (C, K) fp32, nn.Conv1d's (C, 1, K) weight        */
+  const float* bias;    /* (C) fp32 or NULL                                 */
+  void* y;              /* forward: (B, T, ldy) dtype [out]                 */
+  const void* dy;       /* backward: (B, T, ldy) dtype                      */
+  void* dx;             /* backward: (B, T, lddx) dtype [out]               */
+  float* dw;            /* backward: (C, K) fp32 [out]                      */
+  float* dbias;         /* backward: (C) fp32 [out] or NULL                 */
+  void* workspace;
+  size_t workspace_bytes;
+  int dtype;
+  int B, T, C, K;
+  long long ldx, ldy, lddx;
+  int activation;       /* 0 none, 1 SiLU                                    */
+} kata_conv_args;
+
+KATA_API int kata_short_conv_fwd(const kata_conv_args* args, kata_stream_t stream);
+KATA_API size_t kata_short_conv_bwd_workspace_bytes(const kata_conv_args* args);
+KATA_API int kata_short_conv_bwd(const kata_conv_args* args, kata_stream_t stream);
+
+/* Row normalisation with optional rotary embedding, over `rows` contiguous rows of N values (one
+ * (token, head) slice each; row r is position (r / heads) % T):
+ *   norm 1  l2:   y = x / sqrt(sum x^2 + eps)              (fla l2norm; kata/layer.py:346-347)
+ *   norm 2  RMS:  y = x rsqrt(mean x^2 + eps) * w (w NULL: no scale)  (fla RMSNorm: the qk norm
+ *                 of kata/layer.py:166-169 and the output norm over head_v_dim, :199-209, :539)
+ *   norm 0  none
+ * then, if rope != 0, the rotation of fla's RotaryEmbedding with tables cos/sin (T, R/2) fp32:
+ *   rope 1  interleaved pairs (2f, 2f+1) over the whole row, R = N   (kata/layer.py:147-149)
+ *   rope 2  inside every group of R values, value r < R/2 paired with r + R/2 (rope_group,
+ *           kata/layer.py:139-141, :355-366); R/2 a multiple of 8 (16-bit) or 4 (fp32)
+ * N/8 (16-bit) or N/4 (fp32) must be a power of two <= 32.  Forward stores rstd (the per-row
+ * 1/norm, fp32) when norm != 0; backward takes x, rstd, dy and writes dx, and dw (fp32, N) for RMS
+ * with a weight, using kata_rownorm_bwd_workspace_bytes() of workspace.  No counterpart in the
+ * reference as one operation: it fuses the separate fla kernels the layer calls.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* x;        /* (rows, N) dtype                                   */
+  const float* w;       /* (N) fp32 or NULL                                  */
+  const float* cos;     /* (T, R/2) fp32 or NULL                             */
+  const float* sin;     /* (T, R/2) fp32 or NULL                             */
+  void* y;              /* forward: (rows, N) dtype [out]                    */
+  float* rstd;          /* (rows) fp32: forward [out], backward [in]         */
+  const void* dy;       /* backward: (rows, N) dtype                         */
+  void* dx;             /* backward: (rows, N) dtype [out]                   */
+  float* dw;            /* backward: (N) fp32 [out]                          */
+  void* workspace;
+  size_t workspace_bytes;
+  int dtype;
+  long long rows;
+  int N, T, heads;
+  int norm, rope, R;
+  float eps;
+} kata_rownorm_args;
+
+KATA_API int kata_rownorm_fwd(const kata_rownorm_args* args, kata_stream_t stream);
+KATA_API size_t kata_rownorm_bwd_workspace_bytes(const kata_rownorm_args* args);
+KATA_API int kata_rownorm_bwd(const kata_rownorm_args* args, kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

@@ -101,6 +101,24 @@ class GdnBwdArgs(ctypes.Structure):
     ]
 
 
+class ConvArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("w", c_void_p), ("bias", c_void_p), ("y", c_void_p), ("dy", c_void_p), ("dx", c_void_p),
+        ("dw", c_void_p), ("dbias", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dtype", c_int), ("B", c_int), ("T", c_int), ("C", c_int), ("K", c_int),
+        ("ldx", ctypes.c_longlong), ("ldy", ctypes.c_longlong), ("lddx", ctypes.c_longlong), ("activation", c_int),
+    ]
+
+
+class RowNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("w", c_void_p), ("cos", c_void_p), ("sin", c_void_p), ("y", c_void_p), ("rstd", c_void_p),
+        ("dy", c_void_p), ("dx", c_void_p), ("dw", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("dtype", c_int), ("rows", ctypes.c_longlong), ("N", c_int), ("T", c_int), ("heads", c_int),
+        ("norm", c_int), ("rope", c_int), ("R", c_int), ("eps", c_float),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -173,6 +191,14 @@ def lib() -> ctypes.CDLL:
             L.kata_selftest_umma_m64.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 5 + [c_void_p]
             L.kata_selftest_umma_pair.restype = c_int
             L.kata_selftest_umma_pair.argtypes = [c_void_p, c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]
+            for nm, st in (("short_conv", ConvArgs), ("rownorm", RowNormArgs)):
+                for ph in ("fwd", "bwd"):
+                    f = getattr(L, f"kata_{nm}_{ph}")
+                    f.restype = c_int
+                    f.argtypes = [ctypes.POINTER(st), c_void_p]
+                w = getattr(L, f"kata_{nm}_bwd_workspace_bytes")
+                w.restype = c_size_t
+                w.argtypes = [ctypes.POINTER(st)]
             if L.kata_abi_version() != ABI_VERSION:
                 raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
             _lib = L

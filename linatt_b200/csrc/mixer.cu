@@ -1,0 +1,568 @@
+// mixer.cu -- the KATA mixer's prologue and epilogue around the attention op, forward and backward:
+//
+//   short convolution  y[t,c] = act(sum_i w[c,i] x[t-K+1+i, c] + bias[c]), causal, depthwise, act =
+//                      SiLU or none (fla ShortConvolution as used on q, k, v by kata/layer.py:305-319)
+//   row normalisation  per row of N values (a (token, head) slice): l2 (x / sqrt(sum x^2 + eps),
+//                      fla l2norm) or RMS (x rsqrt(mean x^2 + eps) w, fla RMSNorm), then optionally
+//                      RoPE (kata/layer.py:344-372: interleaved pairs over the whole head, or the
+//                      half-rotation inside every group of R values for rope_group); with no rotation
+//                      it is the output RMSNorm over head_v_dim (kata/layer.py:199-209, :539)
+//
+// All of them are HBM-bound passes.  Every thread moves 16-byte vectors (8 bf16/fp16 or 4 fp32
+// values), computes in fp32 and reads every input element once per pass: the convolution keeps a
+// sliding window of the last K inputs (and, backward, the last K gradients) in registers over a run
+// of kConvRun time steps, the row kernels reduce a row over the few lanes that hold it with shuffles.
+// Weight gradients are per-CTA partial sums reduced by a second kernel in a fixed order, so every
+// result is deterministic (no atomics).
+#include <algorithm>
+
+#include "attn_common.cuh"
+#include "host_util.h"
+
+namespace kata {
+namespace {
+
+template <typename T>
+struct VecN {
+  static constexpr int N = 16 / static_cast<int>(sizeof(T));
+};
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* p, float (&v)[VecN<T>::N]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < VecN<T>::N; ++i) v[i] = to_f32<T>(e[i]);
+}
+template <typename T>
+__device__ __forceinline__ void store_vec(T* p, const float (&v)[VecN<T>::N]) {
+  uint4 u;
+  T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < VecN<T>::N; ++i) e[i] = from_f32<T>(v[i]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ float sigmoidf_(float a) { return 1.f / (1.f + __expf(-a)); }
+
+// ------------------------------------------------------------------------------------------------
+// short convolution
+// ------------------------------------------------------------------------------------------------
+constexpr int kConvRun = 64;      // time steps per thread
+constexpr int kConvThreads = 128;  // channel vectors per CTA
+
+struct ConvParams {
+  const void* x;
+  const float* w;
+  const float* bias;
+  void* y;
+  const void* dy;
+  void* dx;
+  float* part;  // backward: (B * nrun, C, K + 1) partial sums of dw and dbias
+  int T, C;
+  long long ldx, ldy, lddx;
+  int act;
+  int nrun;
+};
+
+// grid (channel vectors / kConvThreads, runs of kConvRun steps, B)
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(ConvParams p) {
+  constexpr int V = VecN<T>::N;
+  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * V;
+  if (c0 >= p.C) return;
+  const int b = blockIdx.z, t0 = blockIdx.y * kConvRun;
+  const int t1 = min(t0 + kConvRun, p.T);
+  float wr[K][V], br[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) wr[i][j] = p.w[(c0 + j) * K + i];
+    br[j] = p.bias ? p.bias[c0 + j] : 0.f;
+  }
+  const T* xb = static_cast<const T*>(p.x) + static_cast<size_t>(b) * p.T * p.ldx + c0;
+  T* yb = static_cast<T*>(p.y) + static_cast<size_t>(b) * p.T * p.ldy + c0;
+  float win[K][V];  // win[i] = x[t - K + 1 + i]
+#pragma unroll
+  for (int i = 0; i < K - 1; ++i) {
+    const int t = t0 - (K - 1) + i;
+    if (t >= 0) load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[i]);
+    else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) win[i][j] = 0.f;
+    }
+  }
+  for (int t = t0; t < t1; ++t) {
+    load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[K - 1]);
+    float out[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      float a = br[j];
+#pragma unroll
+      for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
+      out[j] = p.act ? a * sigmoidf_(a) : a;
+    }
+    store_vec<T>(yb + static_cast<size_t>(t) * p.ldy, out);
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+      for (int j = 0; j < V; ++j) win[i][j] = win[i + 1][j];
+  }
+}
+
+// Backward: g = dy * act'(a) (a recomputed from x), dx[s] = sum_i w[i] g[s + K - 1 - i],
+// dw[c,i] = sum_t g[t] x[t - K + 1 + i], dbias[c] = sum_t g[t].  A thread walks its run plus K - 1
+// steps of look-ahead (the g values its last dx outputs need), keeping the last K x and g values.
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(ConvParams p) {
+  constexpr int V = VecN<T>::N;
+  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * V;
+  if (c0 >= p.C) return;
+  const int b = blockIdx.z, t0 = blockIdx.y * kConvRun;
+  const int t1 = min(t0 + kConvRun, p.T);
+  float wr[K][V], br[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) wr[i][j] = p.w[(c0 + j) * K + i];
+    br[j] = p.bias ? p.bias[c0 + j] : 0.f;
+  }
+  const T* xb = static_cast<const T*>(p.x) + static_cast<size_t>(b) * p.T * p.ldx + c0;
+  const T* dyb = static_cast<const T*>(p.dy) + static_cast<size_t>(b) * p.T * p.ldy + c0;
+  T* dxb = static_cast<T*>(p.dx) + static_cast<size_t>(b) * p.T * p.lddx + c0;
+  float win[K][V], gq[K][V], dwa[K][V], dba[V];
+#pragma unroll
+  for (int i = 0; i < K; ++i)
+#pragma unroll
+    for (int j = 0; j < V; ++j) gq[i][j] = dwa[i][j] = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) dba[j] = 0.f;
+#pragma unroll
+  for (int i = 0; i < K - 1; ++i) {
+    const int t = t0 - (K - 1) + i;
+    if (t >= 0) load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[i]);
+    else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) win[i][j] = 0.f;
+    }
+  }
+  const int tend = t1 + K - 1;  // exclusive
+  for (int t = t0; t < tend; ++t) {
+    if (t < p.T) {
+      load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[K - 1]);
+      float d[V];
+      load_vec<T>(dyb + static_cast<size_t>(t) * p.ldy, d);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        float g = d[j];
+        if (p.act) {
+          float a = br[j];
+#pragma unroll
+          for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
+          const float s = sigmoidf_(a);
+          g *= s * (1.f + a * (1.f - s));
+        }
+        gq[K - 1][j] = g;
+      }
+      if (t < t1) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+#pragma unroll
+          for (int i = 0; i < K; ++i) dwa[i][j] = fmaf(gq[K - 1][j], win[i][j], dwa[i][j]);
+          dba[j] += gq[K - 1][j];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) gq[K - 1][j] = 0.f;
+    }
+    const int s = t - (K - 1);  // gq[i] = g[s + i]
+    if (s >= t0) {
+      float out[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < K; ++i) acc = fmaf(wr[i][j], gq[K - 1 - i][j], acc);
+        out[j] = acc;
+      }
+      store_vec<T>(dxb + static_cast<size_t>(s) * p.lddx, out);
+    }
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        win[i][j] = win[i + 1][j];
+        gq[i][j] = gq[i + 1][j];
+      }
+  }
+  float* pr = p.part + (static_cast<size_t>(b) * p.nrun + blockIdx.y) * p.C * (K + 1);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) pr[(c0 + j) * (K + 1) + i] = dwa[i][j];
+    pr[(c0 + j) * (K + 1) + K] = dba[j];
+  }
+}
+
+// dw[c, i] / dbias[c] = sum over the nparts partials, in partial order.
+__global__ void conv_reduce_kernel(const float* part, int nparts, int C, int K, float* dw, float* dbias) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per = C * (K + 1);
+  if (idx >= per) return;
+  float s = 0.f;
+  for (int k = 0; k < nparts; ++k) s += part[static_cast<size_t>(k) * per + idx];
+  const int c = idx / (K + 1), i = idx % (K + 1);
+  if (i < K) dw[c * K + i] = s;
+  else if (dbias) dbias[c] = s;
+}
+
+// ------------------------------------------------------------------------------------------------
+// row normalisation + RoPE
+// ------------------------------------------------------------------------------------------------
+constexpr int kRowThreads = 256;
+constexpr int kRowGrid = 148 * 8;  // grid-stride; the weight-gradient partials are one per CTA
+
+struct RowParams {
+  const void* x;
+  const float* w;
+  const float* cos;
+  const float* sin;
+  void* y;
+  float* rstd;
+  const void* dy;
+  void* dx;
+  float* part;  // backward: (gridDim.x, N) partials of dw
+  long long rows;
+  int N, T, heads;
+  int norm, rope, R;
+  float eps;
+};
+
+// Rotation of the values this thread holds (elements e0 .. e0 + V - 1 of row `row`), by +theta
+// (forward) or -theta (backward, the transpose).  rope 1: pairs (2f, 2f + 1) over the row, angle
+// index f; rope 2: inside every group of R values, element r < R/2 pairs with r + R/2, angle index
+// r % (R/2); the partner lives in lane ^ (R/2/V) of the row's lanes (R/2 a multiple of V).
+template <int V>
+__device__ __forceinline__ void rotate(float (&v)[V], int e0, int t, const RowParams& p, bool inverse) {
+  const float sg = inverse ? -1.f : 1.f;
+  if (p.rope == 1) {
+#pragma unroll
+    for (int j = 0; j < V; j += 2) {
+      const int f = (e0 + j) >> 1;
+      const float c = p.cos[static_cast<size_t>(t) * (p.R / 2) + f], s = sg * p.sin[static_cast<size_t>(t) * (p.R / 2) + f];
+      const float a = v[j], b = v[j + 1];
+      v[j] = a * c - b * s;
+      v[j + 1] = a * s + b * c;
+    }
+  } else if (p.rope == 2) {
+    const int half = p.R / 2;
+    const int r0 = e0 % p.R;
+    const bool lo = r0 < half;
+    float o[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) o[j] = __shfl_xor_sync(0xffffffffu, v[j], half / V);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int f = (r0 + j) % half;
+      const float c = p.cos[static_cast<size_t>(t) * half + f], s = sg * p.sin[static_cast<size_t>(t) * half + f];
+      v[j] = lo ? v[j] * c - o[j] * s : v[j] * c + o[j] * s;
+    }
+  }
+}
+
+// Sum over the TPR lanes that hold one row (TPR a power of two, <= 32, lane groups aligned).
+template <int TPR>
+__device__ __forceinline__ float row_sum(float s) {
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+template <typename T, int TPR>
+__global__ void __launch_bounds__(kRowThreads) row_fwd_kernel(RowParams p) {
+  constexpr int V = VecN<T>::N;
+  constexpr int RPC = kRowThreads / TPR;  // rows per CTA per iteration
+  const int sub = threadIdx.x % TPR, e0 = sub * V;
+  for (long long row = static_cast<long long>(blockIdx.x) * RPC + threadIdx.x / TPR; row - threadIdx.x / TPR < p.rows;
+       row += static_cast<long long>(gridDim.x) * RPC) {
+    const bool live = row < p.rows;
+    float v[V];
+    if (live) load_vec<T>(static_cast<const T*>(p.x) + row * p.N + e0, v);
+    else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) v[j] = 0.f;
+    }
+    if (p.norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < V; ++j) ss = fmaf(v[j], v[j], ss);
+      ss = row_sum<TPR>(ss);
+      const float r = rsqrtf((p.norm == 2 ? ss / p.N : ss) + p.eps);
+#pragma unroll
+      for (int j = 0; j < V; ++j) v[j] *= (p.norm == 2 && p.w) ? r * p.w[e0 + j] : r;
+      if (live && p.rstd && sub == 0) p.rstd[row] = r;
+    }
+    if (p.rope) rotate<V>(v, e0, static_cast<int>((row / p.heads) % p.T), p, false);
+    if (live) store_vec<T>(static_cast<T*>(p.y) + row * p.N + e0, v);
+  }
+}
+
+// Backward: dy0 = R^T dy, then l2: dx = r (dy0 - xh sum(dy0 xh)); RMS: g = dy0 w,
+// dx = r (g - xh mean(g xh)), dw += dy0 xh; no norm: dx = dy0.  xh = x r with the saved r.
+template <typename T, int TPR>
+__global__ void __launch_bounds__(kRowThreads) row_bwd_kernel(RowParams p) {
+  constexpr int V = VecN<T>::N;
+  constexpr int RPC = kRowThreads / TPR;
+  const int sub = threadIdx.x % TPR, e0 = sub * V;
+  float dwa[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) dwa[j] = 0.f;
+  for (long long row = static_cast<long long>(blockIdx.x) * RPC + threadIdx.x / TPR; row - threadIdx.x / TPR < p.rows;
+       row += static_cast<long long>(gridDim.x) * RPC) {
+    const bool live = row < p.rows;
+    float g[V], x[V];
+    if (live) {
+      load_vec<T>(static_cast<const T*>(p.dy) + row * p.N + e0, g);
+      load_vec<T>(static_cast<const T*>(p.x) + row * p.N + e0, x);
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) g[j] = x[j] = 0.f;
+    }
+    if (p.rope) rotate<V>(g, e0, static_cast<int>((row / p.heads) % p.T), p, true);
+    if (p.norm) {
+      const float r = live ? p.rstd[row] : 0.f;
+      float gw[V], dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float xh = x[j] * r;
+        x[j] = xh;
+        gw[j] = (p.norm == 2 && p.w) ? g[j] * p.w[e0 + j] : g[j];
+        if (p.norm == 2 && p.w) dwa[j] = fmaf(g[j], xh, dwa[j]);
+        dot = fmaf(gw[j], xh, dot);
+      }
+      dot = row_sum<TPR>(dot);
+      if (p.norm == 2) dot /= p.N;
+#pragma unroll
+      for (int j = 0; j < V; ++j) g[j] = r * (gw[j] - x[j] * dot);
+    }
+    if (live) store_vec<T>(static_cast<T*>(p.dx) + row * p.N + e0, g);
+  }
+  if (p.part) {
+    // CTA partial of dw: lanes with the same `sub` hold the same columns; sum them in shared memory
+    __shared__ float red[kRowThreads][V + 1];
+#pragma unroll
+    for (int j = 0; j < V; ++j) red[threadIdx.x][j] = dwa[j];
+    __syncthreads();
+    if (threadIdx.x < TPR) {
+      float s[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) s[j] = 0.f;
+      for (int k = threadIdx.x; k < kRowThreads; k += TPR)
+#pragma unroll
+        for (int j = 0; j < V; ++j) s[j] += red[k][j];
+#pragma unroll
+      for (int j = 0; j < V; ++j) p.part[static_cast<size_t>(blockIdx.x) * p.N + e0 + j] = s[j];
+    }
+  }
+}
+
+__global__ void row_reduce_kernel(const float* part, int nparts, int N, float* dw) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  float s = 0.f;
+  for (int k = 0; k < nparts; ++k) s += part[static_cast<size_t>(k) * N + i];
+  dw[i] = s;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+size_t esize(int dtype) { return dtype == KATA_DTYPE_F32 ? 4 : 2; }
+
+int conv_check(const kata_conv_args* a, bool bwd) {
+  if (!a) return KATA_ERR_INVALID;
+  if (a->dtype != KATA_DTYPE_F32 && a->dtype != KATA_DTYPE_BF16 && a->dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (a->B < 0 || a->T < 0 || a->C < 1 || a->K < 1 || a->K > 4) return KATA_ERR_SHAPE;
+  const int V = static_cast<int>(16 / esize(a->dtype));
+  if (a->C % V || a->ldx < a->C || a->ldy < a->C || a->ldx % V || a->ldy % V) return KATA_ERR_SHAPE;
+  if (a->activation != 0 && a->activation != 1) return KATA_ERR_INVALID;
+  if (!a->x || !a->w) return KATA_ERR_INVALID;
+  if (!aligned16(a->x)) return KATA_ERR_ALIGN;
+  if (!bwd) {
+    if (!a->y) return KATA_ERR_INVALID;
+    if (!aligned16(a->y)) return KATA_ERR_ALIGN;
+  } else {
+    if (!a->dy || !a->dx || !a->dw) return KATA_ERR_INVALID;
+    if (a->lddx < a->C || a->lddx % V) return KATA_ERR_SHAPE;
+    if (!aligned16(a->dy) || !aligned16(a->dx)) return KATA_ERR_ALIGN;
+  }
+  return KATA_OK;
+}
+
+template <typename T>
+int conv_launch(const kata_conv_args* a, bool bwd, cudaStream_t st) {
+  constexpr int V = VecN<T>::N;
+  const int nrun = (a->T + kConvRun - 1) / kConvRun;
+  ConvParams p{a->x, a->w, a->bias, a->y, a->dy, a->dx, static_cast<float*>(a->workspace), a->T, a->C, a->ldx,
+               a->ldy, a->lddx, a->activation, nrun};
+  const dim3 grid((a->C / V + kConvThreads - 1) / kConvThreads, nrun, a->B);
+#define KATA_CONV_CASE(KK)                                                                    \
+  case KK:                                                                                    \
+    if (bwd) conv_bwd_kernel<T, KK><<<grid, kConvThreads, 0, st>>>(p);                        \
+    else conv_fwd_kernel<T, KK><<<grid, kConvThreads, 0, st>>>(p);                            \
+    break;
+  switch (a->K) {
+    KATA_CONV_CASE(1)
+    KATA_CONV_CASE(2)
+    KATA_CONV_CASE(3)
+    KATA_CONV_CASE(4)
+    default: return KATA_ERR_SHAPE;
+  }
+#undef KATA_CONV_CASE
+  if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  if (bwd) {
+    const int per = a->C * (a->K + 1);
+    conv_reduce_kernel<<<(per + 255) / 256, 256, 0, st>>>(p.part, a->B * nrun, a->C, a->K, a->dw, a->dbias);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
+  return KATA_OK;
+}
+
+int row_check(const kata_rownorm_args* a, bool bwd) {
+  if (!a) return KATA_ERR_INVALID;
+  if (a->dtype != KATA_DTYPE_F32 && a->dtype != KATA_DTYPE_BF16 && a->dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  const int V = static_cast<int>(16 / esize(a->dtype));
+  const int tpr = a->N / V;
+  if (a->rows < 0 || a->N < V || a->N % V || tpr > 32 || (tpr & (tpr - 1))) return KATA_ERR_SHAPE;
+  if (a->norm < 0 || a->norm > 2 || a->rope < 0 || a->rope > 2) return KATA_ERR_INVALID;
+  if (a->rope) {
+    if (!a->cos || !a->sin || a->T < 1 || a->heads < 1) return KATA_ERR_INVALID;
+    if (a->rope == 1 && a->R != a->N) return KATA_ERR_SHAPE;
+    if (a->rope == 2 && (a->R < 2 || a->N % a->R || (a->R / 2) % V)) return KATA_ERR_SHAPE;
+  }
+  if (a->norm && !a->rstd) return KATA_ERR_INVALID;
+  if (!a->x) return KATA_ERR_INVALID;
+  if (!aligned16(a->x)) return KATA_ERR_ALIGN;
+  if (!bwd) {
+    if (!a->y) return KATA_ERR_INVALID;
+    if (!aligned16(a->y)) return KATA_ERR_ALIGN;
+  } else {
+    if (!a->dy || !a->dx) return KATA_ERR_INVALID;
+    if (!aligned16(a->dy) || !aligned16(a->dx)) return KATA_ERR_ALIGN;
+    if (a->norm == 2 && a->w && !a->dw) return KATA_ERR_INVALID;
+  }
+  return KATA_OK;
+}
+
+template <typename T>
+int row_launch(const kata_rownorm_args* a, bool bwd, cudaStream_t st) {
+  constexpr int V = VecN<T>::N;
+  const int tpr = a->N / V;
+  const bool want_dw = bwd && a->norm == 2 && a->w;
+  RowParams p{a->x, a->w, a->cos, a->sin, a->y, a->rstd, a->dy, a->dx,
+              want_dw ? static_cast<float*>(a->workspace) : nullptr, a->rows, a->N, a->T, a->heads, a->norm,
+              a->rope, a->R, a->eps};
+  const long long rpc = kRowThreads / tpr;
+  const int grid = static_cast<int>(std::min<long long>(kRowGrid, (a->rows + rpc - 1) / rpc));
+  if (grid == 0) {
+    if (want_dw) return from_cuda(cudaMemsetAsync(a->dw, 0, sizeof(float) * a->N, st));
+    return KATA_OK;
+  }
+#define KATA_ROW_CASE(TP)                                                               \
+  case TP:                                                                              \
+    if (bwd) row_bwd_kernel<T, TP><<<grid, kRowThreads, 0, st>>>(p);                    \
+    else row_fwd_kernel<T, TP><<<grid, kRowThreads, 0, st>>>(p);                        \
+    break;
+  switch (tpr) {
+    KATA_ROW_CASE(1)
+    KATA_ROW_CASE(2)
+    KATA_ROW_CASE(4)
+    KATA_ROW_CASE(8)
+    KATA_ROW_CASE(16)
+    KATA_ROW_CASE(32)
+    default: return KATA_ERR_SHAPE;
+  }
+#undef KATA_ROW_CASE
+  if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  if (want_dw) {
+    row_reduce_kernel<<<(a->N + 255) / 256, 256, 0, st>>>(p.part, grid, a->N, a->dw);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
+  return KATA_OK;
+}
+
+int row_grid(const kata_rownorm_args* a) {
+  const int V = static_cast<int>(16 / esize(a->dtype));
+  const long long rpc = kRowThreads / (a->N / V);
+  return static_cast<int>(std::min<long long>(kRowGrid, (a->rows + rpc - 1) / rpc));
+}
+
+}  // namespace
+}  // namespace kata
+
+using namespace kata;
+
+extern "C" int kata_short_conv_fwd(const kata_conv_args* a, kata_stream_t stream) {
+  int e = conv_check(a, false);
+  if (e) return e;
+  if (a->B == 0 || a->T == 0) return KATA_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case KATA_DTYPE_BF16: return conv_launch<__nv_bfloat16>(a, false, st);
+    case KATA_DTYPE_F16: return conv_launch<__half>(a, false, st);
+    default: return conv_launch<float>(a, false, st);
+  }
+}
+
+extern "C" size_t kata_short_conv_bwd_workspace_bytes(const kata_conv_args* a) {
+  if (!a || a->B < 0 || a->T < 0 || a->C < 1 || a->K < 1) return 0;
+  const size_t nrun = (static_cast<size_t>(a->T) + kConvRun - 1) / kConvRun;
+  return sizeof(float) * static_cast<size_t>(a->B) * nrun * a->C * (a->K + 1);
+}
+
+extern "C" int kata_short_conv_bwd(const kata_conv_args* a, kata_stream_t stream) {
+  int e = conv_check(a, true);
+  if (e) return e;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (a->B == 0 || a->T == 0) {
+    if (cudaMemsetAsync(a->dw, 0, sizeof(float) * a->C * a->K, st) != cudaSuccess) return KATA_ERR_CUDA;
+    if (a->dbias && cudaMemsetAsync(a->dbias, 0, sizeof(float) * a->C, st) != cudaSuccess) return KATA_ERR_CUDA;
+    return KATA_OK;
+  }
+  if (!a->workspace || a->workspace_bytes < kata_short_conv_bwd_workspace_bytes(a)) return KATA_ERR_WORKSPACE;
+  switch (a->dtype) {
+    case KATA_DTYPE_BF16: return conv_launch<__nv_bfloat16>(a, true, st);
+    case KATA_DTYPE_F16: return conv_launch<__half>(a, true, st);
+    default: return conv_launch<float>(a, true, st);
+  }
+}
+
+extern "C" int kata_rownorm_fwd(const kata_rownorm_args* a, kata_stream_t stream) {
+  int e = row_check(a, false);
+  if (e) return e;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case KATA_DTYPE_BF16: return row_launch<__nv_bfloat16>(a, false, st);
+    case KATA_DTYPE_F16: return row_launch<__half>(a, false, st);
+    default: return row_launch<float>(a, false, st);
+  }
+}
+
+extern "C" size_t kata_rownorm_bwd_workspace_bytes(const kata_rownorm_args* a) {
+  if (!a || row_check(a, true) == KATA_ERR_SHAPE || a->N < 1) return 0;
+  if (!(a->norm == 2 && a->w)) return 0;
+  return sizeof(float) * static_cast<size_t>(row_grid(a)) * a->N;
+}
+
+extern "C" int kata_rownorm_bwd(const kata_rownorm_args* a, kata_stream_t stream) {
+  int e = row_check(a, true);
+  if (e) return e;
+  if (a->norm == 2 && a->w && a->rows > 0 &&
+      (!a->workspace || a->workspace_bytes < kata_rownorm_bwd_workspace_bytes(a)))
+    return KATA_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case KATA_DTYPE_BF16: return row_launch<__nv_bfloat16>(a, true, st);
+    case KATA_DTYPE_F16: return row_launch<__half>(a, true, st);
+    default: return row_launch<float>(a, true, st);
+  }
+}

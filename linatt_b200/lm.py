@@ -1,0 +1,142 @@
+"""A KATA causal language model whose token mixer is :class:`linatt_b200.mixer.FlashKataMixer`.
+
+Mirrors ``KataForCausalLM`` (kata/modeling.py:33-155) with fla's LinearAttention body: token
+embedding, ``num_hidden_layers`` blocks of [RMSNorm -> KATA mixer -> residual -> RMSNorm -> SwiGLU
+MLP -> residual], a final RMSNorm and an output head tied to the embedding; the loss is the mean
+next-token cross entropy (the last position of every row has no target), as fla's
+``LinearAttentionForCausalLM`` computes it.  Parameter names follow the reference
+(``model.layers.{i}.attn.*``, ``mlp.gate_proj`` / ``up_proj`` / ``down_proj``, ``attn_norm``,
+``mlp_norm``, ``model.norm``, ``lm_head``).  Everything outside the mixer is plain PyTorch
+(cuBLAS GEMMs and PyTorch's fused norm / loss kernels): the hot path of this library is the mixer.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .mixer import FlashKataMixer
+
+__all__ = ["KataLMConfig", "KataLM"]
+
+
+@dataclass
+class KataLMConfig:
+    """Defaults: ``configs/model/200m/kata_quadratic_200m.yaml`` of the reference (the 24-layer,
+    d_model 768, 12 x 64 heads, concat score M = 4, short convolution of width 4, vocab 32000 LM)."""
+
+    hidden_size: int = 768
+    num_hidden_layers: int = 24
+    num_heads: int = 12
+    num_kv_heads: int | None = None
+    expand_k: float = 1.0
+    expand_v: float = 1.0
+    feature_map: str = "kata_quadratic"
+    spd_num_groups: int = 4
+    use_short_conv: bool = True
+    conv_size: int = 4
+    qk_norm: bool = False
+    norm_q: str = "rmsnorm"
+    norm_k: str = "rmsnorm"
+    use_rope: bool = False
+    rope_group: bool = False
+    use_offset_gate: bool = False
+    use_decay: bool = False
+    hidden_ratio: int = 4
+    intermediate_size: int | None = None
+    max_position_embeddings: int = 2048
+    norm_eps: float = 1e-6
+    vocab_size: int = 32000
+    tie_word_embeddings: bool = True
+    initializer_range: float = 0.006
+    extra: dict = field(default_factory=dict)
+
+    def mixer_kwargs(self) -> dict:
+        return dict(hidden_size=self.hidden_size, expand_k=self.expand_k, expand_v=self.expand_v,
+                    num_heads=self.num_heads, num_kv_heads=self.num_kv_heads, feature_map=self.feature_map,
+                    spd_num_groups=self.spd_num_groups, use_short_conv=self.use_short_conv,
+                    conv_size=self.conv_size, qk_norm=self.qk_norm, norm_q=self.norm_q, norm_k=self.norm_k,
+                    use_rope=self.use_rope, rope_group=self.rope_group, use_offset_gate=self.use_offset_gate,
+                    use_decay=self.use_decay, norm_eps=self.norm_eps,
+                    max_position_embeddings=self.max_position_embeddings, **self.extra)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps)
+
+
+class GatedMLP(nn.Module):
+    """SwiGLU MLP (fla ``GatedMLP``): down(silu(gate(x)) * up(x)), intermediate size the multiple of
+    256 nearest above 2/3 * hidden_ratio * hidden_size."""
+
+    def __init__(self, hidden_size: int, hidden_ratio: int, intermediate_size: int | None):
+        super().__init__()
+        if intermediate_size is None:
+            intermediate_size = int(hidden_size * hidden_ratio * 2 / 3)
+            intermediate_size = 256 * ((intermediate_size + 255) // 256)
+        self.gate_proj = nn.Linear(hidden_size, intermediate_size, bias=False)
+        self.up_proj = nn.Linear(hidden_size, intermediate_size, bias=False)
+        self.down_proj = nn.Linear(intermediate_size, hidden_size, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        gu = F.linear(x, torch.cat([self.gate_proj.weight, self.up_proj.weight], dim=0))  # one GEMM
+        g, u = gu.chunk(2, dim=-1)
+        return self.down_proj(F.silu(g) * u)
+
+
+class KataBlock(nn.Module):
+    def __init__(self, cfg: KataLMConfig, layer_idx: int):
+        super().__init__()
+        self.attn_norm = RMSNorm(cfg.hidden_size, cfg.norm_eps)
+        self.attn = FlashKataMixer(layer_idx=layer_idx, **cfg.mixer_kwargs())
+        self.mlp_norm = RMSNorm(cfg.hidden_size, cfg.norm_eps)
+        self.mlp = GatedMLP(cfg.hidden_size, cfg.hidden_ratio, cfg.intermediate_size)
+
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        h = h + self.attn(self.attn_norm(h))[0]
+        return h + self.mlp(self.mlp_norm(h))
+
+
+class _Body(nn.Module):
+    def __init__(self, cfg: KataLMConfig):
+        super().__init__()
+        self.embeddings = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+        self.layers = nn.ModuleList(KataBlock(cfg, i) for i in range(cfg.num_hidden_layers))
+        self.norm = RMSNorm(cfg.hidden_size, cfg.norm_eps)
+
+
+class KataLM(nn.Module):
+    """``forward(input_ids, labels=None)`` returns the logits, or the loss when labels are given."""
+
+    def __init__(self, cfg: KataLMConfig):
+        super().__init__()
+        self.config = cfg
+        self.model = _Body(cfg)
+        self.lm_head = nn.Linear(cfg.hidden_size, cfg.vocab_size, bias=False)
+        self.apply(self._init)
+        if cfg.tie_word_embeddings:
+            self.lm_head.weight = self.model.embeddings.weight
+
+    def _init(self, m: nn.Module) -> None:
+        if isinstance(m, (nn.Linear, nn.Embedding)):
+            nn.init.normal_(m.weight, mean=0.0, std=self.config.initializer_range)
+
+    def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
+        h = self.model.embeddings(input_ids)
+        for blk in self.model.layers:
+            h = blk(h)
+        logits = self.lm_head(self.model.norm(h))
+        if labels is None:
+            return logits
+        # next-token targets; the last position of each row has none
+        tgt = torch.cat([labels[:, 1:], torch.full_like(labels[:, :1], -100)], dim=1)
+        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), tgt.reshape(-1), ignore_index=-100)
