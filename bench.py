@@ -26,6 +26,10 @@ Printed JSON line (rank 0):
             over the N GPUs (strong scaling, the one path with a collective: the prefix state is
             all-gathered over NCCL); its step time, tokens/s, the all-gather alone and the
             shard-local flash kernels alone (a few steps of its own after the headline timing)
+  lm        config 5 on the same ranks: one training step (fwd + bwd + clip + AdamW, bf16 autocast)
+            of the 24-layer KATA LM with the mixer on this library's kernels, micro-batch 32 x 2048
+            per GPU, DDP with NCCL gradient all-reduce (weak scaling); tokens/s, TFLOP/s against the
+            sustained bf16 peak, and an end-to-end leg that uploads every step's token ids
 
 L2: three rotating input sets of 537 MB each (bf16 q, k, v, dO of 134 MB apiece) are cycled, each
 larger than the 126 MB L2, so no step reads inputs left in L2 by the previous step.
@@ -422,6 +426,12 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
         del step
         torch.cuda.empty_cache()
         sp = sp_measure(torch, dist, world, rank, dev, max(3, min(K, args.sp_steps)), 3)
+    # config 5 (the KATA LM training step, DDP over the same ranks): every scaling run of this bench
+    # also records the end-to-end model step
+    lm = None
+    if not args.no_lm:
+        torch.cuda.empty_cache()
+        lm = lm_measure(torch, dist, world, rank, local, dev, max(3, args.lm_steps), 3, args.lm_batch)
 
     if world > 1:
         dist.barrier()
@@ -454,7 +464,7 @@ def run_gpu(args, rank: int, world: int, local: int) -> None:
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(world), "roofline": roofline, "cpu_baseline": cpu,
         "e2e": e2e, "clocks": clk.summary(), "gpu_launches": (4 if DECAY else 3) * K,  # decay: + c transpose
-        "sp": sp,
+        "sp": sp, "lm": lm,
     }
     print(json.dumps(line), flush=True)
 
@@ -667,6 +677,121 @@ def run_gdn(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def lm_step_flops(cfg, batch: int, T: int) -> float:
+    """Algorithmic FLOPs of one training step (fwd + bwd) of the KATA LM: 6 x parameters x tokens for
+    every GEMM weight (the tied head counted once, as the output GEMM), the attention at the survey's
+    3.5 x forward (forward P (2D + 2Dv) per (b, h), P = T (T + 1) / 2); norms, convolution and
+    elementwise work excluded."""
+    H, D = cfg.num_heads, cfg.hidden_size // cfg.num_heads
+    inter = 256 * ((int(cfg.hidden_size * cfg.hidden_ratio * 2 / 3) + 255) // 256)
+    per_layer = 4 * cfg.hidden_size * cfg.hidden_size + 3 * cfg.hidden_size * inter
+    gemm = 6.0 * (cfg.num_hidden_layers * per_layer + cfg.vocab_size * cfg.hidden_size) * batch * T
+    attn = cfg.num_hidden_layers * 3.5 * batch * H * pairs(T) * (2 * D + 2 * D)
+    return gemm + attn
+
+
+LM_METRIC = "KATA LM (24 x d768, FlashKata M=4) DDP training tokens/s at ctx 2048, micro-batch 32 per GPU (config 5)"
+
+
+def lm_measure(torch, dist, world: int, rank: int, local: int, dev, steps: int, warmup: int, batch: int) -> dict:
+    """Config 5 on the ranks of an initialised job: one DDP training step of the 24-layer KATA LM
+    (d_model 768, 12 x 64 heads, concat M = 4, short convolution, SwiGLU, tied embeddings, vocab
+    32000) at context 2048 and `batch` sequences per GPU: bf16 autocast over fp32 weights, AdamW,
+    gradient clipping, NCCL all-reduce of the gradients (DDP buckets overlapping the backward).
+    Token ids uniform in [0, 32000), seeded per rank.  Device-timed steps with the ids resident,
+    then end-to-end steps that upload their ids from pinned host memory and read the loss back."""
+    from linatt_b200.lm import KataLM, KataLMConfig
+
+    cfg = KataLMConfig()
+    Bl, Tl = batch, 2048
+    torch.manual_seed(1234)  # identical initial weights on every rank
+    model = KataLM(cfg).to(dev)
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    g = torch.Generator().manual_seed(7 + rank)
+    host = [torch.randint(0, cfg.vocab_size, (Bl, Tl), generator=g).pin_memory() for _ in range(3)]
+    dev_ids = [h.to(dev) for h in host]
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def train(ids):
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = net(ids, labels=ids)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return loss
+
+    ms, clk = _timed_steps(torch, dist, world, dev, lambda i: train(dev_ids[i % 3]), steps, warmup)
+    buf = torch.empty(Bl, Tl, dtype=torch.long, device=dev)
+
+    def step_e2e(i):
+        buf.copy_(host[i % 3], non_blocking=True)
+        loss = train(buf)
+        loss_host.copy_(loss.detach().float().reshape(1), non_blocking=True)
+
+    k_e2e = max(3, steps // 2)
+    ms_e2e, _ = _timed_steps(torch, dist, world, dev, step_e2e, k_e2e, 3)
+    last_loss = float(loss_host.item())
+    del net, model, opt, dev_ids, buf
+    torch.cuda.empty_cache()
+    peak, src = load_peaks()
+    sustained = peak
+    try:
+        sustained = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops_sustained", peak))
+    except Exception:  # noqa: BLE001
+        pass
+    step_ms = ms / steps
+    tok = world * Bl * Tl
+    fl = lm_step_flops(cfg, Bl, Tl)
+    ach = fl / (step_ms / 1e3) / 1e12
+    return {
+        "metric": LM_METRIC, "value": tok / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": step_ms, "scaling": "weak",
+        "config": {"workload": "KATA LM training step: fwd + bwd + clip + AdamW (config 5)",
+                   "model": "24 layers, d_model 768, 12 heads x 64, concat M=4, short conv 4, SwiGLU 2048, "
+                            "tied embeddings, vocab 32000",
+                   "micro_batch_per_gpu": Bl, "global_batch": world * Bl, "seq_len": Tl,
+                   "parallelism": f"dp{world} (DDP, NCCL all-reduce)" if world > 1 else "dp1",
+                   "l2": "every step streams ~50 GB of activations and 3.9 GB of weights / optimizer state, "
+                         "far above the 126 MB L2"},
+        "roofline": {"bound": "tensor", "achieved": ach, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": ach / sustained, "traffic": None, "peak_source": f"{src} (sustained bf16 GEMM)",
+                     "algorithmic_tflop_per_step": fl / 1e12},
+        "e2e": {"value": tok / (ms_e2e / k_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": Bl * Tl * 8,
+                "d2h_bytes_per_step": 4, "last_loss": last_loss},
+        "clocks": clk,
+        # per layer: 3 convolutions, attention forward, output norm, 2 hidden norms; backward: norms
+        # 2 x 2 + output norm 2, attention 2, convolutions 3 x 3 launches
+        "gpu_launches": steps * cfg.num_hidden_layers * 22,
+    }
+
+
+def run_lm(args, rank: int, world: int, local: int) -> None:
+    """Standalone line of config 5 (see lm_measure)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    r = lm_measure(torch, dist, world, rank, local, dev, args.steps, args.warmup, args.lm_batch)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = dict(r)
+    line.update({"higher_is_better": True, "vs_baseline": None, "dtype": "bf16",
+                 "data": "synthetic token ids uniform in [0, 32000), random-init weights"})
+    print(json.dumps(line), flush=True)
+
+
 def run_delta(args, rank: int, world: int, local: int) -> None:
     """SPD delta rule (flash_delta) fwd+bwd at the 200M-model mixer geometry: B=8, T=2048, H=12,
     D=Dv=64, M=4, scale 0.5, normalised, bf16 inputs, per GPU (weak scaling over B)."""
@@ -804,10 +929,14 @@ def main() -> None:
     ap.add_argument("--score", choices=["concat", "sum"], default="concat")
     ap.add_argument("--decay", action="store_true",
                     help="auxiliary line: the decayed form (device-timed only; no e2e / CPU legs)")
-    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode"], default="attn",
+    ap.add_argument("--no-lm", action="store_true", help="skip the config-5 LM training-step object of the line")
+    ap.add_argument("--lm-steps", type=int, default=5, help="timed steps of the config-5 object (>= 3)")
+    ap.add_argument("--lm-batch", type=int, default=32,
+                    help="micro-batch per GPU of --workload lm (config 5 is quoted at 32; smaller only for captures)")
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm"], default="attn",
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
                          "delta: the SPD delta rule at the mixer geometry; decode: one-token generation "
-                         "steps on the recurrent feature state")
+                         "steps on the recurrent feature state; lm: config 5, the KATA LM DDP training step")
     ap.add_argument("--gdn-batch", type=int, default=8,
                     help="B per GPU of --workload gdn (config 2 is quoted at 8; smaller only for profiler captures)")
     ap.add_argument("--batch", type=int, default=16,
@@ -818,7 +947,7 @@ def main() -> None:
     if DECAY:
         if SCORE != "concat":
             ap.error("--decay pairs with the concat score only (as in the reference)")
-        args.no_e2e = args.no_cpu_baseline = args.no_sp = True
+        args.no_e2e = args.no_cpu_baseline = args.no_sp = args.no_lm = True
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -835,6 +964,8 @@ def main() -> None:
         run_delta(args, rank, world, local)
     elif args.workload == "decode":
         run_decode(args, rank, world, local)
+    elif args.workload == "lm":
+        run_lm(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 

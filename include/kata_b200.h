@@ -447,7 +447,8 @@ KATA_API int kata_short_conv_bwd(const kata_conv_args* args, kata_stream_t strea
  *   rope 1  interleaved pairs (2f, 2f+1) over the whole row, R = N   (kata/layer.py:147-149)
  *   rope 2  inside every group of R values, value r < R/2 paired with r + R/2 (rope_group,
  *           kata/layer.py:139-141, :355-366); R/2 a multiple of 8 (16-bit) or 4 (fp32)
- * N/8 (16-bit) or N/4 (fp32) must be a power of two <= 32.  Forward stores rstd (the per-row
+ * N/8 (16-bit) or N/4 (fp32) must be a power of two <= 32, or (normalisation only, rope 0) 64, 96, 128
+ * or 192 (rows of up to 1536 16-bit values, e.g. a 768-wide hidden state).  Forward stores rstd (the per-row
  * 1/norm, fp32) when norm != 0; backward takes x, rstd, dy and writes dx, and dw (fp32, N) for RMS
  * with a weight, using kata_rownorm_bwd_workspace_bytes() of workspace.  No counterpart in the
  * reference as one operation: it fuses the separate fla kernels the layer calls.

@@ -43,13 +43,13 @@ __device__ __forceinline__ void store_vec(T* p, const float (&v)[VecN<T>::N]) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-__device__ __forceinline__ float sigmoidf_(float a) { return 1.f / (1.f + __expf(-a)); }
+__device__ __forceinline__ float sigmoidf_(float a) { return __fdividef(1.f, 1.f + __expf(-a)); }
 
 // ------------------------------------------------------------------------------------------------
 // short convolution
 // ------------------------------------------------------------------------------------------------
-constexpr int kConvRun = 64;      // time steps per thread
-constexpr int kConvThreads = 128;  // channel vectors per CTA
+constexpr int kConvRun = 32;  // time steps per thread (short runs: enough warps per SM to cover HBM latency)
+constexpr int kConvU = 8;      // time steps whose loads are issued together (memory-level parallelism)
 
 struct ConvParams {
   const void* x;
@@ -65,11 +65,13 @@ struct ConvParams {
   int nrun;
 };
 
-// grid (channel vectors / kConvThreads, runs of kConvRun steps, B)
+// grid (ceil(channel vectors / blockDim), runs of kConvRun steps, B); a thread owns one 16-byte
+// channel vector over one run.  Steps go in batches of kConvU: the batch's loads are issued before
+// any of them is used, so a thread keeps kConvU loads in flight instead of one.
 template <typename T, int K>
-__global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(ConvParams p) {
+__global__ void __launch_bounds__(128) conv_fwd_kernel(ConvParams p) {
   constexpr int V = VecN<T>::N;
-  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * V;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * V;
   if (c0 >= p.C) return;
   const int b = blockIdx.z, t0 = blockIdx.y * kConvRun;
   const int t1 = min(t0 + kConvRun, p.T);
@@ -92,31 +94,71 @@ __global__ void __launch_bounds__(kConvThreads) conv_fwd_kernel(ConvParams p) {
       for (int j = 0; j < V; ++j) win[i][j] = 0.f;
     }
   }
-  for (int t = t0; t < t1; ++t) {
-    load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[K - 1]);
-    float out[V];
+  for (int tb = t0; tb < t1; tb += kConvU) {
+    uint4 raw[kConvU];
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      float a = br[j];
+    for (int u = 0; u < kConvU; ++u)
+      if (tb + u < t1) raw[u] = *reinterpret_cast<const uint4*>(xb + static_cast<size_t>(tb + u) * p.ldx);
 #pragma unroll
-      for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
-      out[j] = p.act ? a * sigmoidf_(a) : a;
+    for (int u = 0; u < kConvU; ++u) {
+      if (tb + u < t1) {  // (a guard, not a break: the batch stays fully unrolled in registers)
+      const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+      for (int j = 0; j < V; ++j) win[K - 1][j] = to_f32<T>(e[j]);
+      float out[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        float a = br[j];
+#pragma unroll
+        for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
+        out[j] = p.act ? a * sigmoidf_(a) : a;
+      }
+      store_vec<T>(yb + static_cast<size_t>(tb + u) * p.ldy, out);
+#pragma unroll
+      for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+        for (int j = 0; j < V; ++j) win[i][j] = win[i + 1][j];
+      }
     }
-    store_vec<T>(yb + static_cast<size_t>(t) * p.ldy, out);
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i)
-#pragma unroll
-      for (int j = 0; j < V; ++j) win[i][j] = win[i + 1][j];
   }
+}
+
+// out[o] = sum over nparts rows of part (nparts x n, row-major) of column o, in row order
+// (deterministic).  Block: 32 columns x 8 row lanes; lane r sums rows r, r + 8, ...; the eight lane
+// sums are added in lane order.  Reads are 128-byte rows per warp.
+__global__ void __launch_bounds__(256) column_sum_kernel(const float* part, int nparts, int n, float* out) {
+  __shared__ float red[8][33];
+  const int col = blockIdx.x * 32 + (threadIdx.x & 31), r = threadIdx.x >> 5;
+  float s = 0.f;
+  if (col < n)
+    for (int k = r; k < nparts; k += 8) s += part[static_cast<size_t>(k) * n + col];
+  red[r][threadIdx.x & 31] = s;
+  __syncthreads();
+  if (r == 0 && col < n) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x & 31];
+    out[col] = t;
+  }
+}
+
+// (C, K + 1) sums -> dw (C, K) and dbias (C).
+__global__ void conv_split_kernel(const float* sums, int C, int K, float* dw, float* dbias) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= C * (K + 1)) return;
+  const int c = idx / (K + 1), i = idx % (K + 1);
+  if (i < K) dw[c * K + i] = sums[idx];
+  else if (dbias) dbias[c] = sums[idx];
 }
 
 // Backward: g = dy * act'(a) (a recomputed from x), dx[s] = sum_i w[i] g[s + K - 1 - i],
 // dw[c,i] = sum_t g[t] x[t - K + 1 + i], dbias[c] = sum_t g[t].  A thread walks its run plus K - 1
-// steps of look-ahead (the g values its last dx outputs need), keeping the last K x and g values.
+// steps of look-ahead (the g values its last dx outputs need), keeping the last K x and g values;
+// loads go in batches of kConvU steps as in the forward.
 template <typename T, int K>
-__global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(ConvParams p) {
+__global__ void __launch_bounds__(128) conv_bwd_kernel(ConvParams p) {
   constexpr int V = VecN<T>::N;
-  const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * V;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * V;
   if (c0 >= p.C) return;
   const int b = blockIdx.z, t0 = blockIdx.y * kConvRun;
   const int t1 = min(t0 + kConvRun, p.T);
@@ -147,54 +189,69 @@ __global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(ConvParams p) {
     }
   }
   const int tend = t1 + K - 1;  // exclusive
-  for (int t = t0; t < tend; ++t) {
-    if (t < p.T) {
-      load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[K - 1]);
-      float d[V];
-      load_vec<T>(dyb + static_cast<size_t>(t) * p.ldy, d);
+  const int tload = min(tend, p.T);
+  for (int tb = t0; tb < tend; tb += kConvU) {
+    uint4 rx[kConvU], rd[kConvU];
 #pragma unroll
-      for (int j = 0; j < V; ++j) {
-        float g = d[j];
-        if (p.act) {
-          float a = br[j];
-#pragma unroll
-          for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
-          const float s = sigmoidf_(a);
-          g *= s * (1.f + a * (1.f - s));
-        }
-        gq[K - 1][j] = g;
+    for (int u = 0; u < kConvU; ++u) {
+      if (tb + u < tload) {
+        rx[u] = *reinterpret_cast<const uint4*>(xb + static_cast<size_t>(tb + u) * p.ldx);
+        rd[u] = *reinterpret_cast<const uint4*>(dyb + static_cast<size_t>(tb + u) * p.ldy);
       }
-      if (t < t1) {
+    }
+#pragma unroll
+    for (int u = 0; u < kConvU; ++u) {
+      const int t = tb + u;
+      if (t < tend) {  // (a guard, not a break: the batch stays fully unrolled in registers)
+      if (t < p.T) {
+        const T* ex = reinterpret_cast<const T*>(&rx[u]);
+        const T* ed = reinterpret_cast<const T*>(&rd[u]);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
+          win[K - 1][j] = to_f32<T>(ex[j]);
+          float g = to_f32<T>(ed[j]);
+          if (p.act) {
+            float a = br[j];
 #pragma unroll
-          for (int i = 0; i < K; ++i) dwa[i][j] = fmaf(gq[K - 1][j], win[i][j], dwa[i][j]);
-          dba[j] += gq[K - 1][j];
+            for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
+            const float sg = sigmoidf_(a);
+            g *= sg * (1.f + a * (1.f - sg));
+          }
+          gq[K - 1][j] = g;
+        }
+        if (t < t1) {
+#pragma unroll
+          for (int j = 0; j < V; ++j) {
+#pragma unroll
+            for (int i = 0; i < K; ++i) dwa[i][j] = fmaf(gq[K - 1][j], win[i][j], dwa[i][j]);
+            dba[j] += gq[K - 1][j];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) gq[K - 1][j] = 0.f;
+      }
+      const int s0 = t - (K - 1);  // gq[i] = g[s0 + i]
+      if (s0 >= t0) {
+        float out[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < K; ++i) acc = fmaf(wr[i][j], gq[K - 1 - i][j], acc);
+          out[j] = acc;
+        }
+        store_vec<T>(dxb + static_cast<size_t>(s0) * p.lddx, out);
+      }
+#pragma unroll
+      for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          win[i][j] = win[i + 1][j];
+          gq[i][j] = gq[i + 1][j];
         }
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < V; ++j) gq[K - 1][j] = 0.f;
     }
-    const int s = t - (K - 1);  // gq[i] = g[s + i]
-    if (s >= t0) {
-      float out[V];
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        float acc = 0.f;
-#pragma unroll
-        for (int i = 0; i < K; ++i) acc = fmaf(wr[i][j], gq[K - 1 - i][j], acc);
-        out[j] = acc;
-      }
-      store_vec<T>(dxb + static_cast<size_t>(s) * p.lddx, out);
-    }
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i)
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        win[i][j] = win[i + 1][j];
-        gq[i][j] = gq[i + 1][j];
-      }
   }
   float* pr = p.part + (static_cast<size_t>(b) * p.nrun + blockIdx.y) * p.C * (K + 1);
 #pragma unroll
@@ -203,18 +260,6 @@ __global__ void __launch_bounds__(kConvThreads) conv_bwd_kernel(ConvParams p) {
     for (int i = 0; i < K; ++i) pr[(c0 + j) * (K + 1) + i] = dwa[i][j];
     pr[(c0 + j) * (K + 1) + K] = dba[j];
   }
-}
-
-// dw[c, i] / dbias[c] = sum over the nparts partials, in partial order.
-__global__ void conv_reduce_kernel(const float* part, int nparts, int C, int K, float* dw, float* dbias) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  const int per = C * (K + 1);
-  if (idx >= per) return;
-  float s = 0.f;
-  for (int k = 0; k < nparts; ++k) s += part[static_cast<size_t>(k) * per + idx];
-  const int c = idx / (K + 1), i = idx % (K + 1);
-  if (i < K) dw[c * K + i] = s;
-  else if (dbias) dbias[c] = s;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -367,12 +412,95 @@ __global__ void __launch_bounds__(kRowThreads) row_bwd_kernel(RowParams p) {
   }
 }
 
-__global__ void row_reduce_kernel(const float* part, int nparts, int N, float* dw) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= N) return;
-  float s = 0.f;
-  for (int k = 0; k < nparts; ++k) s += part[static_cast<size_t>(k) * N + i];
-  dw[i] = s;
+// Rows wider than 32 vectors (e.g. the model's 768-wide hidden RMSNorm): one warp per row, lane l
+// holding the NV vectors l, l + 32, ... (each warp load is 512 contiguous bytes).  Normalisation
+// only (no rotation).
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRowThreads) wide_row_fwd_kernel(RowParams p) {
+  constexpr int V = VecN<T>::N;
+  constexpr int RPC = kRowThreads / 32;
+  const int lane = threadIdx.x & 31;
+  for (long long row = static_cast<long long>(blockIdx.x) * RPC + threadIdx.x / 32; row - threadIdx.x / 32 < p.rows;
+       row += static_cast<long long>(gridDim.x) * RPC) {
+    if (row >= p.rows) continue;  // warp-uniform
+    const T* xr = static_cast<const T*>(p.x) + row * p.N;
+    float v[NV][V];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      load_vec<T>(xr + (lane + 32 * k) * V, v[k]);
+#pragma unroll
+      for (int j = 0; j < V; ++j) ss = fmaf(v[k][j], v[k][j], ss);
+    }
+    ss = row_sum<32>(ss);
+    const float r = rsqrtf((p.norm == 2 ? ss / p.N : ss) + p.eps);
+    if (p.rstd && lane == 0) p.rstd[row] = r;
+    T* yr = static_cast<T*>(p.y) + row * p.N;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lane + 32 * k) * V;
+#pragma unroll
+      for (int j = 0; j < V; ++j) v[k][j] *= (p.norm == 2 && p.w) ? r * p.w[e0 + j] : r;
+      store_vec<T>(yr + e0, v[k]);
+    }
+  }
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRowThreads) wide_row_bwd_kernel(RowParams p) {
+  constexpr int V = VecN<T>::N;
+  constexpr int RPC = kRowThreads / 32;
+  const int lane = threadIdx.x & 31;
+  float dwa[NV][V];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int j = 0; j < V; ++j) dwa[k][j] = 0.f;
+  const bool has_w = p.norm == 2 && p.w;
+  for (long long row = static_cast<long long>(blockIdx.x) * RPC + threadIdx.x / 32; row - threadIdx.x / 32 < p.rows;
+       row += static_cast<long long>(gridDim.x) * RPC) {
+    if (row >= p.rows) continue;  // warp-uniform
+    const float r = p.rstd[row];
+    float g[NV][V], x[NV][V];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lane + 32 * k) * V;
+      load_vec<T>(static_cast<const T*>(p.dy) + row * p.N + e0, g[k]);
+      load_vec<T>(static_cast<const T*>(p.x) + row * p.N + e0, x[k]);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        x[k][j] *= r;
+        if (has_w) {
+          dwa[k][j] = fmaf(g[k][j], x[k][j], dwa[k][j]);
+          g[k][j] *= p.w[e0 + j];
+        }
+        dot = fmaf(g[k][j], x[k][j], dot);
+      }
+    }
+    dot = row_sum<32>(dot);
+    if (p.norm == 2) dot /= p.N;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+#pragma unroll
+      for (int j = 0; j < V; ++j) g[k][j] = r * (g[k][j] - x[k][j] * dot);
+      store_vec<T>(static_cast<T*>(p.dx) + row * p.N + (lane + 32 * k) * V, g[k]);
+    }
+  }
+  if (p.part) {  // CTA partial of dw: the RPC warps' lanes hold the same columns; sum in lane order
+    __shared__ float red[RPC][32 * NV * V];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int j = 0; j < V; ++j) red[threadIdx.x / 32][(lane + 32 * k) * V + j] = dwa[k][j];
+    __syncthreads();
+    for (int e = threadIdx.x; e < p.N; e += kRowThreads) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < RPC; ++w) acc += red[w][e];
+      p.part[static_cast<size_t>(blockIdx.x) * p.N + e] = acc;
+    }
+  }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -404,11 +532,14 @@ int conv_launch(const kata_conv_args* a, bool bwd, cudaStream_t st) {
   const int nrun = (a->T + kConvRun - 1) / kConvRun;
   ConvParams p{a->x, a->w, a->bias, a->y, a->dy, a->dx, static_cast<float*>(a->workspace), a->T, a->C, a->ldx,
                a->ldy, a->lddx, a->activation, nrun};
-  const dim3 grid((a->C / V + kConvThreads - 1) / kConvThreads, nrun, a->B);
+  // as many threads as channel vectors (up to 128, whole warps): no idle lanes at C = 768
+  const int nvec = a->C / V;
+  const int threads = std::min(128, (nvec + 31) / 32 * 32);
+  const dim3 grid((nvec + threads - 1) / threads, nrun, a->B);
 #define KATA_CONV_CASE(KK)                                                                    \
   case KK:                                                                                    \
-    if (bwd) conv_bwd_kernel<T, KK><<<grid, kConvThreads, 0, st>>>(p);                        \
-    else conv_fwd_kernel<T, KK><<<grid, kConvThreads, 0, st>>>(p);                            \
+    if (bwd) conv_bwd_kernel<T, KK><<<grid, threads, 0, st>>>(p);                             \
+    else conv_fwd_kernel<T, KK><<<grid, threads, 0, st>>>(p);                                 \
     break;
   switch (a->K) {
     KATA_CONV_CASE(1)
@@ -421,7 +552,9 @@ int conv_launch(const kata_conv_args* a, bool bwd, cudaStream_t st) {
   if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   if (bwd) {
     const int per = a->C * (a->K + 1);
-    conv_reduce_kernel<<<(per + 255) / 256, 256, 0, st>>>(p.part, a->B * nrun, a->C, a->K, a->dw, a->dbias);
+    float* sums = p.part + static_cast<size_t>(a->B) * nrun * per;  // after the partials
+    column_sum_kernel<<<(per + 31) / 32, 256, 0, st>>>(p.part, a->B * nrun, per, sums);
+    conv_split_kernel<<<(per + 255) / 256, 256, 0, st>>>(sums, a->C, a->K, a->dw, a->dbias);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   return KATA_OK;
@@ -432,7 +565,12 @@ int row_check(const kata_rownorm_args* a, bool bwd) {
   if (a->dtype != KATA_DTYPE_F32 && a->dtype != KATA_DTYPE_BF16 && a->dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
   const int V = static_cast<int>(16 / esize(a->dtype));
   const int tpr = a->N / V;
-  if (a->rows < 0 || a->N < V || a->N % V || tpr > 32 || (tpr & (tpr - 1))) return KATA_ERR_SHAPE;
+  if (a->rows < 0 || a->N < V || a->N % V) return KATA_ERR_SHAPE;
+  if (tpr > 32) {  // wide rows: 2, 3, 4 or 6 vectors per lane of one warp, no rotation
+    if (tpr % 32 || tpr > 192 || tpr == 160 || a->rope) return KATA_ERR_SHAPE;
+  } else if (tpr & (tpr - 1)) {
+    return KATA_ERR_SHAPE;
+  }
   if (a->norm < 0 || a->norm > 2 || a->rope < 0 || a->rope > 2) return KATA_ERR_INVALID;
   if (a->rope) {
     if (!a->cos || !a->sin || a->T < 1 || a->heads < 1) return KATA_ERR_INVALID;
@@ -461,7 +599,7 @@ int row_launch(const kata_rownorm_args* a, bool bwd, cudaStream_t st) {
   RowParams p{a->x, a->w, a->cos, a->sin, a->y, a->rstd, a->dy, a->dx,
               want_dw ? static_cast<float*>(a->workspace) : nullptr, a->rows, a->N, a->T, a->heads, a->norm,
               a->rope, a->R, a->eps};
-  const long long rpc = kRowThreads / tpr;
+  const long long rpc = kRowThreads / std::min(tpr, 32);
   const int grid = static_cast<int>(std::min<long long>(kRowGrid, (a->rows + rpc - 1) / rpc));
   if (grid == 0) {
     if (want_dw) return from_cuda(cudaMemsetAsync(a->dw, 0, sizeof(float) * a->N, st));
@@ -472,7 +610,16 @@ int row_launch(const kata_rownorm_args* a, bool bwd, cudaStream_t st) {
     if (bwd) row_bwd_kernel<T, TP><<<grid, kRowThreads, 0, st>>>(p);                    \
     else row_fwd_kernel<T, TP><<<grid, kRowThreads, 0, st>>>(p);                        \
     break;
+#define KATA_WIDE_CASE(NVV)                                                             \
+  case 32 * NVV:                                                                        \
+    if (bwd) wide_row_bwd_kernel<T, NVV><<<grid, kRowThreads, 0, st>>>(p);              \
+    else wide_row_fwd_kernel<T, NVV><<<grid, kRowThreads, 0, st>>>(p);                  \
+    break;
   switch (tpr) {
+    KATA_WIDE_CASE(2)
+    KATA_WIDE_CASE(3)
+    KATA_WIDE_CASE(4)
+    KATA_WIDE_CASE(6)
     KATA_ROW_CASE(1)
     KATA_ROW_CASE(2)
     KATA_ROW_CASE(4)
@@ -482,9 +629,10 @@ int row_launch(const kata_rownorm_args* a, bool bwd, cudaStream_t st) {
     default: return KATA_ERR_SHAPE;
   }
 #undef KATA_ROW_CASE
+#undef KATA_WIDE_CASE
   if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   if (want_dw) {
-    row_reduce_kernel<<<(a->N + 255) / 256, 256, 0, st>>>(p.part, grid, a->N, a->dw);
+    column_sum_kernel<<<(a->N + 31) / 32, 256, 0, st>>>(p.part, grid, a->N, a->dw);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   return KATA_OK;
@@ -492,7 +640,7 @@ int row_launch(const kata_rownorm_args* a, bool bwd, cudaStream_t st) {
 
 int row_grid(const kata_rownorm_args* a) {
   const int V = static_cast<int>(16 / esize(a->dtype));
-  const long long rpc = kRowThreads / (a->N / V);
+  const long long rpc = kRowThreads / std::min(a->N / V, 32);
   return static_cast<int>(std::min<long long>(kRowGrid, (a->rows + rpc - 1) / rpc));
 }
 
@@ -516,7 +664,7 @@ extern "C" int kata_short_conv_fwd(const kata_conv_args* a, kata_stream_t stream
 extern "C" size_t kata_short_conv_bwd_workspace_bytes(const kata_conv_args* a) {
   if (!a || a->B < 0 || a->T < 0 || a->C < 1 || a->K < 1) return 0;
   const size_t nrun = (static_cast<size_t>(a->T) + kConvRun - 1) / kConvRun;
-  return sizeof(float) * static_cast<size_t>(a->B) * nrun * a->C * (a->K + 1);
+  return sizeof(float) * (static_cast<size_t>(a->B) * nrun + 1) * a->C * (a->K + 1);  // partials + sums
 }
 
 extern "C" int kata_short_conv_bwd(const kata_conv_args* a, kata_stream_t stream) {

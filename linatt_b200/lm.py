@@ -7,7 +7,8 @@ next-token cross entropy (the last position of every row has no target), as fla'
 ``LinearAttentionForCausalLM`` computes it.  Parameter names follow the reference
 (``model.layers.{i}.attn.*``, ``mlp.gate_proj`` / ``up_proj`` / ``down_proj``, ``attn_norm``,
 ``mlp_norm``, ``model.norm``, ``lm_head``).  Everything outside the mixer is plain PyTorch
-(cuBLAS GEMMs and PyTorch's fused norm / loss kernels): the hot path of this library is the mixer.
+(cuBLAS GEMMs, PyTorch's loss and elementwise kernels) except the RMSNorms, which use the mixer's row
+kernel: the hot path of this library is the mixer.
 """
 
 from __future__ import annotations
@@ -18,7 +19,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .mixer import FlashKataMixer
+from .mixer import FlashKataMixer, RowNormFunction
 
 __all__ = ["KataLMConfig", "KataLM"]
 
@@ -65,13 +66,17 @@ class KataLMConfig:
 
 
 class RMSNorm(nn.Module):
+    """Hidden-state RMSNorm (fla ``RMSNorm``) on ``kata_rownorm_*``: one pass forward, one backward
+    pass plus a fixed-order reduction of the fp32 weight gradient."""
+
     def __init__(self, dim: int, eps: float):
         super().__init__()
         self.eps = eps
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps)
+        N = x.shape[-1]
+        return RowNormFunction.apply(x.reshape(-1, N), self.weight, None, None, 2, 0, N, self.eps, 1, 1).view(x.shape)
 
 
 class GatedMLP(nn.Module):

@@ -211,3 +211,37 @@ def test_lm_step():
         losses.append(loss.item())
     assert all(np.isfinite(losses))
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("N", [256, 512, 768, 1024])
+@pytest.mark.parametrize("norm", ["l2", "rms"])
+def test_row_norm_wide(dtype, N, norm):
+    """Rows wider than 32 vectors (the LM's 768-wide hidden RMSNorm): one warp per row, at most six
+    16-byte vectors per lane (fp32 rows up to 768 values, 16-bit rows up to 1536)."""
+    from linatt_b200.mixer import RowNormFunction
+
+    if N // (16 // torch.tensor([], dtype=dtype).element_size()) > 192:
+        pytest.skip("wider than the kernel's 6 x 32 vectors")
+
+    g = torch.Generator(device="cuda").manual_seed(N)
+    rows = 1000
+    x = (3 * torch.randn(rows, N, device="cuda", generator=g)).to(dtype).requires_grad_(True)
+    w = (1 + 0.3 * torch.randn(N, device="cuda", generator=g)).requires_grad_(True)
+    code, eps = (1, 1e-6) if norm == "l2" else (2, 1e-6)
+    wt = w if norm == "rms" else None
+    y = RowNormFunction.apply(x, wt, None, None, code, 0, N, eps, 1, 1)
+    dy = torch.randn(rows, N, device="cuda", generator=g).to(dtype)
+    y.backward(dy)
+    xd = x.detach().double().requires_grad_(True)
+    wd = w.detach().double().requires_grad_(True)
+    if code == 1:
+        r = xd * torch.rsqrt(xd.pow(2).sum(-1, keepdim=True) + eps)
+    else:
+        r = xd * torch.rsqrt(xd.pow(2).mean(-1, keepdim=True) + eps) * wd
+    r.backward(dy.double())
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel(y, r) < tol
+    assert rel(x.grad, xd.grad) < tol
+    if norm == "rms":
+        assert rel(w.grad, wd.grad) < tol
