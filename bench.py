@@ -693,7 +693,8 @@ def lm_step_flops(cfg, batch: int, T: int) -> float:
 LM_METRIC = "KATA LM (24 x d768, FlashKata M=4) DDP training tokens/s at ctx 2048, micro-batch 32 per GPU (config 5)"
 
 
-def lm_measure(torch, dist, world: int, rank: int, local: int, dev, steps: int, warmup: int, batch: int) -> dict:
+def lm_measure(torch, dist, world: int, rank: int, local: int, dev, steps: int, warmup: int, batch: int,
+               profile: bool = False) -> dict:
     """Config 5 on the ranks of an initialised job: one DDP training step of the 24-layer KATA LM
     (d_model 768, 12 x 64 heads, concat M = 4, short convolution, SwiGLU, tied embeddings, vocab
     32000) at context 2048 and `batch` sequences per GPU: bf16 autocast over fp32 weights, AdamW,
@@ -735,6 +736,19 @@ def lm_measure(torch, dist, world: int, rank: int, local: int, dev, steps: int, 
     k_e2e = max(3, steps // 2)
     ms_e2e, _ = _timed_steps(torch, dist, world, dev, step_e2e, k_e2e, 3)
     last_loss = float(loss_host.item())
+    if profile and rank == 0:  # device time per kernel of one more step (CUPTI), to stderr
+        from torch.profiler import ProfilerActivity
+        from torch.profiler import profile as tprof
+
+        with tprof(activities=[ProfilerActivity.CUDA]) as prof:
+            train(dev_ids[0])
+            torch.cuda.synchronize()
+        ev = sorted(prof.key_averages(), key=lambda e: -e.device_time_total)
+        tot = sum(e.device_time_total for e in ev)
+        print(f"# one config-5 step: {tot / 1e3:.2f} ms of kernel time", file=sys.stderr)
+        for e in ev[:30]:
+            print(f"# {e.device_time_total / 1e3:9.3f} ms {100 * e.device_time_total / tot:5.1f} % "
+                  f"x{e.count:5d}  {e.key[:110]}", file=sys.stderr)
     del net, model, opt, dev_ids, buf
     torch.cuda.empty_cache()
     peak, src = load_peaks()
@@ -780,7 +794,7 @@ def run_lm(args, rank: int, world: int, local: int) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-    r = lm_measure(torch, dist, world, rank, local, dev, args.steps, args.warmup, args.lm_batch)
+    r = lm_measure(torch, dist, world, rank, local, dev, args.steps, args.warmup, args.lm_batch, args.lm_profile)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -931,6 +945,8 @@ def main() -> None:
                     help="auxiliary line: the decayed form (device-timed only; no e2e / CPU legs)")
     ap.add_argument("--no-lm", action="store_true", help="skip the config-5 LM training-step object of the line")
     ap.add_argument("--lm-steps", type=int, default=5, help="timed steps of the config-5 object (>= 3)")
+    ap.add_argument("--lm-profile", action="store_true",
+                    help="--workload lm: print the kernel-time breakdown of one extra step (torch.profiler) to stderr")
     ap.add_argument("--lm-batch", type=int, default=32,
                     help="micro-batch per GPU of --workload lm (config 5 is quoted at 32; smaller only for captures)")
     ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm"], default="attn",
