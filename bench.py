@@ -806,6 +806,78 @@ def run_lm(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_mixer(args, rank: int, world: int, local: int) -> None:
+    """The mixer's prologue / epilogue kernels alone at the config-5 layer geometry (B = 32 per GPU,
+    T = 2048, d_model 768, 12 x 64 heads, short convolution of width 4): one step = the short
+    convolution of q, k, v forward and backward (read as column ranges of the fused projection
+    output), the per-head output RMSNorm forward and backward, and the 768-wide hidden RMSNorm
+    forward and backward.  HBM-bound; roofline against the measured copy bandwidth."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from linatt_b200.mixer import RowNormFunction, ShortConvQKVFunction
+
+    Bm, Tm, C, Hh, Dh = args.mixer_batch, 2048, 768, 12, 64
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    sets = []
+    for _ in range(2):  # two rotating sets, each above the 126 MB L2 at B = 32
+        qkv = torch.randn(Bm, Tm, 3 * C, device=dev, generator=g).bfloat16().requires_grad_(True)
+        o = torch.randn(Bm * Tm * Hh, Dh, device=dev, generator=g).bfloat16().requires_grad_(True)
+        h = torch.randn(Bm * Tm, C, device=dev, generator=g).requires_grad_(True)
+        gq = torch.randn(Bm, Tm, C, device=dev, generator=g).bfloat16()
+        sets.append((qkv, o, h, gq))
+    wc = [torch.randn(C, 1, 4, device=dev, generator=g).mul_(0.5).requires_grad_(True) for _ in range(3)]
+    wo = torch.ones(Dh, device=dev, requires_grad=True)
+    wh = torch.ones(C, device=dev, requires_grad=True)
+
+    def step(i):
+        qkv, o, h, gq = sets[i % 2]
+        ys = ShortConvQKVFunction.apply(qkv, True, *wc)
+        torch.autograd.backward(ys, [gq, gq, gq])
+        yo = RowNormFunction.apply(o, wo, None, None, 2, 0, Dh, 1e-6, Hh, Tm)
+        yo.backward(yo)
+        yh = RowNormFunction.apply(h, wh, None, None, 2, 0, C, 1e-6, 1, 1)
+        yh.backward(yh)
+        for t in (qkv, o, h, *wc, wo, wh):
+            t.grad = None
+
+    ms, clk = _timed_steps(torch, dist, world, dev, step, args.steps, args.warmup)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak_hbm, src = load_hbm_peak()
+    step_ms = ms / args.steps
+    n = Bm * Tm
+    # algorithmic bytes: conv fwd reads x, writes y; bwd reads x, dy, writes dx (bf16, 3C channels);
+    # output norm fwd reads o, writes y; bwd reads o, dy, writes dx (bf16, H*Dh); hidden norm the same
+    # in fp32 over C; plus one fp32 rstd per row written and read
+    alg = (n * 3 * C * 2 * (2 + 3) + n * Hh * Dh * 2 * (2 + 3) + n * C * 4 * (2 + 3)
+           + 2 * 4 * (n * Hh + n))
+    ach = alg / (step_ms / 1e3) / 1e9
+    line = {
+        "metric": "KATA mixer prologue/epilogue kernels (short conv + output and hidden RMSNorm, fwd+bwd) "
+                  "tokens/s/GPU at the config-5 layer geometry",
+        "value": world * n / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "mixer prologue / epilogue kernels (config-5 layer)", "batch_per_gpu": Bm,
+                   "seq_len": Tm, "hidden": C, "heads": Hh, "head_dim": Dh, "conv_size": 4,
+                   "l2": "2 rotating input sets, each above the 126 MB L2 at B = 32"},
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": peak_hbm, "unit": "GB/s", "frac": ach / peak_hbm,
+                     "traffic": None, "peak_source": src, "algorithmic_bytes_per_step": alg},
+        "clocks": clk, "gpu_launches": 14 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_delta(args, rank: int, world: int, local: int) -> None:
     """SPD delta rule (flash_delta) fwd+bwd at the 200M-model mixer geometry: B=8, T=2048, H=12,
     D=Dv=64, M=4, scale 0.5, normalised, bf16 inputs, per GPU (weak scaling over B)."""
@@ -949,10 +1021,13 @@ def main() -> None:
                     help="--workload lm: print the kernel-time breakdown of one extra step (torch.profiler) to stderr")
     ap.add_argument("--lm-batch", type=int, default=32,
                     help="micro-batch per GPU of --workload lm (config 5 is quoted at 32; smaller only for captures)")
-    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm"], default="attn",
+    ap.add_argument("--mixer-batch", type=int, default=32,
+                    help="B per GPU of --workload mixer (the config-5 layer is 32; smaller only for captures)")
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm", "mixer"], default="attn",
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
                          "delta: the SPD delta rule at the mixer geometry; decode: one-token generation "
-                         "steps on the recurrent feature state; lm: config 5, the KATA LM DDP training step")
+                         "steps on the recurrent feature state; lm: config 5, the KATA LM DDP training step; "
+                         "mixer: the mixer's prologue / epilogue kernels at the config-5 layer geometry")
     ap.add_argument("--gdn-batch", type=int, default=8,
                     help="B per GPU of --workload gdn (config 2 is quoted at 8; smaller only for profiler captures)")
     ap.add_argument("--batch", type=int, default=16,
@@ -982,6 +1057,8 @@ def main() -> None:
         run_decode(args, rank, world, local)
     elif args.workload == "lm":
         run_lm(args, rank, world, local)
+    elif args.workload == "mixer":
+        run_mixer(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 
