@@ -20,12 +20,14 @@
 // The reference computes the same quantities with Triton K14-K21 (kata/spd/flash_delta.py:27-1116);
 // its O(T^2) chunk loops become the O(T) state scans here.
 #include <cuda_bf16.h>
+#include <type_traits>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "attn_common.cuh"
 #include "attn_internal.h"
 #include "host_util.h"
+#include "tc64.cuh"
 
 namespace kata {
 namespace {
@@ -448,6 +450,319 @@ __global__ void __launch_bounds__(NT) delta_y_scan_kernel(DP p, int F) {
   }
 }
 
+// ================================================================================================
+// Tensor-core scans (16-bit inputs, F <= 192 features, D <= 64, Dv = 64).  One CTA of 128 threads
+// per (b, h) runs every chunk in order (REV: the y-scan, in reverse).  The F x 64 fp32 state lives
+// in registers: thread (warp w, lane l) owns feature row 64 fb + 16 w + (l & 15) of every feature
+// block fb and value columns [32 (l >> 4), +32).  Per chunk:
+//   psi(K) as NFB 64 x 64 16-bit tiles (rows tokens, columns features) and the state as NFB tiles
+//   (rows features, columns values); one M = 64 tcgen05 chain gives P = psi(K) . state in TMEM;
+//   u-scan: rhs = beta (V - P), U = Tm rhs (fp32 on the CUDA cores), E = P + L U;
+//   y-scan: X = dU - P, Y = Tm^T X, W = beta Y;
+//   then the chains psi_fb^T . U (or W) (rows features) update the state, added in fp32.
+// The products take 16-bit operands (psi, the state, U / beta Y rounded to the input type, as the
+// reference's Triton kernels round their inter-chunk operands to bf16) with fp32 accumulation.
+// ================================================================================================
+template <int NFB>
+struct TcScanSmem {
+  uint8_t psi[NFB][tc64::TB];
+  uint8_t st[NFB][tc64::TB];
+  uint8_t w[tc64::TB];  // U (u-scan) or beta Y (y-scan): rows tokens, columns values, 16-bit
+  // chunk inputs, double-buffered (the next chunk's copies land while this one computes)
+  float Tm[2][C][68];
+  float L[2][C][68];      // u-scan only: kappa(k_i, k_j), j < i
+  uint16_t K[2][C * 64];  // chunk keys as loaded (16-bit), row r at r * 64
+  float Kf[C][65];        // the chunk's keys in fp32, rows padded to 65 words: psi reads one column
+                          // of 32 rows at a time, conflict-free (with the 128-byte rows of K it was
+                          // a 32-way bank conflict on every load)
+  float beta[2][C];
+  float R[C][68];         // rhs, then U (u-scan) / X (y-scan): fp32, 16-byte aligned rows
+  unsigned short tab[NFB * 64];
+  uint64_t bar;
+  uint32_t tmem;
+  int abort;
+};
+
+// psi of token row pr, features [ph F / 2, (ph + 1) F / 2) (F = 64 NFB), into the 16-bit psi tiles,
+// eight features per 16-byte store.  E and M are compile-time: the row sits in registers and every
+// feature's (a, b) pair, weight and tile position are constants of the unrolled loops (a table
+// lookup and two shared-memory loads per product otherwise).
+template <typename T, int E, int M, int NFB>
+__device__ __forceinline__ void build_psi_row(const float* krow, int pr, int ph, float scale,
+                                              uint8_t (*psi)[tc64::TB]) {
+  constexpr int F = 64 * NFB, FH = F / 2, FSYM = E * (E + 1) / 2;
+  float k[M * E];
+#pragma unroll
+  for (int i = 0; i < M * E; ++i) k[i] = krow[i];
+  const float w1 = scale, w2 = scale * 1.41421356237309515f;
+  float buf[8];
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    // (a, b) of feature f: row a of the upper triangle starts at a E - a (a - 1) / 2
+    int a = 0;
+#pragma unroll
+    for (int aa = 1; aa < E; ++aa)
+      if (f >= aa * E - (aa * (aa - 1)) / 2) a = aa;
+    const int bc = a + f - (a * E - (a * (a - 1)) / 2);
+    float v = 0.f;
+    if (f < FSYM && f / FH == ph) {
+#pragma unroll
+      for (int g = 0; g < M; ++g) v = fmaf(k[g * E + a], k[g * E + bc], v);
+      v *= a == bc ? w1 : w2;
+    }
+    buf[f & 7] = v;
+    if ((f & 7) == 7 && f / FH == ph) {
+      const int fl = f - 7;
+      tc64::st_shared_v4_at(psi[fl / 64], pr, fl % 64, pack2<T>(buf[0], buf[1]), pack2<T>(buf[2], buf[3]),
+                            pack2<T>(buf[4], buf[5]), pack2<T>(buf[6], buf[7]));
+    }
+  }
+}
+
+// 64 TMEM columns of this warp's lanes; lane half hh keeps columns [32 hh, 32 hh + 32).
+__device__ __forceinline__ void ld_half32(uint32_t taddr, int hh, float (&x)[32]) {
+  uint32_t a[32], b[32];
+  tmem_ld32(taddr, a);
+  tmem_ld32(taddr + 32, b);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(hh ? b[j] : a[j]);
+}
+
+template <typename T, int E, int M, bool REV>
+__global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
+  using namespace tc64;
+  constexpr int NFB = (E * (E + 1) / 2 + 63) / 64;
+  using Sm = TcScanSmem<NFB>;
+  extern __shared__ uint8_t smraw[];
+  Sm& sm = *reinterpret_cast<Sm*>(align1k(smraw));
+  constexpr bool BF = is_bf16<T>();
+  constexpr int F = NFB * 64;
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  constexpr int D = E * M;
+  const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;
+  const T* kp = static_cast<const T*>(p.k) + rowbase * D;
+  if (tid == 0) {
+    sm.abort = 0;
+    mbar_init(&sm.bar, 1);
+    fence_mbar_init();
+  }
+  if (tid < 32) {
+    tmem_alloc(&sm.tmem, 256);
+    tmem_relinquish();
+  }
+  build_feature_table(sm.tab, E, F);
+  const RowMap rm = rowmap();
+  const int m = rm.row, hh = rm.slot;
+  float S[NFB][2][16];
+#pragma unroll
+  for (int fb = 0; fb < NFB; ++fb)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) S[fb][0][j] = S[fb][1][j] = 0.f;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem;
+  uint32_t phase = 0;
+  bool ok = true;
+  const int nch = (p.T + C - 1) / C;
+  const int pr = tid & 63, ph = tid >> 6;  // psi building: token row, feature half of every block
+  // chunk `chn`'s Tm (and L), keys and beta into buffer bf by cp.async (rows past T zero-filled)
+  auto issue = [&](int chn, int bf) {
+    const int cc0 = chn * C, kv = D / 8;
+    for (int idx = tid; idx < C * 16; idx += 128) {
+      const int r = idx >> 4, c = idx & 15, t = cc0 + r;
+      const bool in = t < p.T;
+      const size_t o = (rowbase + static_cast<size_t>(in ? t : 0) * p.H) * C + 4 * c;
+      cp_async16(smem_u32(&sm.Tm[bf][r][4 * c]), p.Tm + o, in);
+      if (!REV) cp_async16(smem_u32(&sm.L[bf][r][4 * c]), p.Lm + o, in);
+    }
+    for (int idx = tid; idx < C * kv; idx += 128) {
+      const int r = idx / kv, c = idx - r * kv, t = cc0 + r;
+      const bool in = t < p.T;
+      cp_async16(smem_u32(&sm.K[bf][r * 64 + 8 * c]), kp + static_cast<size_t>(in ? t : 0) * p.H * D + 8 * c, in);
+    }
+    if (tid < C) {
+      const int t = cc0 + tid;
+      const bool in = t < p.T;
+      cp_async4(smem_u32(&sm.beta[bf][tid]), p.beta + rowbase + static_cast<size_t>(in ? t : 0) * p.H, in);
+    }
+    cp_async_commit();
+  };
+  if (nch > 0) issue(REV ? nch - 1 : 0, 0);
+  for (int it = 0; it < nch && ok; ++it) {
+    const int ch = REV ? nch - 1 - it : it, c0 = ch * C, bf = it & 1;
+    if (it + 1 < nch) {
+      issue(REV ? ch - 1 : ch + 1, bf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    const float(*Tm)[68] = sm.Tm[bf];
+    const float(*Lm)[68] = sm.L[bf];
+    const float* beta = sm.beta[bf];
+    {  // keys to fp32 (this thread's own copies have landed; the barrier below publishes them all)
+      const T* kr = reinterpret_cast<const T*>(sm.K[bf]);
+      __syncthreads();
+      for (int i = tid; i < C * D; i += 128) {
+        const int r = i / D, c = i - r * D;
+        sm.Kf[r][c] = to_f32<T>(kr[r * 64 + c]);
+      }
+    }
+    // the state as 16-bit tiles (rows features), the B operand of P = psi(K) state
+#pragma unroll
+    for (int fb = 0; fb < NFB; ++fb) {
+      st_row16<T>(sm.st[fb], m, 32 * hh, S[fb][0]);
+      st_row16<T>(sm.st[fb], m, 32 * hh + 16, S[fb][1]);
+    }
+    __syncthreads();
+    // psi(K): thread (token pr, half ph) forms features [ph F / 2, (ph + 1) F / 2)
+    build_psi_row<T, E, M, NFB>(sm.Kf[pr], pr, ph, p.scale, sm.psi);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // P = psi(K) . state   (rows tokens)
+      tc_fence_after();
+#pragma unroll
+      for (int fb = 0; fb < NFB; ++fb) mma64x2<BF, false, true>(tbase, sm.psi[fb], sm.st[fb], fb > 0);
+      umma_commit(&sm.bar);
+    }
+    if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
+    float x[32];
+    ld_half32(tbase + rm.lane, hh, x);
+    const int t = c0 + m;
+    const bool in = t < p.T;
+    const size_t vrow = (rowbase + static_cast<size_t>(in ? t : 0) * p.H) * 64 + 32 * hh;
+    {
+      const T* src = static_cast<const T*>(REV ? p.dU : p.v) + vrow;
+      float in32[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u4 = in ? reinterpret_cast<const uint4*>(src)[q] : make_uint4(0u, 0u, 0u, 0u);
+        const T* e = reinterpret_cast<const T*>(&u4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) in32[8 * q + j] = to_f32<T>(e[j]);
+      }
+      const float bm = beta[m];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sm.R[m][32 * hh + j] = REV ? in32[j] - x[j] : bm * (in32[j] - x[j]);
+    }
+    __syncthreads();
+    float y[32];  // u-scan: U = Tm rhs (row m);  y-scan: Y = Tm^T X (row m)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = 0.f;
+    if (!REV) {
+      for (int i = 0; i <= m; ++i) {
+        const float tmi = Tm[m][i];
+        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][32 * hh]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 r4 = rr[q];
+          y[4 * q] = fmaf(tmi, r4.x, y[4 * q]);
+          y[4 * q + 1] = fmaf(tmi, r4.y, y[4 * q + 1]);
+          y[4 * q + 2] = fmaf(tmi, r4.z, y[4 * q + 2]);
+          y[4 * q + 3] = fmaf(tmi, r4.w, y[4 * q + 3]);
+        }
+      }
+    } else {
+      for (int i = m; i < C; ++i) {
+        const float tim = Tm[i][m];
+        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][32 * hh]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 r4 = rr[q];
+          y[4 * q] = fmaf(tim, r4.x, y[4 * q]);
+          y[4 * q + 1] = fmaf(tim, r4.y, y[4 * q + 1]);
+          y[4 * q + 2] = fmaf(tim, r4.z, y[4 * q + 2]);
+          y[4 * q + 3] = fmaf(tim, r4.w, y[4 * q + 3]);
+        }
+      }
+    }
+    __syncthreads();  // every row of R has been read
+    {
+      float* dst = (REV ? p.Y : p.U) + vrow;
+      if (in)
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<float4*>(dst)[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+      const float wsc = REV ? beta[m] : 1.f;  // the state update takes U, or beta Y
+      float w0[16], w1[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        w0[j] = wsc * y[j];
+        w1[j] = wsc * y[16 + j];
+      }
+      st_row16<T>(sm.w, m, 32 * hh, w0);
+      st_row16<T>(sm.w, m, 32 * hh + 16, w1);
+      if (!REV)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sm.R[m][32 * hh + j] = y[j];
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {  // state update psi_fb^T . W   (rows features)
+      tc_fence_after();
+#pragma unroll
+      for (int fb = 0; fb < NFB; ++fb) mma64x2<BF, true, true>(tbase + 64 + 64 * fb, sm.psi[fb], sm.w, false);
+      umma_commit(&sm.bar);
+    }
+    if (!REV && p.E && in) {  // E = P + sum_{i<m} L[m][i] U_i  (overlaps the state-update MMAs)
+      for (int i = 0; i < m; ++i) {
+        const float lmi = Lm[m][i];
+        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][32 * hh]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 r4 = rr[q];
+          x[4 * q] = fmaf(lmi, r4.x, x[4 * q]);
+          x[4 * q + 1] = fmaf(lmi, r4.y, x[4 * q + 1]);
+          x[4 * q + 2] = fmaf(lmi, r4.z, x[4 * q + 2]);
+          x[4 * q + 3] = fmaf(lmi, r4.w, x[4 * q + 3]);
+        }
+      }
+      float* dst = p.E + vrow;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(dst)[q] = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+    }
+    if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
+#pragma unroll
+    for (int fb = 0; fb < NFB; ++fb) {
+      float d[32];
+      ld_half32(tbase + rm.lane + 64 + 64 * fb, hh, d);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        S[fb][0][j] += d[j];
+        S[fb][1][j] += d[16 + j];
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // tiles and R are rewritten by the next chunk
+  }
+  if (ok && !REV && p.S) {  // final state, unpacked to the full E x E feature grid (S[a,b] = S[b,a])
+#pragma unroll
+    for (int fb = 0; fb < NFB; ++fb) {
+      const unsigned tb = sm.tab[64 * fb + m];
+      if (tb == 0xffffu) continue;
+      const int a = static_cast<int>(tb >> 8), bc = static_cast<int>(tb & 0xffu);
+      const float wt = a == bc ? 1.f : 0.70710678118654752f;
+      float* out = p.S + static_cast<size_t>(bh) * E * E * 64 + 32 * hh;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float val = S[fb][j >> 4][j & 15] * wt;
+        out[static_cast<size_t>(a * E + bc) * 64 + j] = val;
+        out[static_cast<size_t>(bc * E + a) * 64 + j] = val;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (!ok && tid == 0) mbar_drain(&sm.bar, phase ^ 1u);
+  tc_fence_before();
+  __syncthreads();
+  if (tid < 32) tmem_dealloc(tbase, 256);
+}
+
 // ------------------------------------------------------------------------------------------------
 // elementwise helpers (one warp per token row)
 // ------------------------------------------------------------------------------------------------
@@ -582,8 +897,32 @@ int run_prep(const DP& p, cudaStream_t st) {
   return from_cuda(cudaGetLastError());
 }
 
+// The tensor-core scans serve 16-bit inputs with Dv = 64 and E = D / M = 16, M in {1, 2, 4} (the
+// mixer's geometry: D = 64, M = 4; F = 192 features); the fp32 CUDA-core scans serve everything
+// else (and stay the fp32-exact mode).
+template <typename T>
+bool tc_scan_ok(const DP& p) {
+  return !std::is_same<T, float>::value && p.Dv == 64 && p.D == 16 * p.M && (p.M == 1 || p.M == 2 || p.M == 4);
+}
+
+template <typename T, bool REV>
+int run_tc_scan(const DP& p, cudaStream_t st) {
+  auto go = [&](auto kern, size_t smem) -> int {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+      return KATA_ERR_CUDA;
+    kern<<<p.B * p.H, 128, smem, st>>>(p);
+    return from_cuda(cudaGetLastError());
+  };
+  constexpr size_t smem = sizeof(TcScanSmem<3>) + 1024;  // E = 16: 136 features in 3 blocks
+  if (p.M == 1) return go(delta_tc_scan_kernel<T, 16, 1, REV>, smem);
+  if (p.M == 2) return go(delta_tc_scan_kernel<T, 16, 2, REV>, smem);
+  return go(delta_tc_scan_kernel<T, 16, 4, REV>, smem);
+}
+
 template <typename T>
 int run_u_scan(const DP& p, cudaStream_t st) {
+  if constexpr (!std::is_same<T, float>::value)
+    if (tc_scan_ok<T>(p)) return run_tc_scan<T, false>(p, st);
   const int F = feat_dim(p.D / p.M), vs = pick_vs(F, p.Dv);
   const dim3 grid(p.Dv / vs, p.B * p.H);
   if (vs == 32) return launch_k(delta_u_scan_kernel<T, 32>, grid, scan_smem(F, p.D, 32, false), st, p, F);
@@ -592,6 +931,8 @@ int run_u_scan(const DP& p, cudaStream_t st) {
 
 template <typename T>
 int run_y_scan(const DP& p, cudaStream_t st) {
+  if constexpr (!std::is_same<T, float>::value)
+    if (tc_scan_ok<T>(p)) return run_tc_scan<T, true>(p, st);
   const int F = feat_dim(p.D / p.M), vs = pick_vs(F, p.Dv);
   const dim3 grid(p.Dv / vs, p.B * p.H);
   if (vs == 32) return launch_k(delta_y_scan_kernel<T, 32>, grid, scan_smem(F, p.D, 32, true), st, p, F);

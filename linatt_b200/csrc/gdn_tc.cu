@@ -26,13 +26,14 @@
 #include "gdn_tc.h"
 #include "host_util.h"
 #include "sm100.cuh"
+#include "tc64.cuh"
 
 namespace kata {
 namespace gdntc {
 namespace {
+using namespace tc64;
 
 constexpr int CH = 64;
-constexpr uint32_t TB = 8192;  // a 64 x 64 16-bit tile: rows of 128 B, 128-byte swizzle
 
 struct Params {
   const void* q;
@@ -123,45 +124,9 @@ __device__ __forceinline__ Item item_of(const Params& p, int s, int items) {
   return it;
 }
 
-__device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
-}
-
 // ------------------------------------------------------------------------------------------------
 // tiles and MMAs
 // ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t toff(int r, int c) { return swz_offset(r, c * 2, 128); }
-
-// K-major operand: tile rows are the M (or N) index, the 64 columns of a row are K.
-__device__ __forceinline__ uint64_t kdesc(const void* t) { return umma_smem_desc(smem_u32(t), 16, 1024, 128); }
-// MN-major operand: tile rows are the K index, the 64 columns of a row are M (or N).
-__device__ __forceinline__ uint64_t mdesc(const void* t) { return umma_smem_desc(smem_u32(t), TB, 1024, 128); }
-
-// D (64 x 64, fp32, TMEM) (+)= A (64 x 64) B (64 x 64); issued by one thread, four K steps of 16.
-template <bool BF, bool AMN, bool BMN>
-__device__ __forceinline__ void mma64(uint32_t d, const void* a, const void* b, bool acc) {
-  constexpr uint32_t idesc = umma_idesc_f16(64, 64, BF, AMN, BMN);
-  const uint64_t ad = AMN ? mdesc(a) : kdesc(a);
-  const uint64_t bd = BMN ? mdesc(b) : kdesc(b);
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    // K step: 32 bytes along a K-major row, or 16 rows (2048 bytes) of an MN-major tile
-    const uint64_t ao = AMN ? static_cast<uint64_t>(kk * 128) : static_cast<uint64_t>(kk * 2);
-    const uint64_t bo = BMN ? static_cast<uint64_t>(kk * 128) : static_cast<uint64_t>(kk * 2);
-    umma_ss(d, ad + ao, bd + bo, idesc, (acc || kk > 0) ? 1u : 0u);
-  }
-}
-
-// Row of the M = 64 accumulators this thread reads: slot = chunk (lane half), row = tile row.
-struct RowMap {
-  int slot, row;
-  uint32_t lane;  // (32 * warp) << 16: the warp's TMEM lane base
-};
-__device__ __forceinline__ RowMap rowmap() {
-  const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
-  return {ln >> 4, w * 16 + (ln & 15), static_cast<uint32_t>(32 * w) << 16};
-}
-
 // 64 fp32 columns of this thread's TMEM lane (warp-collective).
 __device__ __forceinline__ void ld64(uint32_t taddr, float (&x)[64]) {
   uint32_t a[32], b[32];
@@ -259,17 +224,6 @@ __device__ __forceinline__ void ld_g16(const void* src, float (&x)[64], bool ok)
   }
 }
 
-// Async 16-byte copy global -> shared (src-size 0 zero-fills), as in the fp32 scans.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool pred) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool pred) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(pred ? 4 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
 // 64 rows (first `len` valid) of a (tokens, heads, 64) 16-bit tensor into a swizzled tile.
 __device__ __forceinline__ void cpa_tile(uint8_t* tile, const void* base, int heads, int h, int t0, int len) {
   const uint8_t* b = static_cast<const uint8_t*>(base);
@@ -296,16 +250,6 @@ __device__ __forceinline__ void cpa_vec(float* dst, const float* base, int heads
   }
 }
 
-// Bounded wait on the CTA's MMA barrier; false (uniformly) when some thread timed out.
-__device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t& phase, volatile int* abort) {
-  WaitCtx wc{nullptr, abort};
-  const bool ok = mbar_wait(bar, phase, wc);
-  phase ^= 1u;
-  const bool fail = __syncthreads_or(!ok);
-  tc_fence_after();
-  return !fail;
-}
-
 // Unit lower-triangular solve (I + L) x = e_c for one column, in registers (L[i][j] = 0 for j >= i).
 __device__ __forceinline__ void solve_column(const float (*L)[68], int c, float (&x)[64]) {
 #pragma unroll
@@ -325,14 +269,10 @@ __device__ __forceinline__ void solve_column(const float (*L)[68], int c, float 
   }
 }
 
-template <typename T>
-constexpr bool is_bf16() {
-  return std::is_same<T, __nv_bfloat16>::value;
-}
-
 // ------------------------------------------------------------------------------------------------
 // prep: gamma, Tm (or the given A), W, U0.  Two chunks per CTA, 128 threads.
 // ------------------------------------------------------------------------------------------------
+
 struct PrepSmem {
   uint8_t tK[2][TB];  // k, then X1 = beta e^gamma k
   uint8_t tV[2][TB];  // v, then X2 = beta v
@@ -480,24 +420,6 @@ __global__ void __launch_bounds__(128) gdn_tc_prep_kernel(Params p, int items) {
 // the threads write (state, u~, ...) carry only the CTA's 32 columns; the other columns stay zero and
 // their MMA outputs are never read.
 // ------------------------------------------------------------------------------------------------
-// tcgen05.ld / st take one TMEM address for the whole warp, so a lane half cannot name its own
-// columns: the warp loads the CTA's 32 columns and each lane half keeps its 16 (h = lane >> 4).
-__device__ __forceinline__ void ld_quarter(uint32_t taddr, int h, float (&x)[16]) {
-  uint32_t a[32];
-  tmem_ld32(taddr, a);
-  tmem_wait_ld();
-#pragma unroll
-  for (int j = 0; j < 16; ++j) x[j] = __uint_as_float(h ? a[16 + j] : a[j]);
-}
-// 16 values into row r, columns [c0, c0 + 16) of a tile (c0 a multiple of 8).
-template <typename T>
-__device__ __forceinline__ void st_row16(uint8_t* tile, int r, int c0, const float (&x)[16]) {
-  const uint32_t base = smem_u32(tile);
-#pragma unroll
-  for (int c = 0; c < 2; ++c)
-    st_shared_v4(base + toff(r, c0 + 8 * c), pack2<T>(x[8 * c], x[8 * c + 1]), pack2<T>(x[8 * c + 2], x[8 * c + 3]),
-                 pack2<T>(x[8 * c + 4], x[8 * c + 5]), pack2<T>(x[8 * c + 6], x[8 * c + 7]));
-}
 template <typename T>
 __device__ __forceinline__ void ld_row16(const uint8_t* tile, int r, int c0, float (&x)[16]) {
 #pragma unroll
@@ -525,17 +447,6 @@ __device__ __forceinline__ void cpa_f32_half(float* dst, const float* base, int 
     cp_async16(d + (r * 32 + 4 * c) * 4, base + (static_cast<size_t>(t0 + rr) * heads + h) * 64 + c0 + 4 * c, r < len);
   }
 }
-__device__ __forceinline__ void zero_tile(uint8_t* tile) {
-  const uint32_t base = smem_u32(tile);
-  for (int i = threadIdx.x; i < static_cast<int>(TB / 16); i += blockDim.x) st_shared_v4(base + 16 * i, 0u, 0u, 0u, 0u);
-}
-// The same MMA into lane offsets 0 and 16 (both lane halves of every warp receive all 64 rows).
-template <bool BF, bool AMN, bool BMN>
-__device__ __forceinline__ void mma64x2(uint32_t d, const void* a, const void* b, bool acc) {
-  mma64<BF, AMN, BMN>(d, a, b, acc);
-  mma64<BF, AMN, BMN>(d + (16u << 16), a, b, acc);
-}
-
 // ------------------------------------------------------------------------------------------------
 // state: sequential over the chunks of one sequence; CTA = (sequence, value head, value half).
 //   hS[c] = S (16-bit);  u = U0 - W S;  S <- e^{gamma_C} S + K^T diag(e^{gamma_C - gamma}) u

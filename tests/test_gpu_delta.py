@@ -168,7 +168,11 @@ def test_full_size_properties_layer_geometry():
     lhs = U
     rhs = bc.float()[..., None] * (vc.float() - E)
     e = ((lhs - rhs).norm() / rhs.norm()).item()
-    assert e < 1e-4, e
+    # bf16 inputs take the tensor-core scans, whose inter-chunk products psi(K) H use 16-bit
+    # operands (the reference's Triton kernels round the same operands to bf16); the check's E
+    # comes from fp32 kernels, so the identity holds to about the bf16 rounding of those terms
+    # (5.6e-4 measured; 2e-5 with the fp32 scans)
+    assert e < 2e-3, e
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
