@@ -476,6 +476,26 @@ KATA_API int kata_rownorm_fwd(const kata_rownorm_args* args, kata_stream_t strea
 KATA_API size_t kata_rownorm_bwd_workspace_bytes(const kata_rownorm_args* args);
 KATA_API int kata_rownorm_bwd(const kata_rownorm_args* args, kata_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * The KATA LM's MLP activation and loss (kata/modeling.py's fla GatedMLP with fuse_swiglu and the
+ * fused cross entropy of LinearAttentionForCausalLM), for the config-5 training step.
+ *   SwiGLU: gu is (rows, 2I) = [g | u] (the fused gate/up projection), y = silu(g) u (rows, I);
+ *   backward writes dgu = [dy u silu'(g) | dy silu(g)].  I a multiple of 8 (16-bit) or 4 (fp32).
+ *   Cross entropy over rows of V logits with int64 targets (target < 0: ignored row):
+ *   forward writes lse (rows, fp32) and loss_rows = lse - logit[target] (0 when ignored);
+ *   backward writes dlogits = (softmax - onehot) * grad_loss[0] * inv_count[0] (0 for ignored rows),
+ *   both scalars read on the device.  One read of the logits forward, one read and one write
+ *   backward; no fp32 copy of the logits.  No counterpart in the reference's own code (fla kernels).
+ * ------------------------------------------------------------------------------------------- */
+KATA_API int kata_swiglu_fwd(const void* gu, void* y, long long rows, int I, int dtype, kata_stream_t stream);
+KATA_API int kata_swiglu_bwd(const void* gu, const void* dy, void* dgu, long long rows, int I, int dtype,
+                             kata_stream_t stream);
+KATA_API int kata_cross_entropy_fwd(const void* logits, const int64_t* targets, float* lse, float* loss_rows,
+                                    long long rows, int V, int dtype, kata_stream_t stream);
+KATA_API int kata_cross_entropy_bwd(const void* logits, const int64_t* targets, const float* lse,
+                                    const float* grad_loss, const float* inv_count, void* dlogits, long long rows,
+                                    int V, int dtype, kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

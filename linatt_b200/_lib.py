@@ -199,6 +199,15 @@ def lib() -> ctypes.CDLL:
                 w = getattr(L, f"kata_{nm}_bwd_workspace_bytes")
                 w.restype = c_size_t
                 w.argtypes = [ctypes.POINTER(st)]
+            c_ll = ctypes.c_longlong
+            L.kata_swiglu_fwd.restype = c_int
+            L.kata_swiglu_fwd.argtypes = [c_void_p, c_void_p, c_ll, c_int, c_int, c_void_p]
+            L.kata_swiglu_bwd.restype = c_int
+            L.kata_swiglu_bwd.argtypes = [c_void_p, c_void_p, c_void_p, c_ll, c_int, c_int, c_void_p]
+            L.kata_cross_entropy_fwd.restype = c_int
+            L.kata_cross_entropy_fwd.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_ll, c_int, c_int, c_void_p]
+            L.kata_cross_entropy_bwd.restype = c_int
+            L.kata_cross_entropy_bwd.argtypes = [c_void_p] * 6 + [c_ll, c_int, c_int, c_void_p]
             if L.kata_abi_version() != ABI_VERSION:
                 raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
             _lib = L

@@ -7,8 +7,8 @@ next-token cross entropy (the last position of every row has no target), as fla'
 ``LinearAttentionForCausalLM`` computes it.  Parameter names follow the reference
 (``model.layers.{i}.attn.*``, ``mlp.gate_proj`` / ``up_proj`` / ``down_proj``, ``attn_norm``,
 ``mlp_norm``, ``model.norm``, ``lm_head``).  Everything outside the mixer is plain PyTorch
-(cuBLAS GEMMs, PyTorch's loss and elementwise kernels) except the RMSNorms, which use the mixer's row
-kernel: the hot path of this library is the mixer.
+(cuBLAS GEMMs, residual adds, embedding) except the RMSNorms (the mixer's row kernel), the SwiGLU and
+the cross entropy (``lm_ops.cu``): the hot path of this library is the mixer.
 """
 
 from __future__ import annotations
@@ -19,6 +19,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _lib
 from .mixer import FlashKataMixer, RowNormFunction
 
 __all__ = ["KataLMConfig", "KataLM"]
@@ -79,6 +80,69 @@ class RMSNorm(nn.Module):
         return RowNormFunction.apply(x.reshape(-1, N), self.weight, None, None, 2, 0, N, self.eps, 1, 1).view(x.shape)
 
 
+def _dt(t: torch.Tensor) -> int:
+    return _lib.DTYPE[t.dtype]
+
+
+class SwiGLUFunction(torch.autograd.Function):
+    """y = silu(g) * u of a (rows, 2I) tensor [g | u] on ``kata_swiglu_fwd`` / ``_bwd`` (one pass each)."""
+
+    @staticmethod
+    def forward(ctx, gu):
+        dev = _lib.require_cuda(gu)
+        gu = gu.contiguous()
+        I = gu.shape[-1] // 2
+        y = torch.empty(*gu.shape[:-1], I, device=dev, dtype=gu.dtype)
+        rows = gu.numel() // (2 * I)
+        _lib.check(_lib.lib().kata_swiglu_fwd(gu.data_ptr(), y.data_ptr(), rows, I, _dt(gu), _lib.stream_handle(dev)),
+                   "kata_swiglu_fwd")
+        ctx.save_for_backward(gu)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (gu,) = ctx.saved_tensors
+        dy = dy.to(gu.dtype).contiguous()
+        dgu = torch.empty_like(gu)
+        I = gu.shape[-1] // 2
+        _lib.check(_lib.lib().kata_swiglu_bwd(gu.data_ptr(), dy.data_ptr(), dgu.data_ptr(), gu.numel() // (2 * I), I,
+                                              _dt(gu), _lib.stream_handle(gu.device)), "kata_swiglu_bwd")
+        return dgu
+
+
+class CrossEntropyFunction(torch.autograd.Function):
+    """Mean cross entropy of (rows, V) logits against int64 targets (negative: ignored), over the
+    valid rows, on ``kata_cross_entropy_fwd`` / ``_bwd``: the logits are read once forward and once
+    backward in their own dtype (no fp32 copy); the gradient scale comes from device scalars."""
+
+    @staticmethod
+    def forward(ctx, logits, targets):
+        dev = _lib.require_cuda(logits, targets)
+        logits = logits.contiguous()
+        targets = targets.contiguous().to(torch.int64)
+        rows, V = logits.shape
+        lse = torch.empty(rows, device=dev, dtype=torch.float32)
+        loss_rows = torch.empty(rows, device=dev, dtype=torch.float32)
+        _lib.check(_lib.lib().kata_cross_entropy_fwd(logits.data_ptr(), targets.data_ptr(), lse.data_ptr(),
+                                                     loss_rows.data_ptr(), rows, V, _dt(logits),
+                                                     _lib.stream_handle(dev)), "kata_cross_entropy_fwd")
+        inv = 1.0 / (targets >= 0).sum().clamp_min(1).to(torch.float32)
+        ctx.save_for_backward(logits, targets, lse, inv.reshape(1))
+        return loss_rows.sum() * inv
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, targets, lse, inv = ctx.saved_tensors
+        rows, V = logits.shape
+        dl = torch.empty_like(logits)
+        gs = g.detach().to(torch.float32).reshape(1).contiguous()
+        _lib.check(_lib.lib().kata_cross_entropy_bwd(logits.data_ptr(), targets.data_ptr(), lse.data_ptr(),
+                                                     gs.data_ptr(), inv.data_ptr(), dl.data_ptr(), rows, V,
+                                                     _dt(logits), _lib.stream_handle(logits.device)),
+                   "kata_cross_entropy_bwd")
+        return dl, None
+
+
 class GatedMLP(nn.Module):
     """SwiGLU MLP (fla ``GatedMLP``): down(silu(gate(x)) * up(x)), intermediate size the multiple of
     256 nearest above 2/3 * hidden_ratio * hidden_size."""
@@ -94,8 +158,7 @@ class GatedMLP(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         gu = F.linear(x, torch.cat([self.gate_proj.weight, self.up_proj.weight], dim=0))  # one GEMM
-        g, u = gu.chunk(2, dim=-1)
-        return self.down_proj(F.silu(g) * u)
+        return self.down_proj(SwiGLUFunction.apply(gu))
 
 
 class KataBlock(nn.Module):
@@ -144,4 +207,4 @@ class KataLM(nn.Module):
             return logits
         # next-token targets; the last position of each row has none
         tgt = torch.cat([labels[:, 1:], torch.full_like(labels[:, :1], -100)], dim=1)
-        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), tgt.reshape(-1), ignore_index=-100)
+        return CrossEntropyFunction.apply(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1))

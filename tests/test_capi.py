@@ -160,6 +160,7 @@ def test_product_path_refuses_cpu_tensors():
 def test_binding_signatures_match_the_header(L):
     """Every entry point the ctypes binding types has the header's parameter kinds, in order
     (pointer / int / float): a miscounted argument list would pass garbage through the C ABI."""
+    import ctypes
     import re
 
     from linatt_b200 import _lib
@@ -174,8 +175,9 @@ def test_binding_signatures_match_the_header(L):
         kinds = "" if params in ("", "void") else "".join(
             "p" if ("*" in x or "kata_stream_t" in x) else ("f" if x.strip().startswith("float") else "i")
             for x in params.split(","))
+        ints = (_lib.c_int, _lib.c_size_t, ctypes.c_longlong)
         bound = "".join("f" if t is _lib.c_float else ("p" if t in (_lib.c_void_p, ) or hasattr(t, "_type_")
-                                                       and not t in (_lib.c_int, _lib.c_size_t) else "i")
+                                                       and t not in ints else "i")
                         for t in fn.argtypes)
         assert kinds == bound, f"{name}: header {kinds} vs binding {bound}"
         checked += 1

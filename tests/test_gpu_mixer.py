@@ -245,3 +245,32 @@ def test_row_norm_wide(dtype, N, norm):
     assert rel(x.grad, xd.grad) < tol
     if norm == "rms":
         assert rel(w.grad, wd.grad) < tol
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_swiglu_and_cross_entropy(dtype):
+    """The LM's fused SwiGLU and cross entropy against PyTorch in float64 (values and gradients),
+    with ignored (-100) targets and a non-unit upstream gradient."""
+    from linatt_b200.lm import CrossEntropyFunction, SwiGLUFunction
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    gu = (2 * torch.randn(300, 2 * 256, device="cuda", generator=g)).to(dtype).requires_grad_(True)
+    y = SwiGLUFunction.apply(gu)
+    dy = torch.randn(300, 256, device="cuda", generator=g).to(dtype)
+    y.backward(dy)
+    gd = gu.detach().double().requires_grad_(True)
+    a, b = gd.chunk(2, -1)
+    r = F.silu(a) * b
+    r.backward(dy.double())
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel(y, r) < tol and rel(gu.grad, gd.grad) < tol
+    logits = (3 * torch.randn(257, 32000, device="cuda", generator=g)).to(dtype).requires_grad_(True)
+    tgt = torch.randint(0, 32000, (257,), device="cuda", generator=g)
+    tgt[::7] = -100
+    loss = CrossEntropyFunction.apply(logits, tgt)
+    (0.5 * loss).backward()
+    ld = logits.detach().double().requires_grad_(True)
+    ref = F.cross_entropy(ld, tgt, ignore_index=-100)
+    (0.5 * ref).backward()
+    assert abs(loss.item() - ref.item()) / abs(ref.item()) < (1e-6 if dtype == torch.float32 else 1e-3)
+    assert rel(logits.grad, ld.grad) < tol
