@@ -56,8 +56,15 @@ enum { KATA_DTYPE_F32 = 0, KATA_DTYPE_BF16 = 1, KATA_DTYPE_F16 = 2 };
 /* Kernel family.  AUTO picks the tcgen05 tensor-core kernels for bf16/f16 inputs whose shape
  * they cover and the fp32-exact SIMT kernels otherwise (fp32 inputs always take SIMT, which is
  * the fp32-accurate mode).  TC / SIMT force one family (TC returns KATA_ERR_UNSUPPORTED when the
- * shape or dtype is outside its envelope). */
-enum { KATA_ALGO_AUTO = 0, KATA_ALGO_TC = 1, KATA_ALGO_SIMT = 2 };
+ * shape or dtype is outside its envelope).
+ * TC_GRAM: the sum score with groups of 16 (D = 16 M, D in {64, 128}, Dv = 64, bf16) as a linear
+ * score over the 136 entries of the group Gram matrix G(x) = sum_a x_a x_a^T (A[t,s] =
+ * scale^2 <G(q_t), G(k_s)>, the same function): one K = 144 tensor-core product per score tile
+ * instead of M^2 squared parts.  It needs a workspace (kata_attn_fwd_workspace_bytes /
+ * kata_attn_bwd_workspace_bytes); AUTO takes it for such problems when the workspace passed is at
+ * least that large, and the parts form (TC) otherwise.  No counterpart in the reference, whose sum
+ * kernels square the M^2 parts. */
+enum { KATA_ALGO_AUTO = 0, KATA_ALGO_TC = 1, KATA_ALGO_SIMT = 2, KATA_ALGO_TC_GRAM = 3 };
 
 /* Score form.  CONCAT: A[t,s] = sum_g (scale * q_g[t].k_g[s])^2  (kata_quadratic)
  *              SUM:    A[t,s] = sum_{i,j} (scale * q_i[t].k_j[s])^2 (kata_quadratic_sum) */
@@ -87,13 +94,20 @@ typedef struct {
   int score;       /* KATA_SCORE_*                                       */
   int algo;        /* KATA_ALGO_*                                        */
   float scale;     /* per-group dot scale (reference default 1/sqrt(D/M)) */
+  void* workspace; /* optional: kata_attn_fwd_workspace_bytes(args) bytes, 16-byte aligned
+                      (TC_GRAM only; NULL / 0 -> AUTO runs the parts form) */
+  size_t workspace_bytes;
 } kata_attn_fwd_args;
 
 KATA_API int kata_attn_fwd(const kata_attn_fwd_args* args, kata_stream_t stream);
+/* Device workspace the forward can use: the bf16 Gram features of q and k when TC_GRAM (or AUTO
+ * on a TC_GRAM problem) applies, else 0. */
+KATA_API size_t kata_attn_fwd_workspace_bytes(const kata_attn_fwd_args* args);
 
-/* Kernel family that kata_attn_fwd / kata_attn_bwd would run for these arguments (only the shape,
- * dtype, score, decay and algo fields are read; no pointer is touched): KATA_ALGO_TC (tcgen05) or
- * KATA_ALGO_SIMT (fp32 CUDA cores), or a negative KATA_ERR_* code.  Lets a binding tell a caller
+/* Kernel family that kata_attn_fwd / kata_attn_bwd would run for these arguments with the workspace
+ * that kata_attn_*_workspace_bytes asks for (only the shape, dtype, score, decay and algo fields
+ * are read; no pointer is touched): KATA_ALGO_TC_GRAM or KATA_ALGO_TC (tcgen05) or KATA_ALGO_SIMT
+ * (fp32 CUDA cores), or a negative KATA_ERR_* code.  Lets a binding tell a caller
  * when a bf16/f16 problem falls outside the tensor-core envelope and runs on the much slower SIMT
  * kernels.  No counterpart in the reference (its Triton kernels have a single path). */
 KATA_API int kata_attn_algo(const kata_attn_fwd_args* args);
@@ -109,7 +123,9 @@ KATA_API int kata_attn_algo(const kata_attn_fwd_args* args);
  * fallbacks parallel_kata_attn_bwd (:49-146) / parallel_kata_attn_bwd_sum_torch (:579-653),
  * and the autograd recompute of the decayed form (_KataDecayFunction.backward, :329-347).
  * workspace: kata_attn_bwd_workspace_bytes(args) bytes of device memory (may be 0 -> NULL ok);
- * the size depends on B, T, HQ and on whether c is given (decay adds a head-major copy of c).
+ * the size depends on B, T, HQ and on whether c is given (decay adds a head-major copy of c), and
+ * on a TC_GRAM problem (algo AUTO or TC_GRAM) it adds the Gram features and their gradients.  AUTO
+ * given less than that, but at least the parts-form size, runs the parts form.
  * ------------------------------------------------------------------------------------------- */
 typedef struct {
   const void* q;     /* (B,T,HQ,D)  dtype */
@@ -146,8 +162,10 @@ KATA_API int kata_attn_bwd(const kata_attn_bwd_args* args, kata_stream_t stream)
  * interface passes the kernel only its inputs and outputs and offers no workspace.  This entry
  * point runs exactly the computation of kata_attn_bwd but ignores args->workspace and uses a
  * 16 MiB file-scope device array of the library instead (held on every GPU that loads the
- * library until the process exits).  Problems whose kata_attn_bwd_workspace_bytes() exceeds
- * 16 MiB are rejected with KATA_ERR_SCRATCH_LIMIT.  The first call on a device resolves the
+ * library until the process exits).  Problems whose parts-form workspace
+ * (kata_attn_bwd_workspace_bytes() with algo TC or SIMT; TC_GRAM's own size for algo TC_GRAM)
+ * exceeds 16 MiB are rejected with KATA_ERR_SCRATCH_LIMIT; AUTO runs the Gram form of a sum-score
+ * problem only when its larger workspace fits in the array.  The first call on a device resolves the
  * array's address for that device, so make it outside any stream capture; the address is kept for
  * the life of the process, so the device must not be reset (cudaDeviceReset) between calls.  All
  * calls on a device share the array: calls whose kernels overlap on the GPU race on it.  Only the

@@ -20,7 +20,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "libkata_b200.so"
 
 KATA_OK = 0
 DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
-ALGO = {"auto": 0, "tc": 1, "simt": 2}
+ALGO = {"auto": 0, "tc": 1, "simt": 2, "tc_gram": 3}
 SCORE = {"concat": 0, "sum": 1}
 ABI_VERSION = 2
 
@@ -45,6 +45,7 @@ class AttnFwdArgs(ctypes.Structure):
         ("o", c_void_p), ("den", c_void_p), ("status", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HQ", c_int), ("D", c_int), ("Dv", c_int),
         ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -142,6 +143,8 @@ def lib() -> ctypes.CDLL:
             L.kata_attn_fwd.argtypes = [ctypes.POINTER(AttnFwdArgs), c_void_p]
             L.kata_attn_algo.restype = c_int
             L.kata_attn_algo.argtypes = [ctypes.POINTER(AttnFwdArgs)]
+            L.kata_attn_fwd_workspace_bytes.restype = c_size_t
+            L.kata_attn_fwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnFwdArgs)]
             L.kata_attn_bwd.restype = c_int
             L.kata_attn_bwd.argtypes = [ctypes.POINTER(AttnBwdArgs), c_void_p]
             L.kata_attn_bwd_noalloc.restype = c_int

@@ -145,20 +145,26 @@ struct DqRingBars {
   float xch_delta[2][kTile];  // halves of delta_t; with decay, at the end, halves of the dc row sums
 };
 
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM>
 __global__ void __launch_bounds__(kThreadsRing, 1)
     attn_bwd_dq_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                         AttnBwdParams p) {
   constexpr int E = D / M;
-  constexpr int CW = BoxW<E>::value;
+  constexpr int CW = ScoreBoxW<E, GRAM>::value;
   constexpr int NBOX = D / CW;
   constexpr int VCW = BoxW<DV>::value;
   constexpr int NVBOX = DV / VCW;
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kColDQ = 384;
-  constexpr int kItems = 1 + NP;  // items per key tile: dN, then S_0..S_{NP-1}
+  static_assert(!GRAM || (M == 1 && !SUM && !DECAY), "Gram features: one linear score part");
+  // Gram features: dQ (= d phi(q), kGramFP columns) does not fit beside three slots, and the linear
+  // score needs no S here (d phi(q) = dA phi(K)), so the ring has two slots of dN items only, each
+  // overwritten in place by dA' as the TMEM operand of its dQ chain.
+  constexpr int NS = GRAM ? 2 : 3;  // TMEM ring slots
+  constexpr uint32_t kColDQ = GRAM ? 256 : 384;
+  constexpr int kItems = GRAM ? 1 : 1 + NP;  // items per key tile: dN, then S_0..S_{NP-1}
+  constexpr int NPL = GRAM ? 0 : NP;         // score parts the compute warps read
   using L = BwdSmem<D, DV>;
 
   extern __shared__ uint8_t smem_raw[];
@@ -246,8 +252,8 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
     }
   } else if (warp == 1) {
     {  // warp-wide issue (every lane runs the loop; one elected lane issues)
-      // Score issuer: dN and the score parts.  Item `it` = j * kItems + q lives in slot it % 3; the
-      // slot is reused once the chain warp has released the item three back (w_done: its dQ chain,
+      // Score issuer: dN and the score parts.  Item `it` = j * kItems + q lives in slot it % NS; the
+      // slot is reused once the chain warp has released the item NS back (w_done: its dQ chain,
       // if any, has completed).  The ring holds V_j at position 2j and K_j at 2j + 1 (kRingDQ = 4:
       // slot (2j + c) & 3, use parity (j >> 1) & 1).
       const uint32_t id_nn = umma_idesc_f16(128, 128, kBF16, false, false);
@@ -260,13 +266,13 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       const uint64_t rk0 = kmajor_desc<CW>(sRing, 0, E, 0);    // K in ring slot 0, K-major
       static_assert(kRingDQ == 4, "ring positions below assume four slots");
       bool ok = mbar_wait_w(&bars.qo_full, 0, wc);
-      int it = 0, x = 0;       // x = it % 3
-      uint32_t use_par = 0;    // parity of (it / 3), i.e. of the current use of slot x
+      int it = 0, x = 0;       // x = it % NS
+      uint32_t use_par = 0;    // parity of (it / NS), i.e. of the current use of slot x
       for (int j = 0; ok && j < nk; ++j) {
         const uint32_t ring_par = static_cast<uint32_t>(j >> 1) & 1u;
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
-          if (it >= 3 && !mbar_wait_w(&bars.w_done[x], use_par ^ 1, wc)) {
+          if (it >= NS && !mbar_wait_w(&bars.w_done[x], use_par ^ 1, wc)) {
             ok = false;
             break;
           }
@@ -284,7 +290,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
               umma_ss_w(sd, od0 + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
             umma_commit_w(&bars.i_full[x]);
             umma_commit_w(&bars.ring_empty[slotV]);
-            if (!mbar_wait_w(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
+            if (!GRAM && !mbar_wait_w(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
               ok = false;
               break;
             }
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             umma_commit_w(&bars.i_full[x]);
           }
           ++it;
-          if (++x == 3) {
+          if (++x == NS) {
             x = 0;
             use_par ^= 1;
           }
@@ -329,7 +335,20 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             ok = false;
             break;
           }
-          if (q > 0) {
+          if (GRAM) {  // dQ += dA' phi(K_j): the K tile's first and only use
+            const int kslot = (2 * j + 1) & 3;
+            if (!mbar_wait_w(&bars.ring_full[kslot], static_cast<uint32_t>(j >> 1) & 1u, wc)) {
+              ok = false;
+              break;
+            }
+            const uint64_t kd = rkm0 + desc_units(static_cast<uint32_t>(kslot) * L::ITEM);
+            const uint32_t wa = tbase + static_cast<uint32_t>(x) * 128u;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk)
+              umma_ts_w(tbase + kColDQ, wa + packed_col(kk), kd + mnstep<CW>(kk), id_dq, (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit_w(&bars.ring_empty[kslot]);
+          } else if (q > 0) {
             const int pp = q - 1;
             const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
             const bool first = (j == 0) && (!SUM || gb == 0);
@@ -344,7 +363,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             if (pp == NP - 1) umma_commit_w(&bars.ring_empty[kslot]);  // K tile no longer needed
           }
           umma_commit_w(&bars.w_done[x]);
-          if (++x == 3) {
+          if (++x == NS) {
             x = 0;
             use_par ^= 1;
           }
@@ -400,7 +419,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       ws.rden[hm] = rden * scale2;
       ws.dr[hm] = live ? -delta * rden * scale2 : 0.f;
     }
-    const float w_scale = 2.f * p.scale * p.scale;
+    const float w_scale = GRAM ? 1.f : 2.f * p.scale * p.scale;  // Gram: W = dA (linear score)
     const float2 rden_w = make_float2(rden * w_scale, rden * w_scale);
     const float2 ndr_w = make_float2(-delta * rden * w_scale, -delta * rden * w_scale);
     // decay: e(t,s) = exp(min(c_t - c_s, 0)) is folded into dA' once per key tile; the dc row sum
@@ -419,8 +438,8 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       float2 da[32];  // dA' of this thread's 64 key columns
       uint32_t cm[2] = {0u, 0u};  // decay: columns with c_t - c_s > 0 (no dc contribution)
       {
-        const int x = it % 3;
-        if (!mbar_wait(&bars.i_full[x], (it / 3) & 1, wc)) {
+        const int x = it % NS;
+        if (!mbar_wait(&bars.i_full[x], (it / NS) & 1, wc)) {
           ok = false;
           break;
         }
@@ -437,9 +456,11 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
           for (int x2 = 0; x2 < 8; ++x2) da[8 * c + x2] = ffma2(u2f2(rn[cur][2 * x2], rn[cur][2 * x2 + 1]), rden_w, ndr_w);
           if (c < 3) tmem_wait_ld();
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.i_free[x]);
+        if constexpr (!GRAM) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.i_free[x]);
+        }
         ++it;
         if (diag) {
 #pragma unroll
@@ -448,6 +469,19 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             if (s0 > row) da[x2].x = 0.f;
             if (s0 + 1 > row) da[x2].y = 0.f;
           }
+        }
+        if constexpr (GRAM) {  // dA' back into the slot (packed) as the A operand of the dQ chain
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t wv[8];
+#pragma unroll
+            for (int x2 = 0; x2 < 8; ++x2) wv[x2] = pack2<T>(da[8 * c + x2].x, da[8 * c + x2].y);
+            tmem_st8(nbase + c * 8u, wv);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.i_free[x]);
         }
         if (DECAY) {
           // the key tile's c, staged with K_j: wait for that load (the slot is not refilled before
@@ -491,9 +525,9 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
         }
       }
       const bool any_clamp = DECAY && (cm[0] | cm[1]) != 0u;
-      for (int pp = 0; pp < NP; ++pp, ++it) {
-        const int x = it % 3;
-        if (!mbar_wait(&bars.i_full[x], (it / 3) & 1, wc)) {
+      for (int pp = 0; pp < NPL; ++pp, ++it) {
+        const int x = it % NS;
+        if (!mbar_wait(&bars.i_full[x], (it / NS) & 1, wc)) {
           ok = false;
           break;
         }
@@ -540,12 +574,14 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
     if (DECAY && ok && live && hc == 0) p.dc[rowidx] = bars.xch_delta[0][row] + bars.xch_delta[1][row];
     if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
       tc_fence_after();
-      constexpr int HD = D / 2;
-      T* dqrow = static_cast<T*>(p.dq) + rowidx * D + hc * HD;
+      // column halves of dQ: D / 2 each, or 80 + 64 for the kGramFP = 144 Gram columns
+      constexpr int HD0 = GRAM ? 80 : D / 2;
+      T* dqrow = static_cast<T*>(p.dq) + rowidx * D;
+      const int cbeg = hc ? HD0 : 0, cend = hc ? D : HD0;
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
+      for (int c0 = cbeg; c0 < cend; c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(lane_addr + kColDQ + hc * HD + c0, r);
+        tmem_ld16(lane_addr + kColDQ + c0, r);
         tmem_wait_ld();
         if (live) {
 #pragma unroll
@@ -578,13 +614,13 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
 // other half (columns [32,64) and [96,128)).  The issuer reuses a slot only after the compute warps
 // release it, issuing first the dK chain of the W it holds (and, for the last part, the dV chain of
 // P) as tensor-memory-operand MMAs; MMAs of one CTA execute in issue order.
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_dkdv_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                           AttnBwdParams p) {
   constexpr int E = D / M;
-  constexpr int CW = BoxW<E>::value;
+  constexpr int CW = ScoreBoxW<E, GRAM>::value;
   constexpr int NBOX = D / CW;
   constexpr int VCW = BoxW<DV>::value;
   constexpr int NVBOX = DV / VCW;
@@ -592,7 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kItems = 1 + NP;
   constexpr int kR = 4;  // dO / Q ring depth (two query tiles in flight)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kColDK = 256, kColDV = 384;
+  static_assert(!GRAM || (M == 1 && !SUM && !DECAY && DV <= 64), "Gram features: one linear score part");
+  // Gram features: dK (= d phi(k)) takes kGramFP = 144 columns from 256, dV the last 64
+  constexpr uint32_t kColDK = 256, kColDV = GRAM ? 448 : 384;
   using L = BwdSmem<D, DV>;
   static_assert(sizeof(DkvRingBars) <= 256, "barrier block");
   static_assert(L::KR_RING == kR, "ring depth");
@@ -897,8 +935,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int x2 = 0; x2 < 8; ++x2) {
             const float2 sv = u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]);
-            acc[8 * c + x2] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x2]);
-            if constexpr (kBF16) {  // S rounded to bf16, packed product (same operand precision as the MMA)
+            acc[8 * c + x2] = GRAM ? sv : pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x2]);
+            if constexpr (GRAM) {  // linear score: W^T = dA''^T itself
+              wv[x2] = dap[8 * c + x2];
+            } else if constexpr (kBF16) {  // S rounded to bf16, packed product (same operand precision as the MMA)
               wv[x2] = bf2_mul(pack2<T>(sv.x, sv.y), dap[8 * c + x2]);
             } else {
               const float2 w = fmul2(sv, bf2_unpack(dap[8 * c + x2]));
@@ -953,17 +993,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(1, 256);
     if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
       tc_fence_after();
-      constexpr int HD = D / 2, HV = DV / 2;
+      // column halves of dK: D / 2 each, or 80 + 64 for the kGramFP = 144 Gram columns
+      constexpr int HD0 = GRAM ? 80 : D / 2, HV = DV / 2;
       const size_t rowkv = (static_cast<size_t>(b) * T_ + sg) * p.H + h;
-      T* dkrow = static_cast<T*>(p.dk) + rowkv * D + hc * HD;
+      T* dkrow = static_cast<T*>(p.dk) + rowkv * D;
       T* dvrow = static_cast<T*>(p.dv) + rowkv * DV + hc * HV;
+      const int cbeg = hc ? HD0 : 0, cend = hc ? D : HD0;
 #pragma unroll
-      for (int c0 = 0; c0 < HD; c0 += 16) {
+      for (int c0 = cbeg; c0 < cend; c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(lane_addr + kColDK + hc * HD + c0, r);
+        tmem_ld16(lane_addr + kColDK + c0, r);
         tmem_wait_ld();
-        if (live) {  // dK = 2 * (sum of W''^T Q)
-          const auto f = [&](int i) { return 2.f * __uint_as_float(r[i]); };
+        if (live) {  // dK = 2 * (sum of W''^T Q); Gram: the sum itself
+          const auto f = [&](int i) { return (GRAM ? 1.f : 2.f) * __uint_as_float(r[i]); };
 #pragma unroll
           for (int v2 = 0; v2 < 2; ++v2) {
             uint4 w;
@@ -1002,10 +1044,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ================================================================================================
 // host side
 // ================================================================================================
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM = false>
 int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   constexpr int E = D / M;
-  constexpr int CW = BoxW<E>::value;
+  constexpr int CW = ScoreBoxW<E, GRAM>::value;
   constexpr int VCW = BoxW<DV>::value;
   using L = BwdSmem<D, DV>;
   CUtensorMap tq, tk, tv, to;
@@ -1022,7 +1064,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   }
   if (p.phases != 2) {
     // dq pass: tensor-memory ring with two issuers (decay: dc row sums written here)
-    auto kern = attn_bwd_dq_ring_tc<T, D, DV, M, SUM, DECAY>;
+    auto kern = attn_bwd_dq_ring_tc<T, D, DV, M, SUM, DECAY, GRAM>;
     const size_t smem = L::dqr_total(DECAY) + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
@@ -1032,7 +1074,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   }
   if (p.phases != 1) {
     // dk/dv pass: tensor-memory ring (decay: dc column sums added here)
-    auto kern = attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM, DECAY>;
+    auto kern = attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM, DECAY, GRAM>;
     const size_t smem = L::kr_total(DECAY);  // no static shared memory: no alignment slack
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
@@ -1097,6 +1139,13 @@ bool tc_bwd_supported(int dtype, int D, int Dv, int M, bool sum) {
 int tc_attn_bwd(const AttnBwdParams& p, int dtype, bool sum, cudaStream_t st) {
   if (!tc_bwd_supported(dtype, p.D, p.Dv, p.M, sum)) return KATA_ERR_UNSUPPORTED;
   return dtype == KATA_DTYPE_BF16 ? bwd_dims<__nv_bfloat16>(p, sum, st) : bwd_dims<__half>(p, sum, st);
+}
+
+// Linear-score backward over bf16 Gram features: p.q, p.k hold phi (kGramFP columns), p.dq, p.dk
+// receive d phi (bf16, kGramFP columns), p.D = kGramFP, p.M = 1, p.scale = 1.
+int tc_attn_bwd_gram(const AttnBwdParams& p, cudaStream_t st) {
+  if (p.D != kGramFP || p.M != 1 || p.Dv != 64 || p.c) return KATA_ERR_UNSUPPORTED;
+  return launch_bwd<__nv_bfloat16, kGramFP, 64, 1, false, false, true>(p, st);
 }
 
 }  // namespace kata

@@ -27,11 +27,11 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int g, int E, int
 
 // Descriptor increment (in 16-byte units, added to the start-address field) from K-step 0 to K-step
 // kk of a K-major operand stored as boxes of CW columns: 16 elements = 32 bytes per step, and a new
-// box every 64 elements.  Compile-time after unrolling; the start address never carries out of
+// box every CW elements.  Compile-time after unrolling; the start address never carries out of
 // its 14-bit field because shared-memory addresses are below 256 KB.
 template <int CW>
 __device__ __forceinline__ constexpr uint64_t kstep(int kk) {
-  return static_cast<uint64_t>(((kk >> 2) * (kTile * CW * 2) + (kk & 3) * 32) >> 4);
+  return static_cast<uint64_t>(((kk * 16 / CW) * (kTile * CW * 2) + (kk * 16 % CW) * 2) >> 4);
 }
 // Same for an MN-major operand: each K-step is 16 rows of CW*2 bytes.
 template <int CW>
@@ -102,6 +102,21 @@ inline int make_tm_tokens(CUtensorMap* tm, const void* base, int B, int T, int h
 template <int W>
 struct BoxW {
   static constexpr int value = W < 64 ? W : 64;
+};
+
+// Sum score on Gram features.  With groups of E = 16 (D = 16 M) the sum score is a linear score
+//   A[t,s] = scale^2 sum_{a,b} (q_a . k_b)^2 = scale^2 <G(q_t), G(k_s)>_F = <phi(q_t), phi(k_s)>,
+//   G(x) = sum_a x_a x_a^T (16 x 16, symmetric),  phi(x)_(e,f) = scale c_ef G(x)_ef  (e <= f,
+//   c_ee = 1, c_ef = sqrt 2),
+// over kGramF = 136 features, stored as kGramFP = 144 columns (zero-padded to a whole number of
+// 16-column MMA K-steps).  The tensor-core kernels run it as M = 1 with D = kGramFP, no squaring
+// (GRAM), and the feature tiles in 32-byte-swizzled boxes of 16 columns.
+constexpr int kGramE = 16;
+constexpr int kGramF = kGramE * (kGramE + 1) / 2;
+constexpr int kGramFP = 144;
+template <int E, bool GRAM>
+struct ScoreBoxW {
+  static constexpr int value = GRAM ? 16 : BoxW<E>::value;
 };
 
 }  // namespace kata

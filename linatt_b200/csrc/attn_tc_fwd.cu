@@ -59,17 +59,18 @@ struct FwdBarriers {
   alignas(16) float den_x[2][kBT];  // partial row sums of the two column halves (decay: c staging)
 };
 
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
   constexpr int E = D / M;
-  constexpr int CW = E < 64 ? E : 64;  // group box width (elements); swizzle = 2*CW bytes
+  constexpr int CW = ScoreBoxW<E, GRAM>::value;  // group box width (elements); swizzle = 2*CW bytes
   constexpr int NBOX = D / CW;
   constexpr int VCW = DV < 64 ? DV : 64;
   constexpr int NVBOX = DV / VCW;
   constexpr int NP = SUM ? M * M : M;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  static_assert(!GRAM || (M == 1 && !SUM && !DECAY), "Gram features: one linear score part");
   using L = FwdSmem<D, DV>;
 
   extern __shared__ uint8_t smem_raw[];
@@ -288,12 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
-          acc[i] = pp == 0 ? fmul2(x0, x0) : ffma2(x0, x0, acc[i]);
+          acc[i] = GRAM ? x0 : pp == 0 ? fmul2(x0, x0) : ffma2(x0, x0, acc[i]);  // Gram: A = S
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x1 = make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
-          acc[16 + i] = pp == 0 ? fmul2(x1, x1) : ffma2(x1, x1, acc[16 + i]);
+          acc[16 + i] = GRAM ? x1 : pp == 0 ? fmul2(x1, x1) : ffma2(x1, x1, acc[16 + i]);
         }
       }
       if (!ok) break;
@@ -412,10 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tbase, 512);
 }
 
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM = false>
 int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
   constexpr int E = D / M;
-  constexpr int CW = E < 64 ? E : 64;
+  constexpr int CW = ScoreBoxW<E, GRAM>::value;
   constexpr int VCW = DV < 64 ? DV : 64;
   CUtensorMap tq, tk, tv;
   int e = make_tm_tokens(&tq, p.q, p.B, p.T, p.HQ, D, CW);
@@ -423,7 +424,7 @@ int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
   if (!e) e = make_tm_tokens(&tv, p.v, p.B, p.T, p.H, DV, VCW);
   if (e) return e;
   const size_t smem = FwdSmem<D, DV>::TOTAL + 1024;
-  auto kern = attn_fwd_tc<T, D, DV, M, SUM, DECAY>;
+  auto kern = attn_fwd_tc<T, D, DV, M, SUM, DECAY, GRAM>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return KATA_ERR_CUDA;
   const dim3 grid((p.T + kBT - 1) / kBT, p.B * p.HQ);
@@ -483,6 +484,13 @@ bool tc_fwd_supports_decay(bool sum) { return !sum; }
 int tc_attn_fwd(const AttnFwdParams& p, int dtype, bool sum, cudaStream_t st) {
   if (!tc_fwd_supported(dtype, p.D, p.Dv, p.M, sum)) return KATA_ERR_UNSUPPORTED;
   return dtype == KATA_DTYPE_BF16 ? dispatch_dims<__nv_bfloat16>(p, sum, st) : dispatch_dims<__half>(p, sum, st);
+}
+
+// Linear-score forward over bf16 Gram features: p.q, p.k hold phi (kGramFP columns), p.D = kGramFP,
+// p.M = 1, p.scale = 1 (the scale is inside the features).
+int tc_attn_fwd_gram(const AttnFwdParams& p, cudaStream_t st) {
+  if (p.D != kGramFP || p.M != 1 || p.Dv != 64 || p.c) return KATA_ERR_UNSUPPORTED;
+  return launch_fwd<__nv_bfloat16, kGramFP, 64, 1, false, false, true>(p, st);
 }
 
 }  // namespace kata

@@ -1,6 +1,8 @@
 // capi_attn.cu -- C-ABI entry points for causal KATA-SPD attention: argument validation and
-// dispatch between the tcgen05 tensor-core kernels and the fp32-exact SIMT kernels.
+// dispatch between the tcgen05 tensor-core kernels (parts form, or the sum score on Gram features)
+// and the fp32-exact SIMT kernels.
 #include "attn_common.cuh"
+#include "attn_gram.h"
 #include "attn_internal.h"
 #include "host_util.h"
 
@@ -30,7 +32,14 @@ int check_common(int dtype, int B, int T, int H, int HQ, int D, int Dv, int M, i
   return KATA_OK;
 }
 
-// Chooses the kernel family: 1 = tensor cores, 2 = SIMT, or a negative error.
+size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Gram form wanted for these arguments (AUTO or TC_GRAM on a problem it covers)
+bool gram_wanted(int algo, int dtype, int D, int Dv, int M, int score, bool decay) {
+  return (algo == KATA_ALGO_AUTO || algo == KATA_ALGO_TC_GRAM) && gram_supported(dtype, D, Dv, M, score, decay);
+}
+
+// Chooses the kernel family of the parts form: 1 = tensor cores, 2 = SIMT, or a negative error.
 int choose_algo(int algo, bool tc_ok, bool simt_ok, int dtype) {
   if (algo == KATA_ALGO_TC) return tc_ok ? 1 : KATA_ERR_UNSUPPORTED;
   if (algo == KATA_ALGO_SIMT) return simt_ok ? 2 : KATA_ERR_UNSUPPORTED;
@@ -41,19 +50,38 @@ int choose_algo(int algo, bool tc_ok, bool simt_ok, int dtype) {
 
 }  // namespace
 
+extern "C" size_t kata_attn_fwd_workspace_bytes(const kata_attn_fwd_args* a) {
+  if (!a || check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score)) return 0;
+  if (!gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr)) return 0;
+  return gram_fwd_workspace_bytes(a->B, a->T, a->H, a->HQ);
+}
+
 extern "C" int kata_attn_fwd(const kata_attn_fwd_args* a, kata_stream_t stream) {
   if (!a) return KATA_ERR_INVALID;
   int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
   if (e) return e;
   if (!a->q || !a->k || !a->v || !a->o || !a->den) return KATA_ERR_INVALID;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return KATA_ERR_ALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr)) {
+    const size_t need = gram_fwd_workspace_bytes(a->B, a->T, a->H, a->HQ);
+    const bool have = a->workspace && a->workspace_bytes >= need;
+    if (a->algo == KATA_ALGO_TC_GRAM && !have) return KATA_ERR_WORKSPACE;
+    if (have) {
+      if (!aligned16(a->workspace)) return KATA_ERR_ALIGN;
+      AttnFwdParams p{a->q, a->k, a->v, a->c, a->o, a->den, a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
+                      a->HQ / a->H, a->scale};
+      return gram_attn_fwd(p, a->workspace, st);
+    }
+  } else if (a->algo == KATA_ALGO_TC_GRAM) {
+    return KATA_ERR_UNSUPPORTED;
+  }
   const bool sum = a->score == KATA_SCORE_SUM;
   const bool tc_ok = tc_fwd_supported(a->dtype, a->D, a->Dv, a->M, sum) && !(a->c && sum);
   const int alg = choose_algo(a->algo, tc_ok, simt_supported(a->D, a->Dv, a->M, sum), a->dtype);
   if (alg < 0) return alg;
   AttnFwdParams p{a->q, a->k, a->v, a->c, a->o, a->den, a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
                   a->HQ / a->H, a->scale};
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return alg == 1 ? tc_attn_fwd(p, a->dtype, sum, st) : simt_attn_fwd(p, a->dtype, sum, st);
 }
 
@@ -61,6 +89,8 @@ extern "C" int kata_attn_algo(const kata_attn_fwd_args* a) {
   if (!a) return KATA_ERR_INVALID;
   int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
   if (e) return e;
+  if (gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr)) return KATA_ALGO_TC_GRAM;
+  if (a->algo == KATA_ALGO_TC_GRAM) return KATA_ERR_UNSUPPORTED;
   const bool sum = a->score == KATA_SCORE_SUM;
   const bool tc_ok = tc_fwd_supported(a->dtype, a->D, a->Dv, a->M, sum) &&
                      tc_bwd_supported(a->dtype, a->D, a->Dv, a->M, sum) && !(a->c && sum);
@@ -69,12 +99,23 @@ extern "C" int kata_attn_algo(const kata_attn_fwd_args* a) {
   return alg == 1 ? KATA_ALGO_TC : KATA_ALGO_SIMT;
 }
 
-extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
+size_t kata::attn_bwd_min_workspace_bytes(const kata_attn_bwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->HQ < 1) return 0;
   // fp32 delta = <o, dO> per (b, t, hq), plus 1/den and delta/den in a padded head-major layout
   // for the tensor-core key-tile kernel, and with decay (c given) a head-major copy of c (the SIMT
-  // kernels use the first part only)
-  return tc_bwd_workspace_bytes(a->B, a->T, a->HQ, a->c != nullptr);
+  // kernels use the first part only); TC_GRAM adds the features and their gradients
+  const size_t base = tc_bwd_workspace_bytes(a->B, a->T, a->HQ, a->c != nullptr);
+  if (a->algo != KATA_ALGO_TC_GRAM || a->H < 1) return base;
+  return al256(base) + gram_bwd_workspace_bytes(a->B, a->T, a->H, a->HQ);
+}
+
+extern "C" size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* a) {
+  if (!a || a->B < 1 || a->T < 1 || a->HQ < 1) return 0;
+  const size_t base = tc_bwd_workspace_bytes(a->B, a->T, a->HQ, a->c != nullptr);
+  if (a->H < 1 || check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score) ||
+      !gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr))
+    return base;
+  return al256(base) + gram_bwd_workspace_bytes(a->B, a->T, a->H, a->HQ);
 }
 
 int kata::attn_bwd_impl(const kata_attn_bwd_args* a, const float* delta_in, kata_stream_t stream) {
@@ -87,17 +128,28 @@ int kata::attn_bwd_impl(const kata_attn_bwd_args* a, const float* delta_in, kata
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) || !aligned16(a->dout) ||
       !aligned16(a->dq) || !aligned16(a->dk) || !aligned16(a->dv))
     return KATA_ERR_ALIGN;
-  const size_t need = kata_attn_bwd_workspace_bytes(a);
-  if (need && (!a->workspace || a->workspace_bytes < need)) return KATA_ERR_WORKSPACE;
+  if (a->phases < 0 || a->phases > 2) return KATA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  AttnBwdParams p{a->q,  a->k,  a->v,  a->o,  a->den, a->dout, a->c,  a->dq, a->dk,           a->dv,
+                  a->dc, static_cast<float*>(a->workspace), a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
+                  a->HQ / a->H, a->scale, a->phases, delta_in};
+  const size_t base = tc_bwd_workspace_bytes(a->B, a->T, a->HQ, a->c != nullptr);
+  if (gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr)) {
+    const size_t need = al256(base) + gram_bwd_workspace_bytes(a->B, a->T, a->H, a->HQ);
+    const bool have = a->workspace && a->workspace_bytes >= need;
+    if (a->algo == KATA_ALGO_TC_GRAM && !have) return KATA_ERR_WORKSPACE;
+    if (have) {
+      if (!aligned16(a->workspace)) return KATA_ERR_ALIGN;
+      return gram_attn_bwd(p, static_cast<uint8_t*>(a->workspace) + al256(base), st);
+    }
+  } else if (a->algo == KATA_ALGO_TC_GRAM) {
+    return KATA_ERR_UNSUPPORTED;
+  }
+  if (base && (!a->workspace || a->workspace_bytes < base)) return KATA_ERR_WORKSPACE;
   const bool sum = a->score == KATA_SCORE_SUM;
   const bool tc_ok = tc_bwd_supported(a->dtype, a->D, a->Dv, a->M, sum) && !(a->c && sum);
   const int alg = choose_algo(a->algo, tc_ok, simt_supported(a->D, a->Dv, a->M, sum), a->dtype);
   if (alg < 0) return alg;
-  AttnBwdParams p{a->q,  a->k,  a->v,  a->o,  a->den, a->dout, a->c,  a->dq, a->dk,           a->dv,
-                  a->dc, static_cast<float*>(a->workspace), a->status, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M,
-                  a->HQ / a->H, a->scale, a->phases, delta_in};
-  if (a->phases < 0 || a->phases > 2) return KATA_ERR_INVALID;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return alg == 1 ? tc_attn_bwd(p, a->dtype, sum, st) : simt_attn_bwd(p, a->dtype, sum, st);
 }
 

@@ -10,7 +10,8 @@
 //
 // Properties a caller must know:
 //  * capacity: kNoAllocScratchBytes (16 MiB) per device; larger problems are rejected with
-//    KATA_ERR_SCRATCH_LIMIT (kata_attn_bwd_workspace_bytes() tells the requirement);
+//    KATA_ERR_SCRATCH_LIMIT (kata_attn_bwd_workspace_bytes() with algo TC or SIMT tells the
+//    requirement; with AUTO, the Gram form of the sum score runs when its larger workspace fits);
 //  * the array lives until the process exits, on every device that loads this library;
 //  * set-up: the first call on a device resolves the array's device address for that device
 //    (cudaGetSymbolAddress, with that device current); make that first call outside any stream
@@ -30,6 +31,7 @@
 #include <mutex>
 
 #include "attn_common.cuh"
+#include "attn_internal.h"
 #include "host_util.h"
 
 namespace kata {
@@ -66,7 +68,8 @@ int scratch_address(void** out) {
 extern "C" int kata_attn_bwd_noalloc(const kata_attn_bwd_args* args, kata_stream_t stream) {
   if (!args) return KATA_ERR_INVALID;
   if (args->phases != 0) return KATA_ERR_INVALID;
-  const size_t need = kata_attn_bwd_workspace_bytes(args);
+  // AUTO runs the Gram form of the sum score only when it fits in the array, the parts form otherwise
+  const size_t need = kata::attn_bwd_min_workspace_bytes(args);
   if (need > kata::kNoAllocScratchBytes) return KATA_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   const int e = kata::scratch_address(&scratch);

@@ -951,10 +951,27 @@ int check(int dtype, int B, int T, int H, int D, int Dv, int M) {
 size_t esz(int dtype) { return dtype == KATA_DTYPE_F32 ? 4 : 2; }
 
 // ---- workspace layouts (byte offsets, 256-aligned) ------------------------------------------------
+// Workspace the readout / den attention forward (sum score) can use: the Gram features of q and k
+// when that form applies (bf16, groups of 16), else 0.  dv = Dv for the readout, D for den alone.
+size_t attn_fwd_ws_bytes(int dtype, int B, int T, int H, int D, int dv, int M) {
+  kata_attn_fwd_args f{};
+  f.dtype = dtype;
+  f.B = B;
+  f.T = T;
+  f.H = H;
+  f.HQ = H;
+  f.D = D;
+  f.Dv = dv;
+  f.M = M;
+  f.score = KATA_SCORE_SUM;
+  f.algo = KATA_ALGO_AUTO;
+  return kata_attn_fwd_workspace_bytes(&f);
+}
+
 struct FwdWs {
-  size_t Tm, Lm, Ub, oa, E, zv, total;
+  size_t Tm, Lm, Ub, oa, E, zv, attn, attn_bytes, total;
 };
-FwdWs fwd_ws(int dtype, int B, int T, int H, int D, int Dv) {
+FwdWs fwd_ws(int dtype, int B, int T, int H, int D, int Dv, int M) {
   const size_t rows = static_cast<size_t>(B) * T * H;
   FwdWs w{};
   size_t o = 0;
@@ -964,6 +981,9 @@ FwdWs fwd_ws(int dtype, int B, int T, int H, int D, int Dv) {
   w.oa = o; o += al256(rows * (Dv > D ? Dv : D) * esz(dtype));
   w.E = o; o += al256(rows * Dv * 4);
   w.zv = o; o += al256(rows * D * esz(dtype));
+  const size_t a1 = attn_fwd_ws_bytes(dtype, B, T, H, D, Dv, M), a2 = attn_fwd_ws_bytes(dtype, B, T, H, D, D, M);
+  w.attn_bytes = a1 > a2 ? a1 : a2;
+  w.attn = o; o += al256(w.attn_bytes);
   w.total = o;
   return w;
 }
@@ -998,11 +1018,20 @@ BwdWs2 bwd_ws(int dtype, int B, int T, int H, int D, int Dv, size_t attn_bytes) 
   return w;
 }
 
-size_t attn_ws_bytes(int B, int T, int H) {
+// Workspace of the two attention backward calls (sum score; includes the Gram features and their
+// gradients when that form applies)
+size_t attn_ws_bytes(int dtype, int B, int T, int H, int D, int Dv, int M) {
   kata_attn_bwd_args a{};
+  a.dtype = dtype;
   a.B = B;
   a.T = T;
+  a.H = H;
   a.HQ = H;
+  a.D = D;
+  a.Dv = Dv;
+  a.M = M;
+  a.score = KATA_SCORE_SUM;
+  a.algo = KATA_ALGO_AUTO;
   return kata_attn_bwd_workspace_bytes(&a);
 }
 
@@ -1019,7 +1048,7 @@ int cvt(const void* in, bool in_f32, void* out, const float* neg_rowscale, long 
 
 template <typename T>
 int fwd_typed(const kata_delta_fwd_args* a, cudaStream_t st) {
-  const FwdWs w = fwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv);
+  const FwdWs w = fwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv, a->M);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   const long rows = static_cast<long>(a->B) * a->T * a->H;
   DP p{};
@@ -1073,6 +1102,8 @@ int fwd_typed(const kata_delta_fwd_args* a, cudaStream_t st) {
   f.score = KATA_SCORE_SUM;
   f.algo = KATA_ALGO_AUTO;
   f.scale = a->scale;
+  f.workspace = w.attn_bytes ? ws + w.attn : nullptr;
+  f.workspace_bytes = w.attn_bytes;
   e = kata_attn_fwd(&f, reinterpret_cast<kata_stream_t>(st));
   if (e || den_only || !a->o) return e;
   delta_readout_finish_kernel<T><<<warp_blocks(rows), NT, 0, st>>>(static_cast<const T*>(f.o), den, a->o, rows, a->Dv,
@@ -1082,7 +1113,7 @@ int fwd_typed(const kata_delta_fwd_args* a, cudaStream_t st) {
 
 template <typename T>
 int bwd_typed(const kata_delta_bwd_args* a, cudaStream_t st) {
-  const size_t attn_bytes = attn_ws_bytes(a->B, a->T, a->H);
+  const size_t attn_bytes = attn_ws_bytes(a->dtype, a->B, a->T, a->H, a->D, a->Dv, a->M);
   const BwdWs2 w = bwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv, attn_bytes);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   auto F32 = [&](size_t off) { return reinterpret_cast<float*>(ws + off); };
@@ -1172,7 +1203,7 @@ using namespace kata;
 
 extern "C" size_t kata_delta_fwd_workspace_bytes(const kata_delta_fwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->H < 1 || a->D < 1 || a->Dv < 1) return 0;
-  return fwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv).total;
+  return fwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv, a->M).total;
 }
 
 extern "C" int kata_delta_fwd(const kata_delta_fwd_args* a, kata_stream_t stream) {
@@ -1195,7 +1226,8 @@ extern "C" int kata_delta_fwd(const kata_delta_fwd_args* a, kata_stream_t stream
 
 extern "C" size_t kata_delta_bwd_workspace_bytes(const kata_delta_bwd_args* a) {
   if (!a || a->B < 1 || a->T < 1 || a->H < 1 || a->D < 1 || a->Dv < 1) return 0;
-  return bwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv, attn_ws_bytes(a->B, a->T, a->H)).total;
+  return bwd_ws(a->dtype, a->B, a->T, a->H, a->D, a->Dv,
+                attn_ws_bytes(a->dtype, a->B, a->T, a->H, a->D, a->Dv, a->M)).total;
 }
 
 extern "C" int kata_delta_bwd(const kata_delta_bwd_args* a, kata_stream_t stream) {

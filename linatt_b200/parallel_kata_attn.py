@@ -44,8 +44,9 @@ __all__ = [
     "parallel_kata_attn_sum_bwd_triton_M2",
 ]
 
-# Kernel family used by every call of this module ("auto" | "tc" | "simt").  Tests and the bench
-# switch it to exercise one family explicitly; "auto" is the production setting.
+# Kernel family used by every call of this module ("auto" | "tc" | "simt" | "tc_gram").  Tests and
+# the bench switch it to exercise one family explicitly; "auto" is the production setting (it runs
+# the sum score with groups of 16 on Gram features, "tc_gram", and everything else as "tc" / "simt").
 ALGO = "auto"
 
 
@@ -113,8 +114,12 @@ def _fwd(q, k, v, num_groups, scale, score, c=None):
         status=st.data_ptr(), dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HQ=HQ, D=d_k, Dv=d_v, M=num_groups,
         score=_lib.SCORE[score], algo=_lib.ALGO[ALGO], scale=float(scale))
     _warn_if_simt(a, dt)
+    L = _lib.lib()
+    nbytes = L.kata_attn_fwd_workspace_bytes(a)  # Gram features of the sum score, else 0
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
+    a.workspace, a.workspace_bytes = _lib.ptr(ws), nbytes
     with torch.cuda.device(dev):
-        _lib.check(_lib.lib().kata_attn_fwd(a, _lib.stream_handle(dev)), "kata_attn_fwd")
+        _lib.check(L.kata_attn_fwd(a, _lib.stream_handle(dev)), "kata_attn_fwd")
     if _lib.SYNC_CHECK:
         _lib.check_device_status(dev)
     if o.dtype != v.dtype:

@@ -88,6 +88,38 @@ def test_algo_query_reports_the_kernel_family(L):
     assert algo(M=3) == -3
 
 
+def test_gram_form_host_logic(L):
+    """The sum score with groups of 16 (bf16, Dv = 64) runs on Gram features: algo query, workspace
+    sizes (bf16 features of q and k; the backward adds their gradients after the parts-form arrays)
+    and the refusals of a forced TC_GRAM outside its envelope or without its workspace."""
+    from linatt_b200 import _lib
+
+    kw = dict(dtype=1, B=2, T=8, H=1, HQ=2, D=64, Dv=64, M=4, score=1, algo=0, scale=1.0)
+    al = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    phi = al(2 * 8 * 2 * 144 * 2) + al(2 * 8 * 1 * 144 * 2)
+    a = _lib.AttnFwdArgs(**kw)
+    assert L.kata_attn_algo(a) == 3
+    assert L.kata_attn_fwd_workspace_bytes(a) == phi
+    assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "D": 128, "M": 8})) == 3  # groups of 16 at D = 128
+    for other in (dict(score=0), dict(dtype=2), dict(M=2), dict(Dv=128), dict(algo=1), dict(algo=2)):
+        b = _lib.AttnFwdArgs(**{**kw, **other})
+        assert L.kata_attn_fwd_workspace_bytes(b) == 0, other
+        assert L.kata_attn_algo(b) != 3, other
+    assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "score": 0, "algo": 3})) == -8
+    a = _lib.AttnFwdArgs(q=16, k=16, v=16, o=16, den=16, **{**kw, "algo": 3})
+    assert L.kata_attn_fwd(a, None) == -5  # TC_GRAM without its workspace
+    a = _lib.AttnFwdArgs(q=16, k=16, v=16, o=16, den=16, **{**kw, "algo": 3, "score": 0})
+    assert L.kata_attn_fwd(a, None) == -8  # TC_GRAM on the concat score
+    base = 4 * (2 * 8 * 2 + 2 * 2 * 2 * 128)
+    b = _lib.AttnBwdArgs(**kw)
+    assert L.kata_attn_bwd_workspace_bytes(b) == al(base) + 2 * phi
+    b.algo = 1
+    assert L.kata_attn_bwd_workspace_bytes(b) == base
+    b = _lib.AttnBwdArgs(q=16, k=16, v=16, o=16, den=16, dout=16, dq=16, dk=16, dv=16, **{**kw, "algo": 3})
+    b.workspace, b.workspace_bytes = 256, base  # the parts-form size is not enough for TC_GRAM
+    assert L.kata_attn_bwd(b, None) == -5
+
+
 def test_bf16_outside_the_envelope_warns_once(monkeypatch):
     import linatt_b200.parallel_kata_attn as pka
     from linatt_b200 import _lib

@@ -24,6 +24,11 @@ CASES = [
     (128, 128, 0, 0, 128, 128, 1),
     (128, 64, 0, 1, 128, 128, 1),
     (32, 128, 0, 1, 128, 64, 1),
+    # Gram-feature operands (32-byte swizzle, boxes of 16 columns): the K = 144 score product and
+    # the N = 144 gradient chain with its A operand in tensor memory
+    (128, 144, 0, 0, 32, 32, 0),
+    (144, 128, 0, 1, 128, 32, 1),
+    (144, 128, 0, 1, 128, 32, 0),
 ]
 
 
