@@ -920,11 +920,13 @@ def run_delta(args, rank: int, world: int, local: int) -> None:
         return
     peak, src = load_peaks()
     step_ms = ms / args.steps
-    # attention-kernel work of the step (sum score, M*M = 16 parts of E = 16, i.e. 2 GEMM-eq of
-    # K = 256 per pair): readout (S + PV) and two backward calls (S recompute, dN, dQ, dK, dV each),
-    # counted as GEMM-equivalents 2*P*D per (b,h) like the attention bench; scans excluded
-    gemm_eq = Bd * Hd * 2.0 * pairs(Td) * Dd
-    flops = (2 + 2 * 5) * gemm_eq * (Md * Md * (Dd // Md)) / Dd
+    # attention-kernel MMA work of the step: the sum score with groups of 16 runs on 144 Gram-feature
+    # columns (F), v and dO have Dv = Dd columns.  Per causal (t, s) pair and (b, h), 2 FLOPs per
+    # column of each product: readout S (F) + PV (Dv); each of the two backward calls dN (Dv) and
+    # d phi(q) (F) in the dq pass, S^T (F), dN^T (Dv), d phi(k) (F), dV (Dv) in the dk/dv pass
+    F = 144
+    cols = (F + Dd) + 2 * ((Dd + F) + (F + Dd + F + Dd))
+    flops = Bd * Hd * 2.0 * pairs(Td) * cols
     line = {
         "metric": "SPD delta rule fwd+bwd tokens/s/GPU at B8·T2048·H12·D64, M=4 (mixer geometry)",
         "value": world * Bd * Td / (step_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -935,7 +937,8 @@ def run_delta(args, rank: int, world: int, local: int) -> None:
                    "l2": "4 rotating input sets of 151 MB"},
         "roofline": {"bound": "tensor", "achieved": flops / (step_ms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": flops / (step_ms / 1e3) / 1e12 / peak, "traffic": None, "peak_source": src,
-                     "note": "attention-kernel GEMM work only (the O(T) scans are not counted)"},
+                     "note": "attention-kernel MMA work only, sum score on 144 Gram-feature columns (the O(T) scans "
+                             "and the feature maps are not counted)"},
         "clocks": clk, "gpu_launches": None,
     }
     print(json.dumps(line), flush=True)

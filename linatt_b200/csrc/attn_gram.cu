@@ -24,10 +24,7 @@ int tc_attn_bwd_gram(const AttnBwdParams& p, cudaStream_t st);
 namespace {
 
 constexpr float kSqrt2 = 1.4142135623730951f;
-constexpr int kPhiRows = 16;                      // rows per block of the feature map
-constexpr int kPhiChunks = kGramFP / 8;           // 18 chunks of 8 features per row
-constexpr int kPhiThreads = kPhiRows * kPhiChunks;  // 288
-constexpr int kMaxD = 128;
+constexpr int kPhiThreads = 128;
 
 struct PhiJob {
   const __nv_bfloat16* x;  // (rows, D)
@@ -35,25 +32,13 @@ struct PhiJob {
   long long rows;
 };
 
-// Feature index f (e-major over e <= g) -> (e, g); 255 marks the zero padding past kGramF.
-__device__ __forceinline__ void gram_pair(int f, unsigned char& e_out, unsigned char& g_out) {
-  if (f >= kGramF) {
-    e_out = g_out = 255;
-    return;
-  }
-  int e = 0;
-  while (f >= kGramE - e) {
-    f -= kGramE - e;
-    ++e;
-  }
-  e_out = static_cast<unsigned char>(e);
-  g_out = static_cast<unsigned char>(e + f);
-}
-
-__device__ __forceinline__ void unpack8(uint4 u, float (&v)[8]) {
-  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+__device__ __forceinline__ void unpack8(uint4 u, float* v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(h[i]);
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
 }
 __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   uint4 u;
@@ -64,42 +49,38 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return u;
 }
 
-// phi for up to two row sets (blockIdx.y), 16 rows per block: the rows are staged in shared memory,
-// then thread (row, chunk) forms 8 features (M products each) and stores them as one 16-byte vector,
-// so consecutive threads write consecutive 16 bytes of the (rows, 144) output.
-__global__ void __launch_bounds__(kPhiThreads) gram_phi_kernel(PhiJob j0, PhiJob j1, int D, float scale) {
+// Feature index of (e, g), e <= g, e-major over the upper triangle of the 16 x 16 Gram matrix.
+__host__ __device__ constexpr int gram_index(int e, int g) { return e * kGramE - e * (e - 1) / 2 + (g - e); }
+
+// phi for up to two row sets (blockIdx.y): one thread per row, the row's D values in registers and
+// the 136 features formed with compile-time indices (fully unrolled, M products each), stored as
+// 17 16-byte vectors plus one of zero padding.  HBM-bound: 2 D bytes read, 288 written per row.
+template <int M>
+__global__ void __launch_bounds__(kPhiThreads) gram_phi_kernel(PhiJob j0, PhiJob j1, float scale) {
+  constexpr int D = kGramE * M;
   const PhiJob j = blockIdx.y ? j1 : j0;
-  __shared__ float xs[kPhiRows][kMaxD + 1];
-  __shared__ unsigned char pe[kGramFP], pg[kGramFP];
-  const int tid = threadIdx.x;
-  if (tid < kGramFP) gram_pair(tid, pe[tid], pg[tid]);
-  const long long r0 = static_cast<long long>(blockIdx.x) * kPhiRows;
-  if (r0 >= j.rows) return;  // uniform over the block
-  const int nv = D / 8;
-  for (int i = tid; i < kPhiRows * nv; i += kPhiThreads) {
-    const int r = i / nv, c = i % nv;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (r0 + r < j.rows) unpack8(*reinterpret_cast<const uint4*>(j.x + (r0 + r) * D + c * 8), v);
+  const long long row = static_cast<long long>(blockIdx.x) * kPhiThreads + threadIdx.x;
+  if (row >= j.rows) return;
+  float x[D];
+  const uint4* src = reinterpret_cast<const uint4*>(j.x + row * D);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) xs[r][c * 8 + e] = v[e];
-  }
-  __syncthreads();
-  const int r = tid / kPhiChunks, c = tid % kPhiChunks;
-  if (r0 + r >= j.rows) return;
-  const int M = D / kGramE;
+  for (int c = 0; c < D / 8; ++c) unpack8(__ldg(src + c), x + 8 * c);
+  uint4* dst = reinterpret_cast<uint4*>(j.phi + row * kGramFP);
   float out[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int f = c * 8 + i;
-    float s = 0.f;
-    if (pe[f] != 255) {
-      const int e = pe[f], g = pg[f];
-      for (int a = 0; a < M; ++a) s = fmaf(xs[r][a * kGramE + e], xs[r][a * kGramE + g], s);
-      s *= e == g ? scale : scale * kSqrt2;
+  for (int e = 0; e < kGramE; ++e) {
+#pragma unroll
+    for (int g = e; g < kGramE; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int a = 0; a < M; ++a) s = fmaf(x[a * kGramE + e], x[a * kGramE + g], s);
+      const int f = gram_index(e, g);
+      out[f & 7] = s * (e == g ? scale : scale * kSqrt2);
+      if ((f & 7) == 7) dst[f >> 3] = pack8(out);
     }
-    out[i] = s;
   }
-  *reinterpret_cast<uint4*>(j.phi + (r0 + r) * kGramFP + c * 8) = pack8(out);
+  static_assert(kGramF == 17 * 8 && kGramFP == 18 * 8, "136 features in 17 vectors, one of padding");
+  dst[17] = make_uint4(0u, 0u, 0u, 0u);
 }
 
 struct PhiBwdJob {
@@ -109,60 +90,55 @@ struct PhiBwdJob {
   long long rows;
 };
 
-constexpr int kPbThreads = 256;
+// bf16 value i of a row held as packed pairs
+__device__ __forceinline__ float bf_at(const uint32_t* w, int i) {
+  return __uint_as_float((i & 1) ? (w[i >> 1] & 0xffff0000u) : (w[i >> 1] << 16));
+}
 
-// dx for up to two row sets (blockIdx.y): 256 / (D / 8) rows per block staged in shared memory
-// (d phi and x as fp32); thread (row, chunk) forms 8 outputs of one group a, each a 16-term
-// product of a row of scale * Dsym with x_a, and stores them as one 16-byte vector.
-__global__ void __launch_bounds__(kPbThreads) gram_phi_bwd_kernel(PhiBwdJob j0, PhiBwdJob j1, int D, float scale) {
+// dx for up to two row sets (blockIdx.y): one thread per (row, group a), M consecutive threads per
+// row.  dx_a[g] = scale (2 dphi_gg x_a[g] + sqrt 2 sum_{h != g} dphi_(g,h) x_a[h])
+//              = sqrt 2 scale (sum_{h != g} dphi_(g,h) x_a[h] + sqrt 2 dphi_gg x_a[g]),
+// with the row's d phi kept as 68 packed bf16 pairs in registers (compile-time indices).
+template <int M>
+__global__ void __launch_bounds__(kPhiThreads) gram_phi_bwd_kernel(PhiBwdJob j0, PhiBwdJob j1, float scale) {
+  constexpr int D = kGramE * M;
   const PhiBwdJob j = blockIdx.y ? j1 : j0;
-  constexpr int kRowsMax = kPbThreads / 8;  // D = 64
-  __shared__ float ds[kRowsMax][kGramFP + 1];
-  __shared__ float xs[kRowsMax][kMaxD + 1];
-  __shared__ unsigned char gi[kGramE * kGramE];
-  __shared__ float gc[kGramE * kGramE];
-  const int tid = threadIdx.x;
-  {  // (g, h) -> feature index of (min, max) and the coefficient of Dsym (scale folded in)
-    const int g = tid / kGramE, h = tid % kGramE;
-    const int e = g < h ? g : h, f = g < h ? h : g;
-    gi[tid] = static_cast<unsigned char>(e * kGramE - e * (e - 1) / 2 + (f - e));
-    gc[tid] = g == h ? 2.f * scale : kSqrt2 * scale;
+  const long long t = static_cast<long long>(blockIdx.x) * kPhiThreads + threadIdx.x;
+  const long long row = t / M;
+  const int a = static_cast<int>(t % M);
+  if (row >= j.rows) return;
+  uint32_t w[kGramF / 2];
+  const uint4* dsrc = reinterpret_cast<const uint4*>(j.dphi + row * kGramFP);
+#pragma unroll
+  for (int c = 0; c < kGramF / 8; ++c) {
+    const uint4 u = __ldg(dsrc + c);
+    w[4 * c] = u.x;
+    w[4 * c + 1] = u.y;
+    w[4 * c + 2] = u.z;
+    w[4 * c + 3] = u.w;
   }
-  const int cpr = D / 8;  // chunks (threads) per row
-  const int rpb = kPbThreads / cpr;
-  const long long r0 = static_cast<long long>(blockIdx.x) * rpb;
-  if (r0 >= j.rows) return;  // uniform over the block
-  for (int i = tid; i < rpb * kPhiChunks; i += kPbThreads) {
-    const int r = i / kPhiChunks, c = i % kPhiChunks;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (r0 + r < j.rows) unpack8(*reinterpret_cast<const uint4*>(j.dphi + (r0 + r) * kGramFP + c * 8), v);
+  float x[kGramE];
+  const uint4* xsrc = reinterpret_cast<const uint4*>(j.x + row * D + a * kGramE);
+  unpack8(__ldg(xsrc), x);
+  unpack8(__ldg(xsrc + 1), x + 8);
+  const float sc = kSqrt2 * scale;
+  float out[kGramE];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ds[r][c * 8 + e] = v[e];
+  for (int g = 0; g < kGramE; ++g) {
+    float s = kSqrt2 * bf_at(w, gram_index(g, g)) * x[g];
+#pragma unroll
+    for (int h = 0; h < kGramE; ++h)
+      if (h != g) s = fmaf(bf_at(w, h < g ? gram_index(h, g) : gram_index(g, h)), x[h], s);
+    out[g] = s * sc;
   }
-  for (int i = tid; i < rpb * cpr; i += kPbThreads) {
-    const int r = i / cpr, c = i % cpr;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (r0 + r < j.rows) unpack8(*reinterpret_cast<const uint4*>(j.x + (r0 + r) * D + c * 8), v);
+  uint4* dst = reinterpret_cast<uint4*>(j.dx + row * D + a * kGramE);
+  float o8[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) xs[r][c * 8 + e] = v[e];
-  }
-  __syncthreads();
-  const int r = tid / cpr, c = tid % cpr;
-  if (r0 + r >= j.rows) return;
-  const int a = (c * 8) / kGramE, g0 = (c * 8) % kGramE;
-  float xa[kGramE];
+  for (int i = 0; i < 8; ++i) o8[i] = out[i];
+  dst[0] = pack8(o8);
 #pragma unroll
-  for (int h = 0; h < kGramE; ++h) xa[h] = xs[r][a * kGramE + h];
-  float out[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int g = g0 + i;
-    float s = 0.f;
-#pragma unroll
-    for (int h = 0; h < kGramE; ++h) s = fmaf(gc[g * kGramE + h] * ds[r][gi[g * kGramE + h]], xa[h], s);
-    out[i] = s;
-  }
-  *reinterpret_cast<uint4*>(j.dx + (r0 + r) * D + c * 8) = pack8(out);
+  for (int i = 0; i < 8; ++i) o8[i] = out[8 + i];
+  dst[1] = pack8(o8);
 }
 
 size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -170,18 +146,30 @@ size_t phi_bytes(long long rows) { return al256(static_cast<size_t>(rows) * kGra
 
 int launch_phi(PhiJob j0, PhiJob j1, int D, float scale, cudaStream_t st) {
   const long long rmax = j0.rows > j1.rows ? j0.rows : j1.rows;
-  const long long nb = (rmax + kPhiRows - 1) / kPhiRows;
+  const long long nb = (rmax + kPhiThreads - 1) / kPhiThreads;
   if (nb > 0x7fffffffll) return KATA_ERR_SHAPE;
-  gram_phi_kernel<<<dim3(static_cast<unsigned>(nb), j1.rows > 0 ? 2 : 1), kPhiThreads, 0, st>>>(j0, j1, D, scale);
+  const dim3 grid(static_cast<unsigned>(nb), j1.rows > 0 ? 2 : 1);
+  if (D == 64)
+    gram_phi_kernel<4><<<grid, kPhiThreads, 0, st>>>(j0, j1, scale);
+  else if (D == 128)
+    gram_phi_kernel<8><<<grid, kPhiThreads, 0, st>>>(j0, j1, scale);
+  else
+    return KATA_ERR_UNSUPPORTED;
   return from_cuda(cudaGetLastError());
 }
 
 int launch_phi_bwd(PhiBwdJob j0, PhiBwdJob j1, int D, float scale, cudaStream_t st) {
   const long long rmax = j0.rows > j1.rows ? j0.rows : j1.rows;
-  const int rpb = kPbThreads / (D / 8);
-  const long long nb = (rmax + rpb - 1) / rpb;
+  const int M = D / kGramE;
+  const long long nb = (rmax * M + kPhiThreads - 1) / kPhiThreads;
   if (nb > 0x7fffffffll) return KATA_ERR_SHAPE;
-  gram_phi_bwd_kernel<<<dim3(static_cast<unsigned>(nb), j1.rows > 0 ? 2 : 1), kPbThreads, 0, st>>>(j0, j1, D, scale);
+  const dim3 grid(static_cast<unsigned>(nb), j1.rows > 0 ? 2 : 1);
+  if (D == 64)
+    gram_phi_bwd_kernel<4><<<grid, kPhiThreads, 0, st>>>(j0, j1, scale);
+  else if (D == 128)
+    gram_phi_bwd_kernel<8><<<grid, kPhiThreads, 0, st>>>(j0, j1, scale);
+  else
+    return KATA_ERR_UNSUPPORTED;
   return from_cuda(cudaGetLastError());
 }
 

@@ -19,6 +19,7 @@
 //   finalize: dk = sum of the three, dv = beta Y, dbeta = Y.(V - E)
 // The reference computes the same quantities with Triton K14-K21 (kata/spd/flash_delta.py:27-1116);
 // its O(T^2) chunk loops become the O(T) state scans here.
+#include <algorithm>
 #include <cuda_bf16.h>
 #include <type_traits>
 #include <cuda_fp16.h>
@@ -160,6 +161,173 @@ __global__ void __launch_bounds__(NT) delta_prep_kernel(DP p) {
   for (int i = threadIdx.x; i < C * C; i += NT) {
     const int r = i >> 6, c = i & 63, t = c0 + r;
     if (t < p.T) p.Tm[(rowbase + static_cast<size_t>(t) * p.H) * C + c] = sX[r * LDT + c];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// prep on the tensor cores (16-bit keys, E = D / M a multiple of 16, D in {64, 128}): the M^2 part
+// products S_gh = K_g K_h^T of a chunk are M = 64 tcgen05 chains (one K step of 16 per 16 columns of
+// a group) into tensor memory, four parts at a time, each issued twice (lane offsets 0 and 16) so
+// that both lane halves of every warp hold all 64 rows; 8 warps square and sum them, thread (warp
+// w, lane l) owning row 16 (w % 4) + l % 16 and 16 of the 64 columns.  bf16 / fp16 keys are exact
+// in the fp32 accumulators, so kappa matches the CUDA-core form up to summation order.  The unit
+// lower triangular inverse Tm = (I + diag(beta) L)^{-1} is then formed in fp32 by 16 x 16 blocks:
+// the four diagonal blocks by forward substitution (64 threads, one column each), then the blocks
+// at distance d = 1, 2, 3 below the diagonal as X_ij = -X_ii sum_{l=j}^{i-1} B_il X_lj.
+// ------------------------------------------------------------------------------------------------
+constexpr int kPrepThreads = 256;
+constexpr int kPrepParts = 4;  // part accumulators in tensor memory at a time (64 columns each)
+
+struct TcPrepSmem {
+  uint8_t K[2][tc64::TB];  // the chunk's keys, 64 x 128 bytes per 64 columns, 128-byte swizzle
+  float B[C][LDT];         // beta_i kappa(k_i, k_j), j < i
+  float X[C][LDT];         // Tm
+  float R[3][16][17];      // the sums of one distance level
+  float beta[C];
+  uint64_t bar;
+  uint32_t tmem;
+  int abort;
+};
+
+template <typename T, int D, int M>
+__global__ void __launch_bounds__(kPrepThreads) delta_tc_prep_kernel(DP p) {
+  using namespace tc64;
+  constexpr int E = D / M, NP = M * M, NB = (NP + kPrepParts - 1) / kPrepParts;
+  static_assert(E % 16 == 0 && (D == 64 || D == 128), "tensor-core prep geometry");
+  extern __shared__ uint8_t smraw[];
+  TcPrepSmem& sm = *reinterpret_cast<TcPrepSmem*>(align1k(smraw));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = blockIdx.x * C, bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const size_t rowbase = static_cast<size_t>(b) * p.T * p.H + h;  // + t*H
+  const T* kp = static_cast<const T*>(p.k) + rowbase * D;
+  if (tid == 0) {
+    sm.abort = 0;
+    mbar_init(&sm.bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem, 256);
+    tmem_relinquish();
+  }
+  // keys into the swizzled tiles (rows past T zero), beta
+  for (int idx = tid; idx < C * (D / 8); idx += kPrepThreads) {
+    const int r = idx / (D / 8), col = (idx - r * (D / 8)) * 8, t = c0 + r;
+    const bool in = t < p.T;
+    cp_async16(smem_u32(sm.K[col >> 6]) + toff(r, col & 63), kp + static_cast<size_t>(in ? t : c0) * p.H * D + col, in);
+  }
+  cp_async_commit();
+  if (tid < C) sm.beta[tid] = c0 + tid < p.T ? p.beta[rowbase + static_cast<size_t>(c0 + tid) * p.H] : 0.f;
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem;
+  const int qd = warp & 3, chalf = warp >> 2, hl = lane >> 4;
+  const int row = 16 * qd + (lane & 15);
+  const int col0 = 32 * chalf + 16 * hl;  // this thread's 16 columns
+  const uint32_t lane_base = static_cast<uint32_t>(32 * qd) << 16;
+  constexpr uint32_t idesc = umma_idesc_f16(64, 64, is_bf16<T>(), false, false);
+  // K-major descriptor of the 16 columns starting at column c of the key tiles
+  auto kslice = [&](int c) -> uint64_t { return kdesc(sm.K[c >> 6]) + static_cast<uint64_t>(((c & 63) >> 4) * 2); };
+  float kap[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) kap[j] = 0.f;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int nb = 0; nb < NB && ok; ++nb) {
+    if (tid == 0) {
+      tc_fence_after();
+      for (int q = 0; q < kPrepParts && nb * kPrepParts + q < NP; ++q) {
+        const int pp = nb * kPrepParts + q, g = pp / M, hh = pp % M;
+        const uint32_t d = tbase + static_cast<uint32_t>(q * 64);
+#pragma unroll
+        for (int kk = 0; kk < E / 16; ++kk) {
+          const uint64_t ad = kslice(g * E + 16 * kk), bd = kslice(hh * E + 16 * kk);
+          umma_ss(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          umma_ss(d + (16u << 16), ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(&sm.bar);
+    }
+    ok = wait_mma(&sm.bar, phase, &sm.abort);
+    if (!ok) break;
+    for (int q = 0; q < kPrepParts && nb * kPrepParts + q < NP; ++q) {
+      float x[16];
+      ld_quarter(tbase + lane_base + static_cast<uint32_t>(q * 64 + 32 * chalf), hl, x);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) kap[j] = fmaf(x[j], x[j], kap[j]);
+    }
+    tc_fence_before();
+    __syncthreads();  // every part read before the next batch overwrites the accumulators
+  }
+  if (ok) {  // (a timed-out wait leaves Tm and L unwritten, as in the scans)
+    const float sc2 = p.scale * p.scale, bt = sm.beta[row];
+    const int t = c0 + row;
+    float* lrow = p.Lm + (rowbase + static_cast<size_t>(t < p.T ? t : 0) * p.H) * C + col0;
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      float4 lv;
+      float* l = &lv.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = col0 + 4 * j4 + j;
+        l[j] = c < row ? sc2 * kap[4 * j4 + j] : 0.f;
+        sm.B[row][c] = bt * l[j];
+      }
+      if (t < p.T) *reinterpret_cast<float4*>(lrow + 4 * j4) = lv;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+  if (!ok) return;
+  // diagonal blocks: column cc of block blk by forward substitution; zeros above the diagonal blocks
+  for (int i = tid; i < C * C; i += kPrepThreads) {
+    const int r = i >> 6, c = i & 63;
+    if ((r >> 4) < (c >> 4)) sm.X[r][c] = 0.f;
+  }
+  if (tid < C) {
+    const int blk = tid >> 4, cc = tid & 15, o = 16 * blk;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float a = r == cc ? 1.f : 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) a = fmaf(-sm.B[o + r][o + j], x[j], a);
+      x[r] = r < cc ? 0.f : a;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sm.X[o + r][o + cc] = x[r];
+  }
+  __syncthreads();
+  for (int d = 1; d < 4; ++d) {
+    const int nblk = 4 - d;
+    // R_(i, j) = sum_{l=j}^{i-1} B_il X_lj for the blocks (i, j = i - d)
+    for (int idx = tid; idx < nblk * 256; idx += kPrepThreads) {
+      const int q = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+      const int bi = d + q, bj = q;
+      float a = 0.f;
+      for (int l = 16 * bj; l < 16 * bi; ++l) a = fmaf(sm.B[16 * bi + r][l], sm.X[l][16 * bj + c], a);
+      sm.R[q][r][c] = a;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nblk * 256; idx += kPrepThreads) {
+      const int q = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+      const int bi = d + q, bj = q;
+      float a = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m)
+        if (m <= r) a = fmaf(sm.X[16 * bi + r][16 * bi + m], sm.R[q][m][c], a);
+      sm.X[16 * bi + r][16 * bj + c] = -a;
+    }
+    __syncthreads();
+  }
+  for (int i = tid; i < C * (C / 4); i += kPrepThreads) {
+    const int r = i >> 4, c = (i & 15) * 4, t = c0 + r;
+    if (t < p.T)
+      *reinterpret_cast<float4*>(p.Tm + (rowbase + static_cast<size_t>(t) * p.H) * C + c) =
+          make_float4(sm.X[r][c], sm.X[r][c + 1], sm.X[r][c + 2], sm.X[r][c + 3]);
   }
 }
 
@@ -823,12 +991,21 @@ __global__ void __launch_bounds__(NT) delta_finish_kernel(const T* __restrict__ 
                                                           float* __restrict__ dq, float* __restrict__ dk,
                                                           float* __restrict__ dv, float* __restrict__ dbeta, long rows,
                                                           int D, int Dv, int M, float scale) {
-  extern __shared__ float sk[];  // per warp: D values of k
+  extern __shared__ float sk[];  // per warp: D values of k, then the M * M group inner products
   const long warp = (static_cast<long>(blockIdx.x) * NT + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
   if (warp >= rows) return;
-  float* kr = sk + wl * D;
+  float* kr = sk + wl * (D + 16);
+  float* ip = kr + D;  // ip[g * M + h] = k_g . k_h
   for (int c = lane; c < D; c += 32) kr[c] = to_f32<T>(kk[warp * D + c]);
+  __syncwarp();
+  const int E = D / M;
+  if (lane < M * M) {
+    const int g = lane / M, hh = lane - g * M;
+    float s = 0.f;
+    for (int e = 0; e < E; ++e) s = fmaf(kr[g * E + e], kr[hh * E + e], s);
+    ip[lane] = s;
+  }
   __syncwarp();
   const float bt = beta[warp];
   float yu = 0.f, db = 0.f;
@@ -845,16 +1022,11 @@ __global__ void __launch_bounds__(NT) delta_finish_kernel(const T* __restrict__ 
   }
   if (lane == 0) dbeta[warp] = db;
   const float dass = -bt * yu;
-  const int E = D / M;
   for (int c = lane; c < D; c += 32) {
-    const int g = c / E;
+    const int g = c / E, e = c - g * E;
     // dkappa(x,y)/dx_g at x = y = k: 2 scale^2 sum_h (k_g . k_h) k_h
     float dg = 0.f;
-    for (int hh = 0; hh < M; ++hh) {
-      float ip = 0.f;
-      for (int e = 0; e < E; ++e) ip = fmaf(kr[g * E + e], kr[hh * E + e], ip);
-      dg = fmaf(ip, kr[hh * E + (c - g * E)], dg);
-    }
+    for (int hh = 0; hh < M; ++hh) dg = fmaf(ip[g * M + hh], kr[hh * E + e], dg);
     dg *= 2.f * scale * scale;
     dq[warp * D + c] = to_f32<T>(dq1[warp * D + c]);
     dk[warp * D + c] = to_f32<T>(dk1[warp * D + c]) + to_f32<T>(dq2[warp * D + c]) + to_f32<T>(dk2[warp * D + c]) -
@@ -886,8 +1058,27 @@ int launch_k(K kernel, dim3 grid, size_t smem, cudaStream_t st, const DP& p, int
   return from_cuda(cudaGetLastError());
 }
 
+template <typename T, int D, int M>
+int run_tc_prep(const DP& p, cudaStream_t st) {
+  // at least 80 KB per CTA: at most two CTAs (2 x 256 tensor-memory columns) per SM
+  const size_t smem = std::max<size_t>(sizeof(TcPrepSmem) + 1024, 80 * 1024);
+  auto kern = delta_tc_prep_kernel<T, D, M>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return KATA_ERR_CUDA;
+  kern<<<dim3((p.T + C - 1) / C, p.B * p.H), kPrepThreads, smem, st>>>(p);
+  return from_cuda(cudaGetLastError());
+}
+
 template <typename T>
 int run_prep(const DP& p, cudaStream_t st) {
+  if constexpr (!std::is_same<T, float>::value) {
+    if (p.D == 64 && p.M == 4) return run_tc_prep<T, 64, 4>(p, st);
+    if (p.D == 64 && p.M == 2) return run_tc_prep<T, 64, 2>(p, st);
+    if (p.D == 64 && p.M == 1) return run_tc_prep<T, 64, 1>(p, st);
+    if (p.D == 128 && p.M == 4) return run_tc_prep<T, 128, 4>(p, st);
+    if (p.D == 128 && p.M == 2) return run_tc_prep<T, 128, 2>(p, st);
+    if (p.D == 128 && p.M == 1) return run_tc_prep<T, 128, 1>(p, st);
+  }
   const size_t smem = sizeof(float) * (C * (p.D + 1) + 2 * C * LDT + C);
   auto kern = delta_prep_kernel<T>;
   if (smem > 48 * 1024 &&
@@ -1187,7 +1378,7 @@ int bwd_typed(const kata_delta_bwd_args* a, cudaStream_t st) {
   g.dv = ws + w.dv2;
   e = attn_bwd_impl(&g, F32(w.zeros), reinterpret_cast<kata_stream_t>(st));
   if (e) return e;
-  const size_t smem = sizeof(float) * (NT / 32) * a->D;
+  const size_t smem = sizeof(float) * (NT / 32) * (a->D + 16);
   delta_finish_kernel<T><<<warp_blocks(rows), NT, smem, st>>>(
       static_cast<const T*>(static_cast<const void*>(ws + w.dq1)), static_cast<const T*>(static_cast<const void*>(ws + w.dk1)),
       static_cast<const T*>(static_cast<const void*>(ws + w.dq2)), static_cast<const T*>(static_cast<const void*>(ws + w.dk2)),
