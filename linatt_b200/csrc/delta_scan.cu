@@ -651,14 +651,15 @@ struct TcScanSmem {
   int abort;
 };
 
-// psi of token row pr, features [ph F / 2, (ph + 1) F / 2) (F = 64 NFB), into the 16-bit psi tiles,
+// psi of token row pr, features [ph F / NPH, (ph + 1) F / NPH) (F = 64 NFB), into the 16-bit psi tiles,
 // eight features per 16-byte store.  E and M are compile-time: the row sits in registers and every
 // feature's (a, b) pair, weight and tile position are constants of the unrolled loops (a table
 // lookup and two shared-memory loads per product otherwise).
-template <typename T, int E, int M, int NFB>
+template <typename T, int E, int M, int NFB, int NPH>
 __device__ __forceinline__ void build_psi_row(const float* krow, int pr, int ph, float scale,
                                               uint8_t (*psi)[tc64::TB]) {
-  constexpr int F = 64 * NFB, FH = F / 2, FSYM = E * (E + 1) / 2;
+  constexpr int F = 64 * NFB, FH = F / NPH, FSYM = E * (E + 1) / 2;
+  static_assert(FH % 8 == 0, "whole 16-byte stores per part");
   float k[M * E];
 #pragma unroll
   for (int i = 0; i < M * E; ++i) k[i] = krow[i];
@@ -687,18 +688,14 @@ __device__ __forceinline__ void build_psi_row(const float* krow, int pr, int ph,
   }
 }
 
-// 64 TMEM columns of this warp's lanes; lane half hh keeps columns [32 hh, 32 hh + 32).
-__device__ __forceinline__ void ld_half32(uint32_t taddr, int hh, float (&x)[32]) {
-  uint32_t a[32], b[32];
-  tmem_ld32(taddr, a);
-  tmem_ld32(taddr + 32, b);
-  tmem_wait_ld();
-#pragma unroll
-  for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(hh ? b[j] : a[j]);
-}
+constexpr int kScanThreads = 256;
 
+// Thread mapping (8 warps): warp w reads TMEM lane quarter w % 4, where both lane halves hold rows
+// 16 (w % 4) .. + 15 of every M = 64 accumulator (the MMAs are issued at lane offsets 0 and 16);
+// thread (w, lane) owns row m = 16 (w % 4) + lane % 16 and the 16 value columns of group
+// cg = 2 (w / 4) + lane / 16.  The state (F x 64) is held as 16 columns of NFB feature rows per thread.
 template <typename T, int E, int M, bool REV>
-__global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
+__global__ void __launch_bounds__(kScanThreads) delta_tc_scan_kernel(DP p) {
   using namespace tc64;
   constexpr int NFB = (E * (E + 1) / 2 + 63) / 64;
   using Sm = TcScanSmem<NFB>;
@@ -721,13 +718,16 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
     tmem_relinquish();
   }
   build_feature_table(sm.tab, E, F);
-  const RowMap rm = rowmap();
-  const int m = rm.row, hh = rm.slot;
-  float S[NFB][2][16];
+  const int warp = tid >> 5, ln = tid & 31;
+  const int m = 16 * (warp & 3) + (ln & 15), hl = ln >> 4;
+  const int col0 = 16 * (2 * (warp >> 2) + hl);                    // this thread's 16 value columns
+  const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+  const uint32_t tcol = 32u * static_cast<uint32_t>(warp >> 2);   // the 32 columns this warp loads
+  float S[NFB][16];
 #pragma unroll
   for (int fb = 0; fb < NFB; ++fb)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) S[fb][0][j] = S[fb][1][j] = 0.f;
+    for (int j = 0; j < 16; ++j) S[fb][j] = 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -735,18 +735,18 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
   uint32_t phase = 0;
   bool ok = true;
   const int nch = (p.T + C - 1) / C;
-  const int pr = tid & 63, ph = tid >> 6;  // psi building: token row, feature half of every block
+  const int pr = tid & 63, ph = tid >> 6;  // psi building: token row, quarter of the features
   // chunk `chn`'s Tm (and L), keys and beta into buffer bf by cp.async (rows past T zero-filled)
   auto issue = [&](int chn, int bf) {
     const int cc0 = chn * C, kv = D / 8;
-    for (int idx = tid; idx < C * 16; idx += 128) {
+    for (int idx = tid; idx < C * 16; idx += kScanThreads) {
       const int r = idx >> 4, c = idx & 15, t = cc0 + r;
       const bool in = t < p.T;
       const size_t o = (rowbase + static_cast<size_t>(in ? t : 0) * p.H) * C + 4 * c;
       cp_async16(smem_u32(&sm.Tm[bf][r][4 * c]), p.Tm + o, in);
       if (!REV) cp_async16(smem_u32(&sm.L[bf][r][4 * c]), p.Lm + o, in);
     }
-    for (int idx = tid; idx < C * kv; idx += 128) {
+    for (int idx = tid; idx < C * kv; idx += kScanThreads) {
       const int r = idx / kv, c = idx - r * kv, t = cc0 + r;
       const bool in = t < p.T;
       cp_async16(smem_u32(&sm.K[bf][r * 64 + 8 * c]), kp + static_cast<size_t>(in ? t : 0) * p.H * D + 8 * c, in);
@@ -773,20 +773,17 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
     {  // keys to fp32 (this thread's own copies have landed; the barrier below publishes them all)
       const T* kr = reinterpret_cast<const T*>(sm.K[bf]);
       __syncthreads();
-      for (int i = tid; i < C * D; i += 128) {
+      for (int i = tid; i < C * D; i += kScanThreads) {
         const int r = i / D, c = i - r * D;
         sm.Kf[r][c] = to_f32<T>(kr[r * 64 + c]);
       }
     }
     // the state as 16-bit tiles (rows features), the B operand of P = psi(K) state
 #pragma unroll
-    for (int fb = 0; fb < NFB; ++fb) {
-      st_row16<T>(sm.st[fb], m, 32 * hh, S[fb][0]);
-      st_row16<T>(sm.st[fb], m, 32 * hh + 16, S[fb][1]);
-    }
+    for (int fb = 0; fb < NFB; ++fb) st_row16<T>(sm.st[fb], m, col0, S[fb]);
     __syncthreads();
-    // psi(K): thread (token pr, half ph) forms features [ph F / 2, (ph + 1) F / 2)
-    build_psi_row<T, E, M, NFB>(sm.Kf[pr], pr, ph, p.scale, sm.psi);
+    // psi(K): thread (token pr, quarter ph) forms features [ph F / 4, (ph + 1) F / 4)
+    build_psi_row<T, E, M, NFB, kScanThreads / 64>(sm.Kf[pr], pr, ph, p.scale, sm.psi);
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -797,35 +794,35 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
       umma_commit(&sm.bar);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
-    float x[32];
-    ld_half32(tbase + rm.lane, hh, x);
+    float x[16];
+    ld_quarter(tbase + lane_base + tcol, hl, x);
     const int t = c0 + m;
     const bool in = t < p.T;
-    const size_t vrow = (rowbase + static_cast<size_t>(in ? t : 0) * p.H) * 64 + 32 * hh;
+    const size_t vrow = (rowbase + static_cast<size_t>(in ? t : 0) * p.H) * 64 + col0;
     {
       const T* src = static_cast<const T*>(REV ? p.dU : p.v) + vrow;
-      float in32[32];
+      float in16[16];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         const uint4 u4 = in ? reinterpret_cast<const uint4*>(src)[q] : make_uint4(0u, 0u, 0u, 0u);
         const T* e = reinterpret_cast<const T*>(&u4);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) in32[8 * q + j] = to_f32<T>(e[j]);
+        for (int j = 0; j < 8; ++j) in16[8 * q + j] = to_f32<T>(e[j]);
       }
       const float bm = beta[m];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) sm.R[m][32 * hh + j] = REV ? in32[j] - x[j] : bm * (in32[j] - x[j]);
+      for (int j = 0; j < 16; ++j) sm.R[m][col0 + j] = REV ? in16[j] - x[j] : bm * (in16[j] - x[j]);
     }
     __syncthreads();
-    float y[32];  // u-scan: U = Tm rhs (row m);  y-scan: Y = Tm^T X (row m)
+    float y[16];  // u-scan: U = Tm rhs (row m);  y-scan: Y = Tm^T X (row m)
 #pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = 0.f;
+    for (int j = 0; j < 16; ++j) y[j] = 0.f;
     if (!REV) {
       for (int i = 0; i <= m; ++i) {
         const float tmi = Tm[m][i];
-        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][32 * hh]);
+        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][col0]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const float4 r4 = rr[q];
           y[4 * q] = fmaf(tmi, r4.x, y[4 * q]);
           y[4 * q + 1] = fmaf(tmi, r4.y, y[4 * q + 1]);
@@ -836,9 +833,9 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
     } else {
       for (int i = m; i < C; ++i) {
         const float tim = Tm[i][m];
-        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][32 * hh]);
+        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][col0]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const float4 r4 = rr[q];
           y[4 * q] = fmaf(tim, r4.x, y[4 * q]);
           y[4 * q + 1] = fmaf(tim, r4.y, y[4 * q + 1]);
@@ -852,20 +849,16 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
       float* dst = (REV ? p.Y : p.U) + vrow;
       if (in)
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < 4; ++q)
           reinterpret_cast<float4*>(dst)[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
       const float wsc = REV ? beta[m] : 1.f;  // the state update takes U, or beta Y
-      float w0[16], w1[16];
+      float w0[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        w0[j] = wsc * y[j];
-        w1[j] = wsc * y[16 + j];
-      }
-      st_row16<T>(sm.w, m, 32 * hh, w0);
-      st_row16<T>(sm.w, m, 32 * hh + 16, w1);
+      for (int j = 0; j < 16; ++j) w0[j] = wsc * y[j];
+      st_row16<T>(sm.w, m, col0, w0);
       if (!REV)
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sm.R[m][32 * hh + j] = y[j];
+        for (int j = 0; j < 16; ++j) sm.R[m][col0 + j] = y[j];
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -879,9 +872,9 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
     if (!REV && p.E && in) {  // E = P + sum_{i<m} L[m][i] U_i  (overlaps the state-update MMAs)
       for (int i = 0; i < m; ++i) {
         const float lmi = Lm[m][i];
-        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][32 * hh]);
+        const float4* rr = reinterpret_cast<const float4*>(&sm.R[i][col0]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const float4 r4 = rr[q];
           x[4 * q] = fmaf(lmi, r4.x, x[4 * q]);
           x[4 * q + 1] = fmaf(lmi, r4.y, x[4 * q + 1]);
@@ -891,19 +884,16 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
       }
       float* dst = p.E + vrow;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
+      for (int q = 0; q < 4; ++q)
         reinterpret_cast<float4*>(dst)[q] = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
     }
     if (!(ok = wait_mma(&sm.bar, phase, &sm.abort))) break;
 #pragma unroll
     for (int fb = 0; fb < NFB; ++fb) {
-      float d[32];
-      ld_half32(tbase + rm.lane + 64 + 64 * fb, hh, d);
+      float d[16];
+      ld_quarter(tbase + lane_base + 64 + 64 * fb + tcol, hl, d);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        S[fb][0][j] += d[j];
-        S[fb][1][j] += d[16 + j];
-      }
+      for (int j = 0; j < 16; ++j) S[fb][j] += d[j];
     }
     tc_fence_before();
     __syncthreads();  // tiles and R are rewritten by the next chunk
@@ -915,10 +905,10 @@ __global__ void __launch_bounds__(128) delta_tc_scan_kernel(DP p) {
       if (tb == 0xffffu) continue;
       const int a = static_cast<int>(tb >> 8), bc = static_cast<int>(tb & 0xffu);
       const float wt = a == bc ? 1.f : 0.70710678118654752f;
-      float* out = p.S + static_cast<size_t>(bh) * E * E * 64 + 32 * hh;
+      float* out = p.S + static_cast<size_t>(bh) * E * E * 64 + col0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float val = S[fb][j >> 4][j & 15] * wt;
+      for (int j = 0; j < 16; ++j) {
+        const float val = S[fb][j] * wt;
         out[static_cast<size_t>(a * E + bc) * 64 + j] = val;
         out[static_cast<size_t>(bc * E + a) * 64 + j] = val;
       }
@@ -1101,7 +1091,7 @@ int run_tc_scan(const DP& p, cudaStream_t st) {
   auto go = [&](auto kern, size_t smem) -> int {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
       return KATA_ERR_CUDA;
-    kern<<<p.B * p.H, 128, smem, st>>>(p);
+    kern<<<p.B * p.H, kScanThreads, smem, st>>>(p);
     return from_cuda(cudaGetLastError());
   };
   constexpr size_t smem = sizeof(TcScanSmem<3>) + 1024;  // E = 16: 136 features in 3 blocks
