@@ -577,9 +577,12 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       // column halves of dQ: D / 2 each, or 80 + 64 for the kGramFP = 144 Gram columns
       constexpr int HD0 = GRAM ? 80 : D / 2;
       T* dqrow = static_cast<T*>(p.dq) + rowidx * D;
+      constexpr int kSteps = (HD0 > D - HD0 ? HD0 : D - HD0) / 16;  // compile-time trip count
       const int cbeg = hc ? HD0 : 0, cend = hc ? D : HD0;
 #pragma unroll
-      for (int c0 = cbeg; c0 < cend; c0 += 16) {
+      for (int i = 0; i < kSteps; ++i) {
+        const int c0 = cbeg + 16 * i;
+        if (c0 >= cend) break;  // warp-uniform
         uint32_t r[16];
         tmem_ld16(lane_addr + kColDQ + c0, r);
         tmem_wait_ld();
@@ -935,14 +938,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int x2 = 0; x2 < 8; ++x2) {
             const float2 sv = u2f2(rs[cur][2 * x2], rs[cur][2 * x2 + 1]);
-            acc[8 * c + x2] = GRAM ? sv : pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x2]);
-            if constexpr (GRAM) {  // linear score: W^T = dA''^T itself
+            if constexpr (GRAM) {  // linear score: P^T from S itself, W^T = dA''^T
+              acc[8 * c + x2] = sv;
               wv[x2] = dap[8 * c + x2];
-            } else if constexpr (kBF16) {  // S rounded to bf16, packed product (same operand precision as the MMA)
-              wv[x2] = bf2_mul(pack2<T>(sv.x, sv.y), dap[8 * c + x2]);
             } else {
-              const float2 w = fmul2(sv, bf2_unpack(dap[8 * c + x2]));
-              wv[x2] = pack2<T>(w.x, w.y);
+              acc[8 * c + x2] = pp == 0 ? fmul2(sv, sv) : ffma2(sv, sv, acc[8 * c + x2]);
+              if constexpr (kBF16) {  // S rounded to bf16, packed product (same operand precision as the MMA)
+                wv[x2] = bf2_mul(pack2<T>(sv.x, sv.y), dap[8 * c + x2]);
+              } else {
+                const float2 w = fmul2(sv, bf2_unpack(dap[8 * c + x2]));
+                wv[x2] = pack2<T>(w.x, w.y);
+              }
             }
           }
           tmem_st8(sbase + c * 8u, wv);  // columns of S already in registers
@@ -993,27 +999,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(1, 256);
     if (ok && mbar_wait(&bars.acc_done, 0, wc)) {
       tc_fence_after();
-      // column halves of dK: D / 2 each, or 80 + 64 for the kGramFP = 144 Gram columns
-      constexpr int HD0 = GRAM ? 80 : D / 2, HV = DV / 2;
+      constexpr int HV = DV / 2;
       const size_t rowkv = (static_cast<size_t>(b) * T_ + sg) * p.H + h;
-      T* dkrow = static_cast<T*>(p.dk) + rowkv * D;
       T* dvrow = static_cast<T*>(p.dv) + rowkv * DV + hc * HV;
-      const int cbeg = hc ? HD0 : 0, cend = hc ? D : HD0;
+      if constexpr (!GRAM) {
+        constexpr int HD = D / 2;
+        T* dkrow = static_cast<T*>(p.dk) + rowkv * D + hc * HD;
 #pragma unroll
-      for (int c0 = cbeg; c0 < cend; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(lane_addr + kColDK + c0, r);
-        tmem_wait_ld();
-        if (live) {  // dK = 2 * (sum of W''^T Q); Gram: the sum itself
-          const auto f = [&](int i) { return (GRAM ? 1.f : 2.f) * __uint_as_float(r[i]); };
+        for (int c0 = 0; c0 < HD; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(lane_addr + kColDK + hc * HD + c0, r);
+          tmem_wait_ld();
+          if (live) {  // dK = 2 * (sum of W''^T Q)
+            const auto f = [&](int i) { return 2.f * __uint_as_float(r[i]); };
 #pragma unroll
-          for (int v2 = 0; v2 < 2; ++v2) {
-            uint4 w;
-            w.x = pack2<T>(f(8 * v2 + 0), f(8 * v2 + 1));
-            w.y = pack2<T>(f(8 * v2 + 2), f(8 * v2 + 3));
-            w.z = pack2<T>(f(8 * v2 + 4), f(8 * v2 + 5));
-            w.w = pack2<T>(f(8 * v2 + 6), f(8 * v2 + 7));
-            *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
+            for (int v2 = 0; v2 < 2; ++v2) {
+              uint4 w;
+              w.x = pack2<T>(f(8 * v2 + 0), f(8 * v2 + 1));
+              w.y = pack2<T>(f(8 * v2 + 2), f(8 * v2 + 3));
+              w.z = pack2<T>(f(8 * v2 + 4), f(8 * v2 + 5));
+              w.w = pack2<T>(f(8 * v2 + 6), f(8 * v2 + 7));
+              *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
+            }
+          }
+        }
+      } else {  // Gram: d phi(k) over kGramFP = 144 columns, halves of 80 and 64, no doubling
+        T* dkrow = static_cast<T*>(p.dk) + rowkv * D;
+        const int cbeg = hc ? 80 : 0, cend = hc ? D : 80;
+        for (int c0 = cbeg; c0 < cend; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(lane_addr + kColDK + c0, r);
+          tmem_wait_ld();
+          if (live) {
+#pragma unroll
+            for (int v2 = 0; v2 < 2; ++v2) {
+              uint4 w;
+              w.x = pack2<T>(__uint_as_float(r[8 * v2 + 0]), __uint_as_float(r[8 * v2 + 1]));
+              w.y = pack2<T>(__uint_as_float(r[8 * v2 + 2]), __uint_as_float(r[8 * v2 + 3]));
+              w.z = pack2<T>(__uint_as_float(r[8 * v2 + 4]), __uint_as_float(r[8 * v2 + 5]));
+              w.w = pack2<T>(__uint_as_float(r[8 * v2 + 6]), __uint_as_float(r[8 * v2 + 7]));
+              *reinterpret_cast<uint4*>(dkrow + c0 + 8 * v2) = w;
+            }
           }
         }
       }

@@ -15,7 +15,9 @@ plus ``ChunkGatedDeltaRuleFunction`` and the alias ``chunk_gdn``.  All recurrenc
 in ``libkata_b200.so`` (``kata_gdn_fwd`` / ``kata_gdn_bwd``).  The q/k l2norm and the in-kernel
 gate are applied as differentiable torch prologues before the library call.  Context parallelism
 (``cp_context``) is fla's own multi-GPU scheme and is not provided.  The kernels work on 64-wide
-heads; narrower q/k/v heads are zero-padded to 64 (exact), wider ones are not supported yet.
+heads; narrower q/k/v heads are zero-padded to 64 (exact); value heads wider than 64 run as
+independent 64-column slices of the state (exact, see ``_value_slices``); key heads wider than 64
+are not supported.
 """
 
 from __future__ import annotations
@@ -74,10 +76,52 @@ def _check_width(K, V):
         raise NotImplementedError(f"linatt_b200 gated delta rule covers head widths up to {KDIM} (got K={K}, V={V})")
 
 
+def _value_slices(V):
+    """Value-column ranges of at most KDIM.  Every value column of the state S (K x V) follows its
+    own recurrence S[:, j] <- e^g (I - beta k k^T) S[:, j] + beta v_j k, and o[j] = S[:, j] . q, so a
+    head wider than the kernels runs as independent slices of the value dimension whose q, k, g and
+    beta gradients add up (fla's chunk_gated_delta_rule, chunk.py:365, accepts any V)."""
+    return [(s0, min(s0 + KDIM, V)) for s0 in range(0, V, KDIM)]
+
+
+def _fwd_sliced(q, k, v, g, beta, scale, h0, want_final, tables):
+    """_fwd over value slices of at most KDIM columns: (o, A, final state, [forward workspace per slice])."""
+    if v.shape[-1] <= KDIM:
+        o, A, ht, ws = _fwd(q, k, v, g, beta, scale, h0, want_final, tables)
+        return o, A, ht, [ws]
+    os_, hts, wss, A = [], [], [], None
+    for s0, s1 in _value_slices(v.shape[-1]):
+        h0s = None if h0 is None else h0[..., s0:s1].contiguous()
+        o, A, ht, ws = _fwd(q, k, v[..., s0:s1].contiguous(), g, beta, scale, h0s, want_final, tables)
+        os_.append(o)
+        hts.append(ht)
+        wss.append(ws)
+    ht = torch.cat(hts, -1) if want_final else None
+    return torch.cat(os_, -1), A, ht, wss
+
+
+def _bwd_sliced(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws, grad16=False):
+    """_bwd over the value slices of _fwd_sliced (fwd_ws: one workspace per slice)."""
+    if v.shape[-1] <= KDIM:
+        return _bwd(q, k, v, g, beta, A, scale, h0, do, dht, tables, fwd_ws=fwd_ws[0], grad16=grad16)
+    acc, dvs, dh0s = None, [], []
+    for (s0, s1), ws in zip(_value_slices(v.shape[-1]), fwd_ws):
+        h0s = None if h0 is None else h0[..., s0:s1].contiguous()
+        dhts = None if dht is None else dht[..., s0:s1].contiguous()
+        dq, dk, dv, dg, db, dh0 = _bwd(q, k, v[..., s0:s1].contiguous(), g, beta, A, scale, h0s,
+                                       do[..., s0:s1].contiguous(), dhts, tables, fwd_ws=ws)
+        part = [x.float() for x in (dq, dk, dg, db)]
+        acc = part if acc is None else [a + b for a, b in zip(acc, part)]
+        dvs.append(dv)
+        dh0s.append(dh0)
+    dq, dk, dg, db = acc
+    return dq, dk, torch.cat(dvs, -1), dg, db, (None if h0 is None else torch.cat(dh0s, -1))
+
+
 def _fwd(q, k, v, g, beta, scale, h0, want_final, tables):
     dev = _lib.require_cuda(q, k, v, g, beta, h0)
     K0, V0 = q.shape[-1], v.shape[-1]
-    _check_width(K0, V0)
+    _check_width(K0, V0)  # V0 <= KDIM here: wider value heads arrive as slices (_fwd_sliced)
     q, k, v = (_pad_last(x, KDIM).contiguous() for x in (q, k, v))
     h0 = _pad_state(h0)
     B, T, H, K = q.shape
@@ -164,12 +208,14 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
             h0 = initial_state.float()
             h0 = (h0.transpose(-1, -2) if transpose_state_layout else h0).contiguous()
         tables = _chunk_tables(cu_seqlens, cu_seqlens_cpu, B, T, q.device)
-        o, A, ht, ws = _fwd(qc, kc, vc, gc, bc, scale, h0, output_final_state, tables)
+        if q.shape[-1] > KDIM:
+            _check_width(q.shape[-1], v.shape[-1])
+        o, A, ht, ws = _fwd_sliced(qc, kc, vc, gc, bc, scale, h0, output_final_state, tables)
         if ht is not None and transpose_state_layout:
             ht = ht.transpose(-1, -2).contiguous()
         # Besides fla's saved set (q, k, v, g, beta, A, initial state) the forward's workspace (chunk
         # states, u, W, U0, gamma) is kept, so the backward does not recompute the forward scan.
-        ctx.save_for_backward(qc, kc, vc, gc, bc, A, h0, ws)
+        ctx.save_for_backward(qc, kc, vc, gc, bc, A, h0, *ws)
         ctx.tables = tables
         ctx.scale = scale
         ctx.transpose_state_layout = transpose_state_layout
@@ -179,13 +225,13 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do, dht):
-        qc, kc, vc, gc, bc, A, h0, ws = ctx.saved_tensors
+        qc, kc, vc, gc, bc, A, h0, *ws = ctx.saved_tensors
         if dht is not None and ctx.transpose_state_layout:
             dht = dht.transpose(-1, -2)
         tq, tk, tv, tg, tb, th = ctx.dtypes
         same = tq == tk == tv == qc.dtype
-        dq, dk, dv, dg, db, dh0 = _bwd(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables, fwd_ws=ws,
-                                       grad16=same)
+        dq, dk, dv, dg, db, dh0 = _bwd_sliced(qc, kc, vc, gc, bc, A, ctx.scale, h0, do, dht, ctx.tables, ws,
+                                              grad16=same)
         if dh0 is not None:
             dh0 = (dh0.transpose(-1, -2) if ctx.transpose_state_layout else dh0).to(th)
         return (dq.to(tq), dk.to(tk), dv.to(tv), dg.to(tg), db.to(tb), None, dh0, None, None, None, None, None,

@@ -106,6 +106,24 @@ def test_gdn_fp32_matches_oracle(B, T, H, HV, K, V, h0):
         assert e < 1e-5, f"{n}: rel-L2 {e:.3e}"
 
 
+@pytest.mark.parametrize("dtype,V,HV,h0", [(torch.float32, 128, 2, True), (torch.float32, 96, 4, True),
+                                            (torch.bfloat16, 128, 2, False)])
+def test_gdn_value_heads_wider_than_the_kernels(dtype, V, HV, h0):
+    """V > 64: the state's value columns evolve independently, so the value head runs as 64-column
+    slices whose q, k, g, beta gradients add up; the result equals the fp64 oracle on the whole head."""
+    B, T, H, K = 2, 150, 2, 64
+    q, k, v, g, beta, do, s0, dht = draw(V + HV, B, T, H, HV, K, V, h0=h0, dtype=dtype)
+    got = run(q, k, v, g, beta, do, h0=s0, dht=dht)
+    ref = oracle(q, k, v, g, beta, do, h0=s0, dht=dht)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert got["o"].shape[-1] == V and got["ht"].shape[-1] == V
+    assert rel_l2(np64(got["o"]), ref["o"]) < tol
+    assert rel_l2(np64(got["ht"]), ref["final_state"]) < tol
+    for n in GRADS + (("dh0",) if h0 else ()):
+        e = rel_l2(np64(got[n]), ref[n])
+        assert e < tol, f"{n}: rel-L2 {e:.3e}"
+
+
 def test_gdn_gate_l2norm_transpose_options():
     B, T, H, HV, K, V = 1, 150, 2, 2, 64, 64
     q, k, v, g, beta, do, s0, dht = draw(4, B, T, H, HV, K, V, h0=True)
