@@ -18,6 +18,7 @@
 
 #include "attn_common.cuh"
 #include "host_util.h"
+#include "tc64.cuh"
 
 namespace kata {
 namespace {
@@ -45,6 +46,39 @@ __device__ __forceinline__ void store_vec(T* p, const float (&v)[VecN<T>::N]) {
 
 __device__ __forceinline__ float sigmoidf_(float a) { return __fdividef(1.f, 1.f + __expf(-a)); }
 
+// VB-byte vectors (VB = 8 or 16) of the convolution's channel slices
+template <int VB>
+struct VecRaw;
+template <>
+struct VecRaw<16> {
+  using type = uint4;
+};
+template <>
+struct VecRaw<8> {
+  using type = uint2;
+};
+template <typename T, int VB>
+__device__ __forceinline__ void unpack_raw(const typename VecRaw<VB>::type& u, float* v) {
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < VB / static_cast<int>(sizeof(T)); ++i) v[i] = to_f32<T>(e[i]);
+}
+template <typename T, int VB>
+__device__ __forceinline__ void store_raw(T* p, const float* v) {
+  typename VecRaw<VB>::type u;
+  T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < VB / static_cast<int>(sizeof(T)); ++i) e[i] = from_f32<T>(v[i]);
+  *reinterpret_cast<typename VecRaw<VB>::type*>(p) = u;
+}
+template <int VB>
+__device__ __forceinline__ void cp_async_vec(uint32_t dst, const void* src) {
+  if constexpr (VB == 16)
+    tc64::cp_async16(dst, src, true);
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------
 // short convolution
 // ------------------------------------------------------------------------------------------------
@@ -65,12 +99,24 @@ struct ConvParams {
   int nrun;
 };
 
+// Per-thread input ring in shared memory: [buffer][step of the batch][thread] 16-byte slots, filled by
+// cp.async and read back only by the thread that issued the copies (its own commit groups order
+// them, so no barrier is needed).  Two batches of kConvU steps are in flight while one is consumed,
+// and the raw vectors no longer occupy registers.
+template <typename R>
+__device__ __forceinline__ R* conv_slot(R* ring, int bf, int u) {
+  return ring + (bf * kConvU + u) * blockDim.x + threadIdx.x;
+}
+
 // grid (ceil(channel vectors / blockDim), runs of kConvRun steps, B); a thread owns one 16-byte
-// channel vector over one run.  Steps go in batches of kConvU: the batch's loads are issued before
-// any of them is used, so a thread keeps kConvU loads in flight instead of one.
-template <typename T, int K>
+// channel vector over one run.  Steps go in batches of kConvU, double-buffered through the
+// thread's cp.async ring.
+template <typename T, int K, int VB>
 __global__ void __launch_bounds__(128) conv_fwd_kernel(ConvParams p) {
-  constexpr int V = VecN<T>::N;
+  using R = typename VecRaw<VB>::type;
+  extern __shared__ __align__(16) uint8_t conv_smem[];
+  R* conv_ring = reinterpret_cast<R*>(conv_smem);  // [2][kConvU][blockDim.x]
+  constexpr int V = VB / static_cast<int>(sizeof(T));
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * V;
   if (c0 >= p.C) return;
   const int b = blockIdx.z, t0 = blockIdx.y * kConvRun;
@@ -88,23 +134,31 @@ __global__ void __launch_bounds__(128) conv_fwd_kernel(ConvParams p) {
 #pragma unroll
   for (int i = 0; i < K - 1; ++i) {
     const int t = t0 - (K - 1) + i;
-    if (t >= 0) load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[i]);
+    if (t >= 0) unpack_raw<T, VB>(*reinterpret_cast<const R*>(xb + static_cast<size_t>(t) * p.ldx), win[i]);
     else {
 #pragma unroll
       for (int j = 0; j < V; ++j) win[i][j] = 0.f;
     }
   }
-  for (int tb = t0; tb < t1; tb += kConvU) {
-    uint4 raw[kConvU];
+  const auto issue = [&](int tb, int bf) {
 #pragma unroll
     for (int u = 0; u < kConvU; ++u)
-      if (tb + u < t1) raw[u] = *reinterpret_cast<const uint4*>(xb + static_cast<size_t>(tb + u) * p.ldx);
+      if (tb + u < t1) cp_async_vec<VB>(smem_u32(conv_slot(conv_ring, bf, u)), xb + static_cast<size_t>(tb + u) * p.ldx);
+    tc64::cp_async_commit();
+  };
+  issue(t0, 0);
+  for (int tb = t0, it = 0; tb < t1; tb += kConvU, ++it) {
+    const int bf = it & 1;
+    if (tb + kConvU < t1) {
+      issue(tb + kConvU, bf ^ 1);
+      tc64::cp_async_wait<1>();
+    } else {
+      tc64::cp_async_wait<0>();
+    }
 #pragma unroll
     for (int u = 0; u < kConvU; ++u) {
-      if (tb + u < t1) {  // (a guard, not a break: the batch stays fully unrolled in registers)
-      const T* e = reinterpret_cast<const T*>(&raw[u]);
-#pragma unroll
-      for (int j = 0; j < V; ++j) win[K - 1][j] = to_f32<T>(e[j]);
+      if (tb + u < t1) {  // (a guard, not a break: the batch stays fully unrolled)
+      unpack_raw<T, VB>(*conv_slot(conv_ring, bf, u), win[K - 1]);
       float out[V];
 #pragma unroll
       for (int j = 0; j < V; ++j) {
@@ -113,7 +167,7 @@ __global__ void __launch_bounds__(128) conv_fwd_kernel(ConvParams p) {
         for (int i = 0; i < K; ++i) a = fmaf(wr[i][j], win[i][j], a);
         out[j] = p.act ? a * sigmoidf_(a) : a;
       }
-      store_vec<T>(yb + static_cast<size_t>(tb + u) * p.ldy, out);
+      store_raw<T, VB>(yb + static_cast<size_t>(tb + u) * p.ldy, out);
 #pragma unroll
       for (int i = 0; i < K - 1; ++i)
 #pragma unroll
@@ -155,9 +209,12 @@ __global__ void conv_split_kernel(const float* sums, int C, int K, float* dw, fl
 // dw[c,i] = sum_t g[t] x[t - K + 1 + i], dbias[c] = sum_t g[t].  A thread walks its run plus K - 1
 // steps of look-ahead (the g values its last dx outputs need), keeping the last K x and g values;
 // loads go in batches of kConvU steps as in the forward.
-template <typename T, int K>
+template <typename T, int K, int VB>
 __global__ void __launch_bounds__(128) conv_bwd_kernel(ConvParams p) {
-  constexpr int V = VecN<T>::N;
+  using R = typename VecRaw<VB>::type;
+  extern __shared__ __align__(16) uint8_t conv_smem[];
+  R* conv_ring = reinterpret_cast<R*>(conv_smem);  // x: [2][kConvU][blockDim.x], then dy: the same
+  constexpr int V = VB / static_cast<int>(sizeof(T));
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * V;
   if (c0 >= p.C) return;
   const int b = blockIdx.z, t0 = blockIdx.y * kConvRun;
@@ -182,7 +239,7 @@ __global__ void __launch_bounds__(128) conv_bwd_kernel(ConvParams p) {
 #pragma unroll
   for (int i = 0; i < K - 1; ++i) {
     const int t = t0 - (K - 1) + i;
-    if (t >= 0) load_vec<T>(xb + static_cast<size_t>(t) * p.ldx, win[i]);
+    if (t >= 0) unpack_raw<T, VB>(*reinterpret_cast<const R*>(xb + static_cast<size_t>(t) * p.ldx), win[i]);
     else {
 #pragma unroll
       for (int j = 0; j < V; ++j) win[i][j] = 0.f;
@@ -190,26 +247,37 @@ __global__ void __launch_bounds__(128) conv_bwd_kernel(ConvParams p) {
   }
   const int tend = t1 + K - 1;  // exclusive
   const int tload = min(tend, p.T);
-  for (int tb = t0; tb < tend; tb += kConvU) {
-    uint4 rx[kConvU], rd[kConvU];
+  R* ring_d = conv_ring + 2 * kConvU * blockDim.x;
+  const auto issue = [&](int tb, int bf) {
 #pragma unroll
     for (int u = 0; u < kConvU; ++u) {
       if (tb + u < tload) {
-        rx[u] = *reinterpret_cast<const uint4*>(xb + static_cast<size_t>(tb + u) * p.ldx);
-        rd[u] = *reinterpret_cast<const uint4*>(dyb + static_cast<size_t>(tb + u) * p.ldy);
+        cp_async_vec<VB>(smem_u32(conv_slot(conv_ring, bf, u)), xb + static_cast<size_t>(tb + u) * p.ldx);
+        cp_async_vec<VB>(smem_u32(conv_slot(ring_d, bf, u)), dyb + static_cast<size_t>(tb + u) * p.ldy);
       }
+    }
+    tc64::cp_async_commit();
+  };
+  issue(t0, 0);
+  for (int tb = t0, it = 0; tb < tend; tb += kConvU, ++it) {
+    const int bf = it & 1;
+    if (tb + kConvU < tend) {
+      issue(tb + kConvU, bf ^ 1);
+      tc64::cp_async_wait<1>();
+    } else {
+      tc64::cp_async_wait<0>();
     }
 #pragma unroll
     for (int u = 0; u < kConvU; ++u) {
       const int t = tb + u;
-      if (t < tend) {  // (a guard, not a break: the batch stays fully unrolled in registers)
+      if (t < tend) {  // (a guard, not a break: the batch stays fully unrolled)
       if (t < p.T) {
-        const T* ex = reinterpret_cast<const T*>(&rx[u]);
-        const T* ed = reinterpret_cast<const T*>(&rd[u]);
+        float gin[V];
+        unpack_raw<T, VB>(*conv_slot(conv_ring, bf, u), win[K - 1]);
+        unpack_raw<T, VB>(*conv_slot(ring_d, bf, u), gin);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
-          win[K - 1][j] = to_f32<T>(ex[j]);
-          float g = to_f32<T>(ed[j]);
+          float g = gin[j];
           if (p.act) {
             float a = br[j];
 #pragma unroll
@@ -241,7 +309,7 @@ __global__ void __launch_bounds__(128) conv_bwd_kernel(ConvParams p) {
           for (int i = 0; i < K; ++i) acc = fmaf(wr[i][j], gq[K - 1 - i][j], acc);
           out[j] = acc;
         }
-        store_vec<T>(dxb + static_cast<size_t>(s0) * p.lddx, out);
+        store_raw<T, VB>(dxb + static_cast<size_t>(s0) * p.lddx, out);
       }
 #pragma unroll
       for (int i = 0; i < K - 1; ++i)
@@ -528,7 +596,10 @@ int conv_check(const kata_conv_args* a, bool bwd) {
 
 template <typename T>
 int conv_launch(const kata_conv_args* a, bool bwd, cudaStream_t st) {
-  constexpr int V = VecN<T>::N;
+  // 8-byte channel vectors: with 16-byte ones the backward's per-thread window, gradient window
+  // and weight-gradient sums held the registers of only two CTAs per SM
+  const int VB = 8;
+  const int V = VB / static_cast<int>(sizeof(T));
   const int nrun = (a->T + kConvRun - 1) / kConvRun;
   ConvParams p{a->x, a->w, a->bias, a->y, a->dy, a->dx, static_cast<float*>(a->workspace), a->T, a->C, a->ldx,
                a->ldy, a->lddx, a->activation, nrun};
@@ -536,10 +607,17 @@ int conv_launch(const kata_conv_args* a, bool bwd, cudaStream_t st) {
   const int nvec = a->C / V;
   const int threads = std::min(128, (nvec + 31) / 32 * 32);
   const dim3 grid((nvec + threads - 1) / threads, nrun, a->B);
-#define KATA_CONV_CASE(KK)                                                                    \
-  case KK:                                                                                    \
-    if (bwd) conv_bwd_kernel<T, KK><<<grid, threads, 0, st>>>(p);                             \
-    else conv_fwd_kernel<T, KK><<<grid, threads, 0, st>>>(p);                                 \
+  const size_t ring = static_cast<size_t>(VB) * 2 * kConvU * threads * (bwd ? 2 : 1);  // per-thread cp.async rings
+  const auto go = [&](auto kern) -> int {
+    if (ring > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ring)) != cudaSuccess)
+      return KATA_ERR_CUDA;
+    kern<<<grid, threads, ring, st>>>(p);
+    return KATA_OK;
+  };
+#define KATA_CONV_CASE(KK)                                                                            \
+  case KK:                                                                                            \
+    if (const int e = bwd ? go(conv_bwd_kernel<T, KK, 8>) : go(conv_fwd_kernel<T, KK, 8>)) return e;  \
     break;
   switch (a->K) {
     KATA_CONV_CASE(1)
