@@ -514,6 +514,36 @@ KATA_API int kata_cross_entropy_bwd(const void* logits, const int64_t* targets, 
                                     const float* grad_loss, const float* inv_count, void* dlogits, long long rows,
                                     int V, int dtype, kata_stream_t stream);
 
+/* Residual add + RMSNorm of the LM's hidden stream (fla's fused add-norm between the blocks of the
+ * reference model, kata/modeling.py): forward h_out = h + x (fp32), y = h_out rsqrt(mean h_out^2 + eps) w
+ * in x's dtype (bf16 / f16), rstd per row; backward dh = dh_in + d(RMSNorm)/dh_out (fp32; dh_in may be
+ * NULL), dx = dh in x's dtype (either output may be NULL), dw (fp32, reduced in a fixed order over
+ * kata_add_rmsnorm_bwd_workspace_bytes() of partials).  Rows of N values, N a multiple of 256 up to
+ * 1024; every pointer 16-byte aligned. */
+typedef struct {
+  const float* h;      /* (rows, N) fp32 residual stream          [fwd in]  */
+  const void* x;       /* (rows, N) dtype, the block output       [fwd in]  */
+  const float* w;      /* (N) fp32 norm weight                    [in]      */
+  float* h_out;        /* (rows, N) fp32 h + x    [fwd out; bwd in]         */
+  void* y;             /* (rows, N) dtype normalised              [fwd out] */
+  float* rstd;         /* (rows) fp32             [fwd out; bwd in]         */
+  const void* dy;      /* (rows, N) dtype                         [bwd in]  */
+  const float* dh_in;  /* (rows, N) fp32 gradient of h_out's other uses, or NULL [bwd in] */
+  float* dh;           /* (rows, N) fp32                          [bwd out] */
+  void* dx;            /* (rows, N) dtype                         [bwd out] */
+  float* dw;           /* (N) fp32                                [bwd out] */
+  void* workspace;
+  size_t workspace_bytes;
+  long long rows;
+  int N;
+  int dtype;
+  float eps;
+} kata_add_rmsnorm_args;
+
+KATA_API int kata_add_rmsnorm_fwd(const kata_add_rmsnorm_args* args, kata_stream_t stream);
+KATA_API size_t kata_add_rmsnorm_bwd_workspace_bytes(const kata_add_rmsnorm_args* args);
+KATA_API int kata_add_rmsnorm_bwd(const kata_add_rmsnorm_args* args, kata_stream_t stream);
+
 /* Human-readable name of a KATA_ERR_* code (static storage). */
 KATA_API const char* kata_strerror(int code);
 

@@ -120,6 +120,15 @@ class RowNormArgs(ctypes.Structure):
     ]
 
 
+class AddRmsNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("h", c_void_p), ("x", c_void_p), ("w", c_void_p), ("h_out", c_void_p), ("y", c_void_p), ("rstd", c_void_p),
+        ("dy", c_void_p), ("dh_in", c_void_p), ("dh", c_void_p), ("dx", c_void_p), ("dw", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("rows", ctypes.c_longlong), ("N", c_int),
+        ("dtype", c_int), ("eps", c_float),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -211,6 +220,12 @@ def lib() -> ctypes.CDLL:
             L.kata_cross_entropy_fwd.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_ll, c_int, c_int, c_void_p]
             L.kata_cross_entropy_bwd.restype = c_int
             L.kata_cross_entropy_bwd.argtypes = [c_void_p] * 6 + [c_ll, c_int, c_int, c_void_p]
+            for nm in ("fwd", "bwd"):
+                f = getattr(L, f"kata_add_rmsnorm_{nm}")
+                f.restype = c_int
+                f.argtypes = [ctypes.POINTER(AddRmsNormArgs), c_void_p]
+            L.kata_add_rmsnorm_bwd_workspace_bytes.restype = c_size_t
+            L.kata_add_rmsnorm_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AddRmsNormArgs)]
             if L.kata_abi_version() != ABI_VERSION:
                 raise RuntimeError(f"libkata_b200 ABI {L.kata_abi_version()} != expected {ABI_VERSION}")
             _lib = L

@@ -571,6 +571,151 @@ __global__ void __launch_bounds__(kRowThreads) wide_row_bwd_kernel(RowParams p) 
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// residual add + RMSNorm of the LM's hidden stream (fla's fused add-norm around every mixer / MLP):
+//   h_out = h + x (fp32),  y = h_out * rsqrt(mean h_out^2 + eps) * w (in x's 16-bit type)
+// backward: dh = dh_in + r (w g - xhat <w g, xhat> / N), g = dy, xhat = r h_out; dx = dh in x's type
+// One warp per row, eight values per lane and vector (two float4 of h, one 16-byte vector of x / y);
+// N a multiple of 256.  One pass over each operand in each direction (the unfused form reads and
+// writes the fp32 stream twice more per add).
+// ------------------------------------------------------------------------------------------------
+struct AddNormParams {
+  const float* h;
+  const void* x;
+  const float* w;
+  float* h_out;
+  void* y;
+  float* rstd;
+  const void* dy;
+  const float* dh_in;
+  float* dh;
+  void* dx;
+  float* part;
+  long long rows;
+  int N;
+  float eps;
+};
+
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float (&v)[8]) {
+  uint4 u;
+  T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(v[i]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void st8f(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRowThreads) add_rmsnorm_fwd_kernel(AddNormParams p) {
+  constexpr int RPC = kRowThreads / 32;
+  const int lane = threadIdx.x & 31;
+  for (long long row = static_cast<long long>(blockIdx.x) * RPC + threadIdx.x / 32; row - threadIdx.x / 32 < p.rows;
+       row += static_cast<long long>(gridDim.x) * RPC) {
+    if (row >= p.rows) continue;  // warp-uniform
+    const size_t base = static_cast<size_t>(row) * p.N;
+    float v[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lane + 32 * k) * 8;
+      float xv[8];
+      ld8f(p.h + base + e0, v[k]);
+      ld8<T>(static_cast<const T*>(p.x) + base + e0, xv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[k][j] += xv[j];
+        ss = fmaf(v[k][j], v[k][j], ss);
+      }
+      st8f(p.h_out + base + e0, v[k]);
+    }
+    ss = row_sum<32>(ss);
+    const float r = rsqrtf(ss / p.N + p.eps);
+    if (lane == 0) p.rstd[row] = r;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lane + 32 * k) * 8;
+      float wv[8];
+      ld8f(p.w + e0, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[k][j] *= r * wv[j];
+      st8<T>(static_cast<T*>(p.y) + base + e0, v[k]);
+    }
+  }
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRowThreads) add_rmsnorm_bwd_kernel(AddNormParams p) {
+  constexpr int RPC = kRowThreads / 32;
+  const int lane = threadIdx.x & 31;
+  float dwa[NV][8];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwa[k][j] = 0.f;
+  for (long long row = static_cast<long long>(blockIdx.x) * RPC + threadIdx.x / 32; row - threadIdx.x / 32 < p.rows;
+       row += static_cast<long long>(gridDim.x) * RPC) {
+    if (row >= p.rows) continue;  // warp-uniform
+    const size_t base = static_cast<size_t>(row) * p.N;
+    const float r = p.rstd[row];
+    float g[NV][8], xh[NV][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lane + 32 * k) * 8;
+      float wv[8];
+      ld8<T>(static_cast<const T*>(p.dy) + base + e0, g[k]);
+      ld8f(p.h_out + base + e0, xh[k]);
+      ld8f(p.w + e0, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xh[k][j] *= r;
+        dwa[k][j] = fmaf(g[k][j], xh[k][j], dwa[k][j]);
+        g[k][j] *= wv[j];
+        dot = fmaf(g[k][j], xh[k][j], dot);
+      }
+    }
+    dot = row_sum<32>(dot) / p.N;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lane + 32 * k) * 8;
+      float din[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (p.dh_in) ld8f(p.dh_in + base + e0, din);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) g[k][j] = r * (g[k][j] - xh[k][j] * dot) + din[j];
+      if (p.dh) st8f(p.dh + base + e0, g[k]);
+      if (p.dx) st8<T>(static_cast<T*>(p.dx) + base + e0, g[k]);
+    }
+  }
+  // CTA partial of dw: the RPC warps' lanes hold the same columns; summed in warp order
+  __shared__ float red[RPC][32 * NV * 8];
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[threadIdx.x / 32][(lane + 32 * k) * 8 + j] = dwa[k][j];
+  __syncthreads();
+  for (int e = threadIdx.x; e < p.N; e += kRowThreads) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < RPC; ++w) acc += red[w][e];
+    p.part[static_cast<size_t>(blockIdx.x) * p.N + e] = acc;
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 size_t esize(int dtype) { return dtype == KATA_DTYPE_F32 ? 4 : 2; }
 
@@ -791,4 +936,72 @@ extern "C" int kata_rownorm_bwd(const kata_rownorm_args* a, kata_stream_t stream
     case KATA_DTYPE_F16: return row_launch<__half>(a, true, st);
     default: return row_launch<float>(a, true, st);
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// residual add + RMSNorm
+// ------------------------------------------------------------------------------------------------
+namespace {
+int addnorm_check(const kata_add_rmsnorm_args* a, bool bwd) {
+  if (!a) return KATA_ERR_INVALID;
+  if (a->dtype != KATA_DTYPE_BF16 && a->dtype != KATA_DTYPE_F16) return KATA_ERR_DTYPE;
+  if (a->rows < 0 || a->N < 256 || a->N % 256 || a->N > 1024) return KATA_ERR_SHAPE;
+  if (!a->w || !a->h_out || !a->rstd) return KATA_ERR_INVALID;
+  if (!bwd && (!a->h || !a->x || !a->y)) return KATA_ERR_INVALID;
+  if (bwd && (!a->dy || !a->dw || (!a->dh && !a->dx))) return KATA_ERR_INVALID;
+  const void* ptrs[] = {a->h, a->x, a->w, a->h_out, a->y, a->dy, a->dh_in, a->dh, a->dx};
+  for (const void* q : ptrs)
+    if (q && !aligned16(q)) return KATA_ERR_ALIGN;
+  return KATA_OK;
+}
+
+template <typename T>
+int addnorm_launch(const kata_add_rmsnorm_args* a, bool bwd, cudaStream_t st) {
+  const long long need = (a->rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
+  const int grid = static_cast<int>(std::min<long long>(kRowGrid, std::max<long long>(need, 1)));
+  AddNormParams p{a->h, a->x, a->w, a->h_out, a->y, a->rstd, a->dy, a->dh_in, a->dh, a->dx,
+                  static_cast<float*>(a->workspace), a->rows, a->N, a->eps};
+#define KATA_ADDNORM_CASE(NVV)                                                         \
+  case NVV:                                                                            \
+    if (bwd) add_rmsnorm_bwd_kernel<T, NVV><<<grid, kRowThreads, 0, st>>>(p);          \
+    else add_rmsnorm_fwd_kernel<T, NVV><<<grid, kRowThreads, 0, st>>>(p);              \
+    break;
+  switch (a->N / 256) {
+    KATA_ADDNORM_CASE(1)
+    KATA_ADDNORM_CASE(2)
+    KATA_ADDNORM_CASE(3)
+    KATA_ADDNORM_CASE(4)
+    default: return KATA_ERR_SHAPE;
+  }
+#undef KATA_ADDNORM_CASE
+  if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  if (bwd) {
+    column_sum_kernel<<<(a->N + 31) / 32, 256, 0, st>>>(p.part, grid, a->N, a->dw);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
+  return KATA_OK;
+}
+}  // namespace
+
+extern "C" int kata_add_rmsnorm_fwd(const kata_add_rmsnorm_args* a, kata_stream_t stream) {
+  int e = addnorm_check(a, false);
+  if (e) return e;
+  if (a->rows == 0) return KATA_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return a->dtype == KATA_DTYPE_BF16 ? addnorm_launch<__nv_bfloat16>(a, false, st) : addnorm_launch<__half>(a, false, st);
+}
+
+extern "C" size_t kata_add_rmsnorm_bwd_workspace_bytes(const kata_add_rmsnorm_args* a) {
+  if (!a || a->rows <= 0 || a->N < 1) return 0;
+  const long long need = (a->rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
+  return sizeof(float) * static_cast<size_t>(std::min<long long>(kRowGrid, need)) * a->N;
+}
+
+extern "C" int kata_add_rmsnorm_bwd(const kata_add_rmsnorm_args* a, kata_stream_t stream) {
+  int e = addnorm_check(a, true);
+  if (e) return e;
+  if (a->rows == 0) return KATA_OK;
+  if (!a->workspace || a->workspace_bytes < kata_add_rmsnorm_bwd_workspace_bytes(a)) return KATA_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return a->dtype == KATA_DTYPE_BF16 ? addnorm_launch<__nv_bfloat16>(a, true, st) : addnorm_launch<__half>(a, true, st);
 }

@@ -84,6 +84,58 @@ def _dt(t: torch.Tensor) -> int:
     return _lib.DTYPE[t.dtype]
 
 
+class AddRMSNormFunction(torch.autograd.Function):
+    """(h_out, y) = (h + x, RMSNorm(h + x) * w) on ``kata_add_rmsnorm_*``: the residual add of a block
+    output x (bf16 / f16) into the fp32 hidden stream h, fused with the next RMSNorm, whose output is
+    produced directly in x's dtype for the following GEMMs.  One pass each way."""
+
+    @staticmethod
+    def forward(ctx, h, x, w, eps):
+        dev = _lib.require_cuda(h, x, w)
+        N = h.shape[-1]
+        hc, xc = h.float().contiguous(), x.contiguous()
+        rows = hc.numel() // N
+        h_out = torch.empty_like(hc)
+        y = torch.empty(xc.shape, device=dev, dtype=xc.dtype)
+        rstd = torch.empty(rows, device=dev, dtype=torch.float32)
+        a = _lib.AddRmsNormArgs(h=hc.data_ptr(), x=xc.data_ptr(), w=w.data_ptr(), h_out=h_out.data_ptr(),
+                                y=y.data_ptr(), rstd=rstd.data_ptr(), rows=rows, N=N, dtype=_dt(xc), eps=float(eps))
+        _lib.check(_lib.lib().kata_add_rmsnorm_fwd(a, _lib.stream_handle(dev)), "kata_add_rmsnorm_fwd")
+        ctx.save_for_backward(h_out, rstd, w)
+        ctx.eps, ctx.xdtype = eps, xc.dtype
+        return h_out, y
+
+    @staticmethod
+    def backward(ctx, dh_out, dy):
+        h_out, rstd, w = ctx.saved_tensors
+        dev = h_out.device
+        N = h_out.shape[-1]
+        rows = h_out.numel() // N
+        dyc = (dy if dy is not None else torch.zeros(h_out.shape, device=dev)).to(ctx.xdtype).contiguous()
+        dinc = dh_out.float().contiguous() if dh_out is not None else None
+        dh = torch.empty_like(h_out)
+        dx = torch.empty(h_out.shape, device=dev, dtype=ctx.xdtype)
+        dw = torch.empty_like(w)
+        a = _lib.AddRmsNormArgs(h_out=h_out.data_ptr(), rstd=rstd.data_ptr(), w=w.data_ptr(), dy=dyc.data_ptr(),
+                                dh_in=_lib.ptr(dinc), dh=dh.data_ptr(), dx=dx.data_ptr(), dw=dw.data_ptr(),
+                                rows=rows, N=N, dtype=_lib.DTYPE[ctx.xdtype], eps=float(ctx.eps))
+        L = _lib.lib()
+        nb = L.kata_add_rmsnorm_bwd_workspace_bytes(a)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), nb
+        _lib.check(L.kata_add_rmsnorm_bwd(a, _lib.stream_handle(dev)), "kata_add_rmsnorm_bwd")
+        return dh, dx, dw, None
+
+
+def add_rmsnorm(h: torch.Tensor, x: torch.Tensor, norm: "RMSNorm"):
+    """(h + x, norm(h + x)) with the sum kept in fp32 and the normalised output in x's dtype (fused
+    for 16-bit block outputs and widths that are a multiple of 256; otherwise the add, then ``norm``)."""
+    if x.dtype in (torch.bfloat16, torch.float16) and h.shape[-1] % 256 == 0 and h.shape[-1] <= 1024:
+        return AddRMSNormFunction.apply(h, x, norm.weight, norm.eps)
+    h = h + x
+    return h, norm(h)
+
+
 class SwiGLUFunction(torch.autograd.Function):
     """y = silu(g) * u of a (rows, 2I) tensor [g | u] on ``kata_swiglu_fwd`` / ``_bwd`` (one pass each)."""
 
@@ -200,9 +252,15 @@ class KataLM(nn.Module):
 
     def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None) -> torch.Tensor:
         h = self.model.embeddings(input_ids)
-        for blk in self.model.layers:
-            h = blk(h)
-        logits = self.lm_head(self.model.norm(h))
+        layers = self.model.layers
+        # the blocks' residual adds fused with the RMSNorm that follows each of them (the next
+        # block's or the final norm); the same function as KataBlock.forward applied in turn
+        y = layers[0].attn_norm(h)
+        for i, blk in enumerate(layers):
+            h, y = add_rmsnorm(h, blk.attn(y)[0], blk.mlp_norm)
+            nxt = layers[i + 1].attn_norm if i + 1 < len(layers) else self.model.norm
+            h, y = add_rmsnorm(h, blk.mlp(y), nxt)
+        logits = self.lm_head(y)
         if labels is None:
             return logits
         # next-token targets; the last position of each row has none

@@ -247,6 +247,66 @@ def test_row_norm_wide(dtype, N, norm):
         assert rel(w.grad, wd.grad) < tol
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("N", [256, 768, 1024])
+def test_add_rmsnorm(dtype, N):
+    """Residual add + RMSNorm against PyTorch in float64: h_out, y and the gradients of h, x and w,
+    with gradients arriving both through y and through h_out's other uses."""
+    from linatt_b200.lm import AddRMSNormFunction
+
+    g = torch.Generator(device="cuda").manual_seed(N)
+    rows, eps = 700, 1e-6
+    h = (2 * torch.randn(rows, N, device="cuda", generator=g)).requires_grad_(True)
+    x = torch.randn(rows, N, device="cuda", generator=g).to(dtype).requires_grad_(True)
+    w = (1 + 0.3 * torch.randn(N, device="cuda", generator=g)).requires_grad_(True)
+    h_out, y = AddRMSNormFunction.apply(h, x, w, eps)
+    assert h_out.dtype == torch.float32 and y.dtype == dtype
+    dh_out = torch.randn(rows, N, device="cuda", generator=g)
+    dy = torch.randn(rows, N, device="cuda", generator=g).to(dtype)
+    torch.autograd.backward((h_out, y), (dh_out, dy))
+    hd, xd, wd = (t.detach().double().requires_grad_(True) for t in (h, x, w))
+    s = hd + xd
+    r = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps) * wd
+    torch.autograd.backward((s, r), (dh_out.double(), dy.double()))
+    assert rel(h_out, s) < 1e-6
+    assert rel(y, r) < 1e-2
+    for got, ref, n in ((h.grad, hd.grad, "dh"), (x.grad, xd.grad, "dx"), (w.grad, wd.grad, "dw")):
+        e = rel(got, ref)
+        assert e < (1e-5 if n != "dx" else 1e-2), f"{n}: {e:.3e}"
+
+
+def test_lm_fused_add_norm_matches_the_block_form():
+    """KataLM.forward (residual adds fused with the following RMSNorm) equals the plain block-by-block
+    form (KataBlock.forward, then the final norm) on the same weights: loss and gradients."""
+    from linatt_b200.lm import CrossEntropyFunction, KataLM, KataLMConfig
+
+    torch.manual_seed(1)
+    cfg = KataLMConfig(hidden_size=256, num_hidden_layers=2, num_heads=4, vocab_size=512)
+    model = KataLM(cfg).cuda()
+    ids = torch.randint(0, 512, (2, 256), device="cuda")
+
+    def plain(m, input_ids, labels):
+        h = m.model.embeddings(input_ids)
+        for blk in m.model.layers:
+            h = blk(h)
+        logits = m.lm_head(m.model.norm(h))
+        tgt = torch.cat([labels[:, 1:], torch.full_like(labels[:, :1], -100)], dim=1)
+        return CrossEntropyFunction.apply(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1))
+
+    losses, grads = [], []
+    for fn in (lambda: model(ids, labels=ids), lambda: plain(model, ids, ids)):
+        model.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = fn()
+        loss.backward()
+        losses.append(loss.item())
+        grads.append({n: p.grad.detach().clone() for n, p in model.named_parameters() if p.grad is not None})
+    assert abs(losses[0] - losses[1]) < 1e-4 * abs(losses[1])
+    assert grads[0].keys() == grads[1].keys()
+    for n in grads[0]:
+        assert rel(grads[0][n], grads[1][n]) < 2e-2, n
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_swiglu_and_cross_entropy(dtype):
     """The LM's fused SwiGLU and cross entropy against PyTorch in float64 (values and gradients),
