@@ -86,7 +86,7 @@ struct DkvRingBars {
   uint64_t kv_full;
   uint64_t vec_full[2], vec_empty[2];
   uint64_t ring_full[4], ring_empty[4];
-  uint64_t i_full[2], i_free[2];
+  uint64_t i_full[3], i_free[3];
   uint64_t acc_done, drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -632,8 +632,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kR = 4;  // dO / Q ring depth (two query tiles in flight)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   static_assert(!GRAM || (M == 1 && !SUM && !DECAY && DV <= 64), "Gram features: one linear score part");
-  // Gram features: dK (= d phi(k)) takes kGramFP = 144 columns from 256, dV the last 64
-  constexpr uint32_t kColDK = 256, kColDV = GRAM ? 448 : 384;
+  // TMEM: NS 128-column slots for the items, then dK and dV.  At D = Dv = 64 the accumulators take
+  // 64 columns each, which leaves room for a third slot (three items in flight); Gram features: dK
+  // (= d phi(k)) takes kGramFP = 144 columns from 256, dV the last 64
+  constexpr int NS = (!GRAM && D <= 64 && DV <= 64) ? 3 : 2;
+  constexpr uint32_t kColDK = NS * 128, kColDV = GRAM ? 448 : (NS == 3 ? 448 : 384);
+  static_assert(kColDV + DV <= 512 && kColDK + (GRAM ? kGramFP : D) <= (GRAM ? 448u : kColDV), "TMEM budget");
   using L = BwdSmem<D, DV>;
   static_assert(sizeof(DkvRingBars) <= 256, "barrier block");
   static_assert(L::KR_RING == kR, "ring depth");
@@ -663,6 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.vec_full[i], 1);
       mbar_init(&bars.vec_empty[i], 8);
+    }
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&bars.i_full[i], 1);
       mbar_init(&bars.i_free[i], 8);
     }
@@ -749,28 +755,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t rq0 = kmajor_desc<CW>(sRing, 0, E, 0);    // Q in ring slot 0, K-major
       const uint64_t rqm0 = mnmajor_desc<CW>(sRing, 0, 0);     // Q in ring slot 0, MN-major
       bool ok = mbar_wait_w(&bars.kv_full, 0, wc);
-      // Item `it` = n * kItems + q lives in slot it % 2; before reuse, the pending chains of item
-      // it - 2 are issued.  After the last pair, two claims drain the pending chains.  The ring
+      // Item `it` = n * kItems + q lives in slot it % NS; before reuse, the pending chains of item
+      // it - NS are issued.  After the last pair, NS claims drain the pending chains.  The ring
       // holds dO_n at position 2n and Q_n at 2n + 1 (kR = 4: slot (2n + c) & 3, use parity
       // (n >> 1) & 1).
       static_assert(kR == 4, "ring positions below assume four slots");
       int it = 0, x = 0;
       uint32_t use_par = 0;
-      const int n_claims = nwork * kItems + 2;
+      const int n_claims = nwork * kItems + NS;
       for (int n = 0; ok && it < n_claims; ++n) {
         const int slotO = (2 * n) & 3, slotQ = (2 * n + 1) & 3;
         const uint32_t ring_par = static_cast<uint32_t>(n >> 1) & 1u;
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
           if (it >= n_claims) break;
-          if (it >= 2) {
+          if (it >= NS) {
             if (!mbar_wait_w(&bars.i_free[x], use_par ^ 1, wc)) {
               ok = false;
               break;
             }
-            // item it - 2: type pq and pair n + pdn, both compile-time offsets of (n, q)
-            const int pq = ((q - 2) % kItems + kItems) % kItems;
-            const int pdn = (q - 2 - pq) / kItems;
+            // item it - NS: type pq and pair n + pdn, both compile-time offsets of (n, q)
+            const int pq = ((q - NS) % kItems + kItems) % kItems;
+            const int pdn = (q - NS - pq) / kItems;
             if (pq > 0) {
               const int pn = n + pdn, pp = pq - 1;
               const int ga = SUM ? pp / M : pp, gb = SUM ? pp % M : pp;
@@ -797,7 +803,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (n >= nwork) {
             ++it;
-            if (++x == 2) { x = 0; use_par ^= 1; }
+            if (++x == NS) { x = 0; use_par ^= 1; }
             continue;
           }
           const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
@@ -828,7 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit_w(&bars.i_full[x]);
           }
           ++it;
-          if (++x == 2) {
+          if (++x == NS) {
             x = 0;
             use_par ^= 1;
           }
@@ -871,8 +877,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t dap[32];  // dA'^T of this thread's 64 query columns, bf16 pairs
       {
-        const int x = it & 1;
-        if (!mbar_wait(&bars.i_full[x], (it >> 1) & 1, wc)) {
+        const int x = static_cast<int>(static_cast<unsigned>(it) % NS);  // it >= 0: a mask for NS = 2
+        if (!mbar_wait(&bars.i_full[x], (static_cast<unsigned>(it) / NS) & 1u, wc)) {
           ok = false;
           break;
         }
@@ -920,8 +926,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float2 acc[32];
       for (int pp = 0; pp < NP; ++pp, ++it) {
-        const int x = it & 1;
-        if (!mbar_wait(&bars.i_full[x], (it >> 1) & 1, wc)) {
+        const int x = static_cast<int>(static_cast<unsigned>(it) % NS);  // it >= 0: a mask for NS = 2
+        if (!mbar_wait(&bars.i_full[x], (static_cast<unsigned>(it) / NS) & 1u, wc)) {
           ok = false;
           break;
         }
