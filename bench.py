@@ -944,6 +944,80 @@ def run_delta(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_pairs(args, rank: int, world: int, local: int) -> None:
+    """Cost model of the three tensor-core attention passes: each is timed through the C ABI (CUDA
+    events, 20 launches after 3 warm-up launches) at T = 128 .. 4096 with B*H chosen so that every
+    point runs 3072 CTAs, and time = (a * CTAs + b * tile pairs) / 148 SMs is fitted from the end
+    points: b is the cost of one causal 128 x 128 tile pair, a the cost paid once per CTA.  bf16,
+    concat score, M = --num-groups, D = Dv = --pairs-dim.  One GPU; a diagnostic, not a bench line."""
+    import math
+
+    import torch
+
+    from linatt_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    D = Dv = args.pairs_dim
+    Mg = args.num_groups
+    H = 12
+    pts = []
+    for T in (128, 256, 512, 1024, 2048, 4096):
+        nt = T // 128
+        B = max(1, 3072 // nt // H)
+        g = torch.Generator(device=dev).manual_seed(1)
+        q, k = (torch.randn(B, T, H, D, device=dev, generator=g).div(math.sqrt(D)).bfloat16() for _ in range(2))
+        v, do = (torch.randn(B, T, H, Dv, device=dev, generator=g).bfloat16() for _ in range(2))
+        o = torch.empty(B, T, H, Dv, device=dev, dtype=torch.bfloat16)
+        den = torch.empty(B, T, H, device=dev)
+        sc = 1.0 / math.sqrt(D // Mg)
+        fa = _lib.AttnFwdArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(), den=den.data_ptr(),
+                              dtype=1, B=B, T=T, H=H, HQ=H, D=D, Dv=Dv, M=Mg, score=0, algo=1, scale=sc)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        ba = _lib.AttnBwdArgs(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), o=o.data_ptr(), den=den.data_ptr(),
+                              dout=do.data_ptr(), dq=dq.data_ptr(), dk=dk.data_ptr(), dv=dv.data_ptr(), dtype=1, B=B,
+                              T=T, H=H, HQ=H, D=D, Dv=Dv, M=Mg, score=0, algo=1, scale=sc)
+        nb = L.kata_attn_bwd_workspace_bytes(ba)
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+        ba.workspace, ba.workspace_bytes = ws.data_ptr(), nb
+
+        def call(fn, a, ph=None):
+            if ph is not None:
+                a.phases = ph
+            _lib.check(fn(a, st), "attention pass")
+
+        def timeit(fn, a, ph=None, n=20):
+            for _ in range(3):
+                call(fn, a, ph)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            for _ in range(n):
+                call(fn, a, ph)
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / n * 1e3
+
+        call(L.kata_attn_fwd, fa)
+        call(L.kata_attn_bwd, ba, 1)
+        pts.append(dict(T=T, BH=B * H, ctas=nt * B * H, pairs=B * H * nt * (nt + 1) // 2,
+                        fwd_us=timeit(L.kata_attn_fwd, fa), dq_us=timeit(L.kata_attn_bwd, ba, 1),
+                        dkdv_us=timeit(L.kata_attn_bwd, ba, 2)))
+    fit = {}
+    a0, a1 = pts[0], pts[-1]
+    mhz = 1965.0
+    for kname in ("fwd_us", "dq_us", "dkdv_us"):
+        b = (a1[kname] - a0[kname]) / (a1["pairs"] - a0["pairs"])
+        a = (a0[kname] - a0["pairs"] * b) / a0["ctas"]
+        fit[kname[:-3]] = {"per_pair_us_per_sm": b * 148, "per_pair_cycles": b * 148 * mhz,
+                           "per_cta_us_per_sm": a * 148}
+    if rank == 0:
+        print(json.dumps({"workload": "attention pass cost sweep", "head_dim": D, "num_groups": Mg, "score": "concat",
+                          "dtype": "bf16", "points": pts, "fit": fit, "clock_mhz_assumed": mhz}), flush=True)
+
+
 def run_decode(args, rank: int, world: int, local: int) -> None:
     """Generation step of the concat-score attention on the feature state (kata_attn_decode) at the
     headline geometry: B=16 sequences, H=8, D=Dv=128, M=4, after a T=4096 prefix (whose state is
@@ -1026,7 +1100,8 @@ def main() -> None:
                     help="micro-batch per GPU of --workload lm (config 5 is quoted at 32; smaller only for captures)")
     ap.add_argument("--mixer-batch", type=int, default=32,
                     help="B per GPU of --workload mixer (the config-5 layer is 32; smaller only for captures)")
-    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm", "mixer"], default="attn",
+    ap.add_argument("--pairs-dim", type=int, default=64, help="head dim of --workload pairs (64 or 128)")
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm", "mixer", "pairs"], default="attn",
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
                          "delta: the SPD delta rule at the mixer geometry; decode: one-token generation "
                          "steps on the recurrent feature state; lm: config 5, the KATA LM DDP training step; "
@@ -1062,6 +1137,8 @@ def main() -> None:
         run_lm(args, rank, world, local)
     elif args.workload == "mixer":
         run_mixer(args, rank, world, local)
+    elif args.workload == "pairs":
+        run_pairs(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 
