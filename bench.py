@@ -1018,6 +1018,59 @@ def run_pairs(args, rank: int, world: int, local: int) -> None:
                           "dtype": "bf16", "points": pts, "fit": fit, "clock_mhz_assumed": mhz}), flush=True)
 
 
+def run_varlen(args, rank: int, world: int, local: int) -> None:
+    """Packed documents: fwd+bwd of parallel_kata_attn_varlen on ragged documents (lengths uniform
+    in [64, 4096], seeded, ~64 k tokens; H = 8, D = Dv = 128, concat M = --num-groups, bf16), once
+    through the tensor-core kernels' packed-document form and once through the padded batch, each
+    timed with CUDA events over --steps steps after --warmup.  One GPU; a diagnostic line."""
+    import torch
+    import torch.nn.functional as F
+
+    import linatt_b200.varlen as vl
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(11)
+    lens = []
+    while sum(lens) < 65536:
+        lens.append(int(torch.randint(64, 4097, (1,), generator=g)))
+    T, H, D = sum(lens), 8, 128
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=dev)
+    gd = torch.Generator(device=dev).manual_seed(12)
+    q = (torch.randn(1, T, H, D, device=dev, generator=gd) / D ** 0.5).bfloat16()
+    k = F.normalize(torch.randn(1, T, H, D, device=dev, generator=gd), dim=-1).bfloat16()
+    v = torch.randn(1, T, H, D, device=dev, generator=gd).bfloat16()
+    do = torch.randn(1, T, H, D, device=dev, generator=gd).bfloat16()
+    packed_ok = vl._packed_ok
+
+    def timed(packed: bool) -> float:
+        vl._packed_ok = packed_ok if packed else (lambda *a: False)
+        try:
+            def step():
+                leaves = [x.clone().requires_grad_(True) for x in (q, k, v)]
+                vl.parallel_kata_attn_varlen(*leaves, cu, num_groups=args.num_groups, max_seqlen=max(lens)).backward(do)
+            for _ in range(max(3, args.warmup)):
+                step()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            for _ in range(args.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / args.steps
+        finally:
+            vl._packed_ok = packed_ok
+
+    ms_packed, ms_padded = timed(True), timed(False)
+    if rank == 0:
+        print(json.dumps({"workload": "packed documents, fwd+bwd", "documents": len(lens), "tokens": T,
+                          "max_len": max(lens), "padded_tokens": len(lens) * max(lens), "heads": H, "head_dim": D,
+                          "num_groups": args.num_groups, "dtype": "bf16", "ms_packed": ms_packed,
+                          "ms_padded": ms_padded, "tokens_per_s_packed": T / (ms_packed / 1e3),
+                          "speedup": ms_padded / ms_packed}), flush=True)
+
+
 def run_decode(args, rank: int, world: int, local: int) -> None:
     """Generation step of the concat-score attention on the feature state (kata_attn_decode) at the
     headline geometry: B=16 sequences, H=8, D=Dv=128, M=4, after a T=4096 prefix (whose state is
@@ -1101,7 +1154,8 @@ def main() -> None:
     ap.add_argument("--mixer-batch", type=int, default=32,
                     help="B per GPU of --workload mixer (the config-5 layer is 32; smaller only for captures)")
     ap.add_argument("--pairs-dim", type=int, default=64, help="head dim of --workload pairs (64 or 128)")
-    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm", "mixer", "pairs"], default="attn",
+    ap.add_argument("--workload", choices=["attn", "sp", "gdn", "delta", "decode", "lm", "mixer", "pairs", "varlen"],
+                    default="attn",
                     help="attn: the headline config 3 line; sp: config 4 sequence parallel; gdn: config 2; "
                          "delta: the SPD delta rule at the mixer geometry; decode: one-token generation "
                          "steps on the recurrent feature state; lm: config 5, the KATA LM DDP training step; "
@@ -1139,6 +1193,8 @@ def main() -> None:
         run_mixer(args, rank, world, local)
     elif args.workload == "pairs":
         run_pairs(args, rank, world, local)
+    elif args.workload == "varlen":
+        run_varlen(args, rank, world, local)
     else:
         run_gpu(args, rank, world, local)
 

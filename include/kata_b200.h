@@ -97,6 +97,13 @@ typedef struct {
   void* workspace; /* optional: kata_attn_fwd_workspace_bytes(args) bytes, 16-byte aligned
                       (TC_GRAM only; NULL / 0 -> AUTO runs the parts form) */
   size_t workspace_bytes;
+  const int* cu_seqlens; /* optional packed documents: (num_seqs + 1) int32 device offsets into T,
+                            0 = cu[0] <= cu[1] <= ... <= cu[num_seqs] = T, with B = 1; token t of
+                            document n attends to the tokens s <= t of document n only (the kernels
+                            clamp the offsets into [0, T] and to non-decreasing order, so a malformed
+                            array gives wrong documents but no out-of-bounds access).  Tensor-core
+                            parts form only (bf16 / f16, no decay): KATA_ERR_UNSUPPORTED otherwise */
+  int num_seqs;
 } kata_attn_fwd_args;
 
 KATA_API int kata_attn_fwd(const kata_attn_fwd_args* args, kata_stream_t stream);
@@ -151,6 +158,9 @@ typedef struct {
   int phases;        /* 0 = full backward; 1 = dq pass only (also fills the workspace: delta,
                         1/den, delta/den, dc row part); 2 = dk/dv pass only (needs a prior dq
                         pass on the same workspace).  Splitting lets a caller time each pass. */
+  const int* cu_seqlens; /* optional packed documents, as in kata_attn_fwd_args (the workspace
+                            size depends on num_seqs) */
+  int num_seqs;
 } kata_attn_bwd_args;
 
 KATA_API size_t kata_attn_bwd_workspace_bytes(const kata_attn_bwd_args* args);

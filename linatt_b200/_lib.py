@@ -45,7 +45,7 @@ class AttnFwdArgs(ctypes.Structure):
         ("o", c_void_p), ("den", c_void_p), ("status", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HQ", c_int), ("D", c_int), ("Dv", c_int),
         ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float),
-        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("cu_seqlens", c_void_p), ("num_seqs", c_int),
     ]
 
 
@@ -56,6 +56,7 @@ class AttnBwdArgs(ctypes.Structure):
         ("dc", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("status", c_void_p),
         ("dtype", c_int), ("B", c_int), ("T", c_int), ("H", c_int), ("HQ", c_int), ("D", c_int), ("Dv", c_int),
         ("M", c_int), ("score", c_int), ("algo", c_int), ("scale", c_float), ("phases", c_int),
+        ("cu_seqlens", c_void_p), ("num_seqs", c_int),
     ]
 
 

@@ -36,6 +36,9 @@ struct AttnFwdParams {
   int B, T, H, HQ, D, Dv, M;
   int G;  // HQ / H
   float scale;
+  // packed documents (tensor-core kernels only): nseq + 1 offsets into T (B == 1), or null
+  const int* cu;
+  int nseq;
 };
 
 struct AttnBwdParams {
@@ -59,6 +62,9 @@ struct AttnBwdParams {
   // Internal callers only (not in the C ABI): per-row delta_t given instead of <o_t, dO_t>
   // (o is then not read and may be null).  (B,T,HQ) fp32.
   const float* delta_in;
+  // packed documents (tensor-core kernels only): nseq + 1 offsets into T (B == 1), or null
+  const int* cu;
+  int nseq;
 };
 
 }  // namespace kata

@@ -49,8 +49,10 @@ struct BwdWs {
   float* cT;
   int Tp;
 };
-__host__ __device__ inline BwdWs ws_views(float* base, int B, int T, int HQ) {
-  const int Tp = (T + 127) & ~127;
+// With packed documents (nseq > 0) the head-major vectors are indexed by tile number * 128 + row
+// (Tp covers the tile bound), so every tile's 128 values stay one aligned run.
+__host__ __device__ inline BwdWs ws_views(float* base, int B, int T, int HQ, int nseq = 0) {
+  const int Tp = nseq > 0 ? varlen_tile_bound(T, nseq) * 128 : (T + 127) & ~127;
   const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
   const size_t n1 = static_cast<size_t>(B) * HQ * Tp;
   return BwdWs{base, base + n0, base + n0 + n1, base + n0 + 2 * n1, Tp};
@@ -145,7 +147,7 @@ struct DqRingBars {
   float xch_delta[2][kTile];  // halves of delta_t; with decay, at the end, halves of the dc row sums
 };
 
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM, bool VAR>
 __global__ void __launch_bounds__(kThreadsRing, 1)
     attn_bwd_dq_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -170,13 +172,36 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ DqRingBars bars;
+  __shared__ SeqTile seq;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T_ = p.T;
-  const int nqt = (T_ + kTile - 1) / kTile;
-  const int qi = nqt - 1 - static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y, b = bh / p.HQ, hq = bh % p.HQ, h = hq / p.G;
-  const int t0 = qi * kTile;
+  const int bh = blockIdx.y, hq = bh % p.HQ, h = hq / p.G;
+  // query tile qi of a sequence with rows [kbase, t_end) of batch b (packed documents: the tile's
+  // document, B == 1; past the last tile the CTA exits before it allocates anything); vt0 = the
+  // tile's first row in the head-major per-query vectors
+  int qi, b, kbase, t_end, vt0;
+  if constexpr (VAR) {
+    if (warp == 0) {
+      SeqTile st{};
+      const bool have = varlen_tile(p.cu, p.nseq, T_, static_cast<int>(blockIdx.x), st);
+      if (lane == 0) seq = have ? st : SeqTile{0, 0, -1, 0, 0};
+    }
+    __syncthreads();
+    if (seq.j < 0) return;
+    qi = seq.j;
+    b = 0;
+    kbase = seq.start;
+    t_end = seq.end;
+    vt0 = (seq.base + seq.j) * kTile;
+  } else {
+    qi = (T_ + kTile - 1) / kTile - 1 - static_cast<int>(blockIdx.x);
+    b = bh / p.HQ;
+    kbase = 0;
+    t_end = T_;
+    vt0 = qi * kTile;
+  }
+  const int t0 = kbase + qi * kTile;
   const int nk = qi + 1;
   WaitCtx wc{p.status, &bars.abort_flag};
 
@@ -230,13 +255,13 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
           if (item == 0) {
             mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
             for (int bx = 0; bx < NVBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmV, &bars.ring_full[slot], bx * VCW, h, j * kTile, b);
+              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmV, &bars.ring_full[slot], bx * VCW, h, kbase + j * kTile, b);
           } else {
             // with decay, the key tile's c (head-major copy) rides with K_j, whose slot is held
             // until the tile's last dQ chain, i.e. after the compute warps have read it
             mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES + (DECAY ? kTile * 4 : 0));
             for (int bx = 0; bx < NBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, j * kTile, b);
+              tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, kbase + j * kTile, b);
             if (DECAY)
               bulk_load(smem + L::DQ_OFF_C + slot * (kTile * 4),
                         ws_views(p.delta, p.B, T_, p.HQ).cT + (static_cast<size_t>(b) * p.HQ + hq) *
@@ -379,10 +404,10 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int tg = t0 + row;
-    const bool live = tg < T_;
+    const bool live = tg < t_end;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     const size_t rowidx = (static_cast<size_t>(b) * T_ + tg) * p.HQ + hq;  // (b, tg, hq)
-    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
+    const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ, VAR ? p.nseq : 0);
     // ---- delta_t = <o_t, dO_t> over this thread's half of Dv, then exchanged
     float dpart = 0.f;
     if (live && p.delta_in) {
@@ -413,10 +438,11 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
     if (hc == 0) {  // every row of the tile, including rows past T (rden 1, delta 0)
       // For the ring dk/dv kernel, pre-scaled: scale^2 / den and -scale^2 delta / den, so that
       // there P^T = sum S^2 * v0 and dA''^T = dN * v0 + v1 are one packed op each (dK is doubled
-      // in its epilogue: W = 2 S dA'').
-      const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + tg;  // head-major (b, hq, t)
+      // in its epilogue: W = 2 S dA'').  Rows past a packed document's end hold the next
+      // document's tokens (not zeros as past T), so their v0 is 0 as well: no P, no dA.
+      const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + vt0 + row;  // head-major (b, hq, t)
       const float scale2 = p.scale * p.scale;
-      ws.rden[hm] = rden * scale2;
+      ws.rden[hm] = live || !VAR ? rden * scale2 : 0.f;
       ws.dr[hm] = live ? -delta * rden * scale2 : 0.f;
     }
     const float w_scale = GRAM ? 1.f : 2.f * p.scale * p.scale;  // Gram: W = dA (linear score)
@@ -617,7 +643,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
 // other half (columns [32,64) and [96,128)).  The issuer reuses a slot only after the compute warps
 // release it, issuing first the dK chain of the W it holds (and, for the last part, the dV chain of
 // P) as tensor-memory-operand MMAs; MMAs of one CTA execute in issue order.
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM, bool VAR>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_dkdv_ring_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -651,14 +677,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Packed documents (VAR): the key tile's document (B == 1), in the last bytes of the 256-byte
+  // barrier block; the regular kernel never touches it.  Past the last tile the CTA exits before it
+  // allocates anything.
+  SeqTile& seq = *reinterpret_cast<SeqTile*>(smem + L::kr_off_bars(DECAY) + 256 - sizeof(SeqTile));
+  static_assert(sizeof(DkvRingBars) + sizeof(SeqTile) <= 256, "barrier block");
+  if constexpr (VAR) {
+    if (warp == 0) {
+      SeqTile st{};
+      const bool have = varlen_tile(p.cu, p.nseq, p.T, static_cast<int>(blockIdx.x), st);
+      if (lane == 0) seq = have ? st : SeqTile{0, 0, -1, 0, 0};
+    }
+    __syncthreads();
+    if (seq.j < 0) return;
+  }
   const int T_ = p.T;
   const int nqt = (T_ + kTile - 1) / kTile;
-  const int kj = static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
-  const int s0 = kj * kTile;
-  const int nq = nqt - kj;
+  const int kj = VAR ? seq.j : static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y, b = VAR ? 0 : bh / p.H, h = bh % p.H;
+  const int s0 = (VAR ? seq.start : 0) + kj * kTile;
+  const int nq = (VAR ? seq.ntiles : nqt) - kj;
   const int nwork = p.G * nq;
-  const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ);
+  const BwdWs ws = ws_views(p.delta, p.B, T_, p.HQ, VAR ? p.nseq : 0);
   WaitCtx wc{p.status, &bars.abort_flag};
 
   if (threadIdx.x == 0) {
@@ -705,13 +745,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int n = 0; n < nwork && ok; ++n) {
         const int hq = h * p.G + n / nq;
-        const int ti = (kj + n % nq) * kTile;
+        const int ti = (kj + n % nq) * kTile;  // within the sequence (packed: from its first row)
         const int vs = n & 1;
         if (!mbar_wait(&bars.vec_empty[vs], ((n >> 1) & 1) ^ 1, wc)) {
           ok = false;
           break;
         }
-        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + ti;
+        const size_t hm = (static_cast<size_t>(b) * p.HQ + hq) * ws.Tp + ti + (VAR ? seq.base * kTile : 0);
         mbar_arrive_expect_tx(&bars.vec_full[vs], (DECAY ? 3 : 2) * kTile * 4);
         bulk_load(vec + (vs * kNV + 0) * kTile, ws.rden + hm, kTile * 4, &bars.vec_full[vs]);
         bulk_load(vec + (vs * kNV + 1) * kTile, ws.dr + hm, kTile * 4, &bars.vec_full[vs]);
@@ -727,11 +767,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (item == 0) {
             mbar_arrive_expect_tx(&bars.ring_full[slot], L::O_BYTES);
             for (int bx = 0; bx < NVBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmO, &bars.ring_full[slot], bx * VCW, hq, ti, b);
+              tma_load_4d(dst + bx * (kTile * VCW * 2), &tmO, &bars.ring_full[slot], bx * VCW, hq,
+                          ti + (VAR ? seq.start : 0), b);
           } else {
             mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES);
             for (int bx = 0; bx < NBOX; ++bx)
-              tma_load_4d(dst + bx * (kTile * CW * 2), &tmQ, &bars.ring_full[slot], bx * CW, hq, ti, b);
+              tma_load_4d(dst + bx * (kTile * CW * 2), &tmQ, &bars.ring_full[slot], bx * CW, hq,
+                          ti + (VAR ? seq.start : 0), b);
           }
         }
       }
@@ -850,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // key row within the tile
     const int sg = s0 + row;
-    const bool live = sg < T_;
+    const bool live = sg < (VAR ? seq.end : T_);
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(quarter * 32) << 16);
     // The vectors hold v0 = scale^2 / den and v1 = -scale^2 delta / den per query (written by the
     // dq pass), so dA''^T = dN^T v0 + v1 and P^T = v0 sum_p (S^T_p)^2; W''^T_p = S^T_p dA''^T is
@@ -1076,7 +1118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ================================================================================================
 // host side
 // ================================================================================================
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM = false>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM = false, bool VAR = false>
 int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   constexpr int E = D / M;
   constexpr int CW = ScoreBoxW<E, GRAM>::value;
@@ -1096,22 +1138,22 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   }
   if (p.phases != 2) {
     // dq pass: tensor-memory ring with two issuers (decay: dc row sums written here)
-    auto kern = attn_bwd_dq_ring_tc<T, D, DV, M, SUM, DECAY, GRAM>;
+    auto kern = attn_bwd_dq_ring_tc<T, D, DV, M, SUM, DECAY, GRAM, VAR>;
     const size_t smem = L::dqr_total(DECAY) + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
-    kern<<<dim3(nt, p.B * p.HQ), kThreadsRing, smem, st>>>(tq, tk, tv, to, p);
+    kern<<<dim3(VAR ? varlen_tile_bound(p.T, p.nseq) : nt, p.B * p.HQ), kThreadsRing, smem, st>>>(tq, tk, tv, to, p);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   if (p.phases != 1) {
     // dk/dv pass: tensor-memory ring (decay: dc column sums added here)
-    auto kern = attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM, DECAY, GRAM>;
+    auto kern = attn_bwd_dkdv_ring_tc<T, D, DV, M, SUM, DECAY, GRAM, VAR>;
     const size_t smem = L::kr_total(DECAY);  // no static shared memory: no alignment slack
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return KATA_ERR_CUDA;
-    kern<<<dim3(nt, p.B * p.H), kThreads, smem, st>>>(tq, tk, tv, to, p);
+    kern<<<dim3(VAR ? varlen_tile_bound(p.T, p.nseq) : nt, p.B * p.H), kThreads, smem, st>>>(tq, tk, tv, to, p);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   return KATA_OK;
@@ -1120,12 +1162,15 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
 template <typename T, int D, int DV, int M>
 int bwd_variant(const AttnBwdParams& p, bool sum, cudaStream_t st) {
   const bool dec = p.c != nullptr;
+  // packed documents (p.cu): the VAR instantiations (no decay, checked by the caller)
   if (sum) {
     if constexpr (M * M <= 16) {
-      if (!dec) return launch_bwd<T, D, DV, M, true, false>(p, st);
+      if (!dec)
+        return p.cu ? launch_bwd<T, D, DV, M, true, false, false, true>(p, st) : launch_bwd<T, D, DV, M, true, false>(p, st);
     }
     return KATA_ERR_UNSUPPORTED;
   }
+  if (p.cu) return dec ? KATA_ERR_UNSUPPORTED : launch_bwd<T, D, DV, M, false, false, false, true>(p, st);
   return dec ? launch_bwd<T, D, DV, M, false, true>(p, st) : launch_bwd<T, D, DV, M, false, false>(p, st);
 }
 
@@ -1153,8 +1198,9 @@ int bwd_dims(const AttnBwdParams& p, bool sum, cudaStream_t st) {
 
 }  // namespace
 
-size_t tc_bwd_workspace_bytes(int B, int T, int HQ, bool decay) {
-  const size_t Tp = (static_cast<size_t>(T) + 127) & ~static_cast<size_t>(127);
+size_t tc_bwd_workspace_bytes(int B, int T, int HQ, bool decay, int nseq) {
+  const size_t Tp = nseq > 0 ? static_cast<size_t>(varlen_tile_bound(T, nseq)) * 128
+                             : (static_cast<size_t>(T) + 127) & ~static_cast<size_t>(127);
   const size_t n0 = (static_cast<size_t>(B) * T * HQ + 3) & ~static_cast<size_t>(3);
   return sizeof(float) * (n0 + (decay ? 3 : 2) * static_cast<size_t>(B) * HQ * Tp);
 }

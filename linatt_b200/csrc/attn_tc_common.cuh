@@ -104,6 +104,59 @@ struct BoxW {
   static constexpr int value = W < 64 ? W : 64;
 };
 
+// Packed documents (cu_seqlens): every document is cut into its own 128-row tiles, and the tiles of
+// all documents are numbered in document order.  Tile `tile` -> its document's first and one-past-
+// last row, the tile's index j inside the document, the document's tile count and the number of
+// the document's first tile.  The whole warp calls it with the same arguments (a 32-wide scan over
+// the documents: running maximum of the offsets, tile counts, an inclusive prefix sum by shuffles,
+// a ballot for the owner); false past the last tile.  Zero-length documents own no tile.  The
+// offsets are normalised on the fly: each is clamped to [0, T] and raised to the largest offset
+// before it, so the documents come out disjoint, ordered and inside [0, T] whatever the array holds
+// (a valid array is unchanged) and every tile, row and vector index stays in bounds.
+struct SeqTile {
+  int start, end, j, ntiles, base;
+};
+__device__ __forceinline__ bool varlen_tile(const int* cu, int nseq, int T, int tile, SeqTile& out) {
+  const int lane = threadIdx.x & 31;
+  int base = 0;                       // tiles of the documents before this group of 32
+  int carry = min(max(cu[0], 0), T);  // largest offset so far
+  for (int n0 = 0; n0 < nseq; n0 += 32) {
+    const int n = n0 + lane;
+    int e = n < nseq ? min(max(cu[n + 1], 0), T) : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {  // inclusive running maximum over the lanes
+      const int v = __shfl_up_sync(0xffffffffu, e, o);
+      if (lane >= o) e = max(e, v);
+    }
+    e = max(e, carry);
+    int s = __shfl_up_sync(0xffffffffu, e, 1);
+    if (lane == 0) s = carry;
+    const int nt = n < nseq ? (e - s + kTile - 1) / kTile : 0;
+    int incl = nt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int excl = incl - nt;
+    const unsigned own = __ballot_sync(0xffffffffu, nt > 0 && tile >= base + excl && tile < base + incl);
+    if (own) {
+      const int src = __ffs(own) - 1;
+      out.start = __shfl_sync(0xffffffffu, s, src);
+      out.end = __shfl_sync(0xffffffffu, e, src);
+      out.ntiles = __shfl_sync(0xffffffffu, nt, src);
+      out.base = base + __shfl_sync(0xffffffffu, excl, src);
+      out.j = tile - out.base;
+      return true;
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+    carry = __shfl_sync(0xffffffffu, e, 31);
+  }
+  return false;
+}
+// Upper bound on the tiles of T packed rows in nseq documents (each document wastes < 1 tile).
+__host__ __device__ inline int varlen_tile_bound(int T, int nseq) { return (T + kTile - 1) / kTile + nseq; }
+
 // Sum score on Gram features.  With groups of E = 16 (D = 16 M) the sum score is a linear score
 //   A[t,s] = scale^2 sum_{a,b} (q_a . k_b)^2 = scale^2 <G(q_t), G(k_s)>_F = <phi(q_t), phi(k_s)>,
 //   G(x) = sum_a x_a x_a^T (16 x 16, symmetric),  phi(x)_(e,f) = scale c_ef G(x)_ef  (e <= f,

@@ -59,7 +59,7 @@ struct FwdBarriers {
   alignas(16) float den_x[2][kBT];  // partial row sums of the two column halves (decay: c staging)
 };
 
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM, bool VAR>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
@@ -76,13 +76,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ FwdBarriers bars;
+  __shared__ SeqTile seq;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T_ = p.T;
-  const int nqt = (T_ + kBT - 1) / kBT;
-  const int qt = nqt - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
-  const int bh = blockIdx.y, b = bh / p.HQ, hq = bh % p.HQ, h = hq / p.G;
-  const int t0 = qt * kBT;
+  const int bh = blockIdx.y, hq = bh % p.HQ, h = hq / p.G;
+  // Rows of this CTA: query tile qt of a sequence whose rows are [kbase, t_end) of batch b; its key
+  // tiles 0..qt start at kbase.  Packed documents: the tile's document (B == 1; past the last tile
+  // the CTA exits before it allocates anything).
+  int qt, b, kbase, t_end;
+  if constexpr (VAR) {
+    if (warp == 0) {
+      SeqTile st{};
+      const bool have = varlen_tile(p.cu, p.nseq, T_, static_cast<int>(blockIdx.x), st);
+      if (lane == 0) seq = have ? st : SeqTile{0, 0, -1, 0, 0};
+    }
+    __syncthreads();
+    if (seq.j < 0) return;
+    qt = seq.j;
+    b = 0;
+    kbase = seq.start;
+    t_end = seq.end;
+  } else {
+    qt = (T_ + kBT - 1) / kBT - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
+    b = bh / p.HQ;
+    kbase = 0;
+    t_end = T_;
+  }
+  const int t0 = kbase + qt * kBT;
   const int nk = qt + 1;  // causal: key tiles 0..qt
   WaitCtx wc{p.status, &bars.abort_flag};
 
@@ -131,13 +152,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&bars.k_full[st], L::K_BYTES);
         uint8_t* sk = smem + L::OFF_K + st * L::K_BYTES;
         for (int bx = 0; bx < NBOX; ++bx)
-          tma_load_4d(sk + bx * (kBK * CW * 2), &tmK, &bars.k_full[st], bx * CW, h, j * kBK, b);
+          tma_load_4d(sk + bx * (kBK * CW * 2), &tmK, &bars.k_full[st], bx * CW, h, kbase + j * kBK, b);
         issued_k = j + 1;
         if (!mbar_wait(&bars.v_empty[st], ph ^ 1, wc)) break;
         mbar_arrive_expect_tx(&bars.v_full[st], L::V_BYTES);
         uint8_t* sv = smem + L::OFF_V + st * L::V_BYTES;
         for (int bx = 0; bx < NVBOX; ++bx)
-          tma_load_4d(sv + bx * (kBK * VCW * 2), &tmV, &bars.v_full[st], bx * VCW, h, j * kBK, b);
+          tma_load_4d(sv + bx * (kBK * VCW * 2), &tmV, &bars.v_full[st], bx * VCW, h, kbase + j * kBK, b);
         issued_v = j + 1;
       }
       if (*wc.abort) {
@@ -263,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (DECAY) {
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const int s0 = j * kBK + hc * 64 + h2 * 32 + lane;
+          const int s0 = kbase + j * kBK + hc * 64 + h2 * 32 + lane;
           cpre[h2] = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
         }
       }
@@ -309,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc[i] = fmul2(acc[i], sc2);
       }
-      const int s_base = j * kBK + hc * 64;
+      const int s_base = kbase + j * kBK + hc * 64;
       if (j == qt) {  // diagonal tile: causal mask
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -388,12 +409,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv = 1.f / (den_o > 0.f ? den_o : 1.f);
       constexpr int HALF = DV / 2;
       T* orow = static_cast<T*>(p.o) + ((static_cast<size_t>(b) * T_ + t) * p.HQ + hq) * DV + hc * HALF;
+      const bool live = t < t_end;
 #pragma unroll
       for (int c0 = 0; c0 < HALF; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(lane_addr + kOCol + hc * HALF + c0, r);
         tmem_wait_ld();
-        if (t < T_) {
+        if (live) {
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
             uint4 w;
@@ -405,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (hc == 0 && t < T_) p.den[(static_cast<size_t>(b) * T_ + t) * p.HQ + hq] = den_all;
+      if (hc == 0 && live) p.den[(static_cast<size_t>(b) * T_ + t) * p.HQ + hq] = den_all;
     }
   }
   tc_fence_before();
@@ -413,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tbase, 512);
 }
 
-template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM = false>
+template <typename T, int D, int DV, int M, bool SUM, bool DECAY, bool GRAM = false, bool VAR = false>
 int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
   constexpr int E = D / M;
   constexpr int CW = ScoreBoxW<E, GRAM>::value;
@@ -424,10 +446,11 @@ int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
   if (!e) e = make_tm_tokens(&tv, p.v, p.B, p.T, p.H, DV, VCW);
   if (e) return e;
   const size_t smem = FwdSmem<D, DV>::TOTAL + 1024;
-  auto kern = attn_fwd_tc<T, D, DV, M, SUM, DECAY, GRAM>;
+  auto kern = attn_fwd_tc<T, D, DV, M, SUM, DECAY, GRAM, VAR>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return KATA_ERR_CUDA;
-  const dim3 grid((p.T + kBT - 1) / kBT, p.B * p.HQ);
+  const int ntiles = VAR ? varlen_tile_bound(p.T, p.nseq) : (p.T + kBT - 1) / kBT;
+  const dim3 grid(ntiles, p.B * p.HQ);
   kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
   return from_cuda(cudaGetLastError());
 }
@@ -435,13 +458,16 @@ int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
 template <typename T, int D, int DV, int M>
 int dispatch_variant(const AttnFwdParams& p, bool sum, cudaStream_t st) {
   const bool dec = p.c != nullptr;
+  // packed documents (p.cu): the VAR instantiations (no decay, checked by the caller)
   if (sum) {
     // the reference pairs decay with the concat score only (kata/layer.py:187-193)
     if constexpr (M * M <= 16) {
-      if (!dec) return launch_fwd<T, D, DV, M, true, false>(p, st);
+      if (!dec)
+        return p.cu ? launch_fwd<T, D, DV, M, true, false, false, true>(p, st) : launch_fwd<T, D, DV, M, true, false>(p, st);
     }
     return KATA_ERR_UNSUPPORTED;
   }
+  if (p.cu) return dec ? KATA_ERR_UNSUPPORTED : launch_fwd<T, D, DV, M, false, false, false, true>(p, st);
   return dec ? launch_fwd<T, D, DV, M, false, true>(p, st) : launch_fwd<T, D, DV, M, false, false>(p, st);
 }
 

@@ -84,7 +84,8 @@ def _warn_if_simt(a, dt) -> None:
         "kernels (much slower)", RuntimeWarning, stacklevel=4)
 
 
-def _fwd(q, k, v, num_groups, scale, score, c=None):
+def _fwd(q, k, v, num_groups, scale, score, c=None, cu=None):
+    """cu: optional (N+1) int32 device offsets of packed documents along T (B = 1)."""
     dev = _lib.require_cuda(q, k, v, c)
     B, T, HQ, d_k = q.shape
     H = k.shape[2]
@@ -112,7 +113,8 @@ def _fwd(q, k, v, num_groups, scale, score, c=None):
     a = _lib.AttnFwdArgs(
         q=qc.data_ptr(), k=kc.data_ptr(), v=vc.data_ptr(), c=_lib.ptr(cc), o=o.data_ptr(), den=den.data_ptr(),
         status=st.data_ptr(), dtype=_lib.DTYPE[dt], B=B, T=T, H=H, HQ=HQ, D=d_k, Dv=d_v, M=num_groups,
-        score=_lib.SCORE[score], algo=_lib.ALGO[ALGO], scale=float(scale))
+        score=_lib.SCORE[score], algo=_lib.ALGO[ALGO], scale=float(scale),
+        cu_seqlens=_lib.ptr(cu), num_seqs=0 if cu is None else cu.numel() - 1)
     _warn_if_simt(a, dt)
     L = _lib.lib()
     nbytes = L.kata_attn_fwd_workspace_bytes(a)  # Gram features of the sum score, else 0
@@ -127,7 +129,7 @@ def _fwd(q, k, v, num_groups, scale, score, c=None):
     return o, den
 
 
-def _bwd(q, k, v, o, den, do, num_groups, scale, score, c=None):
+def _bwd(q, k, v, o, den, do, num_groups, scale, score, c=None, cu=None):
     dev = _lib.require_cuda(q, k, v, o, den, do, c)
     B, T, HQ, d_k = q.shape
     H = k.shape[2]
@@ -150,7 +152,7 @@ def _bwd(q, k, v, o, den, do, num_groups, scale, score, c=None):
         dout=doc.data_ptr(), c=_lib.ptr(cc), dq=dq.data_ptr(), dk=dk.data_ptr(), dv=dv.data_ptr(),
         dc=_lib.ptr(dc), workspace=None, workspace_bytes=0, status=st.data_ptr(), dtype=_lib.DTYPE[dt],
         B=B, T=T, H=H, HQ=HQ, D=d_k, Dv=d_v, M=num_groups, score=_lib.SCORE[score], algo=_lib.ALGO[ALGO],
-        scale=float(scale))
+        scale=float(scale), cu_seqlens=_lib.ptr(cu), num_seqs=0 if cu is None else cu.numel() - 1)
     L = _lib.lib()
     nbytes = L.kata_attn_bwd_workspace_bytes(a)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)

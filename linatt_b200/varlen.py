@@ -6,17 +6,25 @@ Documents are packed along T as (1, T_total, H, D) with ``cu_seqlens`` = [0, l_0
 (``kata/kernels/parallel_kata_hopper.py:18-44``).  Token t of document n attends to the tokens
 s <= t of document n only.
 
-Each document is scattered into its own row of a zero-padded (N, T_max, H, D) batch, the flash
-kernels run on that batch, and the rows are gathered back.  Padding sits after each document's
-last token, so causality keeps it out of every real row: the outputs and gradients equal those of
-one call per document.  The cost is the padding (sum of T_max - l_n tokens) and one scatter /
-gather pass over q, k, v, o (and their gradients); the gradients flow through the index ops.
+On the tensor-core kernels (bf16 / f16 inputs in their envelope, no decay) the documents go to the
+kernels as they lie: each CTA takes one 128-row tile of one document (the tiles of all documents
+numbered in document order, ``cu_seqlens`` read on the device), its key tiles start at the
+document's first row, and rows past the document's end are masked (their outputs are not written,
+and in the backward their per-query vectors are zero).  No padding and no scatter / gather pass.
+
+Otherwise (fp32, decay, shapes outside that envelope) each document is scattered into its own row
+of a zero-padded (N, T_max, H, D) batch, the flash kernels run on that batch, and the rows are
+gathered back.  Padding sits after each document's last token, so causality keeps it out of every
+real row: the outputs and gradients equal those of one call per document.  The cost is the padding
+(sum of T_max - l_n tokens) and one scatter / gather pass over q, k, v, o (and their gradients).
 """
 
 from __future__ import annotations
 
 import torch
 
+from . import _lib
+from . import parallel_kata_attn as _pka
 from .parallel_kata_attn import parallel_kata_attn, parallel_kata_attn_decay, parallel_kata_attn_sum
 
 __all__ = ["varlen_index", "pack_rows", "unpack_rows", "parallel_kata_attn_varlen"]
@@ -53,6 +61,35 @@ def unpack_rows(y: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
     return y.reshape((-1,) + tuple(y.shape[2:])).index_select(0, dst).unsqueeze(0)
 
 
+class _PackedKataFunction(torch.autograd.Function):
+    """Packed documents straight through the tensor-core kernels (``cu_seqlens`` on the device)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cu, num_groups, scale, score):
+        o, den = _pka._fwd(q, k, v, num_groups, scale, score, cu=cu)
+        ctx.save_for_backward(q, k, v, o, den, cu)
+        ctx.num_groups, ctx.scale, ctx.score = num_groups, scale, score
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, den, cu = ctx.saved_tensors
+        dq, dk, dv, _ = _pka._bwd(q, k, v, o, den, do, ctx.num_groups, ctx.scale, ctx.score, cu=cu)
+        return dq, dk, dv, None, None, None, None
+
+
+def _packed_ok(q, k, v, num_groups, score, c, nseq) -> bool:
+    """True when the tensor-core kernels take the packed documents as they lie."""
+    if c is not None or _pka.ALGO in ("simt", "tc_gram") or q.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    if k.dtype != q.dtype or v.dtype != q.dtype or not q.is_cuda or nseq < 1:
+        return False
+    a = _lib.AttnFwdArgs(dtype=_lib.DTYPE[q.dtype], B=1, T=max(q.shape[1], 1), H=k.shape[2], HQ=q.shape[2],
+                         D=q.shape[-1], Dv=v.shape[-1], M=num_groups, score=_lib.SCORE[score],
+                         algo=_lib.ALGO["tc"], scale=1.0, cu_seqlens=1, num_seqs=nseq)
+    return _lib.lib().kata_attn_algo(a) == _lib.ALGO["tc"]
+
+
 def parallel_kata_attn_varlen(q, k, v, cu_seqlens, num_groups=4, scale=None, score="concat", c=None,
                               max_seqlen=None):
     """Causal KATA-SPD attention over packed documents.
@@ -86,6 +123,10 @@ def parallel_kata_attn_varlen(q, k, v, cu_seqlens, num_groups=4, scale=None, sco
             raise ValueError(f"cu_seqlens covers {int(cpu[-1])} tokens, q has {q.shape[1]}")
         if max_seqlen is not None and int(lens.max()) > int(max_seqlen):
             raise ValueError(f"max_seqlen {max_seqlen} is below the longest document ({int(lens.max())})")
+    nseq = cu_seqlens.numel() - 1
+    if q.shape[1] > 0 and _packed_ok(q, k, v, num_groups, score, c, nseq):
+        cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+        return _PackedKataFunction.apply(q, k, v, cu, num_groups, scale, score)
     dst, N, T_max = varlen_index(cu_seqlens.to(q.device), max_seqlen, total=q.shape[1])
     qp, kp, vp = (pack_rows(x, dst, N, T_max) for x in (q, k, v))
     if c is not None:
