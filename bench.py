@@ -1020,7 +1020,8 @@ def run_pairs(args, rank: int, world: int, local: int) -> None:
 
 def run_varlen(args, rank: int, world: int, local: int) -> None:
     """Packed documents: fwd+bwd of parallel_kata_attn_varlen on ragged documents (lengths uniform
-    in [64, 4096], seeded, ~64 k tokens; H = 8, D = Dv = 128, concat M = --num-groups, bf16), once
+    in [64, 4096], seeded, ~64 k tokens; H = 8, D = Dv = 128, concat M = --num-groups, bf16; with
+    --decay a per-token log-decay c as in the tests), once
     through the tensor-core kernels' packed-document form and once through the padded batch, each
     timed with CUDA events over --steps steps after --warmup.  One GPU; a diagnostic line."""
     import torch
@@ -1041,6 +1042,7 @@ def run_varlen(args, rank: int, world: int, local: int) -> None:
     k = F.normalize(torch.randn(1, T, H, D, device=dev, generator=gd), dim=-1).bfloat16()
     v = torch.randn(1, T, H, D, device=dev, generator=gd).bfloat16()
     do = torch.randn(1, T, H, D, device=dev, generator=gd).bfloat16()
+    c = -F.softplus(torch.randn(1, T, H, device=dev, generator=gd)).cumsum(1) if args.decay else None
     packed_ok = vl._packed_ok
 
     def timed(packed: bool) -> float:
@@ -1048,7 +1050,9 @@ def run_varlen(args, rank: int, world: int, local: int) -> None:
         try:
             def step():
                 leaves = [x.clone().requires_grad_(True) for x in (q, k, v)]
-                vl.parallel_kata_attn_varlen(*leaves, cu, num_groups=args.num_groups, max_seqlen=max(lens)).backward(do)
+                cc = None if c is None else c.clone().requires_grad_(True)
+                vl.parallel_kata_attn_varlen(*leaves, cu, num_groups=args.num_groups, max_seqlen=max(lens),
+                                             c=cc).backward(do)
             for _ in range(max(3, args.warmup)):
                 step()
             torch.cuda.synchronize()
@@ -1066,7 +1070,7 @@ def run_varlen(args, rank: int, world: int, local: int) -> None:
     if rank == 0:
         print(json.dumps({"workload": "packed documents, fwd+bwd", "documents": len(lens), "tokens": T,
                           "max_len": max(lens), "padded_tokens": len(lens) * max(lens), "heads": H, "head_dim": D,
-                          "num_groups": args.num_groups, "dtype": "bf16", "ms_packed": ms_packed,
+                          "num_groups": args.num_groups, "decay": bool(args.decay), "dtype": "bf16", "ms_packed": ms_packed,
                           "ms_padded": ms_padded, "tokens_per_s_packed": T / (ms_packed / 1e3),
                           "speedup": ms_padded / ms_packed}), flush=True)
 

@@ -102,7 +102,8 @@ typedef struct {
                             document n attends to the tokens s <= t of document n only (the kernels
                             clamp the offsets into [0, T] and to non-decreasing order, so a malformed
                             array gives wrong documents but no out-of-bounds access).  Tensor-core
-                            parts form only (bf16 / f16, no decay): KATA_ERR_UNSUPPORTED otherwise */
+                            parts form only (bf16 / f16; decay allowed, c per packed token):
+                            KATA_ERR_UNSUPPORTED otherwise */
   int num_seqs;
 } kata_attn_fwd_args;
 

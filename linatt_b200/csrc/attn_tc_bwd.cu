@@ -123,6 +123,25 @@ __global__ void decay_c_transpose(const float* __restrict__ c, float* __restrict
   }
 }
 
+// The same copy for packed documents (B == 1): indexed by tile number (documents cut into their own
+// 128-row tiles, numbered in document order), rows past a document's end 0.  One CTA of 128
+// threads per tile, one row per thread.
+__global__ void __launch_bounds__(128) decay_c_transpose_var(const float* __restrict__ c, float* __restrict__ cT,
+                                                             int T, int HQ, int Tp, const int* __restrict__ cu,
+                                                             int nseq) {
+  __shared__ SeqTile seq;
+  if (threadIdx.x < 32) {
+    SeqTile st{};
+    const bool have = varlen_tile(cu, nseq, T, static_cast<int>(blockIdx.x), st);
+    if (threadIdx.x == 0) seq = have ? st : SeqTile{0, 0, -1, 0, 0};
+  }
+  __syncthreads();
+  if (seq.j < 0) return;
+  const int t = seq.start + seq.j * kTile + static_cast<int>(threadIdx.x);
+  const size_t col = static_cast<size_t>(blockIdx.x) * kTile + threadIdx.x;
+  for (int hq = 0; hq < HQ; ++hq) cT[static_cast<size_t>(hq) * Tp + col] = t < seq.end ? c[static_cast<size_t>(t) * HQ + hq] : 0.f;
+}
+
 // ================================================================================================
 // dq kernel (tensor-memory ring)
 // ================================================================================================
@@ -262,11 +281,17 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
             mbar_arrive_expect_tx(&bars.ring_full[slot], L::Q_BYTES + (DECAY ? kTile * 4 : 0));
             for (int bx = 0; bx < NBOX; ++bx)
               tma_load_4d(dst + bx * (kTile * CW * 2), &tmK, &bars.ring_full[slot], bx * CW, h, kbase + j * kTile, b);
-            if (DECAY)
+            if (DECAY && !VAR)
               bulk_load(smem + L::DQ_OFF_C + slot * (kTile * 4),
                         ws_views(p.delta, p.B, T_, p.HQ).cT + (static_cast<size_t>(b) * p.HQ + hq) *
                             static_cast<size_t>((T_ + 127) & ~127) + static_cast<size_t>(j) * kTile,
                         kTile * 4, &bars.ring_full[slot]);
+            if constexpr (DECAY && VAR) {  // packed documents: the copy of c is indexed by tile number
+              const BwdWs wv = ws_views(p.delta, p.B, T_, p.HQ, p.nseq);
+              bulk_load(smem + L::DQ_OFF_C + slot * (kTile * 4),
+                        wv.cT + static_cast<size_t>(hq) * wv.Tp + static_cast<size_t>(seq.base + j) * kTile,
+                        kTile * 4, &bars.ring_full[slot]);
+            }
           }
         }
       }
@@ -1131,9 +1156,14 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
   if (!e) e = make_tm_tokens(&to, p.dout, p.B, p.T, p.HQ, DV, VCW);
   if (e) return e;
   const int nt = (p.T + kTile - 1) / kTile;
-  if (DECAY) {  // head-major copy of c for both passes' bulk copies
+  if (DECAY && !VAR) {  // head-major copy of c for both passes' bulk copies
     const BwdWs ws = ws_views(p.delta, p.B, p.T, p.HQ);
     decay_c_transpose<<<296, 256, 0, st>>>(p.c, ws.cT, p.B, p.T, p.HQ, ws.Tp);
+    if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
+  }
+  if (DECAY && VAR) {
+    const BwdWs ws = ws_views(p.delta, p.B, p.T, p.HQ, p.nseq);
+    decay_c_transpose_var<<<varlen_tile_bound(p.T, p.nseq), kTile, 0, st>>>(p.c, ws.cT, p.T, p.HQ, ws.Tp, p.cu, p.nseq);
     if (cudaGetLastError() != cudaSuccess) return KATA_ERR_CUDA;
   }
   if (p.phases != 2) {
@@ -1162,7 +1192,7 @@ int launch_bwd(const AttnBwdParams& p, cudaStream_t st) {
 template <typename T, int D, int DV, int M>
 int bwd_variant(const AttnBwdParams& p, bool sum, cudaStream_t st) {
   const bool dec = p.c != nullptr;
-  // packed documents (p.cu): the VAR instantiations (no decay, checked by the caller)
+  // packed documents (p.cu): the VAR instantiations
   if (sum) {
     if constexpr (M * M <= 16) {
       if (!dec)
@@ -1170,7 +1200,8 @@ int bwd_variant(const AttnBwdParams& p, bool sum, cudaStream_t st) {
     }
     return KATA_ERR_UNSUPPORTED;
   }
-  if (p.cu) return dec ? KATA_ERR_UNSUPPORTED : launch_bwd<T, D, DV, M, false, false, false, true>(p, st);
+  if (p.cu)
+    return dec ? launch_bwd<T, D, DV, M, false, true, false, true>(p, st) : launch_bwd<T, D, DV, M, false, false, false, true>(p, st);
   return dec ? launch_bwd<T, D, DV, M, false, true>(p, st) : launch_bwd<T, D, DV, M, false, false>(p, st);
 }
 

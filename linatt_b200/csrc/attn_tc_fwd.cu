@@ -458,7 +458,7 @@ int launch_fwd(const AttnFwdParams& p, cudaStream_t st) {
 template <typename T, int D, int DV, int M>
 int dispatch_variant(const AttnFwdParams& p, bool sum, cudaStream_t st) {
   const bool dec = p.c != nullptr;
-  // packed documents (p.cu): the VAR instantiations (no decay, checked by the caller)
+  // packed documents (p.cu): the VAR instantiations
   if (sum) {
     // the reference pairs decay with the concat score only (kata/layer.py:187-193)
     if constexpr (M * M <= 16) {
@@ -467,7 +467,8 @@ int dispatch_variant(const AttnFwdParams& p, bool sum, cudaStream_t st) {
     }
     return KATA_ERR_UNSUPPORTED;
   }
-  if (p.cu) return dec ? KATA_ERR_UNSUPPORTED : launch_fwd<T, D, DV, M, false, false, false, true>(p, st);
+  if (p.cu)
+    return dec ? launch_fwd<T, D, DV, M, false, true, false, true>(p, st) : launch_fwd<T, D, DV, M, false, false, false, true>(p, st);
   return dec ? launch_fwd<T, D, DV, M, false, true>(p, st) : launch_fwd<T, D, DV, M, false, false>(p, st);
 }
 

@@ -39,13 +39,12 @@ bool gram_wanted(int algo, int dtype, int D, int Dv, int M, int score, bool deca
   return (algo == KATA_ALGO_AUTO || algo == KATA_ALGO_TC_GRAM) && gram_supported(dtype, D, Dv, M, score, decay);
 }
 
-// Packed documents: B = 1, at least one document, the tensor-core parts form (16-bit, no decay);
-// KATA_OK when cu_seqlens is not given.
-int varlen_check(const int* cu, int nseq, int B, int dtype, bool decay, int algo) {
+// Packed documents: B = 1, at least one document, the tensor-core parts form (16-bit); KATA_OK
+// when cu_seqlens is not given.
+int varlen_check(const int* cu, int nseq, int B, int dtype, int algo) {
   if (!cu) return KATA_OK;
   if (B != 1 || nseq < 1) return KATA_ERR_SHAPE;
-  if (dtype == KATA_DTYPE_F32 || decay || algo == KATA_ALGO_SIMT || algo == KATA_ALGO_TC_GRAM)
-    return KATA_ERR_UNSUPPORTED;
+  if (dtype == KATA_DTYPE_F32 || algo == KATA_ALGO_SIMT || algo == KATA_ALGO_TC_GRAM) return KATA_ERR_UNSUPPORTED;
   return KATA_OK;
 }
 
@@ -72,7 +71,7 @@ extern "C" int kata_attn_fwd(const kata_attn_fwd_args* a, kata_stream_t stream) 
   if (e) return e;
   if (!a->q || !a->k || !a->v || !a->o || !a->den) return KATA_ERR_INVALID;
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o)) return KATA_ERR_ALIGN;
-  if ((e = varlen_check(a->cu_seqlens, a->num_seqs, a->B, a->dtype, a->c != nullptr, a->algo))) return e;
+  if ((e = varlen_check(a->cu_seqlens, a->num_seqs, a->B, a->dtype, a->algo))) return e;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (!a->cu_seqlens && gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr)) {
     const size_t need = gram_fwd_workspace_bytes(a->B, a->T, a->H, a->HQ);
@@ -100,7 +99,7 @@ extern "C" int kata_attn_algo(const kata_attn_fwd_args* a) {
   if (!a) return KATA_ERR_INVALID;
   int e = check_common(a->dtype, a->B, a->T, a->H, a->HQ, a->D, a->Dv, a->M, a->score);
   if (e) return e;
-  if ((e = varlen_check(a->cu_seqlens, a->num_seqs, a->B, a->dtype, a->c != nullptr, a->algo))) return e;
+  if ((e = varlen_check(a->cu_seqlens, a->num_seqs, a->B, a->dtype, a->algo))) return e;
   if (!a->cu_seqlens && gram_wanted(a->algo, a->dtype, a->D, a->Dv, a->M, a->score, a->c != nullptr))
     return KATA_ALGO_TC_GRAM;
   if (a->algo == KATA_ALGO_TC_GRAM) return KATA_ERR_UNSUPPORTED;
@@ -142,7 +141,7 @@ int kata::attn_bwd_impl(const kata_attn_bwd_args* a, const float* delta_in, kata
       !aligned16(a->dq) || !aligned16(a->dk) || !aligned16(a->dv))
     return KATA_ERR_ALIGN;
   if (a->phases < 0 || a->phases > 2) return KATA_ERR_INVALID;
-  if ((e = varlen_check(a->cu_seqlens, a->num_seqs, a->B, a->dtype, a->c != nullptr, a->algo))) return e;
+  if ((e = varlen_check(a->cu_seqlens, a->num_seqs, a->B, a->dtype, a->algo))) return e;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int nseq = a->cu_seqlens ? a->num_seqs : 0;
   AttnBwdParams p{a->q,  a->k,  a->v,  a->o,  a->den, a->dout, a->c,  a->dq, a->dk,           a->dv,

@@ -6,13 +6,13 @@ Documents are packed along T as (1, T_total, H, D) with ``cu_seqlens`` = [0, l_0
 (``kata/kernels/parallel_kata_hopper.py:18-44``).  Token t of document n attends to the tokens
 s <= t of document n only.
 
-On the tensor-core kernels (bf16 / f16 inputs in their envelope, no decay) the documents go to the
+On the tensor-core kernels (bf16 / f16 inputs in their envelope, with or without decay) the documents go to the
 kernels as they lie: each CTA takes one 128-row tile of one document (the tiles of all documents
 numbered in document order, ``cu_seqlens`` read on the device), its key tiles start at the
 document's first row, and rows past the document's end are masked (their outputs are not written,
 and in the backward their per-query vectors are zero).  No padding and no scatter / gather pass.
 
-Otherwise (fp32, decay, shapes outside that envelope) each document is scattered into its own row
+Otherwise (fp32, shapes outside that envelope) each document is scattered into its own row
 of a zero-padded (N, T_max, H, D) batch, the flash kernels run on that batch, and the rows are
 gathered back.  Padding sits after each document's last token, so causality keeps it out of every
 real row: the outputs and gradients equal those of one call per document.  The cost is the padding
@@ -62,31 +62,32 @@ def unpack_rows(y: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
 
 
 class _PackedKataFunction(torch.autograd.Function):
-    """Packed documents straight through the tensor-core kernels (``cu_seqlens`` on the device)."""
+    """Packed documents straight through the tensor-core kernels (``cu_seqlens`` on the device);
+    ``c`` (1, T_total, HQ) fp32 log-decay or None."""
 
     @staticmethod
-    def forward(ctx, q, k, v, cu, num_groups, scale, score):
-        o, den = _pka._fwd(q, k, v, num_groups, scale, score, cu=cu)
-        ctx.save_for_backward(q, k, v, o, den, cu)
+    def forward(ctx, q, k, v, c, cu, num_groups, scale, score):
+        o, den = _pka._fwd(q, k, v, num_groups, scale, score, c=c, cu=cu)
+        ctx.save_for_backward(q, k, v, o, den, cu, c)
         ctx.num_groups, ctx.scale, ctx.score = num_groups, scale, score
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, o, den, cu = ctx.saved_tensors
-        dq, dk, dv, _ = _pka._bwd(q, k, v, o, den, do, ctx.num_groups, ctx.scale, ctx.score, cu=cu)
-        return dq, dk, dv, None, None, None, None
+        q, k, v, o, den, cu, c = ctx.saved_tensors
+        dq, dk, dv, dc = _pka._bwd(q, k, v, o, den, do, ctx.num_groups, ctx.scale, ctx.score, c=c, cu=cu)
+        return dq, dk, dv, dc, None, None, None, None
 
 
 def _packed_ok(q, k, v, num_groups, score, c, nseq) -> bool:
     """True when the tensor-core kernels take the packed documents as they lie."""
-    if c is not None or _pka.ALGO in ("simt", "tc_gram") or q.dtype not in (torch.bfloat16, torch.float16):
+    if _pka.ALGO in ("simt", "tc_gram") or q.dtype not in (torch.bfloat16, torch.float16):
         return False
     if k.dtype != q.dtype or v.dtype != q.dtype or not q.is_cuda or nseq < 1:
         return False
     a = _lib.AttnFwdArgs(dtype=_lib.DTYPE[q.dtype], B=1, T=max(q.shape[1], 1), H=k.shape[2], HQ=q.shape[2],
                          D=q.shape[-1], Dv=v.shape[-1], M=num_groups, score=_lib.SCORE[score],
-                         algo=_lib.ALGO["tc"], scale=1.0, cu_seqlens=1, num_seqs=nseq)
+                         algo=_lib.ALGO["tc"], scale=1.0, c=None if c is None else 16, cu_seqlens=1, num_seqs=nseq)
     return _lib.lib().kata_attn_algo(a) == _lib.ALGO["tc"]
 
 
@@ -126,7 +127,7 @@ def parallel_kata_attn_varlen(q, k, v, cu_seqlens, num_groups=4, scale=None, sco
     nseq = cu_seqlens.numel() - 1
     if q.shape[1] > 0 and _packed_ok(q, k, v, num_groups, score, c, nseq):
         cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
-        return _PackedKataFunction.apply(q, k, v, cu, num_groups, scale, score)
+        return _PackedKataFunction.apply(q, k, v, c, cu, num_groups, scale, score)
     dst, N, T_max = varlen_index(cu_seqlens.to(q.device), max_seqlen, total=q.shape[1])
     qp, kp, vp = (pack_rows(x, dst, N, T_max) for x in (q, k, v))
     if c is not None:

@@ -121,8 +121,8 @@ def test_gram_form_host_logic(L):
 
 
 def test_packed_documents_host_logic(L):
-    """cu_seqlens (packed documents): B = 1 and the tensor-core parts form only; the backward's
-    workspace grows by one 128-row tile of per-query vectors per document."""
+    """cu_seqlens (packed documents): B = 1 and the tensor-core parts form only (with or without
+    decay); the backward's workspace grows by one 128-row tile of per-query vectors per document."""
     from linatt_b200 import _lib
 
     kw = dict(dtype=1, B=1, T=1000, H=2, HQ=2, D=128, Dv=128, M=4, score=0, algo=0, scale=1.0,
@@ -132,7 +132,7 @@ def test_packed_documents_host_logic(L):
     assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "num_seqs": 0})) == -3
     assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "dtype": 0})) == -8      # fp32
     assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "algo": 2})) == -8       # SIMT
-    assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "c": 16})) == -8         # decay
+    assert L.kata_attn_algo(_lib.AttnFwdArgs(**{**kw, "c": 16})) == 1          # decay: tensor cores too
     # a sum score with groups of 16 stays on the parts form (no Gram features for packed documents)
     g = {**kw, "D": 64, "Dv": 64, "score": 1}
     assert L.kata_attn_algo(_lib.AttnFwdArgs(**g)) == 1

@@ -1,8 +1,8 @@
 """GPU parity of the packed-sequence API: outputs and gradients of parallel_kata_attn_varlen over
 packed documents equal one flash call per document (bf16 / fp16: rel-L2 <= 1e-2, fp32: <= 1e-5), for
 the concat and sum scores, the decayed form and GQA, with ragged, empty and length-1 documents.
-16-bit inputs without decay take the tensor-core kernels' packed-document form (no padding); fp32
-and the decayed form take the padded batch.  The two forms are also compared with each other."""
+16-bit inputs take the tensor-core kernels' packed-document form (no padding), with or without
+decay; fp32 takes the padded batch.  The two forms are also compared with each other."""
 
 from __future__ import annotations
 
@@ -67,12 +67,14 @@ def test_varlen_matches_per_document_calls(lens, HQ, H, D, M, score, dtype, deca
             assert _rel(leaves[i].grad[:, s:e], part[i].grad) < tol, f"doc {n} {name}"
 
 
-@pytest.mark.parametrize("lens,HQ,H,D,M,score", [
-    ([100, 1, 256, 63, 0, 130], 4, 2, 128, 4, "concat"),
-    ([65, 130, 7, 300], 2, 2, 64, 4, "sum"),
-    ([3 + 7 * i for i in range(70)], 2, 2, 64, 2, "concat"),
+@pytest.mark.parametrize("lens,HQ,H,D,M,score,decay", [
+    ([100, 1, 256, 63, 0, 130], 4, 2, 128, 4, "concat", False),
+    ([65, 130, 7, 300], 2, 2, 64, 4, "sum", False),
+    ([3 + 7 * i for i in range(70)], 2, 2, 64, 2, "concat", False),
+    ([100, 1, 256, 63, 0, 130], 4, 2, 128, 4, "concat", True),
+    ([129, 40, 300], 2, 2, 64, 4, "concat", True),
 ])
-def test_packed_form_matches_padded_form(lens, HQ, H, D, M, score, monkeypatch):
+def test_packed_form_matches_padded_form(lens, HQ, H, D, M, score, decay, monkeypatch):
     """The tensor-core packed-document form against the padded batch on the same bf16 inputs: the
     same function, so outputs and gradients agree to the bf16 tolerance; the packed form must be
     the one AUTO takes for these inputs."""
@@ -85,17 +87,19 @@ def test_packed_form_matches_padded_form(lens, HQ, H, D, M, score, monkeypatch):
     k = F.normalize(torch.randn(1, T, H, D, generator=g), dim=-1).bfloat16().cuda()
     v = torch.randn(1, T, H, D, generator=g).bfloat16().cuda()
     do = torch.randn(1, T, HQ, D, generator=g).bfloat16().cuda()
-    assert vl._packed_ok(q, k, v, M, score, None, len(lens))
+    c = -F.softplus(torch.randn(1, T, HQ, generator=g)).cumsum(1).cuda() if decay else None
+    assert vl._packed_ok(q, k, v, M, score, c, len(lens))
 
     def run(packed):
         monkeypatch.setattr(vl, "_packed_ok", (lambda *a: True) if packed else (lambda *a: False))
-        leaves = [x.clone().requires_grad_(True) for x in (q, k, v)]
-        o = vl.parallel_kata_attn_varlen(*leaves, cu, num_groups=M, score=score, max_seqlen=max(lens))
+        leaves = [x.clone().requires_grad_(True) for x in (q, k, v)] + ([c.clone().requires_grad_(True)] if decay else [])
+        o = vl.parallel_kata_attn_varlen(*leaves[:3], cu, num_groups=M, score=score, max_seqlen=max(lens),
+                                         c=leaves[3] if decay else None)
         o.backward(do)
         torch.cuda.synchronize()
         return [o.detach()] + [x.grad for x in leaves]
 
     got, ref = run(True), run(False)
-    for name, a, b in zip(("o", "dq", "dk", "dv"), got, ref):
+    for name, a, b in zip(("o", "dq", "dk", "dv", "dc"), got, ref):
         assert torch.isfinite(a.float()).all(), name
         assert _rel(a, b) < 1e-2, name
