@@ -104,6 +104,28 @@ __device__ __forceinline__ uint32_t bf2_pack(float2 v) {
 __device__ __forceinline__ float2 bf2_unpack(uint32_t u) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
 }
+// Causal mask of one diagonal tile on a thread's 64 consecutive columns held as 32 packed 16-bit
+// pairs (low half = even column): columns below `lim` (counted from the first) become zero.  Kept
+// out of the per-element loops, so the off-diagonal tiles run none of it.
+__device__ __forceinline__ void mask_words_below(uint32_t (&w)[32], int lim) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (2 * i + 1 < lim)
+      w[i] = 0u;
+    else if (2 * i < lim)
+      w[i] &= 0xffff0000u;
+  }
+}
+// The same on 64 fp32 columns held as 32 pairs.
+__device__ __forceinline__ void mask_pairs_below(float2 (&a)[32], int lim) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (2 * i + 1 < lim)
+      a[i] = make_float2(0.f, 0.f);
+    else if (2 * i < lim)
+      a[i].x = 0.f;
+  }
+}
 // Packed bf16 product (round to nearest even), one instruction for two elements.
 __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -967,13 +989,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                               make_float2(dr.x, dr.y));
             float2 d1 = ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
                               make_float2(dr.z, dr.w));
-            if (diag) {  // causal: query t >= key s
-              const int tl = cbase + 4 * x4;
-              if (tl < row) d0.x = 0.f;
-              if (tl + 1 < row) d0.y = 0.f;
-              if (tl + 2 < row) d1.x = 0.f;
-              if (tl + 3 < row) d1.y = 0.f;
-            }
             if (DECAY) {
               const float4 ct = *reinterpret_cast<const float4*>(v_c + cbase + 4 * x4);
               d0.x *= __expf(fminf(ct.x - c_s, 0.f));
@@ -989,6 +1004,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars.i_free[x]);
+        if (diag) mask_words_below(dap, row - hc * 64);  // causal: query t >= key s
         ++it;
       }
       float2 acc[32];
@@ -1028,32 +1044,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c < 3) tmem_wait_ld();
         }
         if (pp == NP - 1) {  // P^T = scale^2 A / den into the other half of the slot (all S is read)
+          // one copy of the stage for the diagonal tile (causal mask) and one without any mask
+          const auto p_stage = [&](auto diag_c) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int cbase = hc * 64 + c * 16;
-            uint32_t pv[8];
+            for (int c = 0; c < 4; ++c) {
+              const int cbase = hc * 64 + c * 16;
+              uint32_t pv[8];
 #pragma unroll
-            for (int x2 = 0; x2 < 8; ++x2) {
-              const int tl = cbase + 2 * x2;
-              const float2 a = fmul2(acc[8 * c + x2], *reinterpret_cast<const float2*>(v_rd + tl));
-              float a0 = a.x, a1 = a.y;
-              if (DECAY) {
-                const float2 ct = *reinterpret_cast<const float2*>(v_c + tl);
-                const float x0 = ct.x - c_s, x1 = ct.y - c_s;
-                a0 *= __expf(fminf(x0, 0.f));
-                a1 *= __expf(fminf(x1, 0.f));
-                const float2 dd = bf2_unpack(dap[8 * c + x2]);  // dA''_dec, causally masked
-                if (x0 <= 0.f) csum = fmaf(dd.x, acc[8 * c + x2].x, csum);
-                if (x1 <= 0.f) csum = fmaf(dd.y, acc[8 * c + x2].y, csum);
+              for (int x2 = 0; x2 < 8; ++x2) {
+                const int tl = cbase + 2 * x2;
+                const float2 a = fmul2(acc[8 * c + x2], *reinterpret_cast<const float2*>(v_rd + tl));
+                float a0 = a.x, a1 = a.y;
+                if (DECAY) {
+                  const float2 ct = *reinterpret_cast<const float2*>(v_c + tl);
+                  const float x0 = ct.x - c_s, x1 = ct.y - c_s;
+                  a0 *= __expf(fminf(x0, 0.f));
+                  a1 *= __expf(fminf(x1, 0.f));
+                  const float2 dd = bf2_unpack(dap[8 * c + x2]);  // dA''_dec, causally masked
+                  if (x0 <= 0.f) csum = fmaf(dd.x, acc[8 * c + x2].x, csum);
+                  if (x1 <= 0.f) csum = fmaf(dd.y, acc[8 * c + x2].y, csum);
+                }
+                if constexpr (decltype(diag_c)::value) {
+                  if (tl < row) a0 = 0.f;
+                  if (tl + 1 < row) a1 = 0.f;
+                }
+                pv[x2] = pack2<T>(a0, a1);
               }
-              if (diag) {
-                if (tl < row) a0 = 0.f;
-                if (tl + 1 < row) a1 = 0.f;
-              }
-              pv[x2] = pack2<T>(a0, a1);
+              tmem_st8(sbase + 32u + c * 8u, pv);
             }
-            tmem_st8(sbase + 32u + c * 8u, pv);
-          }
+          };
+          if (diag)
+            p_stage(std::true_type{});
+          else
+            p_stage(std::false_type{});
         }
         tmem_wait_st();
         tc_fence_before();
