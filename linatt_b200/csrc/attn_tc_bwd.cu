@@ -104,28 +104,6 @@ __device__ __forceinline__ uint32_t bf2_pack(float2 v) {
 __device__ __forceinline__ float2 bf2_unpack(uint32_t u) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
 }
-// Causal mask of one diagonal tile on a thread's 64 consecutive columns held as 32 packed 16-bit
-// pairs (low half = even column): columns below `lim` (counted from the first) become zero.  Kept
-// out of the per-element loops, so the off-diagonal tiles run none of it.
-__device__ __forceinline__ void mask_words_below(uint32_t (&w)[32], int lim) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    if (2 * i + 1 < lim)
-      w[i] = 0u;
-    else if (2 * i < lim)
-      w[i] &= 0xffff0000u;
-  }
-}
-// The same on 64 fp32 columns held as 32 pairs.
-__device__ __forceinline__ void mask_pairs_below(float2 (&a)[32], int lim) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    if (2 * i + 1 < lim)
-      a[i] = make_float2(0.f, 0.f);
-    else if (2 * i < lim)
-      a[i].x = 0.f;
-  }
-}
 // Packed bf16 product (round to nearest even), one instruction for two elements.
 __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -973,38 +951,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t nbase = lane_addr + x * 128u + hc * 64u;
-        uint32_t rn[2][16];
-        tmem_ld16(nbase, rn[0]);
-        tmem_wait_ld();
+        // one copy of the item for the diagonal tile (causal mask: query t >= key s), one without
+        const auto dn_item = [&](auto diag_c) {
+          uint32_t rn[2][16];
+          tmem_ld16(nbase, rn[0]);
+          tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cur = c & 1;
-          if (c < 3) tmem_ld16(nbase + (c + 1) * 16u, rn[cur ^ 1]);
-          const int cbase = hc * 64 + c * 16;
+          for (int c = 0; c < 4; ++c) {
+            const int cur = c & 1;
+            if (c < 3) tmem_ld16(nbase + (c + 1) * 16u, rn[cur ^ 1]);
+            const int cbase = hc * 64 + c * 16;
 #pragma unroll
-          for (int x4 = 0; x4 < 4; ++x4) {
-            const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
-            const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
-            float2 d0 = ffma2(u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]), make_float2(rd.x, rd.y),
-                              make_float2(dr.x, dr.y));
-            float2 d1 = ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
-                              make_float2(dr.z, dr.w));
-            if (DECAY) {
-              const float4 ct = *reinterpret_cast<const float4*>(v_c + cbase + 4 * x4);
-              d0.x *= __expf(fminf(ct.x - c_s, 0.f));
-              d0.y *= __expf(fminf(ct.y - c_s, 0.f));
-              d1.x *= __expf(fminf(ct.z - c_s, 0.f));
-              d1.y *= __expf(fminf(ct.w - c_s, 0.f));
+            for (int x4 = 0; x4 < 4; ++x4) {
+              const float4 rd = *reinterpret_cast<const float4*>(v_rd + cbase + 4 * x4);
+              const float4 dr = *reinterpret_cast<const float4*>(v_dr + cbase + 4 * x4);
+              float2 d0 = ffma2(u2f2(rn[cur][4 * x4], rn[cur][4 * x4 + 1]), make_float2(rd.x, rd.y),
+                                make_float2(dr.x, dr.y));
+              float2 d1 = ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
+                                make_float2(dr.z, dr.w));
+              if constexpr (decltype(diag_c)::value) {
+                const int tl = cbase + 4 * x4;
+                if (tl < row) d0.x = 0.f;
+                if (tl + 1 < row) d0.y = 0.f;
+                if (tl + 2 < row) d1.x = 0.f;
+                if (tl + 3 < row) d1.y = 0.f;
+              }
+              if (DECAY) {
+                const float4 ct = *reinterpret_cast<const float4*>(v_c + cbase + 4 * x4);
+                d0.x *= __expf(fminf(ct.x - c_s, 0.f));
+                d0.y *= __expf(fminf(ct.y - c_s, 0.f));
+                d1.x *= __expf(fminf(ct.z - c_s, 0.f));
+                d1.y *= __expf(fminf(ct.w - c_s, 0.f));
+              }
+              dap[8 * c + 2 * x4] = bf2_pack(d0);
+              dap[8 * c + 2 * x4 + 1] = bf2_pack(d1);
             }
-            dap[8 * c + 2 * x4] = bf2_pack(d0);
-            dap[8 * c + 2 * x4 + 1] = bf2_pack(d1);
+            if (c < 3) tmem_wait_ld();
           }
-          if (c < 3) tmem_wait_ld();
-        }
+        };
+        if (diag)
+          dn_item(std::true_type{});
+        else
+          dn_item(std::false_type{});
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars.i_free[x]);
-        if (diag) mask_words_below(dap, row - hc * 64);  // causal: query t >= key s
         ++it;
       }
       float2 acc[32];
