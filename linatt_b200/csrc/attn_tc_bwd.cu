@@ -315,21 +315,21 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       const uint64_t rv0 = kmajor_desc<VCW>(sRing, 0, DV, 0);  // V in ring slot 0, K-major
       const uint64_t rk0 = kmajor_desc<CW>(sRing, 0, E, 0);    // K in ring slot 0, K-major
       static_assert(kRingDQ == 4, "ring positions below assume four slots");
-      bool ok = mbar_wait_w(&bars.qo_full, 0, wc);
+      bool ok = mbar_wait_w_inl(&bars.qo_full, 0, wc);
       int it = 0, x = 0;       // x = it % NS
       uint32_t use_par = 0;    // parity of (it / NS), i.e. of the current use of slot x
       for (int j = 0; ok && j < nk; ++j) {
         const uint32_t ring_par = static_cast<uint32_t>(j >> 1) & 1u;
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
-          if (it >= NS && !mbar_wait_w(&bars.w_done[x], use_par ^ 1, wc)) {
+          if (it >= NS && !mbar_wait_w_inl(&bars.w_done[x], use_par ^ 1, wc)) {
             ok = false;
             break;
           }
           const uint32_t sd = tbase + static_cast<uint32_t>(x) * 128u;
           if (q == 0) {  // dN = dO V_j^T
             const int slotV = (2 * j) & 3;
-            if (!mbar_wait_w(&bars.ring_full[slotV], ring_par, wc)) {
+            if (!mbar_wait_w_inl(&bars.ring_full[slotV], ring_par, wc)) {
               ok = false;
               break;
             }
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
               umma_ss_w(sd, od0 + kstep<VCW>(kk), vd + kstep<VCW>(kk), id_nn, kk > 0 ? 1u : 0u);
             umma_commit_w(&bars.i_full[x]);
             umma_commit_w(&bars.ring_empty[slotV]);
-            if (!GRAM && !mbar_wait_w(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
+            if (!GRAM && !mbar_wait_w_inl(&bars.ring_full[(2 * j + 1) & 3], ring_par, wc)) {  // K_j
               ok = false;
               break;
             }
@@ -381,13 +381,13 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       for (int j = 0; ok && j < nk; ++j) {
 #pragma unroll
         for (int q = 0; q < kItems; ++q) {
-          if (!mbar_wait_w(&bars.i_free[x], use_par, wc)) {
+          if (!mbar_wait_w_inl(&bars.i_free[x], use_par, wc)) {
             ok = false;
             break;
           }
           if (GRAM) {  // dQ += dA' phi(K_j): the K tile's first and only use
             const int kslot = (2 * j + 1) & 3;
-            if (!mbar_wait_w(&bars.ring_full[kslot], static_cast<uint32_t>(j >> 1) & 1u, wc)) {
+            if (!mbar_wait_w_inl(&bars.ring_full[kslot], static_cast<uint32_t>(j >> 1) & 1u, wc)) {
               ok = false;
               break;
             }

@@ -288,6 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           cpre[h2] = (s0 < T_) ? __ldg(cbase + static_cast<size_t>(s0) * p.HQ) : 0.f;
         }
       }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.f, 0.f);  // fma(s, s, 0) == s * s
       for (int pp = 0; pp < NP; ++pp, ++u) {
         slot = u % kSlots;
         if (!mbar_wait(&bars.s_full[slot], (u / kSlots) & 1, wc)) {
@@ -310,12 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x0 = make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
-          acc[i] = GRAM ? x0 : pp == 0 ? fmul2(x0, x0) : ffma2(x0, x0, acc[i]);  // Gram: A = S
+          acc[i] = GRAM ? x0 : ffma2(x0, x0, acc[i]);  // Gram: A = S
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x1 = make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
-          acc[16 + i] = GRAM ? x1 : pp == 0 ? fmul2(x1, x1) : ffma2(x1, x1, acc[16 + i]);
+          acc[16 + i] = GRAM ? x1 : ffma2(x1, x1, acc[16 + i]);
         }
       }
       if (!ok) break;

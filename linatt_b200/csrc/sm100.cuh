@@ -99,11 +99,33 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
   return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, w.status, w.abort);
 }
+// The same bounded wait with its polling loop inline (no call).  Which form is faster depends on
+// the kernel: measured on B200, the dq pass's two issuer warps run 6 % faster with this one, while
+// the forward's and the dk/dv pass's issuers, and every kernel's compute warps, are faster with the
+// out-of-line loop.
+__device__ __forceinline__ bool mbar_wait_inl(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*w.abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *w.abort = 1;
+        if (w.status) atomicCAS(w.status, 0, kStatusWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
 // Warp-uniform bounded wait for a warp that issues with the _w forms below: every lane waits and
 // the result is the AND over the warp, so no lane leaves a loop that the others continue (a lane
 // that timed out and a lane that saw the phase complete both take the abort path).
 __device__ __forceinline__ bool mbar_wait_w(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, w));
+}
+__device__ __forceinline__ bool mbar_wait_w_inl(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
+  return __all_sync(0xffffffffu, mbar_wait_inl(bar, parity, w));
 }
 
 // Bounded wait used only on the abort path to let in-flight copies / MMAs land before the CTA
