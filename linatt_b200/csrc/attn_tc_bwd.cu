@@ -969,7 +969,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 make_float2(dr.x, dr.y));
               float2 d1 = ffma2(u2f2(rn[cur][4 * x4 + 2], rn[cur][4 * x4 + 3]), make_float2(rd.z, rd.w),
                                 make_float2(dr.z, dr.w));
-              if constexpr (decltype(diag_c)::value) {
+              if (decltype(diag_c)::value && diag) {
                 const int tl = cbase + 4 * x4;
                 if (tl < row) d0.x = 0.f;
                 if (tl + 1 < row) d0.y = 0.f;
@@ -989,7 +989,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (c < 3) tmem_wait_ld();
           }
         };
-        if (diag)
+        // (with decay, one copy that tests the tile: the second copy made the decayed variant spill)
+        if (DECAY || diag)
           dn_item(std::true_type{});
         else
           dn_item(std::false_type{});
@@ -1055,7 +1056,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (x0 <= 0.f) csum = fmaf(dd.x, acc[8 * c + x2].x, csum);
                   if (x1 <= 0.f) csum = fmaf(dd.y, acc[8 * c + x2].y, csum);
                 }
-                if constexpr (decltype(diag_c)::value) {
+                if (decltype(diag_c)::value && diag) {
                   if (tl < row) a0 = 0.f;
                   if (tl + 1 < row) a1 = 0.f;
                 }
@@ -1064,7 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem_st8(sbase + 32u + c * 8u, pv);
             }
           };
-          if (diag)
+          if (DECAY || diag)
             p_stage(std::true_type{});
           else
             p_stage(std::false_type{});
