@@ -489,8 +489,8 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       float2 da[32];  // dA' of this thread's 64 key columns
       uint32_t cm[2] = {0u, 0u};  // decay: columns with c_t - c_s > 0 (no dc contribution)
       {
-        const int x = it % NS;
-        if (!mbar_wait(&bars.i_full[x], (it / NS) & 1, wc)) {
+        const int x = static_cast<int>(static_cast<unsigned>(it) % NS);  // it >= 0
+        if (!mbar_wait(&bars.i_full[x], (static_cast<unsigned>(it) / NS) & 1u, wc)) {
           ok = false;
           break;
         }
@@ -577,8 +577,8 @@ __global__ void __launch_bounds__(kThreadsRing, 1)
       }
       const bool any_clamp = DECAY && (cm[0] | cm[1]) != 0u;
       for (int pp = 0; pp < NPL; ++pp, ++it) {
-        const int x = it % NS;
-        if (!mbar_wait(&bars.i_full[x], (it / NS) & 1, wc)) {
+        const int x = static_cast<int>(static_cast<unsigned>(it) % NS);  // it >= 0
+        if (!mbar_wait(&bars.i_full[x], (static_cast<unsigned>(it) / NS) & 1u, wc)) {
           ok = false;
           break;
         }
